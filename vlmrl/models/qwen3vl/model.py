@@ -1,0 +1,362 @@
+"""Qwen3-VL text decoder: explicit forward / backward executor over flat parameter units.
+
+The decoder (HF ``Qwen3VLTextModel``; reference ``models/qwen3vl/model.py:425-884``)
+is pre-norm: ``h += o_proj(attn(qk_norm_rope(qkv(rms(h)))))`` then
+``h += down(swiglu(gate_up(rms(h))))``; vision embeddings replace the
+``<|image_pad|>`` rows of the token embeddings and, after decoder layers
+``0..len(deepstack)-1``, the deepstack features are added at the same rows.
+
+Instead of autograd, ``forward_train`` records what each layer needs and
+``backward_train`` runs the hand-written backward of every op in reverse,
+writing weight gradients straight into per-unit fp32 flat buffers supplied by
+the parameter source.  That is what lets FSDP reduce-scatter a unit's gradient
+the moment its backward finishes (see ``vlmrl.parallel.fsdp``).
+
+Design choices (vs. the reference):
+
+* packed varlen token layout (``cu_seqlens``) — no padding in any kernel;
+* the vocab projection only runs on rows whose target is in the loss mask,
+  through the fused ``vocab_logprob`` op (logp, entropy, lse) that never
+  materialises fp32 logits;
+* the KV cache is ``[L, B, Hkv, Tmax, D]`` bf16, written by ``kv_write`` /
+  the decode step; decode positions are ``cache_len + rope_delta``.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from vlmrl import ops
+from vlmrl.models.qwen3vl.config import Qwen3VLSpec
+from vlmrl.models.qwen3vl.params import UnitLayout, all_layouts, text_layouts, vision_layout
+
+
+# --------------------------------------------------------------------------- containers
+@dataclass
+class VisionEmbeddings:
+    """Merged vision tokens (packed over images) and deepstack features of the same rows."""
+    tokens: torch.Tensor
+    deepstack: Tuple[torch.Tensor, ...] = ()
+
+    @classmethod
+    def concatenate(cls, embeds: Sequence["VisionEmbeddings"]) -> "VisionEmbeddings":
+        if not embeds:
+            return cls(tokens=torch.zeros(0, 0))
+        n = len(embeds[0].deepstack)
+        if any(len(e.deepstack) != n for e in embeds):
+            raise ValueError("All VisionEmbeddings must have the same number of DeepStack levels to concatenate.")
+        return cls(tokens=torch.cat([e.tokens for e in embeds], 0),
+                   deepstack=tuple(torch.cat([e.deepstack[i] for e in embeds], 0) for i in range(n)))
+
+    def cast(self, dtype) -> "VisionEmbeddings":
+        return VisionEmbeddings(self.tokens.to(dtype), tuple(d.to(dtype) for d in self.deepstack))
+
+    def to(self, device) -> "VisionEmbeddings":
+        return VisionEmbeddings(self.tokens.to(device), tuple(d.to(device) for d in self.deepstack))
+
+    def select(self, rows: torch.Tensor) -> "VisionEmbeddings":
+        return VisionEmbeddings(self.tokens[rows], tuple(d[rows] for d in self.deepstack))
+
+
+@dataclass
+class PackedBatch:
+    """Device-side packed sequences for the decoder.
+
+    ``tokens``/``targets`` [T] int64 (targets only where ``loss_rows`` points),
+    ``pos`` [3, T] int32, ``cu_seqlens`` [B+1] int32, ``vis_rows`` [R] int64
+    (rows of ``<|image_pad|>`` tokens, in order), ``loss_rows`` [M] int64 rows
+    whose next-token log-prob is scored.
+    """
+    tokens: torch.Tensor
+    pos: torch.Tensor
+    cu_seqlens: torch.Tensor
+    max_seqlen: int
+    vis_rows: torch.Tensor
+    loss_rows: torch.Tensor
+    targets: torch.Tensor
+    vision: Optional[VisionEmbeddings] = None
+
+
+class KVCache:
+    """Preallocated per-sequence KV cache ``[L, B, Hkv, Tmax, D]`` plus lengths ``[B]``."""
+
+    def __init__(self, num_layers: int, batch: int, num_kv_heads: int, max_len: int, head_dim: int,
+                 dtype=torch.bfloat16, device="cpu"):
+        shape = (num_layers, batch, num_kv_heads, max_len, head_dim)
+        self.keys = torch.zeros(shape, dtype=dtype, device=device)
+        self.values = torch.zeros(shape, dtype=dtype, device=device)
+        self.lengths = torch.zeros(batch, dtype=torch.int32, device=device)
+        self.max_len = max_len
+
+    @classmethod
+    def init(cls, batch, num_layers, num_heads, head_dim, max_len, dtype=torch.bfloat16, device="cpu"):
+        return cls(num_layers, batch, num_heads, max_len, head_dim, dtype, device)
+
+
+# --------------------------------------------------------------------------- parameter sources
+class LocalParams:
+    """Full parameter units resident on one device (no sharding).
+
+    ``get(name)`` returns the unit's flat compute-dtype buffer; ``grad(name)``
+    the fp32 gradient accumulator (allocated on first use) and
+    ``grad_done(name)`` is the hook where a sharded source reduces gradients.
+    """
+
+    def __init__(self, units: Dict[str, torch.Tensor], trainable: Optional[Sequence[str]] = None):
+        self.units = units
+        self.trainable = set(trainable) if trainable is not None else set(units)
+        self.grads: Dict[str, torch.Tensor] = {}
+
+    def get(self, name: str) -> torch.Tensor:
+        return self.units[name]
+
+    def release(self, name: str) -> None:
+        pass
+
+    def grad(self, name: str) -> Optional[torch.Tensor]:
+        if name not in self.trainable:
+            return None
+        g = self.grads.get(name)
+        if g is None:
+            g = torch.zeros(self.units[name].numel(), dtype=torch.float32, device=self.units[name].device)
+            self.grads[name] = g
+        return g
+
+    def grad_done(self, name: str) -> None:
+        pass
+
+    def zero_grads(self) -> None:
+        for g in self.grads.values():
+            g.zero_()
+
+
+# --------------------------------------------------------------------------- decoder
+@dataclass
+class _LayerCtx:
+    x: torch.Tensor
+    xn: torch.Tensor
+    r1: torch.Tensor
+    qkv: torch.Tensor
+    q: torch.Tensor
+    k: torch.Tensor
+    v: torch.Tensor
+    rq: torch.Tensor
+    rk: torch.Tensor
+    o: torch.Tensor
+    lse: torch.Tensor
+    h1: torch.Tensor
+    hn: torch.Tensor
+    r2: torch.Tensor
+    act: torch.Tensor
+    pre: torch.Tensor
+
+
+@dataclass
+class TrainCtx:
+    batch: PackedBatch
+    layers: List[_LayerCtx] = field(default_factory=list)
+    h_loss: Optional[torch.Tensor] = None
+    hn_loss: Optional[torch.Tensor] = None
+    r_final: Optional[torch.Tensor] = None
+    lse: Optional[torch.Tensor] = None
+    ent: Optional[torch.Tensor] = None
+
+
+class TextDecoder:
+    def __init__(self, spec: Qwen3VLSpec):
+        self.spec = spec
+        t = spec.text
+        self.t = t
+        self.H, self.D = t.hidden_size, t.head_dim
+        self.nq, self.nkv = t.num_attention_heads, t.num_key_value_heads
+        self.eps = t.rms_norm_eps
+        self.scale = 1.0 / math.sqrt(t.head_dim)
+        self.rope = ops.RopeCfg(t.head_dim, t.rope_theta, t.rope_section, t.mrope_interleaved)
+        self.layouts = {l.name: l for l in text_layouts(spec)}
+        self.n_layers = t.num_hidden_layers
+
+    # ---------------------------------------------------------------- helpers
+    def _w(self, params, name: str) -> Dict[str, torch.Tensor]:
+        return self.layouts[name].views(params.get(name))
+
+    def _g(self, params, name: str) -> Optional[Dict[str, torch.Tensor]]:
+        g = params.grad(name)
+        return None if g is None else self.layouts[name].views(g)
+
+    def embed_inputs(self, params, batch: PackedBatch) -> torch.Tensor:
+        e = self._w(params, "embed")["embed"]
+        h = ops.embed(batch.tokens, e)
+        if batch.vision is not None and batch.vis_rows.numel():
+            ops.scatter_rows_(h, batch.vis_rows, batch.vision.tokens.to(h.dtype), add=False)
+        params.release("embed")
+        return h
+
+    def _deepstack(self, h, batch: PackedBatch, i: int):
+        if batch.vision is not None and i < len(batch.vision.deepstack) and batch.vis_rows.numel():
+            ops.scatter_rows_(h, batch.vis_rows, batch.vision.deepstack[i].to(h.dtype), add=True)
+        return h
+
+    # ---------------------------------------------------------------- layer fwd
+    def layer_forward(self, w: Dict[str, torch.Tensor], x: torch.Tensor, pos: torch.Tensor, cu: torch.Tensor,
+                      max_seqlen: int, save: bool, kv_sink=None):
+        T = x.shape[0]
+        xn, r1 = ops.rms_norm(x, w["input_norm"], self.eps)
+        qkv = ops.linear(xn, w["qkv_w"], bias=w["qkv_b"], out_dtype=x.dtype)
+        q, k, v, rq, rk = ops.qk_norm_rope(qkv, w["q_norm"], w["k_norm"], pos, self.rope,
+                                           n_q=self.nq, n_kv=self.nkv, eps=self.eps)
+        if kv_sink is not None:
+            kv_sink(k, v)
+        o, lse = ops.flash_attn(q, k, v, cu, max_seqlen, causal=True, scale=self.scale)
+        h1 = ops.linear(o.reshape(T, self.nq * self.D), w["o_w"], residual=x, out_dtype=x.dtype)
+        hn, r2 = ops.rms_norm(h1, w["post_norm"], self.eps)
+        act, pre = ops.linear_swiglu(hn, w["gu_w"], save_pre=save)
+        out = ops.linear(act, w["down_w"], residual=h1, out_dtype=x.dtype)
+        ctx = _LayerCtx(x, xn, r1, qkv, q, k, v, rq, rk, o, lse, h1, hn, r2, act, pre) if save else None
+        return out, ctx
+
+    # ---------------------------------------------------------------- layer bwd
+    def layer_backward(self, w, g, c: _LayerCtx, dy: torch.Tensor, pos, cu, max_seqlen) -> torch.Tensor:
+        T = dy.shape[0]
+        dt = dy.dtype
+        # MLP
+        if g is not None:
+            ops.grad_weight(dy, c.act, accumulate=g["down_w"])
+        d_act = ops.grad_input(dy, w["down_w"], out_dtype=dt)
+        d_pre = ops.swiglu_bwd(d_act, c.pre)
+        if g is not None:
+            ops.grad_weight(d_pre, c.hn, accumulate=g["gu_w"])
+        d_hn = ops.grad_input(d_pre, w["gu_w"], out_dtype=dt)
+        d_h1 = ops.rms_norm_bwd(d_hn, c.h1, w["post_norm"], c.r2, dw_accum=None if g is None else g["post_norm"])
+        d_h1 = (d_h1.float() + dy.float()).to(dt)
+        # attention
+        o2 = c.o.reshape(T, self.nq * self.D)
+        if g is not None:
+            ops.grad_weight(d_h1, o2, accumulate=g["o_w"])
+        d_o = ops.grad_input(d_h1, w["o_w"], out_dtype=dt).view(T, self.nq, self.D)
+        dq, dk, dv = ops.flash_attn_bwd(d_o, c.q, c.k, c.v, c.o, c.lse, cu, max_seqlen, causal=True, scale=self.scale)
+        d_qkv = ops.qk_norm_rope_bwd(dq, dk, dv, c.qkv, w["q_norm"], w["k_norm"], pos, c.rq, c.rk, self.rope,
+                                     n_q=self.nq, n_kv=self.nkv, eps=self.eps,
+                                     dqw_accum=None if g is None else g["q_norm"],
+                                     dkw_accum=None if g is None else g["k_norm"])
+        if g is not None:
+            ops.grad_weight(d_qkv, c.xn, accumulate=g["qkv_w"])
+            g["qkv_b"].add_(d_qkv.float().sum(0))
+        d_xn = ops.grad_input(d_qkv, w["qkv_w"], out_dtype=dt)
+        dx = ops.rms_norm_bwd(d_xn, c.x, w["input_norm"], c.r1, dw_accum=None if g is None else g["input_norm"])
+        return (dx.float() + d_h1.float()).to(dt)
+
+    # ---------------------------------------------------------------- full passes
+    def hidden_states(self, params, batch: PackedBatch, *, save: bool = False, ctx: Optional[TrainCtx] = None,
+                      kv_writer=None) -> torch.Tensor:
+        h = self.embed_inputs(params, batch)
+        for i in range(self.n_layers):
+            w = self._w(params, f"layer{i}")
+            sink = (lambda k, v, i=i: kv_writer(i, k, v)) if kv_writer is not None else None
+            h, lc = self.layer_forward(w, h, batch.pos, batch.cu_seqlens, batch.max_seqlen, save, sink)
+            params.release(f"layer{i}")
+            if ctx is not None:
+                ctx.layers.append(lc)
+            h = self._deepstack(h, batch, i)
+        return h
+
+    def forward_logprobs(self, params, batch: PackedBatch, *, save: bool = False):
+        """Per-loss-row (logp, entropy); with ``save`` also the TrainCtx for ``backward``."""
+        ctx = TrainCtx(batch=batch) if save else None
+        h = self.hidden_states(params, batch, save=save, ctx=ctx)
+        head = self._w(params, "head")
+        hs = h.index_select(0, batch.loss_rows)
+        hn, r = ops.rms_norm(hs, head["final_norm"], self.eps)
+        logp, ent, lse = ops.vocab_logprob(hn, head["lm_head"], batch.targets)
+        params.release("head")
+        if ctx is not None:
+            ctx.h_loss, ctx.hn_loss, ctx.r_final, ctx.lse, ctx.ent = hs, hn, r, lse, ent
+        return logp, ent, ctx
+
+    def backward(self, params, ctx: TrainCtx, g_logp: torch.Tensor, g_ent: torch.Tensor) -> None:
+        """Accumulate parameter gradients of ``sum(g_logp*logp + g_ent*entropy)``."""
+        b = ctx.batch
+        head = self._w(params, "head")
+        gh = self._g(params, "head")
+        dw_lm = gh["lm_head"] if gh is not None else torch.zeros_like(head["lm_head"], dtype=torch.float32)
+        d_hn = ops.vocab_logprob_bwd(ctx.hn_loss, head["lm_head"], b.targets, ctx.lse, ctx.ent,
+                                     g_logp.float().contiguous(), g_ent.float().contiguous(), dw_lm)
+        d_hs = ops.rms_norm_bwd(d_hn, ctx.h_loss, head["final_norm"], ctx.r_final,
+                                dw_accum=None if gh is None else gh["final_norm"])
+        params.grad_done("head")
+        params.release("head")
+        T = b.tokens.shape[0]
+        dh = torch.zeros(T, self.H, dtype=d_hs.dtype, device=d_hs.device)
+        dh.index_copy_(0, b.loss_rows, d_hs)
+        for i in reversed(range(self.n_layers)):
+            w = self._w(params, f"layer{i}")
+            g = self._g(params, f"layer{i}")
+            dh = self.layer_backward(w, g, ctx.layers[i], dh, b.pos, b.cu_seqlens, b.max_seqlen)
+            ctx.layers[i] = None
+            params.grad_done(f"layer{i}")
+            params.release(f"layer{i}")
+        ge = self._g(params, "embed")
+        if ge is not None:
+            toks = b.tokens
+            if b.vision is not None and b.vis_rows.numel():
+                toks = toks.clone()
+                toks[b.vis_rows] = -1            # injected rows carry no embedding gradient
+            ops.embed_bwd(toks, dh, ge["embed"])
+            params.grad_done("embed")
+
+    # ---------------------------------------------------------------- inference
+    def final_logits(self, params, h_rows: torch.Tensor) -> torch.Tensor:
+        head = self._w(params, "head")
+        hn, _ = ops.rms_norm(h_rows, head["final_norm"], self.eps)
+        logits = ops.lm_logits(hn, head["lm_head"])
+        params.release("head")
+        return logits
+
+    def prefill(self, params, batch: PackedBatch, cache: KVCache, slots: torch.Tensor) -> torch.Tensor:
+        """Run the prompt, fill the KV cache rows ``slots[b]`` and return last-token logits [B, V] fp32."""
+        cu = batch.cu_seqlens
+        lens = (cu[1:] - cu[:-1]).to(torch.int64)
+        T = batch.tokens.shape[0]
+        seq_of_tok = torch.repeat_interleave(torch.arange(lens.numel(), device=cu.device), lens)
+        pos_in_seq = torch.arange(T, device=cu.device) - cu[:-1].to(torch.int64)[seq_of_tok]
+        slot_of_tok = slots.to(torch.int64)[seq_of_tok]
+
+        def writer(i, k, v):
+            ops.kv_write(k, v, cache.keys[i], cache.values[i], slot_of_tok, pos_in_seq)
+
+        h = self.hidden_states(params, batch, save=False, kv_writer=writer)
+        last = (cu[1:].to(torch.int64) - 1)
+        cache.lengths[slots.long()] = lens.to(torch.int32)
+        return self.final_logits(params, h.index_select(0, last))
+
+    def decode_hidden(self, params, tokens: torch.Tensor, cache: KVCache, rope_delta: torch.Tensor) -> torch.Tensor:
+        """One decode step for all B cache rows; appends k, v at ``cache.lengths`` (not advanced here)."""
+        e = self._w(params, "embed")["embed"]
+        x = ops.embed(tokens, e)
+        params.release("embed")
+        B = tokens.shape[0]
+        p1 = (cache.lengths.to(torch.int64) + rope_delta.to(torch.int64)).to(torch.int32)
+        pos = p1[None].expand(3, B).contiguous()
+        rows = torch.arange(B, device=tokens.device)
+        cur = cache.lengths.to(torch.int64)
+        lens_after = cache.lengths + 1
+        for i in range(self.n_layers):
+            w = self._w(params, f"layer{i}")
+            xn, _ = ops.rms_norm(x, w["input_norm"], self.eps)
+            qkv = ops.linear(xn, w["qkv_w"], bias=w["qkv_b"], out_dtype=x.dtype)
+            q, k, v, _, _ = ops.qk_norm_rope(qkv, w["q_norm"], w["k_norm"], pos, self.rope,
+                                             n_q=self.nq, n_kv=self.nkv, eps=self.eps)
+            ops.kv_write(k, v, cache.keys[i], cache.values[i], rows, cur)
+            o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale)
+            h1 = ops.linear(o.reshape(B, self.nq * self.D), w["o_w"], residual=x, out_dtype=x.dtype)
+            hn, _ = ops.rms_norm(h1, w["post_norm"], self.eps)
+            act, _ = ops.linear_swiglu(hn, w["gu_w"], save_pre=False)
+            x = ops.linear(act, w["down_w"], residual=h1, out_dtype=x.dtype)
+            params.release(f"layer{i}")
+        return x
+
+
+__all__ = ["VisionEmbeddings", "PackedBatch", "KVCache", "LocalParams", "TextDecoder", "TrainCtx"]

@@ -1,0 +1,112 @@
+"""Qwen3-VL vision tower executor (forward only; the tower is frozen during RL).
+
+HF-faithful architecture (``transformers`` ``Qwen3VLVisionModel``), which the
+reference approximates (reference ``models/qwen3vl/vision.py:178-331``; its
+RMSNorm/SwiGLU/windowed deviations are not reproduced):
+
+1. patch embedding: rows ``[N, C*Tp*P*P]`` -> ``[N, Hv]`` (Conv3d as one GEMM, with bias);
+2. + bilinearly interpolated learned position embedding (merge-window order);
+3. ``depth`` blocks: LayerNorm -> fused qkv (bias) -> 2-D rotary -> full
+   bidirectional attention within each image -> proj (+residual) ->
+   LayerNorm -> fc1 + GELU(tanh) -> fc2 (+residual);
+4. after blocks in ``deepstack_visual_indexes``: a post-shuffle merger
+   (2x2 concat -> LayerNorm(4Hv) -> fc1 -> GELU -> fc2) produces a deepstack feature;
+5. final merger: LayerNorm(Hv) -> 2x2 concat -> fc1 -> GELU -> fc2 -> ``[N/4, out]``.
+
+Every GEMM is ``vlmrl.ops.gemm`` (bias / GELU / residual fused in the epilogue)
+and attention is ``vlmrl.ops.flash_attn`` over per-image ``cu_seqlens``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from vlmrl import ops
+from vlmrl.models.qwen3vl.config import Qwen3VLSpec
+from vlmrl.models.qwen3vl.params import vision_layout
+from vlmrl.models.qwen3vl.rope import pos_embed_interp_index, vision_rotary_pos
+
+
+@dataclass
+class VisionInputs:
+    """Device-side metadata of a batch of images (built once per grid set)."""
+    rc: torch.Tensor           # [N, 2] int32 (row, col) per patch
+    pos_idx: torch.Tensor      # [4, N] int64 bilinear corners
+    pos_w: torch.Tensor        # [4, N] fp32 weights
+    cu_seqlens: torch.Tensor   # [images+1] int32
+    max_seqlen: int
+
+
+def prepare_vision_inputs(spec: Qwen3VLSpec, grids: Sequence[Tuple[int, int, int]], device) -> VisionInputs:
+    v = spec.vision
+    rc = torch.from_numpy(vision_rotary_pos(grids, v.spatial_merge_size).astype(np.int32)).to(device)
+    if v.num_position_embeddings:
+        side = int(round(float(v.num_position_embeddings) ** 0.5))
+        idx, w = pos_embed_interp_index(grids, side, v.spatial_merge_size)
+        pos_idx, pos_w = torch.from_numpy(idx).to(device), torch.from_numpy(w).to(device)
+    else:
+        pos_idx = pos_w = torch.empty(0, device=device)
+    lens = [int(t) * int(h) * int(w) for t, h, w in grids]
+    # one attention sequence per frame (HF repeats h*w for each of the t frames)
+    seq = []
+    for t, h, w in grids:
+        seq += [int(h) * int(w)] * int(t)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(seq)]).astype(np.int32), device=device)
+    return VisionInputs(rc=rc, pos_idx=pos_idx, pos_w=pos_w, cu_seqlens=cu, max_seqlen=max(seq) if seq else 0)
+
+
+class VisionTower:
+    def __init__(self, spec: Qwen3VLSpec):
+        if spec.vision is None:
+            raise ValueError("spec has no vision tower")
+        self.spec = spec
+        self.v = spec.vision
+        self.layout = vision_layout(spec)
+
+    def _merge(self, x: torch.Tensor, p: Dict[str, torch.Tensor], prefix: str, post_norm: bool) -> torch.Tensor:
+        M = self.v.merged_hidden_size
+        eps = 1e-6
+        if post_norm:
+            x = ops.layer_norm(x.reshape(-1, M), p[prefix + "norm_w"], p[prefix + "norm_b"], eps)
+        else:
+            x = ops.layer_norm(x, p[prefix + "norm_w"], p[prefix + "norm_b"], eps).reshape(-1, M)
+        h = ops.gemm(x, p[prefix + "fc1_w"], bias=p[prefix + "fc1_b"], epilogue=ops.EPI_GELU_ERF, out_dtype=x.dtype)
+        return ops.gemm(h, p[prefix + "fc2_w"], bias=p[prefix + "fc2_b"], out_dtype=x.dtype)
+
+    @torch.no_grad()
+    def forward(self, flat: torch.Tensor, pixel_rows: torch.Tensor, vin: VisionInputs):
+        """pixel_rows [N, patch_volume] -> (merged [N/4, out], [deepstack_k [N/4, out]])."""
+        v = self.v
+        p = self.layout.views(flat)
+        dt = flat.dtype
+        x = pixel_rows.to(dt)
+        x = ops.gemm(x, p["patch_w"], bias=p["patch_b"], out_dtype=dt)
+        if "pos_embed" in p and vin.pos_idx.numel():
+            pe = (p["pos_embed"][vin.pos_idx].float() * vin.pos_w[..., None]).sum(0)
+            x = (x.float() + pe).to(dt)
+        H, nh = v.hidden_size, v.num_heads
+        hd = H // nh
+        deep_idx = list(v.deepstack_visual_indexes)
+        deep: List[torch.Tensor] = []
+        act = ops.EPI_GELU_TANH if "tanh" in v.hidden_act else ops.EPI_GELU_ERF
+        for j in range(v.depth):
+            b = f"b{j}."
+            xn = ops.layer_norm(x, p[b + "n1_w"], p[b + "n1_b"], 1e-6)
+            qkv = ops.gemm(xn, p[b + "qkv_w"], bias=p[b + "qkv_b"], out_dtype=dt)
+            q, k, vv = ops.vision_rope(qkv, vin.rc, n_heads=nh, head_dim=hd)
+            o, _ = ops.flash_attn(q, k, vv, vin.cu_seqlens, vin.max_seqlen, causal=False)
+            x = ops.gemm(o.reshape(-1, H), p[b + "proj_w"], bias=p[b + "proj_b"], residual=x, out_dtype=dt)
+            xn = ops.layer_norm(x, p[b + "n2_w"], p[b + "n2_b"], 1e-6)
+            h = ops.gemm(xn, p[b + "fc1_w"], bias=p[b + "fc1_b"], epilogue=act, out_dtype=dt)
+            x = ops.gemm(h, p[b + "fc2_w"], bias=p[b + "fc2_b"], residual=x, out_dtype=dt)
+            if j in deep_idx:
+                deep.append(self._merge(x, p, f"d{deep_idx.index(j)}.", post_norm=True))
+        merged = self._merge(x, p, "m.", post_norm=False)
+        return merged, deep
+
+
+__all__ = ["VisionInputs", "prepare_vision_inputs", "VisionTower"]

@@ -1,0 +1,356 @@
+"""Hot ops: hand-written sm_100a CUDA kernels (``vlmrl._C``) with PyTorch oracles.
+
+Every public function dispatches on the device of its first tensor argument:
+CUDA tensors run the native kernel (and raise if the extension is not built —
+there is no silent fallback on a GPU), CPU tensors run the fp32 oracle in
+``vlmrl.ops.reference`` (the CPU/gloo test path).  Shapes and layouts are
+documented in ``vlmrl.ops.reference``.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+from vlmrl.ops import reference as ref
+from vlmrl.ops._ext import ext, has_ext
+
+# GEMM epilogue codes (must match csrc/gemm_sm100.cu)
+EPI_STORE = 0
+EPI_SWIGLU = 1
+EPI_GELU_TANH = 2
+EPI_GELU_ERF = 3
+
+
+def _cuda(x: torch.Tensor) -> bool:
+    return x.is_cuda
+
+
+def _opt(x: Optional[torch.Tensor]):
+    return x if x is not None else torch.Tensor()
+
+
+# ------------------------------------------------------------------ GEMM family
+def gemm(a: torch.Tensor, b: torch.Tensor, *, a_kmajor: bool = True, b_kmajor: bool = True,
+         bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None, alpha: float = 1.0,
+         out_dtype: torch.dtype = torch.bfloat16, accumulate: Optional[torch.Tensor] = None,
+         out: Optional[torch.Tensor] = None, epilogue: int = EPI_STORE,
+         aux: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """D = alpha * A·Bᵀ (+bias)(+residual)(+=accumulate) with an optional activation epilogue.
+
+    ``epilogue=EPI_SWIGLU`` treats column pairs (2j, 2j+1) as (gate, up) and
+    writes ``silu(gate)*up`` into an ``[M, N/2]`` output; ``aux`` (optional
+    ``[M, N]``) then receives the pre-activation.
+    """
+    M = a.shape[0] if a_kmajor else a.shape[1]
+    N = b.shape[0] if b_kmajor else b.shape[1]
+    if not _cuda(a):
+        if epilogue == EPI_SWIGLU:
+            pre = ref.gemm(a, b, a_kmajor=a_kmajor, b_kmajor=b_kmajor, bias=bias, alpha=alpha, out_dtype=torch.float32)
+            if aux is not None:
+                aux.copy_(pre.to(aux.dtype))
+            res = ref.swiglu_interleaved(pre).to(out_dtype)
+        elif epilogue in (EPI_GELU_TANH, EPI_GELU_ERF):
+            pre = ref.gemm(a, b, a_kmajor=a_kmajor, b_kmajor=b_kmajor, bias=bias, alpha=alpha, out_dtype=torch.float32)
+            res = ref.gelu(pre, "tanh" if epilogue == EPI_GELU_TANH else "none").to(out_dtype)
+        else:
+            res = ref.gemm(a, b, a_kmajor=a_kmajor, b_kmajor=b_kmajor, bias=bias, residual=residual, alpha=alpha,
+                           out_dtype=out_dtype, accumulate=accumulate)
+        if out is not None and accumulate is None:
+            out.copy_(res)
+            return out
+        return res
+    if accumulate is not None:
+        d = accumulate
+    elif out is not None:
+        d = out
+    else:
+        width = N // 2 if epilogue == EPI_SWIGLU else N
+        d = torch.empty(M, width, dtype=out_dtype, device=a.device)
+    ext().gemm(a, b, d, _opt(bias), _opt(residual), _opt(aux), bool(a_kmajor), bool(b_kmajor), float(alpha),
+               int(epilogue), accumulate is not None)
+    return d
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias=None, residual=None, out_dtype=torch.bfloat16, out=None):
+    """y = x @ w.T (+ bias) (+ residual)."""
+    return gemm(x, w, bias=bias, residual=residual, out_dtype=out_dtype, out=out)
+
+
+def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, save_pre: bool = True):
+    """act [M,F] = silu(gate)*up for interleaved w_gu [2F,K]; also returns pre [M,2F] when ``save_pre``."""
+    pre = torch.empty(x.shape[0], w_gu.shape[0], dtype=x.dtype, device=x.device) if save_pre else None
+    act = gemm(x, w_gu, epilogue=EPI_SWIGLU, aux=pre, out_dtype=x.dtype)
+    return act, pre
+
+
+def grad_input(dy: torch.Tensor, w: torch.Tensor, out_dtype=torch.bfloat16, out=None):
+    """dX [M,K] = dY [M,N] @ W [N,K]."""
+    return gemm(dy, w, b_kmajor=False, out_dtype=out_dtype, out=out)
+
+
+def grad_weight(dy: torch.Tensor, x: torch.Tensor, accumulate: Optional[torch.Tensor] = None,
+                out_dtype=torch.float32):
+    """dW [N,K] (+)= dY[M,N]ᵀ @ X[M,K] (fp32 accumulation buffer)."""
+    return gemm(dy, x, a_kmajor=False, b_kmajor=False, out_dtype=out_dtype, accumulate=accumulate)
+
+
+def swiglu_bwd(d_act: torch.Tensor, pre: torch.Tensor) -> torch.Tensor:
+    if not _cuda(d_act):
+        return ref.swiglu_bwd(d_act, pre)
+    out = torch.empty_like(pre)
+    ext().swiglu_bwd(d_act, pre, out)
+    return out
+
+
+# ------------------------------------------------------------------ norms
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    if not _cuda(x):
+        return ref.rms_norm(x, w, eps)
+    y = torch.empty_like(x)
+    rstd = torch.empty(x.shape[0], dtype=torch.float32, device=x.device)
+    ext().rms_norm_fwd(x, w, y, rstd, float(eps))
+    return y, rstd
+
+
+def rms_norm_bwd(dy, x, w, rstd, dw_accum: Optional[torch.Tensor] = None):
+    """Returns dx; adds the weight gradient into ``dw_accum`` (fp32 [H]) when given."""
+    if not _cuda(x):
+        dx, dw = ref.rms_norm_bwd(dy, x, w, rstd)
+        if dw_accum is not None:
+            dw_accum.add_(dw.to(dw_accum.dtype))
+        return dx
+    dx = torch.empty_like(x)
+    ext().rms_norm_bwd(dy, x, w, rstd, dx, _opt(dw_accum))
+    return dx
+
+
+def layer_norm(x, w, b, eps: float):
+    if not _cuda(x):
+        return ref.layer_norm(x, w, b, eps)
+    y = torch.empty_like(x)
+    ext().layer_norm_fwd(x, w, _opt(b), y, float(eps))
+    return y
+
+
+# ------------------------------------------------------------------ rotary
+class RopeCfg:
+    """Static rotary parameters of a text decoder (head_dim, theta, MRoPE sections, layout)."""
+
+    def __init__(self, head_dim: int, theta: float, section: Sequence[int], interleaved: bool):
+        self.head_dim = int(head_dim)
+        self.theta = float(theta)
+        self.section = tuple(int(s) for s in section)
+        self.interleaved = bool(interleaved)
+        self._tables = {}
+
+    def device_tables(self, device) -> Tuple[torch.Tensor, torch.Tensor]:
+        """(inv_freq fp32 [D/2], axis int32 [D/2]) resident on ``device``."""
+        key = str(device)
+        if key not in self._tables:
+            from vlmrl.models.qwen3vl.rope import inv_freq, mrope_axis_map
+
+            f = torch.from_numpy(inv_freq(self.head_dim, self.theta)).to(device)
+            a = torch.from_numpy(mrope_axis_map(self.section, self.head_dim // 2, self.interleaved)).to(device)
+            self._tables[key] = (f, a.to(torch.int32))
+        return self._tables[key]
+
+
+def qk_norm_rope(qkv, q_w, k_w, pos, rope: RopeCfg, *, n_q: int, n_kv: int, eps: float):
+    if not _cuda(qkv):
+        return ref.qk_norm_rope(qkv, q_w, k_w, pos, n_q=n_q, n_kv=n_kv, head_dim=rope.head_dim, theta=rope.theta,
+                                section=rope.section, interleaved=rope.interleaved, eps=eps)
+    T, D = qkv.shape[0], rope.head_dim
+    q = torch.empty(T, n_q, D, dtype=qkv.dtype, device=qkv.device)
+    k = torch.empty(T, n_kv, D, dtype=qkv.dtype, device=qkv.device)
+    v = torch.empty(T, n_kv, D, dtype=qkv.dtype, device=qkv.device)
+    rq = torch.empty(T, n_q, dtype=torch.float32, device=qkv.device)
+    rk = torch.empty(T, n_kv, dtype=torch.float32, device=qkv.device)
+    f, ax = rope.device_tables(qkv.device)
+    ext().qk_norm_rope_fwd(qkv, q_w, k_w, pos, f, ax, q, k, v, rq, rk, n_q, n_kv, float(eps))
+    return q, k, v, rq, rk
+
+
+def qk_norm_rope_bwd(dq, dk, dv, qkv, q_w, k_w, pos, rq, rk, rope: RopeCfg, *, n_q, n_kv, eps,
+                     dqw_accum=None, dkw_accum=None):
+    if not _cuda(qkv):
+        dqkv, dqw, dkw = ref.qk_norm_rope_bwd(dq, dk, dv, qkv, q_w, k_w, pos, rq, rk, n_q=n_q, n_kv=n_kv,
+                                              head_dim=rope.head_dim, theta=rope.theta, section=rope.section,
+                                              interleaved=rope.interleaved, eps=eps)
+        if dqw_accum is not None:
+            dqw_accum.add_(dqw)
+        if dkw_accum is not None:
+            dkw_accum.add_(dkw)
+        return dqkv
+    dqkv = torch.empty_like(qkv)
+    f, ax = rope.device_tables(qkv.device)
+    ext().qk_norm_rope_bwd(dq, dk, dv, qkv, q_w, k_w, pos, f, ax, rq, rk, dqkv, _opt(dqw_accum), _opt(dkw_accum),
+                           n_q, n_kv, float(eps))
+    return dqkv
+
+
+def vision_rope(qkv, rc, *, n_heads: int, head_dim: int):
+    if not _cuda(qkv):
+        return ref.vision_rope(qkv, rc, n_heads=n_heads, head_dim=head_dim)
+    N = qkv.shape[0]
+    q = torch.empty(N, n_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
+    k = torch.empty_like(q)
+    v = torch.empty_like(q)
+    ext().vision_rope(qkv, rc, q, k, v, n_heads)
+    return q, k, v
+
+
+# ------------------------------------------------------------------ attention
+def flash_attn(q, k, v, cu_seqlens, max_seqlen: int, *, causal: bool, scale: Optional[float] = None):
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if not _cuda(q):
+        return ref.flash_attn(q, k, v, cu_seqlens, max_seqlen, causal=causal, scale=scale)
+    o = torch.empty_like(q)
+    lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=q.device)
+    ext().flash_attn_fwd(q, k, v, cu_seqlens, o, lse, int(max_seqlen), bool(causal), float(scale))
+    return o, lse
+
+
+def flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen: int, *, causal: bool, scale: Optional[float] = None):
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if not _cuda(q):
+        return ref.flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen, causal=causal, scale=scale)
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    ext().flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, dq, dk, dv, int(max_seqlen), bool(causal), float(scale))
+    return dq, dk, dv
+
+
+def decode_attn(q, k_cache, v_cache, lengths, *, scale: Optional[float] = None, out=None):
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if not _cuda(q):
+        return ref.decode_attn(q, k_cache, v_cache, lengths, scale=scale)
+    o = out if out is not None else torch.empty_like(q)
+    ext().decode_attn(q, k_cache, v_cache, lengths, o, float(scale))
+    return o
+
+
+def kv_write(k, v, k_cache, v_cache, seq_idx, pos_idx):
+    """Scatter packed k, v [T,Hkv,D] into caches [B,Hkv,Tmax,D] at (seq_idx[t], pos_idx[t])."""
+    if not _cuda(k):
+        si, pi = seq_idx.long(), pos_idx.long()
+        k_cache[si, :, pi] = k.to(k_cache.dtype)
+        v_cache[si, :, pi] = v.to(v_cache.dtype)
+        return
+    ext().kv_write(k, v, k_cache, v_cache, seq_idx, pos_idx)
+
+
+# ------------------------------------------------------------------ embedding
+def embed(tokens, table, out=None):
+    if not _cuda(table):
+        return ref.embed(tokens, table)
+    o = out if out is not None else torch.empty(tokens.shape[0], table.shape[1], dtype=table.dtype, device=table.device)
+    ext().embed(tokens, table, o)
+    return o
+
+
+def scatter_rows_(h, rows, src, add: bool):
+    """In place: h[rows] = src (or += src)."""
+    if not _cuda(h):
+        h.copy_(ref.scatter_rows(h, rows, src, add))
+        return h
+    ext().scatter_rows(h, rows, src, bool(add))
+    return h
+
+
+def embed_bwd(tokens, dh, dtable):
+    if not _cuda(dh):
+        return ref.embed_bwd(tokens, dh, dtable)
+    ext().embed_bwd(tokens, dh, dtable)
+    return dtable
+
+
+# ------------------------------------------------------------------ vocab
+def vocab_logprob(h, w, targets):
+    """(logp[target], entropy, lse) fp32 [M] without materialising fp32 logits."""
+    if not _cuda(h):
+        return ref.vocab_logprob(h, w, targets)
+    M = h.shape[0]
+    logp = torch.empty(M, dtype=torch.float32, device=h.device)
+    ent = torch.empty_like(logp)
+    lse = torch.empty_like(logp)
+    ext().vocab_logprob_fwd(h, w, targets, logp, ent, lse)
+    return logp, ent, lse
+
+
+def vocab_logprob_bwd(h, w, targets, lse, ent, g_logp, g_ent, dw_accum: torch.Tensor):
+    """Returns dh (h.dtype); accumulates dW into ``dw_accum`` (fp32 [V,H])."""
+    if not _cuda(h):
+        dh, dw = ref.vocab_logprob_bwd(h, w, targets, lse, ent, g_logp, g_ent)
+        dw_accum.add_(dw)
+        return dh.to(h.dtype)
+    dh = torch.empty_like(h)
+    ext().vocab_logprob_bwd(h, w, targets, lse, ent, g_logp, g_ent, dh, dw_accum)
+    return dh
+
+
+def lm_logits(h, w, out=None):
+    if not _cuda(h):
+        return ref.lm_logits(h, w)
+    return gemm(h, w, out_dtype=torch.float32, out=out)
+
+
+# ------------------------------------------------------------------ sampling
+def sample(logits, *, temperature: float, top_k: int, top_p: float, seed: int, step, row_offset: int = 0,
+           out_tokens=None, out_logprobs=None):
+    """``step`` may be an int or a 1-element int64 CUDA tensor (graph-capturable counter)."""
+    if not _cuda(logits):
+        s = int(step.item()) if torch.is_tensor(step) else int(step)
+        return ref.sample(logits, temperature=temperature, top_k=top_k, top_p=top_p, seed=seed, step=s,
+                          row_offset=row_offset)
+    B = logits.shape[0]
+    tok = out_tokens if out_tokens is not None else torch.empty(B, dtype=torch.int64, device=logits.device)
+    lp = out_logprobs if out_logprobs is not None else torch.empty(B, dtype=torch.float32, device=logits.device)
+    if not torch.is_tensor(step):
+        step = torch.tensor([int(step)], dtype=torch.int64, device=logits.device)
+    ext().sample(logits, tok, lp, step, float(temperature), int(top_k or 0), float(top_p or 0.0),
+                 int(seed) & ((1 << 63) - 1), int(row_offset))
+    return tok, lp
+
+
+# ------------------------------------------------------------------ optimizer
+def adamw_(p, g, m, v, *, lr, beta1, beta2, eps, weight_decay, step, grad_scale=1.0, p_half=None):
+    if not _cuda(p):
+        return ref.adamw_(p, g, m, v, lr=lr, beta1=beta1, beta2=beta2, eps=eps, weight_decay=weight_decay, step=step,
+                          grad_scale=grad_scale, p_half=p_half)
+    if torch.is_tensor(grad_scale):
+        scale_t = grad_scale
+    else:
+        scale_t = torch.tensor([float(grad_scale)], dtype=torch.float32, device=p.device)
+    ext().adamw(p, g, m, v, _opt(p_half), scale_t, float(lr), float(beta1), float(beta2), float(eps),
+                float(weight_decay), int(step))
+
+
+def sq_norm(x, out: Optional[torch.Tensor] = None):
+    """Sum of squares in fp32; with ``out`` ([1] fp32) the result is added into it."""
+    if not _cuda(x):
+        r = ref.sq_norm(x)
+        if out is not None:
+            out.add_(r)
+            return out
+        return r
+    o = out if out is not None else torch.zeros(1, dtype=torch.float32, device=x.device)
+    ext().sq_norm_acc(x, o)
+    return o
+
+
+def patchify_uint8(images, *, patch: int, temporal: int, merge: int, mean, std, out_dtype=torch.bfloat16):
+    if not _cuda(images):
+        return ref.patchify_uint8(images, patch=patch, temporal=temporal, merge=merge, mean=mean, std=std).to(out_dtype)
+    N, H, W, C = images.shape
+    rows = N * (H // patch) * (W // patch)
+    out = torch.empty(rows, C * temporal * patch * patch, dtype=out_dtype, device=images.device)
+    ms = torch.tensor(list(mean) + list(std), dtype=torch.float32, device=images.device)
+    ext().patchify(images, ms, out, patch, temporal, merge)
+    return out
+
+
+__all__ = [n for n in dir() if not n.startswith("_")]
