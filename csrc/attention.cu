@@ -1,0 +1,773 @@
+// Varlen GQA flash attention (forward + backward) and KV-cache decode attention.
+//
+// Forward: one CTA = 64 queries of one (sequence, q-head); 4 warps x 16 query rows;
+// K/V tiles of 64 keys are double-buffered in swizzled shared memory with
+// cp.async; S = Q.K^T and O += P.V run on bf16 mma.sync m16n8k16 with fp32
+// accumulation; online softmax in base 2.  Outputs O (bf16) and the natural-log
+// LSE [Hq, T] for the backward.
+//
+// Backward (no atomics): (1) delta = rowsum(dO * O); (2) one CTA per
+// (sequence, 64-key block, kv-head) accumulates dK, dV over every q-head of the
+// GQA group and every q block; (3) one CTA per (sequence, 64-query block, q-head)
+// recomputes P and dP to form dQ.
+//
+// Decode: one CTA per (sequence, kv-head) scores all cached keys for the
+// group's q-heads, softmaxes in shared memory and reduces P.V across warps.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace vlm {
+
+using bf16 = __nv_bfloat16;
+
+// ------------------------------------------------------------------ mma / ldmatrix / cp.async
+VLM_DEV void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+VLM_DEV void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+VLM_DEV void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+VLM_DEV void cp_async16(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(valid ? 16 : 0)
+               : "memory");
+}
+VLM_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+VLM_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// [rows][D] bf16 tile with the 16-byte chunks of each row XOR-swizzled by the row index.
+template <int D>
+struct Tile {
+  static constexpr int CH = D / 8;
+  static constexpr int SW = CH < 8 ? CH : 8;
+  VLM_DEV static int off(int row, int col) { return row * D + ((((col >> 3) ^ (row & (SW - 1)))) << 3) + (col & 7); }
+};
+
+// Load `rows` rows (row r from token t0+r of a [T, H, D] tensor at head h) into a swizzled tile; rows past `limit`
+// are zero-filled.
+template <int D>
+VLM_DEV void load_rows(bf16* s, const bf16* g, int t0, int rows, int limit, int H, int h, int tid, int nthr) {
+  constexpr int CH = D / 8;
+  for (int i = tid; i < rows * CH; i += nthr) {
+    const int r = i / CH, c = i % CH;
+    const bool ok = t0 + r < limit;
+    const bf16* src = g + ((static_cast<int64_t>(ok ? t0 + r : 0) * H + h) * D + c * 8);
+    cp_async16(s + Tile<D>::off(r, c * 8), src, ok);
+  }
+}
+
+// A fragment (16 x 16) at (r0, c0) of a swizzled [rows][D] tile.
+template <int D>
+VLM_DEV void frag_a(uint32_t (&a)[4], const bf16* s, int r0, int c0, int lane) {
+  const int r = r0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+  const int c = c0 + (lane >> 4) * 8;
+  ldsm_x4(a, s + Tile<D>::off(r, c));
+}
+// B fragments for two n-blocks (n0, n0+8) x k-step (k0..k0+15), where the tile is stored [n][k]
+// (rows = n, contiguous k).  b[0],b[1] -> n-block n0; b[2],b[3] -> n-block n0+8.
+template <int D>
+VLM_DEV void frag_b_nk(uint32_t (&b)[4], const bf16* s, int n0, int k0, int lane) {
+  const int r = n0 + (lane & 7) + (lane >> 4) * 8;
+  const int c = k0 + ((lane >> 3) & 1) * 8;
+  ldsm_x4(b, s + Tile<D>::off(r, c));
+}
+// B fragments for two n-blocks (n0, n0+8) x k-step, where the tile is stored [k][n] (rows = k).
+template <int D>
+VLM_DEV void frag_b_kn(uint32_t (&b)[4], const bf16* s, int k0, int n0, int lane) {
+  const int r = k0 + (lane & 7) + ((lane >> 3) & 1) * 8;
+  const int c = n0 + (lane >> 4) * 8;
+  ldsm_x4_t(b, s + Tile<D>::off(r, c));
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// ------------------------------------------------------------------ forward
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(128) flash_fwd_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
+                                                        const bf16* __restrict__ V, const int* __restrict__ cu,
+                                                        bf16* __restrict__ O, float* __restrict__ LSE, int Hq, int Hkv,
+                                                        int T, float scale_log2) {
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int s0 = cu[b], L = cu[b + 1] - s0;
+  const int q0 = qb * 64;
+  if (q0 >= L) return;
+  const int hk = h / (Hq / Hkv);
+  extern __shared__ __align__(128) uint8_t smem_bytes[];
+  bf16* sQ = reinterpret_cast<bf16*>(smem_bytes);
+  bf16* sK = sQ + 64 * D;
+  bf16* sV = sK + 2 * 64 * D;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tq = lane & 3;
+
+  const bf16* Qs = Q + static_cast<int64_t>(s0) * Hq * D;
+  const bf16* Ks = K + static_cast<int64_t>(s0) * Hkv * D;
+  const bf16* Vs = V + static_cast<int64_t>(s0) * Hkv * D;
+  load_rows<D>(sQ, Qs, q0, 64, L, Hq, h, tid, 128);
+  const int nkb = CAUSAL ? min((L + 63) / 64, qb + 1) : (L + 63) / 64;
+  load_rows<D>(sK, Ks, 0, 64, L, Hkv, hk, tid, 128);
+  load_rows<D>(sV, Vs, 0, 64, L, Hkv, hk, tid, 128);
+  cp_async_commit();
+
+  float acc[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const int row0 = q0 + warp * 16 + g, row1 = row0 + 8;
+
+  for (int j = 0; j < nkb; ++j) {
+    const int buf = j & 1;
+    if (j + 1 < nkb) {
+      load_rows<D>(sK + (buf ^ 1) * 64 * D, Ks, (j + 1) * 64, 64, L, Hkv, hk, tid, 128);
+      load_rows<D>(sV + (buf ^ 1) * 64 * D, Vs, (j + 1) * 64, 64, L, Hkv, hk, tid, 128);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const bf16* k_t = sK + buf * 64 * D;
+    const bf16* v_t = sV + buf * 64 * D;
+    float s[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4];
+      frag_a<D>(a, sQ, warp * 16, kk * 16, lane);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t bb[4];
+        frag_b_nk<D>(bb, k_t, np * 16, kk * 16, lane);
+        mma_bf16(s[2 * np], a, bb[0], bb[1]);
+        mma_bf16(s[2 * np + 1], a, bb[2], bb[3]);
+      }
+    }
+    // scale + mask + online softmax
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = j * 64 + nb * 8 + 2 * tq + e;
+        const bool bad0 = key >= L || (CAUSAL && key > row0);
+        const bool bad1 = key >= L || (CAUSAL && key > row1);
+        s[nb][e] = bad0 ? -INFINITY : s[nb][e] * scale_log2;
+        s[nb][2 + e] = bad1 ? -INFINITY : s[nb][2 + e] * scale_log2;
+        mx0 = fmaxf(mx0, s[nb][e]);
+        mx1 = fmaxf(mx1, s[nb][2 + e]);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float base0 = mn0 == -INFINITY ? 0.f : mn0, base1 = mn1 == -INFINITY ? 0.f : mn1;
+    const float al0 = exp2f(m0 - base0), al1 = exp2f(m1 - base1);
+    m0 = mn0;
+    m1 = mn1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+      s[nb][0] = exp2f(s[nb][0] - base0);
+      s[nb][1] = exp2f(s[nb][1] - base0);
+      s[nb][2] = exp2f(s[nb][2] - base1);
+      s[nb][3] = exp2f(s[nb][3] - base1);
+      ps0 += s[nb][0] + s[nb][1];
+      ps1 += s[nb][2] + s[nb][3];
+    }
+    l0 = l0 * al0 + ps0;
+    l1 = l1 * al1 + ps1;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      acc[i][0] *= al0;
+      acc[i][1] *= al0;
+      acc[i][2] *= al1;
+      acc[i][3] *= al1;
+    }
+    // O += P . V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t a[4];
+      a[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+      a[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+      a[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      a[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        uint32_t bb[4];
+        frag_b_kn<D>(bb, v_t, kk * 16, dp * 16, lane);
+        mma_bf16(acc[2 * dp], a, bb[0], bb[1]);
+        mma_bf16(acc[2 * dp + 1], a, bb[2], bb[3]);
+      }
+    }
+    __syncthreads();
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+#pragma unroll
+  for (int nb = 0; nb < D / 8; ++nb) {
+    const int col = nb * 8 + 2 * tq;
+    if (row0 < L)
+      *reinterpret_cast<uint32_t*>(O + ((static_cast<int64_t>(s0 + row0) * Hq + h) * D + col)) =
+          pack_bf16x2(acc[nb][0] * inv0, acc[nb][1] * inv0);
+    if (row1 < L)
+      *reinterpret_cast<uint32_t*>(O + ((static_cast<int64_t>(s0 + row1) * Hq + h) * D + col)) =
+          pack_bf16x2(acc[nb][2] * inv1, acc[nb][3] * inv1);
+  }
+  if (tq == 0) {
+    if (row0 < L) LSE[static_cast<int64_t>(h) * T + s0 + row0] = l0 > 0.f ? (m0 + log2f(l0)) * kLn2 : -INFINITY;
+    if (row1 < L) LSE[static_cast<int64_t>(h) * T + s0 + row1] = l1 > 0.f ? (m1 + log2f(l1)) * kLn2 : -INFINITY;
+  }
+}
+
+// ------------------------------------------------------------------ backward: delta = rowsum(dO * O)
+__global__ void attn_delta_kernel(const bf16* __restrict__ dO, const bf16* __restrict__ O, float* __restrict__ delta,
+                                  int T, int H, int D) {
+  const int64_t w = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= static_cast<int64_t>(T) * H) return;
+  const int t = static_cast<int>(w / H), h = static_cast<int>(w % H);
+  const bf16* a = dO + w * D;
+  const bf16* o = O + w * D;
+  float s = 0.f;
+  for (int c = lane; c < D; c += 32) s += bf2f(a[c]) * bf2f(o[c]);
+  s = warp_sum(s);
+  if (lane == 0) delta[static_cast<int64_t>(h) * T + t] = s;
+}
+
+// ------------------------------------------------------------------ backward: dK, dV
+// CTA = (64-key block, kv-head, sequence); warp w owns keys [16w, 16w+16).  Queries are
+// processed in chunks of 32 for every q-head of the GQA group.
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(128) flash_bwd_dkdv_kernel(
+    const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __restrict__ V, const bf16* __restrict__ dO,
+    const float* __restrict__ LSE, const float* __restrict__ DELTA, const int* __restrict__ cu, bf16* __restrict__ dK,
+    bf16* __restrict__ dV, int Hq, int Hkv, int T, float scale_log2, float scale) {
+  constexpr int QC = 32;
+  const int kb = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int s0 = cu[b], L = cu[b + 1] - s0;
+  const int k0 = kb * 64;
+  if (k0 >= L) return;
+  const int rep = Hq / Hkv;
+  extern __shared__ __align__(128) uint8_t smem_bytes[];
+  bf16* sK = reinterpret_cast<bf16*>(smem_bytes);
+  bf16* sV = sK + 64 * D;
+  bf16* sQ = sV + 64 * D;        // [2][QC][D]
+  bf16* sdO = sQ + 2 * QC * D;   // [2][QC][D]
+  float* sL = reinterpret_cast<float*>(sdO + 2 * QC * D);  // [2][QC]
+  float* sDl = sL + 2 * QC;                                 // [2][QC]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const bf16* Ks = K + static_cast<int64_t>(s0) * Hkv * D;
+  const bf16* Vs = V + static_cast<int64_t>(s0) * Hkv * D;
+  const bf16* Qs = Q + static_cast<int64_t>(s0) * Hq * D;
+  const bf16* dOs = dO + static_cast<int64_t>(s0) * Hq * D;
+  load_rows<D>(sK, Ks, k0, 64, L, Hkv, hk, tid, 128);
+  load_rows<D>(sV, Vs, k0, 64, L, Hkv, hk, tid, 128);
+  cp_async_commit();
+
+  float dk[D / 8][4], dv[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dk[i][e] = dv[i][e] = 0.f;
+
+  const int qc_start = CAUSAL ? k0 / QC : 0;
+  const int qc_end = (L + QC - 1) / QC;
+  const int n_chunks = qc_end - qc_start;
+  const int total = rep * n_chunks;
+  auto issue = [&](int it, int buf) {
+    const int hh = hk * rep + it / n_chunks;
+    const int qs = (qc_start + it % n_chunks) * QC;
+    load_rows<D>(sQ + buf * QC * D, Qs, qs, QC, L, Hq, hh, tid, 128);
+    load_rows<D>(sdO + buf * QC * D, dOs, qs, QC, L, Hq, hh, tid, 128);
+    for (int i = tid; i < QC; i += 128) {
+      const bool ok = qs + i < L;
+      sL[buf * QC + i] = ok ? LSE[static_cast<int64_t>(hh) * T + s0 + qs + i] * kLog2e : INFINITY;
+      sDl[buf * QC + i] = ok ? DELTA[static_cast<int64_t>(hh) * T + s0 + qs + i] : 0.f;
+    }
+  };
+  if (total > 0) issue(0, 0);
+  cp_async_commit();
+  const int key_r0 = k0 + warp * 16 + g, key_r1 = key_r0 + 8;
+
+  for (int it = 0; it < total; ++it) {
+    const int buf = it & 1;
+    if (it + 1 < total) {
+      __syncthreads();  // buffer buf^1 no longer read
+      issue(it + 1, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int qs = (qc_start + it % n_chunks) * QC;
+    const bf16* q_t = sQ + buf * QC * D;
+    const bf16* do_t = sdO + buf * QC * D;
+    const float* lt = sL + buf * QC;
+    const float* dlt = sDl + buf * QC;
+    // S^T (16 keys x QC queries) = K_w . Q^T
+    float st[QC / 8][4];
+#pragma unroll
+    for (int i = 0; i < QC / 8; ++i) st[i][0] = st[i][1] = st[i][2] = st[i][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4];
+      frag_a<D>(a, sK, warp * 16, kk * 16, lane);
+#pragma unroll
+      for (int np = 0; np < QC / 16; ++np) {
+        uint32_t bb[4];
+        frag_b_nk<D>(bb, q_t, np * 16, kk * 16, lane);
+        mma_bf16(st[2 * np], a, bb[0], bb[1]);
+        mma_bf16(st[2 * np + 1], a, bb[2], bb[3]);
+      }
+    }
+    // P^T = exp2(S^T*scale - lse)
+#pragma unroll
+    for (int nb = 0; nb < QC / 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int qi = nb * 8 + 2 * tq + e;
+        const int qa = qs + qi;
+        const bool bad0 = qa >= L || key_r0 >= L || (CAUSAL && qa < key_r0);
+        const bool bad1 = qa >= L || key_r1 >= L || (CAUSAL && qa < key_r1);
+        st[nb][e] = bad0 ? 0.f : exp2f(st[nb][e] * scale_log2 - lt[qi]);
+        st[nb][2 + e] = bad1 ? 0.f : exp2f(st[nb][2 + e] * scale_log2 - lt[qi]);
+      }
+    }
+    // dV += P^T . dO
+#pragma unroll
+    for (int kk = 0; kk < QC / 16; ++kk) {
+      uint32_t a[4];
+      a[0] = pack_bf16x2(st[2 * kk][0], st[2 * kk][1]);
+      a[1] = pack_bf16x2(st[2 * kk][2], st[2 * kk][3]);
+      a[2] = pack_bf16x2(st[2 * kk + 1][0], st[2 * kk + 1][1]);
+      a[3] = pack_bf16x2(st[2 * kk + 1][2], st[2 * kk + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        uint32_t bb[4];
+        frag_b_kn<D>(bb, do_t, kk * 16, dp * 16, lane);
+        mma_bf16(dv[2 * dp], a, bb[0], bb[1]);
+        mma_bf16(dv[2 * dp + 1], a, bb[2], bb[3]);
+      }
+    }
+    // dP^T = V_w . dO^T
+    float dpt[QC / 8][4];
+#pragma unroll
+    for (int i = 0; i < QC / 8; ++i) dpt[i][0] = dpt[i][1] = dpt[i][2] = dpt[i][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4];
+      frag_a<D>(a, sV, warp * 16, kk * 16, lane);
+#pragma unroll
+      for (int np = 0; np < QC / 16; ++np) {
+        uint32_t bb[4];
+        frag_b_nk<D>(bb, do_t, np * 16, kk * 16, lane);
+        mma_bf16(dpt[2 * np], a, bb[0], bb[1]);
+        mma_bf16(dpt[2 * np + 1], a, bb[2], bb[3]);
+      }
+    }
+    // dS^T = P^T * (dP^T - delta)
+#pragma unroll
+    for (int nb = 0; nb < QC / 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int qi = nb * 8 + 2 * tq + e;
+        st[nb][e] = st[nb][e] * (dpt[nb][e] - dlt[qi]);
+        st[nb][2 + e] = st[nb][2 + e] * (dpt[nb][2 + e] - dlt[qi]);
+      }
+    }
+    // dK += dS^T . Q
+#pragma unroll
+    for (int kk = 0; kk < QC / 16; ++kk) {
+      uint32_t a[4];
+      a[0] = pack_bf16x2(st[2 * kk][0], st[2 * kk][1]);
+      a[1] = pack_bf16x2(st[2 * kk][2], st[2 * kk][3]);
+      a[2] = pack_bf16x2(st[2 * kk + 1][0], st[2 * kk + 1][1]);
+      a[3] = pack_bf16x2(st[2 * kk + 1][2], st[2 * kk + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        uint32_t bb[4];
+        frag_b_kn<D>(bb, q_t, kk * 16, dp * 16, lane);
+        mma_bf16(dk[2 * dp], a, bb[0], bb[1]);
+        mma_bf16(dk[2 * dp + 1], a, bb[2], bb[3]);
+      }
+    }
+  }
+#pragma unroll
+  for (int nb = 0; nb < D / 8; ++nb) {
+    const int col = nb * 8 + 2 * tq;
+    if (key_r0 < L) {
+      const int64_t o = (static_cast<int64_t>(s0 + key_r0) * Hkv + hk) * D + col;
+      *reinterpret_cast<uint32_t*>(dK + o) = pack_bf16x2(dk[nb][0] * scale, dk[nb][1] * scale);
+      *reinterpret_cast<uint32_t*>(dV + o) = pack_bf16x2(dv[nb][0], dv[nb][1]);
+    }
+    if (key_r1 < L) {
+      const int64_t o = (static_cast<int64_t>(s0 + key_r1) * Hkv + hk) * D + col;
+      *reinterpret_cast<uint32_t*>(dK + o) = pack_bf16x2(dk[nb][2] * scale, dk[nb][3] * scale);
+      *reinterpret_cast<uint32_t*>(dV + o) = pack_bf16x2(dv[nb][2], dv[nb][3]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ backward: dQ
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(128) flash_bwd_dq_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
+                                                           const bf16* __restrict__ V, const bf16* __restrict__ dO,
+                                                           const float* __restrict__ LSE,
+                                                           const float* __restrict__ DELTA, const int* __restrict__ cu,
+                                                           bf16* __restrict__ dQ, int Hq, int Hkv, int T,
+                                                           float scale_log2, float scale) {
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int s0 = cu[b], L = cu[b + 1] - s0;
+  const int q0 = qb * 64;
+  if (q0 >= L) return;
+  const int hk = h / (Hq / Hkv);
+  extern __shared__ __align__(128) uint8_t smem_bytes[];
+  bf16* sQ = reinterpret_cast<bf16*>(smem_bytes);
+  bf16* sdO = sQ + 64 * D;
+  bf16* sK = sdO + 64 * D;  // [2][64][D]
+  bf16* sV = sK + 2 * 64 * D;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const bf16* Ks = K + static_cast<int64_t>(s0) * Hkv * D;
+  const bf16* Vs = V + static_cast<int64_t>(s0) * Hkv * D;
+  load_rows<D>(sQ, Q + static_cast<int64_t>(s0) * Hq * D, q0, 64, L, Hq, h, tid, 128);
+  load_rows<D>(sdO, dO + static_cast<int64_t>(s0) * Hq * D, q0, 64, L, Hq, h, tid, 128);
+  load_rows<D>(sK, Ks, 0, 64, L, Hkv, hk, tid, 128);
+  load_rows<D>(sV, Vs, 0, 64, L, Hkv, hk, tid, 128);
+  cp_async_commit();
+  const int row0 = q0 + warp * 16 + g, row1 = row0 + 8;
+  const float lse0 = row0 < L ? LSE[static_cast<int64_t>(h) * T + s0 + row0] * kLog2e : INFINITY;
+  const float lse1 = row1 < L ? LSE[static_cast<int64_t>(h) * T + s0 + row1] * kLog2e : INFINITY;
+  const float dl0 = row0 < L ? DELTA[static_cast<int64_t>(h) * T + s0 + row0] : 0.f;
+  const float dl1 = row1 < L ? DELTA[static_cast<int64_t>(h) * T + s0 + row1] : 0.f;
+  float dq[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
+  const int nkb = CAUSAL ? min((L + 63) / 64, qb + 1) : (L + 63) / 64;
+  for (int j = 0; j < nkb; ++j) {
+    const int buf = j & 1;
+    if (j + 1 < nkb) {
+      load_rows<D>(sK + (buf ^ 1) * 64 * D, Ks, (j + 1) * 64, 64, L, Hkv, hk, tid, 128);
+      load_rows<D>(sV + (buf ^ 1) * 64 * D, Vs, (j + 1) * 64, 64, L, Hkv, hk, tid, 128);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const bf16* k_t = sK + buf * 64 * D;
+    const bf16* v_t = sV + buf * 64 * D;
+    float s[8][4], dp[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[i][e] = dp[i][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a[4], ad[4];
+      frag_a<D>(a, sQ, warp * 16, kk * 16, lane);
+      frag_a<D>(ad, sdO, warp * 16, kk * 16, lane);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        uint32_t bb[4], bv[4];
+        frag_b_nk<D>(bb, k_t, np * 16, kk * 16, lane);
+        frag_b_nk<D>(bv, v_t, np * 16, kk * 16, lane);
+        mma_bf16(s[2 * np], a, bb[0], bb[1]);
+        mma_bf16(s[2 * np + 1], a, bb[2], bb[3]);
+        mma_bf16(dp[2 * np], ad, bv[0], bv[1]);
+        mma_bf16(dp[2 * np + 1], ad, bv[2], bv[3]);
+      }
+    }
+#pragma unroll
+    for (int nb = 0; nb < 8; ++nb) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = j * 64 + nb * 8 + 2 * tq + e;
+        const bool bad0 = key >= L || row0 >= L || (CAUSAL && key > row0);
+        const bool bad1 = key >= L || row1 >= L || (CAUSAL && key > row1);
+        const float p0 = bad0 ? 0.f : exp2f(s[nb][e] * scale_log2 - lse0);
+        const float p1 = bad1 ? 0.f : exp2f(s[nb][2 + e] * scale_log2 - lse1);
+        s[nb][e] = p0 * (dp[nb][e] - dl0);
+        s[nb][2 + e] = p1 * (dp[nb][2 + e] - dl1);
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t a[4];
+      a[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+      a[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+      a[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      a[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dd = 0; dd < D / 16; ++dd) {
+        uint32_t bb[4];
+        frag_b_kn<D>(bb, k_t, kk * 16, dd * 16, lane);
+        mma_bf16(dq[2 * dd], a, bb[0], bb[1]);
+        mma_bf16(dq[2 * dd + 1], a, bb[2], bb[3]);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int nb = 0; nb < D / 8; ++nb) {
+    const int col = nb * 8 + 2 * tq;
+    if (row0 < L)
+      *reinterpret_cast<uint32_t*>(dQ + ((static_cast<int64_t>(s0 + row0) * Hq + h) * D + col)) =
+          pack_bf16x2(dq[nb][0] * scale, dq[nb][1] * scale);
+    if (row1 < L)
+      *reinterpret_cast<uint32_t*>(dQ + ((static_cast<int64_t>(s0 + row1) * Hq + h) * D + col)) =
+          pack_bf16x2(dq[nb][2] * scale, dq[nb][3] * scale);
+  }
+}
+
+// ------------------------------------------------------------------ decode attention
+// q [B, Hq, D], caches [B, Hkv, Tmax, D], len [B] -> o [B, Hq, D].  CTA = (b, kv-head), 8 warps.
+template <int D, int REP>
+__global__ void __launch_bounds__(256) decode_attn_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
+                                                          const bf16* __restrict__ vc, const int* __restrict__ lens,
+                                                          bf16* __restrict__ o, int Hq, int Hkv, int Tmax, float scale) {
+  const int hk = blockIdx.x, b = blockIdx.y;
+  const int L = min(lens[b], Tmax);
+  extern __shared__ float dsm[];
+  float* sq = dsm;                 // [REP][D]
+  float* sp = sq + REP * D;        // [REP][Tmax]
+  float* so = sp + REP * Tmax;     // [8 warps][REP][D]
+  float* red = so + 8 * REP * D;   // [REP][2]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < REP * D; i += 256) {
+    const int r = i / D, d = i % D;
+    sq[i] = bf2f(q[(static_cast<int64_t>(b) * Hq + hk * REP + r) * D + d]) * scale;
+  }
+  __syncthreads();
+  const bf16* kb = kc + (static_cast<int64_t>(b) * Hkv + hk) * Tmax * D;
+  const bf16* vb = vc + (static_cast<int64_t>(b) * Hkv + hk) * Tmax * D;
+  // scores: one key per thread, full-D dot products against all REP heads
+  for (int t = tid; t < L; t += 256) {
+    float acc[REP];
+#pragma unroll
+    for (int r = 0; r < REP; ++r) acc[r] = 0.f;
+    const uint4* kr = reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(t) * D);
+#pragma unroll 4
+    for (int c = 0; c < D / 8; ++c) {
+      const uint4 kv = kr[c];
+      const uint32_t u[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(u[j]);
+#pragma unroll
+        for (int r = 0; r < REP; ++r) acc[r] += f.x * sq[r * D + c * 8 + 2 * j] + f.y * sq[r * D + c * 8 + 2 * j + 1];
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < REP; ++r) sp[r * Tmax + t] = acc[r];
+  }
+  __syncthreads();
+  // softmax per head: warp r handles head r (REP <= 8)
+  if (warp < REP) {
+    float mx = -INFINITY;
+    for (int t = lane; t < L; t += 32) mx = fmaxf(mx, sp[warp * Tmax + t]);
+    mx = warp_max(mx);
+    float sum = 0.f;
+    for (int t = lane; t < L; t += 32) {
+      const float e = __expf(sp[warp * Tmax + t] - mx);
+      sp[warp * Tmax + t] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) red[warp] = sum > 0.f ? 1.f / sum : 0.f;
+  }
+  __syncthreads();
+  // P.V: warps split keys, lanes split D
+  float acc[REP][D / 32];
+#pragma unroll
+  for (int r = 0; r < REP; ++r)
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) acc[r][j] = 0.f;
+  for (int t = warp; t < L; t += 8) {
+    const bf16* vr = vb + static_cast<int64_t>(t) * D;
+    float vv[D / 32];
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) vv[j] = bf2f(vr[lane + 32 * j]);
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      const float p = sp[r * Tmax + t];
+#pragma unroll
+      for (int j = 0; j < D / 32; ++j) acc[r][j] += p * vv[j];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < REP; ++r)
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) so[(warp * REP + r) * D + lane + 32 * j] = acc[r][j];
+  __syncthreads();
+  for (int i = tid; i < REP * D; i += 256) {
+    const int r = i / D, d = i % D;
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += so[(w * REP + r) * D + d];
+    o[(static_cast<int64_t>(b) * Hq + hk * REP + r) * D + d] = f2bf(s * red[r]);
+  }
+}
+
+// ------------------------------------------------------------------ host
+template <typename KernT>
+static void set_smem(KernT k, int bytes) {
+  VLM_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+}
+
+template <int D>
+static void fwd_dispatch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
+                         at::Tensor& o, at::Tensor& lse, int max_seqlen, bool causal, float scale) {
+  const int B = static_cast<int>(cu.numel() - 1), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(k.size(1));
+  const int T = static_cast<int>(q.size(0));
+  const dim3 grid((max_seqlen + 63) / 64, Hq, B);
+  const int smem = 5 * 64 * D * 2;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  auto args = std::make_tuple(reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
+                              reinterpret_cast<const bf16*>(v.data_ptr()), cu.data_ptr<int>(),
+                              reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), Hq, Hkv, T,
+                              scale * kLog2e);
+  if (causal) {
+    auto kern = flash_fwd_kernel<D, true>;
+    set_smem(kern, smem);
+    std::apply([&](auto... a) { kern<<<grid, 128, smem, st>>>(a...); }, args);
+  } else {
+    auto kern = flash_fwd_kernel<D, false>;
+    set_smem(kern, smem);
+    std::apply([&](auto... a) { kern<<<grid, 128, smem, st>>>(a...); }, args);
+  }
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at::Tensor o, at::Tensor lse,
+                    int64_t max_seqlen, bool causal, double scale) {
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous(), "attn: contiguous");
+  TORCH_CHECK(cu.scalar_type() == at::kInt, "attn: cu_seqlens int32");
+  TORCH_CHECK(q.size(1) % k.size(1) == 0, "attn: Hq must be a multiple of Hkv");
+  if (q.size(0) == 0 || max_seqlen == 0) return;
+  const c10::cuda::CUDAGuard g(q.device());
+  const int D = static_cast<int>(q.size(2));
+  switch (D) {
+    case 16: fwd_dispatch<16>(q, k, v, cu, o, lse, static_cast<int>(max_seqlen), causal, static_cast<float>(scale)); break;
+    case 32: fwd_dispatch<32>(q, k, v, cu, o, lse, static_cast<int>(max_seqlen), causal, static_cast<float>(scale)); break;
+    case 64: fwd_dispatch<64>(q, k, v, cu, o, lse, static_cast<int>(max_seqlen), causal, static_cast<float>(scale)); break;
+    case 128: fwd_dispatch<128>(q, k, v, cu, o, lse, static_cast<int>(max_seqlen), causal, static_cast<float>(scale)); break;
+    default: TORCH_CHECK(false, "attn: unsupported head_dim ", D);
+  }
+}
+
+template <int D>
+static void bwd_dispatch(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                         const at::Tensor& lse, const at::Tensor& delta, const at::Tensor& cu, at::Tensor& dq,
+                         at::Tensor& dk, at::Tensor& dv, int max_seqlen, bool causal, float scale) {
+  const int B = static_cast<int>(cu.numel() - 1), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(k.size(1));
+  const int T = static_cast<int>(q.size(0));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const float sl2 = scale * kLog2e;
+  {
+    const dim3 grid((max_seqlen + 63) / 64, Hkv, B);
+    const int smem = (2 * 64 * D + 4 * 32 * D) * 2 + 4 * 32 * 4;
+    auto kern = causal ? flash_bwd_dkdv_kernel<D, true> : flash_bwd_dkdv_kernel<D, false>;
+    set_smem(kern, smem);
+    kern<<<grid, 128, smem, st>>>(reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
+                                  reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
+                                  lse.data_ptr<float>(), delta.data_ptr<float>(), cu.data_ptr<int>(),
+                                  reinterpret_cast<bf16*>(dk.data_ptr()), reinterpret_cast<bf16*>(dv.data_ptr()), Hq, Hkv, T,
+                                  sl2, scale);
+    VLM_CUDA_CHECK(cudaGetLastError());
+  }
+  {
+    const dim3 grid((max_seqlen + 63) / 64, Hq, B);
+    const int smem = 6 * 64 * D * 2;
+    auto kern = causal ? flash_bwd_dq_kernel<D, true> : flash_bwd_dq_kernel<D, false>;
+    set_smem(kern, smem);
+    kern<<<grid, 128, smem, st>>>(reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
+                                  reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
+                                  lse.data_ptr<float>(), delta.data_ptr<float>(), cu.data_ptr<int>(),
+                                  reinterpret_cast<bf16*>(dq.data_ptr()), Hq, Hkv, T, sl2, scale);
+    VLM_CUDA_CHECK(cudaGetLastError());
+  }
+}
+
+void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
+                    at::Tensor cu, at::Tensor dq, at::Tensor dk, at::Tensor dv, int64_t max_seqlen, bool causal,
+                    double scale) {
+  TORCH_CHECK(dout.is_contiguous() && q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous(),
+              "attn bwd: contiguous");
+  if (q.size(0) == 0 || max_seqlen == 0) return;
+  const c10::cuda::CUDAGuard g(q.device());
+  const int T = static_cast<int>(q.size(0)), Hq = static_cast<int>(q.size(1)), D = static_cast<int>(q.size(2));
+  at::Tensor delta = at::empty({Hq, T}, q.options().dtype(at::kFloat));
+  const int64_t warps = static_cast<int64_t>(T) * Hq;
+  attn_delta_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(dout.data_ptr()), reinterpret_cast<const bf16*>(o.data_ptr()), delta.data_ptr<float>(),
+      T, Hq, D);
+  VLM_CUDA_CHECK(cudaGetLastError());
+  const int ms = static_cast<int>(max_seqlen);
+  const float sc = static_cast<float>(scale);
+  switch (D) {
+    case 16: bwd_dispatch<16>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc); break;
+    case 32: bwd_dispatch<32>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc); break;
+    case 64: bwd_dispatch<64>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc); break;
+    case 128: bwd_dispatch<128>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc); break;
+    default: TORCH_CHECK(false, "attn bwd: unsupported head_dim ", D);
+  }
+}
+
+template <int D, int REP>
+static void decode_dispatch(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& lens,
+                            at::Tensor& o, float scale) {
+  const int B = static_cast<int>(q.size(0)), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(kc.size(1));
+  const int Tmax = static_cast<int>(kc.size(2));
+  const int smem = (REP * D + REP * Tmax + 8 * REP * D + 2 * REP) * 4;
+  TORCH_CHECK(smem <= 227 * 1024, "decode_attn: cache too long for the single-pass kernel (Tmax=", Tmax, ")");
+  auto kern = decode_attn_kernel<D, REP>;
+  set_smem(kern, smem);
+  kern<<<dim3(Hkv, B), 256, smem, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(kc.data_ptr()),
+      reinterpret_cast<const bf16*>(vc.data_ptr()), lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()), Hq, Hkv,
+      Tmax, scale);
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale) {
+  TORCH_CHECK(q.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(), "decode_attn: contiguous");
+  TORCH_CHECK(lens.scalar_type() == at::kInt, "decode_attn: int32 lengths");
+  if (q.size(0) == 0) return;
+  const c10::cuda::CUDAGuard g(q.device());
+  const int D = static_cast<int>(q.size(2));
+  const int rep = static_cast<int>(q.size(1) / kc.size(1));
+  const float sc = static_cast<float>(scale);
+#define VLM_DEC(DD, RR) \
+  if (D == DD && rep == RR) return decode_dispatch<DD, RR>(q, kc, vc, lens, o, sc);
+  VLM_DEC(128, 4) VLM_DEC(128, 2) VLM_DEC(128, 1) VLM_DEC(128, 8) VLM_DEC(64, 4) VLM_DEC(64, 2) VLM_DEC(64, 1)
+  VLM_DEC(32, 2) VLM_DEC(32, 4) VLM_DEC(32, 1)
+#undef VLM_DEC
+  TORCH_CHECK(false, "decode_attn: unsupported head_dim/group ", D, "/", rep);
+}
+
+}  // namespace vlm

@@ -1,0 +1,30 @@
+// Python bindings of the vlmrl sm_100a kernels (module vlmrl._C).
+#include <torch/extension.h>
+
+#include "vlm_ops.h"
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "vlmrl hand-written sm_100a kernels";
+  m.def("gemm", &vlm::gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("rms_norm_fwd", &vlm::rms_norm_fwd);
+  m.def("rms_norm_bwd", &vlm::rms_norm_bwd);
+  m.def("layer_norm_fwd", &vlm::layer_norm_fwd);
+  m.def("qk_norm_rope_fwd", &vlm::qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &vlm::qk_norm_rope_bwd);
+  m.def("vision_rope", &vlm::vision_rope);
+  m.def("swiglu_bwd", &vlm::swiglu_bwd);
+  m.def("embed", &vlm::embed);
+  m.def("scatter_rows", &vlm::scatter_rows);
+  m.def("embed_bwd", &vlm::embed_bwd);
+  m.def("kv_write", &vlm::kv_write);
+  m.def("adamw", &vlm::adamw);
+  m.def("sq_norm_acc", &vlm::sq_norm_acc);
+  m.def("patchify", &vlm::patchify);
+  m.def("flash_attn_fwd", &vlm::flash_attn_fwd);
+  m.def("flash_attn_bwd", &vlm::flash_attn_bwd);
+  m.def("decode_attn", &vlm::decode_attn);
+  m.def("sample", &vlm::sample);
+  m.def("vocab_logprob_fwd", &vlm::vocab_logprob_fwd);
+  m.def("vocab_logprob_bwd", &vlm::vocab_logprob_bwd);
+  m.def("read_and_clear_error", &vlm::read_and_clear_error);
+}

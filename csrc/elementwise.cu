@@ -1,0 +1,584 @@
+// Memory-bound kernels: RMSNorm / LayerNorm, q/k-norm + MRoPE, ViT 2-D rotary,
+// SwiGLU backward, embedding gather / scatter / backward, KV-cache writes, AdamW,
+// sum of squares and the uint8 image patchifier.
+//
+// All kernels are one-pass-per-row (warp or block per row) with 16-byte vector
+// accesses where the row is 8-element aligned, fp32 math and a single rounding
+// to bf16 on the way out.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace vlm {
+
+using bf16 = __nv_bfloat16;
+
+static inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream(); }
+static inline int blocks_for(int64_t n, int per) { return static_cast<int>(std::min<int64_t>((n + per - 1) / per, 1 << 20)); }
+
+// ------------------------------------------------------------------ RMSNorm
+// y = w * bf16(x * rstd): the normalised row is rounded to the input dtype before the
+// weight multiply, as the HF Qwen3 RMSNorm does.
+__global__ void rms_norm_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, bf16* __restrict__ y,
+                                    float* __restrict__ rstd, int M, int H, float eps) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+    const bf16* xr = x + static_cast<int64_t>(row) * H;
+    float ss = 0.f;
+    for (int c = lane * 8; c < H; c += 256) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(u[j]);
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / H + eps);
+    if (lane == 0 && rstd) rstd[row] = r;
+    bf16* yr = y + static_cast<int64_t>(row) * H;
+    for (int c = lane * 8; c < H; c += 256) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+      const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w}, uw[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack_bf16x2(u[j]), g = unpack_bf16x2(uw[j]);
+        o[j] = pack_bf16x2(bf2f(f2bf(f.x * r)) * g.x, bf2f(f2bf(f.y * r)) * g.y);
+      }
+      *reinterpret_cast<uint4*>(yr + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// dx = r * (g - xhat * mean(g * xhat)),  g = dy * w;  dw += sum_rows dy * xhat
+__global__ void rms_norm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                    const float* __restrict__ rstd, bf16* __restrict__ dx, float* __restrict__ dw,
+                                    int M, int H) {
+  extern __shared__ float sdw[];
+  if (dw)
+    for (int c = threadIdx.x; c < H; c += blockDim.x) sdw[c] = 0.f;
+  __syncthreads();
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+    const bf16* xr = x + static_cast<int64_t>(row) * H;
+    const bf16* dyr = dy + static_cast<int64_t>(row) * H;
+    const float r = rstd[row];
+    float dot = 0.f;
+    for (int c = lane * 8; c < H; c += 256) {
+      const uint4 a = *reinterpret_cast<const uint4*>(xr + c), b = *reinterpret_cast<const uint4*>(dyr + c),
+                  ww = *reinterpret_cast<const uint4*>(w + c);
+      const uint32_t ua[4] = {a.x, a.y, a.z, a.w}, ub[4] = {b.x, b.y, b.z, b.w}, uw[4] = {ww.x, ww.y, ww.z, ww.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 fx = unpack_bf16x2(ua[j]), fd = unpack_bf16x2(ub[j]), fw = unpack_bf16x2(uw[j]);
+        dot += fd.x * fw.x * fx.x * r + fd.y * fw.y * fx.y * r;
+        if (dw) {
+          atomicAdd(&sdw[c + 2 * j], fd.x * fx.x * r);
+          atomicAdd(&sdw[c + 2 * j + 1], fd.y * fx.y * r);
+        }
+      }
+    }
+    dot = warp_sum(dot) / H;
+    bf16* dxr = dx + static_cast<int64_t>(row) * H;
+    for (int c = lane * 8; c < H; c += 256) {
+      const uint4 a = *reinterpret_cast<const uint4*>(xr + c), b = *reinterpret_cast<const uint4*>(dyr + c),
+                  ww = *reinterpret_cast<const uint4*>(w + c);
+      const uint32_t ua[4] = {a.x, a.y, a.z, a.w}, ub[4] = {b.x, b.y, b.z, b.w}, uw[4] = {ww.x, ww.y, ww.z, ww.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 fx = unpack_bf16x2(ua[j]), fd = unpack_bf16x2(ub[j]), fw = unpack_bf16x2(uw[j]);
+        o[j] = pack_bf16x2(r * (fd.x * fw.x - fx.x * r * dot), r * (fd.y * fw.y - fx.y * r * dot));
+      }
+      *reinterpret_cast<uint4*>(dxr + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  if (dw) {
+    __syncthreads();
+    for (int c = threadIdx.x; c < H; c += blockDim.x) atomicAdd(&dw[c], sdw[c]);
+  }
+}
+
+void rms_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps) {
+  TORCH_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "rms_norm: bf16");
+  const int H = static_cast<int>(x.size(-1));
+  const int M = static_cast<int>(x.numel() / H);
+  TORCH_CHECK(H % 8 == 0, "rms_norm: hidden size must be a multiple of 8");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard g(x.device());
+  rms_norm_fwd_kernel<<<blocks_for(M, 8), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
+      reinterpret_cast<bf16*>(y.data_ptr()), rstd.defined() && rstd.numel() ? rstd.data_ptr<float>() : nullptr, M, H,
+      static_cast<float>(eps));
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+void rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor dx, at::Tensor dw) {
+  const int H = static_cast<int>(x.size(-1));
+  const int M = static_cast<int>(x.numel() / H);
+  if (M == 0) return;
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous(), "rms_norm_bwd: contiguous inputs");
+  const c10::cuda::CUDAGuard g(x.device());
+  const bool has_dw = dw.defined() && dw.numel();
+  const int blocks = std::min(blocks_for(M, 8), num_sms(x.device().index()) * 4);
+  rms_norm_bwd_kernel<<<blocks, 256, has_dw ? H * sizeof(float) : 0, cur_stream()>>>(
+      reinterpret_cast<const bf16*>(dy.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
+      reinterpret_cast<const bf16*>(w.data_ptr()), rstd.data_ptr<float>(), reinterpret_cast<bf16*>(dx.data_ptr()),
+      has_dw ? dw.data_ptr<float>() : nullptr, M, H);
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ LayerNorm (ViT, forward only)
+__global__ void layer_norm_fwd_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, const bf16* __restrict__ b,
+                                      bf16* __restrict__ y, int M, int H, float eps) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+    const bf16* xr = x + static_cast<int64_t>(row) * H;
+    float s = 0.f;
+    for (int c = lane; c < H; c += 32) s += bf2f(xr[c]);
+    const float mean = warp_sum(s) / H;
+    float v = 0.f;
+    for (int c = lane; c < H; c += 32) {
+      const float d = bf2f(xr[c]) - mean;
+      v += d * d;
+    }
+    const float r = rsqrtf(warp_sum(v) / H + eps);
+    bf16* yr = y + static_cast<int64_t>(row) * H;
+    for (int c = lane; c < H; c += 32) yr[c] = f2bf((bf2f(xr[c]) - mean) * r * bf2f(w[c]) + (b ? bf2f(b[c]) : 0.f));
+  }
+}
+
+void layer_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor b, at::Tensor y, double eps) {
+  const int H = static_cast<int>(x.size(-1));
+  const int M = static_cast<int>(x.numel() / H);
+  if (M == 0) return;
+  TORCH_CHECK(x.is_contiguous(), "layer_norm: contiguous input");
+  const c10::cuda::CUDAGuard g(x.device());
+  layer_norm_fwd_kernel<<<blocks_for(M, 8), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
+      b.defined() && b.numel() ? reinterpret_cast<const bf16*>(b.data_ptr()) : nullptr,
+      reinterpret_cast<bf16*>(y.data_ptr()), M, H, static_cast<float>(eps));
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ q/k RMSNorm + MRoPE
+// One warp per (token, head).  Heads [0, nq) are q, [nq, nq+nkv) are k, the rest v (copied).
+// Frequency j of the rotate-half pair (j, j + D/2) uses position axis ax[j] and inv_freq[j].
+__global__ void qk_norm_rope_fwd_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ qw,
+                                        const bf16* __restrict__ kw, const int* __restrict__ pos, int64_t pos_stride,
+                                        const float* __restrict__ inv_freq, const int* __restrict__ ax,
+                                        bf16* __restrict__ q, bf16* __restrict__ k, bf16* __restrict__ v,
+                                        float* __restrict__ rq, float* __restrict__ rk, int T, int nq, int nkv, int D,
+                                        float eps) {
+  const int nh = nq + 2 * nkv;
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (gw >= static_cast<int64_t>(T) * nh) return;
+  const int t = static_cast<int>(gw / nh), h = static_cast<int>(gw % nh);
+  const bf16* src = qkv + (static_cast<int64_t>(t) * nh + h) * D;
+  if (h >= nq + nkv) {
+    bf16* dst = v + (static_cast<int64_t>(t) * nkv + (h - nq - nkv)) * D;
+    for (int c = lane; c < D; c += 32) dst[c] = src[c];
+    return;
+  }
+  const bool is_q = h < nq;
+  float ss = 0.f;
+  for (int c = lane; c < D; c += 32) {
+    const float f = bf2f(src[c]);
+    ss += f * f;
+  }
+  const float r = rsqrtf(warp_sum(ss) / D + eps);
+  const bf16* wt = is_q ? qw : kw;
+  bf16* dst = is_q ? q + (static_cast<int64_t>(t) * nq + h) * D : k + (static_cast<int64_t>(t) * nkv + (h - nq)) * D;
+  if (lane == 0) {
+    if (is_q)
+      rq[static_cast<int64_t>(t) * nq + h] = r;
+    else
+      rk[static_cast<int64_t>(t) * nkv + (h - nq)] = r;
+  }
+  const int half = D / 2;
+  for (int j = lane; j < half; j += 32) {
+    const float x1 = bf2f(src[j]) * r * bf2f(wt[j]);
+    const float x2 = bf2f(src[j + half]) * r * bf2f(wt[j + half]);
+    const float p = static_cast<float>(pos[ax[j] * pos_stride + t]);
+    float s, c;
+    sincosf(p * inv_freq[j], &s, &c);
+    dst[j] = f2bf(x1 * c - x2 * s);
+    dst[j + half] = f2bf(x2 * c + x1 * s);
+  }
+}
+
+// Backward: un-rotate the incoming gradient, then the per-head RMSNorm backward.
+__global__ void qk_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16* __restrict__ dk,
+                                        const bf16* __restrict__ dv, const bf16* __restrict__ qkv,
+                                        const bf16* __restrict__ qw, const bf16* __restrict__ kw,
+                                        const int* __restrict__ pos, int64_t pos_stride,
+                                        const float* __restrict__ inv_freq, const int* __restrict__ ax,
+                                        const float* __restrict__ rq, const float* __restrict__ rk,
+                                        bf16* __restrict__ dqkv, float* __restrict__ dqw, float* __restrict__ dkw,
+                                        int T, int nq, int nkv, int D) {
+  extern __shared__ float sw[];  // [2*D] partial weight grads (q then k)
+  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) sw[i] = 0.f;
+  __syncthreads();
+  const int nh = nq + 2 * nkv;
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (gw < static_cast<int64_t>(T) * nh) {
+    const int t = static_cast<int>(gw / nh), h = static_cast<int>(gw % nh);
+    bf16* out = dqkv + (static_cast<int64_t>(t) * nh + h) * D;
+    if (h >= nq + nkv) {
+      const bf16* g = dv + (static_cast<int64_t>(t) * nkv + (h - nq - nkv)) * D;
+      for (int c = lane; c < D; c += 32) out[c] = g[c];
+    } else {
+      const bool is_q = h < nq;
+      const bf16* g = is_q ? dq + (static_cast<int64_t>(t) * nq + h) * D : dk + (static_cast<int64_t>(t) * nkv + h - nq) * D;
+      const bf16* x = qkv + (static_cast<int64_t>(t) * nh + h) * D;
+      const bf16* wt = is_q ? qw : kw;
+      const float r = is_q ? rq[static_cast<int64_t>(t) * nq + h] : rk[static_cast<int64_t>(t) * nkv + h - nq];
+      float* swp = sw + (is_q ? 0 : D);
+      const int half = D / 2;
+      // pass 1: dot = mean(gw * xhat)
+      float dot = 0.f;
+      for (int j = lane; j < half; j += 32) {
+        const float p = static_cast<float>(pos[ax[j] * pos_stride + t]);
+        float s, c;
+        sincosf(p * inv_freq[j], &s, &c);
+        const float g1 = bf2f(g[j]), g2 = bf2f(g[j + half]);
+        const float n1 = g1 * c + g2 * s, n2 = g2 * c - g1 * s;  // rotate by -angle
+        const float xh1 = bf2f(x[j]) * r, xh2 = bf2f(x[j + half]) * r;
+        dot += n1 * bf2f(wt[j]) * xh1 + n2 * bf2f(wt[j + half]) * xh2;
+        atomicAdd(&swp[j], n1 * xh1);
+        atomicAdd(&swp[j + half], n2 * xh2);
+      }
+      dot = warp_sum(dot) / D;
+      for (int j = lane; j < half; j += 32) {
+        const float p = static_cast<float>(pos[ax[j] * pos_stride + t]);
+        float s, c;
+        sincosf(p * inv_freq[j], &s, &c);
+        const float g1 = bf2f(g[j]), g2 = bf2f(g[j + half]);
+        const float n1 = g1 * c + g2 * s, n2 = g2 * c - g1 * s;
+        const float xh1 = bf2f(x[j]) * r, xh2 = bf2f(x[j + half]) * r;
+        out[j] = f2bf(r * (n1 * bf2f(wt[j]) - xh1 * dot));
+        out[j + half] = f2bf(r * (n2 * bf2f(wt[j + half]) - xh2 * dot));
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) {
+    float* dst = i < D ? dqw : dkw;
+    if (dst) atomicAdd(&dst[i % D], sw[i]);
+  }
+}
+
+void qk_norm_rope_fwd(at::Tensor qkv, at::Tensor qw, at::Tensor kw, at::Tensor pos, at::Tensor inv_freq, at::Tensor ax,
+                      at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor rq, at::Tensor rk, int64_t nq, int64_t nkv,
+                      double eps) {
+  const int T = static_cast<int>(qkv.size(0));
+  const int D = static_cast<int>(q.size(-1));
+  if (T == 0) return;
+  TORCH_CHECK(qkv.is_contiguous() && pos.scalar_type() == at::kInt && pos.dim() == 2 && pos.stride(1) == 1,
+              "qk_norm_rope: layout");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  const int64_t warps = static_cast<int64_t>(T) * (nq + 2 * nkv);
+  qk_norm_rope_fwd_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const bf16*>(qkv.data_ptr()), reinterpret_cast<const bf16*>(qw.data_ptr()),
+      reinterpret_cast<const bf16*>(kw.data_ptr()), pos.data_ptr<int>(), pos.stride(0), inv_freq.data_ptr<float>(),
+      ax.data_ptr<int>(), reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(k.data_ptr()),
+      reinterpret_cast<bf16*>(v.data_ptr()), rq.data_ptr<float>(), rk.data_ptr<float>(), T, static_cast<int>(nq),
+      static_cast<int>(nkv), D, static_cast<float>(eps));
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+void qk_norm_rope_bwd(at::Tensor dq, at::Tensor dk, at::Tensor dv, at::Tensor qkv, at::Tensor qw, at::Tensor kw,
+                      at::Tensor pos, at::Tensor inv_freq, at::Tensor ax, at::Tensor rq, at::Tensor rk, at::Tensor dqkv,
+                      at::Tensor dqw, at::Tensor dkw, int64_t nq, int64_t nkv, double eps) {
+  const int T = static_cast<int>(qkv.size(0));
+  const int D = static_cast<int>(dq.size(-1));
+  if (T == 0) return;
+  TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous(), "qk_norm_rope_bwd: contiguous grads");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  const int64_t warps = static_cast<int64_t>(T) * (nq + 2 * nkv);
+  qk_norm_rope_bwd_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 2 * D * sizeof(float), cur_stream()>>>(
+      reinterpret_cast<const bf16*>(dq.data_ptr()), reinterpret_cast<const bf16*>(dk.data_ptr()),
+      reinterpret_cast<const bf16*>(dv.data_ptr()), reinterpret_cast<const bf16*>(qkv.data_ptr()),
+      reinterpret_cast<const bf16*>(qw.data_ptr()), reinterpret_cast<const bf16*>(kw.data_ptr()), pos.data_ptr<int>(),
+      pos.stride(0), inv_freq.data_ptr<float>(), ax.data_ptr<int>(), rq.data_ptr<float>(), rk.data_ptr<float>(),
+      reinterpret_cast<bf16*>(dqkv.data_ptr()), dqw.defined() && dqw.numel() ? dqw.data_ptr<float>() : nullptr,
+      dkw.defined() && dkw.numel() ? dkw.data_ptr<float>() : nullptr, T, static_cast<int>(nq), static_cast<int>(nkv), D);
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ ViT 2-D rotary
+// qkv [N, 3, H, D] -> q, k (rotated), v.  Pair j of (j, j+D/2): angle = (j < D/4 ? row : col) * 1e4^(-(j mod D/4)/(D/4)).
+__global__ void vision_rope_kernel(const bf16* __restrict__ qkv, const int* __restrict__ rc, bf16* __restrict__ q,
+                                   bf16* __restrict__ k, bf16* __restrict__ v, int N, int H, int D) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int half = D / 2, quarter = D / 4;
+  const int64_t total = static_cast<int64_t>(N) * H * half;
+  if (idx >= total) return;
+  const int j = static_cast<int>(idx % half);
+  const int h = static_cast<int>((idx / half) % H);
+  const int n = static_cast<int>(idx / (static_cast<int64_t>(half) * H));
+  const int64_t base = static_cast<int64_t>(n) * 3 * H * D;
+  const int64_t o = (static_cast<int64_t>(n) * H + h) * D;
+  const int coord = j < quarter ? rc[2 * n] : rc[2 * n + 1];
+  const float freq = exp2f(-static_cast<float>(j % quarter) / quarter * 13.287712379549449f);  // log2(1e4)
+  float s, c;
+  sincosf(static_cast<float>(coord) * freq, &s, &c);
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+    const bf16* src = qkv + base + static_cast<int64_t>(which) * H * D + static_cast<int64_t>(h) * D;
+    bf16* dst = (which == 0 ? q : k) + o;
+    const float x1 = bf2f(src[j]), x2 = bf2f(src[j + half]);
+    dst[j] = f2bf(x1 * c - x2 * s);
+    dst[j + half] = f2bf(x2 * c + x1 * s);
+  }
+  const bf16* sv = qkv + base + 2ll * H * D + static_cast<int64_t>(h) * D;
+  v[o + j] = sv[j];
+  v[o + j + half] = sv[j + half];
+}
+
+void vision_rope(at::Tensor qkv, at::Tensor rc, at::Tensor q, at::Tensor k, at::Tensor v, int64_t n_heads) {
+  const int N = static_cast<int>(qkv.size(0));
+  const int D = static_cast<int>(q.size(-1));
+  if (N == 0) return;
+  TORCH_CHECK(rc.scalar_type() == at::kInt && rc.is_contiguous(), "vision_rope: rc int32 [N,2]");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  const int64_t total = static_cast<int64_t>(N) * n_heads * (D / 2);
+  vision_rope_kernel<<<static_cast<int>((total + 255) / 256), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const bf16*>(qkv.data_ptr()), rc.data_ptr<int>(), reinterpret_cast<bf16*>(q.data_ptr()),
+      reinterpret_cast<bf16*>(k.data_ptr()), reinterpret_cast<bf16*>(v.data_ptr()), N, static_cast<int>(n_heads), D);
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ SwiGLU backward
+// pre [M, 2F] interleaved (gate, up); d_act [M, F] -> d_pre [M, 2F]
+__global__ void swiglu_bwd_kernel(const bf16* __restrict__ da, const bf16* __restrict__ pre, bf16* __restrict__ dpre,
+                                  int64_t n_pairs) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n_pairs) return;
+  const float2 gu = unpack_bf16x2(reinterpret_cast<const uint32_t*>(pre)[i]);
+  const float g = gu.x, u = gu.y;
+  const float s = 1.f / (1.f + __expf(-g));
+  const float d = bf2f(da[i]);
+  reinterpret_cast<uint32_t*>(dpre)[i] = pack_bf16x2(d * u * s * (1.f + g * (1.f - s)), d * g * s);
+}
+
+void swiglu_bwd(at::Tensor d_act, at::Tensor pre, at::Tensor out) {
+  const int64_t n = d_act.numel();
+  if (n == 0) return;
+  TORCH_CHECK(d_act.is_contiguous() && pre.is_contiguous() && out.is_contiguous(), "swiglu_bwd: contiguous");
+  const c10::cuda::CUDAGuard g(pre.device());
+  swiglu_bwd_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, cur_stream()>>>(
+      reinterpret_cast<const bf16*>(d_act.data_ptr()), reinterpret_cast<const bf16*>(pre.data_ptr()),
+      reinterpret_cast<bf16*>(out.data_ptr()), n);
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ embedding gather / scatter
+__global__ void embed_kernel(const int64_t* __restrict__ tok, const bf16* __restrict__ table, bf16* __restrict__ out,
+                             int T, int H, int64_t V) {
+  const int row = blockIdx.x;
+  if (row >= T) return;
+  int64_t id = tok[row];
+  if (id < 0 || id >= V) id = 0;
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * H);
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * H);
+  for (int c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
+}
+
+void embed(at::Tensor tokens, at::Tensor table, at::Tensor out) {
+  const int T = static_cast<int>(tokens.numel());
+  const int H = static_cast<int>(table.size(1));
+  if (T == 0) return;
+  TORCH_CHECK(tokens.scalar_type() == at::kLong && H % 8 == 0, "embed: int64 tokens, H % 8 == 0");
+  const c10::cuda::CUDAGuard g(table.device());
+  embed_kernel<<<T, 128, 0, cur_stream()>>>(tokens.data_ptr<int64_t>(), reinterpret_cast<const bf16*>(table.data_ptr()),
+                                            reinterpret_cast<bf16*>(out.data_ptr()), T, H, table.size(0));
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+__global__ void scatter_rows_kernel(bf16* __restrict__ h, const int64_t* __restrict__ rows, const bf16* __restrict__ src,
+                                    int R, int H, int add) {
+  const int r = blockIdx.x;
+  if (r >= R) return;
+  bf16* dst = h + rows[r] * H;
+  const bf16* s = src + static_cast<int64_t>(r) * H;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) dst[c] = add ? f2bf(bf2f(dst[c]) + bf2f(s[c])) : s[c];
+}
+
+void scatter_rows(at::Tensor h, at::Tensor rows, at::Tensor src, bool add) {
+  const int R = static_cast<int>(rows.numel());
+  if (R == 0) return;
+  TORCH_CHECK(rows.scalar_type() == at::kLong && src.is_contiguous() && h.is_contiguous(), "scatter_rows: layout");
+  const c10::cuda::CUDAGuard g(h.device());
+  scatter_rows_kernel<<<R, 128, 0, cur_stream()>>>(reinterpret_cast<bf16*>(h.data_ptr()), rows.data_ptr<int64_t>(),
+                                                   reinterpret_cast<const bf16*>(src.data_ptr()), R,
+                                                   static_cast<int>(h.size(1)), add ? 1 : 0);
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+__global__ void embed_bwd_kernel(const int64_t* __restrict__ tok, const bf16* __restrict__ dh, float* __restrict__ dt,
+                                 int T, int H) {
+  const int row = blockIdx.x;
+  if (row >= T) return;
+  const int64_t id = tok[row];
+  if (id < 0) return;
+  for (int c = threadIdx.x; c < H; c += blockDim.x) atomicAdd(&dt[id * H + c], bf2f(dh[static_cast<int64_t>(row) * H + c]));
+}
+
+void embed_bwd(at::Tensor tokens, at::Tensor dh, at::Tensor dtable) {
+  const int T = static_cast<int>(tokens.numel());
+  if (T == 0) return;
+  TORCH_CHECK(dtable.scalar_type() == at::kFloat && dh.is_contiguous(), "embed_bwd: fp32 table grad");
+  const c10::cuda::CUDAGuard g(dh.device());
+  embed_bwd_kernel<<<T, 256, 0, cur_stream()>>>(tokens.data_ptr<int64_t>(), reinterpret_cast<const bf16*>(dh.data_ptr()),
+                                                dtable.data_ptr<float>(), T, static_cast<int>(dh.size(1)));
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ KV-cache write
+// k, v [T, Hkv, D] -> cache [B, Hkv, Tmax, D] at (seq[t], pos[t])
+__global__ void kv_write_kernel(const bf16* __restrict__ k, const bf16* __restrict__ v, bf16* __restrict__ kc,
+                                bf16* __restrict__ vc, const int64_t* __restrict__ seq, const int64_t* __restrict__ pos,
+                                int T, int Hkv, int Tmax, int D) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const int64_t s = seq[t], p = pos[t];
+  if (p < 0 || p >= Tmax) return;
+  for (int i = threadIdx.x; i < Hkv * D / 8; i += blockDim.x) {
+    const int h = (i * 8) / D, d = (i * 8) % D;
+    const int64_t src = (static_cast<int64_t>(t) * Hkv + h) * D + d;
+    const int64_t dst = ((s * Hkv + h) * Tmax + p) * D + d;
+    *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(k + src);
+    *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(v + src);
+  }
+}
+
+void kv_write(at::Tensor k, at::Tensor v, at::Tensor kc, at::Tensor vc, at::Tensor seq, at::Tensor pos) {
+  const int T = static_cast<int>(k.size(0));
+  if (T == 0) return;
+  TORCH_CHECK(k.is_contiguous() && v.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(), "kv_write: layout");
+  TORCH_CHECK(seq.scalar_type() == at::kLong && pos.scalar_type() == at::kLong, "kv_write: int64 indices");
+  const c10::cuda::CUDAGuard g(k.device());
+  kv_write_kernel<<<T, 128, 0, cur_stream()>>>(
+      reinterpret_cast<const bf16*>(k.data_ptr()), reinterpret_cast<const bf16*>(v.data_ptr()),
+      reinterpret_cast<bf16*>(kc.data_ptr()), reinterpret_cast<bf16*>(vc.data_ptr()), seq.data_ptr<int64_t>(),
+      pos.data_ptr<int64_t>(), T, static_cast<int>(k.size(1)), static_cast<int>(kc.size(2)), static_cast<int>(k.size(2)));
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ AdamW (optax.adamw semantics)
+__global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
+                             float* __restrict__ v, bf16* __restrict__ ph, const float* __restrict__ scale_ptr,
+                             int64_t n, float lr, float b1, float b2, float eps, float wd, float bc1, float bc2) {
+  const float scale = *scale_ptr;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float gi = g[i] * scale;
+    const float mi = b1 * m[i] + (1.f - b1) * gi;
+    const float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    const float upd = (mi / bc1) / (sqrtf(vi / bc2) + eps) + wd * p[i];
+    const float pn = p[i] - lr * upd;
+    p[i] = pn;
+    if (ph) ph[i] = f2bf(pn);
+  }
+}
+
+void adamw(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor ph, at::Tensor scale, double lr, double b1,
+           double b2, double eps, double wd, int64_t step) {
+  const int64_t n = p.numel();
+  if (n == 0) return;
+  TORCH_CHECK(p.scalar_type() == at::kFloat && g.scalar_type() == at::kFloat && p.is_contiguous() && g.is_contiguous(),
+              "adamw: fp32 contiguous");
+  const c10::cuda::CUDAGuard gd(p.device());
+  const float bc1 = static_cast<float>(1.0 - std::pow(b1, static_cast<double>(step)));
+  const float bc2 = static_cast<float>(1.0 - std::pow(b2, static_cast<double>(step)));
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, num_sms(p.device().index()) * 8));
+  adamw_kernel<<<blocks, 256, 0, cur_stream()>>>(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(),
+                                                 v.data_ptr<float>(),
+                                                 ph.defined() && ph.numel() ? reinterpret_cast<bf16*>(ph.data_ptr()) : nullptr,
+                                                 scale.data_ptr<float>(), n, static_cast<float>(lr), static_cast<float>(b1),
+                                                 static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd),
+                                                 bc1, bc2);
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ sum of squares (fp32 accumulate)
+template <typename T>
+__global__ void sq_norm_kernel(const T* __restrict__ x, int64_t n, float* __restrict__ out) {
+  float s = 0.f;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float f = static_cast<float>(x[i]);
+    s += f * f;
+  }
+  s = warp_sum(s);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) atomicAdd(out, t);
+  }
+}
+
+void sq_norm_acc(at::Tensor x, at::Tensor out) {
+  const int64_t n = x.numel();
+  if (n == 0) return;
+  TORCH_CHECK(x.is_contiguous() && out.scalar_type() == at::kFloat, "sq_norm: contiguous input, fp32 out");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, num_sms(x.device().index()) * 4));
+  if (x.scalar_type() == at::kFloat)
+    sq_norm_kernel<float><<<blocks, 256, 0, cur_stream()>>>(x.data_ptr<float>(), n, out.data_ptr<float>());
+  else
+    sq_norm_kernel<__nv_bfloat16><<<blocks, 256, 0, cur_stream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), n, out.data_ptr<float>());
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ uint8 image -> patch rows
+// images [N, H, W, 3] uint8 -> rows [N*gh*gw, 3*Tp*P*P] bf16, rows in merge-window order,
+// row layout (c, t, py, px); the single frame is repeated over the temporal patch.
+__global__ void patchify_kernel(const uint8_t* __restrict__ img, const float* __restrict__ ms, bf16* __restrict__ out,
+                                int N, int H, int W, int P, int Tp, int merge) {
+  const int gh = H / P, gw = W / P;
+  const int row = blockIdx.x;  // over N*gh*gw
+  const int per_img = gh * gw;
+  const int n = row / per_img, r = row % per_img;
+  const int wb_count = gw / merge;
+  const int blk = r / (merge * merge), in = r % (merge * merge);
+  const int hb = blk / wb_count, wb = blk % wb_count;
+  const int py0 = (hb * merge + in / merge) * P, px0 = (wb * merge + in % merge) * P;
+  const int cols = 3 * Tp * P * P;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) {
+    const int ch = c / (Tp * P * P);
+    const int rem = c % (P * P);
+    const int y = py0 + rem / P, x = px0 + rem % P;
+    const float val = static_cast<float>(img[((static_cast<int64_t>(n) * H + y) * W + x) * 3 + ch]) * (1.f / 255.f);
+    out[static_cast<int64_t>(row) * cols + c] = f2bf((val - ms[ch]) / ms[3 + ch]);
+  }
+}
+
+void patchify(at::Tensor images, at::Tensor ms, at::Tensor out, int64_t patch, int64_t temporal, int64_t merge) {
+  TORCH_CHECK(images.scalar_type() == at::kByte && images.is_contiguous() && images.size(3) == 3, "patchify: uint8 NHWC");
+  const int N = static_cast<int>(images.size(0)), H = static_cast<int>(images.size(1)), W = static_cast<int>(images.size(2));
+  const int rows = N * (H / static_cast<int>(patch)) * (W / static_cast<int>(patch));
+  if (rows == 0) return;
+  const c10::cuda::CUDAGuard g(images.device());
+  patchify_kernel<<<rows, 256, 0, cur_stream()>>>(images.data_ptr<uint8_t>(), ms.data_ptr<float>(),
+                                                  reinterpret_cast<bf16*>(out.data_ptr()), N, H, W, static_cast<int>(patch),
+                                                  static_cast<int>(temporal), static_cast<int>(merge));
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace vlm

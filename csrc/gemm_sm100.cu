@@ -1,0 +1,546 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   D[M,N] = alpha * A[M,K] . B[N,K]^T   (+bias[N]) (+residual[M,N]) (activation) (+= D when accumulating)
+//
+// * A and B are bf16 in either K-major or MN-major layout (the latter lets the
+//   backward GEMMs dX = dY.W and dW = dY^T.X read activations and weights in
+//   place, without transposes).
+// * Tiles are 128 x BN x 64 (BN = 128 or 256).  Operands are staged by TMA
+//   (128-byte swizzle) into a STAGES-deep shared-memory ring guarded by
+//   mbarriers; one elected thread issues tcgen05.mma (UMMA 128xBNx16) into a
+//   double-buffered TMEM accumulator; four epilogue warps drain TMEM with
+//   tcgen05.ld while the next tile's MMAs run.
+// * Warp roles: 0 = TMA producer, 1 = MMA issuer (+TMEM owner), 2..5 = epilogue.
+// * Grid = min(#tiles, #SMs) CTAs, one per SM; tiles are walked in groups of
+//   16 M-tiles so concurrently running CTAs share B tiles in L2.
+// * Every wait is bounded (see common.cuh); on timeout the kernel records an
+//   error code, drains its own in-flight TMA copies and MMAs, frees TMEM and exits.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+#include "vlm_ops.h"
+
+namespace vlm {
+
+enum Epi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GELU_TANH = 2, EPI_GELU_ERF = 3, EPI_VOCAB_STATS = 4, EPI_VOCAB_GRAD = 5 };
+
+struct GemmParams {
+  int M, N, K;
+  void* D;
+  long long ldd;
+  int d_f32;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* residual;
+  long long ldr;
+  __nv_bfloat16* aux;
+  long long ld_aux;
+  float alpha;
+  int epi;
+  int accumulate;
+  int tiles_m, tiles_n;
+  int* err;
+  // vocab epilogues (per-row data of the fused lm_head -> log-softmax)
+  const int64_t* targets;
+  const float* row_lse;
+  const float* row_ent;
+  const float* g_lp;
+  const float* g_ent;
+  float* part;  // [M, tiles_n, 4] partial (max, sum exp, sum exp*z, target logit)
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+};
+
+VLM_DEV void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  constexpr int G = 16;
+  const int group = G * tiles_n;
+  const int gid = t / group;
+  const int first = gid * G;
+  const int gsz = min(tiles_m - first, G);
+  const int r = t - gid * group;
+  tm = first + r % gsz;
+  tn = r / gsz;
+}
+
+VLM_DEV float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+VLM_DEV float gelu_erf(float x) { return 0.5f * x * (1.f + erff(x * 0.7071067811865476f)); }
+VLM_DEV float silu(float x) { return x / (1.f + __expf(-x)); }
+
+VLM_DEV void epilogue_chunk(const GemmParams& p, int row, int col, const uint32_t (&r)[16]) {
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+  const int ncols = min(16, p.N - col);
+  const bool full = ncols == 16;
+  if (p.epi == EPI_SWIGLU) {
+    if (p.aux) {
+      __nv_bfloat16* a = p.aux + static_cast<long long>(row) * p.ld_aux + col;
+      if (full) {
+        uint4 w0 = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                              pack_bf16x2(v[6], v[7]));
+        uint4 w1 = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]), pack_bf16x2(v[12], v[13]),
+                              pack_bf16x2(v[14], v[15]));
+        reinterpret_cast<uint4*>(a)[0] = w0;
+        reinterpret_cast<uint4*>(a)[1] = w1;
+      } else {
+        for (int i = 0; i < ncols; ++i) a[i] = f2bf(v[i]);
+      }
+    }
+    // gate/up are rounded to bf16 first, like an unfused bf16 GEMM followed by the activation
+    float o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float g = bf2f(f2bf(v[2 * j])), u = bf2f(f2bf(v[2 * j + 1]));
+      o[j] = silu(g) * u;
+    }
+    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + static_cast<long long>(row) * p.ldd + col / 2;
+    if (full) {
+      reinterpret_cast<uint4*>(d)[0] =
+          make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+    } else {
+      for (int j = 0; j < ncols / 2; ++j) d[j] = f2bf(o[j]);
+    }
+    return;
+  }
+  if (p.bias) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (i < ncols) v[i] += bf2f(p.bias[col + i]);
+  }
+  if (p.epi == EPI_GELU_TANH) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = gelu_tanh(v[i]);
+  } else if (p.epi == EPI_GELU_ERF) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = gelu_erf(v[i]);
+  }
+  if (p.residual) {
+    const __nv_bfloat16* rs = p.residual + static_cast<long long>(row) * p.ldr + col;
+    if (full) {
+      const uint4 a = reinterpret_cast<const uint4*>(rs)[0], b = reinterpret_cast<const uint4*>(rs)[1];
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 f = unpack_bf16x2(w[j]);
+        v[2 * j] += f.x;
+        v[2 * j + 1] += f.y;
+      }
+    } else {
+      for (int i = 0; i < ncols; ++i) v[i] += bf2f(rs[i]);
+    }
+  }
+  if (p.d_f32) {
+    float* d = reinterpret_cast<float*>(p.D) + static_cast<long long>(row) * p.ldd + col;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float4 x = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        if (p.accumulate) {
+          const float4 o = reinterpret_cast<const float4*>(d)[j];
+          x.x += o.x;
+          x.y += o.y;
+          x.z += o.z;
+          x.w += o.w;
+        }
+        reinterpret_cast<float4*>(d)[j] = x;
+      }
+    } else {
+      for (int i = 0; i < ncols; ++i) d[i] = p.accumulate ? d[i] + v[i] : v[i];
+    }
+  } else {
+    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + static_cast<long long>(row) * p.ldd + col;
+    if (full) {
+      reinterpret_cast<uint4*>(d)[0] =
+          make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+      reinterpret_cast<uint4*>(d)[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]),
+                                                  pack_bf16x2(v[12], v[13]), pack_bf16x2(v[14], v[15]));
+    } else {
+      for (int i = 0; i < ncols; ++i) d[i] = f2bf(v[i]);
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  using C = GemmCfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+  const int kb_count = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      long long issued = 0;
+      bool ok = true;
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+        const int m0 = tm * kBM, n0 = tn * BN;
+        for (int kb = 0; kb < kb_count; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a = sA + stage * C::A_BYTES;
+          uint8_t* b = sB + stage * C::B_BYTES;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          const int k0 = kb * kBK;
+          if constexpr (!A_MN) {
+            tma_load_2d(a, &tmA, &full[stage], k0, m0);
+          } else {
+            tma_load_2d(a, &tmA, &full[stage], m0, k0);
+            tma_load_2d(a + 8192, &tmA, &full[stage], m0 + 64, k0);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(b, &tmB, &full[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0);
+          }
+          ++issued;
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // drain this thread's in-flight copies (at most STAGES) before the CTA exits
+        for (long long i = issued - 1; i >= 0 && i >= issued - C::STAGES; --i) {
+          volatile int no_abort = 0;
+          mbar_wait(&full[i % C::STAGES], static_cast<uint32_t>((i / C::STAGES) & 1), &no_abort, nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, A_MN, B_MN);
+      bool ok = true;
+      int stage = 0;
+      uint32_t phase = 0;
+      int lt = 0;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++lt) {
+        const int acc = lt & 1;
+        const uint32_t use = static_cast<uint32_t>(lt >> 1);
+        if (!mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abort_flag, p.err, kErrTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kb_count; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a_addr + k * 2048, 8192, 1024) : sdesc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_addr + k * 2048, 8192, 1024) : sdesc_sw128(b_addr + k * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == C::STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+      if (!ok) {
+        umma_commit(drain);
+        volatile int no_abort = 0;
+        mbar_wait(drain, 0, &no_abort, nullptr, 0);
+      }
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lanes [32q, 32q+32) are the ones this warp may read
+    const int row_in_tile = q * 32 + lane;
+    int lt = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
+      const int acc = lt & 1;
+      const uint32_t use = static_cast<uint32_t>(lt >> 1);
+      if (!mbar_wait(&tfull[acc], use & 1u, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      const int row = tm * kBM + row_in_tile;
+      const int n0 = tn * BN;
+      const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
+      if (p.epi == EPI_VOCAB_STATS) {
+        // online (max, sum exp, sum exp*z) of this row over the tile's columns; never stores logits
+        float mx = -INFINITY, se = 0.f, sz = 0.f, zt = __int_as_float(0x7fc00000);
+        const int64_t tgt = row < p.M ? p.targets[row] : -1;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c, r);
+          tmem_ld_wait();
+          const int col0 = n0 + c;
+          const int nv = min(16, p.N - col0);
+          if (nv <= 0) continue;
+          float cm = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (i < nv) cm = fmaxf(cm, __uint_as_float(r[i]) * p.alpha);
+          if (cm > mx) {
+            const float sc = __expf(mx - cm);
+            se *= sc;
+            sz *= sc;
+            mx = cm;
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (i < nv) {
+              const float z = __uint_as_float(r[i]) * p.alpha;
+              const float e = __expf(z - mx);
+              se += e;
+              sz += e * z;
+            }
+          }
+          if (tgt >= col0 && tgt < col0 + nv) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (col0 + i == tgt) zt = __uint_as_float(r[i]) * p.alpha;
+          }
+        }
+        if (row < p.M) {
+          reinterpret_cast<float4*>(p.part)[static_cast<int64_t>(row) * p.tiles_n + tn] = make_float4(mx, se, sz, zt);
+        }
+      } else if (p.epi == EPI_VOCAB_GRAD) {
+        // dlogits = g_lp * (onehot - p) - g_ent * p * (log p + H), p = exp(z - lse)
+        float lse = 0.f, ent = 0.f, glp = 0.f, gent = 0.f;
+        int64_t tgt = -1;
+        if (row < p.M) {
+          lse = p.row_lse[row];
+          ent = p.row_ent[row];
+          glp = p.g_lp[row];
+          gent = p.g_ent[row];
+          tgt = p.targets[row];
+        }
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c, r);
+          tmem_ld_wait();
+          const int col0 = n0 + c;
+          if (row >= p.M || col0 >= p.N) continue;
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float lp = __uint_as_float(r[i]) * p.alpha - lse;
+            const float pr = __expf(lp);
+            v[i] = -glp * pr - gent * pr * (lp + ent) + (col0 + i == tgt ? glp : 0.f);
+          }
+          __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + static_cast<long long>(row) * p.ldd + col0;
+          if (col0 + 16 <= p.N) {
+            reinterpret_cast<uint4*>(d)[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                                        pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+            reinterpret_cast<uint4*>(d)[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]),
+                                                        pack_bf16x2(v[12], v[13]), pack_bf16x2(v[14], v[15]));
+          } else {
+            for (int i = 0; i < p.N - col0; ++i) d[i] = f2bf(v[i]);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c, r);
+          tmem_ld_wait();
+          if (row < p.M && n0 + c < p.N) epilogue_chunk(p, row, n0 + c, r);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+template <int BN, bool A_MN, bool B_MN>
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid, cudaStream_t st) {
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN>;
+  static bool configured = false;
+  if (!configured) {
+    VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM));
+    configured = true;
+  }
+  kern<<<grid, 192, GemmCfg<BN>::SMEM, st>>>(ta, tb, p);
+  VLM_CUDA_CHECK(cudaGetLastError());
+}
+
+static void check_operand(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, " must be a CUDA bf16 tensor");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2-D with a contiguous inner dimension");
+  TORCH_CHECK(t.stride(0) % 8 == 0 || t.size(0) == 1, name, " leading stride must be a multiple of 8 elements");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+
+void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
+             bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, const VocabArgs* vocab,
+             int force_bn) {
+  check_operand(A, "A");
+  check_operand(B, "B");
+  const c10::cuda::CUDAGuard guard(A.device());
+  const int64_t M = a_kmajor ? A.size(0) : A.size(1);
+  const int64_t K = a_kmajor ? A.size(1) : A.size(0);
+  const int64_t N = b_kmajor ? B.size(0) : B.size(1);
+  const int64_t Kb = b_kmajor ? B.size(1) : B.size(0);
+  TORCH_CHECK(K == Kb, "gemm: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(K > 0 && M > 0 && N > 0, "gemm: empty problem");
+  TORCH_CHECK(N % 8 == 0, "gemm: N must be a multiple of 8");
+  const bool is_stats = epi == EPI_VOCAB_STATS;
+  TORCH_CHECK(is_stats || (D.is_cuda() && D.dim() == 2 && D.stride(1) == 1), "gemm: bad output");
+  TORCH_CHECK((epi != EPI_VOCAB_STATS && epi != EPI_VOCAB_GRAD) || vocab != nullptr, "gemm: vocab epilogue needs row data");
+  const bool d_f32 = !is_stats && D.scalar_type() == at::kFloat;
+  if (!is_stats) {
+    TORCH_CHECK(d_f32 || D.scalar_type() == at::kBFloat16, "gemm: output must be bf16 or fp32");
+    TORCH_CHECK(!accumulate || d_f32, "gemm: accumulate needs an fp32 output");
+    TORCH_CHECK(D.size(0) == M && D.size(1) == (epi == EPI_SWIGLU ? N / 2 : N), "gemm: output shape mismatch");
+    TORCH_CHECK(D.stride(0) % 8 == 0, "gemm: output leading stride must be a multiple of 8");
+  }
+
+  GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.D = is_stats ? nullptr : D.data_ptr();
+  p.ldd = is_stats ? 0 : D.stride(0);
+  if (vocab) {
+    p.targets = vocab->targets;
+    p.row_lse = vocab->lse;
+    p.row_ent = vocab->ent;
+    p.g_lp = vocab->g_lp;
+    p.g_ent = vocab->g_ent;
+    p.part = vocab->part;
+  }
+  p.d_f32 = d_f32;
+  p.alpha = static_cast<float>(alpha);
+  p.epi = static_cast<int>(epi);
+  p.accumulate = accumulate;
+  p.err = err_word(A.device().index());
+  if (bias.defined() && bias.numel()) {
+    TORCH_CHECK(bias.scalar_type() == at::kBFloat16 && bias.is_contiguous() && bias.numel() == N, "gemm: bad bias");
+    p.bias = reinterpret_cast<const __nv_bfloat16*>(bias.data_ptr());
+  }
+  if (residual.defined() && residual.numel()) {
+    TORCH_CHECK(residual.scalar_type() == at::kBFloat16 && residual.stride(1) == 1 && residual.size(0) == M &&
+                    residual.size(1) == N && residual.stride(0) % 8 == 0,
+                "gemm: bad residual");
+    p.residual = reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr());
+    p.ldr = residual.stride(0);
+  }
+  if (aux.defined() && aux.numel()) {
+    TORCH_CHECK(aux.scalar_type() == at::kBFloat16 && aux.stride(1) == 1 && aux.size(0) == M && aux.size(1) == N &&
+                    aux.stride(0) % 8 == 0,
+                "gemm: bad aux");
+    p.aux = reinterpret_cast<__nv_bfloat16*>(aux.data_ptr());
+    p.ld_aux = aux.stride(0);
+  }
+
+  const int sms = num_sms(A.device().index());
+  const int64_t tiles256 = ((M + kBM - 1) / kBM) * ((N + 255) / 256);
+  const int BN = force_bn ? force_bn : ((tiles256 >= sms || N > 4096) ? 256 : 128);
+  p.tiles_m = static_cast<int>((M + kBM - 1) / kBM);
+  p.tiles_n = static_cast<int>((N + BN - 1) / BN);
+  const int grid = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(p.tiles_m) * p.tiles_n, sms));
+
+  // tensor maps: inner dimension first
+  CUtensorMap ta, tb;
+  if (a_kmajor)
+    ta = make_tmap_2d_bf16(A.data_ptr(), K, M, A.stride(0), 64, 128);
+  else
+    ta = make_tmap_2d_bf16(A.data_ptr(), M, K, A.stride(0), 64, 64);
+  if (b_kmajor)
+    tb = make_tmap_2d_bf16(B.data_ptr(), K, N, B.stride(0), 64, BN);
+  else
+    tb = make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, 64);
+
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (a_kmajor && b_kmajor) {
+    BN == 256 ? launch<256, false, false>(ta, tb, p, grid, st) : launch<128, false, false>(ta, tb, p, grid, st);
+  } else if (a_kmajor && !b_kmajor) {
+    BN == 256 ? launch<256, false, true>(ta, tb, p, grid, st) : launch<128, false, true>(ta, tb, p, grid, st);
+  } else if (!a_kmajor && !b_kmajor) {
+    BN == 256 ? launch<256, true, true>(ta, tb, p, grid, st) : launch<128, true, true>(ta, tb, p, grid, st);
+  } else {
+    TORCH_CHECK(false, "gemm: MN-major A with K-major B is not instantiated");
+  }
+}
+
+void gemm(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux, bool a_kmajor,
+          bool b_kmajor, double alpha, int64_t epi, bool accumulate) {
+  TORCH_CHECK(epi >= EPI_STORE && epi <= EPI_GELU_ERF, "gemm: epilogue code ", epi, " is internal");
+  gemm_ex(A, B, D, bias, residual, aux, a_kmajor, b_kmajor, alpha, epi, accumulate, nullptr, 0);
+}
+
+}  // namespace vlm

@@ -1,0 +1,65 @@
+// Declarations shared between kernel translation units and the Python bindings.
+#pragma once
+
+#include <torch/extension.h>
+
+namespace vlm {
+
+struct VocabArgs {
+  const int64_t* targets;
+  const float* lse;
+  const float* ent;
+  const float* g_lp;
+  const float* g_ent;
+  float* part;
+};
+
+// gemm_sm100.cu
+void gemm(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux, bool a_kmajor,
+          bool b_kmajor, double alpha, int64_t epi, bool accumulate);
+void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
+             bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, const VocabArgs* vocab,
+             int force_bn);
+
+// elementwise.cu
+void rms_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps);
+void rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor dx, at::Tensor dw);
+void layer_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor b, at::Tensor y, double eps);
+void qk_norm_rope_fwd(at::Tensor qkv, at::Tensor qw, at::Tensor kw, at::Tensor pos, at::Tensor inv_freq, at::Tensor ax,
+                      at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor rq, at::Tensor rk, int64_t nq, int64_t nkv,
+                      double eps);
+void qk_norm_rope_bwd(at::Tensor dq, at::Tensor dk, at::Tensor dv, at::Tensor qkv, at::Tensor qw, at::Tensor kw,
+                      at::Tensor pos, at::Tensor inv_freq, at::Tensor ax, at::Tensor rq, at::Tensor rk, at::Tensor dqkv,
+                      at::Tensor dqw, at::Tensor dkw, int64_t nq, int64_t nkv, double eps);
+void vision_rope(at::Tensor qkv, at::Tensor rc, at::Tensor q, at::Tensor k, at::Tensor v, int64_t n_heads);
+void swiglu_bwd(at::Tensor d_act, at::Tensor pre, at::Tensor out);
+void embed(at::Tensor tokens, at::Tensor table, at::Tensor out);
+void scatter_rows(at::Tensor h, at::Tensor rows, at::Tensor src, bool add);
+void embed_bwd(at::Tensor tokens, at::Tensor dh, at::Tensor dtable);
+void kv_write(at::Tensor k, at::Tensor v, at::Tensor kc, at::Tensor vc, at::Tensor seq, at::Tensor pos);
+void adamw(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor ph, at::Tensor scale, double lr, double b1,
+           double b2, double eps, double wd, int64_t step);
+void sq_norm_acc(at::Tensor x, at::Tensor out);
+void patchify(at::Tensor images, at::Tensor ms, at::Tensor out, int64_t patch, int64_t temporal, int64_t merge);
+
+// attention.cu
+void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at::Tensor o, at::Tensor lse,
+                    int64_t max_seqlen, bool causal, double scale);
+void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
+                    at::Tensor cu, at::Tensor dq, at::Tensor dk, at::Tensor dv, int64_t max_seqlen, bool causal,
+                    double scale);
+void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale);
+
+// sampler.cu
+void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, double temperature, int64_t top_k,
+            double top_p, int64_t seed, int64_t row_offset);
+
+// vocab.cu
+void vocab_logprob_fwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tensor logp, at::Tensor ent, at::Tensor lse);
+void vocab_logprob_bwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tensor lse, at::Tensor ent, at::Tensor g_lp,
+                       at::Tensor g_ent, at::Tensor dh, at::Tensor dw);
+
+// host_utils.cu
+int64_t read_and_clear_error(int64_t device);
+
+}  // namespace vlm

@@ -1,0 +1,248 @@
+"""GPU kernel tests: every CUDA op against its fp32 PyTorch oracle (vlmrl.ops.reference)."""
+
+import math
+
+import pytest
+import torch
+
+from vlmrl import ops
+from vlmrl.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ext_loaded():
+    from vlmrl.ops._ext import ext, loaded_path
+
+    ext()
+    assert loaded_path().endswith(".so")
+
+
+def _r(*shape, scale=1.0, dtype=torch.bfloat16, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device=DEV) * scale).to(dtype)
+
+
+def _close(out, exp, rtol=2e-2, atol=2e-2, name=""):
+    out, exp = out.float(), exp.float()
+    err = (out - exp).abs().max().item()
+    lim = atol + rtol * exp.abs().max().item()
+    assert err <= lim, f"{name}: max err {err:.4g} > {lim:.4g}"
+
+
+def _no_device_error():
+    from vlmrl.ops._ext import ext
+
+    assert ext().read_and_clear_error(torch.cuda.current_device()) == 0
+
+
+def test_extension_loaded():
+    _ext_loaded()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (200, 392, 136), (1000, 2056, 520), (64, 6144, 2560), (4096, 4096, 2560)])
+def test_gemm_nt(M, N, K):
+    a, b = _r(M, K, seed=1), _r(N, K, seed=2)
+    bias, res = _r(N, seed=3), _r(M, N, seed=4)
+    out = ops.gemm(a, b)
+    _close(out, ref.gemm(a, b, out_dtype=torch.float32), name="nt")
+    out = ops.gemm(a, b, bias=bias, residual=res, alpha=0.5)
+    _close(out, ref.gemm(a, b, bias=bias, residual=res, alpha=0.5, out_dtype=torch.float32), name="nt+epi")
+    out32 = ops.gemm(a, b, out_dtype=torch.float32)
+    _close(out32, ref.gemm(a, b, out_dtype=torch.float32), rtol=5e-3, atol=5e-3, name="nt f32")
+    _no_device_error()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (192, 264, 200), (2048, 2560, 9728)])
+def test_gemm_nn_tn(M, N, K):
+    dy = _r(M, K, seed=5)          # [M, K]
+    w = _r(K, N, seed=6)           # stored [K, N] (MN-major B)
+    _close(ops.gemm(dy, w, b_kmajor=False), dy.float() @ w.float(), name="nn")
+    x = _r(K, N, seed=7)           # dW [M?]: A stored [K, M], B stored [K, N]
+    a = _r(K, M, seed=8)
+    acc = torch.ones(M, N, device=DEV, dtype=torch.float32)
+    ops.gemm(a, x, a_kmajor=False, b_kmajor=False, accumulate=acc)
+    _close(acc, a.float().t() @ x.float() + 1.0, rtol=5e-3, atol=5e-3, name="tn acc")
+    _no_device_error()
+
+
+def test_gemm_activation_epilogues():
+    M, N, K = 300, 512, 256
+    x, w = _r(M, K, seed=9), _r(N, K, scale=0.1, seed=10)
+    act, pre = ops.linear_swiglu(x, w)
+    pre_ref = ref.gemm(x, w, out_dtype=torch.float32)
+    _close(pre, pre_ref, name="swiglu pre")
+    _close(act, ref.swiglu_interleaved(pre_ref.to(torch.bfloat16)), name="swiglu act")
+    b = _r(N, seed=11)
+    for epi, approx in ((ops.EPI_GELU_TANH, "tanh"), (ops.EPI_GELU_ERF, "none")):
+        out = ops.gemm(x, w, bias=b, epilogue=epi)
+        _close(out, ref.gelu(ref.gemm(x, w, bias=b, out_dtype=torch.float32), approx), name=f"gelu {approx}")
+    _no_device_error()
+
+
+def test_norms():
+    x, w = _r(333, 2560, seed=12), (1 + 0.1 * _r(2560, seed=13).float()).to(torch.bfloat16)
+    y, r = ops.rms_norm(x, w, 1e-6)
+    yr, rr = ref.rms_norm(x, w, 1e-6)
+    _close(y, yr, name="rms")
+    _close(r, rr, rtol=1e-4, atol=1e-5, name="rstd")
+    dy = _r(333, 2560, seed=14)
+    dw = torch.zeros(2560, device=DEV)
+    dx = ops.rms_norm_bwd(dy, x, w, r, dw_accum=dw)
+    dxr, dwr = ref.rms_norm_bwd(dy, x, w, rr)
+    _close(dx, dxr, name="rms dx")
+    _close(dw, dwr, rtol=1e-3, atol=1e-3, name="rms dw")
+    b = _r(1024, seed=15)
+    x2, w2 = _r(77, 1024, seed=16), _r(1024, seed=17)
+    _close(ops.layer_norm(x2, w2, b, 1e-6), ref.layer_norm(x2, w2, b, 1e-6), name="layernorm")
+
+
+@pytest.mark.parametrize("D,nq,nkv", [(128, 32, 8), (32, 4, 2)])
+def test_qk_norm_rope(D, nq, nkv):
+    T = 97
+    qkv = _r(T, (nq + 2 * nkv) * D, seed=18)
+    qw, kw = (1 + 0.1 * _r(D, seed=19).float()).bfloat16(), (1 + 0.1 * _r(D, seed=20).float()).bfloat16()
+    pos = torch.randint(0, 500, (3, T), device=DEV, dtype=torch.int32)
+    rope = ops.RopeCfg(D, 5e6, (24, 20, 20) if D == 128 else (6, 5, 5), True)
+    q, k, v, rq, rk = ops.qk_norm_rope(qkv, qw, kw, pos, rope, n_q=nq, n_kv=nkv, eps=1e-6)
+    qr, kr, vr, rqr, rkr = ref.qk_norm_rope(qkv, qw, kw, pos, n_q=nq, n_kv=nkv, head_dim=D, theta=5e6,
+                                            section=rope.section, interleaved=True, eps=1e-6)
+    _close(q, qr, name="q")
+    _close(k, kr, name="k")
+    _close(v, vr, rtol=0, atol=0, name="v")
+    dq, dk, dv = _r(T, nq, D, seed=21), _r(T, nkv, D, seed=22), _r(T, nkv, D, seed=23)
+    dqw, dkw = torch.zeros(D, device=DEV), torch.zeros(D, device=DEV)
+    dqkv = ops.qk_norm_rope_bwd(dq, dk, dv, qkv, qw, kw, pos, rq, rk, rope, n_q=nq, n_kv=nkv, eps=1e-6,
+                                dqw_accum=dqw, dkw_accum=dkw)
+    dref, dqwr, dkwr = ref.qk_norm_rope_bwd(dq, dk, dv, qkv, qw, kw, pos, rqr, rkr, n_q=nq, n_kv=nkv, head_dim=D,
+                                            theta=5e6, section=rope.section, interleaved=True, eps=1e-6)
+    _close(dqkv, dref, name="dqkv")
+    _close(dqw, dqwr, rtol=1e-3, atol=1e-2, name="dqw")
+    _close(dkw, dkwr, rtol=1e-3, atol=1e-2, name="dkw")
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,causal", [(128, 8, 2, True), (64, 4, 4, False), (32, 4, 2, True), (16, 4, 4, False)])
+def test_flash_attn(D, Hq, Hkv, causal):
+    lens = [1, 63, 64, 130, 388, 17]
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=DEV)
+    T = sum(lens)
+    q, k, v = _r(T, Hq, D, seed=24), _r(T, Hkv, D, seed=25), _r(T, Hkv, D, seed=26)
+    scale = 1 / math.sqrt(D)
+    o, lse = ops.flash_attn(q, k, v, cu, max(lens), causal=causal, scale=scale)
+    orf, lser = ref.flash_attn(q, k, v, cu, max(lens), causal=causal, scale=scale)
+    _close(o, orf, name="attn o")
+    _close(lse, lser, rtol=1e-3, atol=2e-3, name="attn lse")
+    do = _r(T, Hq, D, seed=27)
+    dq, dk, dv = ops.flash_attn_bwd(do, q, k, v, o, lse, cu, max(lens), causal=causal, scale=scale)
+    dqr, dkr, dvr = ref.flash_attn_bwd(do, q, k, v, orf, lser, cu, max(lens), causal=causal, scale=scale)
+    _close(dq, dqr, name="dq")
+    _close(dk, dkr, name="dk")
+    _close(dv, dvr, name="dv")
+
+
+def test_decode_attn_and_kv_write():
+    B, Hq, Hkv, D, Tmax = 5, 32, 8, 128, 300
+    kc = torch.zeros(B, Hkv, Tmax, D, device=DEV, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    lens = torch.tensor([1, 17, 128, 299, 200], device=DEV, dtype=torch.int32)
+    k, v = _r(int(lens.sum()), Hkv, D, seed=28), _r(int(lens.sum()), Hkv, D, seed=29)
+    seq = torch.repeat_interleave(torch.arange(B, device=DEV), lens.long())
+    pos = torch.cat([torch.arange(int(n), device=DEV) for n in lens])
+    ops.kv_write(k, v, kc, vc, seq, pos)
+    kc2, vc2 = torch.zeros_like(kc), torch.zeros_like(vc)
+    kc2[seq, :, pos] = k
+    vc2[seq, :, pos] = v
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    q = _r(B, Hq, D, seed=30)
+    _close(ops.decode_attn(q, kc, vc, lens), ref.decode_attn(q, kc, vc, lens, scale=1 / math.sqrt(D)), name="decode")
+
+
+def test_embedding_ops():
+    V, H, T = 1000, 256, 77
+    table = _r(V, H, seed=31)
+    tok = torch.randint(0, V, (T,), device=DEV)
+    h = ops.embed(tok, table)
+    assert torch.equal(h, table[tok])
+    rows = torch.tensor([3, 9, 40], device=DEV)
+    src = _r(3, H, seed=32)
+    h2 = h.clone()
+    ops.scatter_rows_(h2, rows, src, add=True)
+    _close(h2, ref.scatter_rows(h, rows, src, True), name="scatter add")
+    ops.scatter_rows_(h2, rows, src, add=False)
+    assert torch.equal(h2[rows], src)
+    dh = _r(T, H, seed=33)
+    tok2 = tok.clone()
+    tok2[5] = -1
+    dt = torch.zeros(V, H, device=DEV)
+    ops.embed_bwd(tok2, dh, dt)
+    _close(dt, ref.embed_bwd(tok2, dh, torch.zeros(V, H, device=DEV)), rtol=1e-5, atol=1e-5, name="embed bwd")
+
+
+def test_swiglu_bwd_and_vision_rope():
+    pre, da = _r(50, 2 * 384, seed=34), _r(50, 384, seed=35)
+    _close(ops.swiglu_bwd(da, pre), ref.swiglu_bwd(da, pre), name="swiglu bwd")
+    N, H, D = 64, 16, 64
+    qkv = _r(N, 3 * H * D, seed=36)
+    rc = torch.randint(0, 40, (N, 2), device=DEV, dtype=torch.int32)
+    for a, b in zip(ops.vision_rope(qkv, rc, n_heads=H, head_dim=D), ref.vision_rope(qkv, rc, n_heads=H, head_dim=D)):
+        _close(a, b, name="vision rope")
+
+
+def test_patchify():
+    from vlmrl.utils.vlm import CLIP_MEAN, CLIP_STD
+
+    img = torch.randint(0, 256, (3, 64, 96, 3), device=DEV, dtype=torch.uint8)
+    out = ops.patchify_uint8(img, patch=16, temporal=2, merge=2, mean=CLIP_MEAN.tolist(), std=CLIP_STD.tolist())
+    exp = ref.patchify_uint8(img, patch=16, temporal=2, merge=2, mean=CLIP_MEAN.tolist(), std=CLIP_STD.tolist())
+    _close(out, exp, rtol=1e-2, atol=1e-2, name="patchify")
+
+
+@pytest.mark.parametrize("M,V,H", [(200, 1000, 128), (1100, 151936, 2560)])
+def test_vocab_logprob(M, V, H):
+    h, w = _r(M, H, seed=37), _r(V, H, scale=0.05, seed=38)
+    tgt = torch.randint(0, V, (M,), device=DEV)
+    logp, ent, lse = ops.vocab_logprob(h, w, tgt)
+    lr, er, sr = ref.vocab_logprob(h, w, tgt)
+    _close(lse, sr, rtol=1e-4, atol=1e-3, name="lse")
+    _close(logp, lr, rtol=1e-4, atol=1e-3, name="logp")
+    _close(ent, er, rtol=1e-4, atol=1e-3, name="entropy")
+    if V > 10000:
+        return
+    g1, g2 = torch.randn(M, device=DEV), torch.randn(M, device=DEV)
+    dw = torch.zeros(V, H, device=DEV)
+    dh = ops.vocab_logprob_bwd(h, w, tgt, lse, ent, g1, g2, dw)
+    dhr, dwr = ref.vocab_logprob_bwd(h, w, tgt, sr, er, g1, g2)
+    _close(dh, dhr, rtol=3e-2, atol=3e-2, name="dh")
+    _close(dw, dwr, rtol=3e-2, atol=3e-2, name="dw")
+    _no_device_error()
+
+
+@pytest.mark.parametrize("k,p,temp", [(5, 0.9, 0.7), (50, 0.95, 1.0), (1024, 1.0, 0.7)])
+def test_sampler_matches_oracle(k, p, temp):
+    B, V = 16, 151936
+    logits = torch.randn(B, V, device=DEV) * 3
+    tok, lp = ops.sample(logits, temperature=temp, top_k=k, top_p=p, seed=1234, step=7)
+    tr, lr = ref.sample(logits.cpu(), temperature=temp, top_k=k, top_p=p, seed=1234, step=7)
+    agree = (tok.cpu() == tr).float().mean().item()
+    assert agree >= 0.9, f"token agreement {agree}"
+    same = tok.cpu() == tr
+    torch.testing.assert_close(lp.cpu()[same], lr[same], atol=1e-3, rtol=1e-3)
+
+
+def test_adamw_and_sqnorm():
+    n = 10000
+    p = torch.randn(n, device=DEV)
+    g = torch.randn(n, device=DEV)
+    m, v = torch.zeros(n, device=DEV), torch.zeros(n, device=DEV)
+    p2, g2, m2, v2 = p.cpu().clone(), g.cpu(), m.cpu().clone(), v.cpu().clone()
+    ph = torch.empty(n, device=DEV, dtype=torch.bfloat16)
+    for step in (1, 2, 3):
+        ops.adamw_(p, g, m, v, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=step,
+                   grad_scale=0.5, p_half=ph)
+        ref.adamw_(p2, g2, m2, v2, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=step,
+                   grad_scale=0.5)
+    torch.testing.assert_close(p.cpu(), p2, atol=1e-6, rtol=1e-5)
+    s = ops.sq_norm(g)
+    torch.testing.assert_close(s.cpu()[0], (g2 ** 2).sum(), rtol=1e-4, atol=1e-3)
