@@ -1,0 +1,269 @@
+#!/usr/bin/env python
+"""GRPO RL steps/sec (+ rollout decode tok/s) on the Qwen3-VL-4B architecture, 1..8 B200s.
+
+Workload (random-init weights, synthetic data): groups_per_batch 8 x group_size 8
+= 64 sequences per RL step, one 448x448 uniform-random RGB image (784 patches ->
+196 image tokens) + 64 uniform-random prompt tokens per prompt, 128 sampled
+tokens (temperature 0.7, top-p 0.9, top-k 5), geodesic reward on coordinates
+parsed from the response (0 when unparseable), PPO clip 0.2, KL to a frozen
+reference copy of the initial weights, AdamW lr 5e-7, 2 minibatches, bf16
+compute with fp32 master weights and moments.  One RL step = vision encode ->
+prefill -> 128-token KV-cache decode -> rewards -> reference + old-policy scoring
+-> 2 x (forward, backward, AdamW).  With N GPUs the global batch stays 64
+(strong scaling): each rank rolls out 8/N groups, FSDP shards the optimizer state.
+
+Timing: W untimed warm-up steps, then K steps bracketed by barrier +
+synchronize and timed with CUDA events on the launching stream; the max over
+ranks is reported.  The per-step working set (8.8 GB of weights) exceeds the
+126 MB L2, so no flush is needed.  ``e2e`` re-times K steps by wall clock
+through the public ``GRPOTrainer.step`` API, which copies the step's images
+from pinned host memory and reads back tokens, rewards and metrics.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+METRIC = "GRPO RL steps/sec + rollout decode tok/s, Qwen3-VL-4B, 1/2/4/8 B200"
+
+
+def parse():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--preset", default="qwen3vl_4b")
+    ap.add_argument("--groups", type=int, default=8)
+    ap.add_argument("--group-size", type=int, default=8)
+    ap.add_argument("--max-new", type=int, default=128)
+    ap.add_argument("--prompt-tokens", type=int, default=64)
+    ap.add_argument("--image", type=int, default=448)
+    ap.add_argument("--minibatches", type=int, default=2)
+    ap.add_argument("--top-k", type=int, default=5)
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def reference_arm(args):
+    why = ("reference is JAX 0.6.1/Flax/Optax (uv.lock); no jax, flax or optax wheel exists in the offline "
+           "wheelhouse, so `pip install --no-deps` of the package succeeds but it cannot be imported")
+    print(json.dumps({"impl": "reference", "metric": METRIC, "unavailable": why, "n_gpus": args.gpus}))
+    return 0
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1])]
+        pw = [num(r[3]) or 0.0 for r in rows]
+        loaded = [num(r[1]) for r in rows if (num(r[3]) or 0) > 300 and num(r[1])] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": num(rows[0][2]),
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+    import torch
+    import torch.distributed as dist
+
+    from vlmrl import ops
+    from vlmrl.core.optim import AdamWConfig
+    from vlmrl.core.ppo import TrainerConfig
+    from vlmrl.core.trainer import GRPOTrainer
+    from vlmrl.envs.base import create_env
+    from vlmrl.models.qwen3vl.api import Qwen3VLModel
+    from vlmrl.models.qwen3vl.config import get_preset
+    from vlmrl.utils.tokenizer import ByteTokenizer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+
+    spec = get_preset(args.preset)
+    tok = ByteTokenizer(spec.text.vocab_size)
+    cfg = TrainerConfig(temperature=0.7, top_p=0.9, top_k=args.top_k, max_new_tokens=args.max_new,
+                        groups_per_batch=args.groups, group_size=args.group_size, kl_ref_coef=0.01,
+                        n_minibatches=args.minibatches, clip_epsilon=0.2, adaptive_kl=False)
+    adamw = AdamWConfig(lr=5e-7, weight_decay=0.01, max_grad_norm=1.0)
+    env = create_env("synthetic_geo", tok, image_size=args.image, prompt_tokens=args.prompt_tokens, num_tasks=1024,
+                     seed=0)
+    if world > 1:
+        from vlmrl.parallel.fsdp import build_fsdp_models
+
+        model, ref_model, train_state = build_fsdp_models(spec, adamw, seed=0, device=dev)
+    else:
+        model = Qwen3VLModel(spec, device=dev, dtype=torch.bfloat16, seed=0)
+        text_units = {k: v for k, v in model.params.units.items() if k != "visual"}
+        ref_model = Qwen3VLModel(spec, units=text_units, device=dev, dtype=torch.bfloat16)
+        train_state = None
+    trainer = GRPOTrainer(model, tok, env, cfg, adamw, ref_model=ref_model, seed=0, rank=rank, world_size=world,
+                          train_state=train_state)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        trainer.step()
+    ops.check_errors()
+
+    # ---- device-timed region
+    barrier()
+    torch.cuda.synchronize()
+    gen = trainer.generator
+    l0, g0 = ops.launch_count(), gen.graph_kernel_launches
+    decode_ms, decode_tokens, gen_tokens = 0.0, 0, 0
+    with ClockSampler(dev.index) as clocks:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        metrics = []
+        for _ in range(args.steps):
+            m = trainer.step()
+            metrics.append(m)
+            decode_ms += gen.decode_time_ms()
+            decode_tokens += gen.last_decode_tokens
+            gen_tokens += int(m["tokens/generated"])
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    launches = (ops.launch_count() - l0) + (gen.graph_kernel_launches - g0)
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    decode_ms = max_over_ranks(decode_ms / args.steps)
+    ops.check_errors()
+    clk = clocks.summary()
+
+    # ---- end-to-end (wall clock, public API, includes pinned H2D of images and D2H of results)
+    e2e = None
+    if not args.no_e2e:
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            trainer.step()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
+        img_bytes = args.groups // world * args.image * args.image * 3
+        prompt_len = 196 * (args.image // 448) ** 2 + 2 + args.prompt_tokens
+        seqs = args.groups * args.group_size // world
+        h2d = img_bytes + seqs * (prompt_len + args.max_new) * 8 * 5  # images + packed ids/positions/indices
+        d2h = seqs * args.max_new * 12 + 8 * 64                         # tokens, logprobs, lengths, metrics
+        e2e = {"value": 1.0 / e2e_s, "unit": "RL steps/s", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3}
+
+    total_seqs = args.groups * args.group_size
+    decode_tok_s = (total_seqs * (args.max_new - 1)) / (decode_ms / 1e3) if decode_ms > 0 else None
+    last = metrics[-1]
+    out = {
+        "metric": METRIC,
+        "value": 1000.0 / ms,
+        "unit": "RL steps/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (uniform-random 448x448 RGB images and prompt ids, uniform-on-sphere targets), random-init weights",
+        "config": {"model": f"{args.preset} architecture (random init)", "global_batch": total_seqs,
+                   "seq_len": f"{196 + 2 + args.prompt_tokens} prompt + {args.max_new} new",
+                   "parallelism": f"fsdp{world}" if world > 1 else "single-gpu",
+                   "groups_per_batch": args.groups, "group_size": args.group_size, "minibatches": args.minibatches,
+                   "kl_ref_coef": 0.01, "top_k": args.top_k, "top_p": 0.9, "temperature": 0.7,
+                   "l2": "no flush: per-step working set (8.8 GB weights) >> 126 MB L2"},
+        "decode_tok_s": decode_tok_s,
+        "decode_ms_per_step": decode_ms,
+        "rollout_tokens_per_step": gen_tokens / max(1, args.steps) * world,
+        "phase_ms": {k: v for k, v in last.items() if k.startswith("time/")},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "e2e": e2e,
+    }
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

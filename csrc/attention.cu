@@ -660,7 +660,7 @@ static void fwd_dispatch(const at::Tensor& q, const at::Tensor& k, const at::Ten
     set_smem(kern, smem);
     std::apply([&](auto... a) { kern<<<grid, 128, smem, st>>>(a...); }, args);
   }
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at::Tensor o, at::Tensor lse,
@@ -698,7 +698,7 @@ static void bwd_dispatch(const at::Tensor& dout, const at::Tensor& q, const at::
                                   lse.data_ptr<float>(), delta.data_ptr<float>(), cu.data_ptr<int>(),
                                   reinterpret_cast<bf16*>(dk.data_ptr()), reinterpret_cast<bf16*>(dv.data_ptr()), Hq, Hkv, T,
                                   sl2, scale);
-    VLM_CUDA_CHECK(cudaGetLastError());
+    VLM_LAUNCHED();
   }
   {
     const dim3 grid((max_seqlen + 63) / 64, Hq, B);
@@ -709,7 +709,7 @@ static void bwd_dispatch(const at::Tensor& dout, const at::Tensor& q, const at::
                                   reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
                                   lse.data_ptr<float>(), delta.data_ptr<float>(), cu.data_ptr<int>(),
                                   reinterpret_cast<bf16*>(dq.data_ptr()), Hq, Hkv, T, sl2, scale);
-    VLM_CUDA_CHECK(cudaGetLastError());
+    VLM_LAUNCHED();
   }
 }
 
@@ -726,7 +726,7 @@ void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, a
   attn_delta_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const bf16*>(dout.data_ptr()), reinterpret_cast<const bf16*>(o.data_ptr()), delta.data_ptr<float>(),
       T, Hq, D);
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
   const int ms = static_cast<int>(max_seqlen);
   const float sc = static_cast<float>(scale);
   switch (D) {
@@ -751,7 +751,7 @@ static void decode_dispatch(const at::Tensor& q, const at::Tensor& kc, const at:
       reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(kc.data_ptr()),
       reinterpret_cast<const bf16*>(vc.data_ptr()), lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()), Hq, Hkv,
       Tmax, scale);
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale) {

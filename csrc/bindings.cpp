@@ -27,4 +27,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("vocab_logprob_fwd", &vlm::vocab_logprob_fwd);
   m.def("vocab_logprob_bwd", &vlm::vocab_logprob_bwd);
   m.def("read_and_clear_error", &vlm::read_and_clear_error);
+  m.def("launch_count", &vlm::launch_count, "kernel launches issued by this library so far");
 }

@@ -116,7 +116,7 @@ void rms_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, dou
       reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
       reinterpret_cast<bf16*>(y.data_ptr()), rstd.defined() && rstd.numel() ? rstd.data_ptr<float>() : nullptr, M, H,
       static_cast<float>(eps));
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 void rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor dx, at::Tensor dw) {
@@ -131,7 +131,7 @@ void rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at
       reinterpret_cast<const bf16*>(dy.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
       reinterpret_cast<const bf16*>(w.data_ptr()), rstd.data_ptr<float>(), reinterpret_cast<bf16*>(dx.data_ptr()),
       has_dw ? dw.data_ptr<float>() : nullptr, M, H);
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 // ------------------------------------------------------------------ LayerNorm (ViT, forward only)
@@ -164,7 +164,7 @@ void layer_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor b, at::Tensor y, doub
       reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
       b.defined() && b.numel() ? reinterpret_cast<const bf16*>(b.data_ptr()) : nullptr,
       reinterpret_cast<bf16*>(y.data_ptr()), M, H, static_cast<float>(eps));
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 // ------------------------------------------------------------------ q/k RMSNorm + MRoPE
@@ -292,7 +292,7 @@ void qk_norm_rope_fwd(at::Tensor qkv, at::Tensor qw, at::Tensor kw, at::Tensor p
       ax.data_ptr<int>(), reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(k.data_ptr()),
       reinterpret_cast<bf16*>(v.data_ptr()), rq.data_ptr<float>(), rk.data_ptr<float>(), T, static_cast<int>(nq),
       static_cast<int>(nkv), D, static_cast<float>(eps));
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 void qk_norm_rope_bwd(at::Tensor dq, at::Tensor dk, at::Tensor dv, at::Tensor qkv, at::Tensor qw, at::Tensor kw,
@@ -311,7 +311,7 @@ void qk_norm_rope_bwd(at::Tensor dq, at::Tensor dk, at::Tensor dv, at::Tensor qk
       pos.stride(0), inv_freq.data_ptr<float>(), ax.data_ptr<int>(), rq.data_ptr<float>(), rk.data_ptr<float>(),
       reinterpret_cast<bf16*>(dqkv.data_ptr()), dqw.defined() && dqw.numel() ? dqw.data_ptr<float>() : nullptr,
       dkw.defined() && dkw.numel() ? dkw.data_ptr<float>() : nullptr, T, static_cast<int>(nq), static_cast<int>(nkv), D);
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 // ------------------------------------------------------------------ ViT 2-D rotary
@@ -354,7 +354,7 @@ void vision_rope(at::Tensor qkv, at::Tensor rc, at::Tensor q, at::Tensor k, at::
   vision_rope_kernel<<<static_cast<int>((total + 255) / 256), 256, 0, cur_stream()>>>(
       reinterpret_cast<const bf16*>(qkv.data_ptr()), rc.data_ptr<int>(), reinterpret_cast<bf16*>(q.data_ptr()),
       reinterpret_cast<bf16*>(k.data_ptr()), reinterpret_cast<bf16*>(v.data_ptr()), N, static_cast<int>(n_heads), D);
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 // ------------------------------------------------------------------ SwiGLU backward
@@ -378,7 +378,7 @@ void swiglu_bwd(at::Tensor d_act, at::Tensor pre, at::Tensor out) {
   swiglu_bwd_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, cur_stream()>>>(
       reinterpret_cast<const bf16*>(d_act.data_ptr()), reinterpret_cast<const bf16*>(pre.data_ptr()),
       reinterpret_cast<bf16*>(out.data_ptr()), n);
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 // ------------------------------------------------------------------ embedding gather / scatter
@@ -401,7 +401,7 @@ void embed(at::Tensor tokens, at::Tensor table, at::Tensor out) {
   const c10::cuda::CUDAGuard g(table.device());
   embed_kernel<<<T, 128, 0, cur_stream()>>>(tokens.data_ptr<int64_t>(), reinterpret_cast<const bf16*>(table.data_ptr()),
                                             reinterpret_cast<bf16*>(out.data_ptr()), T, H, table.size(0));
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 __global__ void scatter_rows_kernel(bf16* __restrict__ h, const int64_t* __restrict__ rows, const bf16* __restrict__ src,
@@ -421,7 +421,7 @@ void scatter_rows(at::Tensor h, at::Tensor rows, at::Tensor src, bool add) {
   scatter_rows_kernel<<<R, 128, 0, cur_stream()>>>(reinterpret_cast<bf16*>(h.data_ptr()), rows.data_ptr<int64_t>(),
                                                    reinterpret_cast<const bf16*>(src.data_ptr()), R,
                                                    static_cast<int>(h.size(1)), add ? 1 : 0);
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 __global__ void embed_bwd_kernel(const int64_t* __restrict__ tok, const bf16* __restrict__ dh, float* __restrict__ dt,
@@ -440,7 +440,7 @@ void embed_bwd(at::Tensor tokens, at::Tensor dh, at::Tensor dtable) {
   const c10::cuda::CUDAGuard g(dh.device());
   embed_bwd_kernel<<<T, 256, 0, cur_stream()>>>(tokens.data_ptr<int64_t>(), reinterpret_cast<const bf16*>(dh.data_ptr()),
                                                 dtable.data_ptr<float>(), T, static_cast<int>(dh.size(1)));
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 // ------------------------------------------------------------------ KV-cache write
@@ -471,7 +471,7 @@ void kv_write(at::Tensor k, at::Tensor v, at::Tensor kc, at::Tensor vc, at::Tens
       reinterpret_cast<const bf16*>(k.data_ptr()), reinterpret_cast<const bf16*>(v.data_ptr()),
       reinterpret_cast<bf16*>(kc.data_ptr()), reinterpret_cast<bf16*>(vc.data_ptr()), seq.data_ptr<int64_t>(),
       pos.data_ptr<int64_t>(), T, static_cast<int>(k.size(1)), static_cast<int>(kc.size(2)), static_cast<int>(k.size(2)));
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 // ------------------------------------------------------------------ AdamW (optax.adamw semantics)
@@ -509,7 +509,7 @@ void adamw(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor ph
                                                  scale.data_ptr<float>(), n, static_cast<float>(lr), static_cast<float>(b1),
                                                  static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd),
                                                  bc1, bc2);
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 // ------------------------------------------------------------------ sum of squares (fp32 accumulate)
@@ -543,7 +543,7 @@ void sq_norm_acc(at::Tensor x, at::Tensor out) {
   else
     sq_norm_kernel<__nv_bfloat16><<<blocks, 256, 0, cur_stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), n, out.data_ptr<float>());
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 // ------------------------------------------------------------------ uint8 image -> patch rows
@@ -578,7 +578,7 @@ void patchify(at::Tensor images, at::Tensor ms, at::Tensor out, int64_t patch, i
   patchify_kernel<<<rows, 256, 0, cur_stream()>>>(images.data_ptr<uint8_t>(), ms.data_ptr<float>(),
                                                   reinterpret_cast<bf16*>(out.data_ptr()), N, H, W, static_cast<int>(patch),
                                                   static_cast<int>(temporal), static_cast<int>(merge));
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 }  // namespace vlm

@@ -435,7 +435,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParam
     configured = true;
   }
   kern<<<grid, 192, GemmCfg<BN>::SMEM, st>>>(ta, tb, p);
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 static void check_operand(const at::Tensor& t, const char* name) {

@@ -2,6 +2,7 @@
 // cached device properties and the per-device error word.
 #include <ATen/cuda/CUDAContext.h>
 
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -28,9 +29,13 @@ EncodeTiledFn encode_fn() {
 }
 
 std::mutex g_mu;
+std::atomic<int64_t> g_launches{0};
 std::vector<int*> g_err(64, nullptr);
 std::vector<int> g_sms(64, 0);
 }  // namespace
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+int64_t launch_count() { return g_launches.load(); }
 
 int* err_word(int device) {
   std::lock_guard<std::mutex> lk(g_mu);

@@ -16,6 +16,17 @@
 
 namespace vlm {
 
+// Host-side count of kernel launches issued by this library (graph captures count once per
+// captured launch).
+void note_launch();
+int64_t launch_count();
+
+#define VLM_LAUNCHED() \
+  do {                 \
+    VLM_CUDA_CHECK(cudaGetLastError()); \
+    ::vlm::note_launch();               \
+  } while (0)
+
 // Per-device error word written by bounded waits (0 = ok).  Allocated once per device.
 int* err_word(int device);
 // Reads and clears the error word of ``device`` (synchronises the current stream).

@@ -8,8 +8,8 @@
 //     cut (cumulative <= top_p, the first entry always kept), renormalisation;
 //  4. inverse-CDF draw with a Philox-4x32-10 uniform keyed by (seed, row, step),
 //     so the draw is reproducible and independent of launch order.
-// The step counter is read from device memory, so a captured CUDA graph can
-// advance it between replays.  k <= 1024 (k = 0 or k > 1024 uses 1024).
+// The step counter and the seed are read from device memory, so a captured CUDA
+// graph can advance / reseed them between replays.  k <= 1024 (k = 0 or k > 1024 uses 1024).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -31,7 +31,7 @@ VLM_DEV uint32_t ordered_key(float f) {
 __global__ void __launch_bounds__(kSampThreads) sample_kernel(const float* __restrict__ logits, int64_t ld, int V,
                                                               int64_t* __restrict__ tok_out, float* __restrict__ lp_out,
                                                               const int64_t* __restrict__ step_ptr, float inv_temp,
-                                                              int k, float top_p, unsigned long long seed,
+                                                              int k, float top_p, const int64_t* __restrict__ seed_ptr,
                                                               long long row_offset) {
   __shared__ uint32_t hist[256];
   __shared__ uint32_t s_prefix;
@@ -147,6 +147,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const float* __res
   const float kept_total = cum[keep - 1];
   // 4. inverse-CDF draw
   const unsigned int step = static_cast<unsigned int>(*step_ptr);
+  const unsigned long long seed = static_cast<unsigned long long>(*seed_ptr);
   const float u = philox_uniform(seed, static_cast<unsigned long long>(row + row_offset), step) * kept_total;
   if (tid == 0) s_choice = keep - 1;
   __syncthreads();
@@ -163,10 +164,11 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const float* __res
   }
 }
 
-void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, double temperature, int64_t top_k,
-            double top_p, int64_t seed, int64_t row_offset) {
+void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, at::Tensor seed, double temperature,
+            int64_t top_k, double top_p, int64_t row_offset) {
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1, "sample: fp32 [B, V]");
   TORCH_CHECK(step.scalar_type() == at::kLong && step.is_cuda(), "sample: step must be an int64 CUDA tensor");
+  TORCH_CHECK(seed.scalar_type() == at::kLong && seed.is_cuda(), "sample: seed must be an int64 CUDA tensor");
   TORCH_CHECK(temperature > 0, "sample: temperature must be positive");
   const int B = static_cast<int>(logits.size(0));
   if (B == 0) return;
@@ -175,8 +177,8 @@ void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, d
   sample_kernel<<<B, kSampThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       logits.data_ptr<float>(), logits.stride(0), static_cast<int>(logits.size(1)), tok.data_ptr<int64_t>(),
       lp.data_ptr<float>(), step.data_ptr<int64_t>(), static_cast<float>(1.0 / temperature), k,
-      static_cast<float>(top_p), static_cast<unsigned long long>(seed), static_cast<long long>(row_offset));
-  VLM_CUDA_CHECK(cudaGetLastError());
+      static_cast<float>(top_p), seed.data_ptr<int64_t>(), static_cast<long long>(row_offset));
+  VLM_LAUNCHED();
 }
 
 }  // namespace vlm

@@ -51,8 +51,8 @@ void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, a
 void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale);
 
 // sampler.cu
-void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, double temperature, int64_t top_k,
-            double top_p, int64_t seed, int64_t row_offset);
+void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, at::Tensor seed, double temperature,
+            int64_t top_k, double top_p, int64_t row_offset);
 
 // vocab.cu
 void vocab_logprob_fwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tensor logp, at::Tensor ent, at::Tensor lse);
@@ -61,5 +61,6 @@ void vocab_logprob_bwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tenso
 
 // host_utils.cu
 int64_t read_and_clear_error(int64_t device);
+int64_t launch_count();
 
 }  // namespace vlm

@@ -67,7 +67,7 @@ void vocab_logprob_fwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tenso
   vocab_combine_kernel<<<static_cast<int>((M * 32 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const float4*>(part.data_ptr<float>()), tiles, static_cast<int>(M), logp.data_ptr<float>(),
       ent.data_ptr<float>(), lse.data_ptr<float>());
-  VLM_CUDA_CHECK(cudaGetLastError());
+  VLM_LAUNCHED();
 }
 
 void vocab_logprob_bwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tensor lse, at::Tensor ent, at::Tensor g_lp,

@@ -1,0 +1,177 @@
+"""PPO / GRPO learner: ``TrainerConfig``, ``collect`` and ``update`` (reference ``core/ppo.py:28-254``).
+
+``collect`` samples ``groups_per_batch x group_size`` episodes in one batched
+rollout and builds one packed batch per minibatch.  ``update`` runs, for every
+epoch and minibatch: the policy forward with activations saved, the per-token
+loss (``vlmrl.core.grpo.ppo_loss``), the explicit backward and one AdamW step.
+
+Old log-probs (``old_logprob_source``):
+* ``"policy"`` (default) — the policy's own scoring pass before any update, so
+  the first minibatch starts at ratio 1 (the first minibatch reuses its own
+  training forward; later minibatches are scored up front);
+* ``"sampler"`` — the sampler's log-probs (the reference's behaviour, which
+  uses the tempered/top-k masked distribution).
+KL to the frozen reference policy uses the reference model's log-probs on the
+same tokens, computed once per iteration.
+"""
+
+from __future__ import annotations
+
+from dataclasses import asdict, dataclass, field
+from typing import Any, Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from vlmrl.core.batching import pack_sequences
+from vlmrl.core.grpo import group_advantages, ppo_loss, token_advantages
+from vlmrl.core.kl import AdaptiveKL
+from vlmrl.core.minibatch import minibatch_indices
+from vlmrl.core.rollout import EpisodeBatch, collect_episodes
+from vlmrl.core.types import Rollout, SamplingConfig
+from vlmrl.models.qwen3vl.model import PackedBatch
+
+
+@dataclass
+class TrainerConfig:
+    temperature: float = 0.7
+    top_p: Optional[float] = 0.9
+    top_k: Optional[int] = 1024
+    max_new_tokens: int = 64
+    max_sequence_length: int = 2048
+    clip_epsilon: float = 0.2
+    entropy_coef: float = 0.0
+    kl_coef: float = 0.0
+    adaptive_kl: bool = False
+    kl_target: float = 0.02
+    kl_adapt_rate: float = 1.5
+    kl_coef_min: float = 1e-5
+    kl_coef_max: float = 0.5
+    ppo_minibatch: int = 64
+    ppo_epochs: int = 1
+    n_minibatches: int = 0
+    groups_per_batch: int = 16
+    group_size: int = 1
+    kl_ref_coef: float = 0.0
+    adv_norm: str = "group"
+    old_logprob_source: str = "policy"
+    vlm_min_pixels: int = -1
+    vlm_max_pixels: int = -1
+
+
+@dataclass
+class MiniBatch:
+    batch: PackedBatch
+    seq_index: np.ndarray          # episode indices in this minibatch
+    counts: np.ndarray             # scored tokens per sequence
+    adv_tok: torch.Tensor          # [M]
+    sampler_lp: torch.Tensor       # [M]
+    old_lp: Optional[torch.Tensor] = None
+    ref_lp: Optional[torch.Tensor] = None
+
+
+@dataclass
+class CollectResult:
+    episodes: EpisodeBatch
+    rewards: torch.Tensor
+    advantages: torch.Tensor
+    minibatches: List[MiniBatch] = field(default_factory=list)
+    rollout: Optional[Rollout] = None
+
+
+def sampling_config(cfg: TrainerConfig, eos_id: Optional[int], pad_id: int = 0) -> SamplingConfig:
+    return SamplingConfig(temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k, eos_id=eos_id,
+                          pad_id=pad_id, max_new_tokens=cfg.max_new_tokens)
+
+
+def _minibatch_count(cfg: TrainerConfig, n: int) -> int:
+    if cfg.n_minibatches and cfg.n_minibatches > 0:
+        return int(cfg.n_minibatches)
+    return max(1, n // max(1, int(cfg.ppo_minibatch)))
+
+
+def build_minibatches(model, eb: EpisodeBatch, adv_seq: torch.Tensor, n_minibatches: int,
+                      max_sequence_length: Optional[int] = None) -> List[MiniBatch]:
+    eps = eb.episodes
+    merge = model.spec.vision.spatial_merge_size
+    # vision rows per episode (episodes are stored contiguously in eb.vision)
+    counts_img = [sum(int(t) * (int(h) // merge) * (int(w) // merge) for t, h, w in ep.grids) for ep in eps]
+    starts = np.concatenate([[0], np.cumsum(counts_img)])
+    out: List[MiniBatch] = []
+    for idx in minibatch_indices(len(eps), n_minibatches, eb.group_size):
+        sub = [eps[i] for i in idx]
+        rows = np.concatenate([np.arange(starts[i], starts[i + 1]) for i in idx])
+        vis = eb.vision.select(torch.from_numpy(rows).to(eb.vision.tokens.device)) if eb.vision is not None else None
+        seqs = [np.asarray(e.full_tokens, np.int64) for e in sub]
+        if max_sequence_length:
+            seqs = [s[:int(max_sequence_length)] for s in seqs]
+        batch, counts = pack_sequences(model.spec, seqs, [e.prompt_length for e in sub], [e.grids for e in sub], vis,
+                                       device=model.device)
+        samp = np.concatenate([np.asarray(e.action_logprobs[:c], np.float32) for e, c in zip(sub, counts)])
+        out.append(MiniBatch(batch=batch, seq_index=idx, counts=counts,
+                             adv_tok=token_advantages(adv_seq[torch.from_numpy(idx)], counts, model.device),
+                             sampler_lp=torch.from_numpy(samp).to(model.device)))
+    return out
+
+
+def collect(env, tokenizer, model, ts, cfg: TrainerConfig, batch_size: Optional[int] = None, rng: int = 0, *,
+            eos_id: Optional[int] = None, generator=None, task_offset: int = 0, row_offset: int = 0) -> CollectResult:
+    """Roll out one iteration and build the minibatches (reference ``collect``, ``core/ppo.py:51-92``)."""
+    G = int(batch_size) if batch_size else int(cfg.groups_per_batch)
+    eb = collect_episodes(env, tokenizer, model, sampling_config(cfg, eos_id), groups_per_batch=G,
+                          group_size=cfg.group_size, seed=rng, task_offset=task_offset, generator=generator,
+                          min_pixels=cfg.vlm_min_pixels, max_pixels=cfg.vlm_max_pixels,
+                          max_sequence_length=cfg.max_sequence_length, row_offset=row_offset)
+    rewards = torch.tensor([e.reward for e in eb.episodes], dtype=torch.float32)
+    adv = group_advantages(rewards, cfg.group_size, cfg.adv_norm).to(model.device)
+    mbs = build_minibatches(model, eb, adv, _minibatch_count(cfg, len(eb.episodes)), cfg.max_sequence_length)
+    return CollectResult(episodes=eb, rewards=rewards, advantages=adv, minibatches=mbs)
+
+
+@torch.no_grad()
+def score(model, mb: MiniBatch) -> torch.Tensor:
+    logp, _, _ = model.token_logprobs(mb.batch, save=False)
+    return logp
+
+
+def update(ts, cr: CollectResult, cfg: TrainerConfig, *, ref_model=None, kl_ctrl: Optional[AdaptiveKL] = None,
+           kl_coef: Optional[float] = None) -> Tuple[Any, Dict[str, float]]:
+    """PPO/GRPO epochs over the collected minibatches; returns (train_state, host metrics)."""
+    model = ts.model
+    mbs = cr.minibatches
+    use_policy_old = cfg.old_logprob_source == "policy"
+    reuse_first = use_policy_old and cfg.ppo_epochs == 1
+    for i, mb in enumerate(mbs):
+        if not use_policy_old:
+            mb.old_lp = mb.sampler_lp
+        elif not (reuse_first and i == 0):
+            mb.old_lp = score(model, mb)
+        if ref_model is not None and cfg.kl_ref_coef > 0:
+            mb.ref_lp = score(ref_model, mb)
+    coef = float(cfg.kl_coef if kl_coef is None else kl_coef)
+    sums: Dict[str, torch.Tensor] = {}
+    n = 0
+    for _ in range(int(cfg.ppo_epochs)):
+        for mb in mbs:
+            logp, ent, ctx = model.token_logprobs(mb.batch, save=True)
+            if mb.old_lp is None:
+                mb.old_lp = logp.detach().clone()
+            _, g_lp, g_ent, m = ppo_loss(logp, ent, mb.old_lp, mb.adv_tok, clip_epsilon=cfg.clip_epsilon,
+                                         entropy_coef=cfg.entropy_coef, kl_coef=coef, ref_logp=mb.ref_lp,
+                                         kl_ref_coef=cfg.kl_ref_coef)
+            with torch.no_grad():
+                model.backward(ctx, g_lp, g_ent)
+            del ctx
+            m.update(ts.apply_gradients())
+            if kl_ctrl is not None:
+                coef = kl_ctrl.update(float(m["approx_kl"]), coef)
+            for k, v in m.items():
+                sums[k] = sums.get(k, 0.0) + v.detach().float()
+            n += 1
+    host = {k: float(v) / max(1, n) for k, v in sums.items()}
+    host["kl_coef"] = coef
+    return ts, host
+
+
+__all__ = ["TrainerConfig", "MiniBatch", "CollectResult", "sampling_config", "build_minibatches", "collect", "score",
+           "update"]

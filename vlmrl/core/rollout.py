@@ -1,0 +1,245 @@
+"""Environment <-> model glue: prompt preparation, batched episode collection, training batches.
+
+Counterpart of reference ``core/rollout.py:46-426``, batched instead of serial:
+
+* ``prepare_prompts`` turns observations into token ids + one vision encode for
+  every image of the batch.  Same-size uint8 images (the synthetic envs) are
+  copied to the GPU through one pinned buffer and patchified there; other
+  images go through ``preprocess_image`` (PIL bicubic, CPU).  Single-image
+  observations (``image``/``image_path`` + ``question``) use the chat template
+  of ``chat_prompt_with_image``; two-image observations (``image_left``,
+  ``image_right``, ``statement``) use ``chat_prompt_with_images`` with the
+  question ``"Look at the two images. {statement}"``; synthetic observations
+  carry token ids directly (vision block per image + prompt ids).
+* ``collect_episodes`` resets ``groups_per_batch`` tasks, samples
+  ``group_size`` responses per task in ONE batched generate call (the prompt is
+  prefilled once per group and its KV cache replicated), scores them with
+  ``env.step_list`` and returns an ``EpisodeBatch``.
+* ``episodes_to_training_batch`` builds the packed training batch (inputs
+  ``s[:-1]``, targets ``s[1:]``, loss rows on the action tokens) and the
+  ``Rollout`` record.  Actions are cut after the first EOS (inclusive), so
+  EOS padding is not trained on.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any, Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+
+from vlmrl.core.batching import pack_sequences
+from vlmrl.core.sampling import Generator
+from vlmrl.core.types import Rollout, SamplingConfig
+from vlmrl.envs.base import BaseEnv, BaseState
+from vlmrl.models.qwen3vl.model import VisionEmbeddings
+from vlmrl.utils.vlm import (DEFAULT_MAX_PIXELS, DEFAULT_MIN_PIXELS, chat_prompt_with_image, chat_prompt_with_images,
+                             preprocess_image, smart_resize)
+
+
+@dataclass
+class PreparedPrompt:
+    prompt_tokens: np.ndarray
+    prompt_length: int
+    grids: List[Tuple[int, int, int]]
+    prompt_text: str = ""
+
+
+@dataclass
+class Episode:
+    state: BaseState
+    observation: Any
+    prompt_text: str
+    prompt_tokens: np.ndarray
+    prompt_length: int
+    full_tokens: np.ndarray
+    full_logprobs: np.ndarray
+    action_tokens: List[int]
+    action_logprobs: np.ndarray
+    action_length: int
+    generated_text: str
+    grids: List[Tuple[int, int, int]]
+    reward: float
+    done: bool
+    info: Dict[str, Any] = field(default_factory=dict)
+    group_id: int = 0
+
+
+@dataclass
+class EpisodeBatch:
+    episodes: List[Episode]
+    raw_info: Dict[str, List[Any]]
+    vision: Optional[VisionEmbeddings] = None       # per episode, in episode order
+    group_size: int = 1
+
+
+def _images_of(obs) -> List[Any]:
+    if hasattr(obs, "images"):
+        return list(obs.images)
+    if hasattr(obs, "image_left") and hasattr(obs, "image_right"):
+        return [obs.image_left, obs.image_right]
+    img = getattr(obs, "image", None)
+    if img is None:
+        img = getattr(obs, "image_path", None)
+    if img is None:
+        raise ValueError("Observation must expose `image` or `image_path` for vision sampling.")
+    return [img]
+
+
+def _gpu_ready(images: Sequence[Any], factor: int, min_px: int, max_px: int) -> bool:
+    """All images are same-size uint8 HWC arrays that need no resize."""
+    if not images or not all(isinstance(im, np.ndarray) and im.dtype == np.uint8 and im.ndim == 3 for im in images):
+        return False
+    h, w = images[0].shape[:2]
+    if any(im.shape != images[0].shape for im in images):
+        return False
+    return smart_resize(h, w, factor=factor, min_pixels=min_px, max_pixels=max_px) == (h, w)
+
+
+def encode_images(model, images: Sequence[Any], *, min_pixels: int = DEFAULT_MIN_PIXELS,
+                  max_pixels: int = DEFAULT_MAX_PIXELS) -> Tuple[VisionEmbeddings, List[Tuple[int, int, int]]]:
+    v = model.spec.vision
+    factor = v.patch_size * v.spatial_merge_size
+    if model.device.type == "cuda" and _gpu_ready(images, factor, min_pixels, max_pixels):
+        host = torch.from_numpy(np.stack(images)).pin_memory()
+        dev = host.to(model.device, non_blocking=True)
+        emb = model.encode_images_uint8(dev)
+        h, w = images[0].shape[:2]
+        return emb, [(1, h // v.patch_size, w // v.patch_size)] * len(images)
+    rows, grids = [], []
+    for im in images:
+        px, g = preprocess_image(im, patch_size=v.patch_size, spatial_merge_size=v.spatial_merge_size,
+                                 temporal_patch_size=v.temporal_patch_size, min_pixels=min_pixels, max_pixels=max_pixels)
+        rows.append(px)
+        grids.append(tuple(int(x) for x in g[0].tolist()))
+    emb = model.encode_vision(torch.cat(rows).to(model.device, model.dtype), grids)
+    return emb, grids
+
+
+def _merged_count(grid, merge: int) -> int:
+    t, h, w = grid
+    return int(t) * (int(h) // merge) * (int(w) // merge)
+
+
+def prepare_prompts(model, tokenizer, observations: Sequence[Any], *, min_pixels: Optional[int] = None,
+                    max_pixels: Optional[int] = None) -> Tuple[List[PreparedPrompt], VisionEmbeddings]:
+    spec = model.spec
+    merge = spec.vision.spatial_merge_size
+    min_px = int(min_pixels) if min_pixels and min_pixels > 0 else DEFAULT_MIN_PIXELS
+    max_px = int(max_pixels) if max_pixels and max_pixels > 0 else DEFAULT_MAX_PIXELS
+    per_obs = [_images_of(o) for o in observations]
+    flat = [im for ims in per_obs for im in ims]
+    vision, grids = encode_images(model, flat, min_pixels=min_px, max_pixels=max_px)
+    out: List[PreparedPrompt] = []
+    gi = 0
+    for obs, ims in zip(observations, per_obs):
+        g = grids[gi:gi + len(ims)]
+        gi += len(ims)
+        counts = [_merged_count(x, merge) for x in g]
+        if hasattr(obs, "prompt_ids") and getattr(obs, "question", None) is None:
+            ids: List[int] = []
+            for c in counts:
+                ids += [spec.vision_start_token_id] + [spec.image_token_id] * c + [spec.vision_end_token_id]
+            ids += [int(t) for t in np.asarray(obs.prompt_ids).reshape(-1)]
+            text = ""
+        else:
+            if hasattr(obs, "statement") and len(ims) == 2:
+                question = f"Look at the two images. {getattr(obs, 'statement', '')}"
+            else:
+                question = getattr(obs, "question", "") or ""
+            text = chat_prompt_with_image(counts[0], question) if len(counts) == 1 else chat_prompt_with_images(counts, question)
+            ids = list(tokenizer.encode(text, add_special_tokens=False))
+        arr = np.asarray(ids, dtype=np.int64)
+        out.append(PreparedPrompt(prompt_tokens=arr, prompt_length=len(arr), grids=list(g), prompt_text=text))
+    return out, vision
+
+
+def _vision_rows_per_prompt(prompts: Sequence[PreparedPrompt], merge: int) -> List[np.ndarray]:
+    rows, off = [], 0
+    for p in prompts:
+        n = sum(_merged_count(g, merge) for g in p.grids)
+        rows.append(np.arange(off, off + n))
+        off += n
+    return rows
+
+
+def collect_episodes(env: BaseEnv, tokenizer, model, sampling_cfg: SamplingConfig, *, batch_size: int = 0,
+                     groups_per_batch: int = 0, group_size: int = 1, seed: int = 0, task_offset: int = 0,
+                     min_pixels: Optional[int] = None, max_pixels: Optional[int] = None,
+                     max_sequence_length: Optional[int] = None, generator: Optional[Generator] = None,
+                     row_offset: int = 0, **_: Any) -> EpisodeBatch:
+    """Reset ``groups_per_batch`` tasks (or ``batch_size`` tasks with group_size 1) and sample ``group_size`` each."""
+    G = int(groups_per_batch) if groups_per_batch else int(batch_size)
+    gs = max(1, int(group_size))
+    states, observations = [], []
+    for g in range(G):
+        s, o = env.reset(task_offset + g)
+        states.append(s)
+        observations.append(o)
+    prompts, vision = prepare_prompts(model, tokenizer, observations, min_pixels=min_pixels, max_pixels=max_pixels)
+    merge = model.spec.vision.spatial_merge_size
+    gen = generator if generator is not None else Generator(model)
+    res = gen.generate([p.prompt_tokens for p in prompts], [p.grids for p in prompts], vision, sampling_cfg,
+                       seed=seed, row_offset=row_offset, group_size=gs)
+    toks = res.tokens.cpu().numpy()
+    lps = res.logprobs.cpu().numpy()
+    lens = res.lengths.cpu().numpy()
+    # episodes in (group, member) order
+    ep_states, actions, meta = [], [], []
+    for g in range(G):
+        for j in range(gs):
+            b = g * gs + j
+            p = prompts[g]
+            n = int(lens[b])
+            if max_sequence_length is not None:
+                n = max(0, min(n, int(max_sequence_length) - p.prompt_length))
+            ep_states.append(states[g])
+            actions.append(toks[b, :n].tolist())
+            meta.append((g, b, n))
+    _, _, rewards, dones, info = env.step_list(ep_states, actions)
+    texts = [tokenizer.decode(a, skip_special_tokens=True) if tokenizer is not None else "" for a in actions]
+    episodes: List[Episode] = []
+    for i, (g, b, n) in enumerate(meta):
+        p = prompts[g]
+        act = np.asarray(actions[i], dtype=np.int64)
+        alp = lps[b, :n].astype(np.float32)
+        episodes.append(Episode(
+            state=ep_states[i], observation=observations[g], prompt_text=p.prompt_text, prompt_tokens=p.prompt_tokens,
+            prompt_length=p.prompt_length, full_tokens=np.concatenate([p.prompt_tokens, act]),
+            full_logprobs=np.concatenate([np.zeros(p.prompt_length, np.float32), alp]), action_tokens=actions[i],
+            action_logprobs=alp, action_length=n, generated_text=texts[i], grids=p.grids, reward=float(rewards[i]),
+            done=bool(dones[i]), info={k: v[i] for k, v in info.items() if i < len(v)}, group_id=g))
+    # vision rows of every episode (group members share their prompt's rows)
+    rows = _vision_rows_per_prompt(prompts, merge)
+    ep_rows = np.concatenate([rows[g] for g in range(G) for _ in range(gs)]) if G else np.zeros(0, np.int64)
+    idx = torch.from_numpy(ep_rows).to(vision.tokens.device)
+    return EpisodeBatch(episodes=episodes, raw_info=info, vision=vision.select(idx), group_size=gs)
+
+
+def episodes_to_training_batch(model, episodes: Sequence[Episode], *, vision: Optional[VisionEmbeddings] = None,
+                               pad_id: int = 0, max_sequence_length: Optional[int] = None, device=None):
+    """-> (Rollout, PackedBatch).  ``vision`` must hold every episode's image rows in episode order."""
+    if not episodes:
+        raise ValueError("episodes_to_training_batch requires at least one episode.")
+    spec = model.spec
+    device = device or model.device
+    seqs = [np.asarray(ep.full_tokens, dtype=np.int64) for ep in episodes]
+    plens = np.asarray([ep.prompt_length for ep in episodes], dtype=np.int64)
+    alens = np.asarray([ep.action_length for ep in episodes], dtype=np.int64)
+    if max_sequence_length is not None:
+        seqs = [s[:int(max_sequence_length)] for s in seqs]
+    batch, counts = pack_sequences(spec, seqs, plens, [ep.grids for ep in episodes], vision, device=device)
+    # sampler log-probs of exactly the scored rows (action tokens)
+    samp = np.concatenate([np.asarray(ep.action_logprobs[:c], np.float32) for ep, c in zip(episodes, counts)])
+    samp_t = torch.from_numpy(samp).to(device)
+    rollout = Rollout(
+        tokens=seqs, old_logprobs=samp_t.clone(), returns=torch.tensor([ep.reward for ep in episodes], dtype=torch.float32),
+        mask_targets=torch.ones(len(samp), dtype=torch.float32, device=device), prompt_lens=plens, action_lens=alens,
+        texts=[ep.generated_text for ep in episodes], group_ids=np.asarray([ep.group_id for ep in episodes]),
+        sampler_logprobs=samp_t, token_counts=counts)
+    return rollout, batch
+
+
+__all__ = ["PreparedPrompt", "Episode", "EpisodeBatch", "encode_images", "prepare_prompts", "collect_episodes",
+           "episodes_to_training_batch"]

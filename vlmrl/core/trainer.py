@@ -1,0 +1,116 @@
+"""High-level GRPO trainer: one call = one RL iteration (rollout -> rewards -> PPO/GRPO update).
+
+``GRPOTrainer.step()`` is the public entry point used by the CLI (``vlmrl.core.train``)
+and the benchmark.  It owns the train state (AdamW), the CUDA-graph sampler,
+the frozen reference model for the KL penalty, the RNG stream and the dataset
+cursor (the reference's ``RollingEnv``, ``core/train.py:112-141``).  With a
+process group it runs data-parallel rollouts (each rank takes its share of the
+groups; rows keep global Philox ids) and an FSDP update (``vlmrl.parallel.fsdp``).
+
+Per-phase device times (rollout, scoring+update) are measured with CUDA events
+and reported with the metrics; the only host synchronisation of a step is the
+token read-back that the environments need to compute rewards and the final
+metric read.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import asdict
+from typing import Any, Dict, Optional
+
+import numpy as np
+import torch
+
+from vlmrl.core.kl import AdaptiveKL
+from vlmrl.core.optim import AdamWConfig
+from vlmrl.core.ppo import TrainerConfig, collect, update
+from vlmrl.core.sampling import Generator
+from vlmrl.utils.rng import RngSeq, fold_in
+from vlmrl.utils.train_state import TrainState
+
+
+class _Timer:
+    def __init__(self, device):
+        self.cuda = device.type == "cuda"
+        self.marks = []
+
+    def mark(self, name):
+        if self.cuda:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.marks.append((name, e))
+        else:
+            self.marks.append((name, time.perf_counter()))
+
+    def spans(self) -> Dict[str, float]:
+        out = {}
+        if self.cuda and self.marks:
+            self.marks[-1][1].synchronize()
+        for (a, ta), (b, tb) in zip(self.marks, self.marks[1:]):
+            ms = ta.elapsed_time(tb) if self.cuda else (tb - ta) * 1e3
+            out[f"time/{b}_ms"] = ms
+        return out
+
+
+class GRPOTrainer:
+    def __init__(self, model, tokenizer, env, cfg: TrainerConfig, adamw: AdamWConfig, *, ref_model=None,
+                 seed: int = 0, master=None, eos_id: Optional[int] = None, rank: int = 0, world_size: int = 1,
+                 train_state=None):
+        self.model = model
+        self.tokenizer = tokenizer
+        self.env = env
+        self.cfg = cfg
+        self.ts = train_state if train_state is not None else TrainState.create_with_params(model, adamw, master)
+        self.ref_model = ref_model
+        self.generator = Generator(model)
+        self.kl_ctrl = (AdaptiveKL(cfg.kl_target, cfg.kl_adapt_rate, cfg.kl_coef_min, cfg.kl_coef_max)
+                        if cfg.adaptive_kl else None)
+        self.kl_coef = float(cfg.kl_coef)
+        self.rng = RngSeq(seed)
+        self.seed = int(seed)
+        self.eos_id = eos_id if eos_id is not None else model.spec.eos_token_id
+        self.rank, self.world = int(rank), int(world_size)
+        self.cursor = 0
+        self.iteration = 0
+        self.last_collect = None
+
+    @property
+    def groups_per_rank(self) -> int:
+        g = int(self.cfg.groups_per_batch)
+        if g % self.world:
+            raise ValueError(f"groups_per_batch={g} must be divisible by the world size {self.world}")
+        return g // self.world
+
+    def step(self) -> Dict[str, Any]:
+        cfg = self.cfg
+        timer = _Timer(self.model.device)
+        timer.mark("start")
+        seed = self.rng.next()
+        G = self.groups_per_rank
+        cr = collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G, rng=seed, eos_id=self.eos_id,
+                     generator=self.generator, task_offset=self.cursor + self.rank * G,
+                     row_offset=self.rank * G * cfg.group_size)
+        timer.mark("rollout")
+        self.cursor += G * self.world
+        num_tasks = getattr(self.env, "num_tasks", -1)
+        if num_tasks and num_tasks > 0:
+            self.cursor %= num_tasks
+        self.ts, m = update(self.ts, cr, cfg, ref_model=self.ref_model, kl_ctrl=self.kl_ctrl, kl_coef=self.kl_coef)
+        timer.mark("update")
+        self.kl_coef = m.get("kl_coef", self.kl_coef)
+        self.iteration += 1
+        self.last_collect = cr
+        eps = cr.episodes.episodes
+        m.update(timer.spans())
+        m["reward/mean"] = float(cr.rewards.mean())
+        m["reward/std"] = float(cr.rewards.std(unbiased=False)) if cr.rewards.numel() > 1 else 0.0
+        m["tokens/generated"] = float(sum(e.action_length for e in eps))
+        m["tokens/total"] = float(sum(len(e.full_tokens) for e in eps))
+        m["step"] = self.ts.step
+        if eps:
+            m["sample/text"] = eps[0].generated_text[:200]
+        return m
+
+
+__all__ = ["GRPOTrainer"]

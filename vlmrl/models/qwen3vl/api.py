@@ -34,7 +34,7 @@ class Qwen3VLModel:
             if units is None:
                 units = init_params(spec, seed=seed, dtype=dtype, device=self.device)
             else:
-                units = {k: v.to(self.device, dtype).contiguous() for k, v in units.items()}
+                units = {k: v.detach().to(self.device, dtype, copy=True).contiguous() for k, v in units.items()}
             params = LocalParams(units, trainable=[l.name for l in text_layouts(spec)])
         self.params = params
         self._vin_cache: Dict[Tuple, object] = {}

@@ -24,6 +24,21 @@ EPI_GELU_TANH = 2
 EPI_GELU_ERF = 3
 
 
+def launch_count() -> int:
+    """Kernel launches issued by the native library so far (0 when it is not loaded)."""
+    return int(ext().launch_count()) if has_ext() else 0
+
+
+def check_errors(device: Optional[int] = None) -> None:
+    """Raise if a bounded wait inside a kernel timed out (reads and clears the device error word)."""
+    if not has_ext() or not torch.cuda.is_available():
+        return
+    dev = torch.cuda.current_device() if device is None else int(device)
+    code = int(ext().read_and_clear_error(dev))
+    if code:
+        raise RuntimeError(f"vlmrl kernel reported error code {code} (bounded wait timed out) on cuda:{dev}")
+
+
 def _cuda(x: torch.Tensor) -> bool:
     return x.is_cuda
 
@@ -299,20 +314,27 @@ def lm_logits(h, w, out=None):
 
 
 # ------------------------------------------------------------------ sampling
-def sample(logits, *, temperature: float, top_k: int, top_p: float, seed: int, step, row_offset: int = 0,
+def sample(logits, *, temperature: float, top_k: int, top_p: float, seed, step, row_offset: int = 0,
            out_tokens=None, out_logprobs=None):
-    """``step`` may be an int or a 1-element int64 CUDA tensor (graph-capturable counter)."""
+    """Fused top-k / top-p / temperature sampler.
+
+    ``seed`` and ``step`` may be ints or 1-element int64 CUDA tensors (device
+    counters keep a captured CUDA graph valid across replays).
+    """
     if not _cuda(logits):
         s = int(step.item()) if torch.is_tensor(step) else int(step)
-        return ref.sample(logits, temperature=temperature, top_k=top_k, top_p=top_p, seed=seed, step=s,
+        sd = int(seed.item()) if torch.is_tensor(seed) else int(seed)
+        return ref.sample(logits, temperature=temperature, top_k=top_k, top_p=top_p, seed=sd, step=s,
                           row_offset=row_offset)
     B = logits.shape[0]
     tok = out_tokens if out_tokens is not None else torch.empty(B, dtype=torch.int64, device=logits.device)
     lp = out_logprobs if out_logprobs is not None else torch.empty(B, dtype=torch.float32, device=logits.device)
     if not torch.is_tensor(step):
         step = torch.tensor([int(step)], dtype=torch.int64, device=logits.device)
-    ext().sample(logits, tok, lp, step, float(temperature), int(top_k or 0), float(top_p or 0.0),
-                 int(seed) & ((1 << 63) - 1), int(row_offset))
+    if not torch.is_tensor(seed):
+        seed = torch.tensor([int(seed) & ((1 << 63) - 1)], dtype=torch.int64, device=logits.device)
+    ext().sample(logits, tok, lp, step, seed, float(temperature), int(top_k or 0), float(top_p or 0.0),
+                 int(row_offset))
     return tok, lp
 
 
