@@ -11,8 +11,9 @@
 // GQA group and every q block; (3) one CTA per (sequence, 64-query block, q-head)
 // recomputes P and dP to form dQ.
 //
-// Decode: one CTA per (sequence, kv-head) scores all cached keys for the
-// group's q-heads, softmaxes in shared memory and reduces P.V across warps.
+// Decode: flash-decoding over the KV cache, one CTA per (kv-head, sequence,
+// key split), coalesced row reads, per-warp online softmax, warp merge in
+// shared memory (plus a combine kernel when keys are split across CTAs).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -544,92 +545,212 @@ __global__ void __launch_bounds__(128) flash_bwd_dq_kernel(const bf16* __restric
   }
 }
 
-// ------------------------------------------------------------------ decode attention
-// q [B, Hq, D], caches [B, Hkv, Tmax, D], len [B] -> o [B, Hq, D].  CTA = (b, kv-head), 8 warps.
-template <int D, int REP>
-__global__ void __launch_bounds__(256) decode_attn_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
-                                                          const bf16* __restrict__ vc, const int* __restrict__ lens,
-                                                          bf16* __restrict__ o, int Hq, int Hkv, int Tmax, float scale) {
-  const int hk = blockIdx.x, b = blockIdx.y;
+// ------------------------------------------------------------------ decode attention (flash-decoding)
+// q [B, Hq, D], caches [B, Hkv, Tmax, D], len [B] -> o [B, Hq, D].
+// CTA = (kv-head, sequence, key split), NW warps.  The keys of a (sequence, kv-head) are contiguous rows of
+// the cache, so thread 0 streams them with 1-D TMA bulk copies (KC keys of K and of V per stage) into a
+// STAGES-deep shared-memory ring whose mbarriers the warps wait on (bounded).  Warp w scores keys
+// w, w+NW, ... of each stage for the REP q-heads of the group (lane l owns D/32 dims, warp-shuffle
+// reduction) and keeps its own online softmax; warps merge in shared memory at the end.  With more than
+// one split the CTA writes (max, sum, unnormalised acc) and decode_combine_kernel finishes.
+template <int D, int REP, int NW = 8, int KC = 32, int STAGES = 4>
+__global__ void __launch_bounds__(NW * 32) decode_attn_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
+                                                              const bf16* __restrict__ vc, const int* __restrict__ lens,
+                                                              bf16* __restrict__ o, float* __restrict__ part, int Hq,
+                                                              int Hkv, int Tmax, float scale_log2, int splits,
+                                                              int* err) {
+  constexpr int ND = D / 32;
+  constexpr int KPW = KC / NW;  // keys per warp per stage
+  constexpr int CHUNK = KC * D * 2;
+  extern __shared__ __align__(128) uint8_t dsm_raw[];
+  bf16* sK = reinterpret_cast<bf16*>(dsm_raw);
+  bf16* sV = sK + STAGES * KC * D;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sV + STAGES * KC * D);
+  float* sm_m = reinterpret_cast<float*>(full + STAGES);    // [NW][REP]
+  float* sm_l = sm_m + NW * REP;                             // [NW][REP]
+  float* sm_acc = sm_l + NW * REP;                           // [NW][REP][D]
+  __shared__ int abort_flag;
+
+  const int hk = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
   const int L = min(lens[b], Tmax);
-  extern __shared__ float dsm[];
-  float* sq = dsm;                 // [REP][D]
-  float* sp = sq + REP * D;        // [REP][Tmax]
-  float* so = sp + REP * Tmax;     // [8 warps][REP][D]
-  float* red = so + 8 * REP * D;   // [REP][2]
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < REP * D; i += 256) {
-    const int r = i / D, d = i % D;
-    sq[i] = bf2f(q[(static_cast<int64_t>(b) * Hq + hk * REP + r) * D + d]) * scale;
+  const int per = (L + splits - 1) / splits;
+  const int k0 = sp * per, k1 = min(L, k0 + per);
+  const int nk = max(0, k1 - k0);
+  const int nchunks = (nk + KC - 1) / KC;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bf16* kbase = kc + ((static_cast<int64_t>(b) * Hkv + hk) * Tmax + k0) * D;
+  const bf16* vbase = vc + ((static_cast<int64_t>(b) * Hkv + hk) * Tmax + k0) * D;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
   }
   __syncthreads();
-  const bf16* kb = kc + (static_cast<int64_t>(b) * Hkv + hk) * Tmax * D;
-  const bf16* vb = vc + (static_cast<int64_t>(b) * Hkv + hk) * Tmax * D;
-  // scores: one key per thread, full-D dot products against all REP heads
-  for (int t = tid; t < L; t += 256) {
-    float acc[REP];
+  auto issue = [&](int c) {
+    const int st = c % STAGES;
+    const int keys = min(KC, nk - c * KC);
+    const uint32_t bytes = static_cast<uint32_t>(keys) * D * 2;
+    mbar_arrive_expect_tx(&full[st], 2 * bytes);
+    bulk_load(sK + st * KC * D, kbase + static_cast<int64_t>(c) * KC * D, bytes, &full[st]);
+    bulk_load(sV + st * KC * D, vbase + static_cast<int64_t>(c) * KC * D, bytes, &full[st]);
+  };
+  if (threadIdx.x == 0)
+    for (int c = 0; c < STAGES && c < nchunks; ++c) issue(c);
+
+  float qv[REP][ND];
 #pragma unroll
-    for (int r = 0; r < REP; ++r) acc[r] = 0.f;
-    const uint4* kr = reinterpret_cast<const uint4*>(kb + static_cast<int64_t>(t) * D);
-#pragma unroll 4
-    for (int c = 0; c < D / 8; ++c) {
-      const uint4 kv = kr[c];
-      const uint32_t u[4] = {kv.x, kv.y, kv.z, kv.w};
+  for (int r = 0; r < REP; ++r) {
+    const bf16* qr = q + (static_cast<int64_t>(b) * Hq + hk * REP + r) * D + lane * ND;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = unpack_bf16x2(u[j]);
+    for (int j = 0; j < ND; ++j) qv[r][j] = bf2f(qr[j]) * scale_log2;
+  }
+  float m[REP], l[REP], acc[REP][ND];
 #pragma unroll
-        for (int r = 0; r < REP; ++r) acc[r] += f.x * sq[r * D + c * 8 + 2 * j] + f.y * sq[r * D + c * 8 + 2 * j + 1];
+  for (int r = 0; r < REP; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.f;
+#pragma unroll
+    for (int j = 0; j < ND; ++j) acc[r][j] = 0.f;
+  }
+  auto load_nd = [&](const bf16* src, float (&out)[ND]) {
+    if constexpr (ND == 4) {
+      const uint2 u = *reinterpret_cast<const uint2*>(src);
+      const float2 a = unpack_bf16x2(u.x), c = unpack_bf16x2(u.y);
+      out[0] = a.x; out[1] = a.y; out[2] = c.x; out[3] = c.y;
+    } else if constexpr (ND == 2) {
+      const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(src));
+      out[0] = a.x; out[1] = a.y;
+    } else {
+#pragma unroll
+      for (int j = 0; j < ND; ++j) out[j] = bf2f(src[j]);
+    }
+  };
+  int consumed = 0;
+  for (int c = 0; c < nchunks; ++c) {
+    const int st = c % STAGES;
+    if (!mbar_wait(&full[st], static_cast<uint32_t>((c / STAGES) & 1), &abort_flag, err, kErrTimeoutFlag)) break;
+    consumed = c + 1;
+    const int keys = min(KC, nk - c * KC);
+    const bf16* ks = sK + st * KC * D + lane * ND;
+    const bf16* vs = sV + st * KC * D + lane * ND;
+    float kv[KPW][ND], vv[KPW][ND];
+    bool ok[KPW];
+#pragma unroll
+    for (int u = 0; u < KPW; ++u) {
+      const int t = warp + u * NW;
+      ok[u] = t < keys;
+      if (ok[u]) {
+        load_nd(ks + t * D, kv[u]);
+        load_nd(vs + t * D, vv[u]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < ND; ++j) kv[u][j] = vv[u][j] = 0.f;
       }
     }
+    float sc[KPW][REP];
 #pragma unroll
-    for (int r = 0; r < REP; ++r) sp[r * Tmax + t] = acc[r];
-  }
-  __syncthreads();
-  // softmax per head: warp r handles head r (REP <= 8)
-  if (warp < REP) {
-    float mx = -INFINITY;
-    for (int t = lane; t < L; t += 32) mx = fmaxf(mx, sp[warp * Tmax + t]);
-    mx = warp_max(mx);
-    float sum = 0.f;
-    for (int t = lane; t < L; t += 32) {
-      const float e = __expf(sp[warp * Tmax + t] - mx);
-      sp[warp * Tmax + t] = e;
-      sum += e;
-    }
-    sum = warp_sum(sum);
-    if (lane == 0) red[warp] = sum > 0.f ? 1.f / sum : 0.f;
-  }
-  __syncthreads();
-  // P.V: warps split keys, lanes split D
-  float acc[REP][D / 32];
+    for (int u = 0; u < KPW; ++u)
 #pragma unroll
-  for (int r = 0; r < REP; ++r)
+      for (int r = 0; r < REP; ++r) {
+        float x = 0.f;
 #pragma unroll
-    for (int j = 0; j < D / 32; ++j) acc[r][j] = 0.f;
-  for (int t = warp; t < L; t += 8) {
-    const bf16* vr = vb + static_cast<int64_t>(t) * D;
-    float vv[D / 32];
+        for (int j = 0; j < ND; ++j) x += qv[r][j] * kv[u][j];
+        sc[u][r] = x;
+      }
 #pragma unroll
-    for (int j = 0; j < D / 32; ++j) vv[j] = bf2f(vr[lane + 32 * j]);
+    for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+      for (int u = 0; u < KPW; ++u)
+#pragma unroll
+        for (int r = 0; r < REP; ++r) sc[u][r] += __shfl_xor_sync(0xffffffffu, sc[u][r], off);
 #pragma unroll
     for (int r = 0; r < REP; ++r) {
-      const float p = sp[r * Tmax + t];
+      float mx = m[r];
 #pragma unroll
-      for (int j = 0; j < D / 32; ++j) acc[r][j] += p * vv[j];
+      for (int u = 0; u < KPW; ++u)
+        if (ok[u]) mx = fmaxf(mx, sc[u][r]);
+      const float cf = mx == -INFINITY ? 1.f : exp2f(m[r] - mx);
+      l[r] *= cf;
+#pragma unroll
+      for (int j = 0; j < ND; ++j) acc[r][j] *= cf;
+#pragma unroll
+      for (int u = 0; u < KPW; ++u) {
+        const float pr = ok[u] ? exp2f(sc[u][r] - mx) : 0.f;
+        l[r] += pr;
+#pragma unroll
+        for (int j = 0; j < ND; ++j) acc[r][j] += pr * vv[u][j];
+      }
+      m[r] = mx;
+    }
+    __syncthreads();  // stage st fully consumed
+    if (threadIdx.x == 0 && c + STAGES < nchunks) issue(c + STAGES);
+  }
+  if (abort_flag) {
+    // drain this CTA's in-flight bulk copies before it exits
+    if (threadIdx.x == 0) {
+      const int issued = min(nchunks, consumed + STAGES);
+      for (int c = consumed; c < issued; ++c) {
+        volatile int no_abort = 0;
+        mbar_wait(&full[c % STAGES], static_cast<uint32_t>((c / STAGES) & 1), &no_abort, nullptr, 0);
+      }
+    }
+    return;
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int r = 0; r < REP; ++r) {
+      sm_m[warp * REP + r] = m[r];
+      sm_l[warp * REP + r] = l[r];
     }
   }
 #pragma unroll
   for (int r = 0; r < REP; ++r)
 #pragma unroll
-    for (int j = 0; j < D / 32; ++j) so[(warp * REP + r) * D + lane + 32 * j] = acc[r][j];
+    for (int j = 0; j < ND; ++j) sm_acc[(warp * REP + r) * D + lane * ND + j] = acc[r][j];
   __syncthreads();
-  for (int i = tid; i < REP * D; i += 256) {
+  for (int i = threadIdx.x; i < REP * D; i += NW * 32) {
     const int r = i / D, d = i % D;
-    float s = 0.f;
+    float mx = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += so[(w * REP + r) * D + d];
-    o[(static_cast<int64_t>(b) * Hq + hk * REP + r) * D + d] = f2bf(s * red[r]);
+    for (int w = 0; w < NW; ++w) mx = fmaxf(mx, sm_m[w * REP + r]);
+    float lt = 0.f, at = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      const float cf = sm_m[w * REP + r] == -INFINITY ? 0.f : exp2f(sm_m[w * REP + r] - mx);
+      lt += sm_l[w * REP + r] * cf;
+      at += sm_acc[(w * REP + r) * D + d] * cf;
+    }
+    const int h = hk * REP + r;
+    if (splits == 1) {
+      o[(static_cast<int64_t>(b) * Hq + h) * D + d] = f2bf(lt > 0.f ? at / lt : 0.f);
+    } else {
+      float* pp = part + ((static_cast<int64_t>(b) * Hq + h) * splits + sp) * (D + 2);
+      pp[2 + d] = at;
+      if (d == 0) {
+        pp[0] = mx;
+        pp[1] = lt;
+      }
+    }
+  }
+}
+
+// Merges the key splits of decode_attn_kernel: part [B, Hq, splits, 2 + D] -> o [B, Hq, D].
+__global__ void decode_combine_kernel(const float* __restrict__ part, bf16* __restrict__ o, int BH, int splits, int D) {
+  const int bh = blockIdx.x;
+  if (bh >= BH) return;
+  const float* p = part + static_cast<int64_t>(bh) * splits * (D + 2);
+  float mx = -INFINITY;
+  for (int s = 0; s < splits; ++s) mx = fmaxf(mx, p[s * (D + 2)]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float lt = 0.f, at = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float ms = p[s * (D + 2)];
+      const float c = ms == -INFINITY ? 0.f : exp2f(ms - mx);
+      lt += p[s * (D + 2) + 1] * c;
+      at += p[s * (D + 2) + 2 + d] * c;
+    }
+    o[static_cast<int64_t>(bh) * D + d] = f2bf(lt > 0.f ? at / lt : 0.f);
   }
 }
 
@@ -741,17 +862,33 @@ void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, a
 template <int D, int REP>
 static void decode_dispatch(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& lens,
                             at::Tensor& o, float scale) {
+  constexpr int NW = 8, KC = 32, STAGES = 4;
   const int B = static_cast<int>(q.size(0)), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(kc.size(1));
   const int Tmax = static_cast<int>(kc.size(2));
-  const int smem = (REP * D + REP * Tmax + 8 * REP * D + 2 * REP) * 4;
-  TORCH_CHECK(smem <= 227 * 1024, "decode_attn: cache too long for the single-pass kernel (Tmax=", Tmax, ")");
-  auto kern = decode_attn_kernel<D, REP>;
-  set_smem(kern, smem);
-  kern<<<dim3(Hkv, B), 256, smem, at::cuda::getCurrentCUDAStream()>>>(
+  const int sms = num_sms(q.device().index());
+  // ~3 CTAs per SM; each split keeps >= 2 chunks of keys
+  const int splits = std::max(1, std::min((3 * sms + B * Hkv - 1) / (B * Hkv), Tmax / (2 * KC)));
+  const int smem = 2 * STAGES * KC * D * 2 + STAGES * 8 + (2 * NW * REP + NW * REP * D) * 4;
+  auto kern = decode_attn_kernel<D, REP, NW, KC, STAGES>;
+  static bool configured = false;
+  if (!configured) {
+    VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    configured = true;
+  }
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  at::Tensor part;
+  if (splits > 1) part = at::empty({B, Hq, splits, D + 2}, q.options().dtype(at::kFloat));
+  kern<<<dim3(Hkv, B, splits), NW * 32, smem, st>>>(
       reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(kc.data_ptr()),
-      reinterpret_cast<const bf16*>(vc.data_ptr()), lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()), Hq, Hkv,
-      Tmax, scale);
+      reinterpret_cast<const bf16*>(vc.data_ptr()), lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()),
+      splits > 1 ? part.data_ptr<float>() : nullptr, Hq, Hkv, Tmax, scale * kLog2e, splits,
+      err_word(q.device().index()));
   VLM_LAUNCHED();
+  if (splits > 1) {
+    decode_combine_kernel<<<B * Hq, 128, 0, st>>>(part.data_ptr<float>(), reinterpret_cast<bf16*>(o.data_ptr()), B * Hq,
+                                                  splits, D);
+    VLM_LAUNCHED();
+  }
 }
 
 void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale) {

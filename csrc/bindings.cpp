@@ -6,6 +6,10 @@
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vlmrl hand-written sm_100a kernels";
   m.def("gemm", &vlm::gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("gemm_partials", &vlm::gemm_partials, "stream-K partial sums for the fused decode consumers");
+  m.def("dec_qkv", &vlm::dec_qkv);
+  m.def("dec_residual_norm", &vlm::dec_residual_norm);
+  m.def("dec_swiglu", &vlm::dec_swiglu);
   m.def("rms_norm_fwd", &vlm::rms_norm_fwd);
   m.def("rms_norm_bwd", &vlm::rms_norm_bwd);
   m.def("layer_norm_fwd", &vlm::layer_norm_fwd);

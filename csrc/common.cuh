@@ -86,6 +86,14 @@ VLM_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, 
       : "memory");
 }
 
+// 1-D bulk copy global -> this CTA's shared memory (16-byte aligned, size % 16 == 0), mbarrier completion.
+VLM_DEV void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // ------------------------------------------------------------------ tcgen05 / TMEM
 VLM_DEV void tmem_alloc(uint32_t* smem_holder, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_holder)),

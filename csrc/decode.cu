@@ -1,0 +1,198 @@
+// Decode-step kernels that consume the stream-K partial sums of the skinny (M = batch) GEMMs and
+// fuse the memory-bound work that follows each of them:
+//   dec_qkv            sum partials + bias -> per-head RMSNorm of q/k -> MRoPE -> q out, k/v into the KV cache
+//   dec_residual_norm  sum partials + residual -> h (bf16) -> RMSNorm(h) -> hn (bf16)
+//   dec_swiglu         sum partials -> silu(gate) * up
+// so a decoder layer is 4 GEMMs + 3 of these + attention, with no separate reduction launches.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+#include "streamk.cuh"
+#include "vlm_ops.h"
+
+namespace vlm {
+
+using bf16 = __nv_bfloat16;
+
+static SkMeta meta_of(const std::vector<int64_t>& v) {
+  TORCH_CHECK(v.size() == 8, "stream-K meta must have 8 entries");
+  return SkMeta{static_cast<int>(v[0]), static_cast<int>(v[1]), static_cast<int>(v[2]), static_cast<int>(v[3]),
+                static_cast<int>(v[4]), static_cast<int>(v[5]), static_cast<int>(v[6]), static_cast<int>(v[7])};
+}
+
+VLM_DEV void store8(bf16* dst, const float (&v)[8]) {
+  *reinterpret_cast<uint4*>(dst) =
+      make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+}
+
+// One CTA per token row; thread i owns qkv columns [8i, 8i+8).  TPH = D/8 threads per head.
+template <int D>
+__global__ void dec_qkv_kernel(const float* __restrict__ ws, SkMeta m, const bf16* __restrict__ bias,
+                               const bf16* __restrict__ qw, const bf16* __restrict__ kw, const int* __restrict__ lengths,
+                               const int64_t* __restrict__ delta, const float* __restrict__ inv_freq,
+                               bf16* __restrict__ q, bf16* __restrict__ kc, bf16* __restrict__ vc, int nq, int nkv,
+                               int Tmax, float eps) {
+  constexpr int TPH = D / 8;
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int head = tid / TPH, t = tid % TPH;
+  const int col = tid * 8;
+  float x[8];
+  sk_sum8(ws, m, row, col, x);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = bf2f(f2bf(x[i] + (bias ? bf2f(bias[col + i]) : 0.f)));
+  const int len = lengths[row];
+  const bool is_v = head >= nq + nkv;
+  const bool is_q = head < nq;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+#pragma unroll
+  for (int off = TPH / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float r = rsqrtf(ss / D + eps);
+  const bf16* wt = is_q ? qw : kw;
+  float xn[8], y[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) xn[i] = is_v ? x[i] : x[i] * r * bf2f(wt[t * 8 + i]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) y[i] = __shfl_xor_sync(0xffffffffu, xn[i], TPH / 2);
+  if (is_v) {
+    store8(vc + ((static_cast<int64_t>(row) * nkv + (head - nq - nkv)) * Tmax + len) * D + t * 8, x);
+    return;
+  }
+  const float pos = static_cast<float>(static_cast<int64_t>(len) + delta[row]);
+  const bool first_half = t < TPH / 2;
+  float out[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float s, c;
+    sincosf(pos * inv_freq[(t % (TPH / 2)) * 8 + i], &s, &c);
+    out[i] = first_half ? xn[i] * c - y[i] * s : xn[i] * c + y[i] * s;
+  }
+  if (is_q)
+    store8(q + (static_cast<int64_t>(row) * nq + head) * D + t * 8, out);
+  else
+    store8(kc + ((static_cast<int64_t>(row) * nkv + (head - nq)) * Tmax + len) * D + t * 8, out);
+}
+
+// One CTA per row; thread i owns columns [8i, 8i+8).
+__global__ void dec_resnorm_kernel(const float* __restrict__ ws, SkMeta m, const bf16* __restrict__ res,
+                                   const bf16* __restrict__ w, bf16* __restrict__ h_out, bf16* __restrict__ hn_out,
+                                   int H, float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x, col = threadIdx.x * 8;
+  float x[8];
+  float ss = 0.f;
+  if (col < H) {
+    sk_sum8(ws, m, row, col, x);
+    const uint4 rv = *reinterpret_cast<const uint4*>(res + static_cast<int64_t>(row) * H + col);
+    const uint32_t u[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(u[j]);
+      x[2 * j] = bf2f(f2bf(x[2 * j] + f.x));
+      x[2 * j + 1] = bf2f(f2bf(x[2 * j + 1] + f.y));
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    store8(h_out + static_cast<int64_t>(row) * H + col, x);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x + 31) / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  if (col < H) {
+    const float r = rsqrtf(red[0] / H + eps);
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = bf2f(f2bf(x[i] * r)) * bf2f(w[col + i]);
+    store8(hn_out + static_cast<int64_t>(row) * H + col, o);
+  }
+}
+
+__global__ void dec_swiglu_kernel(const float* __restrict__ ws, SkMeta m, bf16* __restrict__ act, int N) {
+  const int row = blockIdx.y;
+  const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (col >= N) return;
+  float x[8];
+  sk_sum8(ws, m, row, col, x);
+  float o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float g = bf2f(f2bf(x[2 * j])), u = bf2f(f2bf(x[2 * j + 1]));
+    o[j] = g / (1.f + __expf(-g)) * u;
+  }
+  *reinterpret_cast<uint2*>(act + static_cast<int64_t>(row) * (N / 2) + col / 2) =
+      make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+}
+
+at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at::Tensor qw, at::Tensor kw,
+                   at::Tensor lengths, at::Tensor delta, at::Tensor inv_freq, at::Tensor kc, at::Tensor vc, int64_t nq,
+                   int64_t nkv, double eps) {
+  const SkMeta m = meta_of(meta);
+  const int D = static_cast<int>(kc.size(-1));
+  const int Tmax = static_cast<int>(kc.size(-2));
+  TORCH_CHECK(m.N == (nq + 2 * nkv) * D, "dec_qkv: width mismatch");
+  TORCH_CHECK(lengths.scalar_type() == at::kInt && delta.scalar_type() == at::kLong, "dec_qkv: int32 lengths, int64 deltas");
+  TORCH_CHECK(kc.is_contiguous() && vc.is_contiguous(), "dec_qkv: contiguous cache layer");
+  const c10::cuda::CUDAGuard g(ws.device());
+  at::Tensor q = at::empty({m.M, nq, D}, kc.options());
+  const int threads = static_cast<int>((nq + 2 * nkv) * D / 8);
+  TORCH_CHECK(threads <= 1024, "dec_qkv: too many heads for one CTA");
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  auto args = [&](auto kern) {
+    kern<<<m.M, threads, 0, st>>>(ws.data_ptr<float>(), m,
+                                  bias.defined() && bias.numel() ? reinterpret_cast<const bf16*>(bias.data_ptr()) : nullptr,
+                                  reinterpret_cast<const bf16*>(qw.data_ptr()), reinterpret_cast<const bf16*>(kw.data_ptr()),
+                                  lengths.data_ptr<int>(), delta.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),
+                                  reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(kc.data_ptr()),
+                                  reinterpret_cast<bf16*>(vc.data_ptr()), static_cast<int>(nq), static_cast<int>(nkv), Tmax,
+                                  static_cast<float>(eps));
+  };
+  if (D == 128)
+    args(dec_qkv_kernel<128>);
+  else if (D == 64)
+    args(dec_qkv_kernel<64>);
+  else if (D == 32)
+    args(dec_qkv_kernel<32>);
+  else
+    TORCH_CHECK(false, "dec_qkv: unsupported head_dim ", D);
+  VLM_LAUNCHED();
+  return q;
+}
+
+std::tuple<at::Tensor, at::Tensor> dec_residual_norm(at::Tensor ws, std::vector<int64_t> meta, at::Tensor residual,
+                                                     at::Tensor w, double eps) {
+  const SkMeta m = meta_of(meta);
+  TORCH_CHECK(residual.is_contiguous() && residual.size(0) == m.M && residual.size(1) == m.N, "dec_residual_norm: shape");
+  TORCH_CHECK(m.N % 8 == 0 && m.N / 8 <= 1024, "dec_residual_norm: width");
+  const c10::cuda::CUDAGuard g(ws.device());
+  at::Tensor h = at::empty_like(residual), hn = at::empty_like(residual);
+  const int threads = ((m.N / 8 + 31) / 32) * 32;
+  dec_resnorm_kernel<<<m.M, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      ws.data_ptr<float>(), m, reinterpret_cast<const bf16*>(residual.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
+      reinterpret_cast<bf16*>(h.data_ptr()), reinterpret_cast<bf16*>(hn.data_ptr()), m.N, static_cast<float>(eps));
+  VLM_LAUNCHED();
+  return {h, hn};
+}
+
+at::Tensor dec_swiglu(at::Tensor ws, std::vector<int64_t> meta) {
+  const SkMeta m = meta_of(meta);
+  TORCH_CHECK(m.N % 16 == 0, "dec_swiglu: width must be a multiple of 16");
+  const c10::cuda::CUDAGuard g(ws.device());
+  at::Tensor act = at::empty({m.M, m.N / 2}, ws.options().dtype(at::kBFloat16));
+  const dim3 grid((m.N / 8 + 255) / 256, m.M);
+  dec_swiglu_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(ws.data_ptr<float>(), m,
+                                                                        reinterpret_cast<bf16*>(act.data_ptr()), m.N);
+  VLM_LAUNCHED();
+  return act;
+}
+
+}  // namespace vlm

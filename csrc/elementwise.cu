@@ -105,6 +105,47 @@ __global__ void rms_norm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __r
   }
 }
 
+// Small-M variant (decode): one CTA per row, one 16-byte chunk per thread held in registers.
+__global__ void rms_norm_row_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, bf16* __restrict__ y,
+                                    float* __restrict__ rstd, int H, float eps) {
+  const int row = blockIdx.x, c = threadIdx.x * 8;
+  __shared__ float red[32];
+  const bf16* xr = x + static_cast<int64_t>(row) * H;
+  uint4 v = make_uint4(0, 0, 0, 0);
+  float ss = 0.f;
+  if (c < H) {
+    v = *reinterpret_cast<const uint4*>(xr + c);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(u[j]);
+      ss += f.x * f.x + f.y * f.y;
+    }
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x + 31) / 32 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float r = rsqrtf(red[0] / H + eps);
+  if (threadIdx.x == 0 && rstd) rstd[row] = r;
+  if (c < H) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w}, uw[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(u[j]), g = unpack_bf16x2(uw[j]);
+      o[j] = pack_bf16x2(bf2f(f2bf(f.x * r)) * g.x, bf2f(f2bf(f.y * r)) * g.y);
+    }
+    *reinterpret_cast<uint4*>(y + static_cast<int64_t>(row) * H + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 void rms_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps) {
   TORCH_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "rms_norm: bf16");
   const int H = static_cast<int>(x.size(-1));
@@ -112,6 +153,15 @@ void rms_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, dou
   TORCH_CHECK(H % 8 == 0, "rms_norm: hidden size must be a multiple of 8");
   if (M == 0) return;
   const c10::cuda::CUDAGuard g(x.device());
+  if (M < 1024 && H <= 8192) {
+    const int threads = ((H / 8 + 31) / 32) * 32;
+    rms_norm_row_kernel<<<M, threads, 0, cur_stream()>>>(
+        reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
+        reinterpret_cast<bf16*>(y.data_ptr()), rstd.defined() && rstd.numel() ? rstd.data_ptr<float>() : nullptr, H,
+        static_cast<float>(eps));
+    VLM_LAUNCHED();
+    return;
+  }
   rms_norm_fwd_kernel<<<blocks_for(M, 8), 256, 0, cur_stream()>>>(
       reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
       reinterpret_cast<bf16*>(y.data_ptr()), rstd.defined() && rstd.numel() ? rstd.data_ptr<float>() : nullptr, M, H,

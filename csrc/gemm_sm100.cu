@@ -22,6 +22,7 @@
 #include "common.cuh"
 #include "host_utils.h"
 #include "vlm_ops.h"
+#include "streamk.cuh"
 
 namespace vlm {
 
@@ -49,6 +50,58 @@ struct GemmParams {
   const float* g_lp;
   const float* g_ent;
   float* part;  // [M, tiles_n, 4] partial (max, sum exp, sum exp*z, target logit)
+  // split-K: tile t -> (mn tile = t / splits, split = t % splits); each split stores raw fp32
+  // partial sums to ws[split] ([M, N] row-major) and splitk_reduce applies the epilogue.
+  int splits;
+  int kb_per_split;
+  float* ws;
+  // stream-K: CTA c owns the contiguous (tile, k-block) units [c*U/G, (c+1)*U/G), U = tiles*kb_count
+  int streamk;
+  int sk_grid;  // grid size of the stream-K launch
+  int bn;
+};
+
+// Work item: one accumulation segment of one output tile.
+struct Work {
+  int tile, kb0, kb1, slot;
+};
+
+struct WorkIter {
+  int kb_count, units_total;
+  long long u, u_end, U;
+  int t, grid;
+  VLM_DEV WorkIter(const GemmParams& p, int kbc) : kb_count(kbc) {
+    grid = gridDim.x;
+    units_total = p.tiles_m * p.tiles_n * p.splits;
+    t = blockIdx.x;
+    U = static_cast<long long>(p.tiles_m) * p.tiles_n * kbc;
+    u = (static_cast<long long>(blockIdx.x) * U) / grid;
+    u_end = (static_cast<long long>(blockIdx.x + 1) * U) / grid;
+  }
+  VLM_DEV long long cta_of(long long x) const { return ((x + 1) * grid - 1) / U; }
+  // number of CTAs whose unit range intersects `tile`
+  VLM_DEV int slots_of(int tile) const {
+    const long long first = static_cast<long long>(tile) * kb_count;
+    return static_cast<int>(cta_of(first + kb_count - 1) - cta_of(first) + 1);
+  }
+  VLM_DEV bool next(const GemmParams& p, Work& w) {
+    if (!p.streamk) {
+      if (t >= units_total) return false;
+      w.tile = t / p.splits;
+      w.slot = t % p.splits;
+      w.kb0 = w.slot * p.kb_per_split;
+      w.kb1 = min(kb_count, w.kb0 + p.kb_per_split);
+      t += grid;
+      return true;
+    }
+    if (u >= u_end) return false;
+    w.tile = static_cast<int>(u / kb_count);
+    w.kb0 = static_cast<int>(u % kb_count);
+    w.kb1 = static_cast<int>(min(static_cast<long long>(kb_count), w.kb0 + (u_end - u)));
+    w.slot = static_cast<int>(blockIdx.x - cta_of(static_cast<long long>(w.tile) * kb_count));
+    u += w.kb1 - w.kb0;
+    return true;
+  }
 };
 
 constexpr int kBM = 128;
@@ -193,7 +246,6 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_tiles = p.tiles_m * p.tiles_n;
   const int kb_count = (p.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -228,11 +280,13 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      WorkIter it(p, kb_count);
+      Work w;
+      while (ok && it.next(p, w)) {
         int tm, tn;
-        tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+        tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
         const int m0 = tm * kBM, n0 = tn * BN;
-        for (int kb = 0; kb < kb_count; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
@@ -275,7 +329,9 @@ __global__ void __launch_bounds__(192, 1)
       int stage = 0;
       uint32_t phase = 0;
       int lt = 0;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++lt) {
+      WorkIter it(p, kb_count);
+      Work w;
+      for (; ok && it.next(p, w); ++lt) {
         const int acc = lt & 1;
         const uint32_t use = static_cast<uint32_t>(lt >> 1);
         if (!mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abort_flag, p.err, kErrTimeoutMma)) {
@@ -284,7 +340,8 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < kb_count; ++kb) {
+        const int kb0 = w.kb0, kb1 = w.kb1;
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrTimeoutMma)) {
             ok = false;
             break;
@@ -296,7 +353,7 @@ __global__ void __launch_bounds__(192, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = A_MN ? sdesc_sw128(a_addr + k * 2048, 8192, 1024) : sdesc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(b_addr + k * 2048, 8192, 1024) : sdesc_sw128(b_addr + k * 32, 16, 1024);
-            umma_f16(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16(d_tmem, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
@@ -317,17 +374,37 @@ __global__ void __launch_bounds__(192, 1)
     const int q = warp & 3;  // TMEM lanes [32q, 32q+32) are the ones this warp may read
     const int row_in_tile = q * 32 + lane;
     int lt = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++lt) {
+    WorkIter it(p, kb_count);
+    Work w;
+    for (; it.next(p, w); ++lt) {
       const int acc = lt & 1;
       const uint32_t use = static_cast<uint32_t>(lt >> 1);
       if (!mbar_wait(&tfull[acc], use & 1u, abort_flag, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       int tm, tn;
-      tile_coords(t, p.tiles_m, p.tiles_n, tm, tn);
+      tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
       const int row = tm * kBM + row_in_tile;
       const int n0 = tn * BN;
       const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-      if (p.epi == EPI_VOCAB_STATS) {
+      if (p.streamk) {
+        float* wsr = p.ws + (static_cast<int64_t>(w.slot) * p.M + row) * p.N;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c, r);
+          tmem_ld_wait();
+          const int col0 = n0 + c;
+          if (row >= p.M || col0 >= p.N) continue;
+          if (col0 + 16 <= p.N) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              reinterpret_cast<float4*>(wsr + col0)[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                                     __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          } else {
+            for (int i = 0; i < p.N - col0; ++i) wsr[col0 + i] = __uint_as_float(r[i]);
+          }
+        }
+      } else if (p.epi == EPI_VOCAB_STATS) {
         // online (max, sum exp, sum exp*z) of this row over the tile's columns; never stores logits
         float mx = -INFINITY, se = 0.f, sz = 0.f, zt = __int_as_float(0x7fc00000);
         const int64_t tgt = row < p.M ? p.targets[row] : -1;
@@ -425,6 +502,29 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// Generic consumer of stream-K partials: sums the slots of 16 columns and applies the GEMM epilogue.
+__global__ void sk_reduce_kernel(GemmParams p, SkMeta m) {
+  const int chunks = (p.N + 15) / 16;
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<int64_t>(p.M) * chunks) return;
+  const int row = static_cast<int>(idx / chunks), col = static_cast<int>(idx % chunks) * 16;
+  float a[8], b[8];
+  sk_sum8(p.ws, m, row, col, a);
+  if (col + 8 < p.N) {
+    sk_sum8(p.ws, m, row, col + 8, b);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b[i] = 0.f;
+  }
+  uint32_t r[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    r[i] = __float_as_uint(a[i]);
+    r[8 + i] = __float_as_uint(b[i]);
+  }
+  epilogue_chunk(p, row, col, r);
+}
+
 // ------------------------------------------------------------------ host side
 template <int BN, bool A_MN, bool B_MN>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid, cudaStream_t st) {
@@ -447,7 +547,7 @@ static void check_operand(const at::Tensor& t, const char* name) {
 
 void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
              bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, const VocabArgs* vocab,
-             int force_bn) {
+             int force_bn, at::Tensor* partials_out, SkMeta* meta_out) {
   check_operand(A, "A");
   check_operand(B, "B");
   const c10::cuda::CUDAGuard guard(A.device());
@@ -458,7 +558,8 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   TORCH_CHECK(K == Kb, "gemm: K mismatch ", K, " vs ", Kb);
   TORCH_CHECK(K > 0 && M > 0 && N > 0, "gemm: empty problem");
   TORCH_CHECK(N % 8 == 0, "gemm: N must be a multiple of 8");
-  const bool is_stats = epi == EPI_VOCAB_STATS;
+  const bool want_partials = partials_out != nullptr;
+  const bool is_stats = epi == EPI_VOCAB_STATS || want_partials;
   TORCH_CHECK(is_stats || (D.is_cuda() && D.dim() == 2 && D.stride(1) == 1), "gemm: bad output");
   TORCH_CHECK((epi != EPI_VOCAB_STATS && epi != EPI_VOCAB_GRAD) || vocab != nullptr, "gemm: vocab epilogue needs row data");
   const bool d_f32 = !is_stats && D.scalar_type() == at::kFloat;
@@ -508,11 +609,39 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   }
 
   const int sms = num_sms(A.device().index());
-  const int64_t tiles256 = ((M + kBM - 1) / kBM) * ((N + 255) / 256);
-  const int BN = force_bn ? force_bn : ((tiles256 >= sms || N > 4096) ? 256 : 128);
-  p.tiles_m = static_cast<int>((M + kBM - 1) / kBM);
+  const int64_t tm_count = (M + kBM - 1) / kBM;
+  // pick the tile width with the better wave efficiency (ties -> 256, the more efficient tile)
+  auto wave_eff = [&](int bn) {
+    const double t = static_cast<double>(tm_count * ((N + bn - 1) / bn));
+    return t / (std::ceil(t / sms) * sms);
+  };
+  int BN = force_bn;
+  if (!BN) BN = (M <= kBM || wave_eff(128) > wave_eff(256) + 0.1) ? 128 : 256;
+  p.tiles_m = static_cast<int>(tm_count);
   p.tiles_n = static_cast<int>((N + BN - 1) / BN);
-  const int grid = static_cast<int>(std::min<int64_t>(static_cast<int64_t>(p.tiles_m) * p.tiles_n, sms));
+  const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+  const int kb_count = static_cast<int>((K + kBK - 1) / kBK);
+  // split-K for skinny problems that would leave most SMs idle
+  int splits = 1;
+  at::Tensor ws;
+  const bool splittable = epi <= EPI_GELU_ERF && !accumulate;
+  p.bn = BN;
+  p.kb_per_split = kb_count;
+  int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+  // Skinny problems (decode, M <= 2 tiles): stream-K over (tile, k-block) units so every SM gets the
+  // same amount of weight streaming; partial sums go to a [slots, M, N] fp32 workspace.
+  const int64_t units = tiles * kb_count;
+  if (want_partials || (splittable && p.tiles_m <= 2 && tiles < 4 * sms && units >= 2 * sms)) {
+    TORCH_CHECK(!want_partials || (a_kmajor && b_kmajor && alpha == 1.0), "gemm partials: K-major operands only");
+    p.streamk = 1;
+    grid = static_cast<int>(std::min<int64_t>(sms, units));
+    const int64_t per_cta = std::max<int64_t>(1, units / grid);
+    const int64_t slots = std::min<int64_t>((kb_count + per_cta - 1) / per_cta + 1, grid);
+    ws = at::empty({slots, M, N}, A.options().dtype(at::kFloat));
+    p.ws = ws.data_ptr<float>();
+    p.sk_grid = grid;
+  }
+  p.splits = splits;
 
   // tensor maps: inner dimension first
   CUtensorMap ta, tb;
@@ -535,12 +664,31 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   } else {
     TORCH_CHECK(false, "gemm: MN-major A with K-major B is not instantiated");
   }
+  if (p.streamk) {
+    SkMeta m{p.M, p.N, p.tiles_m, p.tiles_n, kb_count, grid, kBM, BN};
+    if (want_partials) {
+      *partials_out = ws;
+      *meta_out = m;
+    } else {
+      const int64_t threads = M * ((N + 15) / 16);
+      sk_reduce_kernel<<<static_cast<int>((threads + 127) / 128), 128, 0, st>>>(p, m);
+      VLM_LAUNCHED();
+    }
+  }
 }
 
 void gemm(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux, bool a_kmajor,
           bool b_kmajor, double alpha, int64_t epi, bool accumulate) {
   TORCH_CHECK(epi >= EPI_STORE && epi <= EPI_GELU_ERF, "gemm: epilogue code ", epi, " is internal");
-  gemm_ex(A, B, D, bias, residual, aux, a_kmajor, b_kmajor, alpha, epi, accumulate, nullptr, 0);
+  gemm_ex(A, B, D, bias, residual, aux, a_kmajor, b_kmajor, alpha, epi, accumulate, nullptr, 0, nullptr, nullptr);
+}
+
+std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials(at::Tensor A, at::Tensor B) {
+  at::Tensor ws;
+  SkMeta m{};
+  gemm_ex(A, B, at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(), true, true, 1.0, EPI_STORE, false, nullptr, 0,
+          &ws, &m);
+  return {ws, {m.M, m.N, m.tiles_m, m.tiles_n, m.kb_count, m.grid, m.bm, m.bn}};
 }
 
 }  // namespace vlm

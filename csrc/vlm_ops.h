@@ -3,7 +3,12 @@
 
 #include <torch/extension.h>
 
+#include <tuple>
+#include <vector>
+
 namespace vlm {
+
+struct SkMeta;
 
 struct VocabArgs {
   const int64_t* targets;
@@ -19,7 +24,17 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor 
           bool b_kmajor, double alpha, int64_t epi, bool accumulate);
 void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
              bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, const VocabArgs* vocab,
-             int force_bn);
+             int force_bn, at::Tensor* partials_out, SkMeta* meta_out);
+// Stream-K partial sums of A.B^T without an epilogue: (ws [slots, M, N] fp32, meta) for the fused consumers.
+std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials(at::Tensor A, at::Tensor B);
+
+// decode.cu: consumers of stream-K partials fused with the decode step's memory-bound ops
+at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at::Tensor qw, at::Tensor kw,
+                   at::Tensor lengths, at::Tensor delta, at::Tensor inv_freq, at::Tensor kc, at::Tensor vc, int64_t nq,
+                   int64_t nkv, double eps);
+std::tuple<at::Tensor, at::Tensor> dec_residual_norm(at::Tensor ws, std::vector<int64_t> meta, at::Tensor residual,
+                                                     at::Tensor w, double eps);
+at::Tensor dec_swiglu(at::Tensor ws, std::vector<int64_t> meta);
 
 // elementwise.cu
 void rms_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps);

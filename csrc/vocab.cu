@@ -63,7 +63,7 @@ void vocab_logprob_fwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tenso
   at::Tensor part = at::empty({M, tiles, 4}, h.options().dtype(at::kFloat));
   VocabArgs va{targets.data_ptr<int64_t>(), nullptr, nullptr, nullptr, nullptr, part.data_ptr<float>()};
   gemm_ex(h, w, at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(), true, true, 1.0, kEpiVocabStats, false, &va,
-          kVocabBN);
+          kVocabBN, nullptr, nullptr);
   vocab_combine_kernel<<<static_cast<int>((M * 32 + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const float4*>(part.data_ptr<float>()), tiles, static_cast<int>(M), logp.data_ptr<float>(),
       ent.data_ptr<float>(), lse.data_ptr<float>());
@@ -86,7 +86,8 @@ void vocab_logprob_bwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tenso
     at::Tensor dzc = dz.narrow(0, 0, mc);
     VocabArgs va{targets.data_ptr<int64_t>() + r0, lse.data_ptr<float>() + r0, ent.data_ptr<float>() + r0,
                  g_lp.data_ptr<float>() + r0, g_ent.data_ptr<float>() + r0, nullptr};
-    gemm_ex(hc, w, dzc, at::Tensor(), at::Tensor(), at::Tensor(), true, true, 1.0, kEpiVocabGrad, false, &va, kVocabBN);
+    gemm_ex(hc, w, dzc, at::Tensor(), at::Tensor(), at::Tensor(), true, true, 1.0, kEpiVocabGrad, false, &va, kVocabBN,
+            nullptr, nullptr);
     gemm(dzc, w, dh.narrow(0, r0, mc), at::Tensor(), at::Tensor(), at::Tensor(), true, false, 1.0, 0, false);
     gemm(dzc, hc, dw, at::Tensor(), at::Tensor(), at::Tensor(), false, false, 1.0, 0, true);
   }

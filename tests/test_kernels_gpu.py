@@ -68,6 +68,19 @@ def test_gemm_nn_tn(M, N, K):
     _no_device_error()
 
 
+@pytest.mark.parametrize("M,N,K", [(64, 2560, 4096), (64, 19456, 2560), (7, 160, 1024), (64, 151936, 2560), (200, 6144, 2560)])
+def test_gemm_splitk_skinny(M, N, K):
+    x, w = _r(M, K, seed=40), _r(N, K, scale=0.05, seed=41)
+    res, b = _r(M, N, seed=42), _r(N, seed=43)
+    _close(ops.gemm(x, w, bias=b, residual=res), ref.gemm(x, w, bias=b, residual=res, out_dtype=torch.float32),
+           name="splitk store")
+    act, pre = ops.linear_swiglu(x, w)
+    pre_ref = ref.gemm(x, w, out_dtype=torch.float32)
+    _close(pre, pre_ref, name="splitk swiglu pre")
+    _close(act, ref.swiglu_interleaved(pre_ref.to(torch.bfloat16)), name="splitk swiglu")
+    _no_device_error()
+
+
 def test_gemm_activation_epilogues():
     M, N, K = 300, 512, 256
     x, w = _r(M, K, seed=9), _r(N, K, scale=0.1, seed=10)

@@ -113,9 +113,9 @@ class Qwen3VLModel:
     @torch.no_grad()
     def decode_step(self, token: torch.Tensor, cache: KVCache, rope_deltas: torch.Tensor) -> torch.Tensor:
         """Logits [B, V] fp32 of the next token; appends this token's k/v and advances ``cache.lengths``."""
-        h = self.decoder.decode_hidden(self.params, token, cache, rope_deltas.reshape(-1))
+        h, normed = self.decoder.decode_hidden(self.params, token, cache, rope_deltas.reshape(-1))
         cache.lengths += 1
-        return self.decoder.final_logits(self.params, h)
+        return self.decoder.final_logits(self.params, h, normed=normed)
 
     def parameter_count(self, trainable_only: bool = False) -> int:
         return sum(l.numel for l in all_layouts(self.spec) if (l.trainable or not trainable_only))

@@ -308,9 +308,9 @@ class TextDecoder:
             params.grad_done("embed")
 
     # ---------------------------------------------------------------- inference
-    def final_logits(self, params, h_rows: torch.Tensor) -> torch.Tensor:
+    def final_logits(self, params, h_rows: torch.Tensor, normed: bool = False) -> torch.Tensor:
         head = self._w(params, "head")
-        hn, _ = ops.rms_norm(h_rows, head["final_norm"], self.eps)
+        hn = h_rows if normed else ops.rms_norm(h_rows, head["final_norm"], self.eps)[0]
         logits = ops.lm_logits(hn, head["lm_head"])
         params.release("head")
         return logits
@@ -332,12 +332,19 @@ class TextDecoder:
         cache.lengths[slots.long()] = lens.to(torch.int32)
         return self.final_logits(params, h.index_select(0, last))
 
-    def decode_hidden(self, params, tokens: torch.Tensor, cache: KVCache, rope_delta: torch.Tensor) -> torch.Tensor:
-        """One decode step for all B cache rows; appends k, v at ``cache.lengths`` (not advanced here)."""
+    def decode_hidden(self, params, tokens: torch.Tensor, cache: KVCache, rope_delta: torch.Tensor):
+        """One decode step for all B cache rows; appends k, v at ``cache.lengths`` (not advanced here).
+
+        Returns ``(h, normed)``: on a GPU the step runs the fused path (stream-K GEMM partials consumed by
+        kernels that also do bias / q-k norm / RoPE / KV write, residual + RMSNorm, SwiGLU) and ``h`` is
+        already normalised by ``final_norm``; on the CPU ``h`` is the raw residual stream.
+        """
         e = self._w(params, "embed")["embed"]
         x = ops.embed(tokens, e)
         params.release("embed")
         B = tokens.shape[0]
+        if tokens.is_cuda:
+            return self._decode_fused(params, x, cache, rope_delta), True
         p1 = (cache.lengths.to(torch.int64) + rope_delta.to(torch.int64)).to(torch.int32)
         pos = p1[None].expand(3, B).contiguous()
         rows = torch.arange(B, device=tokens.device)
@@ -356,7 +363,33 @@ class TextDecoder:
             act, _ = ops.linear_swiglu(hn, w["gu_w"], save_pre=False)
             x = ops.linear(act, w["down_w"], residual=h1, out_dtype=x.dtype)
             params.release(f"layer{i}")
-        return x
+        return x, False
+
+    def _decode_fused(self, params, x: torch.Tensor, cache: KVCache, rope_delta: torch.Tensor) -> torch.Tensor:
+        B = x.shape[0]
+        lens = cache.lengths
+        delta = rope_delta.to(torch.int64)
+        lens_after = lens + 1
+        w = self._w(params, "layer0")
+        xn, _ = ops.rms_norm(x, w["input_norm"], self.eps)
+        for i in range(self.n_layers):
+            w = self._w(params, f"layer{i}")
+            ws, meta = ops.gemm_partials(xn, w["qkv_w"])
+            q = ops.dec_qkv(ws, meta, w["qkv_b"], w["q_norm"], w["k_norm"], lens, delta, self.rope,
+                            cache.keys[i], cache.values[i], n_q=self.nq, n_kv=self.nkv, eps=self.eps)
+            o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale)
+            ws, meta = ops.gemm_partials(o.reshape(B, self.nq * self.D), w["o_w"])
+            h1, hn = ops.dec_residual_norm(ws, meta, x, w["post_norm"], self.eps)
+            ws, meta = ops.gemm_partials(hn, w["gu_w"])
+            act = ops.dec_swiglu(ws, meta)
+            ws, meta = ops.gemm_partials(act, w["down_w"])
+            if i + 1 < self.n_layers:
+                nxt = self._w(params, f"layer{i + 1}")["input_norm"]
+            else:
+                nxt = self._w(params, "head")["final_norm"]
+            x, xn = ops.dec_residual_norm(ws, meta, h1, nxt, self.eps)
+            params.release(f"layer{i}")
+        return xn
 
 
 __all__ = ["VisionEmbeddings", "PackedBatch", "KVCache", "LocalParams", "TextDecoder", "TrainCtx"]

@@ -101,6 +101,32 @@ def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, save_pre: bool = True):
     return act, pre
 
 
+def gemm_partials(a: torch.Tensor, b: torch.Tensor):
+    """Stream-K partial sums of ``a @ b.T`` for the fused decode consumers: (ws fp32 [slots, M, N], meta).
+
+    CUDA only: the CPU executor never takes the fused decode path.
+    """
+    return ext().gemm_partials(a, b)
+
+
+def dec_qkv(ws, meta, bias, q_w, k_w, lengths, delta, rope: "RopeCfg", k_cache, v_cache, *, n_q: int, n_kv: int,
+            eps: float):
+    """Sum QKV partials (+bias), RMSNorm q/k heads, MRoPE at position ``lengths + delta``, write k/v into the
+    cache at ``lengths``; returns q [B, n_q, D]."""
+    f, _ = rope.device_tables(ws.device)
+    return ext().dec_qkv(ws, list(meta), _opt(bias), q_w, k_w, lengths, delta, f, k_cache, v_cache, n_q, n_kv, float(eps))
+
+
+def dec_residual_norm(ws, meta, residual, w, eps: float):
+    """h = sum(partials) + residual (bf16); returns (h, rms_norm(h) * w)."""
+    return ext().dec_residual_norm(ws, list(meta), residual, w, float(eps))
+
+
+def dec_swiglu(ws, meta):
+    """silu(gate) * up of interleaved gate/up partial sums -> [M, N/2] bf16."""
+    return ext().dec_swiglu(ws, list(meta))
+
+
 def grad_input(dy: torch.Tensor, w: torch.Tensor, out_dtype=torch.bfloat16, out=None):
     """dX [M,K] = dY [M,N] @ W [N,K]."""
     return gemm(dy, w, b_kmajor=False, out_dtype=out_dtype, out=out)
