@@ -123,7 +123,18 @@ def collect(env, tokenizer, model, ts, cfg: TrainerConfig, batch_size: Optional[
                           min_pixels=cfg.vlm_min_pixels, max_pixels=cfg.vlm_max_pixels,
                           max_sequence_length=cfg.max_sequence_length, row_offset=row_offset)
     rewards = torch.tensor([e.reward for e in eb.episodes], dtype=torch.float32)
-    adv = group_advantages(rewards, cfg.group_size, cfg.adv_norm).to(model.device)
+    if cfg.adv_norm == "batch" and _distributed():
+        import torch.distributed as dist
+
+        st = torch.tensor([float(rewards.sum()), float((rewards ** 2).sum()), float(rewards.numel())],
+                          dtype=torch.float64, device=model.device)
+        dist.all_reduce(st)
+        mean = st[0] / st[2]
+        std = (st[1] / st[2] - mean ** 2).clamp_min(0).sqrt()
+        a = rewards.to(model.device, torch.float64) - mean
+        adv = (a / std if std > 1e-8 else a).float()
+    else:
+        adv = group_advantages(rewards, cfg.group_size, cfg.adv_norm).to(model.device)
     mbs = build_minibatches(model, eb, adv, _minibatch_count(cfg, len(eb.episodes)), cfg.max_sequence_length)
     return CollectResult(episodes=eb, rewards=rewards, advantages=adv, minibatches=mbs)
 
@@ -134,10 +145,29 @@ def score(model, mb: MiniBatch) -> torch.Tensor:
     return logp
 
 
+_TOKEN_METRICS = ("loss", "loss_pg", "loss_ent", "loss_kl", "entropy", "approx_kl", "clip_fraction",
+                  "token_logprob_mean", "ref_kl")
+
+
+def _distributed() -> bool:
+    import torch.distributed as dist
+
+    return dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
+
+
 def update(ts, cr: CollectResult, cfg: TrainerConfig, *, ref_model=None, kl_ctrl: Optional[AdaptiveKL] = None,
            kl_coef: Optional[float] = None) -> Tuple[Any, Dict[str, float]]:
-    """PPO/GRPO epochs over the collected minibatches; returns (train_state, host metrics)."""
+    """PPO/GRPO epochs over the collected minibatches; returns (train_state, host metrics).
+
+    Under data parallelism every rank holds its share of each minibatch; the
+    loss is normalised by the GLOBAL number of scored tokens of the minibatch,
+    so the summed (reduce-scattered) gradients equal the single-process
+    gradient, and the token-mean metrics are summed across ranks.
+    """
+    import torch.distributed as dist
+
     model = ts.model
+    distributed = _distributed()
     mbs = cr.minibatches
     use_policy_old = cfg.old_logprob_source == "policy"
     reuse_first = use_policy_old and cfg.ppo_epochs == 1
@@ -156,9 +186,19 @@ def update(ts, cr: CollectResult, cfg: TrainerConfig, *, ref_model=None, kl_ctrl
             logp, ent, ctx = model.token_logprobs(mb.batch, save=True)
             if mb.old_lp is None:
                 mb.old_lp = logp.detach().clone()
+            denom = None
+            if distributed:
+                cnt = torch.tensor([float(logp.numel())], device=logp.device)
+                dist.all_reduce(cnt)
+                denom = max(float(cnt.item()), 1e-8)
             _, g_lp, g_ent, m = ppo_loss(logp, ent, mb.old_lp, mb.adv_tok, clip_epsilon=cfg.clip_epsilon,
                                          entropy_coef=cfg.entropy_coef, kl_coef=coef, ref_logp=mb.ref_lp,
-                                         kl_ref_coef=cfg.kl_ref_coef)
+                                         kl_ref_coef=cfg.kl_ref_coef, denom=denom)
+            if distributed:
+                packed = torch.stack([m[k].float().reshape(()) for k in _TOKEN_METRICS])
+                dist.all_reduce(packed)
+                for i, k in enumerate(_TOKEN_METRICS):
+                    m[k] = packed[i]
             with torch.no_grad():
                 model.backward(ctx, g_lp, g_ent)
             del ctx

@@ -103,10 +103,19 @@ class GRPOTrainer:
         self.last_collect = cr
         eps = cr.episodes.episodes
         m.update(timer.spans())
-        m["reward/mean"] = float(cr.rewards.mean())
-        m["reward/std"] = float(cr.rewards.std(unbiased=False)) if cr.rewards.numel() > 1 else 0.0
-        m["tokens/generated"] = float(sum(e.action_length for e in eps))
-        m["tokens/total"] = float(sum(len(e.full_tokens) for e in eps))
+        r = cr.rewards.double()
+        stats = torch.tensor([float(r.sum()), float((r * r).sum()), float(r.numel()),
+                              float(sum(e.action_length for e in eps)), float(sum(len(e.full_tokens) for e in eps))],
+                             dtype=torch.float64, device=self.model.device)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(stats)
+        mean = stats[0] / stats[2]
+        m["reward/mean"] = float(mean)
+        m["reward/std"] = float((stats[1] / stats[2] - mean * mean).clamp_min(0).sqrt())
+        m["tokens/generated"] = float(stats[3])
+        m["tokens/total"] = float(stats[4])
         m["step"] = self.ts.step
         if eps:
             m["sample/text"] = eps[0].generated_text[:200]
