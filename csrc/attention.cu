@@ -571,6 +571,8 @@ __global__ void __launch_bounds__(NW * 32) decode_attn_kernel(const bf16* __rest
   float* sm_acc = sm_l + NW * REP;                           // [NW][REP][D]
   __shared__ int abort_flag;
 
+  pdl_wait();
+  pdl_trigger();
   const int hk = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
   const int L = min(lens[b], Tmax);
   const int per = (L + splits - 1) / splits;
@@ -737,6 +739,8 @@ __global__ void __launch_bounds__(NW * 32) decode_attn_kernel(const bf16* __rest
 
 // Merges the key splits of decode_attn_kernel: part [B, Hq, splits, 2 + D] -> o [B, Hq, D].
 __global__ void decode_combine_kernel(const float* __restrict__ part, bf16* __restrict__ o, int BH, int splits, int D) {
+  pdl_wait();
+  pdl_trigger();
   const int bh = blockIdx.x;
   if (bh >= BH) return;
   const float* p = part + static_cast<int64_t>(bh) * splits * (D + 2);
@@ -878,16 +882,13 @@ static void decode_dispatch(const at::Tensor& q, const at::Tensor& kc, const at:
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   at::Tensor part;
   if (splits > 1) part = at::empty({B, Hq, splits, D + 2}, q.options().dtype(at::kFloat));
-  kern<<<dim3(Hkv, B, splits), NW * 32, smem, st>>>(
-      reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(kc.data_ptr()),
-      reinterpret_cast<const bf16*>(vc.data_ptr()), lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()),
-      splits > 1 ? part.data_ptr<float>() : nullptr, Hq, Hkv, Tmax, scale * kLog2e, splits,
-      err_word(q.device().index()));
-  VLM_LAUNCHED();
+  launch_pdl(kern, dim3(Hkv, B, splits), dim3(NW * 32), smem, st, reinterpret_cast<const bf16*>(q.data_ptr()),
+             reinterpret_cast<const bf16*>(kc.data_ptr()), reinterpret_cast<const bf16*>(vc.data_ptr()),
+             lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()), splits > 1 ? part.data_ptr<float>() : nullptr,
+             Hq, Hkv, Tmax, scale * kLog2e, splits, err_word(q.device().index()));
   if (splits > 1) {
-    decode_combine_kernel<<<B * Hq, 128, 0, st>>>(part.data_ptr<float>(), reinterpret_cast<bf16*>(o.data_ptr()), B * Hq,
-                                                  splits, D);
-    VLM_LAUNCHED();
+    launch_pdl(decode_combine_kernel, dim3(B * Hq), dim3(128), 0, st, part.data_ptr<float>(),
+               reinterpret_cast<bf16*>(o.data_ptr()), B * Hq, splits, D);
   }
 }
 
@@ -908,3 +909,4 @@ void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at
 }
 
 }  // namespace vlm
+

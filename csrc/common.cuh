@@ -77,7 +77,7 @@ VLM_DEV void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled load, global -> this CTA's shared memory, completion on an mbarrier (no multicast).
+// 2-D tiled load, global -> this CTA's own shared memory, completion on an mbarrier.
 VLM_DEV void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -93,6 +93,13 @@ VLM_DEV void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_
                "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
+
+// ------------------------------------------------------------------ programmatic dependent launch
+// pdl_wait: block until the preceding kernel in the stream has completed and its memory is visible
+// (a no-op when the kernel was launched without the programmatic-serialization attribute).
+VLM_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// pdl_trigger: allow the next kernel of the stream to be scheduled before this one finishes.
+VLM_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // ------------------------------------------------------------------ tcgen05 / TMEM
 VLM_DEV void tmem_alloc(uint32_t* smem_holder, uint32_t ncols) {

@@ -36,6 +36,8 @@ __global__ void dec_qkv_kernel(const float* __restrict__ ws, SkMeta m, const bf1
                                bf16* __restrict__ q, bf16* __restrict__ kc, bf16* __restrict__ vc, int nq, int nkv,
                                int Tmax, float eps) {
   constexpr int TPH = D / 8;
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x, tid = threadIdx.x;
   const int head = tid / TPH, t = tid % TPH;
   const int col = tid * 8;
@@ -82,6 +84,8 @@ __global__ void dec_resnorm_kernel(const float* __restrict__ ws, SkMeta m, const
                                    const bf16* __restrict__ w, bf16* __restrict__ h_out, bf16* __restrict__ hn_out,
                                    int H, float eps) {
   __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x, col = threadIdx.x * 8;
   float x[8];
   float ss = 0.f;
@@ -118,6 +122,8 @@ __global__ void dec_resnorm_kernel(const float* __restrict__ ws, SkMeta m, const
 }
 
 __global__ void dec_swiglu_kernel(const float* __restrict__ ws, SkMeta m, bf16* __restrict__ act, int N) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.y;
   const int col = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (col >= N) return;
@@ -148,13 +154,13 @@ at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at
   TORCH_CHECK(threads <= 1024, "dec_qkv: too many heads for one CTA");
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   auto args = [&](auto kern) {
-    kern<<<m.M, threads, 0, st>>>(ws.data_ptr<float>(), m,
-                                  bias.defined() && bias.numel() ? reinterpret_cast<const bf16*>(bias.data_ptr()) : nullptr,
-                                  reinterpret_cast<const bf16*>(qw.data_ptr()), reinterpret_cast<const bf16*>(kw.data_ptr()),
-                                  lengths.data_ptr<int>(), delta.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),
-                                  reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(kc.data_ptr()),
-                                  reinterpret_cast<bf16*>(vc.data_ptr()), static_cast<int>(nq), static_cast<int>(nkv), Tmax,
-                                  static_cast<float>(eps));
+    launch_pdl(kern, dim3(m.M), dim3(threads), 0, st, ws.data_ptr<float>(), m,
+               bias.defined() && bias.numel() ? reinterpret_cast<const bf16*>(bias.data_ptr()) : nullptr,
+               reinterpret_cast<const bf16*>(qw.data_ptr()), reinterpret_cast<const bf16*>(kw.data_ptr()),
+               lengths.data_ptr<int>(), delta.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),
+               reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(kc.data_ptr()),
+               reinterpret_cast<bf16*>(vc.data_ptr()), static_cast<int>(nq), static_cast<int>(nkv), Tmax,
+               static_cast<float>(eps));
   };
   if (D == 128)
     args(dec_qkv_kernel<128>);
@@ -164,7 +170,6 @@ at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at
     args(dec_qkv_kernel<32>);
   else
     TORCH_CHECK(false, "dec_qkv: unsupported head_dim ", D);
-  VLM_LAUNCHED();
   return q;
 }
 
@@ -176,10 +181,9 @@ std::tuple<at::Tensor, at::Tensor> dec_residual_norm(at::Tensor ws, std::vector<
   const c10::cuda::CUDAGuard g(ws.device());
   at::Tensor h = at::empty_like(residual), hn = at::empty_like(residual);
   const int threads = ((m.N / 8 + 31) / 32) * 32;
-  dec_resnorm_kernel<<<m.M, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      ws.data_ptr<float>(), m, reinterpret_cast<const bf16*>(residual.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
-      reinterpret_cast<bf16*>(h.data_ptr()), reinterpret_cast<bf16*>(hn.data_ptr()), m.N, static_cast<float>(eps));
-  VLM_LAUNCHED();
+  launch_pdl(dec_resnorm_kernel, dim3(m.M), dim3(threads), 0, at::cuda::getCurrentCUDAStream(), ws.data_ptr<float>(), m,
+             reinterpret_cast<const bf16*>(residual.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
+             reinterpret_cast<bf16*>(h.data_ptr()), reinterpret_cast<bf16*>(hn.data_ptr()), m.N, static_cast<float>(eps));
   return {h, hn};
 }
 
@@ -189,9 +193,8 @@ at::Tensor dec_swiglu(at::Tensor ws, std::vector<int64_t> meta) {
   const c10::cuda::CUDAGuard g(ws.device());
   at::Tensor act = at::empty({m.M, m.N / 2}, ws.options().dtype(at::kBFloat16));
   const dim3 grid((m.N / 8 + 255) / 256, m.M);
-  dec_swiglu_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(ws.data_ptr<float>(), m,
-                                                                        reinterpret_cast<bf16*>(act.data_ptr()), m.N);
-  VLM_LAUNCHED();
+  launch_pdl(dec_swiglu_kernel, grid, dim3(256), 0, at::cuda::getCurrentCUDAStream(), ws.data_ptr<float>(), m,
+             reinterpret_cast<bf16*>(act.data_ptr()), m.N);
   return act;
 }
 

@@ -108,6 +108,8 @@ __global__ void rms_norm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __r
 // Small-M variant (decode): one CTA per row, one 16-byte chunk per thread held in registers.
 __global__ void rms_norm_row_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, bf16* __restrict__ y,
                                     float* __restrict__ rstd, int H, float eps) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x, c = threadIdx.x * 8;
   __shared__ float red[32];
   const bf16* xr = x + static_cast<int64_t>(row) * H;
@@ -155,11 +157,9 @@ void rms_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, dou
   const c10::cuda::CUDAGuard g(x.device());
   if (M < 1024 && H <= 8192) {
     const int threads = ((H / 8 + 31) / 32) * 32;
-    rms_norm_row_kernel<<<M, threads, 0, cur_stream()>>>(
-        reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
-        reinterpret_cast<bf16*>(y.data_ptr()), rstd.defined() && rstd.numel() ? rstd.data_ptr<float>() : nullptr, H,
-        static_cast<float>(eps));
-    VLM_LAUNCHED();
+    launch_pdl(rms_norm_row_kernel, dim3(M), dim3(threads), 0, cur_stream(), reinterpret_cast<const bf16*>(x.data_ptr()),
+               reinterpret_cast<const bf16*>(w.data_ptr()), reinterpret_cast<bf16*>(y.data_ptr()),
+               rstd.defined() && rstd.numel() ? rstd.data_ptr<float>() : nullptr, H, static_cast<float>(eps));
     return;
   }
   rms_norm_fwd_kernel<<<blocks_for(M, 8), 256, 0, cur_stream()>>>(
@@ -434,6 +434,8 @@ void swiglu_bwd(at::Tensor d_act, at::Tensor pre, at::Tensor out) {
 // ------------------------------------------------------------------ embedding gather / scatter
 __global__ void embed_kernel(const int64_t* __restrict__ tok, const bf16* __restrict__ table, bf16* __restrict__ out,
                              int T, int H, int64_t V) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   if (row >= T) return;
   int64_t id = tok[row];
@@ -449,9 +451,8 @@ void embed(at::Tensor tokens, at::Tensor table, at::Tensor out) {
   if (T == 0) return;
   TORCH_CHECK(tokens.scalar_type() == at::kLong && H % 8 == 0, "embed: int64 tokens, H % 8 == 0");
   const c10::cuda::CUDAGuard g(table.device());
-  embed_kernel<<<T, 128, 0, cur_stream()>>>(tokens.data_ptr<int64_t>(), reinterpret_cast<const bf16*>(table.data_ptr()),
-                                            reinterpret_cast<bf16*>(out.data_ptr()), T, H, table.size(0));
-  VLM_LAUNCHED();
+  launch_pdl(embed_kernel, dim3(T), dim3(128), 0, cur_stream(), tokens.data_ptr<int64_t>(),
+             reinterpret_cast<const bf16*>(table.data_ptr()), reinterpret_cast<bf16*>(out.data_ptr()), T, H, table.size(0));
 }
 
 __global__ void scatter_rows_kernel(bf16* __restrict__ h, const int64_t* __restrict__ rows, const bf16* __restrict__ src,

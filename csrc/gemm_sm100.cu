@@ -59,6 +59,7 @@ struct GemmParams {
   int streamk;
   int sk_grid;  // grid size of the stream-K launch
   int bn;
+  int b_prefetch;  // B may be loaded before pdl_wait (B is a weight no earlier kernel of the step writes)
 };
 
 // Work item: one accumulation segment of one output tile.
@@ -280,20 +281,48 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       int stage = 0;
       uint32_t phase = 0;
+      auto load_b = [&](uint8_t* b, int k0, int n0) {
+        if constexpr (!B_MN) {
+          tma_load_2d(b, &tmB, &full[stage], k0, n0);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0);
+        }
+      };
       WorkIter it(p, kb_count);
       Work w;
+      // Programmatic dependent launch: the weight operand B (never written by earlier kernels of the
+      // step) of the first STAGES k-blocks is requested before waiting for the previous kernel.
+      int prefetched = 0;
+      {
+        WorkIter it0 = it;
+        Work w0;
+        if (p.b_prefetch && it0.next(p, w0)) {
+          int tm0, tn0;
+          tile_coords(w0.tile, p.tiles_m, p.tiles_n, tm0, tn0);
+          prefetched = min(C::STAGES, w0.kb1 - w0.kb0);
+          for (int i = 0; i < prefetched; ++i) {
+            stage = i;
+            mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+            load_b(sB + i * C::B_BYTES, (w0.kb0 + i) * kBK, tn0 * BN);
+          }
+          stage = 0;
+        }
+      }
+      pdl_wait();
       while (ok && it.next(p, w)) {
         int tm, tn;
         tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
         const int m0 = tm * kBM, n0 = tn * BN;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrTimeoutProducer)) {
+          const bool pre = prefetched > 0;
+          if (!pre && !mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
           }
           uint8_t* a = sA + stage * C::A_BYTES;
           uint8_t* b = sB + stage * C::B_BYTES;
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          if (!pre) mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
           const int k0 = kb * kBK;
           if constexpr (!A_MN) {
             tma_load_2d(a, &tmA, &full[stage], k0, m0);
@@ -301,12 +330,8 @@ __global__ void __launch_bounds__(192, 1)
             tma_load_2d(a, &tmA, &full[stage], m0, k0);
             tma_load_2d(a + 8192, &tmA, &full[stage], m0 + 64, k0);
           }
-          if constexpr (!B_MN) {
-            tma_load_2d(b, &tmB, &full[stage], k0, n0);
-          } else {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0);
-          }
+          if (!pre) load_b(b, k0, n0);
+          if (pre) --prefetched;
           ++issued;
           if (++stage == C::STAGES) {
             stage = 0;
@@ -371,6 +396,8 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
+    pdl_wait();  // epilogue reads residual / writes outputs the previous kernel may still touch
+    if (threadIdx.x == 64) pdl_trigger();  // only after the wait: dependents never overlap our predecessor
     const int q = warp & 3;  // TMEM lanes [32q, 32q+32) are the ones this warp may read
     const int row_in_tile = q * 32 + lane;
     int lt = 0;
@@ -504,6 +531,7 @@ __global__ void __launch_bounds__(192, 1)
 
 // Generic consumer of stream-K partials: sums the slots of 16 columns and applies the GEMM epilogue.
 __global__ void sk_reduce_kernel(GemmParams p, SkMeta m) {
+  pdl_wait();
   const int chunks = (p.N + 15) / 16;
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= static_cast<int64_t>(p.M) * chunks) return;
@@ -526,6 +554,11 @@ __global__ void sk_reduce_kernel(GemmParams p, SkMeta m) {
 }
 
 // ------------------------------------------------------------------ host side
+// Set while the weights are read-only (the decode loop): GEMMs may then stream B before the wait on
+// their predecessor kernel.
+static thread_local bool g_static_weights = false;
+void set_static_weights(bool on) { g_static_weights = on; }
+
 template <int BN, bool A_MN, bool B_MN>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid, cudaStream_t st) {
   auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN>;
@@ -534,8 +567,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParam
     VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM));
     configured = true;
   }
-  kern<<<grid, 192, GemmCfg<BN>::SMEM, st>>>(ta, tb, p);
-  VLM_LAUNCHED();
+  launch_pdl(kern, dim3(grid), dim3(192), GemmCfg<BN>::SMEM, st, ta, tb, p);
 }
 
 static void check_operand(const at::Tensor& t, const char* name) {
@@ -589,6 +621,9 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   p.epi = static_cast<int>(epi);
   p.accumulate = accumulate;
   p.err = err_word(A.device().index());
+  // B is prefetched ahead of the dependency wait only when it is a K-major weight: the forward and
+  // decode GEMMs.  Backward GEMMs (MN-major operands) read activation gradients as B.
+  p.b_prefetch = (g_static_weights && b_kmajor && !accumulate && epi != EPI_VOCAB_GRAD) ? 1 : 0;
   if (bias.defined() && bias.numel()) {
     TORCH_CHECK(bias.scalar_type() == at::kBFloat16 && bias.is_contiguous() && bias.numel() == N, "gemm: bad bias");
     p.bias = reinterpret_cast<const __nv_bfloat16*>(bias.data_ptr());
@@ -671,8 +706,7 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
       *meta_out = m;
     } else {
       const int64_t threads = M * ((N + 15) / 16);
-      sk_reduce_kernel<<<static_cast<int>((threads + 127) / 128), 128, 0, st>>>(p, m);
-      VLM_LAUNCHED();
+      launch_pdl(sk_reduce_kernel, dim3(static_cast<int>((threads + 127) / 128)), dim3(128), 0, st, p, m);
     }
   }
 }

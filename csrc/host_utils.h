@@ -27,6 +27,33 @@ int64_t launch_count();
     ::vlm::note_launch();               \
   } while (0)
 
+// Launch with programmatic stream serialization (PDL): the kernel may start while its predecessor in
+// the stream is still running and must call pdl_wait() before reading or writing data the predecessor
+// touches.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  // Every kernel launched here asks for the maximum shared-memory carveout, so SMs never have to be
+  // reconfigured between consecutive kernels of different shared-memory footprints (which would also
+  // serialise programmatic dependent launches).
+  static bool carveout_set = false;
+  if (!carveout_set) {
+    VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    carveout_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  VLM_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(std::forward<Args>(args))...));
+  note_launch();
+}
+
 // Per-device error word written by bounded waits (0 = ok).  Allocated once per device.
 int* err_word(int device);
 // Reads and clears the error word of ``device`` (synchronises the current stream).

@@ -40,6 +40,8 @@ __global__ void __launch_bounds__(kSampThreads) sample_kernel(const float* __res
   __shared__ int ci[kKMax];
   __shared__ float cum[kKMax];
   __shared__ int s_choice;
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x, tid = threadIdx.x;
   const float* x = logits + static_cast<int64_t>(row) * ld;
   k = min(k, V);
@@ -174,11 +176,10 @@ void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, a
   if (B == 0) return;
   const c10::cuda::CUDAGuard g(logits.device());
   const int k = (top_k <= 0 || top_k > kKMax) ? kKMax : static_cast<int>(top_k);
-  sample_kernel<<<B, kSampThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      logits.data_ptr<float>(), logits.stride(0), static_cast<int>(logits.size(1)), tok.data_ptr<int64_t>(),
-      lp.data_ptr<float>(), step.data_ptr<int64_t>(), static_cast<float>(1.0 / temperature), k,
-      static_cast<float>(top_p), seed.data_ptr<int64_t>(), static_cast<long long>(row_offset));
-  VLM_LAUNCHED();
+  launch_pdl(sample_kernel, dim3(B), dim3(kSampThreads), 0, at::cuda::getCurrentCUDAStream(), logits.data_ptr<float>(),
+             logits.stride(0), static_cast<int>(logits.size(1)), tok.data_ptr<int64_t>(), lp.data_ptr<float>(),
+             step.data_ptr<int64_t>(), static_cast<float>(1.0 / temperature), k, static_cast<float>(top_p),
+             seed.data_ptr<int64_t>(), static_cast<long long>(row_offset));
 }
 
 }  // namespace vlm

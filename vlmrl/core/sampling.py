@@ -177,7 +177,7 @@ class Generator:
         torch.cuda.current_stream().wait_stream(s)
         g = torch.cuda.CUDAGraph()
         n0 = ops.launch_count()
-        with torch.cuda.graph(g):
+        with ops.static_weights(), torch.cuda.graph(g):
             self._decode_step(st, cfg, row_offset)
         st.graph_kernels = ops.launch_count() - n0
         for t, v in zip(state, snap):

@@ -29,6 +29,21 @@ def launch_count() -> int:
     return int(ext().launch_count()) if has_ext() else 0
 
 
+class static_weights:
+    """Context: parameters are read-only inside (decode loop), so GEMMs may stream weights ahead of their
+    dependency wait (programmatic dependent launch).  Never use it around optimizer or collective updates."""
+
+    def __enter__(self):
+        if has_ext():
+            ext().set_static_weights(True)
+        return self
+
+    def __exit__(self, *exc):
+        if has_ext():
+            ext().set_static_weights(False)
+        return False
+
+
 def check_errors(device: Optional[int] = None) -> None:
     """Raise if a bounded wait inside a kernel timed out (reads and clears the device error word)."""
     if not has_ext() or not torch.cuda.is_available():

@@ -190,7 +190,8 @@ def bench_decode_step(t: Timer, eager_steps: int = 0):
         torch.cuda.cudart().cudaProfilerStop()
         return
     weights = sum(v.numel() for k, v in m.params.units.items() if k != "visual") * 2
-    ms = t(step)
+    with ops.static_weights():
+        ms = t(step)
     emit("decode_step_4b_B64_T390", ms, bytes_=weights + 36 * 2 * B * 8 * 390 * 128 * 2)
 
 
