@@ -910,3 +910,91 @@ void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at
 
 }  // namespace vlm
 
+// =====================================================================================================
+// Allocation-free decode attention entry point.
+//
+// Declaration: this entry point has no counterpart in the reference project; it exists for callers of
+// this library that cannot allocate device memory at call time.  Examples: an inference host whose own
+// pool allocator owns all device memory (a cudaMalloc behind its back breaks its accounting and can
+// fail under its memory cap), code running where allocation would be an unsynchronised driver call in
+// a latency-critical loop, or plugin code that may only touch buffers it was handed.  Such callers
+// pass inputs and outputs only; the key-split partial results, which the regular decode_attn path
+// keeps in a temporary buffer from the PyTorch allocator, live here in a fixed device array instead.
+//
+// Contract:
+//  * Scratch: the file-scope array below, kNoAllocScratchFloats floats (4 MiB) per GPU.  Every GPU
+//    that loads this library holds it until the process exits.  A problem needing more than
+//    B * Hq * splits * (D + 2) <= kNoAllocScratchFloats floats is rejected (return value -2).
+//  * Set-up: the first call on a device (with that device current) resolves the array's device
+//    address with cudaGetSymbolAddress; make that first call before any CUDA-graph capture.
+//  * Sharing: all calls on a device share the one array and it keeps the last call's contents.
+//    Every partial slot a call reads is written earlier by the same call, so nothing needs clearing,
+//    but calls that overlap on the GPU (different streams, or graphs replayed concurrently) race
+//    on the array and must be serialised by the caller.
+//  * No cudaMalloc, cudaFree or allocating library routine is called.
+//  * Return value: 0 ok, -1 unsupported shape, -2 problem exceeds the scratch array, -3 CUDA error.
+// =====================================================================================================
+namespace vlm {
+
+constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 20;  // 4 MiB of fp32 partials
+static __device__ __align__(256) float g_noalloc_decode_scratch[kNoAllocScratchFloats];
+
+namespace {
+float* g_noalloc_ptr[64] = {nullptr};
+
+template <int D, int REP>
+int noalloc_decode_launch(const bf16* q, const bf16* kc, const bf16* vc, const int* lens, bf16* o, int B, int Hq,
+                          int Hkv, int Tmax, float scale, float* scratch, int sms, cudaStream_t st) {
+  constexpr int NW = 8, KC = 32, STAGES = 4;
+  // at least two key splits, so the partial results always go through the scratch array
+  const int splits =
+      std::max(2, std::min((3 * sms + B * Hkv - 1) / (B * Hkv), std::max(2, Tmax / (2 * KC))));
+  if (static_cast<int64_t>(B) * Hq * splits * (D + 2) > kNoAllocScratchFloats) return -2;
+  const int smem = 2 * STAGES * KC * D * 2 + STAGES * 8 + (2 * NW * REP + NW * REP * D) * 4;
+  auto kern = decode_attn_kernel<D, REP, NW, KC, STAGES>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -3;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -3;
+  kern<<<dim3(Hkv, B, splits), NW * 32, smem, st>>>(q, kc, vc, lens, o, scratch, Hq, Hkv, Tmax, scale * kLog2e,
+                                                     splits, err_word(dev));
+  if (cudaGetLastError() != cudaSuccess) return -3;
+  decode_combine_kernel<<<B * Hq, 128, 0, st>>>(scratch, o, B * Hq, splits, D);
+  if (cudaGetLastError() != cudaSuccess) return -3;
+  return 0;
+}
+}  // namespace
+
+}  // namespace vlm
+
+// q [B, Hq, D] bf16, k_cache / v_cache [B, Hkv, Tmax, D] bf16, lengths [B] int32 (valid keys per
+// sequence), out [B, Hq, D] bf16; all device pointers, contiguous.  `stream` is a cudaStream_t (0 for
+// the legacy default stream).  Computes out = softmax(q.K^T * scale) . V over the first lengths[b]
+// keys of each sequence (grouped-query attention, Hq / Hkv query heads per key head).
+extern "C" int vlmrl_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                              const int* lengths, void* out, int B, int Hq, int Hkv, int Tmax, int D,
+                                              float scale, void* stream) {
+  using namespace vlm;
+  if (B <= 0 || Hkv <= 0 || Hq % Hkv != 0 || Tmax <= 0) return -1;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_decode_scratch) != cudaSuccess || p == nullptr) return -3;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -3;
+  const auto* qq = static_cast<const bf16*>(q);
+  const auto* kk = static_cast<const bf16*>(k_cache);
+  const auto* vv = static_cast<const bf16*>(v_cache);
+  auto* oo = static_cast<bf16*>(out);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rep = Hq / Hkv;
+  float* scratch = g_noalloc_ptr[dev];
+  if (D == 128 && rep == 4) return noalloc_decode_launch<128, 4>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, scratch, sms, st);
+  if (D == 128 && rep == 2) return noalloc_decode_launch<128, 2>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, scratch, sms, st);
+  if (D == 128 && rep == 1) return noalloc_decode_launch<128, 1>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, scratch, sms, st);
+  if (D == 64 && rep == 4) return noalloc_decode_launch<64, 4>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, scratch, sms, st);
+  if (D == 32 && rep == 2) return noalloc_decode_launch<32, 2>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, scratch, sms, st);
+  return -1;
+}
