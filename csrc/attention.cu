@@ -12,8 +12,9 @@
 // recomputes P and dP to form dQ.
 //
 // Decode: flash-decoding over the KV cache, one CTA per (kv-head, sequence,
-// key split), coalesced row reads, per-warp online softmax, warp merge in
-// shared memory (plus a combine kernel when keys are split across CTAs).
+// key split).  For head_dim 128 the K/V chunks arrive by 2-D TMA into swizzled
+// tiles and both products run on mma.sync; other head sizes use 1-D bulk copies
+// and warp-shuffle dot products.  A combine kernel merges key splits.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -737,6 +738,197 @@ __global__ void __launch_bounds__(NW * 32) decode_attn_kernel(const bf16* __rest
   }
 }
 
+// Tensor-core decode attention (head_dim 128).  CTA = (kv-head, sequence, key split), 4 warps.
+// K and V chunks of 64 keys arrive by 2-D TMA as two 64x64 bf16 boxes each (128-byte swizzle, the same
+// XOR layout as Tile<64>), STAGES deep.  Warp w owns keys [16w, 16w+16) of every chunk:
+// S = Q.K^T with the REP query heads of the group as rows 0..REP-1 of a 16-row mma.sync tile,
+// online softmax per head row, O += P.V; the four warps merge through shared memory at the end.
+template <int REP, int STAGES = 3>
+__global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                             const __grid_constant__ CUtensorMap tmV,
+                                                             const bf16* __restrict__ q, const int* __restrict__ lens,
+                                                             bf16* __restrict__ o, float* __restrict__ part, int Hq,
+                                                             int Hkv, int Tmax, float scale_log2, int splits, int* err) {
+  constexpr int D = 128, KC = 64;
+  constexpr int HALF = KC * 64;  // elements of one 64x64 box
+  extern __shared__ __align__(1024) uint8_t tc_raw[];
+  bf16* sm = reinterpret_cast<bf16*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
+  bf16* sK = sm;                       // [STAGES][2 halves][64][64]
+  bf16* sV = sK + STAGES * 2 * HALF;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sV + STAGES * 2 * HALF);
+  float* red = reinterpret_cast<float*>(full + STAGES);  // merge area [4][REP][D + 2]
+  __shared__ int abort_flag;
+  pdl_wait();
+  pdl_trigger();
+  const int hk = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
+  const int L = min(lens[b], Tmax);
+  const int per = (L + splits - 1) / splits;
+  const int k0 = sp * per, k1 = min(L, k0 + per);
+  const int nk = max(0, k1 - k0);
+  const int nchunks = (nk + KC - 1) / KC;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int row_base = (b * Hkv + hk) * Tmax + k0;
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int c) {
+    const int st = c % STAGES;
+    mbar_arrive_expect_tx(&full[st], 4 * HALF * 2);
+    const int y = row_base + c * KC;
+    tma_load_2d(sK + (st * 2 + 0) * HALF, &tmK, &full[st], 0, y);
+    tma_load_2d(sK + (st * 2 + 1) * HALF, &tmK, &full[st], 64, y);
+    tma_load_2d(sV + (st * 2 + 0) * HALF, &tmV, &full[st], 0, y);
+    tma_load_2d(sV + (st * 2 + 1) * HALF, &tmV, &full[st], 64, y);
+  };
+  if (tid == 0)
+    for (int c = 0; c < STAGES && c < nchunks; ++c) issue(c);
+  // Q fragments: rows g < REP are the group's heads, the rest zero
+  uint32_t qa[D / 16][4];
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    qa[kk][1] = qa[kk][3] = 0u;
+    if (g < REP) {
+      const bf16* qr = q + (static_cast<int64_t>(b) * Hq + hk * REP + g) * D + kk * 16 + 2 * tq;
+      qa[kk][0] = *reinterpret_cast<const uint32_t*>(qr) ;
+      qa[kk][2] = *reinterpret_cast<const uint32_t*>(qr + 8);
+    } else {
+      qa[kk][0] = qa[kk][2] = 0u;
+    }
+  }
+  float acc[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  float m = -INFINITY, l = 0.f;  // running stats of row g (only rows g < REP are real)
+  int consumed = 0;
+  for (int c = 0; c < nchunks; ++c) {
+    const int st = c % STAGES;
+    const bool ok = mbar_wait(&full[st], static_cast<uint32_t>((c / STAGES) & 1), &abort_flag, err, kErrTimeoutFlag);
+    if (__syncthreads_or(!ok)) break;  // every thread leaves at the same chunk
+    consumed = c + 1;
+    const bf16* kt = sK + st * 2 * HALF;
+    bf16* vt = sV + st * 2 * HALF;
+    if ((c + 1) * KC > nk) {
+      // keys past this split's range: their V rows may hold anything (other sequences, unwritten
+      // cache slots), and P = 0 does not cancel a NaN there, so zero them; only the last chunk is
+      // partial and no later copy targets its stage.
+      for (int i = lane; i < 16 * 16; i += 32) {
+        const int r = warp * 16 + (i >> 4), ch = i & 15;
+        if (c * KC + r >= nk) reinterpret_cast<uint4*>(vt + (ch >> 3) * HALF + r * 64)[ch & 7] = make_uint4(0, 0, 0, 0);
+      }
+      __syncwarp();
+    }
+    float s[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t bb[4];
+      frag_b_nk<64>(bb, kt + (kk >> 2) * HALF, warp * 16, (kk & 3) * 16, lane);
+      mma_bf16(s[0], qa[kk], bb[0], bb[1]);
+      mma_bf16(s[1], qa[kk], bb[2], bb[3]);
+    }
+    const int kbase = c * KC + warp * 16;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool ok = kbase + nb * 8 + 2 * tq + e < nk;
+        s[nb][e] = ok ? s[nb][e] * scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[nb][e]);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(m, mx);
+    const float base = mn == -INFINITY ? 0.f : mn;
+    const float cf = exp2f(m - base);
+    float ps = 0.f;
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        s[nb][e] = exp2f(s[nb][e] - base);
+        ps += s[nb][e];
+      }
+    l = l * cf + ps;
+    m = mn;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      acc[i][0] *= cf;
+      acc[i][1] *= cf;
+    }
+    uint32_t pa[4];
+    pa[0] = pack_bf16x2(s[0][0], s[0][1]);
+    pa[1] = 0u;
+    pa[2] = pack_bf16x2(s[1][0], s[1][1]);
+    pa[3] = 0u;
+#pragma unroll
+    for (int dp = 0; dp < D / 16; ++dp) {
+      uint32_t bb[4];
+      frag_b_kn<64>(bb, vt + (dp >> 2) * HALF, warp * 16, (dp & 3) * 16, lane);
+      mma_bf16(acc[2 * dp], pa, bb[0], bb[1]);
+      mma_bf16(acc[2 * dp + 1], pa, bb[2], bb[3]);
+    }
+    __syncthreads();
+    if (tid == 0 && c + STAGES < nchunks) issue(c + STAGES);
+  }
+  if (consumed < nchunks) {  // aborted: drain the copies still in flight, then leave
+    if (tid == 0) {
+      const int issued = min(nchunks, consumed + STAGES);
+      for (int c = consumed; c < issued; ++c) {
+        volatile int no_abort = 0;
+        mbar_wait(&full[c % STAGES], static_cast<uint32_t>((c / STAGES) & 1), &no_abort, nullptr, 0);
+      }
+    }
+    return;
+  }
+  // per-warp row sums, then merge the four warps
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  float* rw = red + warp * REP * (D + 2);
+  if (g < REP) {
+    if (tq == 0) {
+      rw[g * (D + 2)] = m;
+      rw[g * (D + 2) + 1] = l;
+    }
+#pragma unroll
+    for (int nb = 0; nb < D / 8; ++nb) {
+      rw[g * (D + 2) + 2 + nb * 8 + 2 * tq] = acc[nb][0];
+      rw[g * (D + 2) + 2 + nb * 8 + 2 * tq + 1] = acc[nb][1];
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < REP * D; i += 128) {
+    const int r = i / D, d = i % D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, red[(w * REP + r) * (D + 2)]);
+    float lt = 0.f, at = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float* e = red + (w * REP + r) * (D + 2);
+      const float cfw = e[0] == -INFINITY ? 0.f : exp2f(e[0] - mx);
+      lt += e[1] * cfw;
+      at += e[2 + d] * cfw;
+    }
+    const int h = hk * REP + r;
+    if (splits == 1) {
+      o[(static_cast<int64_t>(b) * Hq + h) * D + d] = f2bf(lt > 0.f ? at / lt : 0.f);
+    } else {
+      float* pp = part + ((static_cast<int64_t>(b) * Hq + h) * splits + sp) * (D + 2);
+      pp[2 + d] = at;
+      if (d == 0) {
+        pp[0] = mx;
+        pp[1] = lt;
+      }
+    }
+  }
+}
+
 // Merges the key splits of decode_attn_kernel: part [B, Hq, splits, 2 + D] -> o [B, Hq, D].
 __global__ void decode_combine_kernel(const float* __restrict__ part, bf16* __restrict__ o, int BH, int splits, int D) {
   pdl_wait();
@@ -892,6 +1084,32 @@ static void decode_dispatch(const at::Tensor& q, const at::Tensor& kc, const at:
   }
 }
 
+template <int REP>
+static void decode_tc_dispatch(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& lens,
+                               at::Tensor& o, float scale) {
+  constexpr int STAGES = 3, D = 128;
+  const int B = static_cast<int>(q.size(0)), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(kc.size(1));
+  const int Tmax = static_cast<int>(kc.size(2));
+  const int sms = num_sms(q.device().index());
+  const int splits = std::max(1, std::min((2 * sms + B * Hkv - 1) / (B * Hkv), Tmax / 128));
+  const int smem = 1024 + STAGES * 4 * 64 * 64 * 2 + STAGES * 8 + 4 * REP * (D + 2) * 4;
+  const int64_t rows = static_cast<int64_t>(B) * Hkv * Tmax;
+  const CUtensorMap tk = make_tmap_2d_bf16(kc.data_ptr(), D, rows, D, 64, 64);
+  const CUtensorMap tv = make_tmap_2d_bf16(vc.data_ptr(), D, rows, D, 64, 64);
+  auto kern = decode_attn_tc_kernel<REP, STAGES>;
+  VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  at::Tensor part;
+  if (splits > 1) part = at::empty({B, Hq, splits, D + 2}, q.options().dtype(at::kFloat));
+  launch_pdl(kern, dim3(Hkv, B, splits), dim3(128), smem, st, tk, tv, reinterpret_cast<const bf16*>(q.data_ptr()),
+             lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()), splits > 1 ? part.data_ptr<float>() : nullptr,
+             Hq, Hkv, Tmax, scale * kLog2e, splits, err_word(q.device().index()));
+  if (splits > 1) {
+    launch_pdl(decode_combine_kernel, dim3(B * Hq), dim3(128), 0, st, part.data_ptr<float>(),
+               reinterpret_cast<bf16*>(o.data_ptr()), B * Hq, splits, D);
+  }
+}
+
 void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale) {
   TORCH_CHECK(q.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(), "decode_attn: contiguous");
   TORCH_CHECK(lens.scalar_type() == at::kInt, "decode_attn: int32 lengths");
@@ -900,6 +1118,9 @@ void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at
   const int D = static_cast<int>(q.size(2));
   const int rep = static_cast<int>(q.size(1) / kc.size(1));
   const float sc = static_cast<float>(scale);
+  if (D == 128 && rep == 4) return decode_tc_dispatch<4>(q, kc, vc, lens, o, sc);
+  if (D == 128 && rep == 2) return decode_tc_dispatch<2>(q, kc, vc, lens, o, sc);
+  if (D == 128 && rep == 8) return decode_tc_dispatch<8>(q, kc, vc, lens, o, sc);
 #define VLM_DEC(DD, RR) \
   if (D == DD && rep == RR) return decode_dispatch<DD, RR>(q, kc, vc, lens, o, sc);
   VLM_DEC(128, 4) VLM_DEC(128, 2) VLM_DEC(128, 1) VLM_DEC(128, 8) VLM_DEC(64, 4) VLM_DEC(64, 2) VLM_DEC(64, 1)

@@ -35,11 +35,7 @@ inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   // Every kernel launched here asks for the maximum shared-memory carveout, so SMs never have to be
   // reconfigured between consecutive kernels of different shared-memory footprints (which would also
   // serialise programmatic dependent launches).
-  static bool carveout_set = false;
-  if (!carveout_set) {
-    VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-    carveout_set = true;
-  }
+  VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;

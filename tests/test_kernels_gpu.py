@@ -172,6 +172,25 @@ def test_decode_attn_and_kv_write():
     _close(ops.decode_attn(q, kc, vc, lens), ref.decode_attn(q, kc, vc, lens, scale=1 / math.sqrt(D)), name="decode")
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,Tmax", [(3, 32, 8, 1000), (2, 16, 8, 700), (4, 64, 8, 260), (64, 32, 8, 390)])
+def test_decode_attn_poisoned_cache(B, Hq, Hkv, Tmax):
+    """Cache slots past each length hold NaN: the kernel must not read them into the output."""
+    D = 128
+    g = torch.Generator(device="cpu").manual_seed(B * 1000 + Tmax)
+    lens = torch.randint(1, Tmax + 1, (B,), generator=g).to(DEV, torch.int32)
+    lens[0] = Tmax
+    kc = _r(B, Hkv, Tmax, D, seed=40)
+    vc = _r(B, Hkv, Tmax, D, seed=41)
+    pos = torch.arange(Tmax, device=DEV)[None, None, :, None]
+    valid = pos < lens.long()[:, None, None, None]
+    kp = torch.where(valid, kc, torch.full_like(kc, float("nan")))
+    vp = torch.where(valid, vc, torch.full_like(vc, float("nan")))
+    q = _r(B, Hq, D, seed=42)
+    out = ops.decode_attn(q, kp, vp, lens)
+    assert torch.isfinite(out.float()).all()
+    _close(out, ref.decode_attn(q, kc * valid, vc * valid, lens, scale=1 / math.sqrt(D)), name="decode_poisoned")
+
+
 def test_embedding_ops():
     V, H, T = 1000, 256, 77
     table = _r(V, H, seed=31)

@@ -105,6 +105,19 @@ def bench_gemm(t: Timer):
         emit(f"gemm_swiglu_M{M}", ms, flops=2 * M * 2 * F * H)
 
 
+def bench_gemm_tiny(t: Timer):
+    """Fixed per-launch cost of the GEMM: one k-block / one tile / many k-blocks / many tiles."""
+    for M, N, K in ((64, 128, 64), (64, 128, 2560), (64, 6144, 64), (64, 6144, 2560), (256, 6144, 2560)):
+        a, b = _r(M, K), _r(N, K, scale=0.02)
+        ms = t(lambda: ops.gemm(a, b))
+        emit(f"gemm_tiny_M{M}_N{N}_K{K}", ms, bytes_=2 * (M * K + N * K + M * N))
+        ms = t(lambda: ops.gemm_partials(a, b))
+        emit(f"gemm_partials_M{M}_N{N}_K{K}", ms, bytes_=2 * (M * K + N * K + M * N))
+    x = torch.zeros(1, device="cuda")
+    ms = t(lambda: x.add_(1.0))
+    emit("empty_torch_kernel", ms)
+
+
 def bench_attn(t: Timer):
     B, L, Hq, Hkv, D = 32, 389, 32, 8, 128
     cu = torch.arange(0, (B + 1) * L, L, dtype=torch.int32, device="cuda")
@@ -213,7 +226,8 @@ def profile_small():
 
 
 CASES = {"gemm": bench_gemm, "attn": bench_attn, "decode": bench_decode, "vocab": bench_vocab, "norm": bench_norm,
-         "decode_step": bench_decode_step}
+         "decode_step": bench_decode_step,
+         "gemm_tiny": bench_gemm_tiny}
 
 
 def main():
