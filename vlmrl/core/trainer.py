@@ -74,6 +74,7 @@ class GRPOTrainer:
         self.cursor = 0
         self.iteration = 0
         self.last_collect = None
+        self.last_infos: Dict[str, Any] = {}
 
     @property
     def groups_per_rank(self) -> int:
@@ -101,6 +102,7 @@ class GRPOTrainer:
         self.kl_coef = m.get("kl_coef", self.kl_coef)
         self.iteration += 1
         self.last_collect = cr
+        self.last_infos = cr.episodes.raw_info or {}
         eps = cr.episodes.episodes
         m.update(timer.spans())
         r = cr.rewards.double()

@@ -196,19 +196,29 @@ class FSDPOptimizer:
         p.invalidate()
 
 
-def build_fsdp_models(spec, adamw: AdamWConfig, *, seed: int = 0, device=None, group=None, dtype=torch.bfloat16):
-    """-> (policy model on FSDP params, frozen replicated reference model, TrainState)."""
+def build_fsdp_models(spec, adamw: AdamWConfig, *, seed: int = 0, device=None, group=None, dtype=torch.bfloat16,
+                      units: Optional[Dict[str, torch.Tensor]] = None):
+    """-> (policy model on FSDP params, frozen replicated reference model, TrainState).
+
+    ``units`` (full parameter units, e.g. loaded from a checkpoint) replace the seeded random init.
+    """
     from vlmrl.models.qwen3vl.api import Qwen3VLModel
     from vlmrl.models.qwen3vl.params import all_layouts, init_params, text_layouts
     from vlmrl.utils.train_state import TrainState
 
     device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    units = init_params(spec, seed=seed, dtype=dtype, device=device)
+    if units is None:
+        units = init_params(spec, seed=seed, dtype=dtype, device=device)
+    else:
+        units = {k: v.to(device, dtype) for k, v in units.items()}
     ref = Qwen3VLModel(spec, units={k: v for k, v in units.items() if k != "visual"}, device=device, dtype=dtype)
     fp = FSDPParams(all_layouts(spec), units, group=group, dtype=dtype,
                     trainable=[l.name for l in text_layouts(spec)], replicate=["visual"])
     del units
     model = Qwen3VLModel(spec, params=fp, device=device, dtype=dtype)
+    if not isinstance(adamw, AdamWConfig):
+        raise NotImplementedError("the FSDP engine shards AdamW state only (factored Adafactor statistics need "
+                                  "whole rows); use optimizer=adamw or a single process")
     ts = TrainState(model, FSDPOptimizer(fp, adamw))
     return model, ref, ts
 

@@ -61,9 +61,15 @@ class TrainState:
 
     @classmethod
     def create_with_params(cls, model, cfg, master=None, use_ema: bool = False, rng: int = 0):
-        from vlmrl.core.optim import LocalOptimizer
+        from vlmrl.core.optim import make_optimizer
 
-        return cls(model, LocalOptimizer(model.params, cfg, master=master), step=1, rng=rng, use_ema=use_ema)
+        return cls(model, make_optimizer(model.params, cfg, master=master, spec=model.spec), step=1, rng=rng,
+                   use_ema=use_ema)
+
+    def enable_ema(self) -> None:
+        """Start an EMA copy of the parameters (``use_ema``) from the current master weights."""
+        self.use_ema = True
+        self.params_ema = {u: t.detach().float().clone() for u, t in self.optimizer.master_units().items()}
 
     # -------------------------------------------------------------- updates
     def apply_gradients(self) -> Dict[str, torch.Tensor]:
@@ -87,6 +93,12 @@ class TrainState:
         master = self._host_units(opt.master_units())
         params_full = self._host_units({**{k: v for k, v in opt.all_param_units().items()}, **master})
         tree = units_to_flax(model.spec, params_full)
+        ema = None
+        if self.params_ema is not None:
+            ema = units_to_flax(model.spec, _full_units(model, self._host_units(self.params_ema)))
+        if hasattr(opt, "state_tree"):  # Adafactor: factored statistics keyed unit/leaf
+            return {"params": tree, "params_ema": ema, "opt_state": {"adafactor": opt.state_tree()},
+                    "step": int(self.step)}
         mu = units_to_flax(model.spec, _full_units(model, self._host_units(opt.moment_units(0))))
         nu = units_to_flax(model.spec, _full_units(model, self._host_units(opt.moment_units(1))))
         adam = ScaleByAdamState(count=np.asarray(self.step - 1, dtype=np.int32), mu=mu, nu=nu)
@@ -102,6 +114,11 @@ class TrainState:
         units = flax_to_units(spec, data["params"])
         opt_state = data.get("opt_state")
         adam = None
+        if isinstance(opt_state, dict) and "adafactor" in opt_state:
+            self.optimizer.load_units(units)
+            self.optimizer.load_state_tree(opt_state["adafactor"])
+            self.step = int(np.asarray(data.get("step", 1)))
+            return self
         if opt_state is not None:
             inner = opt_state[1] if len(opt_state) == 2 and isinstance(opt_state[1], tuple) else opt_state
             adam = inner[0]

@@ -98,12 +98,13 @@ class MetricLogger:
     def log(self, metrics: Dict[str, Any], step: int) -> None:
         if self.rank != 0:
             return
-        row = {"step": int(step), "time": time.time()}
+        row = {}
         for k, v in metrics.items():
             if isinstance(v, (int, float, str, bool)) or v is None:
                 row[k] = v
             elif hasattr(v, "item"):
                 row[k] = v.item()
+        row.update(step=int(step), time=time.time())  # the explicit step wins over a metric named "step"
         if self._fh:
             self._fh.write(json.dumps(row) + "\n")
             self._fh.flush()
