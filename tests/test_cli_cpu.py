@@ -99,3 +99,98 @@ def test_adafactor_matches_numpy_statement():
     for name, p0 in before.items():
         exp = _adafactor_leaf_np(p0, gl[name], 1e-2, 1e-2, 2)
         np.testing.assert_allclose(after[name].numpy(), exp, rtol=2e-4, atol=1e-6, err_msg=name)
+
+
+def test_eval_cli_text_and_image(tmp_path):
+    from PIL import Image
+
+    from vlmrl.core import eval as eval_cli
+
+    img = tmp_path / "img.png"
+    Image.fromarray(np.random.default_rng(0).integers(0, 256, (64, 64, 3), dtype=np.uint8)).save(img)
+    dump = tmp_path / "m.json"
+    rep = eval_cli.main(["--preset=tiny", "--prompt=Where is this?", f"--image={img}", "--max_new_tokens=5",
+                         "--benchmark_runs=2", "--batch=2", f"--dump_metrics={dump}",
+                         f"--plot_path={tmp_path / 'chart.png'}"])
+    s = rep["native"]["summary"]
+    assert s["runs"] == 2 and s["tokens_total"] > 0 and "steady_throughput_mean" in s
+    assert rep["native"]["first_token_s"] is not None
+    assert json.load(open(dump))["native"]["summary"]["runs"] == 2
+    rep = eval_cli.main(["--preset=tiny", "--prompt=hello", "--max_new_tokens=3", "--benchmark_runs=1"])
+    assert rep["native"]["summary"]["runs"] == 1
+
+
+def test_hf_to_jax_round_trip(tmp_path):
+    from safetensors.torch import save_file
+
+    from vlmrl.models.qwen3vl.config import spec_to_config
+    from vlmrl.models.qwen3vl.weights import create_model_from_ckpt, units_to_hf_state_dict
+    from vlmrl.utils import hf_to_jax
+
+    spec, units, _ = tiny_model(seed=11)
+    snap = tmp_path / "snap"
+    snap.mkdir()
+    json.dump(spec_to_config(spec), open(snap / "config.json", "w"))
+    json.dump({"chat_template": "x"}, open(snap / "chat_template.json", "w"))
+    sd = {k: v.contiguous() for k, v in units_to_hf_state_dict(spec, units).items()}
+    save_file(sd, str(snap / "model.safetensors"))
+    out = tmp_path / "ckpt"
+    hf_to_jax.main([f"--model_dir={out}", f"--hf_dir={snap}"])
+    assert (out / "params.pkl").exists() and (out / "config.json").exists() and (out / "chat_template.json").exists()
+    model, params = create_model_from_ckpt(str(out))
+    assert "params" not in params and len(params) > 0
+    for name, t in units.items():
+        torch.testing.assert_close(model.params.units[name], t, msg=lambda s: f"{name}: {s}")
+
+
+def test_policy_token_logprobs_dense_matches_full_logits():
+    from vlmrl.core.policy import build_rope, token_logprobs_vlm
+    from vlmrl.models.qwen3vl.rope import mrope_cos_sin
+    from helpers import tiny_episodes
+
+    spec, units, m = tiny_model(seed=4)
+    batch, counts, seqs, plens = tiny_episodes(spec, m, n=2, prompt_text=7, action=3)
+    T = max(len(s) for s in seqs)
+    tok = torch.zeros(2, T, dtype=torch.long)
+    mask = torch.zeros(2, T - 1)
+    for b, s in enumerate(seqs):
+        tok[b, :len(s)] = torch.as_tensor(s)
+        mask[b, :len(s) - 1] = 1
+    grids = [[(1, 4, 4)], [(1, 4, 4)]]
+    vis = batch.vision
+    lp = token_logprobs_vlm(m, spec.image_token_id, tok, mask, vis, grids)
+    n_img = 4
+    for b, s in enumerate(seqs):
+        rows = torch.arange(b * n_img, (b + 1) * n_img)
+        logits = m.forward_vlm(torch.as_tensor(s[:-1])[None], vis.select(rows), [(1, 4, 4)])[0]
+        exp = torch.log_softmax(logits.float(), -1).gather(-1, torch.as_tensor(s[1:])[:, None])[:, 0]
+        torch.testing.assert_close(lp[b, :len(s) - 1], exp, atol=1e-4, rtol=1e-4)
+        assert float(lp[b, len(s) - 1:].abs().sum()) == 0.0
+    cos, sin = build_rope(spec, tok, grids)
+    assert cos.shape == (2, T, spec.text.head_dim)
+    assert torch.allclose(cos[0, 0], torch.ones(spec.text.head_dim))
+
+
+def test_sharding_plans():
+    from vlmrl.utils.sharding import create_sharding, get_local_slice, shard_axis
+
+    shapes = {"embed": (151936, 2560), "norm": (2560,), "odd": (1001, 1003)}
+    plan, rep, data, shard_data = create_sharding("fsdp", shapes, world=8)
+    assert plan["embed"].axis == 0 and plan["norm"].axis is None and plan["odd"].axis is None
+    assert shard_axis((7, 4096, 1024), 2, 8) == 1
+    x = torch.arange(16).reshape(8, 2)
+    assert torch.equal(shard_data(x), x[0:1])  # rank 0 of the 8 the plan was made for
+    assert torch.equal(shard_data(x[:3]), x[:3])  # not divisible: kept whole
+    assert torch.equal(get_local_slice(x, world=4, rank=1), x[2:4])
+    plan, *_ = create_sharding("dp")
+    assert plan.axis is None
+
+
+def test_rollout_cli(capsys):
+    from vlmrl.core import rollout
+
+    rewards = rollout.main(["--preset=tiny", "--env_name=synthetic_parity", "--episodes=5", "--batch_size=2",
+                            "--max_new_tokens=4", "--top_k=8"])
+    assert len(rewards) == 5
+    out = capsys.readouterr().out
+    assert "[episode 4]" in out and "Collected 5 episodes" in out

@@ -241,5 +241,72 @@ def episodes_to_training_batch(model, episodes: Sequence[Episode], *, vision: Op
     return rollout, batch
 
 
+def main(argv=None) -> List[float]:
+    """Sample environment episodes without training (reference CLI, ``core/rollout.py:451-521``)."""
+    import argparse
+
+    from vlmrl.core.train import load_policy, resolve_pad_and_eos
+    from vlmrl.envs.base import create_env
+    from vlmrl.utils.rng import RngSeq
+    from vlmrl.utils.tokenizer import load_tokenizer
+
+    ap = argparse.ArgumentParser(description="Collect RL episodes using the unified sampler.")
+    ap.add_argument("--model_dir", default="", type=str)
+    ap.add_argument("--preset", default="", type=str, help="random-init architecture when model_dir has no weights")
+    ap.add_argument("--env_name", required=True, type=str)
+    ap.add_argument("--episodes", type=int, default=4)
+    ap.add_argument("--batch_size", type=int, default=1)
+    ap.add_argument("--group_size", type=int, default=1)
+    ap.add_argument("--temperature", type=float, default=0.7)
+    ap.add_argument("--top_p", type=float, default=0.9)
+    ap.add_argument("--top_k", type=int, default=None)
+    ap.add_argument("--max_new_tokens", type=int, default=64)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--min_pixels", type=int, default=-1)
+    ap.add_argument("--max_pixels", type=int, default=-1)
+    args = ap.parse_args(argv)
+    dev = torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
+    model, _ = load_policy(args.model_dir, args.preset, dev, torch.bfloat16 if dev.type == "cuda" else torch.float32,
+                           seed=args.seed)
+    tokenizer = load_tokenizer(args.model_dir or None, vocab_size=model.spec.text.vocab_size)
+    env = create_env(args.env_name, tokenizer)
+    pad_id, eos_id = resolve_pad_and_eos(tokenizer, model.spec)
+    cfg = SamplingConfig(temperature=float(args.temperature),
+                         top_p=float(args.top_p) if 0.0 < float(args.top_p) < 1.0 else None,
+                         top_k=int(args.top_k) if args.top_k is not None and int(args.top_k) > 0 else None,
+                         eos_id=eos_id, pad_id=pad_id, max_new_tokens=int(args.max_new_tokens))
+    rng = RngSeq(int(args.seed))
+    gen = Generator(model)
+    remaining, taken, cursor = max(0, int(args.episodes)), 0, 0
+    rewards: List[float] = []
+    gs = max(1, int(args.group_size))
+    while remaining > 0:
+        take = max(1, min(int(args.batch_size), -(-remaining // gs)))
+        eb = collect_episodes(env, tokenizer, model, cfg, groups_per_batch=take, group_size=gs, seed=rng.next(),
+                              task_offset=cursor, generator=gen,
+                              min_pixels=args.min_pixels if args.min_pixels > 0 else None,
+                              max_pixels=args.max_pixels if args.max_pixels > 0 else None)
+        cursor += take
+        for ep in eb.episodes[:remaining]:
+            rewards.append(float(ep.reward))
+            resp = ep.generated_text.replace("\n", " ").strip()
+            prompt = ep.prompt_text.strip().splitlines()[-1] if ep.prompt_text.strip() else ""
+            keys = ", ".join(sorted(ep.info.keys())) if ep.info else "none"
+            print(f"[episode {taken}] reward={ep.reward:.3f} done={ep.done} prompt='{prompt}' response='{resp}' "
+                  f"info_keys={keys}")
+            taken += 1
+        remaining -= min(remaining, len(eb.episodes))
+    if rewards:
+        print(f"Collected {len(rewards)} episodes. reward_mean={float(np.mean(rewards)):.3f} "
+              f"reward_std={float(np.std(rewards)):.3f}")
+    else:
+        print("No episodes collected.")
+    return rewards
+
+
 __all__ = ["PreparedPrompt", "Episode", "EpisodeBatch", "encode_images", "prepare_prompts", "collect_episodes",
-           "episodes_to_training_batch"]
+           "episodes_to_training_batch", "main"]
+
+
+if __name__ == "__main__":
+    main()
