@@ -247,6 +247,7 @@ def main():
         "config": {"model": f"{args.preset} architecture (random init)", "global_batch": total_seqs,
                    "seq_len": f"{196 + 2 + args.prompt_tokens} prompt + {args.max_new} new",
                    "parallelism": f"fsdp{world}" if world > 1 else "single-gpu",
+                   "fsdp_comm": getattr(model.params, "comm", None) if world > 1 else None,
                    "groups_per_batch": args.groups, "group_size": args.group_size, "minibatches": args.minibatches,
                    "kl_ref_coef": 0.01, "top_k": args.top_k, "top_p": 0.9, "temperature": 0.7,
                    "l2": "no flush: per-step working set (8.8 GB weights) >> 126 MB L2"},
@@ -261,6 +262,9 @@ def main():
     if rank == 0:
         print(json.dumps(out))
     if world > 1:
+        close = getattr(model.params, "close", None)
+        if close is not None:
+            close()
         dist.destroy_process_group()
     return 0
 

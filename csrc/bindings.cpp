@@ -31,6 +31,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &vlm::sample);
   m.def("vocab_logprob_fwd", &vlm::vocab_logprob_fwd);
   m.def("vocab_logprob_bwd", &vlm::vocab_logprob_bwd);
+  m.def("symm_alloc", &vlm::symm_alloc, "cudaMalloc an IPC-exportable buffer");
+  m.def("symm_free", &vlm::symm_free);
+  m.def("symm_ipc_handle", &vlm::symm_ipc_handle);
+  m.def("symm_open", &vlm::symm_open, "map a peer's buffer from its IPC handle");
+  m.def("symm_close", &vlm::symm_close);
+  m.def("symm_view", &vlm::symm_view);
+  m.def("rs_pull", &vlm::rs_pull, "reduce-scatter by pulling shards from peer memory");
+  m.def("adamw_push", &vlm::adamw_push, "sharded AdamW storing bf16 params into every rank's gathered buffer");
+  m.def("peer_wait", &vlm::peer_wait);
+  m.def("peer_barrier", &vlm::peer_barrier);
   m.def("read_and_clear_error", &vlm::read_and_clear_error);
   m.def("launch_count", &vlm::launch_count, "kernel launches issued by this library so far");
 }

@@ -76,6 +76,22 @@ void vocab_logprob_fwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tenso
 void vocab_logprob_bwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tensor lse, at::Tensor ent, at::Tensor g_lp,
                        at::Tensor g_ent, at::Tensor dh, at::Tensor dw);
 
+// symm.cu (peer-memory collectives)
+int64_t symm_alloc(int64_t bytes, int64_t device);
+void symm_free(int64_t ptr, int64_t device);
+at::Tensor symm_ipc_handle(int64_t ptr, int64_t device);
+int64_t symm_open(at::Tensor handle, int64_t device);
+void symm_close(int64_t ptr, int64_t device);
+at::Tensor symm_view(int64_t base, int64_t offset_bytes, std::vector<int64_t> sizes, at::ScalarType dtype,
+                     int64_t device);
+void rs_pull(std::vector<int64_t> bufs, int64_t unit_off_bytes, int64_t shard_off, at::Tensor out, bool accumulate,
+             std::vector<int64_t> sigs, int64_t slot, int64_t epoch, int64_t rank, int64_t max_ctas);
+int64_t adamw_push(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, std::vector<int64_t> dst,
+                   int64_t dst_off_bytes, at::Tensor scale, double lr, double b1, double b2, double eps, double wd,
+                   int64_t step, std::vector<int64_t> sigs, int64_t slot, int64_t rank);
+void peer_wait(int64_t local_sig, int64_t slot, int64_t target, int64_t rank, int64_t world, int64_t device);
+void peer_barrier(std::vector<int64_t> sigs, int64_t slot, int64_t epoch, int64_t rank, int64_t device);
+
 // host_utils.cu
 int64_t read_and_clear_error(int64_t device);
 int64_t launch_count();

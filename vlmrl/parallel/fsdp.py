@@ -6,39 +6,56 @@ wired in): here FSDP is the training path for N > 1 GPUs.
 Layout: every parameter unit (``vlmrl.models.qwen3vl.params``) is padded to a
 multiple of ``128 * world`` elements and split into ``world`` contiguous
 shards.  Rank r keeps shard r of: the bf16 compute copy, the fp32 master, the
-AdamW moments and the fp32 gradient.
+AdamW moments and the fp32 gradient.  The bf16 unit is kept gathered (with
+180 GB of HBM a replicated bf16 copy of a 4-8B model is cheap, so only the
+fp32 optimizer state — 16 bytes/param — is sharded).
 
-* ``get(unit)`` all-gathers the bf16 unit on first use and keeps it until the
-  next optimizer step (the forward's gathered weights serve the backward too:
-  with 180 GB of HBM a replicated bf16 copy of a 4-8B model is cheap, so only
-  the fp32 optimizer state — 16 bytes/param — is sharded).
-* ``grad(unit)`` hands the executor a full-size fp32 accumulator;
-  ``grad_done(unit)`` reduce-scatters it (sum) into this rank's gradient shard
-  on a side stream, overlapped with the backward of the next unit.
-* ``FSDPOptimizer.step`` computes the global gradient norm (shard sums
-  all-reduced), clips, runs the AdamW kernel on the shards (which also writes
-  the bf16 shard) and invalidates the gathered copies.
+Communication (``comm``):
 
-Collectives go through NCCL (``vlmrl.parallel.dist``); the NVLink peer-memory
-kernels in ``vlmrl.parallel.symm`` replace them where a fused path exists.
+* ``p2p`` (default with NCCL ranks on one node): gathered bf16 units and the
+  full-size fp32 gradients live in IPC-shared buffers mapped by every rank
+  (``vlmrl.parallel.symm``).  ``grad_done(unit)`` launches the peer-pull
+  reduce-scatter kernel on a side stream (overlapped with the backward of the
+  next unit); ``FSDPOptimizer.step`` all-reduces the squared norm (one float),
+  then one fused kernel per unit applies AdamW to the shard and stores the bf16
+  result into every rank's gathered unit; a bounded device-side wait publishes
+  them.  No NCCL all-gather or reduce-scatter runs in a step.
+* ``nccl`` (also gloo on CPU): NCCL/gloo reduce-scatter per unit and an
+  all-gather of each stale unit on first use after a step — the baseline.
 """
 
 from __future__ import annotations
 
+import os
 from typing import Dict, Iterable, List, Optional, Sequence
 
 import torch
 import torch.distributed as dist
 
 from vlmrl import ops
+from vlmrl.ops._ext import ext
 from vlmrl.core.optim import AdamWConfig, _unit_order
 from vlmrl.models.qwen3vl.params import UnitLayout
 from vlmrl.parallel.dist import all_gather_into, all_reduce_, reduce_scatter_into
 
 
 class FSDPParams:
+    """Sharded parameter source for the executor (``get``/``grad``/``grad_done`` protocol).
+
+    ``comm="p2p"`` (default with NCCL on one node): gathered bf16 units and
+    full-size fp32 gradients live in IPC-shared buffers (``SymmetricBuffer``);
+    ``grad_done`` launches the peer-pull reduce-scatter kernel and the
+    optimizer's fused AdamW kernel stores the new bf16 shard into every rank's
+    gathered copy, so no NCCL all-gather or reduce-scatter runs in a step.
+    ``comm="nccl"`` (and gloo on CPU): the same protocol over NCCL/gloo
+    collectives, the baseline the fused path is measured against.  Both keep
+    the gathered buffers at fixed addresses, so CUDA graphs that captured them
+    stay valid across optimizer steps.
+    """
+
     def __init__(self, layouts: Sequence[UnitLayout], full_units: Dict[str, torch.Tensor], *, group=None,
-                 dtype=torch.bfloat16, trainable: Optional[Iterable[str]] = None, replicate: Iterable[str] = ()):
+                 dtype=torch.bfloat16, trainable: Optional[Iterable[str]] = None, replicate: Iterable[str] = (),
+                 comm: Optional[str] = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -49,12 +66,21 @@ class FSDPParams:
         self.shards: Dict[str, torch.Tensor] = {}
         self.padded: Dict[str, int] = {}
         self.gathered: Dict[str, torch.Tensor] = {}
+        self.fresh: Dict[str, bool] = {}
         self.grads_full: Dict[str, torch.Tensor] = {}
         self.grad_shards: Dict[str, torch.Tensor] = {}
-        self._pending: List = []
         self.device = next(iter(full_units.values())).device
         self.comm_stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
+        if comm is None:
+            comm = os.environ.get("VLMRL_FSDP_COMM", "p2p")
+        if comm == "p2p":
+            from vlmrl.parallel.symm import p2p_supported
+
+            if self.device.type != "cuda" or self.world > 8 or not p2p_supported(group):
+                comm = "nccl"
+        self.comm = comm
         rep = set(replicate)
+        sharded = []
         for name, lay in self.layouts.items():
             full = full_units[name]
             if name in rep or name not in self.trainable:
@@ -67,17 +93,65 @@ class FSDPParams:
             buf[:lay.numel].copy_(full[:lay.numel])
             self.shards[name] = buf[self.rank * n:(self.rank + 1) * n].clone()
             self.grad_shards[name] = torch.zeros(n, dtype=torch.float32, device=self.device)
+            sharded.append(name)
+        self.order = sorted(sharded, key=_unit_order)
+        self.slot = {u: i for i, u in enumerate(self.order)}
+        if self.comm == "p2p":
+            self._init_p2p()
+        else:
+            for u in self.order:
+                self.gathered[u] = torch.empty(self.padded[u], dtype=dtype, device=self.device)
+                self.fresh[u] = False
         self.units = self.replicated  # frozen units, for code that wants a plain dict
+
+    # ---------------------------------------------------------------- peer-memory setup
+    def _init_p2p(self) -> None:
+        from vlmrl.parallel.symm import SymmetricBuffer
+
+        W = self.world
+        self.g_off: Dict[str, int] = {}
+        self.p_off: Dict[str, int] = {}
+        go = po = 0
+        for u in self.order:
+            self.g_off[u], self.p_off[u] = go, po
+            go += self.padded[u] * 4
+            po += self.padded[u] * 2
+        self.sym_grad = SymmetricBuffer(go, self.group, self.device)
+        self.sym_param = SymmetricBuffer(po, self.group, self.device)
+        self.n_slots = len(self.order) + 2          # one per unit (reduce-scatter), push, barrier
+        self.sym_sig = SymmetricBuffer(self.n_slots * W * 8, self.group, self.device)
+        self.push_slot, self.barrier_slot = len(self.order), len(self.order) + 1
+        self.rs_epoch = [0] * len(self.order)
+        self.push_target = 0
+        self.barrier_epoch = 0
+        self.grad_live: Dict[str, bool] = {}
+        self.reduced: Dict[str, bool] = {u: False for u in self.order}
+        for u in self.order:
+            self.gathered[u] = self.sym_param.view(self.p_off[u], (self.padded[u],), self.dtype)
+            self.grads_full[u] = self.sym_grad.view(self.g_off[u], (self.padded[u],), torch.float32)
+            self.grad_live[u] = False
+            all_gather_into(self.gathered[u], self.shards[u], group=self.group)
+            self.fresh[u] = True
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        """Release the IPC-shared buffers (collective)."""
+        if self.comm == "p2p":
+            for b in (self.sym_grad, self.sym_param, self.sym_sig):
+                b.close()
+            self.gathered.clear()
+            self.grads_full.clear()
+            self.comm = "closed"
 
     # ---------------------------------------------------------------- ParamSource protocol
     def get(self, name: str) -> torch.Tensor:
         if name in self.replicated:
             return self.replicated[name]
-        buf = self.gathered.get(name)
-        if buf is None:
-            buf = torch.empty(self.padded[name], dtype=self.dtype, device=self.device)
+        buf = self.gathered[name]
+        if not self.fresh[name]:
             all_gather_into(buf, self.shards[name], group=self.group)
-            self.gathered[name] = buf
+            self.fresh[name] = True
         return buf[:self.layouts[name].numel]
 
     def release(self, name: str) -> None:
@@ -86,6 +160,21 @@ class FSDPParams:
     def grad(self, name: str) -> Optional[torch.Tensor]:
         if name not in self.trainable or name in self.replicated:
             return None
+        if self.comm == "p2p":
+            g = self.grads_full[name]
+            if not self.grad_live[name]:
+                if self.reduced[name]:
+                    # a peer may still be pulling from this buffer (no optimizer step since the last
+                    # reduce-scatter): wait for every rank's reduce-scatters before overwriting it
+                    self.sync_grads()
+                    self.barrier_epoch += 1
+                    ext().peer_barrier(self.sym_sig.ptrs, self.barrier_slot, self.barrier_epoch, self.rank,
+                                       self.sym_sig.dev_index)
+                    for u in self.reduced:
+                        self.reduced[u] = False
+                g.zero_()
+                self.grad_live[name] = True
+            return g[:self.layouts[name].numel]
         g = self.grads_full.get(name)
         if g is None:
             g = torch.zeros(self.padded[name], dtype=torch.float32, device=self.device)
@@ -93,6 +182,19 @@ class FSDPParams:
         return g[:self.layouts[name].numel]
 
     def grad_done(self, name: str) -> None:
+        if self.comm == "p2p":
+            if not self.grad_live.get(name):
+                return
+            self.grad_live[name] = False
+            self.reduced[name] = True
+            i = self.slot[name]
+            self.rs_epoch[i] += 1
+            n = self.padded[name] // self.world
+            self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.comm_stream):
+                ext().rs_pull(self.sym_grad.ptrs, self.g_off[name], self.rank * n, self.grad_shards[name], True,
+                                  self.sym_sig.ptrs, i, self.rs_epoch[i], self.rank, 32)
+            return
         g = self.grads_full.pop(name, None)
         if g is None:
             return
@@ -113,7 +215,10 @@ class FSDPParams:
             torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
 
     def invalidate(self) -> None:
-        self.gathered.clear()
+        """The shards changed (optimizer step or load): gathered copies are stale until re-gathered."""
+        if self.comm != "p2p":
+            for u in self.fresh:
+                self.fresh[u] = False
 
     def zero_grads(self) -> None:
         for g in self.grad_shards.values():
@@ -123,9 +228,20 @@ class FSDPParams:
         """Gathered unit (collective: every rank must call it)."""
         return self.get(name)
 
+    def regather(self) -> None:
+        """Refill every gathered buffer from the shards (collective; used after loading a checkpoint)."""
+        for u in self.order:
+            all_gather_into(self.gathered[u], self.shards[u], group=self.group)
+            self.fresh[u] = True
+
 
 class FSDPOptimizer:
-    """AdamW over the local shards; the global gradient norm is an all-reduce of shard sums."""
+    """AdamW over the local shards; the global gradient norm is an all-reduce of shard sums.
+
+    With peer-memory communication the AdamW kernel also performs the
+    parameter all-gather (``adamw_push``) and one bounded device-side wait
+    (``peer_wait``) publishes the new parameters before the next forward.
+    """
 
     def __init__(self, params: FSDPParams, cfg: AdamWConfig):
         self.params = params
@@ -145,11 +261,26 @@ class FSDPOptimizer:
         norm = sq.sqrt()
         scale = torch.clamp(c.max_grad_norm / (norm + 1e-12), max=1.0) if c.max_grad_norm and c.max_grad_norm > 0 \
             else torch.ones_like(norm)
-        for u in self.units:
-            ops.adamw_(self.master[u], p.grad_shards[u], self.m[u], self.v[u], lr=c.lr, beta1=c.beta1, beta2=c.beta2,
-                       eps=c.eps, weight_decay=c.weight_decay, step=step, grad_scale=scale, p_half=p.shards[u])
-            p.grad_shards[u].zero_()
-        p.invalidate()
+        if p.comm == "p2p":
+            W = p.world
+            for u in self.units:
+                n = p.padded[u] // W
+                grid = ext().adamw_push(self.master[u], p.grad_shards[u], self.m[u], self.v[u], p.sym_param.ptrs,
+                                            p.p_off[u] + p.rank * n * 2, scale, c.lr, c.beta1, c.beta2, c.eps,
+                                            c.weight_decay, step, p.sym_sig.ptrs, p.push_slot, p.rank)
+                p.push_target += int(grid)
+                p.shards[u].copy_(self.master[u])
+                p.grad_shards[u].zero_()
+            ext().peer_wait(p.sym_sig.local, p.push_slot, p.push_target, p.rank, W, p.sym_sig.dev_index)
+            for u in p.reduced:
+                p.reduced[u] = False
+        else:
+            for u in self.units:
+                ops.adamw_(self.master[u], p.grad_shards[u], self.m[u], self.v[u], lr=c.lr, beta1=c.beta1,
+                           beta2=c.beta2, eps=c.eps, weight_decay=c.weight_decay, step=step, grad_scale=scale,
+                           p_half=p.shards[u])
+                p.grad_shards[u].zero_()
+            p.invalidate()
         return {"grad_norm": norm[0], "grad_sq_sum": sq[0]}
 
     # ---------------------------------------------------------------- checkpointing (collectives)
@@ -194,6 +325,8 @@ class FSDPOptimizer:
             if nu is not None:
                 self.v[u].copy_(shard_of(nu[u]))
         p.invalidate()
+        if p.comm == "p2p":
+            p.regather()
 
 
 def build_fsdp_models(spec, adamw: AdamWConfig, *, seed: int = 0, device=None, group=None, dtype=torch.bfloat16,
