@@ -208,21 +208,60 @@ def bench_decode_step(t: Timer, eager_steps: int = 0):
     emit("decode_step_4b_B64_T390", ms, bytes_=weights + 36 * 2 * B * 8 * 390 * 128 * 2)
 
 
-def profile_small():
-    """One launch each of the decode-shaped kernels inside a profiler range (for a targeted ncu capture)."""
+def _profile_inputs(case: str):
+    """-> a zero-argument callable running one launch of the kernel(s) of ``case`` on a small input."""
     H, D = 2560, 128
-    x, w = _r(64, H), _r(6144, H, scale=0.02)
-    kc, vc = _r(64, 8, 448, D), _r(64, 8, 448, D)
-    q = _r(64, 32, D)
-    lens = torch.full((64,), 390, dtype=torch.int32, device="cuda")
-    ops.gemm(x, w)
-    ops.decode_attn(q, kc, vc, lens)
+    if case == "decode":        # skinny stream-K GEMM + decode attention (B=64, cache 390)
+        x, w = _r(64, H), _r(6144, H, scale=0.02)
+        kc, vc = _r(64, 8, 448, D), _r(64, 8, 448, D)
+        q = _r(64, 32, D)
+        lens = torch.full((64,), 390, dtype=torch.int32, device="cuda")
+        return lambda: (ops.gemm(x, w), ops.decode_attn(q, kc, vc, lens))
+    if case == "gemm":          # training-shaped GEMM, 8192 x 6144 x 2560 (173 MB of operands > L2)
+        a, b = _r(8192, H), _r(6144, H, scale=0.02)
+        return lambda: ops.gemm(a, b)
+    if case == "attn":          # varlen causal flash attention fwd + bwd, 16 x 388 tokens, 32/8 heads
+        L, n = 388, 16
+        T = L * n
+        cu = torch.arange(0, T + 1, L, dtype=torch.int32, device="cuda")
+        q, k, v = _r(T, 32, D), _r(T, 8, D), _r(T, 8, D)
+        do = _r(T, 32, D)
+
+        def run():
+            o, lse = ops.flash_attn(q, k, v, cu, L, causal=True)
+            ops.flash_attn_bwd(do, q, k, v, o, lse, cu, L, causal=True)
+        return run
+    if case == "vocab":         # fused lm_head log-prob fwd + bwd, 2048 rows x 151936 vocab
+        V = 151936
+        h, w = _r(2048, H), _r(V, H, scale=0.02)
+        tgt = torch.randint(0, V, (2048,), device="cuda")
+        g = torch.randn(2048, device="cuda")
+        dw = torch.zeros(V, H, dtype=torch.float32, device="cuda")
+
+        def run():
+            lp, ent, lse = ops.vocab_logprob(h, w, tgt)
+            ops.vocab_logprob_bwd(h, w, tgt, lse, ent, g, g, dw)
+        return run
+    if case == "adamw":         # one 100M-parameter shard
+        n = 100 * 2 ** 20
+        p, gg, m, v = (torch.randn(n, device="cuda") for _ in range(4))
+        v.abs_()
+        ph = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+        return lambda: ops.adamw_(p, gg, m, v, lr=1e-6, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01,
+                                  step=1, p_half=ph)
+    raise KeyError(case)
+
+
+def profile_small(case: str = "decode"):
+    """One warm launch, then one launch inside a profiler range (for a targeted ncu capture)."""
+    run = _profile_inputs(case)
+    run()
     torch.cuda.synchronize()
     torch.cuda.cudart().cudaProfilerStart()
-    ops.gemm(x, w)
-    ops.decode_attn(q, kc, vc, lens)
+    run()
     torch.cuda.synchronize()
     torch.cuda.cudart().cudaProfilerStop()
+    ops.check_errors()
 
 
 CASES = {"gemm": bench_gemm, "attn": bench_attn, "decode": bench_decode, "vocab": bench_vocab, "norm": bench_norm,
@@ -236,11 +275,11 @@ def main():
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--eager-steps", type=int, default=0,
                     help="decode_step only: run N eager steps without timing (for a profiler launch list)")
-    ap.add_argument("--profile-small", action="store_true",
-                    help="one launch of the skinny GEMM and of decode attention inside a profiler range")
+    ap.add_argument("--profile-small", default=None, choices=["decode", "gemm", "attn", "vocab", "adamw"],
+                    help="one launch of the named case's kernels inside a profiler range")
     args = ap.parse_args()
     if args.profile_small:
-        profile_small()
+        profile_small(args.profile_small)
         return
     if args.eager_steps:
         bench_decode_step(None, args.eager_steps)
