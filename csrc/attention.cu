@@ -105,11 +105,13 @@ template <int D, bool CAUSAL>
 __global__ void __launch_bounds__(128) flash_fwd_kernel(const bf16* __restrict__ Q, const bf16* __restrict__ K,
                                                         const bf16* __restrict__ V, const int* __restrict__ cu,
                                                         bf16* __restrict__ O, float* __restrict__ LSE, int Hq, int Hkv,
-                                                        int T, float scale_log2) {
+                                                        int T, float scale_log2, const int* __restrict__ pre) {
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int s0 = cu[b], L = cu[b + 1] - s0;
   const int q0 = qb * 64;
   if (q0 >= L) return;
+  // shared prefix: every query of this segment also sees keys [pstart, pstart + plen) (no causal mask)
+  const int pstart = pre ? pre[2 * b] : 0, plen = pre ? pre[2 * b + 1] : 0;
   const int hk = h / (Hq / Hkv);
   extern __shared__ __align__(128) uint8_t smem_bytes[];
   bf16* sQ = reinterpret_cast<bf16*>(smem_bytes);
@@ -121,10 +123,21 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(const bf16* __restrict__
   const bf16* Qs = Q + static_cast<int64_t>(s0) * Hq * D;
   const bf16* Ks = K + static_cast<int64_t>(s0) * Hkv * D;
   const bf16* Vs = V + static_cast<int64_t>(s0) * Hkv * D;
+  const bf16* Kp = K + static_cast<int64_t>(pstart) * Hkv * D;
+  const bf16* Vp = V + static_cast<int64_t>(pstart) * Hkv * D;
   load_rows<D>(sQ, Qs, q0, 64, L, Hq, h, tid, 128);
-  const int nkb = CAUSAL ? min((L + 63) / 64, qb + 1) : (L + 63) / 64;
-  load_rows<D>(sK, Ks, 0, 64, L, Hkv, hk, tid, 128);
-  load_rows<D>(sV, Vs, 0, 64, L, Hkv, hk, tid, 128);
+  const int nkp = (plen + 63) / 64;
+  const int nkb = nkp + (CAUSAL ? min((L + 63) / 64, qb + 1) : (L + 63) / 64);
+  auto load_kv = [&](int j, int buf) {
+    if (j < nkp) {
+      load_rows<D>(sK + buf * 64 * D, Kp, j * 64, 64, plen, Hkv, hk, tid, 128);
+      load_rows<D>(sV + buf * 64 * D, Vp, j * 64, 64, plen, Hkv, hk, tid, 128);
+    } else {
+      load_rows<D>(sK + buf * 64 * D, Ks, (j - nkp) * 64, 64, L, Hkv, hk, tid, 128);
+      load_rows<D>(sV + buf * 64 * D, Vs, (j - nkp) * 64, 64, L, Hkv, hk, tid, 128);
+    }
+  };
+  load_kv(0, 0);
   cp_async_commit();
 
   float acc[D / 8][4];
@@ -136,14 +149,16 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(const bf16* __restrict__
   for (int j = 0; j < nkb; ++j) {
     const int buf = j & 1;
     if (j + 1 < nkb) {
-      load_rows<D>(sK + (buf ^ 1) * 64 * D, Ks, (j + 1) * 64, 64, L, Hkv, hk, tid, 128);
-      load_rows<D>(sV + (buf ^ 1) * 64 * D, Vs, (j + 1) * 64, 64, L, Hkv, hk, tid, 128);
+      load_kv(j + 1, buf ^ 1);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
+    const bool in_pre = j < nkp;
+    const int kbase = in_pre ? j * 64 : (j - nkp) * 64;
+    const int klim = in_pre ? plen : L;
     const bf16* k_t = sK + buf * 64 * D;
     const bf16* v_t = sV + buf * 64 * D;
     float s[8][4];
@@ -167,9 +182,9 @@ __global__ void __launch_bounds__(128) flash_fwd_kernel(const bf16* __restrict__
     for (int nb = 0; nb < 8; ++nb) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int key = j * 64 + nb * 8 + 2 * tq + e;
-        const bool bad0 = key >= L || (CAUSAL && key > row0);
-        const bool bad1 = key >= L || (CAUSAL && key > row1);
+        const int key = kbase + nb * 8 + 2 * tq + e;
+        const bool bad0 = key >= klim || (CAUSAL && !in_pre && key > row0);
+        const bool bad1 = key >= klim || (CAUSAL && !in_pre && key > row1);
         s[nb][e] = bad0 ? -INFINITY : s[nb][e] * scale_log2;
         s[nb][2 + e] = bad1 ? -INFINITY : s[nb][2 + e] * scale_log2;
         mx0 = fmaxf(mx0, s[nb][e]);
@@ -265,12 +280,14 @@ template <int D, bool CAUSAL>
 __global__ void __launch_bounds__(128) flash_bwd_dkdv_kernel(
     const bf16* __restrict__ Q, const bf16* __restrict__ K, const bf16* __restrict__ V, const bf16* __restrict__ dO,
     const float* __restrict__ LSE, const float* __restrict__ DELTA, const int* __restrict__ cu, bf16* __restrict__ dK,
-    bf16* __restrict__ dV, int Hq, int Hkv, int T, float scale_log2, float scale) {
+    bf16* __restrict__ dV, int Hq, int Hkv, int T, float scale_log2, float scale, const int* __restrict__ xq) {
   constexpr int QC = 32;
   const int kb = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
   const int s0 = cu[b], L = cu[b + 1] - s0;
   const int k0 = kb * 64;
   if (k0 >= L) return;
+  // queries [xs, xs + xlen) outside this segment see all of its keys (segments sharing it as a prefix)
+  const int xs = xq ? xq[2 * b] : 0, xlen = xq ? xq[2 * b + 1] - xq[2 * b] : 0;
   const int rep = Hq / Hkv;
   extern __shared__ __align__(128) uint8_t smem_bytes[];
   bf16* sK = reinterpret_cast<bf16*>(smem_bytes);
@@ -297,17 +314,24 @@ __global__ void __launch_bounds__(128) flash_bwd_dkdv_kernel(
 
   const int qc_start = CAUSAL ? k0 / QC : 0;
   const int qc_end = (L + QC - 1) / QC;
-  const int n_chunks = qc_end - qc_start;
+  const int n_own = qc_end - qc_start;
+  const int n_chunks = n_own + (xlen + QC - 1) / QC;
   const int total = rep * n_chunks;
+  const bf16* Qx = Q + static_cast<int64_t>(xs) * Hq * D;
+  const bf16* dOx = dO + static_cast<int64_t>(xs) * Hq * D;
   auto issue = [&](int it, int buf) {
     const int hh = hk * rep + it / n_chunks;
-    const int qs = (qc_start + it % n_chunks) * QC;
-    load_rows<D>(sQ + buf * QC * D, Qs, qs, QC, L, Hq, hh, tid, 128);
-    load_rows<D>(sdO + buf * QC * D, dOs, qs, QC, L, Hq, hh, tid, 128);
+    const int c = it % n_chunks;
+    const bool own = c < n_own;
+    const int qs = own ? (qc_start + c) * QC : (c - n_own) * QC;
+    const int qlim = own ? L : xlen;
+    const int abs0 = own ? s0 : xs;
+    load_rows<D>(sQ + buf * QC * D, own ? Qs : Qx, qs, QC, qlim, Hq, hh, tid, 128);
+    load_rows<D>(sdO + buf * QC * D, own ? dOs : dOx, qs, QC, qlim, Hq, hh, tid, 128);
     for (int i = tid; i < QC; i += 128) {
-      const bool ok = qs + i < L;
-      sL[buf * QC + i] = ok ? LSE[static_cast<int64_t>(hh) * T + s0 + qs + i] * kLog2e : INFINITY;
-      sDl[buf * QC + i] = ok ? DELTA[static_cast<int64_t>(hh) * T + s0 + qs + i] : 0.f;
+      const bool ok = qs + i < qlim;
+      sL[buf * QC + i] = ok ? LSE[static_cast<int64_t>(hh) * T + abs0 + qs + i] * kLog2e : INFINITY;
+      sDl[buf * QC + i] = ok ? DELTA[static_cast<int64_t>(hh) * T + abs0 + qs + i] : 0.f;
     }
   };
   if (total > 0) issue(0, 0);
@@ -325,7 +349,10 @@ __global__ void __launch_bounds__(128) flash_bwd_dkdv_kernel(
       cp_async_wait<0>();
     }
     __syncthreads();
-    const int qs = (qc_start + it % n_chunks) * QC;
+    const int c = it % n_chunks;
+    const bool own = c < n_own;
+    const int qs = own ? (qc_start + c) * QC : (c - n_own) * QC;
+    const int qlim = own ? L : xlen;
     const bf16* q_t = sQ + buf * QC * D;
     const bf16* do_t = sdO + buf * QC * D;
     const float* lt = sL + buf * QC;
@@ -353,8 +380,8 @@ __global__ void __launch_bounds__(128) flash_bwd_dkdv_kernel(
       for (int e = 0; e < 2; ++e) {
         const int qi = nb * 8 + 2 * tq + e;
         const int qa = qs + qi;
-        const bool bad0 = qa >= L || key_r0 >= L || (CAUSAL && qa < key_r0);
-        const bool bad1 = qa >= L || key_r1 >= L || (CAUSAL && qa < key_r1);
+        const bool bad0 = qa >= qlim || key_r0 >= L || (CAUSAL && own && qa < key_r0);
+        const bool bad1 = qa >= qlim || key_r1 >= L || (CAUSAL && own && qa < key_r1);
         st[nb][e] = bad0 ? 0.f : exp2f(st[nb][e] * scale_log2 - lt[qi]);
         st[nb][2 + e] = bad1 ? 0.f : exp2f(st[nb][2 + e] * scale_log2 - lt[qi]);
       }
@@ -441,11 +468,12 @@ __global__ void __launch_bounds__(128) flash_bwd_dq_kernel(const bf16* __restric
                                                            const float* __restrict__ LSE,
                                                            const float* __restrict__ DELTA, const int* __restrict__ cu,
                                                            bf16* __restrict__ dQ, int Hq, int Hkv, int T,
-                                                           float scale_log2, float scale) {
+                                                           float scale_log2, float scale, const int* __restrict__ pre) {
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int s0 = cu[b], L = cu[b + 1] - s0;
   const int q0 = qb * 64;
   if (q0 >= L) return;
+  const int pstart = pre ? pre[2 * b] : 0, plen = pre ? pre[2 * b + 1] : 0;
   const int hk = h / (Hq / Hkv);
   extern __shared__ __align__(128) uint8_t smem_bytes[];
   bf16* sQ = reinterpret_cast<bf16*>(smem_bytes);
@@ -458,8 +486,19 @@ __global__ void __launch_bounds__(128) flash_bwd_dq_kernel(const bf16* __restric
   const bf16* Vs = V + static_cast<int64_t>(s0) * Hkv * D;
   load_rows<D>(sQ, Q + static_cast<int64_t>(s0) * Hq * D, q0, 64, L, Hq, h, tid, 128);
   load_rows<D>(sdO, dO + static_cast<int64_t>(s0) * Hq * D, q0, 64, L, Hq, h, tid, 128);
-  load_rows<D>(sK, Ks, 0, 64, L, Hkv, hk, tid, 128);
-  load_rows<D>(sV, Vs, 0, 64, L, Hkv, hk, tid, 128);
+  const bf16* Kp = K + static_cast<int64_t>(pstart) * Hkv * D;
+  const bf16* Vp = V + static_cast<int64_t>(pstart) * Hkv * D;
+  const int nkp = (plen + 63) / 64;
+  auto load_kv = [&](int j, int buf) {
+    if (j < nkp) {
+      load_rows<D>(sK + buf * 64 * D, Kp, j * 64, 64, plen, Hkv, hk, tid, 128);
+      load_rows<D>(sV + buf * 64 * D, Vp, j * 64, 64, plen, Hkv, hk, tid, 128);
+    } else {
+      load_rows<D>(sK + buf * 64 * D, Ks, (j - nkp) * 64, 64, L, Hkv, hk, tid, 128);
+      load_rows<D>(sV + buf * 64 * D, Vs, (j - nkp) * 64, 64, L, Hkv, hk, tid, 128);
+    }
+  };
+  load_kv(0, 0);
   cp_async_commit();
   const int row0 = q0 + warp * 16 + g, row1 = row0 + 8;
   const float lse0 = row0 < L ? LSE[static_cast<int64_t>(h) * T + s0 + row0] * kLog2e : INFINITY;
@@ -469,18 +508,20 @@ __global__ void __launch_bounds__(128) flash_bwd_dq_kernel(const bf16* __restric
   float dq[D / 8][4];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
-  const int nkb = CAUSAL ? min((L + 63) / 64, qb + 1) : (L + 63) / 64;
+  const int nkb = nkp + (CAUSAL ? min((L + 63) / 64, qb + 1) : (L + 63) / 64);
   for (int j = 0; j < nkb; ++j) {
     const int buf = j & 1;
     if (j + 1 < nkb) {
-      load_rows<D>(sK + (buf ^ 1) * 64 * D, Ks, (j + 1) * 64, 64, L, Hkv, hk, tid, 128);
-      load_rows<D>(sV + (buf ^ 1) * 64 * D, Vs, (j + 1) * 64, 64, L, Hkv, hk, tid, 128);
+      load_kv(j + 1, buf ^ 1);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
+    const bool in_pre = j < nkp;
+    const int kbase = in_pre ? j * 64 : (j - nkp) * 64;
+    const int klim = in_pre ? plen : L;
     const bf16* k_t = sK + buf * 64 * D;
     const bf16* v_t = sV + buf * 64 * D;
     float s[8][4], dp[8][4];
@@ -508,9 +549,9 @@ __global__ void __launch_bounds__(128) flash_bwd_dq_kernel(const bf16* __restric
     for (int nb = 0; nb < 8; ++nb) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int key = j * 64 + nb * 8 + 2 * tq + e;
-        const bool bad0 = key >= L || row0 >= L || (CAUSAL && key > row0);
-        const bool bad1 = key >= L || row1 >= L || (CAUSAL && key > row1);
+        const int key = kbase + nb * 8 + 2 * tq + e;
+        const bool bad0 = key >= klim || row0 >= L || (CAUSAL && !in_pre && key > row0);
+        const bool bad1 = key >= klim || row1 >= L || (CAUSAL && !in_pre && key > row1);
         const float p0 = bad0 ? 0.f : exp2f(s[nb][e] * scale_log2 - lse0);
         const float p1 = bad1 ? 0.f : exp2f(s[nb][2 + e] * scale_log2 - lse1);
         s[nb][e] = p0 * (dp[nb][e] - dl0);
@@ -958,7 +999,7 @@ static void set_smem(KernT k, int bytes) {
 
 template <int D>
 static void fwd_dispatch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
-                         at::Tensor& o, at::Tensor& lse, int max_seqlen, bool causal, float scale) {
+                         at::Tensor& o, at::Tensor& lse, int max_seqlen, bool causal, float scale, const int* pre) {
   const int B = static_cast<int>(cu.numel() - 1), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(k.size(1));
   const int T = static_cast<int>(q.size(0));
   const dim3 grid((max_seqlen + 63) / 64, Hq, B);
@@ -967,7 +1008,7 @@ static void fwd_dispatch(const at::Tensor& q, const at::Tensor& k, const at::Ten
   auto args = std::make_tuple(reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
                               reinterpret_cast<const bf16*>(v.data_ptr()), cu.data_ptr<int>(),
                               reinterpret_cast<bf16*>(o.data_ptr()), lse.data_ptr<float>(), Hq, Hkv, T,
-                              scale * kLog2e);
+                              scale * kLog2e, pre);
   if (causal) {
     auto kern = flash_fwd_kernel<D, true>;
     set_smem(kern, smem);
@@ -980,19 +1021,31 @@ static void fwd_dispatch(const at::Tensor& q, const at::Tensor& k, const at::Ten
   VLM_LAUNCHED();
 }
 
+static const int* seg_ptr(const c10::optional<at::Tensor>& t, const at::Tensor& cu, const char* what) {
+  if (!t.has_value() || !t->defined()) return nullptr;
+  TORCH_CHECK(t->scalar_type() == at::kInt && t->is_contiguous() && t->numel() == 2 * (cu.numel() - 1) &&
+                  t->device() == cu.device(),
+              "attn: ", what, " must be int32 [segments, 2] on the device of cu_seqlens");
+  return t->data_ptr<int>();
+}
+
+// pre[b] = (start, len): keys every query of segment b also attends to (a shared prefix).
 void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at::Tensor o, at::Tensor lse,
-                    int64_t max_seqlen, bool causal, double scale) {
+                    int64_t max_seqlen, bool causal, double scale, c10::optional<at::Tensor> pre) {
   TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous(), "attn: contiguous");
   TORCH_CHECK(cu.scalar_type() == at::kInt, "attn: cu_seqlens int32");
   TORCH_CHECK(q.size(1) % k.size(1) == 0, "attn: Hq must be a multiple of Hkv");
   if (q.size(0) == 0 || max_seqlen == 0) return;
   const c10::cuda::CUDAGuard g(q.device());
   const int D = static_cast<int>(q.size(2));
+  const int* pp = seg_ptr(pre, cu, "pre");
+  const int ms = static_cast<int>(max_seqlen);
+  const float sc = static_cast<float>(scale);
   switch (D) {
-    case 16: fwd_dispatch<16>(q, k, v, cu, o, lse, static_cast<int>(max_seqlen), causal, static_cast<float>(scale)); break;
-    case 32: fwd_dispatch<32>(q, k, v, cu, o, lse, static_cast<int>(max_seqlen), causal, static_cast<float>(scale)); break;
-    case 64: fwd_dispatch<64>(q, k, v, cu, o, lse, static_cast<int>(max_seqlen), causal, static_cast<float>(scale)); break;
-    case 128: fwd_dispatch<128>(q, k, v, cu, o, lse, static_cast<int>(max_seqlen), causal, static_cast<float>(scale)); break;
+    case 16: fwd_dispatch<16>(q, k, v, cu, o, lse, ms, causal, sc, pp); break;
+    case 32: fwd_dispatch<32>(q, k, v, cu, o, lse, ms, causal, sc, pp); break;
+    case 64: fwd_dispatch<64>(q, k, v, cu, o, lse, ms, causal, sc, pp); break;
+    case 128: fwd_dispatch<128>(q, k, v, cu, o, lse, ms, causal, sc, pp); break;
     default: TORCH_CHECK(false, "attn: unsupported head_dim ", D);
   }
 }
@@ -1000,7 +1053,8 @@ void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at:
 template <int D>
 static void bwd_dispatch(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                          const at::Tensor& lse, const at::Tensor& delta, const at::Tensor& cu, at::Tensor& dq,
-                         at::Tensor& dk, at::Tensor& dv, int max_seqlen, bool causal, float scale) {
+                         at::Tensor& dk, at::Tensor& dv, int max_seqlen, bool causal, float scale, const int* pre,
+                         const int* xq) {
   const int B = static_cast<int>(cu.numel() - 1), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(k.size(1));
   const int T = static_cast<int>(q.size(0));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
@@ -1014,7 +1068,7 @@ static void bwd_dispatch(const at::Tensor& dout, const at::Tensor& q, const at::
                                   reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
                                   lse.data_ptr<float>(), delta.data_ptr<float>(), cu.data_ptr<int>(),
                                   reinterpret_cast<bf16*>(dk.data_ptr()), reinterpret_cast<bf16*>(dv.data_ptr()), Hq, Hkv, T,
-                                  sl2, scale);
+                                  sl2, scale, xq);
     VLM_LAUNCHED();
   }
   {
@@ -1025,14 +1079,15 @@ static void bwd_dispatch(const at::Tensor& dout, const at::Tensor& q, const at::
     kern<<<grid, 128, smem, st>>>(reinterpret_cast<const bf16*>(q.data_ptr()), reinterpret_cast<const bf16*>(k.data_ptr()),
                                   reinterpret_cast<const bf16*>(v.data_ptr()), reinterpret_cast<const bf16*>(dout.data_ptr()),
                                   lse.data_ptr<float>(), delta.data_ptr<float>(), cu.data_ptr<int>(),
-                                  reinterpret_cast<bf16*>(dq.data_ptr()), Hq, Hkv, T, sl2, scale);
+                                  reinterpret_cast<bf16*>(dq.data_ptr()), Hq, Hkv, T, sl2, scale, pre);
     VLM_LAUNCHED();
   }
 }
 
+// xq[b] = (start, end): queries outside segment b that attend to all of its keys (the inverse of pre).
 void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
                     at::Tensor cu, at::Tensor dq, at::Tensor dk, at::Tensor dv, int64_t max_seqlen, bool causal,
-                    double scale) {
+                    double scale, c10::optional<at::Tensor> pre, c10::optional<at::Tensor> xq) {
   TORCH_CHECK(dout.is_contiguous() && q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && o.is_contiguous(),
               "attn bwd: contiguous");
   if (q.size(0) == 0 || max_seqlen == 0) return;
@@ -1046,11 +1101,14 @@ void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, a
   VLM_LAUNCHED();
   const int ms = static_cast<int>(max_seqlen);
   const float sc = static_cast<float>(scale);
+  const int* pp = seg_ptr(pre, cu, "pre");
+  const int* xp = seg_ptr(xq, cu, "xq");
+  TORCH_CHECK((pp == nullptr) == (xp == nullptr), "attn bwd: pass both pre and xq, or neither");
   switch (D) {
-    case 16: bwd_dispatch<16>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc); break;
-    case 32: bwd_dispatch<32>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc); break;
-    case 64: bwd_dispatch<64>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc); break;
-    case 128: bwd_dispatch<128>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc); break;
+    case 16: bwd_dispatch<16>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc, pp, xp); break;
+    case 32: bwd_dispatch<32>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc, pp, xp); break;
+    case 64: bwd_dispatch<64>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc, pp, xp); break;
+    case 128: bwd_dispatch<128>(dout, q, k, v, lse, delta, cu, dq, dk, dv, ms, causal, sc, pp, xp); break;
     default: TORCH_CHECK(false, "attn bwd: unsupported head_dim ", D);
   }
 }

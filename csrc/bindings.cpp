@@ -25,8 +25,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw", &vlm::adamw);
   m.def("sq_norm_acc", &vlm::sq_norm_acc);
   m.def("patchify", &vlm::patchify);
-  m.def("flash_attn_fwd", &vlm::flash_attn_fwd);
-  m.def("flash_attn_bwd", &vlm::flash_attn_bwd);
+  m.def("flash_attn_fwd", &vlm::flash_attn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("cu"), py::arg("o"),
+        py::arg("lse"), py::arg("max_seqlen"), py::arg("causal"), py::arg("scale"), py::arg("pre") = py::none());
+  m.def("flash_attn_bwd", &vlm::flash_attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
+        py::arg("lse"), py::arg("cu"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("max_seqlen"),
+        py::arg("causal"), py::arg("scale"), py::arg("pre") = py::none(), py::arg("xq") = py::none());
   m.def("decode_attn", &vlm::decode_attn);
   m.def("sample", &vlm::sample);
   m.def("vocab_logprob_fwd", &vlm::vocab_logprob_fwd);

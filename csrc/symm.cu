@@ -89,24 +89,41 @@ __global__ void __launch_bounds__(256) rs_pull_kernel(PeerTable bufs, int64_t sh
     ok = wait_peers(reinterpret_cast<const unsigned long long*>(sigs.p[rank]), slot, W, rank, epoch, err);
   __syncthreads();
   if (!ok) return;
+  // each thread keeps U float4 loads of one rank in flight (U * 16 B per thread; ~2.4 MB per GPU with one
+  // 256-thread CTA per SM, enough to cover NVLink latency), summing ranks in rank order
+  constexpr int U = 4;
   const int64_t n4 = n >> 2;
   float4* o4 = reinterpret_cast<float4*>(out);
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float4 acc = accumulate ? o4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-    float4 part[kMaxRanks];
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; base < n4; base += stride * U) {
+    float4 acc[U];
 #pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p)
-      if (p < W) part[p] = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(bufs.p[p]) + shard_off)[i];
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = base + u * stride;
+      acc[u] = (accumulate && i < n4) ? o4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll 1
+    for (int p = 0; p < W; ++p) {
+      const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(bufs.p[p]) + shard_off);
+      float4 x[U];
 #pragma unroll
-    for (int p = 0; p < kMaxRanks; ++p)
-      if (p < W) {
-        acc.x += part[p].x;
-        acc.y += part[p].y;
-        acc.z += part[p].z;
-        acc.w += part[p].w;
+      for (int u = 0; u < U; ++u) {
+        const int64_t i = base + u * stride;
+        x[u] = i < n4 ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-    o4[i] = acc;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        acc[u].x += x[u].x;
+        acc[u].y += x[u].y;
+        acc[u].z += x[u].z;
+        acc[u].w += x[u].w;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t i = base + u * stride;
+      if (i < n4) o4[i] = acc[u];
+    }
   }
 }
 
@@ -241,7 +258,7 @@ void rs_pull(std::vector<int64_t> bufs, int64_t unit_off_bytes, int64_t shard_of
   TORCH_CHECK((unit_off_bytes + shard_off * 4) % 16 == 0, "rs_pull: 16-byte aligned shards");
   const c10::cuda::CUDAGuard g(out.device());
   const int dev = out.device().index();
-  int grid = peer_grid(out.numel() / 4, dev);
+  int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((out.numel() / 4 + 1023) / 1024, num_sms(dev))));
   if (max_ctas > 0) grid = std::min<int>(grid, static_cast<int>(max_ctas));
   rs_pull_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       make_table(bufs, unit_off_bytes), shard_off, out.numel(), out.data_ptr<float>(), accumulate ? 1 : 0,

@@ -61,10 +61,10 @@ void patchify(at::Tensor images, at::Tensor ms, at::Tensor out, int64_t patch, i
 
 // attention.cu
 void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at::Tensor o, at::Tensor lse,
-                    int64_t max_seqlen, bool causal, double scale);
+                    int64_t max_seqlen, bool causal, double scale, c10::optional<at::Tensor> pre);
 void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
                     at::Tensor cu, at::Tensor dq, at::Tensor dk, at::Tensor dv, int64_t max_seqlen, bool causal,
-                    double scale);
+                    double scale, c10::optional<at::Tensor> pre, c10::optional<at::Tensor> xq);
 void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale);
 
 // sampler.cu

@@ -155,6 +155,42 @@ def test_flash_attn(D, Hq, Hkv, causal):
     _close(dv, dvr, name="dv")
 
 
+@pytest.mark.parametrize("D,Hq,Hkv", [(128, 32, 8), (64, 16, 16)])
+def test_flash_attn_shared_prefix(D, Hq, Hkv):
+    """Segments that attend to a shared prompt prefix (pack_groups layout): fwd + bwd vs the fp32 oracle."""
+    # two groups: prompt lengths 150 / 70, members of lengths (90, 1, 130) / (64, 65)
+    layout = [(150, [90, 1, 130]), (70, [64, 65])]
+    cu, pre, xq = [0], [], []
+    for P, members in layout:
+        p0 = cu[-1]
+        cu.append(p0 + P)
+        pre.append((0, 0))
+        slot = len(pre) - 1
+        first = cu[-1]
+        for n in members:
+            cu.append(cu[-1] + n)
+            pre.append((p0, P))
+            xq.append((0, 0))
+        xq.insert(slot, (first, cu[-1]))
+    T = cu[-1]
+    cu_t = torch.tensor(cu, dtype=torch.int32, device=DEV)
+    pre_t = torch.tensor(pre, dtype=torch.int32, device=DEV)
+    xq_t = torch.tensor(xq, dtype=torch.int32, device=DEV)
+    L = max(b - a for a, b in zip(cu, cu[1:]))
+    q, k, v = _r(T, Hq, D, seed=50), _r(T, Hkv, D, seed=51), _r(T, Hkv, D, seed=52)
+    scale = 1 / math.sqrt(D)
+    o, lse = ops.flash_attn(q, k, v, cu_t, L, causal=True, scale=scale, pre=pre_t)
+    orf, lser = ref.flash_attn(q, k, v, cu_t, L, causal=True, scale=scale, pre=pre_t)
+    _close(o, orf, name="o")
+    torch.testing.assert_close(lse, lser, atol=2e-3, rtol=2e-3)
+    do = _r(T, Hq, D, seed=53)
+    dq, dk, dv = ops.flash_attn_bwd(do, q, k, v, o, lse, cu_t, L, causal=True, scale=scale, pre=pre_t, xq=xq_t)
+    dqr, dkr, dvr = ref.flash_attn_bwd(do, q, k, v, orf, lser, cu_t, L, causal=True, scale=scale, pre=pre_t)
+    _close(dq, dqr, name="dq")
+    _close(dk, dkr, name="dk")
+    _close(dv, dvr, name="dv")
+
+
 def test_decode_attn_and_kv_write():
     B, Hq, Hkv, D, Tmax = 5, 32, 8, 128, 300
     kc = torch.zeros(B, Hkv, Tmax, D, device=DEV, dtype=torch.bfloat16)

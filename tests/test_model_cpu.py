@@ -94,3 +94,49 @@ def test_prefill_decode_matches_full_forward():
         lg = m.decode_step(tok, cache, torch.from_numpy(deltas))
         for b in range(2):
             torch.testing.assert_close(lg[b], full[b][plens[b] + t], atol=1e-4, rtol=1e-4)
+
+
+def test_shared_prompt_packing_matches_full_sequences():
+    """pack_groups (prompt once per group) gives the same log-probs and gradients as packing every member."""
+    from vlmrl.core.batching import pack_groups, pack_sequences
+    from vlmrl.utils.vlm import preprocess_image
+
+    spec, units, m = tiny_model(seed=9)
+    rng = np.random.default_rng(3)
+    prompts, actions, grids, pix = [], [], [], []
+    for g in range(2):
+        p, gr = preprocess_image(rng.integers(0, 256, (64, 64, 3), dtype=np.uint8), patch_size=16,
+                                 spatial_merge_size=2, temporal_patch_size=2)
+        pix.append(p)
+        grids.append([tuple(gr[0].tolist())])
+        prompt = [spec.vision_start_token_id] + [spec.image_token_id] * 4 + [spec.vision_end_token_id]
+        prompt += list(rng.integers(0, 900, 5 + g))
+        prompts.append(np.asarray(prompt))
+        actions.append([rng.integers(0, 900, n) for n in ((3, 1, 6) if g == 0 else (4, 2, 5))])
+    vis = m.encode_vision(torch.cat(pix), [gg[0] for gg in grids])
+    shared, c1 = pack_groups(spec, prompts, actions, grids, vis)
+    seqs, plens, sgrids, rows = [], [], [], []
+    for g, (p, acts) in enumerate(zip(prompts, actions)):
+        for a in acts:
+            seqs.append(np.concatenate([p, a]))
+            plens.append(len(p))
+            sgrids.append(grids[g])
+            rows.append(torch.arange(4 * g, 4 * g + 4))
+    full, c2 = pack_sequences(spec, seqs, plens, sgrids, vis.select(torch.cat(rows)))
+    assert list(c1) == list(c2)
+    assert shared.tokens.numel() < full.tokens.numel()
+    M = int(full.loss_rows.numel())
+    g_lp = torch.randn(M, generator=torch.Generator().manual_seed(1))
+    g_ent = torch.randn(M, generator=torch.Generator().manual_seed(2)) * 0.3
+    out = []
+    for batch in (shared, full):
+        m.params.zero_grads()
+        with torch.no_grad():
+            logp, ent, ctx = m.token_logprobs(batch, save=True)
+            m.backward(ctx, g_lp, g_ent)
+        out.append((logp.clone(), ent.clone(), {k: v.clone() for k, v in m.params.grads.items()}))
+    torch.testing.assert_close(out[0][0], out[1][0], atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(out[0][1], out[1][1], atol=1e-5, rtol=1e-5)
+    for name in out[1][2]:
+        torch.testing.assert_close(out[0][2][name], out[1][2][name], atol=2e-5, rtol=2e-4,
+                                   msg=lambda s: f"{name}: {s}")

@@ -58,3 +58,55 @@ def test_tiny_prefill_decode_gpu():
         vis = batch.vision.select(torch.arange(4 * b, 4 * b + 4, device="cuda"))
         full = m.forward_vlm(torch.tensor([seqs[b]]), vis, [(1, 4, 4)])[0]
         assert (step[b] - full[plens[b]]).abs().max().item() < 0.05
+
+
+@pytest.mark.gpu
+def test_shared_prompt_training_step_matches_full_on_gpu():
+    """bf16 CUDA path: log-probs and gradients of pack_groups agree with per-member packing."""
+    import numpy as np
+
+    from vlmrl.core.batching import pack_groups, pack_sequences
+    from vlmrl.models.qwen3vl.api import Qwen3VLModel
+    from vlmrl.models.qwen3vl.config import get_preset
+    from vlmrl.models.qwen3vl.params import init_params
+    from vlmrl.utils.vlm import preprocess_image
+
+    spec = get_preset("tiny")
+    units = init_params(spec, seed=2)
+    m = Qwen3VLModel(spec, units=units, dtype=torch.bfloat16, device="cuda")
+    rng = np.random.default_rng(5)
+    prompts, actions, grids, pix = [], [], [], []
+    for g in range(3):
+        p, gr = preprocess_image(rng.integers(0, 256, (64, 64, 3), dtype=np.uint8), patch_size=16,
+                                 spatial_merge_size=2, temporal_patch_size=2)
+        pix.append(p)
+        grids.append([tuple(gr[0].tolist())])
+        prompt = [spec.vision_start_token_id] + [spec.image_token_id] * 4 + [spec.vision_end_token_id]
+        prompt += list(rng.integers(0, 900, 70 + 5 * g))
+        prompts.append(np.asarray(prompt))
+        actions.append([rng.integers(0, 900, n) for n in (33, 1, 80, 64)])
+    vis = m.encode_vision(torch.cat(pix).cuda().to(torch.bfloat16), [gg[0] for gg in grids])
+    shared, c1 = pack_groups(spec, prompts, actions, grids, vis, device="cuda")
+    seqs, plens, sgrids, rows = [], [], [], []
+    for g, (p, acts) in enumerate(zip(prompts, actions)):
+        for a in acts:
+            seqs.append(np.concatenate([p, a]))
+            plens.append(len(p))
+            sgrids.append(grids[g])
+            rows.append(torch.arange(4 * g, 4 * g + 4))
+    full, c2 = pack_sequences(spec, seqs, plens, sgrids, vis.select(torch.cat(rows).cuda()), device="cuda")
+    M = int(full.loss_rows.numel())
+    g_lp = torch.randn(M, device="cuda")
+    g_ent = torch.randn(M, device="cuda") * 0.3
+    out = []
+    for batch in (shared, full):
+        m.params.zero_grads()
+        with torch.no_grad():
+            logp, ent, ctx = m.token_logprobs(batch, save=True)
+            m.backward(ctx, g_lp, g_ent)
+        out.append((logp.float().clone(), {k: v.clone() for k, v in m.params.grads.items()}))
+    torch.testing.assert_close(out[0][0], out[1][0], atol=3e-2, rtol=3e-2)
+    for name, gf in out[1][1].items():
+        gs = out[0][1][name]
+        rel = float((gs - gf).norm() / gf.norm().clamp_min(1e-12))
+        assert rel < 3e-2, (name, rel)

@@ -166,6 +166,74 @@ def pack_sequences(spec: Qwen3VLSpec, sequences: Sequence[np.ndarray], prompt_le
     return batch, np.asarray(counts)
 
 
+def pack_groups(spec: Qwen3VLSpec, prompts: Sequence[np.ndarray], actions: Sequence[Sequence[np.ndarray]],
+                grids_per_prompt: Sequence[Sequence[Tuple[int, int, int]]], vision: Optional[VisionEmbeddings],
+                *, device="cpu") -> Tuple[PackedBatch, np.ndarray]:
+    """Training batch where each prompt is computed once for all of its group's continuations.
+
+    Group g packs as one prompt segment followed by one segment per member
+    holding ``a_j[:-1]`` (the member's action tokens except the last).  Every
+    member segment attends to its group's prompt keys (``pre``) and causally to
+    itself; ``xq`` gives each prompt segment the query rows of its members (for
+    the backward).  Member j's first action token is scored from the prompt's
+    last row, the rest from its own rows, so the loss rows (and the per-member
+    counts) come out in the same (group, member) order as ``pack_sequences``
+    over the full sequences ``prompt + a_j``, with the same values: it is the
+    same causal computation with the shared prefix done once.  ``vision`` holds
+    the image tokens of each PROMPT once, in prompt order.
+    """
+    merge = spec.vision.spatial_merge_size if spec.vision is not None else 1
+    toks, poss, vis, loss, targ, counts = [], [], [], [], [], []
+    cu, pre, xq = [0], [], []
+    for p, acts, grids in zip(prompts, actions, grids_per_prompt):
+        p = np.asarray(p, dtype=np.int64)
+        P = len(p)
+        pos_p, delta = get_rope_index(p, grids, spatial_merge_size=merge, image_token_id=spec.image_token_id)
+        p0 = cu[-1]
+        toks.append(p)
+        poss.append(pos_p)
+        vis.append(p0 + np.nonzero(p == spec.image_token_id)[0])
+        cu.append(p0 + P)
+        pre.append((0, 0))
+        seg_of_prompt = len(pre) - 1
+        first_member = cu[-1]
+        for a in acts:
+            a = np.asarray(a, dtype=np.int64)
+            R = len(a)
+            counts.append(R)
+            if R == 0:
+                continue
+            # first action token: scored from the prompt's last row
+            rows = [p0 + P - 1]
+            tg = [a[0]]
+            if R > 1:
+                base = cu[-1]
+                inp = a[:-1]
+                toks.append(inp)
+                idx = P + np.arange(R - 1)
+                poss.append(np.broadcast_to(idx + delta, (3, R - 1)).astype(np.int64))
+                cu.append(base + R - 1)
+                pre.append((p0, P))
+                xq.append((0, 0))
+                rows += list(base + np.arange(R - 1))
+                tg += list(a[1:])
+            loss.append(np.asarray(rows, np.int64))
+            targ.append(np.asarray(tg, np.int64))
+        xq.insert(seg_of_prompt, (first_member, cu[-1]))
+    tokens = np.concatenate(toks)
+    pos = np.concatenate(poss, axis=1).astype(np.int64)
+    empty = np.zeros(0, np.int64)
+    t_tok, t_pos, t_cu, t_vis, t_loss, t_tgt, t_pre, t_xq = _to_device(
+        [tokens, pos, np.asarray(cu, np.int64), np.concatenate(vis) if vis else empty,
+         np.concatenate(loss) if loss else empty, np.concatenate(targ) if targ else empty,
+         np.asarray(pre, np.int64).reshape(-1, 2), np.asarray(xq, np.int64).reshape(-1, 2)], device)
+    max_len = int(max(np.diff(cu))) if len(cu) > 1 else 0
+    batch = PackedBatch(tokens=t_tok, pos=t_pos.to(torch.int32), cu_seqlens=t_cu.to(torch.int32), max_seqlen=max_len,
+                        vis_rows=t_vis, loss_rows=t_loss, targets=t_tgt, vision=vision,
+                        pre=t_pre.to(torch.int32), xq=t_xq.to(torch.int32))
+    return batch, np.asarray(counts)
+
+
 def pack_prompts(spec: Qwen3VLSpec, prompts: Sequence[np.ndarray], grids_per_seq, vision: Optional[VisionEmbeddings],
                  *, device="cpu") -> Tuple[PackedBatch, np.ndarray]:
     """Prefill batch: full prompts, no targets.  Returns (batch, rope deltas [B])."""
@@ -219,5 +287,5 @@ def pack_rows(spec: Qwen3VLSpec, tokens: torch.Tensor, attention_mask: Optional[
     return batch, valid
 
 
-__all__ = ["set_skip_deepstack", "pad_sequences", "pad_float_sequences", "pad_vision", "pad_grid", "build_masks",
+__all__ = ["pack_groups", "set_skip_deepstack", "pad_sequences", "pad_float_sequences", "pad_vision", "pad_grid", "build_masks",
            "pack_sequences", "pack_prompts", "pack_rows"]

@@ -23,7 +23,7 @@ from typing import Any, Dict, List, Optional, Sequence, Tuple
 import numpy as np
 import torch
 
-from vlmrl.core.batching import pack_sequences
+from vlmrl.core.batching import pack_groups, pack_sequences
 from vlmrl.core.grpo import group_advantages, ppo_loss, token_advantages
 from vlmrl.core.kl import AdaptiveKL
 from vlmrl.core.minibatch import minibatch_indices
@@ -55,6 +55,7 @@ class TrainerConfig:
     kl_ref_coef: float = 0.0
     adv_norm: str = "group"
     old_logprob_source: str = "policy"
+    share_prompt: bool = True
     vlm_min_pixels: int = -1
     vlm_max_pixels: int = -1
 
@@ -90,8 +91,23 @@ def _minibatch_count(cfg: TrainerConfig, n: int) -> int:
     return max(1, n // max(1, int(cfg.ppo_minibatch)))
 
 
+def _groups_of(idx: np.ndarray, eps, group_size: int):
+    """Split minibatch episode indices into whole groups (consecutive members), or None if they are not."""
+    if group_size <= 1 or len(idx) % group_size:
+        return None
+    out = []
+    for g in range(0, len(idx), group_size):
+        members = idx[g:g + group_size]
+        gid = eps[members[0]].group_id
+        if np.any(np.diff(members) != 1) or any(eps[i].group_id != gid for i in members):
+            return None
+        out.append(members)
+    return out
+
+
 def build_minibatches(model, eb: EpisodeBatch, adv_seq: torch.Tensor, n_minibatches: int,
-                      max_sequence_length: Optional[int] = None) -> List[MiniBatch]:
+                      max_sequence_length: Optional[int] = None, share_prompt: bool = True) -> List[MiniBatch]:
+    """Packed minibatches; with ``share_prompt`` each group's prompt is computed once (``pack_groups``)."""
     eps = eb.episodes
     merge = model.spec.vision.spatial_merge_size
     # vision rows per episode (episodes are stored contiguously in eb.vision)
@@ -100,13 +116,32 @@ def build_minibatches(model, eb: EpisodeBatch, adv_seq: torch.Tensor, n_minibatc
     out: List[MiniBatch] = []
     for idx in minibatch_indices(len(eps), n_minibatches, eb.group_size):
         sub = [eps[i] for i in idx]
-        rows = np.concatenate([np.arange(starts[i], starts[i + 1]) for i in idx])
-        vis = eb.vision.select(torch.from_numpy(rows).to(eb.vision.tokens.device)) if eb.vision is not None else None
-        seqs = [np.asarray(e.full_tokens, np.int64) for e in sub]
-        if max_sequence_length:
-            seqs = [s[:int(max_sequence_length)] for s in seqs]
-        batch, counts = pack_sequences(model.spec, seqs, [e.prompt_length for e in sub], [e.grids for e in sub], vis,
-                                       device=model.device)
+        groups = _groups_of(np.asarray(idx), eps, eb.group_size) if share_prompt else None
+        if groups is not None:
+            lead = [g[0] for g in groups]
+            rows = np.concatenate([np.arange(starts[i], starts[i + 1]) for i in lead])
+            vis = eb.vision.select(torch.from_numpy(rows).to(eb.vision.tokens.device)) \
+                if eb.vision is not None else None
+            acts = []
+            for g in groups:
+                ga = []
+                for i in g:
+                    a = np.asarray(eps[i].action_tokens, np.int64)
+                    if max_sequence_length:
+                        a = a[:max(0, int(max_sequence_length) - eps[i].prompt_length)]
+                    ga.append(a)
+                acts.append(ga)
+            batch, counts = pack_groups(model.spec, [np.asarray(eps[i].prompt_tokens, np.int64) for i in lead], acts,
+                                        [eps[i].grids for i in lead], vis, device=model.device)
+        else:
+            rows = np.concatenate([np.arange(starts[i], starts[i + 1]) for i in idx])
+            vis = eb.vision.select(torch.from_numpy(rows).to(eb.vision.tokens.device)) \
+                if eb.vision is not None else None
+            seqs = [np.asarray(e.full_tokens, np.int64) for e in sub]
+            if max_sequence_length:
+                seqs = [s[:int(max_sequence_length)] for s in seqs]
+            batch, counts = pack_sequences(model.spec, seqs, [e.prompt_length for e in sub], [e.grids for e in sub],
+                                           vis, device=model.device)
         samp = np.concatenate([np.asarray(e.action_logprobs[:c], np.float32) for e, c in zip(sub, counts)])
         out.append(MiniBatch(batch=batch, seq_index=idx, counts=counts,
                              adv_tok=token_advantages(adv_seq[torch.from_numpy(idx)], counts, model.device),
@@ -135,7 +170,8 @@ def collect(env, tokenizer, model, ts, cfg: TrainerConfig, batch_size: Optional[
         adv = (a / std if std > 1e-8 else a).float()
     else:
         adv = group_advantages(rewards, cfg.group_size, cfg.adv_norm).to(model.device)
-    mbs = build_minibatches(model, eb, adv, _minibatch_count(cfg, len(eb.episodes)), cfg.max_sequence_length)
+    mbs = build_minibatches(model, eb, adv, _minibatch_count(cfg, len(eb.episodes)), cfg.max_sequence_length,
+                            share_prompt=cfg.share_prompt)
     return CollectResult(episodes=eb, rewards=rewards, advantages=adv, minibatches=mbs)
 
 

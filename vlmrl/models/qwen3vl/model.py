@@ -69,7 +69,11 @@ class PackedBatch:
     ``tokens``/``targets`` [T] int64 (targets only where ``loss_rows`` points),
     ``pos`` [3, T] int32, ``cu_seqlens`` [B+1] int32, ``vis_rows`` [R] int64
     (rows of ``<|image_pad|>`` tokens, in order), ``loss_rows`` [M] int64 rows
-    whose next-token log-prob is scored.
+    whose next-token log-prob is scored (a row may repeat: with shared prompts
+    the prompt's last row scores every member's first action token).
+    ``pre``/``xq`` [segments, 2] int32 (optional): the shared-prefix key range
+    of each segment and, inversely, the query rows outside a segment that
+    attend to all of its keys (see ``vlmrl.core.batching.pack_groups``).
     """
     tokens: torch.Tensor
     pos: torch.Tensor
@@ -79,6 +83,8 @@ class PackedBatch:
     loss_rows: torch.Tensor
     targets: torch.Tensor
     vision: Optional[VisionEmbeddings] = None
+    pre: Optional[torch.Tensor] = None
+    xq: Optional[torch.Tensor] = None
 
 
 class KVCache:
@@ -202,7 +208,7 @@ class TextDecoder:
 
     # ---------------------------------------------------------------- layer fwd
     def layer_forward(self, w: Dict[str, torch.Tensor], x: torch.Tensor, pos: torch.Tensor, cu: torch.Tensor,
-                      max_seqlen: int, save: bool, kv_sink=None):
+                      max_seqlen: int, save: bool, kv_sink=None, pre=None):
         T = x.shape[0]
         xn, r1 = ops.rms_norm(x, w["input_norm"], self.eps)
         qkv = ops.linear(xn, w["qkv_w"], bias=w["qkv_b"], out_dtype=x.dtype)
@@ -210,7 +216,7 @@ class TextDecoder:
                                            n_q=self.nq, n_kv=self.nkv, eps=self.eps)
         if kv_sink is not None:
             kv_sink(k, v)
-        o, lse = ops.flash_attn(q, k, v, cu, max_seqlen, causal=True, scale=self.scale)
+        o, lse = ops.flash_attn(q, k, v, cu, max_seqlen, causal=True, scale=self.scale, pre=pre)
         h1 = ops.linear(o.reshape(T, self.nq * self.D), w["o_w"], residual=x, out_dtype=x.dtype)
         hn, r2 = ops.rms_norm(h1, w["post_norm"], self.eps)
         act, pre = ops.linear_swiglu(hn, w["gu_w"], save_pre=save)
@@ -219,7 +225,8 @@ class TextDecoder:
         return out, ctx
 
     # ---------------------------------------------------------------- layer bwd
-    def layer_backward(self, w, g, c: _LayerCtx, dy: torch.Tensor, pos, cu, max_seqlen) -> torch.Tensor:
+    def layer_backward(self, w, g, c: _LayerCtx, dy: torch.Tensor, pos, cu, max_seqlen, pre=None,
+                       xq=None) -> torch.Tensor:
         T = dy.shape[0]
         dt = dy.dtype
         # MLP
@@ -237,7 +244,8 @@ class TextDecoder:
         if g is not None:
             ops.grad_weight(d_h1, o2, accumulate=g["o_w"])
         d_o = ops.grad_input(d_h1, w["o_w"], out_dtype=dt).view(T, self.nq, self.D)
-        dq, dk, dv = ops.flash_attn_bwd(d_o, c.q, c.k, c.v, c.o, c.lse, cu, max_seqlen, causal=True, scale=self.scale)
+        dq, dk, dv = ops.flash_attn_bwd(d_o, c.q, c.k, c.v, c.o, c.lse, cu, max_seqlen, causal=True, scale=self.scale,
+                                        pre=pre, xq=xq)
         d_qkv = ops.qk_norm_rope_bwd(dq, dk, dv, c.qkv, w["q_norm"], w["k_norm"], pos, c.rq, c.rk, self.rope,
                                      n_q=self.nq, n_kv=self.nkv, eps=self.eps,
                                      dqw_accum=None if g is None else g["q_norm"],
@@ -256,7 +264,7 @@ class TextDecoder:
         for i in range(self.n_layers):
             w = self._w(params, f"layer{i}")
             sink = (lambda k, v, i=i: kv_writer(i, k, v)) if kv_writer is not None else None
-            h, lc = self.layer_forward(w, h, batch.pos, batch.cu_seqlens, batch.max_seqlen, save, sink)
+            h, lc = self.layer_forward(w, h, batch.pos, batch.cu_seqlens, batch.max_seqlen, save, sink, batch.pre)
             params.release(f"layer{i}")
             if ctx is not None:
                 ctx.layers.append(lc)
@@ -289,12 +297,17 @@ class TextDecoder:
         params.grad_done("head")
         params.release("head")
         T = b.tokens.shape[0]
-        dh = torch.zeros(T, self.H, dtype=d_hs.dtype, device=d_hs.device)
-        dh.index_copy_(0, b.loss_rows, d_hs)
+        if b.pre is not None:   # loss rows may repeat (shared prompt rows): sum their gradients in fp32
+            dh = torch.zeros(T, self.H, dtype=torch.float32, device=d_hs.device)
+            dh.index_add_(0, b.loss_rows, d_hs.float())
+            dh = dh.to(d_hs.dtype)
+        else:
+            dh = torch.zeros(T, self.H, dtype=d_hs.dtype, device=d_hs.device)
+            dh.index_copy_(0, b.loss_rows, d_hs)
         for i in reversed(range(self.n_layers)):
             w = self._w(params, f"layer{i}")
             g = self._g(params, f"layer{i}")
-            dh = self.layer_backward(w, g, ctx.layers[i], dh, b.pos, b.cu_seqlens, b.max_seqlen)
+            dh = self.layer_backward(w, g, ctx.layers[i], dh, b.pos, b.cu_seqlens, b.max_seqlen, b.pre, b.xq)
             ctx.layers[i] = None
             params.grad_done(f"layer{i}")
             params.release(f"layer{i}")

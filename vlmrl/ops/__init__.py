@@ -259,24 +259,29 @@ def vision_rope(qkv, rc, *, n_heads: int, head_dim: int):
 
 
 # ------------------------------------------------------------------ attention
-def flash_attn(q, k, v, cu_seqlens, max_seqlen: int, *, causal: bool, scale: Optional[float] = None):
+def flash_attn(q, k, v, cu_seqlens, max_seqlen: int, *, causal: bool, scale: Optional[float] = None, pre=None):
+    """Varlen GQA attention; ``pre`` (int32 [segments, 2]) adds a shared, unmasked key prefix per segment."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if not _cuda(q):
-        return ref.flash_attn(q, k, v, cu_seqlens, max_seqlen, causal=causal, scale=scale)
+        return ref.flash_attn(q, k, v, cu_seqlens, max_seqlen, causal=causal, scale=scale, pre=pre)
     o = torch.empty_like(q)
     lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=q.device)
-    ext().flash_attn_fwd(q, k, v, cu_seqlens, o, lse, int(max_seqlen), bool(causal), float(scale))
+    ext().flash_attn_fwd(q, k, v, cu_seqlens, o, lse, int(max_seqlen), bool(causal), float(scale), pre)
     return o, lse
 
 
-def flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen: int, *, causal: bool, scale: Optional[float] = None):
+def flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen: int, *, causal: bool, scale: Optional[float] = None,
+                   pre=None, xq=None):
+    """Backward of ``flash_attn``; with ``pre`` also ``xq`` [segments, 2]: the query rows outside each
+    segment that attend to all of its keys (the inverse map of ``pre``)."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if not _cuda(q):
-        return ref.flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen, causal=causal, scale=scale)
+        return ref.flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen, causal=causal, scale=scale, pre=pre)
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
-    ext().flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, dq, dk, dv, int(max_seqlen), bool(causal), float(scale))
+    ext().flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, dq, dk, dv, int(max_seqlen), bool(causal), float(scale),
+                         pre, xq)
     return dq, dk, dv
 
 

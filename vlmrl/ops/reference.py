@@ -178,26 +178,42 @@ def vision_rope(qkv: torch.Tensor, rc: torch.Tensor, *, n_heads: int, head_dim: 
 
 
 # ------------------------------------------------------------------ attention
-def flash_attn(q, k, v, cu_seqlens: torch.Tensor, max_seqlen: int, *, causal: bool, scale: float):
-    """Varlen GQA attention. Returns (o [T,Hq,D] in q.dtype, lse [Hq,T] fp32)."""
+def _seg_keys(k, v, s, e, pre, b, rep):
+    """Keys/values of segment b ([Hq, P + L, D]) and the prefix length P (shared-prefix segments)."""
+    ps, pl = (int(pre[b, 0]), int(pre[b, 1])) if pre is not None else (0, 0)
+    kk = torch.cat([k[ps:ps + pl], k[s:e]]).float().transpose(0, 1).repeat_interleave(rep, 0)
+    vv = torch.cat([v[ps:ps + pl], v[s:e]]).float().transpose(0, 1).repeat_interleave(rep, 0)
+    return kk, vv, ps, pl
+
+
+def _seg_mask(L: int, pl: int, causal: bool, device):
+    mask = torch.zeros(L, pl + L, dtype=torch.bool, device=device)
+    if causal:
+        mask[:, pl:] = torch.ones(L, L, dtype=torch.bool, device=device).triu(1)
+    return mask
+
+
+def flash_attn(q, k, v, cu_seqlens: torch.Tensor, max_seqlen: int, *, causal: bool, scale: float, pre=None):
+    """Varlen GQA attention. Returns (o [T,Hq,D] in q.dtype, lse [Hq,T] fp32).
+
+    ``pre[b] = (start, len)``: the queries of segment b also attend, without a causal mask, to the
+    keys of rows [start, start + len) (a prefix shared by several segments).
+    """
     T, Hq, D = q.shape
     Hkv = k.shape[1]
     rep = Hq // Hkv
     o = torch.empty(T, Hq, D, dtype=torch.float32, device=q.device)
     lse = torch.empty(Hq, T, dtype=torch.float32, device=q.device)
     cu = cu_seqlens.tolist()
+    pre = pre.cpu() if pre is not None else None
     for b in range(len(cu) - 1):
         s, e = cu[b], cu[b + 1]
         if e <= s:
             continue
         qb = q[s:e].float().transpose(0, 1)                        # [Hq, L, D]
-        kb = k[s:e].float().transpose(0, 1).repeat_interleave(rep, 0)
-        vb = v[s:e].float().transpose(0, 1).repeat_interleave(rep, 0)
+        kb, vb, _, pl = _seg_keys(k, v, s, e, pre, b, rep)
         sc = (qb @ kb.transpose(1, 2)) * scale
-        if causal:
-            L = e - s
-            mask = torch.ones(L, L, dtype=torch.bool, device=q.device).triu(1)
-            sc = sc.masked_fill(mask, float("-inf"))
+        sc = sc.masked_fill(_seg_mask(e - s, pl, causal, q.device), float("-inf"))
         l = torch.logsumexp(sc, dim=-1)
         p = torch.exp(sc - l[..., None])
         o[s:e] = (p @ vb).transpose(0, 1)
@@ -205,7 +221,7 @@ def flash_attn(q, k, v, cu_seqlens: torch.Tensor, max_seqlen: int, *, causal: bo
     return o.to(q.dtype), lse
 
 
-def flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen, *, causal: bool, scale: float):
+def flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen, *, causal: bool, scale: float, pre=None):
     T, Hq, D = q.shape
     Hkv = k.shape[1]
     rep = Hq // Hkv
@@ -213,20 +229,18 @@ def flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen, *, causal: bool,
     dk = torch.zeros(T, Hkv, D, dtype=torch.float32, device=q.device)
     dv = torch.zeros(T, Hkv, D, dtype=torch.float32, device=q.device)
     cu = cu_seqlens.tolist()
+    pre = pre.cpu() if pre is not None else None
     for b in range(len(cu) - 1):
         s, e = cu[b], cu[b + 1]
         if e <= s:
             continue
         L = e - s
         qb = q[s:e].float().transpose(0, 1)
-        kb = k[s:e].float().transpose(0, 1).repeat_interleave(rep, 0)
-        vb = v[s:e].float().transpose(0, 1).repeat_interleave(rep, 0)
+        kb, vb, ps, pl = _seg_keys(k, v, s, e, pre, b, rep)
         dob = do[s:e].float().transpose(0, 1)
         ob = o[s:e].float().transpose(0, 1)
         sc = (qb @ kb.transpose(1, 2)) * scale
-        if causal:
-            mask = torch.ones(L, L, dtype=torch.bool, device=q.device).triu(1)
-            sc = sc.masked_fill(mask, float("-inf"))
+        sc = sc.masked_fill(_seg_mask(L, pl, causal, q.device), float("-inf"))
         p = torch.exp(sc - lse[:, s:e, None])
         dvb = p.transpose(1, 2) @ dob
         dp = dob @ vb.transpose(1, 2)
@@ -235,8 +249,13 @@ def flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen, *, causal: bool,
         dqb = ds @ kb
         dkb = ds.transpose(1, 2) @ qb
         dq[s:e] = dqb.transpose(0, 1)
-        dk[s:e] = dkb.view(Hkv, rep, L, D).sum(1).transpose(0, 1)
-        dv[s:e] = dvb.view(Hkv, rep, L, D).sum(1).transpose(0, 1)
+        dkr = dkb.view(Hkv, rep, pl + L, D).sum(1).transpose(0, 1)
+        dvr = dvb.view(Hkv, rep, pl + L, D).sum(1).transpose(0, 1)
+        dk[s:e] += dkr[pl:]
+        dv[s:e] += dvr[pl:]
+        if pl:
+            dk[ps:ps + pl] += dkr[:pl]
+            dv[ps:ps + pl] += dvr[:pl]
     return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype)
 
 

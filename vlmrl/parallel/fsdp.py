@@ -193,7 +193,7 @@ class FSDPParams:
             self.comm_stream.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.comm_stream):
                 ext().rs_pull(self.sym_grad.ptrs, self.g_off[name], self.rank * n, self.grad_shards[name], True,
-                                  self.sym_sig.ptrs, i, self.rs_epoch[i], self.rank, 32)
+                                  self.sym_sig.ptrs, i, self.rs_epoch[i], self.rank, 0)
             return
         g = self.grads_full.pop(name, None)
         if g is None:
