@@ -53,11 +53,12 @@ __global__ void dec_qkv_kernel(const float* __restrict__ ws, SkMeta m, const bf1
   for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
 #pragma unroll
   for (int off = TPH / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  const float r = rsqrtf(ss / D + eps);
+  const bool norm = qw != nullptr;  // no q/k RMSNorm (Qwen2.5-style attention): rotate only
+  const float r = norm ? rsqrtf(ss / D + eps) : 1.f;
   const bf16* wt = is_q ? qw : kw;
   float xn[8], y[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) xn[i] = is_v ? x[i] : x[i] * r * bf2f(wt[t * 8 + i]);
+  for (int i = 0; i < 8; ++i) xn[i] = (is_v || !norm) ? x[i] : x[i] * r * bf2f(wt[t * 8 + i]);
 #pragma unroll
   for (int i = 0; i < 8; ++i) y[i] = __shfl_xor_sync(0xffffffffu, xn[i], TPH / 2);
   if (is_v) {
@@ -156,7 +157,8 @@ at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at
   auto args = [&](auto kern) {
     launch_pdl(kern, dim3(m.M), dim3(threads), 0, st, ws.data_ptr<float>(), m,
                bias.defined() && bias.numel() ? reinterpret_cast<const bf16*>(bias.data_ptr()) : nullptr,
-               reinterpret_cast<const bf16*>(qw.data_ptr()), reinterpret_cast<const bf16*>(kw.data_ptr()),
+               qw.defined() && qw.numel() ? reinterpret_cast<const bf16*>(qw.data_ptr()) : nullptr,
+               kw.defined() && kw.numel() ? reinterpret_cast<const bf16*>(kw.data_ptr()) : nullptr,
                lengths.data_ptr<int>(), delta.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),
                reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(kc.data_ptr()),
                reinterpret_cast<bf16*>(vc.data_ptr()), static_cast<int>(nq), static_cast<int>(nkv), Tmax,

@@ -238,12 +238,14 @@ __global__ void qk_norm_rope_fwd_kernel(const bf16* __restrict__ qkv, const bf16
     return;
   }
   const bool is_q = h < nq;
+  const bool norm = qw != nullptr;  // Qwen2.5-style attention has no q/k RMSNorm: rotate only
   float ss = 0.f;
-  for (int c = lane; c < D; c += 32) {
-    const float f = bf2f(src[c]);
-    ss += f * f;
-  }
-  const float r = rsqrtf(warp_sum(ss) / D + eps);
+  if (norm)
+    for (int c = lane; c < D; c += 32) {
+      const float f = bf2f(src[c]);
+      ss += f * f;
+    }
+  const float r = norm ? rsqrtf(warp_sum(ss) / D + eps) : 1.f;
   const bf16* wt = is_q ? qw : kw;
   bf16* dst = is_q ? q + (static_cast<int64_t>(t) * nq + h) * D : k + (static_cast<int64_t>(t) * nkv + (h - nq)) * D;
   if (lane == 0) {
@@ -254,8 +256,8 @@ __global__ void qk_norm_rope_fwd_kernel(const bf16* __restrict__ qkv, const bf16
   }
   const int half = D / 2;
   for (int j = lane; j < half; j += 32) {
-    const float x1 = bf2f(src[j]) * r * bf2f(wt[j]);
-    const float x2 = bf2f(src[j + half]) * r * bf2f(wt[j + half]);
+    const float x1 = bf2f(src[j]) * r * (norm ? bf2f(wt[j]) : 1.f);
+    const float x2 = bf2f(src[j + half]) * r * (norm ? bf2f(wt[j + half]) : 1.f);
     const float p = static_cast<float>(pos[ax[j] * pos_stride + t]);
     float s, c;
     sincosf(p * inv_freq[j], &s, &c);
@@ -279,6 +281,7 @@ __global__ void qk_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16*
   const int nh = nq + 2 * nkv;
   const int lane = threadIdx.x & 31;
   const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  bool return_early = false;
   if (gw < static_cast<int64_t>(T) * nh) {
     const int t = static_cast<int>(gw / nh), h = static_cast<int>(gw % nh);
     bf16* out = dqkv + (static_cast<int64_t>(t) * nh + h) * D;
@@ -290,9 +293,21 @@ __global__ void qk_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16*
       const bf16* g = is_q ? dq + (static_cast<int64_t>(t) * nq + h) * D : dk + (static_cast<int64_t>(t) * nkv + h - nq) * D;
       const bf16* x = qkv + (static_cast<int64_t>(t) * nh + h) * D;
       const bf16* wt = is_q ? qw : kw;
-      const float r = is_q ? rq[static_cast<int64_t>(t) * nq + h] : rk[static_cast<int64_t>(t) * nkv + h - nq];
-      float* swp = sw + (is_q ? 0 : D);
       const int half = D / 2;
+      if (wt == nullptr) {  // rotation only: the gradient is rotated back by the same angle
+        for (int j = lane; j < half; j += 32) {
+          const float p = static_cast<float>(pos[ax[j] * pos_stride + t]);
+          float s, c;
+          sincosf(p * inv_freq[j], &s, &c);
+          const float g1 = bf2f(g[j]), g2 = bf2f(g[j + half]);
+          out[j] = f2bf(g1 * c + g2 * s);
+          out[j + half] = f2bf(g2 * c - g1 * s);
+        }
+        return_early = true;
+      }
+      const float r = return_early ? 1.f : (is_q ? rq[static_cast<int64_t>(t) * nq + h] : rk[static_cast<int64_t>(t) * nkv + h - nq]);
+      float* swp = sw + (is_q ? 0 : D);
+      if (!return_early) {
       // pass 1: dot = mean(gw * xhat)
       float dot = 0.f;
       for (int j = lane; j < half; j += 32) {
@@ -317,6 +332,7 @@ __global__ void qk_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16*
         out[j] = f2bf(r * (n1 * bf2f(wt[j]) - xh1 * dot));
         out[j + half] = f2bf(r * (n2 * bf2f(wt[j + half]) - xh2 * dot));
       }
+      }
     }
   }
   __syncthreads();
@@ -324,6 +340,11 @@ __global__ void qk_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16*
     float* dst = i < D ? dqw : dkw;
     if (dst) atomicAdd(&dst[i % D], sw[i]);
   }
+}
+
+// Undefined or empty weight tensors select the rotation-only variant (no q/k RMSNorm).
+static const bf16* opt_bf16(const at::Tensor& t) {
+  return t.defined() && t.numel() ? reinterpret_cast<const bf16*>(t.data_ptr()) : nullptr;
 }
 
 void qk_norm_rope_fwd(at::Tensor qkv, at::Tensor qw, at::Tensor kw, at::Tensor pos, at::Tensor inv_freq, at::Tensor ax,
@@ -337,9 +358,8 @@ void qk_norm_rope_fwd(at::Tensor qkv, at::Tensor qw, at::Tensor kw, at::Tensor p
   const c10::cuda::CUDAGuard g(qkv.device());
   const int64_t warps = static_cast<int64_t>(T) * (nq + 2 * nkv);
   qk_norm_rope_fwd_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, cur_stream()>>>(
-      reinterpret_cast<const bf16*>(qkv.data_ptr()), reinterpret_cast<const bf16*>(qw.data_ptr()),
-      reinterpret_cast<const bf16*>(kw.data_ptr()), pos.data_ptr<int>(), pos.stride(0), inv_freq.data_ptr<float>(),
-      ax.data_ptr<int>(), reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(k.data_ptr()),
+      reinterpret_cast<const bf16*>(qkv.data_ptr()), opt_bf16(qw), opt_bf16(kw), pos.data_ptr<int>(), pos.stride(0),
+      inv_freq.data_ptr<float>(), ax.data_ptr<int>(), reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(k.data_ptr()),
       reinterpret_cast<bf16*>(v.data_ptr()), rq.data_ptr<float>(), rk.data_ptr<float>(), T, static_cast<int>(nq),
       static_cast<int>(nkv), D, static_cast<float>(eps));
   VLM_LAUNCHED();
@@ -356,8 +376,8 @@ void qk_norm_rope_bwd(at::Tensor dq, at::Tensor dk, at::Tensor dv, at::Tensor qk
   const int64_t warps = static_cast<int64_t>(T) * (nq + 2 * nkv);
   qk_norm_rope_bwd_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 2 * D * sizeof(float), cur_stream()>>>(
       reinterpret_cast<const bf16*>(dq.data_ptr()), reinterpret_cast<const bf16*>(dk.data_ptr()),
-      reinterpret_cast<const bf16*>(dv.data_ptr()), reinterpret_cast<const bf16*>(qkv.data_ptr()),
-      reinterpret_cast<const bf16*>(qw.data_ptr()), reinterpret_cast<const bf16*>(kw.data_ptr()), pos.data_ptr<int>(),
+      reinterpret_cast<const bf16*>(dv.data_ptr()), reinterpret_cast<const bf16*>(qkv.data_ptr()), opt_bf16(qw),
+      opt_bf16(kw), pos.data_ptr<int>(),
       pos.stride(0), inv_freq.data_ptr<float>(), ax.data_ptr<int>(), rq.data_ptr<float>(), rk.data_ptr<float>(),
       reinterpret_cast<bf16*>(dqkv.data_ptr()), dqw.defined() && dqw.numel() ? dqw.data_ptr<float>() : nullptr,
       dkw.defined() && dkw.numel() ? dkw.data_ptr<float>() : nullptr, T, static_cast<int>(nq), static_cast<int>(nkv), D);

@@ -2,6 +2,8 @@
 
 import math
 
+import numpy as np
+
 import pytest
 import torch
 
@@ -189,6 +191,18 @@ def test_flash_attn_shared_prefix(D, Hq, Hkv):
     _close(dq, dqr, name="dq")
     _close(dk, dkr, name="dk")
     _close(dv, dvr, name="dv")
+
+
+def test_flash_attn_unsupported_head_dim_pads():
+    """head_dim 80 (Qwen2.5 ViT) runs on the 128 kernel with zero padding."""
+    lens = [196, 64, 300]
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device=DEV)
+    T = int(cu[-1])
+    q, k, v = _r(T, 16, 80, seed=60), _r(T, 16, 80, seed=61), _r(T, 16, 80, seed=62)
+    o, lse = ops.flash_attn(q, k, v, cu, max(lens), causal=False)
+    orf, lser = ref.flash_attn(q, k, v, cu, max(lens), causal=False, scale=1 / math.sqrt(80))
+    _close(o, orf, name="o80")
+    torch.testing.assert_close(lse, lser, atol=2e-3, rtol=2e-3)
 
 
 def test_decode_attn_and_kv_write():

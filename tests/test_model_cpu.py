@@ -140,3 +140,56 @@ def test_shared_prompt_packing_matches_full_sequences():
     for name in out[1][2]:
         torch.testing.assert_close(out[0][2][name], out[1][2][name], atol=2e-5, rtol=2e-4,
                                    msg=lambda s: f"{name}: {s}")
+
+
+def test_qwen25_hf_parity_tiny():
+    """Qwen2.5-VL family (no q/k norm, chunked MRoPE, windowed RMSNorm/SwiGLU ViT) vs HF transformers."""
+    pytest.importorskip("transformers")
+    from transformers import Qwen2_5_VLConfig, Qwen2_5_VLForConditionalGeneration
+
+    from vlmrl.models.qwen25vl import get_rope_index, spec_to_config, units_to_hf_state_dict
+    from vlmrl.models.qwen3vl.config import get_preset
+    from vlmrl.models.qwen3vl.params import init_params
+    from vlmrl.utils.vlm import preprocess_image
+
+    spec = get_preset("tiny_qwen25")
+    units = init_params(spec, seed=4)
+    for name, u in units.items():   # non-trivial norms and biases
+        u.add_(torch.randn(u.shape, generator=torch.Generator().manual_seed(len(name))) * 0.02)
+    m = Qwen3VLModel(spec, units=units, dtype=torch.float32)
+    cfgd = spec_to_config(spec)
+    cfgd["text_config"]["max_position_embeddings"] = 4096
+    cfgd["tie_word_embeddings"] = cfgd["text_config"]["tie_word_embeddings"] = False  # lm_head was perturbed
+    cfg = Qwen2_5_VLConfig(**cfgd)
+    cfg._attn_implementation = "eager"
+    cfg.vision_config._attn_implementation = "eager"
+    cfg.text_config._attn_implementation = "eager"
+    hf = Qwen2_5_VLForConditionalGeneration(cfg).eval()
+    missing, unexpected = hf.load_state_dict(units_to_hf_state_dict(spec, units), strict=False)
+    assert not missing and not unexpected, (missing, unexpected)
+    rng = np.random.default_rng(0)
+    # 112 x 168 px -> grid (1, 8, 12): 2x3 windows of 56 px (window 4x4 patches), one partial
+    pix, grid = preprocess_image(rng.integers(0, 256, (112, 168, 3), dtype=np.uint8), patch_size=14,
+                                 spatial_merge_size=2, temporal_patch_size=2, min_pixels=56 * 56)
+    vis = m.encode_vision(pix, grid)
+    with torch.no_grad():
+        hv = hf.model.visual(pix, grid_thw=grid)
+    hv = getattr(hv, "pooler_output", hv)
+    torch.testing.assert_close(vis.tokens, hv, atol=2e-5, rtol=1e-4)
+    n_img = int(grid[0, 1] * grid[0, 2] // 4)
+    ids = [spec.vision_start_token_id] + [spec.image_token_id] * n_img + [spec.vision_end_token_id]
+    ids += list(rng.integers(0, 900, 9))
+    pos, _ = get_rope_index(ids, [tuple(grid[0].tolist())], spatial_merge_size=2, image_token_id=spec.image_token_id)
+    tok = torch.tensor([ids])
+    # image frames take temporal index 0 (reference models/qwen25vl/model.py:245,283-289), rows/cols follow
+    # the merged grid, text resumes at max + 1
+    img = slice(1, 1 + n_img)
+    assert (pos[0, img] == 1).all() and pos[1, img].max() == 1 + 3 and pos[2, img].max() == 1 + 5
+    assert pos[0, 1 + n_img] == 1 + 6
+    with torch.no_grad():
+        mm = (tok == spec.image_token_id).int()
+        # the network is compared under identical position ids
+        out = hf(input_ids=tok, pixel_values=pix, image_grid_thw=grid, mm_token_type_ids=mm,
+                 position_ids=torch.from_numpy(pos)[:, None, :])
+    logits = m.forward_vlm(tok, vis, grid)
+    torch.testing.assert_close(logits, out.logits, atol=2e-5, rtol=1e-4)

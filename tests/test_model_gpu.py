@@ -110,3 +110,36 @@ def test_shared_prompt_training_step_matches_full_on_gpu():
         gs = out[0][1][name]
         rel = float((gs - gf).norm() / gf.norm().clamp_min(1e-12))
         assert rel < 3e-2, (name, rel)
+
+
+def test_tiny_qwen25_gpu_vs_cpu():
+    """Qwen2.5-VL family on the CUDA path: windowed ViT, rotation-only q/k, chunked MRoPE, fused decode."""
+    from vlmrl.core.batching import pack_prompts
+    from vlmrl.models.qwen3vl.config import get_preset
+    from vlmrl.models.qwen3vl.params import init_params
+    from vlmrl.utils.vlm import preprocess_image
+
+    spec = get_preset("tiny_qwen25")
+    units = init_params(spec, seed=6)
+    m_cpu = Qwen3VLModel(spec, units=units, dtype=torch.float32)
+    m_gpu = Qwen3VLModel(spec, units=units, dtype=torch.bfloat16, device="cuda")
+    rng = np.random.default_rng(1)
+    pix, grid = preprocess_image(rng.integers(0, 256, (112, 168, 3), dtype=np.uint8), patch_size=14,
+                                 spatial_merge_size=2, temporal_patch_size=2, min_pixels=56 * 56)
+    vc = m_cpu.encode_vision(pix, grid)
+    vg = m_gpu.encode_vision(pix.cuda().to(torch.bfloat16), grid)
+    assert _rel(vg.tokens.cpu(), vc.tokens) < 0.03
+    n_img = int(grid[0, 1] * grid[0, 2] // 4)
+    ids = [spec.vision_start_token_id] + [spec.image_token_id] * n_img + [spec.vision_end_token_id]
+    ids += list(rng.integers(0, 900, 12))
+    g3 = [tuple(grid[0].tolist())]
+    lc = m_cpu.forward_vlm(torch.tensor([ids]), vc, g3)[0]
+    lg = m_gpu.forward_vlm(torch.tensor([ids]), vg, g3)[0]
+    assert _rel(lg.cpu(), lc) < 0.03
+    # prefill the first P tokens, then one fused decode step equals the full forward
+    P = len(ids) - 3
+    pb, deltas = pack_prompts(spec, [np.asarray(ids[:P])], [g3], vg, device="cuda")
+    cache = m_gpu.new_cache(1, 64)
+    m_gpu.prefill(pb, cache, torch.arange(1, device="cuda"))
+    step = m_gpu.decode_step(torch.tensor([ids[P]], device="cuda"), cache, torch.from_numpy(deltas).cuda())
+    assert (step[0].float() - lg[P].float()).abs().max().item() < 0.05

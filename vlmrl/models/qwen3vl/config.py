@@ -45,6 +45,8 @@ class TextBackboneSpec:
     vocab_size: int = 151936
     tie_word_embeddings: bool = True
     attention_bias: bool = False
+    # per-head RMSNorm on q and k before RoPE (Qwen3); Qwen2.5 rotates the raw projections
+    qk_norm: bool = True
 
 
 @dataclass
@@ -63,6 +65,7 @@ class VisionBackboneSpec:
     num_position_embeddings: Optional[int] = 2304
     deepstack_visual_indexes: Sequence[int] = ()
     hidden_act: str = "gelu_pytorch_tanh"
+    tokens_per_second: float = 2.0
 
     @property
     def patch_volume(self) -> int:
@@ -84,7 +87,9 @@ class Qwen3VLSpec:
     video_token_id: int = VIDEO_TOKEN_ID
     vision_start_token_id: int = VISION_START_TOKEN_ID
     vision_end_token_id: int = VISION_END_TOKEN_ID
-    # "hf": LayerNorm + GELU MLP ViT with learned pos-embed and full attention (HF Qwen3-VL).
+    # "hf": LayerNorm + GELU MLP ViT with learned pos-embed and full attention (HF Qwen3-VL);
+    # "qwen25": RMSNorm + SwiGLU ViT with window attention and full attention at fullatt_block_indexes
+    # (HF Qwen2.5-VL).
     vision_arch: str = "hf"
 
     def to_dict(self) -> Dict[str, Any]:
@@ -102,8 +107,9 @@ def spec_from_config(cfg: Dict[str, Any]) -> Qwen3VLSpec:
     vision_cfg = cfg.get("vision_config")
 
     scaling_type = rope_cfg.get("type", rope_cfg.get("rope_type")) if isinstance(rope_cfg, dict) else None
-    if scaling_type == "default":
+    if scaling_type in ("default", "mrope"):
         scaling_type = None
+    qwen25 = str(cfg.get("model_type", "")).startswith("qwen2_5_vl") or str(cfg.get("model_type", "")) == "qwen2_vl"
     scaling_factor = rope_cfg.get("factor", rope_cfg.get("finetuned_factor")) if isinstance(rope_cfg, dict) else None
     interleaved = bool(rope_cfg.get("mrope_interleaved", False)) if isinstance(rope_cfg, dict) else False
     section = rope_cfg.get("mrope_section") if isinstance(rope_cfg, dict) else None
@@ -127,7 +133,8 @@ def spec_from_config(cfg: Dict[str, Any]) -> Qwen3VLSpec:
         mrope_interleaved=interleaved, rms_norm_eps=float(text_cfg.get("rms_norm_eps", 1e-6)),
         vocab_size=int(text_cfg["vocab_size"]),
         tie_word_embeddings=bool(cfg.get("tie_word_embeddings", text_cfg.get("tie_word_embeddings", False))),
-        attention_bias=bool(text_cfg.get("attention_bias", False)),
+        attention_bias=bool(text_cfg.get("attention_bias", qwen25)),
+        qk_norm=not qwen25,
     )
     vision = None
     if vision_cfg is not None:
@@ -144,6 +151,7 @@ def spec_from_config(cfg: Dict[str, Any]) -> Qwen3VLSpec:
             fullatt_block_indexes=_int_list(vision_cfg.get("fullatt_block_indexes", deep)),
             num_position_embeddings=vision_cfg.get("num_position_embeddings"),
             deepstack_visual_indexes=deep, hidden_act=str(vision_cfg.get("hidden_act", "gelu_pytorch_tanh")),
+            tokens_per_second=float(vision_cfg.get("tokens_per_second", 2.0)),
         )
     return Qwen3VLSpec(
         text=text, vision=vision, pad_token_id=cfg.get("pad_token_id"), bos_token_id=cfg.get("bos_token_id"),
@@ -151,14 +159,17 @@ def spec_from_config(cfg: Dict[str, Any]) -> Qwen3VLSpec:
         video_token_id=int(cfg.get("video_token_id", VIDEO_TOKEN_ID)),
         vision_start_token_id=int(cfg.get("vision_start_token_id", VISION_START_TOKEN_ID)),
         vision_end_token_id=int(cfg.get("vision_end_token_id", VISION_END_TOKEN_ID)),
+        vision_arch="qwen25" if qwen25 else "hf",
     )
 
 
 def spec_to_config(spec: Qwen3VLSpec) -> Dict[str, Any]:
     """Inverse of ``spec_from_config``: an HF-style ``config.json`` dict."""
     t = spec.text
+    qwen25 = spec.vision_arch == "qwen25"
     cfg: Dict[str, Any] = {
-        "model_type": "qwen3_vl", "architectures": ["Qwen3VLForConditionalGeneration"],
+        "model_type": "qwen2_5_vl" if qwen25 else "qwen3_vl",
+        "architectures": ["Qwen2_5_VLForConditionalGeneration" if qwen25 else "Qwen3VLForConditionalGeneration"],
         "tie_word_embeddings": t.tie_word_embeddings,
         "image_token_id": spec.image_token_id, "video_token_id": spec.video_token_id,
         "vision_start_token_id": spec.vision_start_token_id, "vision_end_token_id": spec.vision_end_token_id,
@@ -184,6 +195,13 @@ def spec_to_config(spec: Qwen3VLSpec) -> Dict[str, Any]:
             "in_channels": v.in_channels, "num_position_embeddings": v.num_position_embeddings,
             "deepstack_visual_indexes": list(v.deepstack_visual_indexes), "hidden_act": v.hidden_act,
         }
+        if qwen25:
+            cfg["vision_config"].update(window_size=v.window_size, fullatt_block_indexes=list(v.fullatt_block_indexes),
+                                        tokens_per_second=int(v.tokens_per_second) if float(v.tokens_per_second).is_integer()
+                                        else v.tokens_per_second, in_chans=v.in_channels)
+            cfg["vision_config"].pop("num_position_embeddings")
+            cfg["vision_config"].pop("deepstack_visual_indexes")
+            cfg["text_config"]["rope_scaling"] = {"type": "mrope", "mrope_section": list(t.rope_section)}
     return cfg
 
 
@@ -192,6 +210,13 @@ def _vision_4b(out_hidden: int) -> VisionBackboneSpec:
                               intermediate_size=4096, patch_size=16, temporal_patch_size=2, spatial_merge_size=2,
                               num_position_embeddings=2304, deepstack_visual_indexes=(5, 11, 17),
                               fullatt_block_indexes=(5, 11, 17))
+
+
+def _qwen25_vision(out_hidden: int, depth: int = 32) -> VisionBackboneSpec:
+    return VisionBackboneSpec(hidden_size=1280, out_hidden_size=out_hidden, depth=depth, num_heads=16,
+                              intermediate_size=3420, patch_size=14, temporal_patch_size=2, spatial_merge_size=2,
+                              window_size=112, fullatt_block_indexes=(7, 15, 23, 31), num_position_embeddings=None,
+                              deepstack_visual_indexes=(), hidden_act="silu", tokens_per_second=2.0)
 
 
 PRESETS: Dict[str, Qwen3VLSpec] = {
@@ -217,6 +242,31 @@ PRESETS: Dict[str, Qwen3VLSpec] = {
                               head_dim=128, intermediate_size=12288, rope_theta=5e6, rope_section=(24, 20, 20),
                               mrope_interleaved=True, vocab_size=151936, tie_word_embeddings=False),
         vision=_vision_4b(4096), eos_token_id=151645, pad_token_id=151643,
+    ),
+    "tiny_qwen25": Qwen3VLSpec(
+        text=TextBackboneSpec(hidden_size=128, num_attention_heads=4, num_hidden_layers=2, num_key_value_heads=2,
+                              head_dim=32, intermediate_size=384, rope_theta=1e6, rope_section=(4, 6, 6),
+                              mrope_interleaved=False, vocab_size=1024, tie_word_embeddings=True,
+                              attention_bias=True, qk_norm=False),
+        vision=VisionBackboneSpec(hidden_size=64, out_hidden_size=128, depth=3, num_heads=4, intermediate_size=160,
+                                  patch_size=14, temporal_patch_size=2, spatial_merge_size=2, window_size=56,
+                                  fullatt_block_indexes=(1,), num_position_embeddings=None, hidden_act="silu"),
+        image_token_id=1024 - 2, video_token_id=1024 - 1, vision_start_token_id=1024 - 4,
+        vision_end_token_id=1024 - 3, eos_token_id=1024 - 5, pad_token_id=1024 - 7, vision_arch="qwen25",
+    ),
+    "qwen25vl_3b": Qwen3VLSpec(
+        text=TextBackboneSpec(hidden_size=2048, num_attention_heads=16, num_hidden_layers=36, num_key_value_heads=2,
+                              head_dim=128, intermediate_size=11008, rope_theta=1e6, rope_section=(16, 24, 24),
+                              mrope_interleaved=False, vocab_size=151936, tie_word_embeddings=True,
+                              attention_bias=True, qk_norm=False),
+        vision=_qwen25_vision(2048), eos_token_id=151645, pad_token_id=151643, vision_arch="qwen25",
+    ),
+    "qwen25vl_7b": Qwen3VLSpec(
+        text=TextBackboneSpec(hidden_size=3584, num_attention_heads=28, num_hidden_layers=28, num_key_value_heads=4,
+                              head_dim=128, intermediate_size=18944, rope_theta=1e6, rope_section=(16, 24, 24),
+                              mrope_interleaved=False, vocab_size=152064, tie_word_embeddings=False,
+                              attention_bias=True, qk_norm=False),
+        vision=_qwen25_vision(3584), eos_token_id=151645, pad_token_id=151643, vision_arch="qwen25",
     ),
 }
 

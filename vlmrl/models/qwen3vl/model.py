@@ -212,7 +212,7 @@ class TextDecoder:
         T = x.shape[0]
         xn, r1 = ops.rms_norm(x, w["input_norm"], self.eps)
         qkv = ops.linear(xn, w["qkv_w"], bias=w["qkv_b"], out_dtype=x.dtype)
-        q, k, v, rq, rk = ops.qk_norm_rope(qkv, w["q_norm"], w["k_norm"], pos, self.rope,
+        q, k, v, rq, rk = ops.qk_norm_rope(qkv, w.get("q_norm"), w.get("k_norm"), pos, self.rope,
                                            n_q=self.nq, n_kv=self.nkv, eps=self.eps)
         if kv_sink is not None:
             kv_sink(k, v)
@@ -246,10 +246,10 @@ class TextDecoder:
         d_o = ops.grad_input(d_h1, w["o_w"], out_dtype=dt).view(T, self.nq, self.D)
         dq, dk, dv = ops.flash_attn_bwd(d_o, c.q, c.k, c.v, c.o, c.lse, cu, max_seqlen, causal=True, scale=self.scale,
                                         pre=pre, xq=xq)
-        d_qkv = ops.qk_norm_rope_bwd(dq, dk, dv, c.qkv, w["q_norm"], w["k_norm"], pos, c.rq, c.rk, self.rope,
+        d_qkv = ops.qk_norm_rope_bwd(dq, dk, dv, c.qkv, w.get("q_norm"), w.get("k_norm"), pos, c.rq, c.rk, self.rope,
                                      n_q=self.nq, n_kv=self.nkv, eps=self.eps,
-                                     dqw_accum=None if g is None else g["q_norm"],
-                                     dkw_accum=None if g is None else g["k_norm"])
+                                     dqw_accum=None if g is None else g.get("q_norm"),
+                                     dkw_accum=None if g is None else g.get("k_norm"))
         if g is not None:
             ops.grad_weight(d_qkv, c.xn, accumulate=g["qkv_w"])
             g["qkv_b"].add_(d_qkv.float().sum(0))
@@ -367,7 +367,7 @@ class TextDecoder:
             w = self._w(params, f"layer{i}")
             xn, _ = ops.rms_norm(x, w["input_norm"], self.eps)
             qkv = ops.linear(xn, w["qkv_w"], bias=w["qkv_b"], out_dtype=x.dtype)
-            q, k, v, _, _ = ops.qk_norm_rope(qkv, w["q_norm"], w["k_norm"], pos, self.rope,
+            q, k, v, _, _ = ops.qk_norm_rope(qkv, w.get("q_norm"), w.get("k_norm"), pos, self.rope,
                                              n_q=self.nq, n_kv=self.nkv, eps=self.eps)
             ops.kv_write(k, v, cache.keys[i], cache.values[i], rows, cur)
             o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale)
@@ -388,7 +388,7 @@ class TextDecoder:
         for i in range(self.n_layers):
             w = self._w(params, f"layer{i}")
             ws, meta = ops.gemm_partials(xn, w["qkv_w"])
-            q = ops.dec_qkv(ws, meta, w["qkv_b"], w["q_norm"], w["k_norm"], lens, delta, self.rope,
+            q = ops.dec_qkv(ws, meta, w["qkv_b"], w.get("q_norm"), w.get("k_norm"), lens, delta, self.rope,
                             cache.keys[i], cache.values[i], n_q=self.nq, n_kv=self.nkv, eps=self.eps)
             o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale)
             ws, meta = ops.gemm_partials(o.reshape(B, self.nq * self.D), w["o_w"])

@@ -91,12 +91,12 @@ def text_layouts(spec: Qwen3VLSpec) -> List[UnitLayout]:
     qkv = (nq + 2 * nkv) * D
     units = [UnitLayout("embed", [ParamSpec("embed", (V, H))])]
     for i in range(t.num_hidden_layers):
+        norms = [ParamSpec("q_norm", (D,), "ones"), ParamSpec("k_norm", (D,), "ones")] if t.qk_norm else []
         units.append(UnitLayout(f"layer{i}", [
             ParamSpec("input_norm", (H,), "ones"),
             ParamSpec("qkv_w", (qkv, H)),
             ParamSpec("qkv_b", (qkv,), "zeros"),
-            ParamSpec("q_norm", (D,), "ones"),
-            ParamSpec("k_norm", (D,), "ones"),
+            *norms,
             ParamSpec("o_w", (H, nq * D)),
             ParamSpec("post_norm", (H,), "ones"),
             ParamSpec("gu_w", (2 * F, H)),
@@ -111,6 +111,21 @@ def vision_layout(spec: Qwen3VLSpec) -> Optional[UnitLayout]:
     if v is None:
         return None
     Hv, I, out, M = v.hidden_size, v.intermediate_size, v.out_hidden_size, v.merged_hidden_size
+    if spec.vision_arch == "qwen25":
+        # RMSNorm blocks with a biased SwiGLU MLP (gate/up rows interleaved), one RMSNorm merger
+        ps = [ParamSpec("patch_w", (Hv, v.patch_volume))]
+        for j in range(v.depth):
+            p = f"b{j}."
+            ps += [ParamSpec(p + "n1_w", (Hv,), "ones"),
+                   ParamSpec(p + "qkv_w", (3 * Hv, Hv)), ParamSpec(p + "qkv_b", (3 * Hv,), "zeros"),
+                   ParamSpec(p + "proj_w", (Hv, Hv)), ParamSpec(p + "proj_b", (Hv,), "zeros"),
+                   ParamSpec(p + "n2_w", (Hv,), "ones"),
+                   ParamSpec(p + "gu_w", (2 * I, Hv)), ParamSpec(p + "gu_b", (2 * I,), "zeros"),
+                   ParamSpec(p + "down_w", (Hv, I)), ParamSpec(p + "down_b", (Hv,), "zeros")]
+        ps += [ParamSpec("m.norm_w", (Hv,), "ones"),
+               ParamSpec("m.fc1_w", (M, M)), ParamSpec("m.fc1_b", (M,), "zeros"),
+               ParamSpec("m.fc2_w", (out, M)), ParamSpec("m.fc2_b", (out,), "zeros")]
+        return UnitLayout("visual", ps, trainable=False)
     ps = [ParamSpec("patch_w", (Hv, v.patch_volume)), ParamSpec("patch_b", (Hv,), "zeros")]
     if v.num_position_embeddings:
         ps.append(ParamSpec("pos_embed", (int(v.num_position_embeddings), Hv)))
@@ -217,54 +232,86 @@ def _merged_names(spec: Qwen3VLSpec):
         yield f"d{k}.", f"visual/deepstack_mergers_{k}"
 
 
-def units_to_flax(spec: Qwen3VLSpec, units: Dict[str, torch.Tensor]) -> Dict[str, Any]:
-    """Flat unit buffers -> nested dict of fp32 NumPy arrays with Flax names/[in,out] kernels."""
+def flax_leaves(spec: Qwen3VLSpec, views: Dict[str, Dict[str, torch.Tensor]]):
+    """Yield (Flax path, unit view, transposed) for every leaf of the checkpoint tree.
+
+    Dense kernels are stored ``[in, out]`` (transposed from the unit's ``[out, in]``
+    rows); the fused qkv / interleaved gate-up rows are split into the separate
+    q/k/v and gate/up leaves.  Both the Qwen3-VL tree and the Qwen2.5-VL tree
+    (no q/k norms; RMSNorm + SwiGLU ViT; ``merger/norm`` without bias) are covered.
+    """
     t = spec.text
     D, nq, nkv = t.head_dim, t.num_attention_heads, t.num_key_value_heads
-    tree: Dict[str, Any] = {}
-    lays = {l.name: l for l in all_layouts(spec)}
-    e = lays["embed"].views(units["embed"])
-    _set(tree, "embed/embedding", _np(e["embed"]))
+    q_rows, kv_rows = nq * D, nkv * D
+    yield "embed/embedding", views["embed"]["embed"], False
     for i in range(t.num_hidden_layers):
-        w = lays[f"layer{i}"].views(units[f"layer{i}"])
+        w = views[f"layer{i}"]
         p = f"layers_{i}"
-        q_rows, kv_rows = nq * D, nkv * D
-        qkv_w, qkv_b = w["qkv_w"], w["qkv_b"]
         for name, a, b in (("q_proj", 0, q_rows), ("k_proj", q_rows, q_rows + kv_rows),
                            ("v_proj", q_rows + kv_rows, q_rows + 2 * kv_rows)):
-            _set(tree, f"{p}/attn/{name}/kernel", _np(qkv_w[a:b].t()))
-            _set(tree, f"{p}/attn/{name}/bias", _np(qkv_b[a:b]))
-        _set(tree, f"{p}/attn/q_norm/weight", _np(w["q_norm"]))
-        _set(tree, f"{p}/attn/k_norm/weight", _np(w["k_norm"]))
-        _set(tree, f"{p}/attn/o_proj/kernel", _np(w["o_w"].t()))
-        _set(tree, f"{p}/mlp/gate_proj/kernel", _np(w["gu_w"][0::2].t()))
-        _set(tree, f"{p}/mlp/up_proj/kernel", _np(w["gu_w"][1::2].t()))
-        _set(tree, f"{p}/mlp/down_proj/kernel", _np(w["down_w"].t()))
-        _set(tree, f"{p}/input_norm/weight", _np(w["input_norm"]))
-        _set(tree, f"{p}/post_norm/weight", _np(w["post_norm"]))
-    h = lays["head"].views(units["head"])
-    _set(tree, "final_norm/weight", _np(h["final_norm"]))
-    _set(tree, "lm_head/kernel", _np(h["lm_head"].t()))
-    if spec.vision is not None and "visual" in units:
-        v = lays["visual"].views(units["visual"])
-        _set(tree, "visual/patch_embed/proj/kernel", _np(v["patch_w"].t()))
-        _set(tree, "visual/patch_embed/proj/bias", _np(v["patch_b"]))
-        if "pos_embed" in v:
-            _set(tree, "visual/pos_embed/embedding", _np(v["pos_embed"]))
+            yield f"{p}/attn/{name}/kernel", w["qkv_w"][a:b], True
+            yield f"{p}/attn/{name}/bias", w["qkv_b"][a:b], False
+        if "q_norm" in w:
+            yield f"{p}/attn/q_norm/weight", w["q_norm"], False
+            yield f"{p}/attn/k_norm/weight", w["k_norm"], False
+        yield f"{p}/attn/o_proj/kernel", w["o_w"], True
+        yield f"{p}/mlp/gate_proj/kernel", w["gu_w"][0::2], True
+        yield f"{p}/mlp/up_proj/kernel", w["gu_w"][1::2], True
+        yield f"{p}/mlp/down_proj/kernel", w["down_w"], True
+        yield f"{p}/input_norm/weight", w["input_norm"], False
+        yield f"{p}/post_norm/weight", w["post_norm"], False
+    yield "final_norm/weight", views["head"]["final_norm"], False
+    yield "lm_head/kernel", views["head"]["lm_head"], True
+    if spec.vision is None or "visual" not in views:
+        return
+    v = views["visual"]
+    yield "visual/patch_embed/proj/kernel", v["patch_w"], True
+    if spec.vision_arch == "qwen25":
         for j in range(spec.vision.depth):
             b, p = f"b{j}.", f"visual/blocks_{j}"
-            for src, dst in (("n1", "norm1"), ("n2", "norm2")):
-                _set(tree, f"{p}/{dst}/weight", _np(v[b + src + "_w"]))
-                _set(tree, f"{p}/{dst}/bias", _np(v[b + src + "_b"]))
-            for src, dst in (("qkv", "attn/qkv"), ("proj", "attn/proj"), ("fc1", "mlp/linear_fc1"), ("fc2", "mlp/linear_fc2")):
-                _set(tree, f"{p}/{dst}/kernel", _np(v[b + src + "_w"].t()))
-                _set(tree, f"{p}/{dst}/bias", _np(v[b + src + "_b"]))
-        for b, p in _merged_names(spec):
-            _set(tree, f"{p}/norm/weight", _np(v[b + "norm_w"]))
-            _set(tree, f"{p}/norm/bias", _np(v[b + "norm_b"]))
-            for src, dst in (("fc1", "linear1"), ("fc2", "linear2")):
-                _set(tree, f"{p}/{dst}/kernel", _np(v[b + src + "_w"].t()))
-                _set(tree, f"{p}/{dst}/bias", _np(v[b + src + "_b"]))
+            yield f"{p}/norm1/weight", v[b + "n1_w"], False
+            yield f"{p}/norm2/weight", v[b + "n2_w"], False
+            for src, dst in (("qkv", "attn/qkv"), ("proj", "attn/proj")):
+                yield f"{p}/{dst}/kernel", v[b + src + "_w"], True
+                yield f"{p}/{dst}/bias", v[b + src + "_b"], False
+            yield f"{p}/mlp/gate_proj/kernel", v[b + "gu_w"][0::2], True
+            yield f"{p}/mlp/gate_proj/bias", v[b + "gu_b"][0::2], False
+            yield f"{p}/mlp/up_proj/kernel", v[b + "gu_w"][1::2], True
+            yield f"{p}/mlp/up_proj/bias", v[b + "gu_b"][1::2], False
+            yield f"{p}/mlp/down_proj/kernel", v[b + "down_w"], True
+            yield f"{p}/mlp/down_proj/bias", v[b + "down_b"], False
+        yield "visual/merger/norm/weight", v["m.norm_w"], False
+        for src, dst in (("fc1", "linear1"), ("fc2", "linear2")):
+            yield f"visual/merger/{dst}/kernel", v["m." + src + "_w"], True
+            yield f"visual/merger/{dst}/bias", v["m." + src + "_b"], False
+        return
+    yield "visual/patch_embed/proj/bias", v["patch_b"], False
+    if "pos_embed" in v:
+        yield "visual/pos_embed/embedding", v["pos_embed"], False
+    for j in range(spec.vision.depth):
+        b, p = f"b{j}.", f"visual/blocks_{j}"
+        for src, dst in (("n1", "norm1"), ("n2", "norm2")):
+            yield f"{p}/{dst}/weight", v[b + src + "_w"], False
+            yield f"{p}/{dst}/bias", v[b + src + "_b"], False
+        for src, dst in (("qkv", "attn/qkv"), ("proj", "attn/proj"), ("fc1", "mlp/linear_fc1"),
+                         ("fc2", "mlp/linear_fc2")):
+            yield f"{p}/{dst}/kernel", v[b + src + "_w"], True
+            yield f"{p}/{dst}/bias", v[b + src + "_b"], False
+    for b, p in _merged_names(spec):
+        yield f"{p}/norm/weight", v[b + "norm_w"], False
+        yield f"{p}/norm/bias", v[b + "norm_b"], False
+        for src, dst in (("fc1", "linear1"), ("fc2", "linear2")):
+            yield f"{p}/{dst}/kernel", v[b + src + "_w"], True
+            yield f"{p}/{dst}/bias", v[b + src + "_b"], False
+
+
+def units_to_flax(spec: Qwen3VLSpec, units: Dict[str, torch.Tensor]) -> Dict[str, Any]:
+    """Flat unit buffers -> nested dict of fp32 NumPy arrays with Flax names/[in,out] kernels."""
+    lays = {l.name: l for l in all_layouts(spec)}
+    views = {n: lays[n].views(u) for n, u in units.items() if n in lays}
+    tree: Dict[str, Any] = {}
+    for path, view, tr in flax_leaves(spec, views):
+        _set(tree, path, _np(view.t() if tr else view))
     return tree
 
 
@@ -273,70 +320,21 @@ def flax_to_units(spec: Qwen3VLSpec, tree: Dict[str, Any], dtype=torch.float32, 
     """Nested Flax-named tree -> flat unit buffers.  Missing leaves keep their random init unless ``strict``."""
     units = init_params(spec, seed=0, dtype=dtype, device=device)
     lays = {l.name: l for l in all_layouts(spec)}
+    views = {n: lays[n].views(u) for n, u in units.items()}
     missing: List[str] = []
-
-    def fetch(path: str):
+    for path, view, tr in flax_leaves(spec, views):
         try:
-            return torch.as_tensor(np.asarray(_get(tree, path)), dtype=torch.float32)
+            val = torch.as_tensor(np.asarray(_get(tree, path)), dtype=torch.float32)
         except (KeyError, TypeError):
             missing.append(path)
-            return None
-
-    def put(view: torch.Tensor, path: str, transpose: bool = False):
-        val = fetch(path)
-        if val is None:
-            return
-        val = val.t() if transpose else val
+            continue
+        val = val.t() if tr else val
         if tuple(val.shape) != tuple(view.shape):
             raise ValueError(f"{path}: shape {tuple(val.shape)} != expected {tuple(view.shape)}")
         view.copy_(val.to(view.dtype))
-
-    t = spec.text
-    D, nq, nkv = t.head_dim, t.num_attention_heads, t.num_key_value_heads
-    put(lays["embed"].views(units["embed"])["embed"], "embed/embedding")
-    for i in range(t.num_hidden_layers):
-        w = lays[f"layer{i}"].views(units[f"layer{i}"])
-        p = f"layers_{i}"
-        q_rows, kv_rows = nq * D, nkv * D
-        for name, a, b in (("q_proj", 0, q_rows), ("k_proj", q_rows, q_rows + kv_rows),
-                           ("v_proj", q_rows + kv_rows, q_rows + 2 * kv_rows)):
-            put(w["qkv_w"][a:b], f"{p}/attn/{name}/kernel", True)
-            put(w["qkv_b"][a:b], f"{p}/attn/{name}/bias")
-        put(w["q_norm"], f"{p}/attn/q_norm/weight")
-        put(w["k_norm"], f"{p}/attn/k_norm/weight")
-        put(w["o_w"], f"{p}/attn/o_proj/kernel", True)
-        put(w["gu_w"][0::2], f"{p}/mlp/gate_proj/kernel", True)
-        put(w["gu_w"][1::2], f"{p}/mlp/up_proj/kernel", True)
-        put(w["down_w"], f"{p}/mlp/down_proj/kernel", True)
-        put(w["input_norm"], f"{p}/input_norm/weight")
-        put(w["post_norm"], f"{p}/post_norm/weight")
-    h = lays["head"].views(units["head"])
-    put(h["final_norm"], "final_norm/weight")
-    put(h["lm_head"], "lm_head/kernel", True)
-    if spec.vision is not None:
-        v = lays["visual"].views(units["visual"])
-        put(v["patch_w"], "visual/patch_embed/proj/kernel", True)
-        put(v["patch_b"], "visual/patch_embed/proj/bias")
-        if "pos_embed" in v:
-            put(v["pos_embed"], "visual/pos_embed/embedding")
-        for j in range(spec.vision.depth):
-            b, p = f"b{j}.", f"visual/blocks_{j}"
-            for src, dst in (("n1", "norm1"), ("n2", "norm2")):
-                put(v[b + src + "_w"], f"{p}/{dst}/weight")
-                put(v[b + src + "_b"], f"{p}/{dst}/bias")
-            for src, dst in (("qkv", "attn/qkv"), ("proj", "attn/proj"), ("fc1", "mlp/linear_fc1"), ("fc2", "mlp/linear_fc2")):
-                put(v[b + src + "_w"], f"{p}/{dst}/kernel", True)
-                put(v[b + src + "_b"], f"{p}/{dst}/bias")
-        for b, p in _merged_names(spec):
-            put(v[b + "norm_w"], f"{p}/norm/weight")
-            put(v[b + "norm_b"], f"{p}/norm/bias")
-            for src, dst in (("fc1", "linear1"), ("fc2", "linear2")):
-                put(v[b + src + "_w"], f"{p}/{dst}/kernel", True)
-                put(v[b + src + "_b"], f"{p}/{dst}/bias")
-    if strict and missing:
-        raise KeyError(f"checkpoint is missing {len(missing)} leaves, e.g. {missing[:5]}")
+    if missing and strict:
+        raise KeyError(f"{len(missing)} leaves missing from the params tree, e.g. {missing[:5]}")
     return units
-
 
 __all__ = ["ALIGN", "ParamSpec", "UnitLayout", "text_layouts", "vision_layout", "all_layouts", "init_unit_",
            "init_params", "unit_seed", "units_to_flax", "flax_to_units"]

@@ -35,7 +35,10 @@ def get_rope_index(
     spatial_merge_size: int,
     image_token_id: int,
     video_token_id: Optional[int] = None,
+    t_scale: Optional[Sequence[float]] = None,
 ) -> Tuple[np.ndarray, int]:
+    """``t_scale[g]`` multiplies grid g's frame index (Qwen2.5-VL video: seconds per grid x tokens per
+    second, truncated to an integer; images use 0); without it frame f takes index f."""
     ids = np.asarray(token_ids, dtype=np.int64).reshape(-1)
     n = ids.shape[0]
     pos = np.empty((3, n), dtype=np.int64)
@@ -63,10 +66,12 @@ def get_rope_index(
         if i + cnt > n or not is_vis[i:i + cnt].all():
             raise ValueError(f"image token run at {i} shorter than its grid ({cnt} tokens)")
         tt, hh, ww = np.meshgrid(np.arange(lt), np.arange(lh), np.arange(lw), indexing="ij")
+        if t_scale is not None:
+            tt = (tt.astype(np.float64) * float(t_scale[gi - 1])).astype(np.int64)
         pos[0, i:i + cnt] = cur + tt.reshape(-1)
         pos[1, i:i + cnt] = cur + hh.reshape(-1)
         pos[2, i:i + cnt] = cur + ww.reshape(-1)
-        cur += max(lt, lh, lw)
+        cur = int(pos[:, i:i + cnt].max()) + 1
         i += cnt
     delta = int(pos.max()) + 1 - n if n else 0
     return pos, delta

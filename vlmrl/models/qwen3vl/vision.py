@@ -15,12 +15,20 @@ RMSNorm/SwiGLU/windowed deviations are not reproduced):
 
 Every GEMM is ``vlmrl.ops.gemm`` (bias / GELU / residual fused in the epilogue)
 and attention is ``vlmrl.ops.flash_attn`` over per-image ``cu_seqlens``.
+
+``vision_arch == "qwen25"`` (HF Qwen2.5-VL, reference ``models/qwen25vl/vision.py``):
+patch embedding without bias and without a position table; the patches are
+permuted into attention windows of ``window_size`` pixels (merge units stay
+together); blocks are RMSNorm -> qkv -> 2-D rotary -> attention within each
+window (whole frame at ``fullatt_block_indexes``) -> proj, then RMSNorm ->
+biased SwiGLU MLP; one merger (RMSNorm -> 2x2 concat -> fc1 -> GELU -> fc2);
+the merged tokens are put back in raster order.
 """
 
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Dict, List, Sequence, Tuple
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
 import torch
@@ -39,6 +47,31 @@ class VisionInputs:
     pos_w: torch.Tensor        # [4, N] fp32 weights
     cu_seqlens: torch.Tensor   # [images+1] int32
     max_seqlen: int
+    # window attention (qwen25): patch order inside the tower, window cu_seqlens, merged-token inverse order
+    perm: Optional[torch.Tensor] = None
+    cu_window: Optional[torch.Tensor] = None
+    max_window: int = 0
+    unperm: Optional[torch.Tensor] = None
+
+
+def window_index(grids: Sequence[Tuple[int, int, int]], merge: int, window_size: int, patch_size: int):
+    """Merge units reordered window by window (row-major windows of ``window_size`` px per frame).
+
+    Returns (order of merge units [U], cu_seqlens over patches of the windows).
+    """
+    ws = max(1, window_size // merge // patch_size)
+    order, cu, off = [], [0], 0
+    for t, h, w in grids:
+        gh, gw = int(h) // merge, int(w) // merge
+        index = np.arange(int(t) * gh * gw).reshape(int(t), gh, gw)
+        for tt in range(int(t)):
+            for r0 in range(0, gh, ws):
+                for c0 in range(0, gw, ws):
+                    blk = index[tt, r0:r0 + ws, c0:c0 + ws].reshape(-1)
+                    order.append(blk + off)
+                    cu.append(cu[-1] + blk.size * merge * merge)
+        off += int(t) * gh * gw
+    return (np.concatenate(order) if order else np.zeros(0, np.int64)), np.asarray(cu, np.int64)
 
 
 def prepare_vision_inputs(spec: Qwen3VLSpec, grids: Sequence[Tuple[int, int, int]], device) -> VisionInputs:
@@ -56,7 +89,17 @@ def prepare_vision_inputs(spec: Qwen3VLSpec, grids: Sequence[Tuple[int, int, int
     for t, h, w in grids:
         seq += [int(h) * int(w)] * int(t)
     cu = torch.tensor(np.concatenate([[0], np.cumsum(seq)]).astype(np.int32), device=device)
-    return VisionInputs(rc=rc, pos_idx=pos_idx, pos_w=pos_w, cu_seqlens=cu, max_seqlen=max(seq) if seq else 0)
+    vin = VisionInputs(rc=rc, pos_idx=pos_idx, pos_w=pos_w, cu_seqlens=cu, max_seqlen=max(seq) if seq else 0)
+    if spec.vision_arch == "qwen25":
+        unit = v.spatial_merge_size ** 2
+        order, cuw = window_index(grids, v.spatial_merge_size, v.window_size, v.patch_size)
+        perm = (order[:, None] * unit + np.arange(unit)[None]).reshape(-1)
+        vin.perm = torch.from_numpy(perm).to(device)
+        vin.rc = vin.rc[vin.perm]
+        vin.cu_window = torch.from_numpy(cuw.astype(np.int32)).to(device)
+        vin.max_window = int(np.diff(cuw).max()) if len(cuw) > 1 else 0
+        vin.unperm = torch.from_numpy(np.argsort(order)).to(device)
+    return vin
 
 
 class VisionTower:
@@ -80,6 +123,8 @@ class VisionTower:
     @torch.no_grad()
     def forward(self, flat: torch.Tensor, pixel_rows: torch.Tensor, vin: VisionInputs):
         """pixel_rows [N, patch_volume] -> (merged [N/4, out], [deepstack_k [N/4, out]])."""
+        if self.spec.vision_arch == "qwen25":
+            return self._forward_windowed(flat, pixel_rows, vin), []
         v = self.v
         p = self.layout.views(flat)
         dt = flat.dtype
@@ -107,6 +152,32 @@ class VisionTower:
                 deep.append(self._merge(x, p, f"d{deep_idx.index(j)}.", post_norm=True))
         merged = self._merge(x, p, "m.", post_norm=False)
         return merged, deep
+
+    def _forward_windowed(self, flat: torch.Tensor, pixel_rows: torch.Tensor, vin: VisionInputs) -> torch.Tensor:
+        v = self.v
+        p = self.layout.views(flat)
+        dt = flat.dtype
+        H, nh = v.hidden_size, v.num_heads
+        hd = H // nh
+        x = ops.gemm(pixel_rows.to(dt), p["patch_w"], out_dtype=dt)
+        x = x.index_select(0, vin.perm)
+        full = set(int(i) for i in v.fullatt_block_indexes)
+        for j in range(v.depth):
+            b = f"b{j}."
+            cu, ms = (vin.cu_seqlens, vin.max_seqlen) if j in full else (vin.cu_window, vin.max_window)
+            xn, _ = ops.rms_norm(x, p[b + "n1_w"], 1e-6)
+            qkv = ops.gemm(xn, p[b + "qkv_w"], bias=p[b + "qkv_b"], out_dtype=dt)
+            q, k, vv = ops.vision_rope(qkv, vin.rc, n_heads=nh, head_dim=hd)
+            o, _ = ops.flash_attn(q, k, vv, cu, ms, causal=False)
+            x = ops.gemm(o.reshape(-1, H), p[b + "proj_w"], bias=p[b + "proj_b"], residual=x, out_dtype=dt)
+            xn, _ = ops.rms_norm(x, p[b + "n2_w"], 1e-6)
+            a = ops.gemm(xn, p[b + "gu_w"], bias=p[b + "gu_b"], epilogue=ops.EPI_SWIGLU, out_dtype=dt)
+            x = ops.gemm(a, p[b + "down_w"], bias=p[b + "down_b"], residual=x, out_dtype=dt)
+        M = v.merged_hidden_size
+        xn, _ = ops.rms_norm(x, p["m.norm_w"], 1e-6)
+        h = ops.gemm(xn.reshape(-1, M), p["m.fc1_w"], bias=p["m.fc1_b"], epilogue=ops.EPI_GELU_ERF, out_dtype=dt)
+        merged = ops.gemm(h, p["m.fc2_w"], bias=p["m.fc2_b"], out_dtype=dt)
+        return merged.index_select(0, vin.unperm)
 
 
 __all__ = ["VisionInputs", "prepare_vision_inputs", "VisionTower"]

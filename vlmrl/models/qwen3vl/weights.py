@@ -42,6 +42,30 @@ def _vision_key(key: str) -> Optional[str]:
     return key[i + len("visual."):] if i >= 0 else None
 
 
+def _put_qwen25_vision(v: Dict[str, torch.Tensor], vk: str, val: torch.Tensor, put) -> None:
+    """HF Qwen2.5-VL vision tensor names -> the qwen25 ``visual`` unit (gate/up rows interleaved)."""
+    m = re.match(r"blocks\.(\d+)\.(.+)\.(weight|bias)$", vk)
+    if m:
+        j, sub, kind = int(m.group(1)), m.group(2), m.group(3)
+        b = f"b{j}."
+        if sub in ("norm1", "norm2") and kind == "weight":
+            put(v[b + ("n1_w" if sub == "norm1" else "n2_w")], val)
+        elif sub in ("attn.qkv", "attn.proj"):
+            put(v[b + sub.split(".")[1] + ("_w" if kind == "weight" else "_b")], val)
+        elif sub in ("mlp.gate_proj", "mlp.up_proj"):
+            rows = slice(0, None, 2) if sub == "mlp.gate_proj" else slice(1, None, 2)
+            put(v[b + ("gu_w" if kind == "weight" else "gu_b")][rows], val)
+        elif sub == "mlp.down_proj":
+            put(v[b + ("down_w" if kind == "weight" else "down_b")], val)
+        return
+    m = re.match(r"merger\.(ln_q|mlp\.0|mlp\.2)\.(weight|bias)$", vk)
+    if m:
+        name = {"ln_q": "norm", "mlp.0": "fc1", "mlp.2": "fc2"}[m.group(1)]
+        if name == "norm" and m.group(2) == "bias":
+            return
+        put(v[f"m.{name}_{'w' if m.group(2) == 'weight' else 'b'}"], val)
+
+
 def hf_state_dict_to_units(spec: Qwen3VLSpec, sd: Dict[str, torch.Tensor], dtype=torch.float32,
                            device="cpu") -> Dict[str, torch.Tensor]:
     units = init_params(spec, seed=0, dtype=dtype, device=device)
@@ -68,6 +92,8 @@ def hf_state_dict_to_units(spec: Qwen3VLSpec, sd: Dict[str, torch.Tensor], dtype
                 put(v["patch_b"], val)
             elif vk == "pos_embed.weight":
                 put(v["pos_embed"], val)
+            elif spec.vision_arch == "qwen25":
+                _put_qwen25_vision(v, vk, val, put)
             else:
                 m = re.match(r"blocks\.(\d+)\.(.+)\.(weight|bias)$", vk)
                 if m:
@@ -141,9 +167,14 @@ def units_to_hf_state_dict(spec: Qwen3VLSpec, units: Dict[str, torch.Tensor]) ->
         sd[p + "self_attn.q_proj.weight"] = w["qkv_w"][:q_rows].clone()
         sd[p + "self_attn.k_proj.weight"] = w["qkv_w"][q_rows:q_rows + kv_rows].clone()
         sd[p + "self_attn.v_proj.weight"] = w["qkv_w"][q_rows + kv_rows:].clone()
+        if t.attention_bias:
+            sd[p + "self_attn.q_proj.bias"] = w["qkv_b"][:q_rows].clone()
+            sd[p + "self_attn.k_proj.bias"] = w["qkv_b"][q_rows:q_rows + kv_rows].clone()
+            sd[p + "self_attn.v_proj.bias"] = w["qkv_b"][q_rows + kv_rows:].clone()
         sd[p + "self_attn.o_proj.weight"] = w["o_w"].clone()
-        sd[p + "self_attn.q_norm.weight"] = w["q_norm"].clone()
-        sd[p + "self_attn.k_norm.weight"] = w["k_norm"].clone()
+        if "q_norm" in w:
+            sd[p + "self_attn.q_norm.weight"] = w["q_norm"].clone()
+            sd[p + "self_attn.k_norm.weight"] = w["k_norm"].clone()
         sd[p + "mlp.gate_proj.weight"] = w["gu_w"][0::2].clone()
         sd[p + "mlp.up_proj.weight"] = w["gu_w"][1::2].clone()
         sd[p + "mlp.down_proj.weight"] = w["down_w"].clone()
@@ -158,6 +189,24 @@ def units_to_hf_state_dict(spec: Qwen3VLSpec, units: Dict[str, torch.Tensor]) ->
         V = "model.visual."
         sd[V + "patch_embed.proj.weight"] = v["patch_w"].reshape(vs.hidden_size, vs.in_channels, vs.temporal_patch_size,
                                                                  vs.patch_size, vs.patch_size).clone()
+        if spec.vision_arch == "qwen25":
+            for j in range(vs.depth):
+                b, q = f"b{j}.", f"{V}blocks.{j}."
+                sd[q + "norm1.weight"] = v[b + "n1_w"].clone()
+                sd[q + "norm2.weight"] = v[b + "n2_w"].clone()
+                for src in ("qkv", "proj"):
+                    sd[q + f"attn.{src}.weight"] = v[b + src + "_w"].clone()
+                    sd[q + f"attn.{src}.bias"] = v[b + src + "_b"].clone()
+                for name, rows in (("gate_proj", slice(0, None, 2)), ("up_proj", slice(1, None, 2))):
+                    sd[q + f"mlp.{name}.weight"] = v[b + "gu_w"][rows].clone()
+                    sd[q + f"mlp.{name}.bias"] = v[b + "gu_b"][rows].clone()
+                sd[q + "mlp.down_proj.weight"] = v[b + "down_w"].clone()
+                sd[q + "mlp.down_proj.bias"] = v[b + "down_b"].clone()
+            sd[V + "merger.ln_q.weight"] = v["m.norm_w"].clone()
+            for src, dst in (("fc1", "mlp.0"), ("fc2", "mlp.2")):
+                sd[f"{V}merger.{dst}.weight"] = v[f"m.{src}_w"].clone()
+                sd[f"{V}merger.{dst}.bias"] = v[f"m.{src}_b"].clone()
+            return sd
         sd[V + "patch_embed.proj.bias"] = v["patch_b"].clone()
         if "pos_embed" in v:
             sd[V + "pos_embed.weight"] = v["pos_embed"].clone()

@@ -126,10 +126,11 @@ def gemm_partials(a: torch.Tensor, b: torch.Tensor):
 
 def dec_qkv(ws, meta, bias, q_w, k_w, lengths, delta, rope: "RopeCfg", k_cache, v_cache, *, n_q: int, n_kv: int,
             eps: float):
-    """Sum QKV partials (+bias), RMSNorm q/k heads, MRoPE at position ``lengths + delta``, write k/v into the
-    cache at ``lengths``; returns q [B, n_q, D]."""
+    """Sum QKV partials (+bias), RMSNorm q/k heads (skipped when ``q_w`` is None), MRoPE at position
+    ``lengths + delta``, write k/v into the cache at ``lengths``; returns q [B, n_q, D]."""
     f, _ = rope.device_tables(ws.device)
-    return ext().dec_qkv(ws, list(meta), _opt(bias), q_w, k_w, lengths, delta, f, k_cache, v_cache, n_q, n_kv, float(eps))
+    return ext().dec_qkv(ws, list(meta), _opt(bias), _opt(q_w), _opt(k_w), lengths, delta, f, k_cache, v_cache, n_q, n_kv,
+                         float(eps))
 
 
 def dec_residual_norm(ws, meta, residual, w, eps: float):
@@ -225,7 +226,7 @@ def qk_norm_rope(qkv, q_w, k_w, pos, rope: RopeCfg, *, n_q: int, n_kv: int, eps:
     rq = torch.empty(T, n_q, dtype=torch.float32, device=qkv.device)
     rk = torch.empty(T, n_kv, dtype=torch.float32, device=qkv.device)
     f, ax = rope.device_tables(qkv.device)
-    ext().qk_norm_rope_fwd(qkv, q_w, k_w, pos, f, ax, q, k, v, rq, rk, n_q, n_kv, float(eps))
+    ext().qk_norm_rope_fwd(qkv, _opt(q_w), _opt(k_w), pos, f, ax, q, k, v, rq, rk, n_q, n_kv, float(eps))
     return q, k, v, rq, rk
 
 
@@ -235,14 +236,15 @@ def qk_norm_rope_bwd(dq, dk, dv, qkv, q_w, k_w, pos, rq, rk, rope: RopeCfg, *, n
         dqkv, dqw, dkw = ref.qk_norm_rope_bwd(dq, dk, dv, qkv, q_w, k_w, pos, rq, rk, n_q=n_q, n_kv=n_kv,
                                               head_dim=rope.head_dim, theta=rope.theta, section=rope.section,
                                               interleaved=rope.interleaved, eps=eps)
-        if dqw_accum is not None:
+        if dqw_accum is not None and dqw is not None:
             dqw_accum.add_(dqw)
-        if dkw_accum is not None:
+        if dkw_accum is not None and dkw is not None:
             dkw_accum.add_(dkw)
         return dqkv
     dqkv = torch.empty_like(qkv)
     f, ax = rope.device_tables(qkv.device)
-    ext().qk_norm_rope_bwd(dq, dk, dv, qkv, q_w, k_w, pos, f, ax, rq, rk, dqkv, _opt(dqw_accum), _opt(dkw_accum),
+    ext().qk_norm_rope_bwd(dq, dk, dv, qkv, _opt(q_w), _opt(k_w), pos, f, ax, rq, rk, dqkv, _opt(dqw_accum),
+                           _opt(dkw_accum),
                            n_q, n_kv, float(eps))
     return dqkv
 
@@ -259,11 +261,22 @@ def vision_rope(qkv, rc, *, n_heads: int, head_dim: int):
 
 
 # ------------------------------------------------------------------ attention
+_ATTN_DIMS = (16, 32, 64, 128)
+
+
 def flash_attn(q, k, v, cu_seqlens, max_seqlen: int, *, causal: bool, scale: Optional[float] = None, pre=None):
     """Varlen GQA attention; ``pre`` (int32 [segments, 2]) adds a shared, unmasked key prefix per segment."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if not _cuda(q):
         return ref.flash_attn(q, k, v, cu_seqlens, max_seqlen, causal=causal, scale=scale, pre=pre)
+    D = q.shape[-1]
+    if D not in _ATTN_DIMS:
+        # head sizes without a kernel instance (e.g. 80 in the Qwen2.5 ViT): zero-pad to the next one;
+        # zero columns add nothing to q.k and produce zero output columns
+        Dp = next(d for d in _ATTN_DIMS if d > D)
+        pad = lambda t: torch.nn.functional.pad(t, (0, Dp - D)).contiguous()
+        o, lse = flash_attn(pad(q), pad(k), pad(v), cu_seqlens, max_seqlen, causal=causal, scale=scale, pre=pre)
+        return o[..., :D].contiguous(), lse
     o = torch.empty_like(q)
     lse = torch.empty(q.shape[1], q.shape[0], dtype=torch.float32, device=q.device)
     ext().flash_attn_fwd(q, k, v, cu_seqlens, o, lse, int(max_seqlen), bool(causal), float(scale), pre)

@@ -135,10 +135,15 @@ def qk_norm_rope(qkv: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor, pos: t
     D = head_dim
     x = qkv.float().view(T, n_q + 2 * n_kv, D)
     q, k, v = x[:, :n_q], x[:, n_q:n_q + n_kv], x[:, n_q + n_kv:]
-    rq = torch.rsqrt(q.pow(2).mean(-1) + eps)
-    rk = torch.rsqrt(k.pow(2).mean(-1) + eps)
-    qn = q * rq[..., None] * q_w.float()
-    kn = k * rk[..., None] * k_w.float()
+    if q_w is None:   # rotation only (attention without q/k RMSNorm)
+        rq = torch.ones(q.shape[:2], device=qkv.device)
+        rk = torch.ones(k.shape[:2], device=qkv.device)
+        qn, kn = q, k
+    else:
+        rq = torch.rsqrt(q.pow(2).mean(-1) + eps)
+        rk = torch.rsqrt(k.pow(2).mean(-1) + eps)
+        qn = q * rq[..., None] * q_w.float()
+        kn = k * rk[..., None] * k_w.float()
     cos, sin = rope_tables(pos, D, theta, section, interleaved)
     dt = qkv.dtype
     return (_rotate(qn, cos, sin).to(dt), _rotate(kn, cos, sin).to(dt), v.to(dt).contiguous(), rq, rk)
@@ -159,8 +164,11 @@ def qk_norm_rope_bwd(dq, dk, dv, qkv, q_w, k_w, pos, rq, rk, *, n_q, n_kv, head_
         dx = r[..., None] * (gw - xhat * (gw * xhat).mean(-1, keepdim=True))
         return dx, (g * xhat).reshape(-1, D).sum(0)
 
-    dq_in, dqw = norm_bwd(dqn, q, rq, q_w)
-    dk_in, dkw = norm_bwd(dkn, k, rk, k_w)
+    if q_w is None:
+        dq_in, dqw, dk_in, dkw = dqn, None, dkn, None
+    else:
+        dq_in, dqw = norm_bwd(dqn, q, rq, q_w)
+        dk_in, dkw = norm_bwd(dkn, k, rk, k_w)
     dqkv = torch.cat([dq_in, dk_in, dv.float()], dim=1).reshape(T, -1)
     return dqkv.to(qkv.dtype), dqw, dkw
 
