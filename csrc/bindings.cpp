@@ -11,6 +11,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dec_qkv", &vlm::dec_qkv);
   m.def("dec_residual_norm", &vlm::dec_residual_norm);
   m.def("dec_swiglu", &vlm::dec_swiglu);
+  m.def("tp_step_begin", &vlm::tp_step_begin, "advance the tensor-parallel decode epoch (device counter)");
+  m.def("dec_residual_norm_tp", &vlm::dec_residual_norm_tp,
+        "residual + RMSNorm consumer that all-reduces row-parallel partials over NVLink");
   m.def("rms_norm_fwd", &vlm::rms_norm_fwd);
   m.def("rms_norm_bwd", &vlm::rms_norm_bwd);
   m.def("layer_norm_fwd", &vlm::layer_norm_fwd);

@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "host_utils.h"
+#include "peer.cuh"
 #include "streamk.cuh"
 #include "vlm_ops.h"
 
@@ -198,6 +199,119 @@ at::Tensor dec_swiglu(at::Tensor ws, std::vector<int64_t> meta) {
   launch_pdl(dec_swiglu_kernel, grid, dim3(256), 0, at::cuda::getCurrentCUDAStream(), ws.data_ptr<float>(), m,
              reinterpret_cast<bf16*>(act.data_ptr()), m.N);
   return act;
+}
+
+
+// ------------------------------------------------------------------ tensor-parallel decode consumers
+// Row-parallel GEMMs (o_proj, down_proj) leave each rank with a partial sum of the full [B, H] output.
+// dec_resnorm_tp_kernel all-reduces it over NVLink inside the consumer: CTA `row` (1) sums this rank's
+// stream-K slots of its row into the rank's IPC-shared row buffer, (2) publishes flag[point][row][rank]
+// = epoch on every peer, (3) waits (bounded) for every peer's flag of the same row, (4) sums all ranks'
+// row buffers in rank order (identical on every rank), adds the residual and applies the RMSNorm.
+// Per-row flags make the exchange fine grained: no grid-wide barrier.  A rank's row buffer for a point
+// is rewritten one decode step later, after the rank has seen every peer's flag of the next point,
+// i.e. after every peer finished reading it.
+__global__ void tp_step_begin_kernel(unsigned long long* epoch) {
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0) epoch[0] += 1ull;
+}
+
+__global__ void dec_resnorm_tp_kernel(const float* __restrict__ ws, SkMeta m, const bf16* __restrict__ res,
+                                      const bf16* __restrict__ w, bf16* __restrict__ h_out, bf16* __restrict__ hn_out,
+                                      int H, float eps, PeerTable rows, PeerTable sigs, int64_t flag_base,
+                                      const unsigned long long* __restrict__ epoch_ptr, int rank, int W, int* err) {
+  __shared__ float red[32];
+  __shared__ int ok;
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x, col = threadIdx.x * 8;
+  const unsigned long long epoch = *epoch_ptr;
+  float x[8];
+  const int64_t off = static_cast<int64_t>(row) * H + col;
+  if (col < H) {
+    sk_sum8(ws, m, row, col, x);
+    float* mine = reinterpret_cast<float*>(rows.p[rank]) + off;
+    reinterpret_cast<float4*>(mine)[0] = make_float4(x[0], x[1], x[2], x[3]);
+    reinterpret_cast<float4*>(mine)[1] = make_float4(x[4], x[5], x[6], x[7]);
+  }
+  __threadfence_system();
+  __syncthreads();
+  const int64_t fb = flag_base + static_cast<int64_t>(row) * W;
+  if (threadIdx.x < W && static_cast<int>(threadIdx.x) != rank)
+    store_release_sys(reinterpret_cast<unsigned long long*>(sigs.p[threadIdx.x]) + fb + rank, epoch);
+  if (threadIdx.x == 0) ok = wait_peers_at(reinterpret_cast<const unsigned long long*>(sigs.p[rank]), fb, W, rank, epoch, err);
+  __syncthreads();
+  if (!ok) return;
+  float ss = 0.f;
+  if (col < H) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = 0.f;
+    for (int p = 0; p < W; ++p) {
+      const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(rows.p[p]) + off);
+      const float4 a = src[0], b = src[1];
+      x[0] += a.x; x[1] += a.y; x[2] += a.z; x[3] += a.w;
+      x[4] += b.x; x[5] += b.y; x[6] += b.z; x[7] += b.w;
+    }
+    const uint4 rv = *reinterpret_cast<const uint4*>(res + off);
+    const uint32_t u[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(u[j]);
+      x[2 * j] = bf2f(f2bf(x[2 * j] + f.x));
+      x[2 * j + 1] = bf2f(f2bf(x[2 * j + 1] + f.y));
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    store8(h_out + off, x);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x + 31) / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  if (col < H) {
+    const float r = rsqrtf(red[0] / H + eps);
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = bf2f(f2bf(x[i] * r)) * bf2f(w[col + i]);
+    store8(hn_out + off, o);
+  }
+}
+
+void tp_step_begin(int64_t epoch_ptr, int64_t device) {
+  const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
+  launch_pdl(tp_step_begin_kernel, dim3(1), dim3(32), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<unsigned long long*>(epoch_ptr));
+}
+
+// h = residual + all-reduce over ranks of this rank's partials; hn = rms_norm(h) * w.  `rows` / `sigs` are
+// the per-rank addresses of the IPC-shared row buffer of this point ([B, H] fp32) and of the flag pad.
+std::tuple<at::Tensor, at::Tensor> dec_residual_norm_tp(at::Tensor ws, std::vector<int64_t> meta, at::Tensor res,
+                                                        at::Tensor w, double eps, std::vector<int64_t> rows,
+                                                        int64_t rows_off_bytes, std::vector<int64_t> sigs,
+                                                        int64_t flag_base, int64_t epoch_ptr, int64_t rank) {
+  const SkMeta m = meta_of(meta);
+  const int H = m.N;
+  const int W = static_cast<int>(rows.size());
+  TORCH_CHECK(H % 8 == 0 && H / 8 <= 1024, "dec_residual_norm_tp: H must be a multiple of 8 and <= 8192");
+  TORCH_CHECK(static_cast<int>(sigs.size()) == W && rank >= 0 && rank < W, "dec_residual_norm_tp: tables");
+  TORCH_CHECK(rows_off_bytes % 16 == 0, "dec_residual_norm_tp: row buffer alignment");
+  const c10::cuda::CUDAGuard g(ws.device());
+  at::Tensor h = at::empty({m.M, H}, res.options());
+  at::Tensor hn = at::empty({m.M, H}, res.options());
+  const int threads = ((H / 8 + 31) / 32) * 32;
+  launch_pdl(dec_resnorm_tp_kernel, dim3(m.M), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
+             ws.data_ptr<float>(), m, reinterpret_cast<const bf16*>(res.data_ptr()),
+             reinterpret_cast<const bf16*>(w.data_ptr()), reinterpret_cast<bf16*>(h.data_ptr()),
+             reinterpret_cast<bf16*>(hn.data_ptr()), H, static_cast<float>(eps), make_peer_table(rows, rows_off_bytes),
+             make_peer_table(sigs), flag_base, reinterpret_cast<const unsigned long long*>(epoch_ptr),
+             static_cast<int>(rank), W, err_word(ws.device().index()));
+  return {h, hn};
 }
 
 }  // namespace vlm

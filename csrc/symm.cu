@@ -33,46 +33,16 @@
 
 #include "common.cuh"
 #include "host_utils.h"
+#include "peer.cuh"
 
 namespace vlm {
 
 using bf16 = __nv_bfloat16;
 
-constexpr int kMaxRanks = 8;
-// ~9 s at 1.9 GHz: generous for rank skew inside a backward pass, still finite.
-constexpr long long kPeerWait = 1ll << 34;
-
-struct PeerTable {
-  unsigned long long p[kMaxRanks];
-};
-
-VLM_DEV void store_release_sys(unsigned long long* addr, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
-}
-VLM_DEV void add_release_sys(unsigned long long* addr, unsigned long long v) {
-  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
-}
-VLM_DEV unsigned long long load_acquire_sys(const unsigned long long* addr) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
-  return v;
-}
-
 // Wait until sig[slot * W + p] >= target for every peer p != rank.  Called by one thread.
 VLM_DEV bool wait_peers(const unsigned long long* sig, int slot, int W, int rank, unsigned long long target,
                         int* err) {
-  const long long t0 = clock64();
-  for (int p = 0; p < W; ++p) {
-    if (p == rank) continue;
-    const unsigned long long* a = sig + static_cast<int64_t>(slot) * W + p;
-    while (load_acquire_sys(a) < target) {
-      if (clock64() - t0 > kPeerWait) {
-        atomicCAS(err, 0, kErrTimeoutPeer);
-        return false;
-      }
-    }
-  }
-  return true;
+  return wait_peers_at(sig, static_cast<int64_t>(slot) * W, W, rank, target, err);
 }
 
 // ------------------------------------------------------------------ reduce-scatter (pull)
@@ -239,10 +209,7 @@ at::Tensor symm_view(int64_t base, int64_t offset_bytes, std::vector<int64_t> si
 }
 
 static PeerTable make_table(const std::vector<int64_t>& ptrs, int64_t byte_off = 0) {
-  TORCH_CHECK(!ptrs.empty() && ptrs.size() <= static_cast<size_t>(kMaxRanks), "peer table: 1..", kMaxRanks, " ranks");
-  PeerTable t{};
-  for (size_t i = 0; i < ptrs.size(); ++i) t.p[i] = static_cast<unsigned long long>(ptrs[i] + byte_off);
-  return t;
+  return make_peer_table(ptrs, byte_off);
 }
 
 static int peer_grid(int64_t items, int device) {
