@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--minibatches", type=int, default=2)
     ap.add_argument("--top-k", type=int, default=5)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--rollout", choices=["tp", "dp"], default="tp",
+                    help="N>1: tensor-parallel decode of the whole batch (tp) or each rank decodes its own groups (dp)")
     return ap.parse_args()
 
 
@@ -167,7 +169,8 @@ def main():
         ref_model = Qwen3VLModel(spec, units=text_units, device=dev, dtype=torch.bfloat16)
         train_state = None
     trainer = GRPOTrainer(model, tok, env, cfg, adamw, ref_model=ref_model, seed=0, rank=rank, world_size=world,
-                          train_state=train_state)
+                          train_state=train_state,
+                          tp_rollout=(world > 1 and args.rollout == "tp"))
 
     def barrier():
         if world > 1:
@@ -220,10 +223,12 @@ def main():
         torch.cuda.synchronize()
         barrier()
         e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
-        img_bytes = args.groups // world * args.image * args.image * 3
+        roll_groups = args.groups if trainer.tp is not None else args.groups // world  # rolled out on this rank
+        img_bytes = roll_groups * args.image * args.image * 3
         prompt_len = 196 * (args.image // 448) ** 2 + 2 + args.prompt_tokens
-        seqs = args.groups * args.group_size // world
-        h2d = img_bytes + seqs * (prompt_len + args.max_new) * 8 * 5  # images + packed ids/positions/indices
+        seqs = args.groups * args.group_size // world                                   # trained on this rank
+        # images + prefill ids/positions + packed training ids/positions/indices (int64)
+        h2d = img_bytes + roll_groups * prompt_len * 8 * 5 + seqs * (prompt_len + args.max_new) * 8 * 5
         d2h = seqs * args.max_new * 12 + 8 * 64                         # tokens, logprobs, lengths, metrics
         e2e = {"value": 1.0 / e2e_s, "unit": "RL steps/s", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3}
@@ -246,14 +251,15 @@ def main():
         "data": "synthetic (uniform-random 448x448 RGB images and prompt ids, uniform-on-sphere targets), random-init weights",
         "config": {"model": f"{args.preset} architecture (random init)", "global_batch": total_seqs,
                    "seq_len": f"{196 + 2 + args.prompt_tokens} prompt + {args.max_new} new",
-                   "parallelism": f"fsdp{world}" if world > 1 else "single-gpu",
+                   "parallelism": (f"fsdp{world}+tp{world}-rollout" if trainer.tp is not None else f"fsdp{world}")
+                   if world > 1 else "single-gpu",
                    "fsdp_comm": getattr(model.params, "comm", None) if world > 1 else None,
                    "groups_per_batch": args.groups, "group_size": args.group_size, "minibatches": args.minibatches,
                    "kl_ref_coef": 0.01, "top_k": args.top_k, "top_p": 0.9, "temperature": 0.7,
                    "l2": "no flush: per-step working set (8.8 GB weights) >> 126 MB L2"},
         "decode_tok_s": decode_tok_s,
         "decode_ms_per_step": decode_ms,
-        "rollout_tokens_per_step": gen_tokens / max(1, args.steps) * world,
+        "rollout_tokens_per_step": gen_tokens / max(1, args.steps),   # already summed over ranks
         "phase_ms": {k: v for k, v in last.items() if k.startswith("time/")},
         "gpu_launches": int(launches),
         "clocks": clk,
@@ -262,6 +268,7 @@ def main():
     if rank == 0:
         print(json.dumps(out))
     if world > 1:
+        trainer.close()
         close = getattr(model.params, "close", None)
         if close is not None:
             close()

@@ -150,13 +150,32 @@ def build_minibatches(model, eb: EpisodeBatch, adv_seq: torch.Tensor, n_minibatc
 
 
 def collect(env, tokenizer, model, ts, cfg: TrainerConfig, batch_size: Optional[int] = None, rng: int = 0, *,
-            eos_id: Optional[int] = None, generator=None, task_offset: int = 0, row_offset: int = 0) -> CollectResult:
-    """Roll out one iteration and build the minibatches (reference ``collect``, ``core/ppo.py:51-92``)."""
+            eos_id: Optional[int] = None, generator=None, task_offset: int = 0, row_offset: int = 0,
+            keep_groups: Optional[Tuple[int, int]] = None) -> CollectResult:
+    """Roll out one iteration and build the minibatches (reference ``collect``, ``core/ppo.py:51-92``).
+
+    ``keep_groups=(g0, g1)``: the rollout covers ``batch_size`` groups (e.g. a tensor-parallel rollout that
+    every rank runs identically) but this process trains on groups [g0, g1) only.
+    """
     G = int(batch_size) if batch_size else int(cfg.groups_per_batch)
     eb = collect_episodes(env, tokenizer, model, sampling_config(cfg, eos_id), groups_per_batch=G,
                           group_size=cfg.group_size, seed=rng, task_offset=task_offset, generator=generator,
                           min_pixels=cfg.vlm_min_pixels, max_pixels=cfg.vlm_max_pixels,
                           max_sequence_length=cfg.max_sequence_length, row_offset=row_offset)
+    if keep_groups is not None:
+        all_rewards = torch.tensor([e.reward for e in eb.episodes], dtype=torch.float32)
+        if cfg.adv_norm == "batch":
+            full_adv = group_advantages(all_rewards, cfg.group_size, "batch")
+        eb = eb.subset(keep_groups[0], keep_groups[1], model.spec.vision.spatial_merge_size)
+        rewards = torch.tensor([e.reward for e in eb.episodes], dtype=torch.float32)
+        gs = max(1, cfg.group_size)
+        if cfg.adv_norm == "batch":
+            adv = full_adv[keep_groups[0] * gs:keep_groups[1] * gs].to(model.device)
+        else:
+            adv = group_advantages(rewards, cfg.group_size, cfg.adv_norm).to(model.device)
+        mbs = build_minibatches(model, eb, adv, _minibatch_count(cfg, len(eb.episodes)), cfg.max_sequence_length,
+                                share_prompt=cfg.share_prompt)
+        return CollectResult(episodes=eb, rewards=rewards, advantages=adv, minibatches=mbs)
     rewards = torch.tensor([e.reward for e in eb.episodes], dtype=torch.float32)
     if cfg.adv_norm == "batch" and _distributed():
         import torch.distributed as dist

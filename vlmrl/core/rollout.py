@@ -73,6 +73,19 @@ class EpisodeBatch:
     vision: Optional[VisionEmbeddings] = None       # per episode, in episode order
     group_size: int = 1
 
+    def subset(self, g0: int, g1: int, merge: int) -> "EpisodeBatch":
+        """Groups [g0, g1) (episodes in (group, member) order) with their vision rows."""
+        gs = max(1, self.group_size)
+        eps = self.episodes[g0 * gs:g1 * gs]
+        vis = self.vision
+        if vis is not None:
+            counts = [sum(_merged_count(g, merge) for g in ep.grids) for ep in self.episodes]
+            start = int(sum(counts[:g0 * gs]))
+            n = int(sum(counts[g0 * gs:g1 * gs]))
+            vis = vis.select(torch.arange(start, start + n, device=vis.tokens.device))
+        info = {k: v[g0 * gs:g1 * gs] for k, v in self.raw_info.items()} if self.raw_info else {}
+        return EpisodeBatch(episodes=eps, raw_info=info, vision=vis, group_size=self.group_size)
+
 
 def _images_of(obs) -> List[Any]:
     if hasattr(obs, "images"):

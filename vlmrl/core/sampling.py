@@ -48,8 +48,12 @@ class _DecodeState:
 
 
 class Generator:
-    def __init__(self, model, *, use_cuda_graph: bool = True):
+    """``tp``: a ``vlmrl.parallel.tp.TPDecoder`` — decode steps then run tensor-parallel over its ranks (every
+    rank must call ``generate`` with the same prompts and seed); the prefill stays replicated."""
+
+    def __init__(self, model, *, use_cuda_graph: bool = True, tp=None):
         self.model = model
+        self.tp = tp
         self.use_cuda_graph = bool(use_cuda_graph) and model.device.type == "cuda"
         self._states: Dict[Tuple[int, int, int], _DecodeState] = {}
         self.graph_kernel_launches = 0   # kernels executed by graph replays (not seen by the launch counter)
@@ -68,7 +72,10 @@ class Generator:
         st.step += 1
 
     def _decode_step(self, st: _DecodeState, cfg: SamplingConfig, row_offset: int):
-        logits = self.model.decode_step(st.tok, st.cache, st.deltas)
+        if self.tp is not None:
+            logits = self.tp.decode_step(st.tok, st.tp_cache, st.deltas)
+        else:
+            logits = self.model.decode_step(st.tok, st.cache, st.deltas)
         nt, lp = ops.sample(logits, temperature=cfg.temperature, top_k=cfg.top_k or 0, top_p=cfg.top_p or 0.0,
                             seed=st.seed, step=st.step, row_offset=row_offset)
         self._record(st, nt, lp, cfg.eos_id)
@@ -89,6 +96,7 @@ class Generator:
             if len(self._states) >= 4:          # bound resident caches
                 self._states.clear()
             st = _DecodeState(self.model, B, max_len, max_new)
+            st.tp_cache = self.tp.new_cache(B, max_len) if self.tp is not None else None
             self._states[key] = st
         return st
 
@@ -134,6 +142,9 @@ class Generator:
         nt, lp = ops.sample(logits, temperature=cfg.temperature, top_k=cfg.top_k or 0, top_p=cfg.top_p or 0.0,
                             seed=st.seed, step=st.step, row_offset=row_offset)
         self._record(st, nt, lp, cfg.eos_id)
+        if self.tp is not None:
+            self.tp.refresh(getattr(m.params, "version", None))
+            self.tp.load_cache(st.cache, st.tp_cache, plen)
         steps = max_new - 1
         if steps > 0:
             if self.use_cuda_graph:

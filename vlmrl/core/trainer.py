@@ -56,14 +56,21 @@ class _Timer:
 class GRPOTrainer:
     def __init__(self, model, tokenizer, env, cfg: TrainerConfig, adamw: AdamWConfig, *, ref_model=None,
                  seed: int = 0, master=None, eos_id: Optional[int] = None, rank: int = 0, world_size: int = 1,
-                 train_state=None):
+                 train_state=None, tp_rollout: bool = False):
         self.model = model
         self.tokenizer = tokenizer
         self.env = env
         self.cfg = cfg
         self.ts = train_state if train_state is not None else TrainState.create_with_params(model, adamw, master)
         self.ref_model = ref_model
-        self.generator = Generator(model)
+        # tp_rollout: every rank decodes the whole batch with 1/world of each layer's weights (tensor
+        # parallel over NVLink), then trains on its own share of the groups (FSDP data parallel)
+        self.tp = None
+        if tp_rollout and world_size > 1:
+            from vlmrl.parallel.tp import maybe_tp_decoder
+
+            self.tp = maybe_tp_decoder(model, max_batch=int(cfg.groups_per_batch) * max(1, int(cfg.group_size)))
+        self.generator = Generator(model, tp=self.tp)
         self.kl_ctrl = (AdaptiveKL(cfg.kl_target, cfg.kl_adapt_rate, cfg.kl_coef_min, cfg.kl_coef_max)
                         if cfg.adaptive_kl else None)
         self.kl_coef = float(cfg.kl_coef)
@@ -83,15 +90,26 @@ class GRPOTrainer:
             raise ValueError(f"groups_per_batch={g} must be divisible by the world size {self.world}")
         return g // self.world
 
+    def close(self) -> None:
+        """Release the tensor-parallel decoder's IPC-shared buffers (collective)."""
+        if self.tp is not None:
+            self.tp.close()
+            self.tp = None
+
     def step(self) -> Dict[str, Any]:
         cfg = self.cfg
         timer = _Timer(self.model.device)
         timer.mark("start")
         seed = self.rng.next()
         G = self.groups_per_rank
-        cr = collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G, rng=seed, eos_id=self.eos_id,
-                     generator=self.generator, task_offset=self.cursor + self.rank * G,
-                     row_offset=self.rank * G * cfg.group_size)
+        if self.tp is not None:
+            cr = collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G * self.world, rng=seed,
+                         eos_id=self.eos_id, generator=self.generator, task_offset=self.cursor, row_offset=0,
+                         keep_groups=(self.rank * G, (self.rank + 1) * G))
+        else:
+            cr = collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G, rng=seed,
+                         eos_id=self.eos_id, generator=self.generator, task_offset=self.cursor + self.rank * G,
+                         row_offset=self.rank * G * cfg.group_size)
         timer.mark("rollout")
         self.cursor += G * self.world
         num_tasks = getattr(self.env, "num_tasks", -1)

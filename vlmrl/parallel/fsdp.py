@@ -103,6 +103,7 @@ class FSDPParams:
                 self.gathered[u] = torch.empty(self.padded[u], dtype=dtype, device=self.device)
                 self.fresh[u] = False
         self.units = self.replicated  # frozen units, for code that wants a plain dict
+        self.version = 0              # bumped by every optimizer step (consumers re-slice derived copies)
 
     # ---------------------------------------------------------------- peer-memory setup
     def _init_p2p(self) -> None:
@@ -281,6 +282,7 @@ class FSDPOptimizer:
                            p_half=p.shards[u])
                 p.grad_shards[u].zero_()
             p.invalidate()
+        p.version += 1
         return {"grad_norm": norm[0], "grad_sq_sum": sq[0]}
 
     # ---------------------------------------------------------------- checkpointing (collectives)
@@ -325,6 +327,7 @@ class FSDPOptimizer:
             if nu is not None:
                 self.v[u].copy_(shard_of(nu[u]))
         p.invalidate()
+        p.version += 1
         if p.comm == "p2p":
             p.regather()
 

@@ -1,0 +1,168 @@
+"""Tensor-parallel decoding over the ranks of a process group (one GPU per rank, NVLink peers).
+
+Every rank decodes the SAME batch of sequences with 1/W of each decoder layer's
+weights (Megatron-style split, rebuilt for the decode step):
+
+* q/k/v projections: column-parallel by attention head (rank r owns q heads
+  ``[r*nq/W, (r+1)*nq/W)`` and kv heads ``[r*nkv/W, (r+1)*nkv/W)``); the KV
+  cache holds only the local kv heads, so attention needs no communication;
+* o_proj and down_proj: row-parallel; their stream-K partial sums are
+  all-reduced INSIDE the residual + RMSNorm consumer kernel
+  (``dec_residual_norm_tp``): each CTA publishes its row of partials in an
+  IPC-shared buffer, flags every peer, waits for theirs and sums all ranks in
+  rank order — so every rank ends with bitwise-identical activations;
+* gate/up: column-parallel (interleaved gate/up row pairs stay together);
+* embedding, final norm, lm_head and the sampler are replicated: every rank
+  computes the same logits and, with the same Philox seed, samples the same
+  tokens, so no collective is needed to agree on the next token.
+
+The prefill runs replicated with the full weights (it is a small part of a
+rollout); the local kv heads are then copied into the tensor-parallel cache.
+Shards are re-sliced from the model's (gathered) parameters whenever they
+changed (``refresh``), into buffers at fixed addresses so a captured decode
+graph stays valid.  Synchronisation uses a device-side step counter (epoch)
+advanced by the first kernel of every step; flags are monotonic, so nothing is
+ever reset, and every wait is bounded (error code instead of a hang).
+
+No reference counterpart: the reference decodes on one device
+(``core/sampling.py:157-224``).
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from vlmrl import ops
+from vlmrl.models.qwen3vl.model import KVCache
+from vlmrl.ops._ext import ext
+
+
+class TPDecoder:
+    def __init__(self, model, group=None, max_batch: int = 64):
+        from vlmrl.parallel.symm import SymmetricBuffer
+
+        self.model = model
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        spec = model.spec
+        t = spec.text
+        W = self.world
+        for name, n in (("attention heads", t.num_attention_heads), ("kv heads", t.num_key_value_heads),
+                        ("intermediate size", t.intermediate_size)):
+            if n % W:
+                raise ValueError(f"tensor parallelism over {W} ranks needs {name} ({n}) divisible by {W}")
+        self.L, self.H, self.D = t.num_hidden_layers, t.hidden_size, t.head_dim
+        self.nq, self.nkv, self.F = t.num_attention_heads, t.num_key_value_heads, t.intermediate_size
+        self.nq_l, self.nkv_l, self.F_l = self.nq // W, self.nkv // W, self.F // W
+        self.max_batch = int(max_batch)
+        dev, dt = model.device, model.dtype
+        L, H, D = self.L, self.H, self.D
+        qkv_l = (self.nq_l + 2 * self.nkv_l) * D
+        self.qkv_w = torch.empty(L, qkv_l, H, dtype=dt, device=dev)
+        self.qkv_b = torch.empty(L, qkv_l, dtype=dt, device=dev)
+        self.o_w = torch.empty(L, H, self.nq_l * D, dtype=dt, device=dev)
+        self.gu_w = torch.empty(L, 2 * self.F_l, H, dtype=dt, device=dev)
+        self.down_w = torch.empty(L, H, self.F_l, dtype=dt, device=dev)
+        self.points = 2 * L
+        self.rows = SymmetricBuffer(self.points * self.max_batch * H * 4, group, dev)
+        self.sigs = SymmetricBuffer(self.points * self.max_batch * W * 8, group, dev)
+        self.epoch = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.version = None
+        self.eps = t.rms_norm_eps
+
+    # ---------------------------------------------------------------- weights
+    @torch.no_grad()
+    def refresh(self, version=None) -> None:
+        """Re-slice this rank's shards from the model's full (gathered) layer weights."""
+        if version is not None and version == self.version:
+            return
+        dec, params, r = self.model.decoder, self.model.params, self.rank
+        D, nq_l, nkv_l, F_l = self.D, self.nq_l, self.nkv_l, self.F_l
+        q0, k0, v0 = r * nq_l * D, self.nq * D + r * nkv_l * D, (self.nq + self.nkv) * D + r * nkv_l * D
+        nqd, nkd = nq_l * D, nkv_l * D
+        for i in range(self.L):
+            w = dec._w(params, f"layer{i}")
+            for dst, src in ((self.qkv_w[i], w["qkv_w"]), (self.qkv_b[i], w["qkv_b"])):
+                dst[:nqd].copy_(src[q0:q0 + nqd])
+                dst[nqd:nqd + nkd].copy_(src[k0:k0 + nkd])
+                dst[nqd + nkd:].copy_(src[v0:v0 + nkd])
+            self.o_w[i].copy_(w["o_w"][:, q0:q0 + nqd])
+            self.gu_w[i].copy_(w["gu_w"][2 * r * F_l:2 * (r + 1) * F_l])
+            self.down_w[i].copy_(w["down_w"][:, r * F_l:(r + 1) * F_l])
+            params.release(f"layer{i}")
+        self.version = version
+
+    # ---------------------------------------------------------------- cache
+    def new_cache(self, batch: int, max_len: int) -> KVCache:
+        if batch > self.max_batch:
+            raise ValueError(f"tensor-parallel decode was sized for {self.max_batch} rows, got {batch}")
+        m = self.model
+        return KVCache(self.L, batch, self.nkv_l, max_len, self.D, m.dtype, m.device)
+
+    @torch.no_grad()
+    def load_cache(self, full: KVCache, local: KVCache, prefix_len: int) -> None:
+        """Copy this rank's kv heads (first ``prefix_len`` positions) of a full cache into the local one."""
+        h0, h1 = self.rank * self.nkv_l, (self.rank + 1) * self.nkv_l
+        local.keys[:, :, :, :prefix_len].copy_(full.keys[:, :, h0:h1, :prefix_len])
+        local.values[:, :, :, :prefix_len].copy_(full.values[:, :, h0:h1, :prefix_len])
+        local.lengths.copy_(full.lengths)
+
+    # ---------------------------------------------------------------- decode
+    def _reduce_norm(self, ws, meta, res, w, point: int):
+        H, B = self.H, self.max_batch
+        return ext().dec_residual_norm_tp(ws, list(meta), res, w, float(self.eps), self.rows.ptrs,
+                                          point * B * H * 4, self.sigs.ptrs, point * B * self.world,
+                                          self.epoch.data_ptr(), self.rank)
+
+    @torch.no_grad()
+    def decode_step(self, tokens: torch.Tensor, cache: KVCache, rope_delta: torch.Tensor) -> torch.Tensor:
+        """Logits [B, V] (identical on every rank); appends this token's local k/v and advances the cache."""
+        m = self.model
+        dec, params = m.decoder, m.params
+        ext().tp_step_begin(self.epoch.data_ptr(), m.device.index if m.device.index is not None else 0)
+        x = ops.embed(tokens, dec._w(params, "embed")["embed"])
+        params.release("embed")
+        B = tokens.shape[0]
+        lens = cache.lengths
+        delta = rope_delta.reshape(-1).to(torch.int64)
+        lens_after = lens + 1
+        w = dec._w(params, "layer0")
+        xn, _ = ops.rms_norm(x, w["input_norm"], self.eps)
+        for i in range(self.L):
+            w = dec._w(params, f"layer{i}")
+            ws, meta = ops.gemm_partials(xn, self.qkv_w[i])
+            q = ops.dec_qkv(ws, meta, self.qkv_b[i], w.get("q_norm"), w.get("k_norm"), lens, delta, dec.rope,
+                            cache.keys[i], cache.values[i], n_q=self.nq_l, n_kv=self.nkv_l, eps=self.eps)
+            o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=dec.scale)
+            ws, meta = ops.gemm_partials(o.reshape(B, self.nq_l * self.D), self.o_w[i])
+            h1, hn = self._reduce_norm(ws, meta, x, w["post_norm"], 2 * i)
+            ws, meta = ops.gemm_partials(hn, self.gu_w[i])
+            act = ops.dec_swiglu(ws, meta)
+            ws, meta = ops.gemm_partials(act, self.down_w[i])
+            nxt = dec._w(params, f"layer{i + 1}")["input_norm"] if i + 1 < self.L else dec._w(params, "head")["final_norm"]
+            x, xn = self._reduce_norm(ws, meta, h1, nxt, 2 * i + 1)
+            params.release(f"layer{i}")
+        cache.lengths += 1
+        return dec.final_logits(params, xn, normed=True)
+
+    def close(self) -> None:
+        for b in (self.rows, self.sigs):
+            b.close()
+
+
+def maybe_tp_decoder(model, group=None, max_batch: int = 64) -> Optional[TPDecoder]:
+    """A TPDecoder when the process group spans several GPUs with peer access, else None."""
+    from vlmrl.parallel.symm import p2p_supported
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) < 2:
+        return None
+    if not p2p_supported(group):
+        return None
+    return TPDecoder(model, group, max_batch)
+
+
+__all__ = ["TPDecoder", "maybe_tp_decoder"]
