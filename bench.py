@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--minibatches", type=int, default=2)
     ap.add_argument("--top-k", type=int, default=5)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--rollout", choices=["tp", "dp"], default="tp",
+    ap.add_argument("--rollout", choices=["tp", "dp"], default="dp",
                     help="N>1: tensor-parallel decode of the whole batch (tp) or each rank decodes its own groups (dp)")
     return ap.parse_args()
 

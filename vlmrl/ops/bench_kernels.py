@@ -208,6 +208,68 @@ def bench_decode_step(t: Timer, eager_steps: int = 0):
     emit("decode_step_4b_B64_T390", ms, bytes_=weights + 36 * 2 * B * 8 * 390 * 128 * 2)
 
 
+def bench_train_step(t: Timer = None, eager_steps: int = 0, iters: int = 5):
+    """One GRPO minibatch update of Qwen3-VL-4B: 4 groups x 8 members (262-token prompt shared per group,
+    128 response tokens), forward with activations saved, backward, AdamW over all text units."""
+    import numpy as np
+
+    from vlmrl.core.batching import pack_groups
+    from vlmrl.core.optim import AdamWConfig, LocalOptimizer
+    from vlmrl.models.qwen3vl.api import Qwen3VLModel
+    from vlmrl.models.qwen3vl.config import get_preset
+    from vlmrl.models.qwen3vl.model import VisionEmbeddings
+
+    spec = get_preset("qwen3vl_4b")
+    m = Qwen3VLModel(spec, device="cuda", dtype=torch.bfloat16, seed=0)
+    opt = LocalOptimizer(m.params, AdamWConfig(lr=1e-7))
+    rng = np.random.default_rng(0)
+    G, gs, n_img, text, resp = 4, 8, 196, 64, 128
+    prompts, actions = [], []
+    for _ in range(G):
+        p = [spec.vision_start_token_id] + [spec.image_token_id] * n_img + [spec.vision_end_token_id]
+        prompts.append(np.asarray(p + list(rng.integers(0, 150000, text))))
+        actions.append([rng.integers(0, 150000, resp) for _ in range(gs)])
+    H = spec.text.hidden_size
+    vis = VisionEmbeddings(torch.randn(G * n_img, H, device="cuda", dtype=torch.bfloat16),
+                           tuple(torch.randn(G * n_img, H, device="cuda", dtype=torch.bfloat16) for _ in range(3)))
+    batch, counts = pack_groups(spec, prompts, actions, [[(1, 28, 28)]] * G, vis, device="cuda")
+    M = int(batch.loss_rows.numel())
+    g_lp = torch.randn(M, device="cuda") / M
+    g_ent = torch.zeros(M, device="cuda")
+    step = [1]
+
+    def run():
+        with torch.no_grad():
+            _, _, ctx = m.token_logprobs(batch, save=True)
+            m.backward(ctx, g_lp, g_ent)
+        opt.step(step[0])
+        step[0] += 1
+
+    run()
+    torch.cuda.synchronize()
+    if eager_steps:
+        torch.cuda.cudart().cudaProfilerStart()
+        for _ in range(eager_steps):
+            run()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        return
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    for _ in range(iters):
+        run()
+    ev[1].record()
+    torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) / iters
+    from vlmrl.models.qwen3vl.params import text_layouts
+
+    tokens = int(batch.tokens.numel())
+    layer_params = sum(l.numel for l in text_layouts(spec) if l.name.startswith("layer"))
+    # dense GEMM FLOPs (fwd + bwd = 3 x 2 per weight per row); attention and norms not counted
+    flops = 6.0 * layer_params * tokens + 6.0 * spec.text.vocab_size * H * M
+    emit("train_minibatch_4b_4x8_shared", ms, flops=flops, tokens=tokens, loss_rows=M)
+
+
 def _profile_inputs(case: str):
     """-> a zero-argument callable running one launch of the kernel(s) of ``case`` on a small input."""
     H, D = 2560, 128
@@ -266,7 +328,7 @@ def profile_small(case: str = "decode"):
 
 CASES = {"gemm": bench_gemm, "attn": bench_attn, "decode": bench_decode, "vocab": bench_vocab, "norm": bench_norm,
          "decode_step": bench_decode_step,
-         "gemm_tiny": bench_gemm_tiny}
+         "gemm_tiny": bench_gemm_tiny, "train_step": bench_train_step}
 
 
 def main():
@@ -274,7 +336,8 @@ def main():
     ap.add_argument("--only", default=",".join(CASES))
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--eager-steps", type=int, default=0,
-                    help="decode_step only: run N eager steps without timing (for a profiler launch list)")
+                    help="decode_step (default) or --only train_step: run N eager steps inside a profiler range "
+                         "(for a launch list)")
     ap.add_argument("--profile-small", default=None, choices=["decode", "gemm", "attn", "vocab", "adamw"],
                     help="one launch of the named case's kernels inside a profiler range")
     args = ap.parse_args()
@@ -282,7 +345,10 @@ def main():
         profile_small(args.profile_small)
         return
     if args.eager_steps:
-        bench_decode_step(None, args.eager_steps)
+        if args.only == "train_step":
+            bench_train_step(None, args.eager_steps)
+        else:
+            bench_decode_step(None, args.eager_steps)
         return
     t = Timer(args.iters)
     for name in args.only.split(","):
