@@ -200,7 +200,8 @@ def build_inputs(model, tokenizer, prompt: str, image: Optional[str], batch: int
 
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--ckpt_dir", type=str, default="", help="checkpoint directory written by hf_to_jax")
+    ap.add_argument("--ckpt_dir", "--model_dir", dest="ckpt_dir", type=str, default="",
+                    help="checkpoint directory written by hf_to_jax (the reference README's --model_dir also works)")
     ap.add_argument("--preset", type=str, default="", help="random-init architecture when no checkpoint is given")
     ap.add_argument("--prompt", type=str, default=None)
     ap.add_argument("--image", type=str, default=None)
