@@ -57,15 +57,19 @@ __global__ void rms_norm_fwd_kernel(const bf16* __restrict__ x, const bf16* __re
 }
 
 // dx = r * (g - xhat * mean(g * xhat)),  g = dy * w;  dw += sum_rows dy * xhat
+// One warp per row (grid-stride).  The weight gradient sum_rows(dy * xhat) accumulates in a per-warp slice
+// of shared memory (lane-disjoint columns: plain adds, no atomics) that the block reduces once at the end.
+// ``add`` (optional) is a second gradient for the same tensor (the residual path), summed before rounding.
 __global__ void rms_norm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                    const float* __restrict__ rstd, bf16* __restrict__ dx, float* __restrict__ dw,
-                                    int M, int H) {
-  extern __shared__ float sdw[];
+                                    const float* __restrict__ rstd, const bf16* __restrict__ add,
+                                    bf16* __restrict__ dx, float* __restrict__ dw, int M, int H) {
+  extern __shared__ float sdw[];  // [warps][H] when dw
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float* mine = sdw + static_cast<int64_t>(wid) * H;
   if (dw)
-    for (int c = threadIdx.x; c < H; c += blockDim.x) sdw[c] = 0.f;
+    for (int c = threadIdx.x; c < warps * H; c += blockDim.x) sdw[c] = 0.f;
   __syncthreads();
-  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
-  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < M; row += gridDim.x * warps) {
+  for (int row = blockIdx.x * warps + wid; row < M; row += gridDim.x * warps) {
     const bf16* xr = x + static_cast<int64_t>(row) * H;
     const bf16* dyr = dy + static_cast<int64_t>(row) * H;
     const float r = rstd[row];
@@ -79,29 +83,43 @@ __global__ void rms_norm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __r
         const float2 fx = unpack_bf16x2(ua[j]), fd = unpack_bf16x2(ub[j]), fw = unpack_bf16x2(uw[j]);
         dot += fd.x * fw.x * fx.x * r + fd.y * fw.y * fx.y * r;
         if (dw) {
-          atomicAdd(&sdw[c + 2 * j], fd.x * fx.x * r);
-          atomicAdd(&sdw[c + 2 * j + 1], fd.y * fx.y * r);
+          mine[c + 2 * j] += fd.x * fx.x * r;
+          mine[c + 2 * j + 1] += fd.y * fx.y * r;
         }
       }
     }
     dot = warp_sum(dot) / H;
     bf16* dxr = dx + static_cast<int64_t>(row) * H;
+    const bf16* ar = add ? add + static_cast<int64_t>(row) * H : nullptr;
     for (int c = lane * 8; c < H; c += 256) {
       const uint4 a = *reinterpret_cast<const uint4*>(xr + c), b = *reinterpret_cast<const uint4*>(dyr + c),
                   ww = *reinterpret_cast<const uint4*>(w + c);
       const uint32_t ua[4] = {a.x, a.y, a.z, a.w}, ub[4] = {b.x, b.y, b.z, b.w}, uw[4] = {ww.x, ww.y, ww.z, ww.w};
+      uint32_t ue[4] = {0u, 0u, 0u, 0u};
+      if (ar) {
+        const uint4 e = *reinterpret_cast<const uint4*>(ar + c);
+        ue[0] = e.x;
+        ue[1] = e.y;
+        ue[2] = e.z;
+        ue[3] = e.w;
+      }
       uint32_t o[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 fx = unpack_bf16x2(ua[j]), fd = unpack_bf16x2(ub[j]), fw = unpack_bf16x2(uw[j]);
-        o[j] = pack_bf16x2(r * (fd.x * fw.x - fx.x * r * dot), r * (fd.y * fw.y - fx.y * r * dot));
+        const float2 fe = unpack_bf16x2(ue[j]);
+        o[j] = pack_bf16x2(r * (fd.x * fw.x - fx.x * r * dot) + fe.x, r * (fd.y * fw.y - fx.y * r * dot) + fe.y);
       }
       *reinterpret_cast<uint4*>(dxr + c) = make_uint4(o[0], o[1], o[2], o[3]);
     }
   }
   if (dw) {
     __syncthreads();
-    for (int c = threadIdx.x; c < H; c += blockDim.x) atomicAdd(&dw[c], sdw[c]);
+    for (int c = threadIdx.x; c < H; c += blockDim.x) {
+      float acc = 0.f;
+      for (int k = 0; k < warps; ++k) acc += sdw[static_cast<int64_t>(k) * H + c];
+      atomicAdd(&dw[c], acc);
+    }
   }
 }
 
@@ -169,17 +187,26 @@ void rms_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, dou
   VLM_LAUNCHED();
 }
 
-void rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor dx, at::Tensor dw) {
+void rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor dx, at::Tensor dw,
+                  at::Tensor add) {
   const int H = static_cast<int>(x.size(-1));
   const int M = static_cast<int>(x.numel() / H);
   if (M == 0) return;
-  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous(), "rms_norm_bwd: contiguous inputs");
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && H % 8 == 0, "rms_norm_bwd: contiguous inputs, H % 8 == 0");
+  const bool has_add = add.defined() && add.numel();
+  TORCH_CHECK(!has_add || (add.is_contiguous() && add.numel() == x.numel() && add.scalar_type() == at::kBFloat16),
+              "rms_norm_bwd: bad residual gradient");
   const c10::cuda::CUDAGuard g(x.device());
   const bool has_dw = dw.defined() && dw.numel();
-  const int blocks = std::min(blocks_for(M, 8), num_sms(x.device().index()) * 4);
-  rms_norm_bwd_kernel<<<blocks, 256, has_dw ? H * sizeof(float) : 0, cur_stream()>>>(
+  constexpr int kThreads = 256;
+  const int smem = has_dw ? (kThreads / 32) * H * static_cast<int>(sizeof(float)) : 0;
+  if (smem > 48 * 1024)
+    VLM_CUDA_CHECK(cudaFuncSetAttribute(rms_norm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int blocks = std::min(blocks_for(M, 8), num_sms(x.device().index()) * (smem > 110 * 1024 ? 1 : 2));
+  rms_norm_bwd_kernel<<<blocks, kThreads, smem, cur_stream()>>>(
       reinterpret_cast<const bf16*>(dy.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
-      reinterpret_cast<const bf16*>(w.data_ptr()), rstd.data_ptr<float>(), reinterpret_cast<bf16*>(dx.data_ptr()),
+      reinterpret_cast<const bf16*>(w.data_ptr()), rstd.data_ptr<float>(),
+      has_add ? reinterpret_cast<const bf16*>(add.data_ptr()) : nullptr, reinterpret_cast<bf16*>(dx.data_ptr()),
       has_dw ? dw.data_ptr<float>() : nullptr, M, H);
   VLM_LAUNCHED();
 }
@@ -267,79 +294,104 @@ __global__ void qk_norm_rope_fwd_kernel(const bf16* __restrict__ qkv, const bf16
 }
 
 // Backward: un-rotate the incoming gradient, then the per-head RMSNorm backward.
-__global__ void qk_norm_rope_bwd_kernel(const bf16* __restrict__ dq, const bf16* __restrict__ dk,
-                                        const bf16* __restrict__ dv, const bf16* __restrict__ qkv,
-                                        const bf16* __restrict__ qw, const bf16* __restrict__ kw,
-                                        const int* __restrict__ pos, int64_t pos_stride,
-                                        const float* __restrict__ inv_freq, const int* __restrict__ ax,
-                                        const float* __restrict__ rq, const float* __restrict__ rk,
-                                        bf16* __restrict__ dqkv, float* __restrict__ dqw, float* __restrict__ dkw,
-                                        int T, int nq, int nkv, int D) {
-  extern __shared__ float sw[];  // [2*D] partial weight grads (q then k)
+// One warp per (token, head) item, grid-stride over items.  Lane l owns elements l + 32 i of a head, so
+// the norm-weight gradient (sum over tokens and heads of g * xhat) accumulates in registers across the
+// warp's items and reaches shared memory once per warp and global memory once per block.
+template <int D>
+__global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(
+    const bf16* __restrict__ dq, const bf16* __restrict__ dk, const bf16* __restrict__ dv,
+    const bf16* __restrict__ qkv, const bf16* __restrict__ qw, const bf16* __restrict__ kw,
+    const int* __restrict__ pos, int64_t pos_stride, const float* __restrict__ inv_freq, const int* __restrict__ ax,
+    const float* __restrict__ rq, const float* __restrict__ rk, bf16* __restrict__ dqkv, float* __restrict__ dqw,
+    float* __restrict__ dkw, int T, int nq, int nkv) {
+  constexpr int HALF = D / 2;
+  constexpr int PER = (HALF + 31) / 32;  // pair slots per lane
+  __shared__ float sw[2 * D];            // q then k norm-weight gradient partials of this block
   for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) sw[i] = 0.f;
   __syncthreads();
   const int nh = nq + 2 * nkv;
   const int lane = threadIdx.x & 31;
-  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  bool return_early = false;
-  if (gw < static_cast<int64_t>(T) * nh) {
+  const bool norm = qw != nullptr;
+  float accq[2 * PER], acck[2 * PER];
+#pragma unroll
+  for (int i = 0; i < 2 * PER; ++i) accq[i] = acck[i] = 0.f;
+  const int64_t items = static_cast<int64_t>(T) * nh;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; gw < items; gw += nwarps) {
     const int t = static_cast<int>(gw / nh), h = static_cast<int>(gw % nh);
     bf16* out = dqkv + (static_cast<int64_t>(t) * nh + h) * D;
     if (h >= nq + nkv) {
       const bf16* g = dv + (static_cast<int64_t>(t) * nkv + (h - nq - nkv)) * D;
       for (int c = lane; c < D; c += 32) out[c] = g[c];
-    } else {
-      const bool is_q = h < nq;
-      const bf16* g = is_q ? dq + (static_cast<int64_t>(t) * nq + h) * D : dk + (static_cast<int64_t>(t) * nkv + h - nq) * D;
-      const bf16* x = qkv + (static_cast<int64_t>(t) * nh + h) * D;
-      const bf16* wt = is_q ? qw : kw;
-      const int half = D / 2;
-      if (wt == nullptr) {  // rotation only: the gradient is rotated back by the same angle
-        for (int j = lane; j < half; j += 32) {
-          const float p = static_cast<float>(pos[ax[j] * pos_stride + t]);
-          float s, c;
-          sincosf(p * inv_freq[j], &s, &c);
-          const float g1 = bf2f(g[j]), g2 = bf2f(g[j + half]);
-          out[j] = f2bf(g1 * c + g2 * s);
-          out[j + half] = f2bf(g2 * c - g1 * s);
+      continue;
+    }
+    const bool is_q = h < nq;
+    const bf16* g = is_q ? dq + (static_cast<int64_t>(t) * nq + h) * D : dk + (static_cast<int64_t>(t) * nkv + h - nq) * D;
+    const bf16* x = qkv + (static_cast<int64_t>(t) * nh + h) * D;
+    float n1[PER], n2[PER], xh1[PER], xh2[PER];
+    float dot = 0.f;
+    const float r = norm ? (is_q ? rq[static_cast<int64_t>(t) * nq + h] : rk[static_cast<int64_t>(t) * nkv + h - nq]) : 1.f;
+    const bf16* wt = is_q ? qw : kw;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int j = lane + 32 * i;
+      n1[i] = n2[i] = xh1[i] = xh2[i] = 0.f;
+      if (j < HALF) {
+        const float p = static_cast<float>(pos[ax[j] * pos_stride + t]);
+        float s, c;
+        sincosf(p * inv_freq[j], &s, &c);
+        const float g1 = bf2f(g[j]), g2 = bf2f(g[j + HALF]);
+        n1[i] = g1 * c + g2 * s;  // rotate back by the same angle
+        n2[i] = g2 * c - g1 * s;
+        if (norm) {
+          xh1[i] = bf2f(x[j]) * r;
+          xh2[i] = bf2f(x[j + HALF]) * r;
+          dot += n1[i] * bf2f(wt[j]) * xh1[i] + n2[i] * bf2f(wt[j + HALF]) * xh2[i];
         }
-        return_early = true;
       }
-      const float r = return_early ? 1.f : (is_q ? rq[static_cast<int64_t>(t) * nq + h] : rk[static_cast<int64_t>(t) * nkv + h - nq]);
-      float* swp = sw + (is_q ? 0 : D);
-      if (!return_early) {
-      // pass 1: dot = mean(gw * xhat)
-      float dot = 0.f;
-      for (int j = lane; j < half; j += 32) {
-        const float p = static_cast<float>(pos[ax[j] * pos_stride + t]);
-        float s, c;
-        sincosf(p * inv_freq[j], &s, &c);
-        const float g1 = bf2f(g[j]), g2 = bf2f(g[j + half]);
-        const float n1 = g1 * c + g2 * s, n2 = g2 * c - g1 * s;  // rotate by -angle
-        const float xh1 = bf2f(x[j]) * r, xh2 = bf2f(x[j + half]) * r;
-        dot += n1 * bf2f(wt[j]) * xh1 + n2 * bf2f(wt[j + half]) * xh2;
-        atomicAdd(&swp[j], n1 * xh1);
-        atomicAdd(&swp[j + half], n2 * xh2);
+    }
+    if (!norm) {
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int j = lane + 32 * i;
+        if (j < HALF) {
+          out[j] = f2bf(n1[i]);
+          out[j + HALF] = f2bf(n2[i]);
+        }
       }
-      dot = warp_sum(dot) / D;
-      for (int j = lane; j < half; j += 32) {
-        const float p = static_cast<float>(pos[ax[j] * pos_stride + t]);
-        float s, c;
-        sincosf(p * inv_freq[j], &s, &c);
-        const float g1 = bf2f(g[j]), g2 = bf2f(g[j + half]);
-        const float n1 = g1 * c + g2 * s, n2 = g2 * c - g1 * s;
-        const float xh1 = bf2f(x[j]) * r, xh2 = bf2f(x[j + half]) * r;
-        out[j] = f2bf(r * (n1 * bf2f(wt[j]) - xh1 * dot));
-        out[j + half] = f2bf(r * (n2 * bf2f(wt[j + half]) - xh2 * dot));
+      continue;
+    }
+    dot = warp_sum(dot) / D;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int j = lane + 32 * i;
+      if (j < HALF) {
+        out[j] = f2bf(r * (n1[i] * bf2f(wt[j]) - xh1[i] * dot));
+        out[j + HALF] = f2bf(r * (n2[i] * bf2f(wt[j + HALF]) - xh2[i] * dot));
+        float* acc = is_q ? accq : acck;
+        acc[2 * i] += n1[i] * xh1[i];
+        acc[2 * i + 1] += n2[i] * xh2[i];
       }
+    }
+  }
+  if (norm) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int j = lane + 32 * i;
+      if (j < HALF) {
+        atomicAdd(&sw[j], accq[2 * i]);
+        atomicAdd(&sw[j + HALF], accq[2 * i + 1]);
+        atomicAdd(&sw[D + j], acck[2 * i]);
+        atomicAdd(&sw[D + j + HALF], acck[2 * i + 1]);
       }
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) {
-    float* dst = i < D ? dqw : dkw;
-    if (dst) atomicAdd(&dst[i % D], sw[i]);
-  }
+  if (norm)
+    for (int i = threadIdx.x; i < 2 * D; i += blockDim.x) {
+      float* dst = i < D ? dqw : dkw;
+      if (dst) atomicAdd(&dst[i % D], sw[i]);
+    }
 }
 
 // Undefined or empty weight tensors select the rotation-only variant (no q/k RMSNorm).
@@ -374,13 +426,25 @@ void qk_norm_rope_bwd(at::Tensor dq, at::Tensor dk, at::Tensor dv, at::Tensor qk
   TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous(), "qk_norm_rope_bwd: contiguous grads");
   const c10::cuda::CUDAGuard g(qkv.device());
   const int64_t warps = static_cast<int64_t>(T) * (nq + 2 * nkv);
-  qk_norm_rope_bwd_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 2 * D * sizeof(float), cur_stream()>>>(
-      reinterpret_cast<const bf16*>(dq.data_ptr()), reinterpret_cast<const bf16*>(dk.data_ptr()),
-      reinterpret_cast<const bf16*>(dv.data_ptr()), reinterpret_cast<const bf16*>(qkv.data_ptr()), opt_bf16(qw),
-      opt_bf16(kw), pos.data_ptr<int>(),
-      pos.stride(0), inv_freq.data_ptr<float>(), ax.data_ptr<int>(), rq.data_ptr<float>(), rk.data_ptr<float>(),
-      reinterpret_cast<bf16*>(dqkv.data_ptr()), dqw.defined() && dqw.numel() ? dqw.data_ptr<float>() : nullptr,
-      dkw.defined() && dkw.numel() ? dkw.data_ptr<float>() : nullptr, T, static_cast<int>(nq), static_cast<int>(nkv), D);
+  // enough warps to fill the GPU a few times; each loops over items so weight partials stay in registers
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((warps + 7) / 8, num_sms(qkv.device().index()) * 8)));
+  auto args = [&](auto kern) {
+    kern<<<blocks, 256, 0, cur_stream()>>>(
+        reinterpret_cast<const bf16*>(dq.data_ptr()), reinterpret_cast<const bf16*>(dk.data_ptr()),
+        reinterpret_cast<const bf16*>(dv.data_ptr()), reinterpret_cast<const bf16*>(qkv.data_ptr()), opt_bf16(qw),
+        opt_bf16(kw), pos.data_ptr<int>(), pos.stride(0), inv_freq.data_ptr<float>(), ax.data_ptr<int>(),
+        rq.data_ptr<float>(), rk.data_ptr<float>(), reinterpret_cast<bf16*>(dqkv.data_ptr()),
+        dqw.defined() && dqw.numel() ? dqw.data_ptr<float>() : nullptr,
+        dkw.defined() && dkw.numel() ? dkw.data_ptr<float>() : nullptr, T, static_cast<int>(nq), static_cast<int>(nkv));
+  };
+  switch (D) {
+    case 32: args(qk_norm_rope_bwd_kernel<32>); break;
+    case 64: args(qk_norm_rope_bwd_kernel<64>); break;
+    case 80: args(qk_norm_rope_bwd_kernel<80>); break;
+    case 128: args(qk_norm_rope_bwd_kernel<128>); break;
+    case 256: args(qk_norm_rope_bwd_kernel<256>); break;
+    default: TORCH_CHECK(false, "qk_norm_rope_bwd: unsupported head_dim ", D);
+  }
   VLM_LAUNCHED();
 }
 
@@ -564,6 +628,52 @@ __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
   }
 }
 
+// Same update, 8 elements per thread with 128-bit loads and stores (the parameter units are padded to
+// multiples of 128 elements, so every unit takes this path).
+__global__ void __launch_bounds__(256) adamw_vec8_kernel(float* __restrict__ p, const float* __restrict__ g,
+                                                         float* __restrict__ m, float* __restrict__ v,
+                                                         bf16* __restrict__ ph, const float* __restrict__ scale_ptr,
+                                                         int64_t n8, float lr, float b1, float b2, float eps, float wd,
+                                                         float bc1, float bc2) {
+  const float scale = *scale_ptr;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float pv[8], gv[8], mv[8], vv[8];
+    const float4* p4 = reinterpret_cast<const float4*>(p) + 2 * i;
+    const float4* g4 = reinterpret_cast<const float4*>(g) + 2 * i;
+    const float4* m4 = reinterpret_cast<const float4*>(m) + 2 * i;
+    const float4* v4 = reinterpret_cast<const float4*>(v) + 2 * i;
+    *reinterpret_cast<float4*>(pv) = p4[0];
+    *reinterpret_cast<float4*>(pv + 4) = p4[1];
+    *reinterpret_cast<float4*>(gv) = g4[0];
+    *reinterpret_cast<float4*>(gv + 4) = g4[1];
+    *reinterpret_cast<float4*>(mv) = m4[0];
+    *reinterpret_cast<float4*>(mv + 4) = m4[1];
+    *reinterpret_cast<float4*>(vv) = v4[0];
+    *reinterpret_cast<float4*>(vv + 4) = v4[1];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float gi = gv[j] * scale;
+      mv[j] = b1 * mv[j] + (1.f - b1) * gi;
+      vv[j] = b2 * vv[j] + (1.f - b2) * gi * gi;
+      const float upd = (mv[j] / bc1) / (sqrtf(vv[j] / bc2) + eps) + wd * pv[j];
+      pv[j] = pv[j] - lr * upd;
+    }
+    float4* po = reinterpret_cast<float4*>(p) + 2 * i;
+    float4* mo = reinterpret_cast<float4*>(m) + 2 * i;
+    float4* vo = reinterpret_cast<float4*>(v) + 2 * i;
+    po[0] = *reinterpret_cast<float4*>(pv);
+    po[1] = *reinterpret_cast<float4*>(pv + 4);
+    mo[0] = *reinterpret_cast<float4*>(mv);
+    mo[1] = *reinterpret_cast<float4*>(mv + 4);
+    vo[0] = *reinterpret_cast<float4*>(vv);
+    vo[1] = *reinterpret_cast<float4*>(vv + 4);
+    if (ph)
+      reinterpret_cast<uint4*>(ph)[i] = make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]),
+                                                   pack_bf16x2(pv[4], pv[5]), pack_bf16x2(pv[6], pv[7]));
+  }
+}
+
 void adamw(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor ph, at::Tensor scale, double lr, double b1,
            double b2, double eps, double wd, int64_t step) {
   const int64_t n = p.numel();
@@ -573,6 +683,19 @@ void adamw(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor ph
   const c10::cuda::CUDAGuard gd(p.device());
   const float bc1 = static_cast<float>(1.0 - std::pow(b1, static_cast<double>(step)));
   const float bc2 = static_cast<float>(1.0 - std::pow(b2, static_cast<double>(step)));
+  auto aligned = [](const at::Tensor& t) { return reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0; };
+  const bool has_ph = ph.defined() && ph.numel();
+  if (n % 8 == 0 && aligned(p) && aligned(g) && aligned(m) && aligned(v) && (!has_ph || aligned(ph)) &&
+      m.is_contiguous() && v.is_contiguous() && (!has_ph || ph.is_contiguous())) {
+    const int blocks = static_cast<int>(std::min<int64_t>((n / 8 + 255) / 256, num_sms(p.device().index()) * 8));
+    adamw_vec8_kernel<<<blocks, 256, 0, cur_stream()>>>(
+        p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+        has_ph ? reinterpret_cast<bf16*>(ph.data_ptr()) : nullptr, scale.data_ptr<float>(), n / 8,
+        static_cast<float>(lr), static_cast<float>(b1), static_cast<float>(b2), static_cast<float>(eps),
+        static_cast<float>(wd), bc1, bc2);
+    VLM_LAUNCHED();
+    return;
+  }
   const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, num_sms(p.device().index()) * 8));
   adamw_kernel<<<blocks, 256, 0, cur_stream()>>>(p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(),
                                                  v.data_ptr<float>(),

@@ -26,7 +26,11 @@
 
 namespace vlm {
 
-enum Epi : int { EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GELU_TANH = 2, EPI_GELU_ERF = 3, EPI_VOCAB_STATS = 4, EPI_VOCAB_GRAD = 5 };
+enum Epi : int {
+  EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GELU_TANH = 2, EPI_GELU_ERF = 3, EPI_VOCAB_STATS = 4, EPI_VOCAB_GRAD = 5,
+  // D [M, 2N] = SwiGLU backward of the product (= dL/d act) with aux = the forward's interleaved (gate, up)
+  EPI_SWIGLU_BWD = 6
+};
 
 struct GemmParams {
   int M, N, K;
@@ -142,6 +146,37 @@ VLM_DEV void epilogue_chunk(const GemmParams& p, int row, int col, const uint32_
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
   const int ncols = min(16, p.N - col);
   const bool full = ncols == 16;
+  if (p.epi == EPI_SWIGLU_BWD) {
+    // v = dL/d act for columns [col, col+16); aux row holds (gate, up) pairs at 2c, 2c+1.  d act is rounded to
+    // bf16 first, like the unfused bf16 GEMM followed by the elementwise backward.
+    const __nv_bfloat16* pre = p.aux + static_cast<long long>(row) * p.ld_aux + 2 * col;
+    __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(p.D) + static_cast<long long>(row) * p.ldd + 2 * col;
+    if (full) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 g4 = reinterpret_cast<const uint4*>(pre)[q];
+        const uint32_t w[4] = {g4.x, g4.y, g4.z, g4.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 gu = unpack_bf16x2(w[j]);
+          const float s = 1.f / (1.f + __expf(-gu.x));
+          const float da = bf2f(f2bf(v[4 * q + j]));
+          o[j] = pack_bf16x2(da * gu.y * s * (1.f + gu.x * (1.f - s)), da * gu.x * s);
+        }
+        reinterpret_cast<uint4*>(d)[q] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    } else {
+      for (int i = 0; i < ncols; ++i) {
+        const float g = bf2f(pre[2 * i]), u = bf2f(pre[2 * i + 1]);
+        const float s = 1.f / (1.f + __expf(-g));
+        const float da = bf2f(f2bf(v[i]));
+        d[2 * i] = f2bf(da * u * s * (1.f + g * (1.f - s)));
+        d[2 * i + 1] = f2bf(da * g * s);
+      }
+    }
+    return;
+  }
   if (p.epi == EPI_SWIGLU) {
     if (p.aux) {
       __nv_bfloat16* a = p.aux + static_cast<long long>(row) * p.ld_aux + col;
@@ -598,7 +633,10 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   if (!is_stats) {
     TORCH_CHECK(d_f32 || D.scalar_type() == at::kBFloat16, "gemm: output must be bf16 or fp32");
     TORCH_CHECK(!accumulate || d_f32, "gemm: accumulate needs an fp32 output");
-    TORCH_CHECK(D.size(0) == M && D.size(1) == (epi == EPI_SWIGLU ? N / 2 : N), "gemm: output shape mismatch");
+    TORCH_CHECK(D.size(0) == M && D.size(1) == (epi == EPI_SWIGLU ? N / 2 : epi == EPI_SWIGLU_BWD ? 2 * N : N),
+                "gemm: output shape mismatch");
+    TORCH_CHECK(epi != EPI_SWIGLU_BWD || (aux.defined() && D.scalar_type() == at::kBFloat16 && !accumulate),
+                "gemm: the SwiGLU-backward epilogue needs the forward's (gate, up) as aux and a bf16 output");
     TORCH_CHECK(D.stride(0) % 8 == 0, "gemm: output leading stride must be a multiple of 8");
   }
 
@@ -636,8 +674,8 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
     p.ldr = residual.stride(0);
   }
   if (aux.defined() && aux.numel()) {
-    TORCH_CHECK(aux.scalar_type() == at::kBFloat16 && aux.stride(1) == 1 && aux.size(0) == M && aux.size(1) == N &&
-                    aux.stride(0) % 8 == 0,
+    TORCH_CHECK(aux.scalar_type() == at::kBFloat16 && aux.stride(1) == 1 && aux.size(0) == M &&
+                    aux.size(1) == (epi == EPI_SWIGLU_BWD ? 2 * N : N) && aux.stride(0) % 8 == 0,
                 "gemm: bad aux");
     p.aux = reinterpret_cast<__nv_bfloat16*>(aux.data_ptr());
     p.ld_aux = aux.stride(0);
@@ -713,7 +751,8 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
 
 void gemm(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux, bool a_kmajor,
           bool b_kmajor, double alpha, int64_t epi, bool accumulate) {
-  TORCH_CHECK(epi >= EPI_STORE && epi <= EPI_GELU_ERF, "gemm: epilogue code ", epi, " is internal");
+  TORCH_CHECK((epi >= EPI_STORE && epi <= EPI_GELU_ERF) || epi == EPI_SWIGLU_BWD, "gemm: epilogue code ", epi,
+              " is internal");
   gemm_ex(A, B, D, bias, residual, aux, a_kmajor, b_kmajor, alpha, epi, accumulate, nullptr, 0, nullptr, nullptr);
 }
 

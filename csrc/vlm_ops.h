@@ -40,7 +40,8 @@ at::Tensor dec_swiglu(at::Tensor ws, std::vector<int64_t> meta);
 
 // elementwise.cu
 void rms_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps);
-void rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor dx, at::Tensor dw);
+void rms_norm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd, at::Tensor dx, at::Tensor dw,
+                  at::Tensor add);
 void layer_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor b, at::Tensor y, double eps);
 void qk_norm_rope_fwd(at::Tensor qkv, at::Tensor qw, at::Tensor kw, at::Tensor pos, at::Tensor inv_freq, at::Tensor ax,
                       at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor rq, at::Tensor rk, int64_t nq, int64_t nkv,

@@ -138,6 +138,32 @@ def test_qk_norm_rope(D, nq, nkv):
     _close(dkw, dkwr, rtol=1e-3, atol=1e-2, name="dkw")
 
 
+@pytest.mark.parametrize("T,norm", [(5111, True), (300, False), (4000, False)])
+def test_qk_rope_bwd_large_and_rotation_only(T, norm):
+    """Many items per warp (grid-stride weight-gradient accumulation) and the no-q/k-norm variant."""
+    D, nq, nkv = 128, 32, 8
+    qkv = _r(T, (nq + 2 * nkv) * D, seed=70)
+    qw, kw = ((1 + 0.1 * _r(D, seed=71).float()).bfloat16(), (1 + 0.1 * _r(D, seed=72).float()).bfloat16()) \
+        if norm else (None, None)
+    pos = torch.randint(0, 2000, (3, T), device=DEV, dtype=torch.int32)
+    rope = ops.RopeCfg(D, 1e6, (24, 20, 20) if norm else (16, 24, 24), norm)
+    q, k, v, rq, rk = ops.qk_norm_rope(qkv, qw, kw, pos, rope, n_q=nq, n_kv=nkv, eps=1e-6)
+    qr, kr, vr, rqr, rkr = ref.qk_norm_rope(qkv, qw, kw, pos, n_q=nq, n_kv=nkv, head_dim=D, theta=1e6,
+                                            section=rope.section, interleaved=norm, eps=1e-6)
+    _close(q, qr, name="q")
+    _close(k, kr, name="k")
+    dq, dk, dv = _r(T, nq, D, seed=73), _r(T, nkv, D, seed=74), _r(T, nkv, D, seed=75)
+    dqw, dkw = torch.zeros(D, device=DEV), torch.zeros(D, device=DEV)
+    dqkv = ops.qk_norm_rope_bwd(dq, dk, dv, qkv, qw, kw, pos, rq, rk, rope, n_q=nq, n_kv=nkv, eps=1e-6,
+                                dqw_accum=dqw if norm else None, dkw_accum=dkw if norm else None)
+    dref, dqwr, dkwr = ref.qk_norm_rope_bwd(dq, dk, dv, qkv, qw, kw, pos, rqr, rkr, n_q=nq, n_kv=nkv, head_dim=D,
+                                            theta=1e6, section=rope.section, interleaved=norm, eps=1e-6)
+    _close(dqkv, dref, name="dqkv")
+    if norm:
+        torch.testing.assert_close(dqw, dqwr.float(), rtol=2e-3, atol=2e-1)
+        torch.testing.assert_close(dkw, dkwr.float(), rtol=2e-3, atol=2e-1)
+
+
 @pytest.mark.parametrize("D,Hq,Hkv,causal", [(128, 8, 2, True), (64, 4, 4, False), (32, 4, 2, True), (16, 4, 4, False)])
 def test_flash_attn(D, Hq, Hkv, causal):
     lens = [1, 63, 64, 130, 388, 17]
@@ -328,3 +354,42 @@ def test_adamw_and_sqnorm():
     torch.testing.assert_close(p.cpu(), p2, atol=1e-6, rtol=1e-5)
     s = ops.sq_norm(g)
     torch.testing.assert_close(s.cpu()[0], (g2 ** 2).sum(), rtol=1e-4, atol=1e-3)
+
+
+def test_down_dgrad_with_fused_swiglu_backward():
+    """The SwiGLU-backward GEMM epilogue equals dgrad followed by the elementwise backward."""
+    M, H, F = 777, 512, 1536
+    dy, w = _r(M, H, seed=80), _r(H, F, scale=0.05, seed=81)
+    pre = _r(M, 2 * F, seed=82)
+    fused = ops.grad_input_swiglu(dy, w, pre)
+    unfused = ops.swiglu_bwd(ops.grad_input(dy, w), pre)
+    torch.testing.assert_close(fused.float(), unfused.float(), atol=1e-2, rtol=1e-2)
+    exp = ref.swiglu_bwd(ref.gemm(dy, w, b_kmajor=False, out_dtype=torch.float32).bfloat16(), pre)
+    _close(fused, exp, name="dpre")
+
+
+def test_adamw_vectorised_matches_oracle():
+    n = 1000 * 128
+    p, g = _r(n, seed=83).float(), _r(n, seed=84).float()
+    m, v = _r(n, seed=85).float() * 0.1, _r(n, seed=86).float().abs() * 0.01
+    ph = torch.empty(n, dtype=torch.bfloat16, device=DEV)
+    pr, mr, vr = p.clone(), m.clone(), v.clone()
+    ops.adamw_(p, g, m, v, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=3, grad_scale=0.5,
+               p_half=ph)
+    ref.adamw_(pr, g, mr, vr, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=3, grad_scale=0.5)
+    torch.testing.assert_close(p, pr, atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(m, mr, atol=1e-6, rtol=1e-5)
+    torch.testing.assert_close(v, vr, atol=1e-7, rtol=1e-5)
+    assert torch.equal(ph, p.bfloat16())
+
+
+@pytest.mark.parametrize("M,H", [(5111, 2560), (37, 4096), (1, 128)])
+def test_rms_norm_bwd_weight_grad_and_residual_add(M, H):
+    x, dy, w = _r(M, H, seed=90), _r(M, H, seed=91), (1 + 0.1 * _r(H, seed=92).float()).bfloat16()
+    add = _r(M, H, seed=93)
+    y, rstd = ops.rms_norm(x, w, 1e-6)
+    dw = torch.zeros(H, device=DEV)
+    dx = ops.rms_norm_bwd(dy, x, w, rstd, dw_accum=dw, add=add)
+    dxr, dwr = ref.rms_norm_bwd(dy, x, w, rstd)
+    _close(dx, (dxr.float() + add.float()), name="dx+add")
+    torch.testing.assert_close(dw, dwr.float(), rtol=2e-3, atol=5e-2)

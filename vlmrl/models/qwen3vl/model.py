@@ -232,13 +232,12 @@ class TextDecoder:
         # MLP
         if g is not None:
             ops.grad_weight(dy, c.act, accumulate=g["down_w"])
-        d_act = ops.grad_input(dy, w["down_w"], out_dtype=dt)
-        d_pre = ops.swiglu_bwd(d_act, c.pre)
+        d_pre = ops.grad_input_swiglu(dy, w["down_w"], c.pre)
         if g is not None:
             ops.grad_weight(d_pre, c.hn, accumulate=g["gu_w"])
         d_hn = ops.grad_input(d_pre, w["gu_w"], out_dtype=dt)
-        d_h1 = ops.rms_norm_bwd(d_hn, c.h1, w["post_norm"], c.r2, dw_accum=None if g is None else g["post_norm"])
-        d_h1 = (d_h1.float() + dy.float()).to(dt)
+        d_h1 = ops.rms_norm_bwd(d_hn, c.h1, w["post_norm"], c.r2, dw_accum=None if g is None else g["post_norm"],
+                                add=dy)
         # attention
         o2 = c.o.reshape(T, self.nq * self.D)
         if g is not None:
@@ -254,8 +253,8 @@ class TextDecoder:
             ops.grad_weight(d_qkv, c.xn, accumulate=g["qkv_w"])
             g["qkv_b"].add_(d_qkv.float().sum(0))
         d_xn = ops.grad_input(d_qkv, w["qkv_w"], out_dtype=dt)
-        dx = ops.rms_norm_bwd(d_xn, c.x, w["input_norm"], c.r1, dw_accum=None if g is None else g["input_norm"])
-        return (dx.float() + d_h1.float()).to(dt)
+        return ops.rms_norm_bwd(d_xn, c.x, w["input_norm"], c.r1, dw_accum=None if g is None else g["input_norm"],
+                                add=d_h1)
 
     # ---------------------------------------------------------------- full passes
     def hidden_states(self, params, batch: PackedBatch, *, save: bool = False, ctx: Optional[TrainCtx] = None,

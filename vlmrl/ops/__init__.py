@@ -20,6 +20,7 @@ from vlmrl.ops._ext import ext, has_ext
 # GEMM epilogue codes (must match csrc/gemm_sm100.cu)
 EPI_STORE = 0
 EPI_SWIGLU = 1
+EPI_SWIGLU_BWD = 6
 EPI_GELU_TANH = 2
 EPI_GELU_ERF = 3
 
@@ -148,6 +149,20 @@ def grad_input(dy: torch.Tensor, w: torch.Tensor, out_dtype=torch.bfloat16, out=
     return gemm(dy, w, b_kmajor=False, out_dtype=out_dtype, out=out)
 
 
+def grad_input_swiglu(dy: torch.Tensor, w_down: torch.Tensor, pre: torch.Tensor):
+    """d pre [M, 2F] (interleaved gate/up) of ``act = silu(gate) * up`` given dL/d(act @ w_down.T) = dy.
+
+    On the GPU the down-projection dgrad GEMM applies the SwiGLU backward in its epilogue, so dL/d act is
+    never written to memory.
+    """
+    if not _cuda(dy):
+        return swiglu_bwd(grad_input(dy, w_down, out_dtype=dy.dtype), pre)
+    M, F = dy.shape[0], w_down.shape[1]
+    out = torch.empty(M, 2 * F, dtype=torch.bfloat16, device=dy.device)
+    ext().gemm(dy, w_down, out, torch.Tensor(), torch.Tensor(), pre, True, False, 1.0, EPI_SWIGLU_BWD, False)
+    return out
+
+
 def grad_weight(dy: torch.Tensor, x: torch.Tensor, accumulate: Optional[torch.Tensor] = None,
                 out_dtype=torch.float32):
     """dW [N,K] (+)= dY[M,N]ᵀ @ X[M,K] (fp32 accumulation buffer)."""
@@ -172,15 +187,18 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> Tuple[torch.Tensor
     return y, rstd
 
 
-def rms_norm_bwd(dy, x, w, rstd, dw_accum: Optional[torch.Tensor] = None):
-    """Returns dx; adds the weight gradient into ``dw_accum`` (fp32 [H]) when given."""
+def rms_norm_bwd(dy, x, w, rstd, dw_accum: Optional[torch.Tensor] = None, add: Optional[torch.Tensor] = None):
+    """Returns dx (+ ``add``, a second gradient of the same tensor, summed before rounding); adds the weight
+    gradient into ``dw_accum`` (fp32 [H]) when given."""
     if not _cuda(x):
         dx, dw = ref.rms_norm_bwd(dy, x, w, rstd)
         if dw_accum is not None:
             dw_accum.add_(dw.to(dw_accum.dtype))
+        if add is not None:
+            dx = (dx.float() + add.float()).to(dx.dtype)
         return dx
     dx = torch.empty_like(x)
-    ext().rms_norm_bwd(dy, x, w, rstd, dx, _opt(dw_accum))
+    ext().rms_norm_bwd(dy, x, w, rstd, dx, _opt(dw_accum), _opt(add))
     return dx
 
 
