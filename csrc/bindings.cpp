@@ -45,7 +45,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_view", &vlm::symm_view);
   m.def("rs_pull", &vlm::rs_pull, "reduce-scatter by pulling shards from peer memory");
   m.def("adamw_push", &vlm::adamw_push, "sharded AdamW storing bf16 params into every rank's gathered buffer");
-  m.def("peer_wait", &vlm::peer_wait);
+  m.def("peer_wait", &vlm::peer_wait, py::arg("local_sig"), py::arg("slot"), py::arg("target"), py::arg("rank"),
+        py::arg("world"), py::arg("device"), py::arg("budget_cycles") = 0);
   m.def("peer_barrier", &vlm::peer_barrier);
   m.def("read_and_clear_error", &vlm::read_and_clear_error);
   m.def("launch_count", &vlm::launch_count, "kernel launches issued by this library so far");

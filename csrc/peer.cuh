@@ -35,13 +35,13 @@ VLM_DEV unsigned long long load_acquire_sys(const unsigned long long* addr) {
 
 // Wait until sig[base + p] >= target for every peer p != rank.  Called by one thread.
 VLM_DEV bool wait_peers_at(const unsigned long long* sig, int64_t base, int W, int rank, unsigned long long target,
-                           int* err) {
+                           int* err, long long budget = kPeerWait) {
   const long long t0 = clock64();
   for (int p = 0; p < W; ++p) {
     if (p == rank) continue;
     const unsigned long long* a = sig + base + p;
     while (load_acquire_sys(a) < target) {
-      if (clock64() - t0 > kPeerWait) {
+      if (clock64() - t0 > budget) {
         atomicCAS(err, 0, kErrTimeoutPeer);
         return false;
       }

@@ -147,8 +147,8 @@ __global__ void __launch_bounds__(256) adamw_push_kernel(float* __restrict__ p, 
 }
 
 __global__ void peer_wait_kernel(const unsigned long long* sig, int slot, unsigned long long target, int rank, int W,
-                                 int* err) {
-  if (threadIdx.x == 0) wait_peers(sig, slot, W, rank, target, err);
+                                 int* err, long long budget) {
+  if (threadIdx.x == 0) wait_peers_at(sig, static_cast<int64_t>(slot) * W, W, rank, target, err, budget);
 }
 
 // Every rank signals slot `slot` with `epoch` and waits for all peers to reach it (a device-side barrier).
@@ -259,12 +259,14 @@ int64_t adamw_push(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, std::
   return grid;
 }
 
-void peer_wait(int64_t local_sig, int64_t slot, int64_t target, int64_t rank, int64_t world, int64_t device) {
+// budget_cycles <= 0 selects the default (kPeerWait); tests pass a short budget to exercise the timeout.
+void peer_wait(int64_t local_sig, int64_t slot, int64_t target, int64_t rank, int64_t world, int64_t device,
+               int64_t budget_cycles) {
   const c10::cuda::CUDAGuard g(static_cast<c10::DeviceIndex>(device));
   peer_wait_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const unsigned long long*>(local_sig), static_cast<int>(slot),
       static_cast<unsigned long long>(target), static_cast<int>(rank), static_cast<int>(world),
-      err_word(static_cast<int>(device)));
+      err_word(static_cast<int>(device)), budget_cycles > 0 ? budget_cycles : kPeerWait);
   VLM_LAUNCHED();
 }
 

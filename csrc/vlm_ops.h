@@ -97,7 +97,8 @@ void rs_pull(std::vector<int64_t> bufs, int64_t unit_off_bytes, int64_t shard_of
 int64_t adamw_push(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, std::vector<int64_t> dst,
                    int64_t dst_off_bytes, at::Tensor scale, double lr, double b1, double b2, double eps, double wd,
                    int64_t step, std::vector<int64_t> sigs, int64_t slot, int64_t rank);
-void peer_wait(int64_t local_sig, int64_t slot, int64_t target, int64_t rank, int64_t world, int64_t device);
+void peer_wait(int64_t local_sig, int64_t slot, int64_t target, int64_t rank, int64_t world, int64_t device,
+               int64_t budget_cycles);
 void peer_barrier(std::vector<int64_t> sigs, int64_t slot, int64_t epoch, int64_t rank, int64_t device);
 
 // host_utils.cu

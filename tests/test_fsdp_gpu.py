@@ -55,6 +55,9 @@ def _worker(rank, world, port, out_path):
                     g.copy_(torch.randn(g.shape, generator=gen, device=dev) * 1e-2)
                     fp.grad_done(u)
             opt.step(step)
+            if comm == "p2p":
+                ops.check_errors(rank)
+                fp.verify_signals()          # every peer counter exactly where the protocol puts it
         ops.check_errors(rank)
         gathered = {u: fp.get(u).float().clone() for u in fp.order}
         master = opt.master_units()

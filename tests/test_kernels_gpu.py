@@ -393,3 +393,18 @@ def test_rms_norm_bwd_weight_grad_and_residual_add(M, H):
     dxr, dwr = ref.rms_norm_bwd(dy, x, w, rstd)
     _close(dx, (dxr.float() + add.float()), name="dx+add")
     torch.testing.assert_close(dw, dwr.float(), rtol=2e-3, atol=5e-2)
+
+
+def test_bounded_peer_wait_reports_timeout_and_context_survives():
+    """A flag that nothing ever sets: the wait gives up after its (short) budget, the host gets a
+    CollectiveTimeout, and the GPU keeps working."""
+    from vlmrl.ops import CollectiveTimeout
+    from vlmrl.ops._ext import ext
+
+    sig = torch.zeros(4, dtype=torch.int64, device=DEV)          # slot 0, world 2: peer 1's counter stays 0
+    ext().peer_wait(sig.data_ptr(), 0, 1, 0, 2, torch.cuda.current_device(), 2_000_000)   # ~1 ms budget
+    with pytest.raises(CollectiveTimeout):
+        ops.check_errors()
+    x = _r(256, 256, seed=99)
+    _close(ops.gemm(x, x), ref.gemm(x, x, out_dtype=torch.float32), name="after timeout")
+    _no_device_error()

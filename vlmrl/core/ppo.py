@@ -30,6 +30,7 @@ from vlmrl.core.minibatch import minibatch_indices
 from vlmrl.core.rollout import EpisodeBatch, collect_episodes
 from vlmrl.core.types import Rollout, SamplingConfig
 from vlmrl.models.qwen3vl.model import PackedBatch
+from vlmrl.utils.profiling import phase
 
 
 @dataclass
@@ -226,13 +227,14 @@ def update(ts, cr: CollectResult, cfg: TrainerConfig, *, ref_model=None, kl_ctrl
     mbs = cr.minibatches
     use_policy_old = cfg.old_logprob_source == "policy"
     reuse_first = use_policy_old and cfg.ppo_epochs == 1
-    for i, mb in enumerate(mbs):
-        if not use_policy_old:
-            mb.old_lp = mb.sampler_lp
-        elif not (reuse_first and i == 0):
-            mb.old_lp = score(model, mb)
-        if ref_model is not None and cfg.kl_ref_coef > 0:
-            mb.ref_lp = score(ref_model, mb)
+    with phase("score"):
+        for i, mb in enumerate(mbs):
+            if not use_policy_old:
+                mb.old_lp = mb.sampler_lp
+            elif not (reuse_first and i == 0):
+                mb.old_lp = score(model, mb)
+            if ref_model is not None and cfg.kl_ref_coef > 0:
+                mb.ref_lp = score(ref_model, mb)
     coef = float(cfg.kl_coef if kl_coef is None else kl_coef)
     sums: Dict[str, torch.Tensor] = {}
     n = 0
@@ -257,7 +259,8 @@ def update(ts, cr: CollectResult, cfg: TrainerConfig, *, ref_model=None, kl_ctrl
             with torch.no_grad():
                 model.backward(ctx, g_lp, g_ent)
             del ctx
-            m.update(ts.apply_gradients())
+            with phase("optimizer"):
+                m.update(ts.apply_gradients())
             if kl_ctrl is not None:
                 coef = kl_ctrl.update(float(m["approx_kl"]), coef)
             for k, v in m.items():

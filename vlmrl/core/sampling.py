@@ -26,6 +26,7 @@ from vlmrl import ops
 from vlmrl.core.batching import pack_prompts
 from vlmrl.core.types import SampleResult, SamplingConfig, VLMInputs
 from vlmrl.models.qwen3vl.model import KVCache, VisionEmbeddings
+from vlmrl.utils.profiling import phase
 
 
 class _DecodeState:
@@ -130,7 +131,8 @@ class Generator:
         st.out_lp.zero_()
         st.deltas.copy_(torch.from_numpy(np.repeat(deltas, gs)))
         st.seed.fill_(int(seed) & ((1 << 63) - 1))
-        logits = m.prefill(batch, st.cache, torch.arange(G, device=m.device) * gs)
+        with phase("prefill"):
+            logits = m.prefill(batch, st.cache, torch.arange(G, device=m.device) * gs)
         if gs > 1:
             L = st.cache.keys.shape[0]
             for buf in (st.cache.keys, st.cache.values):
@@ -155,8 +157,9 @@ class Generator:
                 ev0 = torch.cuda.Event(enable_timing=True)
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev0.record()
-                for _ in range(steps):
-                    st.graph.replay()
+                with phase("decode"):
+                    for _ in range(steps):
+                        st.graph.replay()
                 ev1.record()
                 self._pending_decode = (ev0, ev1)
                 self.graph_kernel_launches += steps * st.graph_kernels

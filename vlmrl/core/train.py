@@ -252,12 +252,18 @@ def maybe_resume(trainer, resume_path: str, rank: int = 0) -> int:
         if rank == 0:
             print(f"[train] Resume path not found: {resume_path}")
         return 0
-    data = Checkpoint(resume_path, parallel=False).load_as_dict()
-    state = data.get("train_state", data)
-    trainer.ts.load(state)
+    try:
+        data = Checkpoint(resume_path, parallel=False).load_as_dict()
+        state = data.get("train_state", data)
+        trainer.ts.load(state)
+    except Exception as exc:  # unreadable or mismatched checkpoint: start fresh, as the reference does
+        if rank == 0:
+            print(f"[train] Failed to resume from {resume_path}: {exc}")
+        return 0
     meta = data.get("metadata") or {}
     it = int(meta.get("step", trainer.ts.step - 1))
     trainer.iteration = it
+    trainer.restore_state(meta.get("trainer"))
     if rank == 0:
         print(f"[train] Resumed state from {resume_path} at iteration {it}")
     return it
@@ -276,7 +282,7 @@ def maybe_save(trainer, save_dir: str, step: int, rank: int = 0) -> Optional[str
     path = os.path.join(save_dir, "train_state.pkl")
     cp = Checkpoint(path, parallel=False)
     cp.train_state = state
-    cp.metadata = {"step": int(step)}
+    cp.metadata = {"step": int(step), "trainer": trainer.state_dict()}
     cp.save()
     return path
 
@@ -331,6 +337,10 @@ def main(argv: Optional[Sequence[str]] = None) -> int:
     if rank == 0:
         print(f"[train] Loading model from {args.model_dir or args.preset}")
     trainer = build_trainer(args, device, rank, world)
+    if world > 1:
+        from vlmrl.parallel.watchdog import Heartbeat
+
+        trainer.watchdog = Heartbeat()
     start = maybe_resume(trainer, str(args.resume_path or ""), rank)
     logger = None
     if rank == 0:
@@ -361,7 +371,12 @@ def main(argv: Optional[Sequence[str]] = None) -> int:
     if world > 1:
         import torch.distributed as dist
 
+        trainer.watchdog.stop(leaving=True)
         dist.barrier()
+        trainer.close()
+        close = getattr(trainer.model.params, "close", None)
+        if close is not None:
+            close()
         dist.destroy_process_group()
     return 0
 

@@ -26,31 +26,9 @@ from vlmrl.core.kl import AdaptiveKL
 from vlmrl.core.optim import AdamWConfig
 from vlmrl.core.ppo import TrainerConfig, collect, update
 from vlmrl.core.sampling import Generator
+from vlmrl.utils.profiling import PhaseTimer, phase
 from vlmrl.utils.rng import RngSeq, fold_in
 from vlmrl.utils.train_state import TrainState
-
-
-class _Timer:
-    def __init__(self, device):
-        self.cuda = device.type == "cuda"
-        self.marks = []
-
-    def mark(self, name):
-        if self.cuda:
-            e = torch.cuda.Event(enable_timing=True)
-            e.record()
-            self.marks.append((name, e))
-        else:
-            self.marks.append((name, time.perf_counter()))
-
-    def spans(self) -> Dict[str, float]:
-        out = {}
-        if self.cuda and self.marks:
-            self.marks[-1][1].synchronize()
-        for (a, ta), (b, tb) in zip(self.marks, self.marks[1:]):
-            ms = ta.elapsed_time(tb) if self.cuda else (tb - ta) * 1e3
-            out[f"time/{b}_ms"] = ms
-        return out
 
 
 class GRPOTrainer:
@@ -82,6 +60,7 @@ class GRPOTrainer:
         self.iteration = 0
         self.last_collect = None
         self.last_infos: Dict[str, Any] = {}
+        self.watchdog = None   # vlmrl.parallel.watchdog.Heartbeat: checked before every step
 
     @property
     def groups_per_rank(self) -> int:
@@ -96,26 +75,47 @@ class GRPOTrainer:
             self.tp.close()
             self.tp = None
 
+    def state_dict(self) -> Dict[str, Any]:
+        """Host state a resumed run needs besides the train state: RNG, dataset cursor, adaptive KL."""
+        return {"rng": self.rng.state(), "cursor": int(self.cursor), "iteration": int(self.iteration),
+                "kl_coef": float(self.kl_coef)}
+
+    def restore_state(self, state: Optional[Dict[str, Any]]) -> None:
+        if not state:
+            return
+        self.rng.set_state(state["rng"])
+        self.cursor = int(state.get("cursor", self.cursor))
+        self.iteration = int(state.get("iteration", self.iteration))
+        self.kl_coef = float(state.get("kl_coef", self.kl_coef))
+
+    def _collect(self, seed: int, G: int):
+        cfg = self.cfg
+        if self.tp is not None:   # every rank rolls out all groups, then keeps its share for training
+            return collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G * self.world, rng=seed,
+                           eos_id=self.eos_id, generator=self.generator, task_offset=self.cursor, row_offset=0,
+                           keep_groups=(self.rank * G, (self.rank + 1) * G))
+        return collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G, rng=seed, eos_id=self.eos_id,
+                       generator=self.generator, task_offset=self.cursor + self.rank * G,
+                       row_offset=self.rank * G * cfg.group_size)
+
     def step(self) -> Dict[str, Any]:
         cfg = self.cfg
-        timer = _Timer(self.model.device)
+        if self.watchdog is not None:
+            self.watchdog.check()   # a dead peer is noticed here, before this step launches anything
+        timer = PhaseTimer(self.model.device)
         timer.mark("start")
         seed = self.rng.next()
         G = self.groups_per_rank
-        if self.tp is not None:
-            cr = collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G * self.world, rng=seed,
-                         eos_id=self.eos_id, generator=self.generator, task_offset=self.cursor, row_offset=0,
-                         keep_groups=(self.rank * G, (self.rank + 1) * G))
-        else:
-            cr = collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G, rng=seed,
-                         eos_id=self.eos_id, generator=self.generator, task_offset=self.cursor + self.rank * G,
-                         row_offset=self.rank * G * cfg.group_size)
+        with phase("rollout"):
+            cr = self._collect(seed, G)
         timer.mark("rollout")
         self.cursor += G * self.world
         num_tasks = getattr(self.env, "num_tasks", -1)
         if num_tasks and num_tasks > 0:
             self.cursor %= num_tasks
-        self.ts, m = update(self.ts, cr, cfg, ref_model=self.ref_model, kl_ctrl=self.kl_ctrl, kl_coef=self.kl_coef)
+        with phase("update"):
+            self.ts, m = update(self.ts, cr, cfg, ref_model=self.ref_model, kl_ctrl=self.kl_ctrl,
+                                kl_coef=self.kl_coef)
         timer.mark("update")
         self.kl_coef = m.get("kl_coef", self.kl_coef)
         self.iteration += 1
@@ -137,6 +137,12 @@ class GRPOTrainer:
         m["tokens/generated"] = float(stats[3])
         m["tokens/total"] = float(stats[4])
         m["step"] = self.ts.step
+        if self.model.device.type == "cuda":
+            m["mem/allocated_gb"] = torch.cuda.memory_allocated(self.model.device) / 2 ** 30
+            m["mem/peak_gb"] = torch.cuda.max_memory_allocated(self.model.device) / 2 ** 30
+            dec_ms = self.generator.decode_time_ms()
+            if dec_ms > 0:
+                m["perf/decode_tok_s"] = self.generator.last_decode_tokens / (dec_ms / 1e3)
         if eps:
             m["sample/text"] = eps[0].generated_text[:200]
         return m

@@ -45,14 +45,35 @@ class static_weights:
         return False
 
 
+class KernelTimeout(RuntimeError):
+    """A bounded wait inside a kernel ran out (a pipeline stage never completed); the kernel left without
+    touching its outputs and the CUDA context is still usable."""
+
+    def __init__(self, code: int, device: int, what: str):
+        super().__init__(f"vlmrl kernel error {code} ({what}) on cuda:{device}")
+        self.code = code
+        self.device = device
+
+
+class CollectiveTimeout(KernelTimeout):
+    """A peer-memory collective waited longer than its budget for another rank's signal (the rank is
+    dead, hung or has left the step)."""
+
+
+_ERR_WHAT = {1: "TMA producer wait timed out", 2: "MMA wait timed out", 3: "epilogue wait timed out",
+             4: "peer rank signal timed out", 5: "bad arguments", 6: "pipeline flag wait timed out"}
+
+
 def check_errors(device: Optional[int] = None) -> None:
-    """Raise if a bounded wait inside a kernel timed out (reads and clears the device error word)."""
+    """Raise ``KernelTimeout`` / ``CollectiveTimeout`` if a kernel recorded an error (reads and clears the
+    device error word; synchronises the current stream)."""
     if not has_ext() or not torch.cuda.is_available():
         return
     dev = torch.cuda.current_device() if device is None else int(device)
     code = int(ext().read_and_clear_error(dev))
     if code:
-        raise RuntimeError(f"vlmrl kernel reported error code {code} (bounded wait timed out) on cuda:{dev}")
+        cls = CollectiveTimeout if code == 4 else KernelTimeout
+        raise cls(code, dev, _ERR_WHAT.get(code, "unknown"))
 
 
 def _cuda(x: torch.Tensor) -> bool:

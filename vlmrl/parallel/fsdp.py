@@ -39,6 +39,9 @@ from vlmrl.models.qwen3vl.params import UnitLayout
 from vlmrl.parallel.dist import all_gather_into, all_reduce_, reduce_scatter_into
 
 
+_CHECK_COLLECTIVES = os.environ.get("VLMRL_CHECK_COLLECTIVES", "0") == "1"
+
+
 class FSDPParams:
     """Sharded parameter source for the executor (``get``/``grad``/``grad_done`` protocol).
 
@@ -135,6 +138,28 @@ class FSDPParams:
             self.fresh[u] = True
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
+
+    def verify_signals(self) -> None:
+        """Debug check of the peer-memory protocol (``VLMRL_CHECK_COLLECTIVES=1`` runs it after every step).
+
+        After a step's device-side wait, every peer's counters in this rank's signal pad must equal the
+        values this rank expects exactly: a smaller value is a lost signal, a larger one a peer that ran
+        ahead of the protocol (a race).  Reads the pad to the host (synchronises).
+        """
+        if self.comm != "p2p":
+            return
+        W = self.world
+        pad = self.sym_sig.view(0, (self.n_slots, W), torch.int64).cpu()
+        bad = []
+        for i, u in enumerate(self.order):
+            for q in range(W):
+                if q != self.rank and int(pad[i, q]) != self.rs_epoch[i]:
+                    bad.append(f"reduce-scatter {u}: rank {q} at {int(pad[i, q])}, expected {self.rs_epoch[i]}")
+        for q in range(W):
+            if q != self.rank and int(pad[self.push_slot, q]) != self.push_target:
+                bad.append(f"parameter push: rank {q} at {int(pad[self.push_slot, q])}, expected {self.push_target}")
+        if bad:
+            raise RuntimeError("peer-memory collective counters out of step: " + "; ".join(bad[:6]))
 
     def close(self) -> None:
         """Release the IPC-shared buffers (collective)."""
@@ -273,6 +298,9 @@ class FSDPOptimizer:
                 p.shards[u].copy_(self.master[u])
                 p.grad_shards[u].zero_()
             ext().peer_wait(p.sym_sig.local, p.push_slot, p.push_target, p.rank, W, p.sym_sig.dev_index)
+            if _CHECK_COLLECTIVES:
+                ops.check_errors(p.sym_sig.dev_index)
+                p.verify_signals()
             for u in p.reduced:
                 p.reduced[u] = False
         else:

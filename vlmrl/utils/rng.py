@@ -39,5 +39,12 @@ class RngSeq:
         self._state = splitmix64(self._state)
         return self._state & ((1 << 63) - 1)
 
+    def state(self) -> int:
+        """The generator position (for checkpoints)."""
+        return int(self._state)
+
+    def set_state(self, state: int) -> None:
+        self._state = int(state) & _MASK64
+
 
 __all__ = ["RngSeq", "fold_in", "splitmix64"]
