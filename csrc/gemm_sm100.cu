@@ -448,14 +448,20 @@ __global__ void __launch_bounds__(192, 1)
       const int row = tm * kBM + row_in_tile;
       const int n0 = tn * BN;
       const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-      if (p.streamk) {
+      if (tm * kBM + q * 32 >= p.M) {
+        // every row of this warp's TMEM lanes is past M (decode-shaped M): nothing to load or store
+      } else if (p.streamk) {
         float* wsr = p.ws + (static_cast<int64_t>(w.slot) * p.M + row) * p.N;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(tbase + c, r);
-          tmem_ld_wait();
-          const int col0 = n0 + c;
+        for (int c4 = 0; c4 < BN; c4 += 64) {
+          uint32_t rr[4][16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tmem_ld16(tbase + c4 + 16 * j, rr[j]);
+          tmem_ld_wait();  // one round trip per 64 columns
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+          const uint32_t (&r)[16] = rr[j];
+          const int col0 = n0 + c4 + 16 * j;
           if (row >= p.M || col0 >= p.N) continue;
           if (col0 + 16 <= p.N) {
 #pragma unroll
@@ -465,17 +471,22 @@ __global__ void __launch_bounds__(192, 1)
           } else {
             for (int i = 0; i < p.N - col0; ++i) wsr[col0 + i] = __uint_as_float(r[i]);
           }
+          }
         }
       } else if (p.epi == EPI_VOCAB_STATS) {
         // online (max, sum exp, sum exp*z) of this row over the tile's columns; never stores logits
         float mx = -INFINITY, se = 0.f, sz = 0.f, zt = __int_as_float(0x7fc00000);
         const int64_t tgt = row < p.M ? p.targets[row] : -1;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(tbase + c, r);
+        for (int c4 = 0; c4 < BN; c4 += 64) {
+          uint32_t rr[4][16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tmem_ld16(tbase + c4 + 16 * j, rr[j]);
           tmem_ld_wait();
-          const int col0 = n0 + c;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+          const uint32_t (&r)[16] = rr[j];
+          const int col0 = n0 + c4 + 16 * j;
           const int nv = min(16, p.N - col0);
           if (nv <= 0) continue;
           float cm = -INFINITY;
@@ -502,6 +513,7 @@ __global__ void __launch_bounds__(192, 1)
             for (int i = 0; i < 16; ++i)
               if (col0 + i == tgt) zt = __uint_as_float(r[i]) * p.alpha;
           }
+          }
         }
         if (row < p.M) {
           reinterpret_cast<float4*>(p.part)[static_cast<int64_t>(row) * p.tiles_n + tn] = make_float4(mx, se, sz, zt);
@@ -518,11 +530,15 @@ __global__ void __launch_bounds__(192, 1)
           tgt = p.targets[row];
         }
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(tbase + c, r);
+        for (int c4 = 0; c4 < BN; c4 += 64) {
+          uint32_t rr[4][16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tmem_ld16(tbase + c4 + 16 * j, rr[j]);
           tmem_ld_wait();
-          const int col0 = n0 + c;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+          const uint32_t (&r)[16] = rr[j];
+          const int col0 = n0 + c4 + 16 * j;
           if (row >= p.M || col0 >= p.N) continue;
           float v[16];
 #pragma unroll
@@ -540,14 +556,18 @@ __global__ void __launch_bounds__(192, 1)
           } else {
             for (int i = 0; i < p.N - col0; ++i) d[i] = f2bf(v[i]);
           }
+          }
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(tbase + c, r);
+        for (int c4 = 0; c4 < BN; c4 += 64) {
+          uint32_t rr[4][16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tmem_ld16(tbase + c4 + 16 * j, rr[j]);
           tmem_ld_wait();
-          if (row < p.M && n0 + c < p.N) epilogue_chunk(p, row, n0 + c, r);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (row < p.M && n0 + c4 + 16 * j < p.N) epilogue_chunk(p, row, n0 + c4 + 16 * j, rr[j]);
         }
       }
       tc_fence_before();
