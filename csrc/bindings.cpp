@@ -7,6 +7,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vlmrl hand-written sm_100a kernels";
   m.def("gemm", &vlm::gemm, "tcgen05 GEMM with fused epilogues");
   m.def("gemm_partials", &vlm::gemm_partials, "stream-K partial sums for the fused decode consumers");
+  m.def("gemm_partials_traced", &vlm::gemm_partials_traced, "gemm_partials with per-CTA phase timestamps");
   m.def("set_static_weights", &vlm::set_static_weights);
   m.def("dec_qkv", &vlm::dec_qkv);
   m.def("dec_residual_norm", &vlm::dec_residual_norm);

@@ -64,7 +64,17 @@ struct GemmParams {
   int sk_grid;  // grid size of the stream-K launch
   int bn;
   int b_prefetch;  // B may be loaded before pdl_wait (B is a weight no earlier kernel of the step writes)
+  // optional phase timestamps (%globaltimer, ns) per CTA: [grid][8] — a measurement aid, null in production
+  unsigned long long* trace;
 };
+
+VLM_DEV void trace_mark(const GemmParams& p, int k) {
+  if (p.trace) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    p.trace[blockIdx.x * 8 + k] = t;
+  }
+}
 
 // Work item: one accumulation segment of one output tile.
 struct Work {
@@ -119,7 +129,9 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  // per epilogue warp: a 32 x 16 fp32 staging tile (rows padded to 20 words) for coalesced partial stores
+  static constexpr int EPI_STAGE_FLOATS = 32 * 20;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 4 * EPI_STAGE_FLOATS * 4;
 };
 
 VLM_DEV void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
@@ -280,9 +292,11 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  float* epi_stage = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + 256);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kb_count = (p.K + kBK - 1) / kBK;
+  if (threadIdx.x == 0) trace_mark(p, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -296,19 +310,42 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  // Programmatic dependent launch: the weight operand B (never written by earlier kernels of the step) of
+  // the first STAGES k-blocks is requested right after the barriers exist — before the TMEM allocation
+  // and the CTA barrier, and before waiting for the previous kernel.  Thread 0 is the TMA producer.
+  int prefetched = 0;
+  if (threadIdx.x == 0 && p.b_prefetch) {
+    WorkIter it0(p, kb_count);
+    Work w0;
+    if (it0.next(p, w0)) {
+      int tm0, tn0;
+      tile_coords(w0.tile, p.tiles_m, p.tiles_n, tm0, tn0);
+      prefetched = min(C::STAGES, w0.kb1 - w0.kb0);
+      for (int i = 0; i < prefetched; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+        uint8_t* b = sB + i * C::B_BYTES;
+        const int k0 = (w0.kb0 + i) * kBK, n0 = tn0 * BN;
+        if constexpr (!B_MN) {
+          tma_load_2d(b, &tmB, &full[i], k0, n0);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 8192, &tmB, &full[i], n0 + 64 * j, k0);
+        }
+      }
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, C::TMEM_COLS);
     tmem_relinquish();
   }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  if (threadIdx.x == 0) trace_mark(p, 1);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -326,25 +363,8 @@ __global__ void __launch_bounds__(192, 1)
       };
       WorkIter it(p, kb_count);
       Work w;
-      // Programmatic dependent launch: the weight operand B (never written by earlier kernels of the
-      // step) of the first STAGES k-blocks is requested before waiting for the previous kernel.
-      int prefetched = 0;
-      {
-        WorkIter it0 = it;
-        Work w0;
-        if (p.b_prefetch && it0.next(p, w0)) {
-          int tm0, tn0;
-          tile_coords(w0.tile, p.tiles_m, p.tiles_n, tm0, tn0);
-          prefetched = min(C::STAGES, w0.kb1 - w0.kb0);
-          for (int i = 0; i < prefetched; ++i) {
-            stage = i;
-            mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-            load_b(sB + i * C::B_BYTES, (w0.kb0 + i) * kBK, tn0 * BN);
-          }
-          stage = 0;
-        }
-      }
       pdl_wait();
+      trace_mark(p, 2);
       while (ok && it.next(p, w)) {
         int tm, tn;
         tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
@@ -406,6 +426,7 @@ __global__ void __launch_bounds__(192, 1)
             ok = false;
             break;
           }
+          if (lt == 0 && kb == kb0) trace_mark(p, 3);
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
           const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
@@ -423,6 +444,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (!ok) break;
         umma_commit(&tfull[acc]);
+        trace_mark(p, 4);
       }
       if (!ok) {
         umma_commit(drain);
@@ -442,6 +464,7 @@ __global__ void __launch_bounds__(192, 1)
       const int acc = lt & 1;
       const uint32_t use = static_cast<uint32_t>(lt >> 1);
       if (!mbar_wait(&tfull[acc], use & 1u, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      if (threadIdx.x == 128 && lt == 0) trace_mark(p, 5);
       tc_fence_after();
       int tm, tn;
       tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
@@ -451,26 +474,44 @@ __global__ void __launch_bounds__(192, 1)
       if (tm * kBM + q * 32 >= p.M) {
         // every row of this warp's TMEM lanes is past M (decode-shaped M): nothing to load or store
       } else if (p.streamk) {
-        float* wsr = p.ws + (static_cast<int64_t>(w.slot) * p.M + row) * p.N;
+        // Each lane holds one row's 16 columns after tcgen05.ld; storing that directly makes every warp
+        // store touch 32 rows.  Stage the 32 x 16 block in shared memory and store it transposed: lane
+        // (r4, c) writes 16 bytes of row 8*i + r4, so one store instruction covers 8 rows x 64 bytes.
+        float* stg = epi_stage + (warp - 2) * C::EPI_STAGE_FLOATS;
+        const int row_base = tm * kBM + q * 32;
+        const int sr = lane >> 2, sc = (lane & 3) * 4;
 #pragma unroll 1
-        for (int c4 = 0; c4 < BN; c4 += 64) {
-          uint32_t rr[4][16];
+        for (int c4 = 0; c4 < BN; c4 += 128) {
+          uint32_t rr[8][16];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) tmem_ld16(tbase + c4 + 16 * j, rr[j]);
-          tmem_ld_wait();  // one round trip per 64 columns
+          for (int j = 0; j < 8; ++j) tmem_ld16(tbase + c4 + 16 * j, rr[j]);
+          tmem_ld_wait();  // one round trip per 128 columns
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-          const uint32_t (&r)[16] = rr[j];
-          const int col0 = n0 + c4 + 16 * j;
-          if (row >= p.M || col0 >= p.N) continue;
-          if (col0 + 16 <= p.N) {
+          for (int j = 0; j < 8; ++j) {
+            const int col0 = n0 + c4 + 16 * j;
+            if (col0 >= p.N) continue;  // warp-uniform
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              reinterpret_cast<float4*>(wsr + col0)[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                                                     __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-          } else {
-            for (int i = 0; i < p.N - col0; ++i) wsr[col0 + i] = __uint_as_float(r[i]);
-          }
+            for (int i = 0; i < 4; ++i)
+              reinterpret_cast<float4*>(stg + lane * 20)[i] =
+                  make_float4(__uint_as_float(rr[j][4 * i]), __uint_as_float(rr[j][4 * i + 1]),
+                              __uint_as_float(rr[j][4 * i + 2]), __uint_as_float(rr[j][4 * i + 3]));
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int r = 8 * i + sr;
+              const int grow = row_base + r;
+              if (grow < p.M) {
+                const float4 v4 = *reinterpret_cast<const float4*>(stg + r * 20 + sc);
+                float* dst = p.ws + (static_cast<int64_t>(w.slot) * p.M + grow) * p.N + col0 + sc;
+                if (col0 + sc + 4 <= p.N) {
+                  *reinterpret_cast<float4*>(dst) = v4;
+                } else {
+                  const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+                  for (int e = 0; e < 4 && col0 + sc + e < p.N; ++e) dst[e] = vv[e];
+                }
+              }
+            }
+            __syncwarp();
           }
         }
       } else if (p.epi == EPI_VOCAB_STATS) {
@@ -573,6 +614,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (threadIdx.x == 128) trace_mark(p, 6);
     }
   }
 
@@ -582,6 +624,7 @@ __global__ void __launch_bounds__(192, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  if (threadIdx.x == 0) trace_mark(p, 7);
 }
 
 // Generic consumer of stream-K partials: sums the slots of 16 columns and applies the GEMM epilogue.
@@ -612,6 +655,8 @@ __global__ void sk_reduce_kernel(GemmParams p, SkMeta m) {
 // Set while the weights are read-only (the decode loop): GEMMs may then stream B before the wait on
 // their predecessor kernel.
 static thread_local bool g_static_weights = false;
+// Set only inside gemm_partials_traced: the next launch records per-CTA phase timestamps here.
+static thread_local unsigned long long* g_trace = nullptr;
 void set_static_weights(bool on) { g_static_weights = on; }
 
 template <int BN, bool A_MN, bool B_MN>
@@ -679,6 +724,7 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   p.epi = static_cast<int>(epi);
   p.accumulate = accumulate;
   p.err = err_word(A.device().index());
+  p.trace = g_trace;
   // B is prefetched ahead of the dependency wait only when it is a K-major weight: the forward and
   // decode GEMMs.  Backward GEMMs (MN-major operands) read activation gradients as B.
   p.b_prefetch = (g_static_weights && b_kmajor && !accumulate && epi != EPI_VOCAB_GRAD) ? 1 : 0;
@@ -774,6 +820,16 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor 
   TORCH_CHECK((epi >= EPI_STORE && epi <= EPI_GELU_ERF) || epi == EPI_SWIGLU_BWD, "gemm: epilogue code ", epi,
               " is internal");
   gemm_ex(A, B, D, bias, residual, aux, a_kmajor, b_kmajor, alpha, epi, accumulate, nullptr, 0, nullptr, nullptr);
+}
+
+// Stream-K partials with per-CTA phase timestamps written to ``trace`` (int64 [>= grid * 8]): a measurement
+// aid for the decode GEMM's fixed latency.
+std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials_traced(at::Tensor A, at::Tensor B, at::Tensor trace) {
+  TORCH_CHECK(trace.scalar_type() == at::kLong && trace.is_cuda() && trace.numel() >= 148 * 8, "trace: int64 [grid*8]");
+  g_trace = reinterpret_cast<unsigned long long*>(trace.data_ptr());
+  auto out = gemm_partials(A, B);
+  g_trace = nullptr;
+  return out;
 }
 
 std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials(at::Tensor A, at::Tensor B) {

@@ -27,6 +27,7 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
              int force_bn, at::Tensor* partials_out, SkMeta* meta_out);
 // Stream-K partial sums of A.B^T without an epilogue: (ws [slots, M, N] fp32, meta) for the fused consumers.
 std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials(at::Tensor A, at::Tensor B);
+std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials_traced(at::Tensor A, at::Tensor B, at::Tensor trace);
 // While on, GEMMs prefetch their K-major B operand before waiting on the previous kernel (PDL).
 void set_static_weights(bool on);
 
