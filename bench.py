@@ -33,6 +33,19 @@ import time
 
 METRIC = "GRPO RL steps/sec + rollout decode tok/s, Qwen3-VL-4B, 1/2/4/8 B200"
 
+# Named workloads.  grpo_4b is the headline configuration; the others are the companion workloads
+# (tiny smoke run, two-image True/False with short answers, 8B with long answers).
+WORKLOADS = {
+    "grpo_4b": dict(preset="qwen3vl_4b", env="synthetic_geo", groups=8, group_size=8, image=448, prompt_tokens=64,
+                    max_new=128, minibatches=2),
+    "tiny": dict(preset="tiny", env="synthetic_parity", groups=4, group_size=4, image=64, prompt_tokens=16,
+                 max_new=16, minibatches=1),
+    "truefalse_4b": dict(preset="qwen3vl_4b", env="synthetic_truefalse", groups=32, group_size=8, image=384,
+                         prompt_tokens=48, max_new=8, minibatches=2),
+    "grpo_8b": dict(preset="qwen3vl_8b", env="synthetic_geo", groups=16, group_size=8, image=672, prompt_tokens=128,
+                    max_new=512, minibatches=2),
+}
+
 
 def parse():
     ap = argparse.ArgumentParser(description=__doc__)
@@ -40,18 +53,24 @@ def parse():
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
-    ap.add_argument("--preset", default="qwen3vl_4b")
-    ap.add_argument("--groups", type=int, default=8)
-    ap.add_argument("--group-size", type=int, default=8)
-    ap.add_argument("--max-new", type=int, default=128)
-    ap.add_argument("--prompt-tokens", type=int, default=64)
-    ap.add_argument("--image", type=int, default=448)
-    ap.add_argument("--minibatches", type=int, default=2)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="grpo_4b",
+                    help="named workload; its fields are the defaults of the flags below")
+    ap.add_argument("--preset", default=None)
+    ap.add_argument("--groups", type=int, default=None)
+    ap.add_argument("--group-size", type=int, default=None)
+    ap.add_argument("--max-new", type=int, default=None)
+    ap.add_argument("--prompt-tokens", type=int, default=None)
+    ap.add_argument("--image", type=int, default=None)
+    ap.add_argument("--minibatches", type=int, default=None)
     ap.add_argument("--top-k", type=int, default=5)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--rollout", choices=["tp", "dp"], default="dp",
                     help="N>1: tensor-parallel decode of the whole batch (tp) or each rank decodes its own groups (dp)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    for k, v in WORKLOADS[args.workload].items():
+        if getattr(args, k, None) is None:
+            setattr(args, k, v)
+    return args
 
 
 def reference_arm(args):
@@ -152,13 +171,14 @@ def main():
     dev = torch.device("cuda", local)
 
     spec = get_preset(args.preset)
+    merge_px = spec.vision.patch_size * spec.vision.spatial_merge_size
+    image_tokens = (args.image // merge_px) ** 2
     tok = ByteTokenizer(spec.text.vocab_size)
     cfg = TrainerConfig(temperature=0.7, top_p=0.9, top_k=args.top_k, max_new_tokens=args.max_new,
                         groups_per_batch=args.groups, group_size=args.group_size, kl_ref_coef=0.01,
                         n_minibatches=args.minibatches, clip_epsilon=0.2, adaptive_kl=False)
     adamw = AdamWConfig(lr=5e-7, weight_decay=0.01, max_grad_norm=1.0)
-    env = create_env("synthetic_geo", tok, image_size=args.image, prompt_tokens=args.prompt_tokens, num_tasks=1024,
-                     seed=0)
+    env = create_env(args.env, tok, image_size=args.image, prompt_tokens=args.prompt_tokens, num_tasks=1024, seed=0)
     if world > 1:
         from vlmrl.parallel.fsdp import build_fsdp_models
 
@@ -224,8 +244,9 @@ def main():
         barrier()
         e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
         roll_groups = args.groups if trainer.tp is not None else args.groups // world  # rolled out on this rank
-        img_bytes = roll_groups * args.image * args.image * 3
-        prompt_len = 196 * (args.image // 448) ** 2 + 2 + args.prompt_tokens
+        n_img = 2 if args.env == "synthetic_truefalse" else 1
+        img_bytes = roll_groups * n_img * args.image * args.image * 3
+        prompt_len = n_img * (image_tokens + 2) + args.prompt_tokens
         seqs = args.groups * args.group_size // world                                   # trained on this rank
         # images + prefill ids/positions + packed training ids/positions/indices (int64)
         h2d = img_bytes + roll_groups * prompt_len * 8 * 5 + seqs * (prompt_len + args.max_new) * 8 * 5
@@ -250,7 +271,9 @@ def main():
         "dtype": "bf16",
         "data": "synthetic (uniform-random 448x448 RGB images and prompt ids, uniform-on-sphere targets), random-init weights",
         "config": {"model": f"{args.preset} architecture (random init)", "global_batch": total_seqs,
-                   "seq_len": f"{196 + 2 + args.prompt_tokens} prompt + {args.max_new} new",
+                   "seq_len": f"{(2 if args.env == 'synthetic_truefalse' else 1) * (image_tokens + 2) + args.prompt_tokens}"
+                              f" prompt + {args.max_new} new",
+                   "workload": args.workload,
                    "parallelism": (f"fsdp{world}+tp{world}-rollout" if trainer.tp is not None else f"fsdp{world}")
                    if world > 1 else "single-gpu",
                    "fsdp_comm": getattr(model.params, "comm", None) if world > 1 else None,
