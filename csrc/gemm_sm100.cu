@@ -64,7 +64,9 @@ struct GemmParams {
   int sk_grid;  // grid size of the stream-K launch
   int bn;
   int b_prefetch;  // B may be loaded before pdl_wait (B is a weight no earlier kernel of the step writes)
-  // optional phase timestamps (%globaltimer, ns) per CTA: [grid][8] — a measurement aid, null in production
+  // optional phase timestamps (%globaltimer, ns) per CTA: [grid][8] — a measurement aid, null in production.
+  // 0 entry, 1 setup done, 2 producer past the dependency wait, 3 first stage ready, 4 last MMA commit,
+  // 5 first accumulator ready (epilogue warp 4), 6 epilogue done (warp 4), 7 exit
   unsigned long long* trace;
 };
 
