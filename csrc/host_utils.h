@@ -6,6 +6,7 @@
 #include <torch/extension.h>
 
 #include <cstdint>
+#include <cstdlib>
 
 #define VLM_CUDA_CHECK(expr)                                                                   \
   do {                                                                                         \
@@ -27,6 +28,15 @@ int64_t launch_count();
     ::vlm::note_launch();               \
   } while (0)
 
+// VLMRL_NO_PDL=1 launches every kernel without programmatic serialization (for A/B measurements).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VLMRL_NO_PDL");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
+
 // Launch with programmatic stream serialization (PDL): the kernel may start while its predecessor in
 // the stream is still running and must call pdl_wait() before reading or writing data the predecessor
 // touches.
@@ -45,7 +55,7 @@ inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   VLM_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(std::forward<Args>(args))...));
   note_launch();
 }

@@ -1,0 +1,158 @@
+"""Device-timed microbenchmarks of the peer-memory collective kernels (one process per GPU).
+
+``torchrun --nproc-per-node N -m vlmrl.parallel.bench_collectives`` times, with
+CUDA events on the launching stream and the max over ranks:
+
+* ``rs_pull``      — gradient reduce-scatter of one decoder layer unit (fp32), the kernel of the FSDP
+                     ``p2p`` path, against ``reduce_scatter_tensor`` (NCCL) on the same buffer;
+* ``adamw_push``   — sharded AdamW + bf16 all-gather by peer stores for one layer, against NCCL
+                     ``all_gather_into_tensor`` of the same bf16 shard (plus the local AdamW kernel);
+* ``dec_residual_norm_tp`` — the tensor-parallel decode consumer (batch 64 x 2560 partials all-reduced
+                     in the kernel), against an NCCL all-reduce of the same fp32 rows.
+
+Roofline: bytes that must cross NVLink per rank / 770 GB/s (the measured peer-copy bandwidth per
+direction); the achieved fraction is that time divided by the measured time.  Prints one JSON line
+per case on rank 0.
+"""
+
+from __future__ import annotations
+
+import datetime
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+LINK_GBS = 770.0
+
+
+def _timed(fn, iters: int = 20, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / iters
+    t = torch.tensor([ms], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main() -> None:
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    from vlmrl import ops
+    from vlmrl.ops._ext import ext
+    from vlmrl.parallel.symm import SymmetricBuffer
+
+    W, r = dist.get_world_size(), dist.get_rank()
+    dev = torch.device("cuda", local)
+    out = []
+
+    # ---- reduce-scatter of one layer's fp32 gradient (4B model: 101M parameters -> padded)
+    n_full = (101 * 2 ** 20 // (128 * W)) * 128 * W
+    n = n_full // W
+    grads = SymmetricBuffer(n_full * 4, None, dev)
+    sig = SymmetricBuffer(4 * W * 8, None, dev)
+    g = grads.view(0, (n_full,), torch.float32)
+    g.normal_()
+    shard = torch.zeros(n, device=dev)
+    epoch = [0]
+
+    def rs_p2p():
+        epoch[0] += 1
+        ext().rs_pull(grads.ptrs, 0, r * n, shard, False, sig.ptrs, 0, epoch[0], r, 0)
+
+    ms = _timed(rs_p2p)
+    ops.check_errors(local)
+    link_bytes = (W - 1) * n * 4           # this rank pulls its shard from every peer
+    ideal = link_bytes / (LINK_GBS * 1e9) * 1e3
+    out.append({"case": f"rs_pull_fp32_{n_full}", "world": W, "ms": round(ms, 4),
+                "link_GBps": round(link_bytes / ms / 1e6, 1), "roofline_ms": round(ideal, 4),
+                "frac_of_roofline": round(ideal / ms, 3)})
+    full = torch.randn(n_full, device=dev)
+    ms_nccl = _timed(lambda: dist.reduce_scatter_tensor(shard, full))
+    out.append({"case": f"nccl_reduce_scatter_fp32_{n_full}", "world": W, "ms": round(ms_nccl, 4),
+                "frac_of_roofline": round(ideal / ms_nccl, 3)})
+
+    # ---- AdamW on the shard + bf16 push into every rank's gathered buffer
+    params = SymmetricBuffer(n_full * 2, None, dev)
+    p32, m, v = torch.randn(n, device=dev), torch.zeros(n, device=dev), torch.zeros(n, device=dev)
+    gs = torch.randn(n, device=dev)
+    scale = torch.ones(1, device=dev)
+    target = [0]
+
+    def push():
+        grid = ext().adamw_push(p32, gs, m, v, params.ptrs, r * n * 2, scale, 1e-7, 0.9, 0.999, 1e-8, 0.01, 1,
+                                sig.ptrs, 1, r)
+        target[0] += int(grid)
+        ext().peer_wait(sig.local, 1, target[0], r, W, local)
+
+    ms = _timed(push)
+    ops.check_errors(local)
+    link_bytes = (W - 1) * n * 2             # this rank's bf16 shard stored into every peer
+    local_bytes = n * (4 * 4 + 3 * 4 + 2)    # AdamW reads p, g, m, v and writes p, m, v, own bf16
+    ideal = max(link_bytes / (LINK_GBS * 1e9), local_bytes / 6.541e12) * 1e3
+    out.append({"case": f"adamw_push_{n_full}", "world": W, "ms": round(ms, 4), "roofline_ms": round(ideal, 4),
+                "frac_of_roofline": round(ideal / ms, 3)})
+    gathered = torch.empty(n_full, dtype=torch.bfloat16, device=dev)
+    ph = torch.empty(n, dtype=torch.bfloat16, device=dev)
+
+    def nccl_path():
+        ops.adamw_(p32, gs, m, v, lr=1e-7, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=1,
+                   grad_scale=scale, p_half=ph)
+        dist.all_gather_into_tensor(gathered, ph)
+
+    ms_nccl = _timed(nccl_path)
+    out.append({"case": f"adamw_then_nccl_all_gather_{n_full}", "world": W, "ms": round(ms_nccl, 4),
+                "frac_of_roofline": round(ideal / ms_nccl, 3)})
+
+    # ---- tensor-parallel decode consumer: 64 x 2560 partial rows all-reduced inside the kernel
+    B, H = 64, 2560
+    rows = SymmetricBuffer(2 * B * H * 4, None, dev)     # two points, used alternately: a row buffer is
+    flags = SymmetricBuffer(2 * B * W * 8, None, dev)    # rewritten only after every peer passed the other
+    it = [0]
+    ep = torch.zeros(1, dtype=torch.int64, device=dev)
+    x = torch.randn(B, 2048 // W, device=dev).to(torch.bfloat16)
+    wgt = (torch.randn(H, 2048 // W, device=dev) * 0.02).to(torch.bfloat16)
+    res = torch.randn(B, H, device=dev).to(torch.bfloat16)
+    nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
+    ws, meta = ops.gemm_partials(x, wgt)
+
+    def tp_consumer():
+        pt = it[0] % 2
+        it[0] += 1
+        ext().tp_step_begin(ep.data_ptr(), local)
+        ext().dec_residual_norm_tp(ws, list(meta), res, nw, 1e-6, rows.ptrs, pt * B * H * 4, flags.ptrs, pt * B * W,
+                                   ep.data_ptr(), r)
+
+    ms = _timed(tp_consumer, iters=50)
+    ops.check_errors(local)
+    link_bytes = (W - 1) * B * H * 4
+    ideal = link_bytes / (LINK_GBS * 1e9) * 1e3
+    out.append({"case": f"dec_residual_norm_tp_{B}x{H}", "world": W, "ms": round(ms, 4),
+                "roofline_ms": round(ideal, 4), "frac_of_roofline": round(ideal / ms, 3),
+                "note": "latency-bound: one flag round trip per row"})
+    red = torch.randn(B, H, device=dev)
+    ms_nccl = _timed(lambda: dist.all_reduce(red), iters=50)
+    out.append({"case": f"nccl_all_reduce_fp32_{B}x{H}", "world": W, "ms": round(ms_nccl, 4)})
+
+    if r == 0:
+        for row in out:
+            print(json.dumps(row), flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    for b in (grads, sig, params, rows, flags):
+        b.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
