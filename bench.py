@@ -64,6 +64,9 @@ def parse():
     ap.add_argument("--minibatches", type=int, default=None)
     ap.add_argument("--top-k", type=int, default=5)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--fsdp-params", choices=["gathered", "sharded"], default="gathered",
+                    help="gathered: bf16 parameters stay all-gathered (pushed by the fused AdamW); sharded: "
+                         "decoder-layer weights are all-gathered inside the GEMMs that consume them")
     ap.add_argument("--rollout", choices=["tp", "dp"], default="dp",
                     help="N>1: tensor-parallel decode of the whole batch (tp) or each rank decodes its own groups (dp)")
     args = ap.parse_args()
@@ -182,7 +185,8 @@ def main():
     if world > 1:
         from vlmrl.parallel.fsdp import build_fsdp_models
 
-        model, ref_model, train_state = build_fsdp_models(spec, adamw, seed=0, device=dev)
+        model, ref_model, train_state = build_fsdp_models(spec, adamw, seed=0, device=dev,
+                                                          shard_params=args.fsdp_params == "sharded")
     else:
         model = Qwen3VLModel(spec, device=dev, dtype=torch.bfloat16, seed=0)
         text_units = {k: v for k, v in model.params.units.items() if k != "visual"}
@@ -275,6 +279,7 @@ def main():
                               f" prompt + {args.max_new} new",
                    "workload": args.workload,
                    "parallelism": (f"fsdp{world}+tp{world}-rollout" if trainer.tp is not None else f"fsdp{world}")
+                   + ("-sharded-params" if args.fsdp_params == "sharded" and world > 1 else "")
                    if world > 1 else "single-gpu",
                    "fsdp_comm": getattr(model.params, "comm", None) if world > 1 else None,
                    "groups_per_batch": args.groups, "group_size": args.group_size, "minibatches": args.minibatches,

@@ -790,7 +790,8 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_consta
                                                              const __grid_constant__ CUtensorMap tmV,
                                                              const bf16* __restrict__ q, const int* __restrict__ lens,
                                                              bf16* __restrict__ o, float* __restrict__ part, int Hq,
-                                                             int Hkv, int Tmax, float scale_log2, int splits, int* err) {
+                                                             int Hkv, int Tmax, float scale_log2, int splits, int* err,
+                                                             L2Prefetch pf) {
   constexpr int D = 128, KC = 64;
   constexpr int HALF = KC * 64;  // elements of one 64x64 box
   extern __shared__ __align__(1024) uint8_t tc_raw[];
@@ -800,6 +801,7 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_consta
   uint64_t* full = reinterpret_cast<uint64_t*>(sV + STAGES * 2 * HALF);
   float* red = reinterpret_cast<float*>(full + STAGES);  // merge area [4][REP][D + 2]
   __shared__ int abort_flag;
+  l2_prefetch_share(pf);
   pdl_wait();
   pdl_trigger();
   const int hk = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
@@ -1145,7 +1147,7 @@ static void decode_dispatch(const at::Tensor& q, const at::Tensor& kc, const at:
 
 template <int REP>
 static void decode_tc_dispatch(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& lens,
-                               at::Tensor& o, float scale) {
+                               at::Tensor& o, float scale, L2Prefetch pf) {
   constexpr int STAGES = 3, D = 128;
   const int B = static_cast<int>(q.size(0)), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(kc.size(1));
   const int Tmax = static_cast<int>(kc.size(2));
@@ -1166,14 +1168,15 @@ static void decode_tc_dispatch(const at::Tensor& q, const at::Tensor& kc, const 
   if (splits > 1) part = at::empty({B, Hq, splits, D + 2}, q.options().dtype(at::kFloat));
   launch_pdl(kern, dim3(Hkv, B, splits), dim3(128), smem, st, tk, tv, reinterpret_cast<const bf16*>(q.data_ptr()),
              lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()), splits > 1 ? part.data_ptr<float>() : nullptr,
-             Hq, Hkv, Tmax, scale * kLog2e, splits, err_word(q.device().index()));
+             Hq, Hkv, Tmax, scale * kLog2e, splits, err_word(q.device().index()), pf);
   if (splits > 1) {
     launch_pdl(decode_combine_kernel, dim3(B * Hq), dim3(128), 0, st, part.data_ptr<float>(),
                reinterpret_cast<bf16*>(o.data_ptr()), B * Hq, splits, D);
   }
 }
 
-void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale) {
+void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale,
+                 c10::optional<at::Tensor> prefetch) {
   TORCH_CHECK(q.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(), "decode_attn: contiguous");
   TORCH_CHECK(lens.scalar_type() == at::kInt, "decode_attn: int32 lengths");
   if (q.size(0) == 0) return;
@@ -1181,9 +1184,10 @@ void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at
   const int D = static_cast<int>(q.size(2));
   const int rep = static_cast<int>(q.size(1) / kc.size(1));
   const float sc = static_cast<float>(scale);
-  if (D == 128 && rep == 4) return decode_tc_dispatch<4>(q, kc, vc, lens, o, sc);
-  if (D == 128 && rep == 2) return decode_tc_dispatch<2>(q, kc, vc, lens, o, sc);
-  if (D == 128 && rep == 8) return decode_tc_dispatch<8>(q, kc, vc, lens, o, sc);
+  const L2Prefetch pf = l2_prefetch_of<L2Prefetch>(prefetch);
+  if (D == 128 && rep == 4) return decode_tc_dispatch<4>(q, kc, vc, lens, o, sc, pf);
+  if (D == 128 && rep == 2) return decode_tc_dispatch<2>(q, kc, vc, lens, o, sc, pf);
+  if (D == 128 && rep == 8) return decode_tc_dispatch<8>(q, kc, vc, lens, o, sc, pf);
 #define VLM_DEC(DD, RR) \
   if (D == DD && rep == RR) return decode_dispatch<DD, RR>(q, kc, vc, lens, o, sc);
   VLM_DEC(128, 4) VLM_DEC(128, 2) VLM_DEC(128, 1) VLM_DEC(128, 8) VLM_DEC(64, 4) VLM_DEC(64, 2) VLM_DEC(64, 1)

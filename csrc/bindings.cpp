@@ -6,12 +6,17 @@
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vlmrl hand-written sm_100a kernels";
   m.def("gemm", &vlm::gemm, "tcgen05 GEMM with fused epilogues");
+  m.def("gemm_gather", &vlm::gemm_gather, "tcgen05 GEMM whose weight operand is all-gathered from peer shards in-kernel");
+  m.def("unit_gather", &vlm::unit_gather, "copy byte ranges of a sharded unit from the peers' shards");
   m.def("gemm_partials", &vlm::gemm_partials, "stream-K partial sums for the fused decode consumers");
   m.def("gemm_partials_traced", &vlm::gemm_partials_traced, "gemm_partials with per-CTA phase timestamps");
   m.def("set_static_weights", &vlm::set_static_weights);
-  m.def("dec_qkv", &vlm::dec_qkv);
-  m.def("dec_residual_norm", &vlm::dec_residual_norm);
-  m.def("dec_swiglu", &vlm::dec_swiglu);
+  m.def("dec_qkv", &vlm::dec_qkv, py::arg("ws"), py::arg("meta"), py::arg("bias"), py::arg("qw"), py::arg("kw"),
+        py::arg("lengths"), py::arg("delta"), py::arg("inv_freq"), py::arg("kc"), py::arg("vc"), py::arg("nq"),
+        py::arg("nkv"), py::arg("eps"), py::arg("prefetch") = py::none());
+  m.def("dec_residual_norm", &vlm::dec_residual_norm, py::arg("ws"), py::arg("meta"), py::arg("residual"), py::arg("w"),
+        py::arg("eps"), py::arg("prefetch") = py::none());
+  m.def("dec_swiglu", &vlm::dec_swiglu, py::arg("ws"), py::arg("meta"), py::arg("prefetch") = py::none());
   m.def("tp_step_begin", &vlm::tp_step_begin, "advance the tensor-parallel decode epoch (device counter)");
   m.def("dec_residual_norm_tp", &vlm::dec_residual_norm_tp,
         "residual + RMSNorm consumer that all-reduces row-parallel partials over NVLink");
@@ -34,7 +39,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_bwd", &vlm::flash_attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
         py::arg("lse"), py::arg("cu"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("max_seqlen"),
         py::arg("causal"), py::arg("scale"), py::arg("pre") = py::none(), py::arg("xq") = py::none());
-  m.def("decode_attn", &vlm::decode_attn);
+  m.def("decode_attn", &vlm::decode_attn, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("lens"), py::arg("o"),
+        py::arg("scale"), py::arg("prefetch") = py::none());
   m.def("sample", &vlm::sample);
   m.def("vocab_logprob_fwd", &vlm::vocab_logprob_fwd);
   m.def("vocab_logprob_bwd", &vlm::vocab_logprob_bwd);

@@ -27,6 +27,7 @@ enum ErrCode : int {
   kErrTimeoutPeer = 4,
   kErrBadArgs = 5,
   kErrTimeoutFlag = 6,
+  kErrTimeoutGather = 7,
 };
 
 VLM_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -92,6 +93,29 @@ VLM_DEV void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_
                    smem_u32(smem_dst)),
                "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+
+// ------------------------------------------------------------------ L2 prefetch
+// A byte range (16-byte aligned) that the L2 should fetch ahead of the kernel that reads it; p == null: none.
+struct L2Prefetch {
+  const uint8_t* p;
+  long long bytes;
+};
+// Thread 0 of every CTA requests its 1/#CTAs share of the range with cp.async.bulk.prefetch.L2, which
+// completes on its own (nothing waits for it).  Latency-bound decode kernels use it so that HBM keeps
+// streaming the next GEMM's weights while they run; that GEMM then finds them in L2.
+VLM_DEV void l2_prefetch_share(const L2Prefetch& pf) {
+  if (pf.p == nullptr || threadIdx.x != 0 || threadIdx.y != 0 || threadIdx.z != 0) return;
+  const long long nct = static_cast<long long>(gridDim.x) * gridDim.y * gridDim.z;
+  const long long cta = blockIdx.x + static_cast<long long>(gridDim.x) * (blockIdx.y + static_cast<long long>(gridDim.y) * blockIdx.z);
+  const long long per = ((pf.bytes + nct - 1) / nct + 15) & ~15ll;
+  long long a = per * cta;
+  const long long e = min(pf.bytes & ~15ll, a + per);
+  constexpr long long kPiece = 1 << 15;
+  for (; a < e; a += kPiece) {
+    const uint32_t n = static_cast<uint32_t>(min(kPiece, e - a));
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(pf.p + a), "r"(n) : "memory");
+  }
 }
 
 // ------------------------------------------------------------------ programmatic dependent launch

@@ -35,8 +35,9 @@ __global__ void dec_qkv_kernel(const float* __restrict__ ws, SkMeta m, const bf1
                                const bf16* __restrict__ qw, const bf16* __restrict__ kw, const int* __restrict__ lengths,
                                const int64_t* __restrict__ delta, const float* __restrict__ inv_freq,
                                bf16* __restrict__ q, bf16* __restrict__ kc, bf16* __restrict__ vc, int nq, int nkv,
-                               int Tmax, float eps) {
+                               int Tmax, float eps, L2Prefetch pf) {
   constexpr int TPH = D / 8;
+  l2_prefetch_share(pf);
   pdl_wait();
   pdl_trigger();
   const int row = blockIdx.x, tid = threadIdx.x;
@@ -84,8 +85,9 @@ __global__ void dec_qkv_kernel(const float* __restrict__ ws, SkMeta m, const bf1
 // One CTA per row; thread i owns columns [8i, 8i+8).
 __global__ void dec_resnorm_kernel(const float* __restrict__ ws, SkMeta m, const bf16* __restrict__ res,
                                    const bf16* __restrict__ w, bf16* __restrict__ h_out, bf16* __restrict__ hn_out,
-                                   int H, float eps) {
+                                   int H, float eps, L2Prefetch pf) {
   __shared__ float red[32];
+  l2_prefetch_share(pf);
   pdl_wait();
   pdl_trigger();
   const int row = blockIdx.x, col = threadIdx.x * 8;
@@ -123,7 +125,8 @@ __global__ void dec_resnorm_kernel(const float* __restrict__ ws, SkMeta m, const
   }
 }
 
-__global__ void dec_swiglu_kernel(const float* __restrict__ ws, SkMeta m, bf16* __restrict__ act, int N) {
+__global__ void dec_swiglu_kernel(const float* __restrict__ ws, SkMeta m, bf16* __restrict__ act, int N, L2Prefetch pf) {
+  l2_prefetch_share(pf);
   pdl_wait();
   pdl_trigger();
   const int row = blockIdx.y;
@@ -143,8 +146,9 @@ __global__ void dec_swiglu_kernel(const float* __restrict__ ws, SkMeta m, bf16* 
 
 at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at::Tensor qw, at::Tensor kw,
                    at::Tensor lengths, at::Tensor delta, at::Tensor inv_freq, at::Tensor kc, at::Tensor vc, int64_t nq,
-                   int64_t nkv, double eps) {
+                   int64_t nkv, double eps, c10::optional<at::Tensor> prefetch) {
   const SkMeta m = meta_of(meta);
+  const L2Prefetch pf = l2_prefetch_of<L2Prefetch>(prefetch);
   const int D = static_cast<int>(kc.size(-1));
   const int Tmax = static_cast<int>(kc.size(-2));
   TORCH_CHECK(m.N == (nq + 2 * nkv) * D, "dec_qkv: width mismatch");
@@ -163,7 +167,7 @@ at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at
                lengths.data_ptr<int>(), delta.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),
                reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(kc.data_ptr()),
                reinterpret_cast<bf16*>(vc.data_ptr()), static_cast<int>(nq), static_cast<int>(nkv), Tmax,
-               static_cast<float>(eps));
+               static_cast<float>(eps), pf);
   };
   if (D == 128)
     args(dec_qkv_kernel<128>);
@@ -177,7 +181,7 @@ at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at
 }
 
 std::tuple<at::Tensor, at::Tensor> dec_residual_norm(at::Tensor ws, std::vector<int64_t> meta, at::Tensor residual,
-                                                     at::Tensor w, double eps) {
+                                                     at::Tensor w, double eps, c10::optional<at::Tensor> prefetch) {
   const SkMeta m = meta_of(meta);
   TORCH_CHECK(residual.is_contiguous() && residual.size(0) == m.M && residual.size(1) == m.N, "dec_residual_norm: shape");
   TORCH_CHECK(m.N % 8 == 0 && m.N / 8 <= 1024, "dec_residual_norm: width");
@@ -186,18 +190,19 @@ std::tuple<at::Tensor, at::Tensor> dec_residual_norm(at::Tensor ws, std::vector<
   const int threads = ((m.N / 8 + 31) / 32) * 32;
   launch_pdl(dec_resnorm_kernel, dim3(m.M), dim3(threads), 0, at::cuda::getCurrentCUDAStream(), ws.data_ptr<float>(), m,
              reinterpret_cast<const bf16*>(residual.data_ptr()), reinterpret_cast<const bf16*>(w.data_ptr()),
-             reinterpret_cast<bf16*>(h.data_ptr()), reinterpret_cast<bf16*>(hn.data_ptr()), m.N, static_cast<float>(eps));
+             reinterpret_cast<bf16*>(h.data_ptr()), reinterpret_cast<bf16*>(hn.data_ptr()), m.N, static_cast<float>(eps),
+             l2_prefetch_of<L2Prefetch>(prefetch));
   return {h, hn};
 }
 
-at::Tensor dec_swiglu(at::Tensor ws, std::vector<int64_t> meta) {
+at::Tensor dec_swiglu(at::Tensor ws, std::vector<int64_t> meta, c10::optional<at::Tensor> prefetch) {
   const SkMeta m = meta_of(meta);
   TORCH_CHECK(m.N % 16 == 0, "dec_swiglu: width must be a multiple of 16");
   const c10::cuda::CUDAGuard g(ws.device());
   at::Tensor act = at::empty({m.M, m.N / 2}, ws.options().dtype(at::kBFloat16));
   const dim3 grid((m.N / 8 + 255) / 256, m.M);
   launch_pdl(dec_swiglu_kernel, grid, dim3(256), 0, at::cuda::getCurrentCUDAStream(), ws.data_ptr<float>(), m,
-             reinterpret_cast<bf16*>(act.data_ptr()), m.N);
+             reinterpret_cast<bf16*>(act.data_ptr()), m.N, l2_prefetch_of<L2Prefetch>(prefetch));
   return act;
 }
 

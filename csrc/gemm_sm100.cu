@@ -15,12 +15,19 @@
 //   16 M-tiles so concurrently running CTAs share B tiles in L2.
 // * Every wait is bounded (see common.cuh); on timeout the kernel records an
 //   error code, drains its own in-flight TMA copies and MMAs, frees TMEM and exits.
+// * GATHER variant (FSDP with sharded parameters): B is a weight whose rows are
+//   spread over the ranks' parameter shards.  Two extra copy warps per CTA pull
+//   64-row chunks from every rank's shard (plain peer loads over NVLink) into
+//   the local buffer the B tensor map covers, 16 KB pieces claimed from a
+//   global queue; the TMA producer waits on a chunk's arrival count before it
+//   loads from that chunk, so the all-gather overlaps the MMAs tile by tile.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
 #include "common.cuh"
 #include "host_utils.h"
+#include "peer.cuh"
 #include "vlm_ops.h"
 #include "streamk.cuh"
 
@@ -68,7 +75,20 @@ struct GemmParams {
   // 0 entry, 1 setup done, 2 producer past the dependency wait, 3 first stage ready, 4 last MMA commit,
   // 5 first accumulator ready (epilogue warp 4), 6 epilogue done (warp 4), 7 exit
   unsigned long long* trace;
+  // fused all-gather of B (GATHER kernels only).  B occupies bytes [g_off, g_off + g_rows*g_row_bytes) of a
+  // flat parameter unit that is split into equal shards of g_shard_bytes; shard r is at g_src.p[r] (a peer
+  // mapping for the other ranks) and the local copy of the unit starts at g_dst.  Rows are N rows of a
+  // K-major B or K rows of an MN-major B; chunk c = rows [64c, 64c+64), copied as g_pieces pieces.
+  PeerTable g_src;
+  uint8_t* g_dst;
+  long long g_off, g_shard_bytes, g_row_bytes;
+  int g_rows, g_chunks, g_pieces;
+  unsigned* g_flags;  // [g_chunks] pieces arrived; zero between launches (the last CTA to exit resets them)
+  unsigned* g_ctr;    // [2] piece claim counter, exited CTAs; zero between launches
 };
+
+constexpr int kGatherPiece = 16384;   // bytes per claimed piece
+constexpr int kGatherMaxChunks = 8192;  // ready bits kept in shared memory by the producer
 
 VLM_DEV void trace_mark(const GemmParams& p, int k) {
   if (p.trace) {
@@ -133,7 +153,7 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = 2 * BN;
   // per epilogue warp: a 32 x 16 fp32 staging tile (rows padded to 20 words) for coalesced partial stores
   static constexpr int EPI_STAGE_FLOATS = 32 * 20;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 4 * EPI_STAGE_FLOATS * 4;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 4 * EPI_STAGE_FLOATS * 4 + kGatherMaxChunks / 8;
 };
 
 VLM_DEV void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
@@ -279,8 +299,86 @@ VLM_DEV void epilogue_chunk(const GemmParams& p, int row, int col, const uint32_
   }
 }
 
-template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(192, 1)
+VLM_DEV unsigned ld_acquire_gpu_u32(const unsigned* a) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+VLM_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Producer side of the fused gather: wait until chunks [c0, c1) have all their pieces.  `ready` caches the
+// chunks this CTA already saw complete.  The proxy fence orders the acquire before the TMA (async proxy)
+// reads of the chunk.
+VLM_DEV bool gather_wait(const GemmParams& p, uint32_t* ready, int c0, int c1, volatile int* abort_flag) {
+  bool fresh = false;
+  for (int c = c0; c < c1; ++c) {
+    const uint32_t bit = 1u << (c & 31);
+    if (ready[c >> 5] & bit) continue;
+    if (ld_acquire_gpu_u32(p.g_flags + c) < static_cast<unsigned>(p.g_pieces)) {
+      const long long t0 = clock64();
+      while (ld_acquire_gpu_u32(p.g_flags + c) < static_cast<unsigned>(p.g_pieces)) {
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitCycles) {
+          *abort_flag = 1;
+          atomicCAS(p.err, 0, kErrTimeoutGather);
+          return false;
+        }
+      }
+    }
+    ready[c >> 5] |= bit;
+    fresh = true;
+  }
+  if (fresh) fence_proxy_async_global();
+  return true;
+}
+
+// Copy warps of the fused gather: claim 16 KB pieces in chunk order until the queue is empty.  Nothing here
+// waits on another CTA, so the copy makes progress whichever CTAs are resident.
+VLM_DEV void gather_copy(const GemmParams& p, int lane) {
+  constexpr int U = 16;  // 16-byte vectors in flight per lane
+  const unsigned total = static_cast<unsigned>(p.g_chunks) * static_cast<unsigned>(p.g_pieces);
+  const long long chunk_bytes = 64ll * p.g_row_bytes;
+  const long long b_bytes = static_cast<long long>(p.g_rows) * p.g_row_bytes;
+  const long long SB = p.g_shard_bytes;
+  while (true) {
+    unsigned idx = 0;
+    if (lane == 0) idx = atomicAdd(p.g_ctr, 1u);
+    idx = __shfl_sync(0xffffffffu, idx, 0);
+    if (idx >= total) break;
+    const int c = static_cast<int>(idx / p.g_pieces), j = static_cast<int>(idx % p.g_pieces);
+    const long long b0 = c * chunk_bytes + static_cast<long long>(j) * kGatherPiece;
+    const long long b1 = min(min(b0 + kGatherPiece, (c + 1) * chunk_bytes), b_bytes);
+    if (b0 < b1) {
+      const long long u0 = p.g_off + b0;
+      const int o0 = static_cast<int>(u0 / SB), o1 = static_cast<int>((p.g_off + b1 - 1) / SB);
+      for (long long x0 = b0; x0 < b1; x0 += 32ll * 16 * U) {
+        uint4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const long long x = x0 + (u * 32 + lane) * 16ll;
+          if (x < b1) {
+            const long long ux = p.g_off + x;
+            const int o = o0 == o1 ? o0 : static_cast<int>(ux / SB);
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(p.g_src.p[o] + (ux - o * SB)));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const long long x = x0 + (u * 32 + lane) * 16ll;
+          if (x < b1) __stcg(reinterpret_cast<uint4*>(p.g_dst + p.g_off + x), v[u]);
+        }
+      }
+    }
+    // publish the piece: generic stores -> async proxy (the consumer's TMA), then a release count
+    fence_proxy_async_global();
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.g_flags + c) : "memory");
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, bool GATHER = false>
+__global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
   using C = GemmCfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -295,6 +393,8 @@ __global__ void __launch_bounds__(192, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* epi_stage = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES + 256);
+  uint32_t* gather_ready = reinterpret_cast<uint32_t*>(epi_stage + 4 * C::EPI_STAGE_FLOATS);
+  int* last_cta = reinterpret_cast<int*>(tmem_holder + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kb_count = (p.K + kBK - 1) / kBK;
@@ -311,6 +411,9 @@ __global__ void __launch_bounds__(192, 1)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    if constexpr (GATHER) {
+      for (int i = 0; i < (p.g_chunks + 31) / 32; ++i) gather_ready[i] = 0;
+    }
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -376,6 +479,15 @@ __global__ void __launch_bounds__(192, 1)
           if (!pre && !mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrTimeoutProducer)) {
             ok = false;
             break;
+          }
+          if constexpr (GATHER) {
+            // K-major B: the tile's BN weight rows (chunks n0/64 ...); MN-major B: this k-block's 64 rows
+            const int c0 = B_MN ? kb : n0 / 64;
+            const int c1 = B_MN ? kb + 1 : min(p.g_chunks, (n0 + BN + 63) / 64);
+            if ((B_MN || kb == w.kb0) && !gather_wait(p, gather_ready, c0, c1, abort_flag)) {
+              ok = false;
+              break;
+            }
           }
           uint8_t* a = sA + stage * C::A_BYTES;
           uint8_t* b = sB + stage * C::B_BYTES;
@@ -454,6 +566,9 @@ __global__ void __launch_bounds__(192, 1)
         mbar_wait(drain, 0, &no_abort, nullptr, 0);
       }
     }
+  } else if (GATHER && warp >= 6) {
+    pdl_wait();  // the previous kernel may still read the buffer being filled
+    gather_copy(p, lane);
   } else {
     pdl_wait();  // epilogue reads residual / writes outputs the previous kernel may still touch
     if (threadIdx.x == 64) pdl_trigger();  // only after the wait: dependents never overlap our predecessor
@@ -626,6 +741,22 @@ __global__ void __launch_bounds__(192, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  if constexpr (GATHER) {
+    // every role of this CTA is done with the gather state; the last CTA out zeroes it for the next launch
+    if (threadIdx.x == 0) {
+      __threadfence();
+      *last_cta = atomicAdd(p.g_ctr + 1, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (*last_cta) {
+      __threadfence();
+      for (int c = threadIdx.x; c < p.g_chunks; c += blockDim.x) p.g_flags[c] = 0;
+      if (threadIdx.x == 0) {
+        p.g_ctr[0] = 0;
+        p.g_ctr[1] = 0;
+      }
+    }
+  }
   if (threadIdx.x == 0) trace_mark(p, 7);
 }
 
@@ -661,15 +792,15 @@ static thread_local bool g_static_weights = false;
 static thread_local unsigned long long* g_trace = nullptr;
 void set_static_weights(bool on) { g_static_weights = on; }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, bool GATHER = false>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid, cudaStream_t st) {
-  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN>;
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, GATHER>;
   static bool configured = false;
   if (!configured) {
     VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM));
     configured = true;
   }
-  launch_pdl(kern, dim3(grid), dim3(192), GemmCfg<BN>::SMEM, st, ta, tb, p);
+  launch_pdl(kern, dim3(grid), dim3(GATHER ? 256 : 192), GemmCfg<BN>::SMEM, st, ta, tb, p);
 }
 
 static void check_operand(const at::Tensor& t, const char* name) {
@@ -681,7 +812,7 @@ static void check_operand(const at::Tensor& t, const char* name) {
 
 void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
              bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, const VocabArgs* vocab,
-             int force_bn, at::Tensor* partials_out, SkMeta* meta_out) {
+             int force_bn, at::Tensor* partials_out, SkMeta* meta_out, const GatherArgs* gather) {
   check_operand(A, "A");
   check_operand(B, "B");
   const c10::cuda::CUDAGuard guard(A.device());
@@ -729,7 +860,33 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   p.trace = g_trace;
   // B is prefetched ahead of the dependency wait only when it is a K-major weight: the forward and
   // decode GEMMs.  Backward GEMMs (MN-major operands) read activation gradients as B.
-  p.b_prefetch = (g_static_weights && b_kmajor && !accumulate && epi != EPI_VOCAB_GRAD) ? 1 : 0;
+  p.b_prefetch = (g_static_weights && b_kmajor && !accumulate && epi != EPI_VOCAB_GRAD && !gather) ? 1 : 0;
+  if (gather) {
+    const int W = static_cast<int>(gather->srcs.size());
+    TORCH_CHECK(W >= 1 && W <= kMaxRanks, "gemm_gather: 1..", kMaxRanks, " shards");
+    TORCH_CHECK(B.is_contiguous(), "gemm_gather: B must be a contiguous view of the unit");
+    const int64_t rows = B.size(0), row_bytes = B.size(1) * 2;
+    const int64_t off = reinterpret_cast<int64_t>(B.data_ptr()) - gather->dst_base;
+    TORCH_CHECK(off >= 0 && off % 16 == 0 && off + rows * row_bytes <= W * gather->shard_bytes,
+                "gemm_gather: B is not inside the unit");
+    TORCH_CHECK(gather->shard_bytes % 16 == 0 && gather->dst_base % 16 == 0, "gemm_gather: 16-byte alignment");
+    const int64_t chunks = (rows + 63) / 64;
+    TORCH_CHECK(chunks <= kGatherMaxChunks, "gemm_gather: more than ", kGatherMaxChunks, " chunks");
+    TORCH_CHECK(gather->flags.is_cuda() && gather->flags.scalar_type() == at::kInt && gather->flags.numel() >= chunks &&
+                    gather->ctr.is_cuda() && gather->ctr.scalar_type() == at::kInt && gather->ctr.numel() >= 2,
+                "gemm_gather: flags int32 [>= chunks] and ctr int32 [2] on the device");
+    TORCH_CHECK(!partials_out && epi != EPI_VOCAB_STATS, "gemm_gather: not with partial-sum outputs");
+    p.g_src = make_peer_table(gather->srcs);
+    p.g_dst = reinterpret_cast<uint8_t*>(gather->dst_base);
+    p.g_off = off;
+    p.g_shard_bytes = gather->shard_bytes;
+    p.g_row_bytes = row_bytes;
+    p.g_rows = static_cast<int>(rows);
+    p.g_chunks = static_cast<int>(chunks);
+    p.g_pieces = static_cast<int>((64 * row_bytes + kGatherPiece - 1) / kGatherPiece);
+    p.g_flags = reinterpret_cast<unsigned*>(gather->flags.data_ptr());
+    p.g_ctr = reinterpret_cast<unsigned*>(gather->ctr.data_ptr());
+  }
   if (bias.defined() && bias.numel()) {
     TORCH_CHECK(bias.scalar_type() == at::kBFloat16 && bias.is_contiguous() && bias.numel() == N, "gemm: bad bias");
     p.bias = reinterpret_cast<const __nv_bfloat16*>(bias.data_ptr());
@@ -796,7 +953,13 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
     tb = make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, 64);
 
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (a_kmajor && b_kmajor) {
+  if (gather) {
+    TORCH_CHECK(a_kmajor, "gemm_gather: K-major A only");
+    if (b_kmajor)
+      BN == 256 ? launch<256, false, false, true>(ta, tb, p, grid, st) : launch<128, false, false, true>(ta, tb, p, grid, st);
+    else
+      BN == 256 ? launch<256, false, true, true>(ta, tb, p, grid, st) : launch<128, false, true, true>(ta, tb, p, grid, st);
+  } else if (a_kmajor && b_kmajor) {
     BN == 256 ? launch<256, false, false>(ta, tb, p, grid, st) : launch<128, false, false>(ta, tb, p, grid, st);
   } else if (a_kmajor && !b_kmajor) {
     BN == 256 ? launch<256, false, true>(ta, tb, p, grid, st) : launch<128, false, true>(ta, tb, p, grid, st);
@@ -822,6 +985,56 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor 
   TORCH_CHECK((epi >= EPI_STORE && epi <= EPI_GELU_ERF) || epi == EPI_SWIGLU_BWD, "gemm: epilogue code ", epi,
               " is internal");
   gemm_ex(A, B, D, bias, residual, aux, a_kmajor, b_kmajor, alpha, epi, accumulate, nullptr, 0, nullptr, nullptr);
+}
+
+void gemm_gather(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
+                 bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, std::vector<int64_t> srcs,
+                 int64_t dst_base, int64_t shard_bytes, at::Tensor flags, at::Tensor ctr) {
+  TORCH_CHECK((epi >= EPI_STORE && epi <= EPI_GELU_ERF) || epi == EPI_SWIGLU_BWD, "gemm_gather: epilogue code ", epi,
+              " is internal");
+  GatherArgs g{std::move(srcs), dst_base, shard_bytes, flags, ctr};
+  gemm_ex(A, B, D, bias, residual, aux, a_kmajor, b_kmajor, alpha, epi, accumulate, nullptr, 0, nullptr, nullptr, &g);
+}
+
+// Ranges of a sharded unit copied by a grid-stride loop of 16-byte vectors (ranges are 16-byte aligned).
+struct UnitRanges {
+  long long start[8], end[8];
+  int n;
+};
+
+__global__ void unit_gather_kernel(PeerTable src, uint8_t* dst, long long SB, UnitRanges r) {
+  pdl_wait();
+  const long long tid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (int i = 0; i < r.n; ++i) {
+    for (long long x = r.start[i] + tid * 16; x < r.end[i]; x += stride * 16) {
+      const int o = static_cast<int>(x / SB);
+      __stcg(reinterpret_cast<uint4*>(dst + x),
+             __ldcg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(src.p[o]) + (x - o * SB))));
+    }
+  }
+}
+
+void unit_gather(std::vector<int64_t> srcs, int64_t dst_base, int64_t shard_bytes, std::vector<int64_t> starts,
+                 std::vector<int64_t> ends) {
+  TORCH_CHECK(starts.size() == ends.size() && !starts.empty() && starts.size() <= 8, "unit_gather: 1..8 ranges");
+  TORCH_CHECK(shard_bytes % 16 == 0 && dst_base % 16 == 0, "unit_gather: 16-byte alignment");
+  UnitRanges r{};
+  r.n = static_cast<int>(starts.size());
+  long long total = 0;
+  for (int i = 0; i < r.n; ++i) {
+    TORCH_CHECK(starts[i] % 16 == 0 && ends[i] % 16 == 0 && starts[i] <= ends[i] &&
+                    ends[i] <= shard_bytes * static_cast<int64_t>(srcs.size()),
+                "unit_gather: ranges must be 16-byte aligned and inside the unit");
+    r.start[i] = starts[i];
+    r.end[i] = ends[i];
+    total = std::max<long long>(total, ends[i] - starts[i]);
+  }
+  if (total == 0) return;
+  const int threads = 256;
+  const int grid = static_cast<int>(std::min<long long>((total / 16 + threads - 1) / threads, 4 * 148));
+  launch_pdl(unit_gather_kernel, dim3(grid), dim3(threads), 0, at::cuda::getCurrentCUDAStream(), make_peer_table(srcs),
+             reinterpret_cast<uint8_t*>(dst_base), static_cast<long long>(shard_bytes), r);
 }
 
 // Stream-K partials with per-CTA phase timestamps written to ``trace`` (int64 [>= grid * 8]): a measurement

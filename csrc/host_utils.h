@@ -28,6 +28,16 @@ int64_t launch_count();
     ::vlm::note_launch();               \
   } while (0)
 
+// Optional tensor -> the L2 prefetch range of a decode kernel (whole tensor; none when absent).
+struct L2Prefetch;
+template <typename R>
+inline R l2_prefetch_of(const c10::optional<at::Tensor>& t) {
+  if (!t.has_value() || !t->defined() || t->numel() == 0) return R{nullptr, 0};
+  TORCH_CHECK(t->is_cuda() && t->is_contiguous() && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+              "prefetch: a contiguous, 16-byte aligned CUDA tensor");
+  return R{reinterpret_cast<const uint8_t*>(t->data_ptr()), static_cast<long long>(t->numel() * t->element_size())};
+}
+
 // VLMRL_NO_PDL=1 launches every kernel without programmatic serialization (for A/B measurements).
 inline bool pdl_enabled() {
   static const bool on = [] {

@@ -46,9 +46,13 @@ VLM_DEV bool wait_peers(const unsigned long long* sig, int slot, int W, int rank
 }
 
 // ------------------------------------------------------------------ reduce-scatter (pull)
+// WR = number of ranks (compile time), so every rank's loads of a vector group are issued together and
+// the NVLink and local HBM latencies overlap; the sum is still taken in rank order.
+template <int WR>
 __global__ void __launch_bounds__(256) rs_pull_kernel(PeerTable bufs, int64_t shard_off, int64_t n, float* out,
                                                       int accumulate, PeerTable sigs, int slot,
-                                                      unsigned long long epoch, int rank, int W, int* err) {
+                                                      unsigned long long epoch, int rank, int* err) {
+  constexpr int W = WR;
   __shared__ int ok;
   if (blockIdx.x == 0 && threadIdx.x < W && static_cast<int>(threadIdx.x) != rank) {
     __threadfence_system();
@@ -59,38 +63,33 @@ __global__ void __launch_bounds__(256) rs_pull_kernel(PeerTable bufs, int64_t sh
     ok = wait_peers(reinterpret_cast<const unsigned long long*>(sigs.p[rank]), slot, W, rank, epoch, err);
   __syncthreads();
   if (!ok) return;
-  // each thread keeps U float4 loads of one rank in flight (U * 16 B per thread; ~2.4 MB per GPU with one
-  // 256-thread CTA per SM, enough to cover NVLink latency), summing ranks in rank order
-  constexpr int U = 4;
+  // U float4 per rank in flight per thread: W * U * 16 bytes
+  constexpr int U = W <= 4 ? 4 : 2;
   const int64_t n4 = n >> 2;
   float4* o4 = reinterpret_cast<float4*>(out);
+  const float4* src[W];
+#pragma unroll
+  for (int q = 0; q < W; ++q) src[q] = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(bufs.p[q]) + shard_off);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; base < n4; base += stride * U) {
+    float4 x[W][U];
     float4 acc[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t i = base + u * stride;
       acc[u] = (accumulate && i < n4) ? o4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-#pragma unroll 1
-    for (int p = 0; p < W; ++p) {
-      const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(bufs.p[p]) + shard_off);
-      float4 x[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t i = base + u * stride;
-        x[u] = i < n4 ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        acc[u].x += x[u].x;
-        acc[u].y += x[u].y;
-        acc[u].z += x[u].z;
-        acc[u].w += x[u].w;
-      }
+      for (int q = 0; q < W; ++q) x[q][u] = i < n4 ? __ldcg(src[q] + i) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
+#pragma unroll
+      for (int q = 0; q < W; ++q) {
+        acc[u].x += x[q][u].x;
+        acc[u].y += x[q][u].y;
+        acc[u].z += x[q][u].z;
+        acc[u].w += x[q][u].w;
+      }
       const int64_t i = base + u * stride;
       if (i < n4) o4[i] = acc[u];
     }
@@ -225,12 +224,25 @@ void rs_pull(std::vector<int64_t> bufs, int64_t unit_off_bytes, int64_t shard_of
   TORCH_CHECK((unit_off_bytes + shard_off * 4) % 16 == 0, "rs_pull: 16-byte aligned shards");
   const c10::cuda::CUDAGuard g(out.device());
   const int dev = out.device().index();
-  int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((out.numel() / 4 + 1023) / 1024, num_sms(dev))));
-  if (max_ctas > 0) grid = std::min<int>(grid, static_cast<int>(max_ctas));
-  rs_pull_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      make_table(bufs, unit_off_bytes), shard_off, out.numel(), out.data_ptr<float>(), accumulate ? 1 : 0,
-      make_table(sigs), static_cast<int>(slot), static_cast<unsigned long long>(epoch), static_cast<int>(rank), W,
-      err_word(dev));
+  // one 256-thread CTA per SM by default (the kernel overlaps the backward on a side stream); max_ctas > 0
+  // sets the grid explicitly
+  const int64_t want = max_ctas > 0 ? max_ctas : num_sms(dev);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((out.numel() / 4 + 255) / 256, want)));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const PeerTable tb = make_table(bufs, unit_off_bytes), ts = make_table(sigs);
+  float* o = out.data_ptr<float>();
+  const int acc = accumulate ? 1 : 0, sl = static_cast<int>(slot), rk = static_cast<int>(rank);
+  const auto ep = static_cast<unsigned long long>(epoch);
+  switch (W) {
+    case 1: rs_pull_kernel<1><<<grid, 256, 0, st>>>(tb, shard_off, out.numel(), o, acc, ts, sl, ep, rk, err_word(dev)); break;
+    case 2: rs_pull_kernel<2><<<grid, 256, 0, st>>>(tb, shard_off, out.numel(), o, acc, ts, sl, ep, rk, err_word(dev)); break;
+    case 3: rs_pull_kernel<3><<<grid, 256, 0, st>>>(tb, shard_off, out.numel(), o, acc, ts, sl, ep, rk, err_word(dev)); break;
+    case 4: rs_pull_kernel<4><<<grid, 256, 0, st>>>(tb, shard_off, out.numel(), o, acc, ts, sl, ep, rk, err_word(dev)); break;
+    case 5: rs_pull_kernel<5><<<grid, 256, 0, st>>>(tb, shard_off, out.numel(), o, acc, ts, sl, ep, rk, err_word(dev)); break;
+    case 6: rs_pull_kernel<6><<<grid, 256, 0, st>>>(tb, shard_off, out.numel(), o, acc, ts, sl, ep, rk, err_word(dev)); break;
+    case 7: rs_pull_kernel<7><<<grid, 256, 0, st>>>(tb, shard_off, out.numel(), o, acc, ts, sl, ep, rk, err_word(dev)); break;
+    default: rs_pull_kernel<8><<<grid, 256, 0, st>>>(tb, shard_off, out.numel(), o, acc, ts, sl, ep, rk, err_word(dev)); break;
+  }
   VLM_LAUNCHED();
 }
 

@@ -19,12 +19,30 @@ struct VocabArgs {
   float* part;
 };
 
+// Fused all-gather of a GEMM's weight operand: B is a view into the local copy of a flat parameter unit
+// (starting at dst_base) whose equal shards of shard_bytes live at srcs[r] (peer mappings for r != rank).
+struct GatherArgs {
+  std::vector<int64_t> srcs;
+  int64_t dst_base;
+  int64_t shard_bytes;
+  at::Tensor flags;  // int32 [>= chunks], zero
+  at::Tensor ctr;    // int32 [2], zero
+};
+
 // gemm_sm100.cu
 void gemm(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux, bool a_kmajor,
           bool b_kmajor, double alpha, int64_t epi, bool accumulate);
 void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
              bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, const VocabArgs* vocab,
-             int force_bn, at::Tensor* partials_out, SkMeta* meta_out);
+             int force_bn, at::Tensor* partials_out, SkMeta* meta_out, const GatherArgs* gather = nullptr);
+// gemm() whose B rows are all-gathered from the ranks' shards inside the kernel (see GatherArgs)
+void gemm_gather(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
+                 bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, std::vector<int64_t> srcs,
+                 int64_t dst_base, int64_t shard_bytes, at::Tensor flags, at::Tensor ctr);
+// Copy byte ranges [starts[i], ends[i]) of a flat unit from the ranks' shards into the local copy (the small
+// leaves a fused gather GEMM does not cover).
+void unit_gather(std::vector<int64_t> srcs, int64_t dst_base, int64_t shard_bytes, std::vector<int64_t> starts,
+                 std::vector<int64_t> ends);
 // Stream-K partial sums of A.B^T without an epilogue: (ws [slots, M, N] fp32, meta) for the fused consumers.
 std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials(at::Tensor A, at::Tensor B);
 std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials_traced(at::Tensor A, at::Tensor B, at::Tensor trace);
@@ -34,10 +52,12 @@ void set_static_weights(bool on);
 // decode.cu: consumers of stream-K partials fused with the decode step's memory-bound ops
 at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at::Tensor qw, at::Tensor kw,
                    at::Tensor lengths, at::Tensor delta, at::Tensor inv_freq, at::Tensor kc, at::Tensor vc, int64_t nq,
-                   int64_t nkv, double eps);
+                   int64_t nkv, double eps,
+                   c10::optional<at::Tensor> prefetch = c10::nullopt);
 std::tuple<at::Tensor, at::Tensor> dec_residual_norm(at::Tensor ws, std::vector<int64_t> meta, at::Tensor residual,
-                                                     at::Tensor w, double eps);
-at::Tensor dec_swiglu(at::Tensor ws, std::vector<int64_t> meta);
+                                                     at::Tensor w, double eps,
+                                                     c10::optional<at::Tensor> prefetch = c10::nullopt);
+at::Tensor dec_swiglu(at::Tensor ws, std::vector<int64_t> meta, c10::optional<at::Tensor> prefetch = c10::nullopt);
 
 // elementwise.cu
 void rms_norm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps);
@@ -67,7 +87,8 @@ void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at:
 void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
                     at::Tensor cu, at::Tensor dq, at::Tensor dk, at::Tensor dv, int64_t max_seqlen, bool causal,
                     double scale, c10::optional<at::Tensor> pre, c10::optional<at::Tensor> xq);
-void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale);
+void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale,
+                 c10::optional<at::Tensor> prefetch = c10::nullopt);
 
 // sampler.cu
 void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, at::Tensor seed, double temperature,

@@ -80,3 +80,27 @@ def test_fsdp_two_ranks_matches_single_process(tmp_path):
         diff = (res["master"][name] - full.cpu()).abs()
         assert diff.max() <= 0.5 * adamw.lr, (name, float(diff.max()))
         assert (diff > 1e-6).float().mean() < 1e-3, name
+
+
+def test_sharded_unit_small_leaf_ranges():
+    """The leaves a sharded layer copies with one unit_gather: everything but the four GEMM matrices,
+    16-byte aligned, neighbours merged across alignment padding, disjoint from the matrices."""
+    from vlmrl.models.qwen3vl.config import get_preset
+    from vlmrl.models.qwen3vl.params import text_layouts
+    from vlmrl.parallel.fsdp import GATHERED_LEAVES, _small_ranges
+
+    lay = [l for l in text_layouts(get_preset("tiny")) if l.name == "layer0"][0]
+    rng = _small_ranges(lay, GATHERED_LEAVES)
+    assert all(a % 16 == 0 and b % 16 == 0 and a < b for a, b in rng)
+    big = [(lay.offsets[k] * 2, (lay.offsets[k] + lay.spec(k).numel) * 2) for k in GATHERED_LEAVES]
+    for a, b in rng:
+        assert all(b <= s or a >= e for s, e in big)
+    covered = set()
+    for a, b in rng:
+        covered.update(range(a, b, 2))
+    for prm in lay.params:
+        if prm.name not in GATHERED_LEAVES:
+            lo = lay.offsets[prm.name] * 2
+            assert set(range(lo, lo + prm.numel * 2, 2)) <= covered, prm.name
+    # input_norm | qkv_b..k_norm | post_norm
+    assert len(rng) == 3

@@ -408,3 +408,59 @@ def test_bounded_peer_wait_reports_timeout_and_context_survives():
     x = _r(256, 256, seed=99)
     _close(ops.gemm(x, x), ref.gemm(x, x, out_dtype=torch.float32), name="after timeout")
     _no_device_error()
+
+
+def _sharded_unit(W, rows, cols, lead, seed=0):
+    """A flat bf16 unit [lead elements | rows x cols matrix | tail] split into W separately allocated shards
+    (W emulated ranks on one GPU); returns (full unit, shard tensors, shard bytes, matrix offset)."""
+    numel = lead + rows * cols + 128
+    P = -(-numel // (128 * W)) * 128 * W
+    full = _r(P, seed=seed)
+    n = P // W
+    shards = [full[r * n:(r + 1) * n].clone() for r in range(W)]
+    return full, shards, n * 2, lead
+
+
+@pytest.mark.parametrize("W", [1, 3, 8])
+@pytest.mark.parametrize("M", [64, 700])
+def test_gemm_with_fused_weight_gather(W, M):
+    """GEMMs whose weight operand is assembled from W shards inside the kernel match the plain GEMM on the
+    full matrix, for the forward (K-major), dgrad (MN-major) and SwiGLU epilogue, and re-launch cleanly."""
+    N, K = 1344, 576
+    full, shards, SB, lead = _sharded_unit(W, N, K, 256)
+    w_full = full[lead:lead + N * K].view(N, K)
+    dst = torch.full_like(full, 7.0)
+    flags = torch.zeros(4096, dtype=torch.int32, device=DEV)
+    ctr = torch.zeros(2, dtype=torch.int32, device=DEV)
+    srcs = [s.data_ptr() for s in shards]
+    sw = ops.ShardedWeight(dst[lead:lead + N * K].view(N, K), srcs, dst.data_ptr(), SB, flags, ctr)
+    x = _r(M, K, seed=1)
+    for rep in range(2):
+        dst.fill_(7.0)
+        y = ops.linear(x, sw)
+        _close(y, x.float() @ w_full.float().T, name=f"fwd rep {rep}")
+        assert torch.equal(dst[lead:lead + N * K], full[lead:lead + N * K])
+    dst.fill_(-3.0)
+    dy = _r(M, N, seed=2)
+    dx = ops.grad_input(dy, sw)
+    _close(dx, dy.float() @ w_full.float(), name="dgrad")
+    dst.fill_(7.0)
+    act, pre = ops.linear_swiglu(x, sw)
+    pre_ref = x.float() @ w_full.float().T
+    _close(pre, pre_ref, name="swiglu pre")
+    _close(act, ref.swiglu_interleaved(pre_ref.bfloat16().float()), name="swiglu act")
+    torch.cuda.synchronize()
+    assert int(flags.abs().sum()) == 0 and int(ctr.abs().sum()) == 0  # the last CTA reset the counters
+    _no_device_error()
+
+
+def test_unit_gather_ranges():
+    W = 4
+    full, shards, SB, lead = _sharded_unit(W, 96, 64, 256, seed=3)
+    dst = torch.zeros_like(full)
+    ranges = [(0, lead * 2), ((lead + 96 * 64) * 2, full.numel() * 2)]
+    ops.unit_gather([s.data_ptr() for s in shards], dst.data_ptr(), SB, ranges)
+    for a, b in ranges:
+        assert torch.equal(dst[a // 2:b // 2], full[a // 2:b // 2])
+    assert int(dst[lead:lead + 96 * 64].abs().sum()) == 0
+    _no_device_error()

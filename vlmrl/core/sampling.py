@@ -150,7 +150,8 @@ class Generator:
         steps = max_new - 1
         if steps > 0:
             if self.use_cuda_graph:
-                gkey = (float(cfg.temperature), cfg.top_k, cfg.top_p, cfg.eos_id, int(row_offset))
+                gkey = (float(cfg.temperature), cfg.top_k, cfg.top_p, cfg.eos_id, int(row_offset),
+                        getattr(m.params, "graph_epoch", 0))
                 if st.graph is None or st.graph_cfg != gkey:
                     self._capture(st, cfg, row_offset)
                     st.graph_cfg = gkey

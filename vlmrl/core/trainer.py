@@ -15,6 +15,8 @@ metric read.
 
 from __future__ import annotations
 
+import contextlib
+
 import time
 from dataclasses import asdict
 from typing import Any, Dict, Optional
@@ -106,7 +108,8 @@ class GRPOTrainer:
         timer.mark("start")
         seed = self.rng.next()
         G = self.groups_per_rank
-        with phase("rollout"):
+        infer = getattr(getattr(self.model, "params", None), "inference_weights", None)
+        with phase("rollout"), (infer() if infer is not None else contextlib.nullcontext()):
             cr = self._collect(seed, G)
         timer.mark("rollout")
         self.cursor += G * self.world

@@ -25,6 +25,7 @@ Design choices (vs. the reference):
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -101,6 +102,10 @@ class KVCache:
     @classmethod
     def init(cls, batch, num_layers, num_heads, head_dim, max_len, dtype=torch.bfloat16, device="cpu"):
         return cls(num_layers, batch, num_heads, max_len, head_dim, dtype, device)
+
+
+# Decode kernels ask the L2 to fetch the next GEMM's weights (VLMRL_DECODE_L2_PREFETCH=0 turns it off).
+_DECODE_L2_PREFETCH = os.environ.get("VLMRL_DECODE_L2_PREFETCH", "1") != "0"
 
 
 # --------------------------------------------------------------------------- parameter sources
@@ -187,6 +192,11 @@ class TextDecoder:
 
     # ---------------------------------------------------------------- helpers
     def _w(self, params, name: str) -> Dict[str, torch.Tensor]:
+        views = getattr(params, "views", None)     # sharded sources hand out gather-on-use weights
+        if views is not None:
+            v = views(name, self.layouts[name])
+            if v is not None:
+                return v
         return self.layouts[name].views(params.get(name))
 
     def _g(self, params, name: str) -> Optional[Dict[str, torch.Tensor]]:
@@ -384,22 +394,33 @@ class TextDecoder:
         lens_after = lens + 1
         w = self._w(params, "layer0")
         xn, _ = ops.rms_norm(x, w["input_norm"], self.eps)
+        # The kernels between two GEMMs are latency-bound; each asks the L2 to fetch (part of) the next
+        # GEMM's weights while it runs: o_proj during the q/k/v consumer, the first half of gate/up during
+        # attention and the rest during the o_proj consumer, down during SwiGLU, the next layer's qkv during
+        # the closing residual + norm.
+        pf = _DECODE_L2_PREFETCH
         for i in range(self.n_layers):
             w = self._w(params, f"layer{i}")
+            nxt_w = self._w(params, f"layer{i + 1}") if i + 1 < self.n_layers else None
+            gu = w["gu_w"].reshape(-1)
+            half = (gu.numel() // 2) // 128 * 128
             ws, meta = ops.gemm_partials(xn, w["qkv_w"])
             q = ops.dec_qkv(ws, meta, w["qkv_b"], w.get("q_norm"), w.get("k_norm"), lens, delta, self.rope,
-                            cache.keys[i], cache.values[i], n_q=self.nq, n_kv=self.nkv, eps=self.eps)
-            o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale)
+                            cache.keys[i], cache.values[i], n_q=self.nq, n_kv=self.nkv, eps=self.eps,
+                            prefetch=w["o_w"] if pf else None)
+            o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale,
+                                prefetch=gu[:half] if pf else None)
             ws, meta = ops.gemm_partials(o.reshape(B, self.nq * self.D), w["o_w"])
-            h1, hn = ops.dec_residual_norm(ws, meta, x, w["post_norm"], self.eps)
+            h1, hn = ops.dec_residual_norm(ws, meta, x, w["post_norm"], self.eps, prefetch=gu[half:] if pf else None)
             ws, meta = ops.gemm_partials(hn, w["gu_w"])
-            act = ops.dec_swiglu(ws, meta)
+            act = ops.dec_swiglu(ws, meta, prefetch=w["down_w"] if pf else None)
             ws, meta = ops.gemm_partials(act, w["down_w"])
-            if i + 1 < self.n_layers:
-                nxt = self._w(params, f"layer{i + 1}")["input_norm"]
+            if nxt_w is not None:
+                nxt = nxt_w["input_norm"]
             else:
                 nxt = self._w(params, "head")["final_norm"]
-            x, xn = ops.dec_residual_norm(ws, meta, h1, nxt, self.eps)
+            x, xn = ops.dec_residual_norm(ws, meta, h1, nxt, self.eps,
+                                          prefetch=nxt_w["qkv_w"] if pf and nxt_w is not None else None)
             params.release(f"layer{i}")
         return xn
 

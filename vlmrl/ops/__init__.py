@@ -61,7 +61,8 @@ class CollectiveTimeout(KernelTimeout):
 
 
 _ERR_WHAT = {1: "TMA producer wait timed out", 2: "MMA wait timed out", 3: "epilogue wait timed out",
-             4: "peer rank signal timed out", 5: "bad arguments", 6: "pipeline flag wait timed out"}
+             4: "peer rank signal timed out", 5: "bad arguments", 6: "pipeline flag wait timed out",
+             7: "gathered weight chunk never arrived"}
 
 
 def check_errors(device: Optional[int] = None) -> None:
@@ -78,6 +79,56 @@ def check_errors(device: Optional[int] = None) -> None:
 
 def _cuda(x: torch.Tensor) -> bool:
     return x.is_cuda
+
+
+class ShardedWeight:
+    """A weight matrix whose rows are spread over the ranks' shards of a flat parameter unit.
+
+    ``local`` is the matrix's view inside this rank's copy of the unit (which starts at ``dst_base``);
+    rank r's shard of ``shard_bytes`` bytes is at address ``srcs[r]`` (a peer mapping for the other
+    ranks).  A GEMM that receives a ``ShardedWeight`` as B copies the rows from the shards into
+    ``local`` inside the kernel while its MMAs run (``flags``/``ctr``: the kernel's zeroed arrival
+    counters, one pair per concurrently used weight).  After that GEMM, ``local`` holds the matrix.
+    """
+
+    __slots__ = ("local", "srcs", "dst_base", "shard_bytes", "flags", "ctr")
+
+    def __init__(self, local: torch.Tensor, srcs: Sequence[int], dst_base: int, shard_bytes: int,
+                 flags: torch.Tensor, ctr: torch.Tensor):
+        self.local, self.srcs, self.dst_base, self.shard_bytes = local, list(srcs), int(dst_base), int(shard_bytes)
+        self.flags, self.ctr = flags, ctr
+
+    @property
+    def shape(self):
+        return self.local.shape
+
+    @property
+    def dtype(self):
+        return self.local.dtype
+
+    @property
+    def device(self):
+        return self.local.device
+
+    @property
+    def is_cuda(self) -> bool:
+        return self.local.is_cuda
+
+
+def _gemm_launch(a, b, d, bias, residual, aux, a_kmajor, b_kmajor, alpha, epi, accumulate):
+    if isinstance(b, ShardedWeight):
+        ext().gemm_gather(a, b.local, d, bias, residual, aux, a_kmajor, b_kmajor, alpha, epi, accumulate, b.srcs,
+                          b.dst_base, b.shard_bytes, b.flags, b.ctr)
+    else:
+        ext().gemm(a, b, d, bias, residual, aux, a_kmajor, b_kmajor, alpha, epi, accumulate)
+
+
+def unit_gather(srcs: Sequence[int], dst_base: int, shard_bytes: int, ranges: Sequence[Tuple[int, int]]) -> None:
+    """Copy byte ranges of a sharded flat unit from every rank's shard into the local copy (CUDA only)."""
+    for i in range(0, len(ranges), 8):
+        part = ranges[i:i + 8]
+        ext().unit_gather(list(srcs), int(dst_base), int(shard_bytes), [int(a) for a, _ in part],
+                          [int(b) for _, b in part])
 
 
 def _opt(x: Optional[torch.Tensor]):
@@ -121,8 +172,8 @@ def gemm(a: torch.Tensor, b: torch.Tensor, *, a_kmajor: bool = True, b_kmajor: b
     else:
         width = N // 2 if epilogue == EPI_SWIGLU else N
         d = torch.empty(M, width, dtype=out_dtype, device=a.device)
-    ext().gemm(a, b, d, _opt(bias), _opt(residual), _opt(aux), bool(a_kmajor), bool(b_kmajor), float(alpha),
-               int(epilogue), accumulate is not None)
+    _gemm_launch(a, b, d, _opt(bias), _opt(residual), _opt(aux), bool(a_kmajor), bool(b_kmajor), float(alpha),
+                 int(epilogue), accumulate is not None)
     return d
 
 
@@ -147,22 +198,25 @@ def gemm_partials(a: torch.Tensor, b: torch.Tensor):
 
 
 def dec_qkv(ws, meta, bias, q_w, k_w, lengths, delta, rope: "RopeCfg", k_cache, v_cache, *, n_q: int, n_kv: int,
-            eps: float):
+            eps: float, prefetch=None):
     """Sum QKV partials (+bias), RMSNorm q/k heads (skipped when ``q_w`` is None), MRoPE at position
-    ``lengths + delta``, write k/v into the cache at ``lengths``; returns q [B, n_q, D]."""
+    ``lengths + delta``, write k/v into the cache at ``lengths``; returns q [B, n_q, D].
+
+    ``prefetch`` (here and in the other decode consumers): a weight tensor whose bytes every CTA asks the
+    L2 to fetch while the kernel runs, so the next GEMM streams it from L2."""
     f, _ = rope.device_tables(ws.device)
     return ext().dec_qkv(ws, list(meta), _opt(bias), _opt(q_w), _opt(k_w), lengths, delta, f, k_cache, v_cache, n_q, n_kv,
-                         float(eps))
+                         float(eps), prefetch)
 
 
-def dec_residual_norm(ws, meta, residual, w, eps: float):
+def dec_residual_norm(ws, meta, residual, w, eps: float, prefetch=None):
     """h = sum(partials) + residual (bf16); returns (h, rms_norm(h) * w)."""
-    return ext().dec_residual_norm(ws, list(meta), residual, w, float(eps))
+    return ext().dec_residual_norm(ws, list(meta), residual, w, float(eps), prefetch)
 
 
-def dec_swiglu(ws, meta):
+def dec_swiglu(ws, meta, prefetch=None):
     """silu(gate) * up of interleaved gate/up partial sums -> [M, N/2] bf16."""
-    return ext().dec_swiglu(ws, list(meta))
+    return ext().dec_swiglu(ws, list(meta), prefetch)
 
 
 def grad_input(dy: torch.Tensor, w: torch.Tensor, out_dtype=torch.bfloat16, out=None):
@@ -180,7 +234,7 @@ def grad_input_swiglu(dy: torch.Tensor, w_down: torch.Tensor, pre: torch.Tensor)
         return swiglu_bwd(grad_input(dy, w_down, out_dtype=dy.dtype), pre)
     M, F = dy.shape[0], w_down.shape[1]
     out = torch.empty(M, 2 * F, dtype=torch.bfloat16, device=dy.device)
-    ext().gemm(dy, w_down, out, torch.Tensor(), torch.Tensor(), pre, True, False, 1.0, EPI_SWIGLU_BWD, False)
+    _gemm_launch(dy, w_down, out, torch.Tensor(), torch.Tensor(), pre, True, False, 1.0, EPI_SWIGLU_BWD, False)
     return out
 
 
@@ -337,12 +391,13 @@ def flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen: int, *, causal: 
     return dq, dk, dv
 
 
-def decode_attn(q, k_cache, v_cache, lengths, *, scale: Optional[float] = None, out=None):
+def decode_attn(q, k_cache, v_cache, lengths, *, scale: Optional[float] = None, out=None, prefetch=None):
+    """``prefetch``: a weight the L2 should fetch while the kernel runs (the next GEMM's operand)."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if not _cuda(q):
         return ref.decode_attn(q, k_cache, v_cache, lengths, scale=scale)
     o = out if out is not None else torch.empty_like(q)
-    ext().decode_attn(q, k_cache, v_cache, lengths, o, float(scale))
+    ext().decode_attn(q, k_cache, v_cache, lengths, o, float(scale), prefetch)
     return o
 
 

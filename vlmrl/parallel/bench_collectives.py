@@ -8,10 +8,15 @@ CUDA events on the launching stream and the max over ranks:
 * ``adamw_push``   — sharded AdamW + bf16 all-gather by peer stores for one layer, against NCCL
                      ``all_gather_into_tensor`` of the same bf16 shard (plus the local AdamW kernel);
 * ``dec_residual_norm_tp`` — the tensor-parallel decode consumer (batch 64 x 2560 partials all-reduced
-                     in the kernel), against an NCCL all-reduce of the same fp32 rows.
+                     in the kernel), against an NCCL all-reduce of the same fp32 rows;
+* ``gemm_gather``  — the FSDP (sharded-parameter) forward GEMM of the gate/up projection, 5112 tokens x
+                     2560 -> 19456, whose weight is all-gathered from the ranks' shards inside the GEMM,
+                     against NCCL ``all_gather_into_tensor`` followed by the same GEMM; also the dgrad form
+                     (MN-major weight operand).
 
 Roofline: bytes that must cross NVLink per rank / 770 GB/s (the measured peer-copy bandwidth per
-direction); the achieved fraction is that time divided by the measured time.  Prints one JSON line
+direction), or for the GEMM cases the slower of that and FLOPs / 1651 TFLOP/s (the measured cuBLAS bf16
+burst peak); the achieved fraction is that time divided by the measured time.  Prints one JSON line
 per case on rank 0.
 """
 
@@ -25,6 +30,7 @@ import torch
 import torch.distributed as dist
 
 LINK_GBS = 770.0
+GEMM_TFLOPS = 1651.0
 
 
 def _timed(fn, iters: int = 20, warmup: int = 3) -> float:
@@ -66,17 +72,18 @@ def main() -> None:
     shard = torch.zeros(n, device=dev)
     epoch = [0]
 
-    def rs_p2p():
-        epoch[0] += 1
-        ext().rs_pull(grads.ptrs, 0, r * n, shard, False, sig.ptrs, 0, epoch[0], r, 0)
-
-    ms = _timed(rs_p2p)
-    ops.check_errors(local)
     link_bytes = (W - 1) * n * 4           # this rank pulls its shard from every peer
     ideal = link_bytes / (LINK_GBS * 1e9) * 1e3
-    out.append({"case": f"rs_pull_fp32_{n_full}", "world": W, "ms": round(ms, 4),
-                "link_GBps": round(link_bytes / ms / 1e6, 1), "roofline_ms": round(ideal, 4),
-                "frac_of_roofline": round(ideal / ms, 3)})
+    for ctas in (0, 296, 592):
+        def rs_p2p(ctas=ctas):
+            epoch[0] += 1
+            ext().rs_pull(grads.ptrs, 0, r * n, shard, False, sig.ptrs, 0, epoch[0], r, ctas)
+
+        ms = _timed(rs_p2p)
+        ops.check_errors(local)
+        out.append({"case": f"rs_pull_fp32_{n_full}", "ctas": ctas or "sms", "world": W, "ms": round(ms, 4),
+                    "link_GBps": round(link_bytes / ms / 1e6, 1), "roofline_ms": round(ideal, 4),
+                    "frac_of_roofline": round(ideal / ms, 3)})
     full = torch.randn(n_full, device=dev)
     ms_nccl = _timed(lambda: dist.reduce_scatter_tensor(shard, full))
     out.append({"case": f"nccl_reduce_scatter_fp32_{n_full}", "world": W, "ms": round(ms_nccl, 4),
@@ -117,7 +124,7 @@ def main() -> None:
     # ---- tensor-parallel decode consumer: 64 x 2560 partial rows all-reduced inside the kernel
     B, H = 64, 2560
     rows = SymmetricBuffer(2 * B * H * 4, None, dev)     # two points, used alternately: a row buffer is
-    flags = SymmetricBuffer(2 * B * W * 8, None, dev)    # rewritten only after every peer passed the other
+    flags_tp = SymmetricBuffer(2 * B * W * 8, None, dev)    # rewritten only after every peer passed the other
     it = [0]
     ep = torch.zeros(1, dtype=torch.int64, device=dev)
     x = torch.randn(B, 2048 // W, device=dev).to(torch.bfloat16)
@@ -130,7 +137,7 @@ def main() -> None:
         pt = it[0] % 2
         it[0] += 1
         ext().tp_step_begin(ep.data_ptr(), local)
-        ext().dec_residual_norm_tp(ws, list(meta), res, nw, 1e-6, rows.ptrs, pt * B * H * 4, flags.ptrs, pt * B * W,
+        ext().dec_residual_norm_tp(ws, list(meta), res, nw, 1e-6, rows.ptrs, pt * B * H * 4, flags_tp.ptrs, pt * B * W,
                                    ep.data_ptr(), r)
 
     ms = _timed(tp_consumer, iters=50)
@@ -144,12 +151,55 @@ def main() -> None:
     ms_nccl = _timed(lambda: dist.all_reduce(red), iters=50)
     out.append({"case": f"nccl_all_reduce_fp32_{B}x{H}", "world": W, "ms": round(ms_nccl, 4)})
 
+    # ---- FSDP forward GEMM with the weight all-gathered inside the kernel (gate/up of the 4B model)
+    M, N, K = 5112, 19456, 2560
+    P = -(-N * K // (128 * W)) * 128 * W
+    n_sh = P // W
+    wsh = SymmetricBuffer(n_sh * 2, None, dev)
+    wsh.view(0, (n_sh,), torch.bfloat16).copy_((torch.randn(n_sh, device=dev) * 0.02).to(torch.bfloat16))
+    dst = torch.empty(P, dtype=torch.bfloat16, device=dev)
+    flags = torch.zeros(4096, dtype=torch.int32, device=dev)
+    ctr = torch.zeros(2, dtype=torch.int32, device=dev)
+    sw = ops.ShardedWeight(dst[:N * K].view(N, K), wsh.ptrs, dst.data_ptr(), n_sh * 2, flags, ctr)
+    x = (torch.randn(M, K, device=dev)).to(torch.bfloat16)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    full = torch.empty(P, dtype=torch.bfloat16, device=dev)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = _timed(lambda: ops.linear(x, sw, out=y), iters=10)
+    ops.check_errors(local)
+    y_fused = y.clone()
+    link_bytes = (W - 1) * n_sh * 2
+    flop_ms = 2.0 * M * N * K / (GEMM_TFLOPS * 1e12) * 1e3
+    ideal = max(link_bytes / (LINK_GBS * 1e9) * 1e3, flop_ms)
+    out.append({"case": f"gemm_gather_fwd_{M}x{K}x{N}", "world": W, "ms": round(ms, 4), "roofline_ms": round(ideal, 4),
+                "gemm_only_roofline_ms": round(flop_ms, 4), "frac_of_roofline": round(ideal / ms, 3)})
+    shard_local = wsh.view(0, (n_sh,), torch.bfloat16)
+
+    def nccl_then_gemm():
+        dist.all_gather_into_tensor(full, shard_local)
+        ops.linear(x, full[:N * K].view(N, K), out=y)
+
+    ms_nccl = _timed(nccl_then_gemm, iters=10)
+    out.append({"case": f"nccl_all_gather_then_gemm_{M}x{K}x{N}", "world": W, "ms": round(ms_nccl, 4),
+                "frac_of_roofline": round(ideal / ms_nccl, 3),
+                "max_abs_diff_vs_fused": float((y.float() - y_fused.float()).abs().max())})
+    ms_g = _timed(lambda: ops.linear(x, full[:N * K].view(N, K), out=y), iters=10)
+    out.append({"case": f"gemm_only_{M}x{K}x{N}", "world": W, "ms": round(ms_g, 4)})
+    # dgrad: dX [M, K] = dY [M, N] . W [N, K] (weight as the MN-major operand, gathered by k-blocks)
+    dy = torch.randn(M, N, device=dev).to(torch.bfloat16)
+    dx = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+    ms = _timed(lambda: ops.grad_input(dy, sw, out=dx), iters=10)
+    ops.check_errors(local)
+    out.append({"case": f"gemm_gather_dgrad_{M}x{N}x{K}", "world": W, "ms": round(ms, 4), "roofline_ms": round(ideal, 4),
+                "frac_of_roofline": round(ideal / ms, 3)})
+
     if r == 0:
         for row in out:
             print(json.dumps(row), flush=True)
     torch.cuda.synchronize()
     dist.barrier()
-    for b in (grads, sig, params, rows, flags):
+    for b in (grads, sig, params, rows, flags_tp, wsh):
         b.close()
     dist.destroy_process_group()
 

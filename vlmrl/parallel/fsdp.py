@@ -22,12 +22,26 @@ Communication (``comm``):
   them.  No NCCL all-gather or reduce-scatter runs in a step.
 * ``nccl`` (also gloo on CPU): NCCL/gloo reduce-scatter per unit and an
   all-gather of each stale unit on first use after a step — the baseline.
+
+Sharded parameters (``shard_params=True`` with ``p2p``; ZeRO-3 style, for
+models whose bf16 copy should not stay resident next to the activations):
+the decoder-layer units keep only their bf16 shard, in an IPC-shared buffer.
+The training forward and backward read the four weight matrices of a layer
+through ``ops.ShardedWeight``: the GEMM that consumes a matrix copies its
+rows from every rank's shard into a local work buffer inside the kernel,
+chunk by chunk, while its MMAs run (the all-gather fused into the GEMM);
+the small leaves (norm weights, biases) come from one ``unit_gather``
+kernel per layer.  Two work buffers alternate between consecutive layers.
+Rollout runs inside ``inference_weights()``, which gathers whole units into
+a temporary copy.  The optimizer writes the new bf16 shard in place and a
+device-side barrier publishes it before the next gather reads it.
 """
 
 from __future__ import annotations
 
+import contextlib
 import os
-from typing import Dict, Iterable, List, Optional, Sequence
+from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
@@ -40,6 +54,24 @@ from vlmrl.parallel.dist import all_gather_into, all_reduce_, reduce_scatter_int
 
 
 _CHECK_COLLECTIVES = os.environ.get("VLMRL_CHECK_COLLECTIVES", "0") == "1"
+
+# matrices of a decoder-layer unit that sharded-parameter mode gathers inside their GEMMs
+GATHERED_LEAVES = ("qkv_w", "o_w", "gu_w", "down_w")
+
+
+def _small_ranges(layout: UnitLayout, skip: Sequence[str]) -> List[Tuple[int, int]]:
+    """Byte ranges of a unit's leaves outside ``skip`` (16-byte rounded, neighbours merged)."""
+    out: List[Tuple[int, int]] = []
+    for prm in layout.params:
+        if prm.name in skip:
+            continue
+        a = layout.offsets[prm.name] * 2
+        b = -(-(layout.offsets[prm.name] + prm.numel) * 2 // 16) * 16
+        if out and a <= -(-out[-1][1] // 256) * 256:
+            out[-1] = (out[-1][0], max(out[-1][1], b))
+        else:
+            out.append((a, b))
+    return out
 
 
 class FSDPParams:
@@ -58,7 +90,7 @@ class FSDPParams:
 
     def __init__(self, layouts: Sequence[UnitLayout], full_units: Dict[str, torch.Tensor], *, group=None,
                  dtype=torch.bfloat16, trainable: Optional[Iterable[str]] = None, replicate: Iterable[str] = (),
-                 comm: Optional[str] = None):
+                 comm: Optional[str] = None, shard_params: Optional[bool] = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -82,6 +114,12 @@ class FSDPParams:
             if self.device.type != "cuda" or self.world > 8 or not p2p_supported(group):
                 comm = "nccl"
         self.comm = comm
+        if shard_params is None:
+            shard_params = os.environ.get("VLMRL_FSDP_SHARD_PARAMS", "0") == "1"
+        self.shard_params = bool(shard_params) and comm == "p2p"
+        self.sharded: List[str] = []
+        self._infer: Optional[Dict[str, torch.Tensor]] = None
+        self.graph_epoch = 0          # changes whenever inference weights move (captured graphs are stale)
         rep = set(replicate)
         sharded = []
         for name, lay in self.layouts.items():
@@ -115,13 +153,29 @@ class FSDPParams:
         W = self.world
         self.g_off: Dict[str, int] = {}
         self.p_off: Dict[str, int] = {}
-        go = po = 0
+        self.s_off: Dict[str, int] = {}
+        self.sharded = [u for u in self.order if self.shard_params and u.startswith("layer")]
+        self.sharded_set = set(self.sharded)
+        go = po = so = 0
         for u in self.order:
-            self.g_off[u], self.p_off[u] = go, po
+            self.g_off[u] = go
             go += self.padded[u] * 4
-            po += self.padded[u] * 2
+            if u in self.sharded_set:
+                self.s_off[u] = so
+                so += self.padded[u] // W * 2
+            else:
+                self.p_off[u] = po
+                po += self.padded[u] * 2
         self.sym_grad = SymmetricBuffer(go, self.group, self.device)
-        self.sym_param = SymmetricBuffer(po, self.group, self.device)
+        self.sym_param = SymmetricBuffer(max(po, 256), self.group, self.device)
+        self.sym_shard = None
+        if self.sharded:
+            self.sym_shard = SymmetricBuffer(so, self.group, self.device)
+            big = max(self.padded[u] for u in self.sharded)
+            self.work = [torch.empty(big, dtype=self.dtype, device=self.device) for _ in range(2)]
+            self.g_flags = torch.zeros(8192, dtype=torch.int32, device=self.device)
+            self.g_ctr = torch.zeros(2, dtype=torch.int32, device=self.device)
+            self.ranges = {u: _small_ranges(self.layouts[u], GATHERED_LEAVES) for u in self.sharded}
         self.n_slots = len(self.order) + 2          # one per unit (reduce-scatter), push, barrier
         self.sym_sig = SymmetricBuffer(self.n_slots * W * 8, self.group, self.device)
         self.push_slot, self.barrier_slot = len(self.order), len(self.order) + 1
@@ -131,11 +185,16 @@ class FSDPParams:
         self.grad_live: Dict[str, bool] = {}
         self.reduced: Dict[str, bool] = {u: False for u in self.order}
         for u in self.order:
-            self.gathered[u] = self.sym_param.view(self.p_off[u], (self.padded[u],), self.dtype)
             self.grads_full[u] = self.sym_grad.view(self.g_off[u], (self.padded[u],), torch.float32)
             self.grad_live[u] = False
-            all_gather_into(self.gathered[u], self.shards[u], group=self.group)
             self.fresh[u] = True
+            if u in self.sharded_set:
+                view = self.sym_shard.view(self.s_off[u], (self.padded[u] // W,), self.dtype)
+                view.copy_(self.shards[u])
+                self.shards[u] = view       # the optimizer writes the gather source in place
+                continue
+            self.gathered[u] = self.sym_param.view(self.p_off[u], (self.padded[u],), self.dtype)
+            all_gather_into(self.gathered[u], self.shards[u], group=self.group)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
 
@@ -164,16 +223,62 @@ class FSDPParams:
     def close(self) -> None:
         """Release the IPC-shared buffers (collective)."""
         if self.comm == "p2p":
-            for b in (self.sym_grad, self.sym_param, self.sym_sig):
-                b.close()
+            for b in (self.sym_grad, self.sym_param, self.sym_sig, self.sym_shard):
+                if b is not None:
+                    b.close()
             self.gathered.clear()
             self.grads_full.clear()
             self.comm = "closed"
+
+    # ---------------------------------------------------------------- sharded parameters
+    def _shard_srcs(self, name: str) -> Tuple[List[int], int]:
+        return [ptr + self.s_off[name] for ptr in self.sym_shard.ptrs], self.padded[name] // self.world * 2
+
+    def _gather_whole(self, name: str) -> torch.Tensor:
+        full = torch.empty(self.padded[name], dtype=self.dtype, device=self.device)
+        srcs, sb = self._shard_srcs(name)
+        ops.unit_gather(srcs, full.data_ptr(), sb, [(0, self.padded[name] * 2)])
+        return full
+
+    def views(self, name: str, layout: UnitLayout) -> Optional[Dict[str, object]]:
+        """Executor hook: the leaves of a sharded unit, its matrices as ``ops.ShardedWeight`` (gathered by the
+        GEMMs that read them).  None for every other unit (the executor then slices ``get(name)``)."""
+        if name not in getattr(self, "sharded_set", ()):
+            return None
+        if self._infer is not None:
+            return layout.views(self._infer[name])
+        buf = self.work[int(name[len("layer"):]) % 2]
+        srcs, sb = self._shard_srcs(name)
+        base = buf.data_ptr()
+        ops.unit_gather(srcs, base, sb, self.ranges[name])
+        v: Dict[str, object] = dict(layout.views(buf))
+        for k in GATHERED_LEAVES:
+            if k in v:
+                v[k] = ops.ShardedWeight(v[k], srcs, base, sb, self.g_flags, self.g_ctr)
+        return v
+
+    @contextlib.contextmanager
+    def inference_weights(self):
+        """Whole copies of the sharded units for rollout (decode graphs need plain weight tensors); freed on
+        exit.  A no-op without sharded parameters."""
+        if not self.sharded or self._infer is not None:
+            yield
+            return
+        self._infer = {u: self._gather_whole(u) for u in self.sharded}
+        self.graph_epoch += 1
+        try:
+            yield
+        finally:
+            self._infer = None
+            self.graph_epoch += 1
 
     # ---------------------------------------------------------------- ParamSource protocol
     def get(self, name: str) -> torch.Tensor:
         if name in self.replicated:
             return self.replicated[name]
+        if name in getattr(self, "sharded_set", ()):
+            full = self._infer[name] if self._infer is not None else self._gather_whole(name)
+            return full[:self.layouts[name].numel]
         buf = self.gathered[name]
         if not self.fresh[name]:
             all_gather_into(buf, self.shards[name], group=self.group)
@@ -257,7 +362,11 @@ class FSDPParams:
     def regather(self) -> None:
         """Refill every gathered buffer from the shards (collective; used after loading a checkpoint)."""
         for u in self.order:
-            all_gather_into(self.gathered[u], self.shards[u], group=self.group)
+            if u in self.gathered:
+                all_gather_into(self.gathered[u], self.shards[u], group=self.group)
+        if self.sharded:    # peers read the reloaded shards directly: publish them
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
             self.fresh[u] = True
 
 
@@ -290,6 +399,13 @@ class FSDPOptimizer:
         if p.comm == "p2p":
             W = p.world
             for u in self.units:
+                if u in p.sharded_set:
+                    # sharded parameters: the new bf16 shard is written in place; peers gather it later
+                    ops.adamw_(self.master[u], p.grad_shards[u], self.m[u], self.v[u], lr=c.lr, beta1=c.beta1,
+                               beta2=c.beta2, eps=c.eps, weight_decay=c.weight_decay, step=step, grad_scale=scale,
+                               p_half=p.shards[u])
+                    p.grad_shards[u].zero_()
+                    continue
                 n = p.padded[u] // W
                 grid = ext().adamw_push(self.master[u], p.grad_shards[u], self.m[u], self.v[u], p.sym_param.ptrs,
                                             p.p_off[u] + p.rank * n * 2, scale, c.lr, c.beta1, c.beta2, c.eps,
@@ -298,6 +414,10 @@ class FSDPOptimizer:
                 p.shards[u].copy_(self.master[u])
                 p.grad_shards[u].zero_()
             ext().peer_wait(p.sym_sig.local, p.push_slot, p.push_target, p.rank, W, p.sym_sig.dev_index)
+            if p.sharded:
+                # every rank's shards are updated before any rank's next gather reads them
+                p.barrier_epoch += 1
+                ext().peer_barrier(p.sym_sig.ptrs, p.barrier_slot, p.barrier_epoch, p.rank, p.sym_sig.dev_index)
             if _CHECK_COLLECTIVES:
                 ops.check_errors(p.sym_sig.dev_index)
                 p.verify_signals()
@@ -361,7 +481,7 @@ class FSDPOptimizer:
 
 
 def build_fsdp_models(spec, adamw: AdamWConfig, *, seed: int = 0, device=None, group=None, dtype=torch.bfloat16,
-                      units: Optional[Dict[str, torch.Tensor]] = None):
+                      units: Optional[Dict[str, torch.Tensor]] = None, shard_params: Optional[bool] = None):
     """-> (policy model on FSDP params, frozen replicated reference model, TrainState).
 
     ``units`` (full parameter units, e.g. loaded from a checkpoint) replace the seeded random init.
@@ -377,7 +497,7 @@ def build_fsdp_models(spec, adamw: AdamWConfig, *, seed: int = 0, device=None, g
         units = {k: v.to(device, dtype) for k, v in units.items()}
     ref = Qwen3VLModel(spec, units={k: v for k, v in units.items() if k != "visual"}, device=device, dtype=dtype)
     fp = FSDPParams(all_layouts(spec), units, group=group, dtype=dtype,
-                    trainable=[l.name for l in text_layouts(spec)], replicate=["visual"])
+                    trainable=[l.name for l in text_layouts(spec)], replicate=["visual"], shard_params=shard_params)
     del units
     model = Qwen3VLModel(spec, params=fp, device=device, dtype=dtype)
     if not isinstance(adamw, AdamWConfig):
