@@ -8,6 +8,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &vlm::gemm, "tcgen05 GEMM with fused epilogues");
   m.def("gemm_gather", &vlm::gemm_gather, "tcgen05 GEMM whose weight operand is all-gathered from peer shards in-kernel");
   m.def("unit_gather", &vlm::unit_gather, "copy byte ranges of a sharded unit from the peers' shards");
+  m.def("dec_gemm_qkv", &vlm::dec_gemm_qkv, "decode qkv GEMM with the q/k norm + RoPE + KV append consumer fused");
+  m.def("dec_gemm_residual_norm", &vlm::dec_gemm_residual_norm, "decode GEMM with residual + RMSNorm fused");
+  m.def("dec_gemm_swiglu", &vlm::dec_gemm_swiglu, "decode gate/up GEMM with SwiGLU fused");
   m.def("gemm_partials", &vlm::gemm_partials, "stream-K partial sums for the fused decode consumers");
   m.def("gemm_partials_traced", &vlm::gemm_partials_traced, "gemm_partials with per-CTA phase timestamps");
   m.def("set_static_weights", &vlm::set_static_weights);

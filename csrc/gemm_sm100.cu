@@ -28,10 +28,18 @@
 #include "common.cuh"
 #include "host_utils.h"
 #include "peer.cuh"
+#include "dec_fused.cuh"
 #include "vlm_ops.h"
 #include "streamk.cuh"
 
 namespace vlm {
+
+using bf16_t = __nv_bfloat16;
+
+struct DecFuse {
+  int consumer;
+  DecArgs args;
+};
 
 enum Epi : int {
   EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GELU_TANH = 2, EPI_GELU_ERF = 3, EPI_VOCAB_STATS = 4, EPI_VOCAB_GRAD = 5,
@@ -85,6 +93,10 @@ struct GemmParams {
   int g_rows, g_chunks, g_pieces;
   unsigned* g_flags;  // [g_chunks] pieces arrived; zero between launches (the last CTA to exit resets them)
   unsigned* g_ctr;    // [2] piece claim counter, exited CTAs; zero between launches
+  // decode consumer run by all CTAs after a grid-wide barrier (stream-K launches only; dec_fused.cuh)
+  int consumer;
+  unsigned* gbar;
+  DecArgs dec;
 };
 
 constexpr int kGatherPiece = 16384;   // bytes per claimed piece
@@ -757,6 +769,23 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       }
     }
   }
+  if constexpr (!A_MN && !B_MN && !GATHER) {
+    if (p.consumer != DEC_NONE && dec_grid_sync(p.gbar, p.err, last_cta)) {
+      const SkMeta m{p.M, p.N, p.tiles_m, p.tiles_n, kb_count, p.sk_grid, kBM, BN};
+      if (p.consumer == DEC_QKV) {
+        if (p.dec.head_dim == 128)
+          dec_qkv_part<128>(p.ws, m, p.dec);
+        else if (p.dec.head_dim == 64)
+          dec_qkv_part<64>(p.ws, m, p.dec);
+        else
+          dec_qkv_part<32>(p.ws, m, p.dec);
+      } else if (p.consumer == DEC_RESNORM) {
+        dec_resnorm_part<4>(p.ws, m, p.dec, epi_stage);
+      } else {
+        dec_swiglu_part(p.ws, m, p.dec);
+      }
+    }
+  }
   if (threadIdx.x == 0) trace_mark(p, 7);
 }
 
@@ -800,7 +829,8 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParam
     VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM));
     configured = true;
   }
-  launch_pdl(kern, dim3(grid), dim3(GATHER ? 256 : 192), GemmCfg<BN>::SMEM, st, ta, tb, p);
+  // a fused decode consumer waits at a grid-wide barrier: cooperative launch keeps every CTA resident
+  launch_ex(p.consumer != DEC_NONE, kern, dim3(grid), dim3(GATHER ? 256 : 192), GemmCfg<BN>::SMEM, st, ta, tb, p);
 }
 
 static void check_operand(const at::Tensor& t, const char* name) {
@@ -812,7 +842,7 @@ static void check_operand(const at::Tensor& t, const char* name) {
 
 void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
              bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, const VocabArgs* vocab,
-             int force_bn, at::Tensor* partials_out, SkMeta* meta_out, const GatherArgs* gather) {
+             int force_bn, at::Tensor* partials_out, SkMeta* meta_out, const GatherArgs* gather, const DecFuse* fuse) {
   check_operand(A, "A");
   check_operand(B, "B");
   const c10::cuda::CUDAGuard guard(A.device());
@@ -929,6 +959,12 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   // Skinny problems (decode, M <= 2 tiles): stream-K over (tile, k-block) units so every SM gets the
   // same amount of weight streaming; partial sums go to a [slots, M, N] fp32 workspace.
   const int64_t units = tiles * kb_count;
+  if (fuse) {
+    TORCH_CHECK(want_partials && !gather, "fused decode consumer: stream-K partials only");
+    p.consumer = fuse->consumer;
+    p.dec = fuse->args;
+    p.gbar = grid_barrier_words(A.device().index());
+  }
   if (want_partials || (splittable && p.tiles_m <= 2 && tiles < 4 * sms && units >= 2 * sms)) {
     TORCH_CHECK(!want_partials || (a_kmajor && b_kmajor && alpha == 1.0), "gemm partials: K-major operands only");
     p.streamk = 1;
@@ -1035,6 +1071,78 @@ void unit_gather(std::vector<int64_t> srcs, int64_t dst_base, int64_t shard_byte
   const int grid = static_cast<int>(std::min<long long>((total / 16 + threads - 1) / threads, 4 * 148));
   launch_pdl(unit_gather_kernel, dim3(grid), dim3(threads), 0, at::cuda::getCurrentCUDAStream(), make_peer_table(srcs),
              reinterpret_cast<uint8_t*>(dst_base), static_cast<long long>(shard_bytes), r);
+}
+
+// ------------------------------------------------------------------ decode GEMMs with fused consumers
+static const bf16_t* bf16_ptr_or_null(const at::Tensor& t) {
+  return t.defined() && t.numel() ? reinterpret_cast<const bf16_t*>(t.data_ptr()) : nullptr;
+}
+
+static void dec_gemm_run(const at::Tensor& x, const at::Tensor& w, DecFuse& f) {
+  at::Tensor ws;
+  SkMeta m{};
+  gemm_ex(x, w, at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(), true, true, 1.0, EPI_STORE, false, nullptr, 0,
+          &ws, &m, nullptr, &f);
+}
+
+at::Tensor dec_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor bias, at::Tensor qw, at::Tensor kw, at::Tensor lengths,
+                        at::Tensor delta, at::Tensor inv_freq, at::Tensor kc, at::Tensor vc, int64_t nq, int64_t nkv,
+                        double eps) {
+  const int D = static_cast<int>(kc.size(-1));
+  TORCH_CHECK(D == 128 || D == 64 || D == 32, "dec_gemm_qkv: head_dim 32, 64 or 128");
+  TORCH_CHECK(w.size(0) == (nq + 2 * nkv) * D, "dec_gemm_qkv: width mismatch");
+  TORCH_CHECK(lengths.scalar_type() == at::kInt && delta.scalar_type() == at::kLong, "dec_gemm_qkv: int32 lengths, int64 deltas");
+  TORCH_CHECK(kc.is_contiguous() && vc.is_contiguous(), "dec_gemm_qkv: contiguous cache layer");
+  const c10::cuda::CUDAGuard g(x.device());
+  at::Tensor q = at::empty({x.size(0), nq, D}, kc.options());
+  DecFuse f{};
+  f.consumer = DEC_QKV;
+  f.args.bias = bf16_ptr_or_null(bias);
+  f.args.qw = bf16_ptr_or_null(qw);
+  f.args.kw = bf16_ptr_or_null(kw);
+  f.args.lengths = lengths.data_ptr<int>();
+  f.args.delta = delta.data_ptr<int64_t>();
+  f.args.inv_freq = inv_freq.data_ptr<float>();
+  f.args.q = reinterpret_cast<bf16_t*>(q.data_ptr());
+  f.args.kc = reinterpret_cast<bf16_t*>(kc.data_ptr());
+  f.args.vc = reinterpret_cast<bf16_t*>(vc.data_ptr());
+  f.args.nq = static_cast<int>(nq);
+  f.args.nkv = static_cast<int>(nkv);
+  f.args.Tmax = static_cast<int>(kc.size(-2));
+  f.args.head_dim = D;
+  f.args.eps = static_cast<float>(eps);
+  dec_gemm_run(x, w, f);
+  return q;
+}
+
+std::tuple<at::Tensor, at::Tensor> dec_gemm_residual_norm(at::Tensor x, at::Tensor w, at::Tensor residual, at::Tensor nw,
+                                                          double eps) {
+  const int64_t H = w.size(0);
+  TORCH_CHECK(residual.is_contiguous() && residual.size(0) == x.size(0) && residual.size(1) == H,
+              "dec_gemm_residual_norm: residual shape");
+  TORCH_CHECK(H % 8 == 0 && H <= 8 * 192 * 4, "dec_gemm_residual_norm: width");
+  const c10::cuda::CUDAGuard g(x.device());
+  at::Tensor h = at::empty_like(residual), hn = at::empty_like(residual);
+  DecFuse f{};
+  f.consumer = DEC_RESNORM;
+  f.args.res = reinterpret_cast<const bf16_t*>(residual.data_ptr());
+  f.args.nw = reinterpret_cast<const bf16_t*>(nw.data_ptr());
+  f.args.h_out = reinterpret_cast<bf16_t*>(h.data_ptr());
+  f.args.hn_out = reinterpret_cast<bf16_t*>(hn.data_ptr());
+  f.args.eps = static_cast<float>(eps);
+  dec_gemm_run(x, w, f);
+  return {h, hn};
+}
+
+at::Tensor dec_gemm_swiglu(at::Tensor x, at::Tensor w) {
+  TORCH_CHECK(w.size(0) % 16 == 0, "dec_gemm_swiglu: width must be a multiple of 16");
+  const c10::cuda::CUDAGuard g(x.device());
+  at::Tensor act = at::empty({x.size(0), w.size(0) / 2}, x.options());
+  DecFuse f{};
+  f.consumer = DEC_SWIGLU;
+  f.args.act = reinterpret_cast<bf16_t*>(act.data_ptr());
+  dec_gemm_run(x, w, f);
+  return act;
 }
 
 // Stream-K partials with per-CTA phase timestamps written to ``trace`` (int64 [>= grid * 8]): a measurement

@@ -48,6 +48,18 @@ int* err_word(int device) {
   return g_err[device];
 }
 
+unsigned* grid_barrier_words(int device) {
+  static std::vector<unsigned*> words(64, nullptr);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!words[device]) {
+    unsigned* p = nullptr;
+    VLM_CUDA_CHECK(cudaMalloc(&p, sizeof(unsigned) * 4));
+    VLM_CUDA_CHECK(cudaMemset(p, 0, sizeof(unsigned) * 4));
+    words[device] = p;
+  }
+  return words[device];
+}
+
 int64_t read_and_clear_error(int64_t device) {
   int* w = err_word(static_cast<int>(device));
   int h = 0;

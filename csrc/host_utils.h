@@ -51,7 +51,8 @@ inline bool pdl_enabled() {
 // the stream is still running and must call pdl_wait() before reading or writing data the predecessor
 // touches.
 template <typename... KArgs, typename... Args>
-inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+inline void launch_ex(bool cooperative, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                      Args&&... args) {
   // Every kernel launched here asks for the maximum shared-memory carveout, so SMs never have to be
   // reconfigured between consecutive kernels of different shared-memory footprints (which would also
   // serialise programmatic dependent launches).
@@ -61,17 +62,33 @@ inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cooperative) {  // all CTAs co-resident (the kernel has a grid-wide barrier), or the launch fails
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n].val.cooperative = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = n;
   VLM_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(std::forward<Args>(args))...));
   note_launch();
 }
 
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  launch_ex(false, kern, grid, block, smem, st, std::forward<Args>(args)...);
+}
+
 // Per-device error word written by bounded waits (0 = ok).  Allocated once per device.
 int* err_word(int device);
+// Per-device words of the self-resetting grid barrier used by the fused decode GEMMs (zeroed once).
+unsigned* grid_barrier_words(int device);
 // Reads and clears the error word of ``device`` (synchronises the current stream).
 int64_t read_and_clear_error(int64_t device);
 int num_sms(int device);

@@ -9,6 +9,7 @@
 namespace vlm {
 
 struct SkMeta;
+struct DecFuse;
 
 struct VocabArgs {
   const int64_t* targets;
@@ -34,7 +35,16 @@ void gemm(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor 
           bool b_kmajor, double alpha, int64_t epi, bool accumulate);
 void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
              bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, const VocabArgs* vocab,
-             int force_bn, at::Tensor* partials_out, SkMeta* meta_out, const GatherArgs* gather = nullptr);
+             int force_bn, at::Tensor* partials_out, SkMeta* meta_out, const GatherArgs* gather = nullptr,
+             const DecFuse* fuse = nullptr);
+// Decode GEMMs (x [B, K] . w^T) whose consumer runs inside the GEMM after a grid-wide barrier: the same
+// results as gemm_partials followed by dec_qkv / dec_residual_norm / dec_swiglu, one launch each.
+at::Tensor dec_gemm_qkv(at::Tensor x, at::Tensor w, at::Tensor bias, at::Tensor qw, at::Tensor kw, at::Tensor lengths,
+                        at::Tensor delta, at::Tensor inv_freq, at::Tensor kc, at::Tensor vc, int64_t nq, int64_t nkv,
+                        double eps);
+std::tuple<at::Tensor, at::Tensor> dec_gemm_residual_norm(at::Tensor x, at::Tensor w, at::Tensor residual, at::Tensor nw,
+                                                          double eps);
+at::Tensor dec_gemm_swiglu(at::Tensor x, at::Tensor w);
 // gemm() whose B rows are all-gathered from the ranks' shards inside the kernel (see GatherArgs)
 void gemm_gather(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tensor residual, at::Tensor aux,
                  bool a_kmajor, bool b_kmajor, double alpha, int64_t epi, bool accumulate, std::vector<int64_t> srcs,

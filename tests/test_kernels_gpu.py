@@ -464,3 +464,54 @@ def test_unit_gather_ranges():
         assert torch.equal(dst[a // 2:b // 2], full[a // 2:b // 2])
     assert int(dst[lead:lead + 96 * 64].abs().sum()) == 0
     _no_device_error()
+
+
+@pytest.mark.parametrize("B", [3, 64])
+@pytest.mark.parametrize("norm", [True, False])
+def test_decode_gemms_with_fused_consumers_match_separate_kernels(B, norm):
+    """The decode GEMMs that run their consumer after a grid-wide barrier (one launch) produce what the
+    stream-K GEMM followed by the separate consumer kernel produces, and replay from a CUDA graph."""
+    nq, nkv, D, H, F, Tmax = 8, 2, 128, 1024, 2048, 96
+    rope = ops.RopeCfg(D, 5e6, (24, 20, 20), True)
+    x = _r(B, H, seed=1)
+    w_qkv = _r((nq + 2 * nkv) * D, H, scale=0.03, seed=2)
+    bias = _r((nq + 2 * nkv) * D, scale=0.1, seed=3)
+    qw, kw = (_r(D, seed=4) + 1, _r(D, seed=5) + 1) if norm else (None, None)
+    g = torch.Generator(device=DEV).manual_seed(6)
+    lens = torch.randint(0, Tmax - 1, (B,), generator=g, device=DEV, dtype=torch.int32)
+    delta = torch.randint(-5, 5, (B,), generator=g, device=DEV, dtype=torch.int64)
+    caches = [(torch.zeros(B, nkv, Tmax, D, dtype=torch.bfloat16, device=DEV),
+               torch.zeros(B, nkv, Tmax, D, dtype=torch.bfloat16, device=DEV)) for _ in range(2)]
+    ws, meta = ops.gemm_partials(x, w_qkv)
+    q1 = ops.dec_qkv(ws, meta, bias, qw, kw, lens, delta, rope, *caches[0], n_q=nq, n_kv=nkv, eps=1e-6)
+    q2 = ops.dec_linear_qkv(x, w_qkv, bias, qw, kw, lens, delta, rope, *caches[1], n_q=nq, n_kv=nkv, eps=1e-6)
+    _close(q2, q1, rtol=1e-2, atol=1e-2, name="q")
+    _close(caches[1][0], caches[0][0], rtol=1e-2, atol=1e-2, name="k cache")
+    _close(caches[1][1], caches[0][1], rtol=1e-2, atol=1e-2, name="v cache")
+
+    res = _r(B, H, seed=7)
+    w_o, nw = _r(H, nq * D, scale=0.03, seed=8), _r(H, seed=9) + 1
+    o = _r(B, nq * D, seed=10)
+    ws, meta = ops.gemm_partials(o, w_o)
+    h1, hn1 = ops.dec_residual_norm(ws, meta, res, nw, 1e-6)
+    h2, hn2 = ops.dec_linear_residual_norm(o, w_o, res, nw, 1e-6)
+    _close(h2, h1, rtol=1e-2, atol=1e-2, name="h")
+    _close(hn2, hn1, rtol=1e-2, atol=1e-2, name="hn")
+
+    w_gu = _r(2 * F, H, scale=0.03, seed=11)
+    ws, meta = ops.gemm_partials(hn1, w_gu)
+    a1 = ops.dec_swiglu(ws, meta)
+    a2 = ops.dec_linear_swiglu(hn1, w_gu)
+    _close(a2, a1, rtol=1e-2, atol=1e-2, name="swiglu")
+
+    # graph replay: the grid barrier resets itself between launches
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        a3 = ops.dec_linear_swiglu(hn1, w_gu)
+        h3, hn3 = ops.dec_linear_residual_norm(o, w_o, res, nw, 1e-6)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    _close(a3, a1, rtol=1e-2, atol=1e-2, name="swiglu (graph)")
+    _close(hn3, hn1, rtol=1e-2, atol=1e-2, name="hn (graph)")
+    _no_device_error()

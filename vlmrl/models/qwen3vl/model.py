@@ -104,8 +104,13 @@ class KVCache:
         return cls(num_layers, batch, num_heads, max_len, head_dim, dtype, device)
 
 
-# Decode kernels ask the L2 to fetch the next GEMM's weights (VLMRL_DECODE_L2_PREFETCH=0 turns it off).
-_DECODE_L2_PREFETCH = os.environ.get("VLMRL_DECODE_L2_PREFETCH", "1") != "0"
+# VLMRL_DECODE_L2_PREFETCH=1: decode kernels ask the L2 to fetch the next GEMM's weights.  Off by default:
+# on the 4B model at batch 64 it measured slower (4.70 vs 4.44 ms per step); the decode GEMMs are bound by
+# their fixed pipeline latency, and the prefetched lines compete with the KV-cache stream for L2.
+_DECODE_L2_PREFETCH = os.environ.get("VLMRL_DECODE_L2_PREFETCH", "0") == "1"
+# Decode GEMMs run their consumer (q/k/v, residual + norm, SwiGLU) in the same launch after a grid-wide
+# barrier; VLMRL_DECODE_FUSED=0 selects separate consumer kernels.
+_DECODE_FUSED_CONSUMERS = os.environ.get("VLMRL_DECODE_FUSED", "1") != "0"
 
 
 # --------------------------------------------------------------------------- parameter sources
@@ -394,14 +399,27 @@ class TextDecoder:
         lens_after = lens + 1
         w = self._w(params, "layer0")
         xn, _ = ops.rms_norm(x, w["input_norm"], self.eps)
-        # The kernels between two GEMMs are latency-bound; each asks the L2 to fetch (part of) the next
-        # GEMM's weights while it runs: o_proj during the q/k/v consumer, the first half of gate/up during
-        # attention and the rest during the o_proj consumer, down during SwiGLU, the next layer's qkv during
-        # the closing residual + norm.
+        # Optional L2 prefetch plan (see _DECODE_L2_PREFETCH): o_proj during the q/k/v consumer, the first
+        # half of gate/up during attention and the rest during the o_proj consumer, down during SwiGLU, the
+        # next layer's qkv during the closing residual + norm.
         pf = _DECODE_L2_PREFETCH
+        fused = _DECODE_FUSED_CONSUMERS and not pf
         for i in range(self.n_layers):
             w = self._w(params, f"layer{i}")
             nxt_w = self._w(params, f"layer{i + 1}") if i + 1 < self.n_layers else None
+            nxt = nxt_w["input_norm"] if nxt_w is not None else self._w(params, "head")["final_norm"]
+            if fused:
+                # four launches + attention per layer: each consumer runs inside its GEMM
+                q = ops.dec_linear_qkv(xn, w["qkv_w"], w["qkv_b"], w.get("q_norm"), w.get("k_norm"), lens, delta,
+                                       self.rope, cache.keys[i], cache.values[i], n_q=self.nq, n_kv=self.nkv,
+                                       eps=self.eps)
+                o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale)
+                h1, hn = ops.dec_linear_residual_norm(o.reshape(B, self.nq * self.D), w["o_w"], x, w["post_norm"],
+                                                      self.eps)
+                act = ops.dec_linear_swiglu(hn, w["gu_w"])
+                x, xn = ops.dec_linear_residual_norm(act, w["down_w"], h1, nxt, self.eps)
+                params.release(f"layer{i}")
+                continue
             gu = w["gu_w"].reshape(-1)
             half = (gu.numel() // 2) // 128 * 128
             ws, meta = ops.gemm_partials(xn, w["qkv_w"])
@@ -415,10 +433,6 @@ class TextDecoder:
             ws, meta = ops.gemm_partials(hn, w["gu_w"])
             act = ops.dec_swiglu(ws, meta, prefetch=w["down_w"] if pf else None)
             ws, meta = ops.gemm_partials(act, w["down_w"])
-            if nxt_w is not None:
-                nxt = nxt_w["input_norm"]
-            else:
-                nxt = self._w(params, "head")["final_norm"]
             x, xn = ops.dec_residual_norm(ws, meta, h1, nxt, self.eps,
                                           prefetch=nxt_w["qkv_w"] if pf and nxt_w is not None else None)
             params.release(f"layer{i}")

@@ -209,6 +209,25 @@ def dec_qkv(ws, meta, bias, q_w, k_w, lengths, delta, rope: "RopeCfg", k_cache, 
                          float(eps), prefetch)
 
 
+def dec_linear_qkv(x, w, bias, q_w, k_w, lengths, delta, rope: "RopeCfg", k_cache, v_cache, *, n_q: int, n_kv: int,
+                   eps: float):
+    """``dec_qkv`` of ``x @ w.T`` in one launch: the consumer runs inside the stream-K GEMM after a grid-wide
+    barrier (CUDA only)."""
+    f, _ = rope.device_tables(x.device)
+    return ext().dec_gemm_qkv(x, w, _opt(bias), _opt(q_w), _opt(k_w), lengths, delta, f, k_cache, v_cache, n_q, n_kv,
+                              float(eps))
+
+
+def dec_linear_residual_norm(x, w, residual, nw, eps: float):
+    """``dec_residual_norm`` of ``x @ w.T`` in one launch (consumer fused into the GEMM; CUDA only)."""
+    return ext().dec_gemm_residual_norm(x, w, residual, nw, float(eps))
+
+
+def dec_linear_swiglu(x, w):
+    """``dec_swiglu`` of ``x @ w.T`` in one launch (consumer fused into the GEMM; CUDA only)."""
+    return ext().dec_gemm_swiglu(x, w)
+
+
 def dec_residual_norm(ws, meta, residual, w, eps: float, prefetch=None):
     """h = sum(partials) + residual (bf16); returns (h, rms_norm(h) * w)."""
     return ext().dec_residual_norm(ws, list(meta), residual, w, float(eps), prefetch)

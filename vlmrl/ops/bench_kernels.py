@@ -312,7 +312,40 @@ def _profile_inputs(case: str):
         ph = torch.empty(n, dtype=torch.bfloat16, device="cuda")
         return lambda: ops.adamw_(p, gg, m, v, lr=1e-6, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01,
                                   step=1, p_half=ph)
+    if case == "gather":        # gate/up GEMM 4096 x 2560 -> 19456 whose weight is assembled from 8 shards
+        return _gather_case(4096)[0]
+    if case == "decode_fused":  # decode GEMMs with their consumers fused behind a grid barrier (B=64)
+        x, w_gu, w_dn = _r(64, H), _r(19456, H, scale=0.02), _r(H, 9728, scale=0.02)
+        res, nw = _r(64, H), _r(H)
+        return lambda: ops.dec_linear_residual_norm(ops.dec_linear_swiglu(x, w_gu), w_dn, res, nw, 1e-6)
     raise KeyError(case)
+
+
+def _gather_case(M: int, W: int = 8):
+    """(fused run, plain run on the gathered weight): the weight of the 4B gate/up projection split into W
+    shards held in separate local buffers, standing in for W ranks (on one GPU the copy reads HBM, not
+    NVLink)."""
+    N, K = 19456, 2560
+    P = -(-N * K // (128 * W)) * 128 * W
+    n = P // W
+    shards = [_r(n, scale=0.02) for _ in range(W)]
+    dst = torch.empty(P, dtype=torch.bfloat16, device="cuda")
+    flags = torch.zeros(8192, dtype=torch.int32, device="cuda")
+    ctr = torch.zeros(2, dtype=torch.int32, device="cuda")
+    sw = ops.ShardedWeight(dst[:N * K].view(N, K), [s.data_ptr() for s in shards], dst.data_ptr(), n * 2, flags, ctr)
+    x = _r(M, K)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    full = torch.cat(shards)[:N * K].view(N, K)
+    return (lambda: ops.linear(x, sw, out=y)), (lambda: ops.linear(x, full, out=y))
+
+
+def bench_gather(t: Timer):
+    """Fused all-gather GEMM vs the same GEMM on a resident weight (1 GPU, 8 emulated ranks)."""
+    M, N, K = 5112, 19456, 2560
+    fused, plain = _gather_case(M)
+    flops = 2.0 * M * N * K
+    for name, fn in (("gemm_gather_8shards", fused), ("gemm_resident_weight", plain)):
+        emit(f"{name}_{M}x{K}x{N}", t(fn), flops=flops)
 
 
 def profile_small(case: str = "decode"):
@@ -328,7 +361,7 @@ def profile_small(case: str = "decode"):
 
 
 CASES = {"gemm": bench_gemm, "attn": bench_attn, "decode": bench_decode, "vocab": bench_vocab, "norm": bench_norm,
-         "decode_step": bench_decode_step,
+         "decode_step": bench_decode_step, "gather": bench_gather,
          "gemm_tiny": bench_gemm_tiny, "train_step": bench_train_step}
 
 
@@ -339,7 +372,7 @@ def main():
     ap.add_argument("--eager-steps", type=int, default=0,
                     help="decode_step (default) or --only train_step: run N eager steps inside a profiler range "
                          "(for a launch list)")
-    ap.add_argument("--profile-small", default=None, choices=["decode", "gemm", "attn", "vocab", "adamw"],
+    ap.add_argument("--profile-small", default=None, choices=["decode", "gemm", "attn", "vocab", "adamw", "gather", "decode_fused"],
                     help="one launch of the named case's kernels inside a profiler range")
     args = ap.parse_args()
     if args.profile_small:
