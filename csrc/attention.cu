@@ -791,7 +791,8 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_consta
                                                              const bf16* __restrict__ q, const int* __restrict__ lens,
                                                              bf16* __restrict__ o, float* __restrict__ part, int Hq,
                                                              int Hkv, int Tmax, float scale_log2, int splits, int* err,
-                                                             L2Prefetch pf) {
+                                                             L2Prefetch pf, const int* __restrict__ lead,
+                                                             const int* __restrict__ share_len) {
   constexpr int D = 128, KC = 64;
   constexpr int HALF = KC * 64;  // elements of one 64x64 box
   extern __shared__ __align__(1024) uint8_t tc_raw[];
@@ -812,7 +813,11 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_consta
   const int nchunks = (nk + KC - 1) / KC;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, tq = lane & 3;
-  const int row_base = (b * Hkv + hk) * Tmax + k0;
+  // Shared prompt (GRPO groups): keys [0, share_len[b]) of row b equal those of row lead[b], so whole
+  // chunks inside that range are read from the leader's row; the group's CTAs then hit the same lines in
+  // L2 instead of streaming identical copies from HBM.
+  const int src_lead = lead ? lead[b] : b;
+  const int src_share = share_len ? share_len[b] : 0;
   if (tid == 0) {
     abort_flag = 0;
     for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
@@ -822,7 +827,8 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_consta
   auto issue = [&](int c) {
     const int st = c % STAGES;
     mbar_arrive_expect_tx(&full[st], 4 * HALF * 2);
-    const int y = row_base + c * KC;
+    const int t0 = k0 + c * KC;
+    const int y = ((t0 + KC <= src_share ? src_lead : b) * Hkv + hk) * Tmax + t0;
     tma_load_2d(sK + (st * 2 + 0) * HALF, &tmK, &full[st], 0, y);
     tma_load_2d(sK + (st * 2 + 1) * HALF, &tmK, &full[st], 64, y);
     tma_load_2d(sV + (st * 2 + 0) * HALF, &tmV, &full[st], 0, y);
@@ -1147,7 +1153,7 @@ static void decode_dispatch(const at::Tensor& q, const at::Tensor& kc, const at:
 
 template <int REP>
 static void decode_tc_dispatch(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& lens,
-                               at::Tensor& o, float scale, L2Prefetch pf) {
+                               at::Tensor& o, float scale, L2Prefetch pf, const int* lead, const int* share_len) {
   constexpr int STAGES = 3, D = 128;
   const int B = static_cast<int>(q.size(0)), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(kc.size(1));
   const int Tmax = static_cast<int>(kc.size(2));
@@ -1168,7 +1174,7 @@ static void decode_tc_dispatch(const at::Tensor& q, const at::Tensor& kc, const 
   if (splits > 1) part = at::empty({B, Hq, splits, D + 2}, q.options().dtype(at::kFloat));
   launch_pdl(kern, dim3(Hkv, B, splits), dim3(128), smem, st, tk, tv, reinterpret_cast<const bf16*>(q.data_ptr()),
              lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()), splits > 1 ? part.data_ptr<float>() : nullptr,
-             Hq, Hkv, Tmax, scale * kLog2e, splits, err_word(q.device().index()), pf);
+             Hq, Hkv, Tmax, scale * kLog2e, splits, err_word(q.device().index()), pf, lead, share_len);
   if (splits > 1) {
     launch_pdl(decode_combine_kernel, dim3(B * Hq), dim3(128), 0, st, part.data_ptr<float>(),
                reinterpret_cast<bf16*>(o.data_ptr()), B * Hq, splits, D);
@@ -1176,7 +1182,8 @@ static void decode_tc_dispatch(const at::Tensor& q, const at::Tensor& kc, const 
 }
 
 void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale,
-                 c10::optional<at::Tensor> prefetch) {
+                 c10::optional<at::Tensor> prefetch, c10::optional<at::Tensor> lead,
+                 c10::optional<at::Tensor> share_len) {
   TORCH_CHECK(q.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(), "decode_attn: contiguous");
   TORCH_CHECK(lens.scalar_type() == at::kInt, "decode_attn: int32 lengths");
   if (q.size(0) == 0) return;
@@ -1185,9 +1192,17 @@ void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at
   const int rep = static_cast<int>(q.size(1) / kc.size(1));
   const float sc = static_cast<float>(scale);
   const L2Prefetch pf = l2_prefetch_of<L2Prefetch>(prefetch);
-  if (D == 128 && rep == 4) return decode_tc_dispatch<4>(q, kc, vc, lens, o, sc, pf);
-  if (D == 128 && rep == 2) return decode_tc_dispatch<2>(q, kc, vc, lens, o, sc, pf);
-  if (D == 128 && rep == 8) return decode_tc_dispatch<8>(q, kc, vc, lens, o, sc, pf);
+  const bool share = lead.has_value() && lead->defined() && share_len.has_value() && share_len->defined();
+  if (share) {
+    TORCH_CHECK(lead->scalar_type() == at::kInt && share_len->scalar_type() == at::kInt && lead->numel() == q.size(0) &&
+                    share_len->numel() == q.size(0) && lead->is_contiguous() && share_len->is_contiguous(),
+                "decode_attn: lead / share_len must be int32 [B]");
+  }
+  const int* ld = share ? lead->data_ptr<int>() : nullptr;
+  const int* sl = share ? share_len->data_ptr<int>() : nullptr;
+  if (D == 128 && rep == 4) return decode_tc_dispatch<4>(q, kc, vc, lens, o, sc, pf, ld, sl);
+  if (D == 128 && rep == 2) return decode_tc_dispatch<2>(q, kc, vc, lens, o, sc, pf, ld, sl);
+  if (D == 128 && rep == 8) return decode_tc_dispatch<8>(q, kc, vc, lens, o, sc, pf, ld, sl);
 #define VLM_DEC(DD, RR) \
   if (D == DD && rep == RR) return decode_dispatch<DD, RR>(q, kc, vc, lens, o, sc);
   VLM_DEC(128, 4) VLM_DEC(128, 2) VLM_DEC(128, 1) VLM_DEC(128, 8) VLM_DEC(64, 4) VLM_DEC(64, 2) VLM_DEC(64, 1)

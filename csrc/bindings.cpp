@@ -43,7 +43,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("lse"), py::arg("cu"), py::arg("dq"), py::arg("dk"), py::arg("dv"), py::arg("max_seqlen"),
         py::arg("causal"), py::arg("scale"), py::arg("pre") = py::none(), py::arg("xq") = py::none());
   m.def("decode_attn", &vlm::decode_attn, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("lens"), py::arg("o"),
-        py::arg("scale"), py::arg("prefetch") = py::none());
+        py::arg("scale"), py::arg("prefetch") = py::none(), py::arg("lead") = py::none(),
+        py::arg("share_len") = py::none());
   m.def("sample", &vlm::sample);
   m.def("vocab_logprob_fwd", &vlm::vocab_logprob_fwd);
   m.def("vocab_logprob_bwd", &vlm::vocab_logprob_bwd);

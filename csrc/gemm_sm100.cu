@@ -90,7 +90,7 @@ struct GemmParams {
   PeerTable g_src;
   uint8_t* g_dst;
   long long g_off, g_shard_bytes, g_row_bytes;
-  int g_rows, g_chunks, g_pieces;
+  int g_rows, g_chunks, g_pieces, g_world;
   unsigned* g_flags;  // [g_chunks] pieces arrived; zero between launches (the last CTA to exit resets them)
   unsigned* g_ctr;    // [2] piece claim counter, exited CTAs; zero between launches
   // decode consumer run by all CTAs after a grid-wide barrier (stream-K launches only; dec_fused.cuh)
@@ -323,6 +323,11 @@ VLM_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global
 // reads of the chunk.
 VLM_DEV bool gather_wait(const GemmParams& p, uint32_t* ready, int c0, int c1, volatile int* abort_flag) {
   bool fresh = false;
+  if (c0 < 0 || c1 > p.g_chunks) {  // never expected: chunk ranges come from in-range tiles
+    *abort_flag = 1;
+    atomicCAS(p.err, 0, kErrBadArgs);
+    return false;
+  }
   for (int c = c0; c < c1; ++c) {
     const uint32_t bit = 1u << (c & 31);
     if (ready[c >> 5] & bit) continue;
@@ -368,16 +373,22 @@ VLM_DEV void gather_copy(const GemmParams& p, int lane) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const long long x = x0 + (u * 32 + lane) * 16ll;
+          v[u] = make_uint4(0, 0, 0, 0);
           if (x < b1) {
             const long long ux = p.g_off + x;
             const int o = o0 == o1 ? o0 : static_cast<int>(ux / SB);
-            v[u] = __ldcg(reinterpret_cast<const uint4*>(p.g_src.p[o] + (ux - o * SB)));
+            const long long off = ux - o * SB;
+            if (o >= 0 && o < p.g_world && off >= 0 && off + 16 <= SB) {
+              v[u] = __ldcg(reinterpret_cast<const uint4*>(p.g_src.p[o] + off));
+            } else {
+              atomicCAS(p.err, 0, kErrBadArgs);  // never expected: the host checked the unit geometry
+            }
           }
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const long long x = x0 + (u * 32 + lane) * 16ll;
-          if (x < b1) __stcg(reinterpret_cast<uint4*>(p.g_dst + p.g_off + x), v[u]);
+          if (x < b1 && p.g_off + x + 16 <= p.g_world * SB) __stcg(reinterpret_cast<uint4*>(p.g_dst + p.g_off + x), v[u]);
         }
       }
     }
@@ -385,7 +396,8 @@ VLM_DEV void gather_copy(const GemmParams& p, int lane) {
     fence_proxy_async_global();
     __threadfence();
     __syncwarp();
-    if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.g_flags + c) : "memory");
+    if (lane == 0 && c < p.g_chunks)
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.g_flags + c) : "memory");
   }
 }
 
@@ -830,7 +842,13 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParam
     configured = true;
   }
   // a fused decode consumer waits at a grid-wide barrier: cooperative launch keeps every CTA resident
-  launch_ex(p.consumer != DEC_NONE, kern, dim3(grid), dim3(GATHER ? 256 : 192), GemmCfg<BN>::SMEM, st, ta, tb, p);
+  // (VLMRL_DECODE_COOP=0 drops the attribute, for timing only: grid <= #SMs at one CTA per SM)
+  static const bool coop = [] {
+    const char* e = std::getenv("VLMRL_DECODE_COOP");
+    return !(e && e[0] == '0');
+  }();
+  launch_ex(p.consumer != DEC_NONE && coop, kern, dim3(grid), dim3(GATHER ? 256 : 192), GemmCfg<BN>::SMEM, st, ta, tb,
+            p);
 }
 
 static void check_operand(const at::Tensor& t, const char* name) {
@@ -914,6 +932,7 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
     p.g_rows = static_cast<int>(rows);
     p.g_chunks = static_cast<int>(chunks);
     p.g_pieces = static_cast<int>((64 * row_bytes + kGatherPiece - 1) / kGatherPiece);
+    p.g_world = W;
     p.g_flags = reinterpret_cast<unsigned*>(gather->flags.data_ptr());
     p.g_ctr = reinterpret_cast<unsigned*>(gather->ctr.data_ptr());
   }

@@ -97,8 +97,10 @@ void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at:
 void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
                     at::Tensor cu, at::Tensor dq, at::Tensor dk, at::Tensor dv, int64_t max_seqlen, bool causal,
                     double scale, c10::optional<at::Tensor> pre, c10::optional<at::Tensor> xq);
+// lead / share_len (int32 [B], optional): keys [0, share_len[b]) of row b may be read from row lead[b].
 void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale,
-                 c10::optional<at::Tensor> prefetch = c10::nullopt);
+                 c10::optional<at::Tensor> prefetch = c10::nullopt, c10::optional<at::Tensor> lead = c10::nullopt,
+                 c10::optional<at::Tensor> share_len = c10::nullopt);
 
 // sampler.cu
 void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, at::Tensor seed, double temperature,

@@ -422,10 +422,11 @@ def _sharded_unit(W, rows, cols, lead, seed=0):
 
 
 @pytest.mark.parametrize("W", [1, 3, 8])
-@pytest.mark.parametrize("M", [64, 700])
+@pytest.mark.parametrize("M", [64, 700, 2100, 6000])
 def test_gemm_with_fused_weight_gather(W, M):
     """GEMMs whose weight operand is assembled from W shards inside the kernel match the plain GEMM on the
-    full matrix, for the forward (K-major), dgrad (MN-major) and SwiGLU epilogue, and re-launch cleanly."""
+    full matrix, for the forward (K-major), dgrad (MN-major) and SwiGLU epilogue, and re-launch cleanly.
+    M covers 128- and 256-wide tiles and CTAs that own one or several tiles."""
     N, K = 1344, 576
     full, shards, SB, lead = _sharded_unit(W, N, K, 256)
     w_full = full[lead:lead + N * K].view(N, K)
@@ -514,4 +515,34 @@ def test_decode_gemms_with_fused_consumers_match_separate_kernels(B, norm):
     torch.cuda.synchronize()
     _close(a3, a1, rtol=1e-2, atol=1e-2, name="swiglu (graph)")
     _close(hn3, hn1, rtol=1e-2, atol=1e-2, name="hn (graph)")
+    _no_device_error()
+
+
+def test_decode_attn_reads_shared_prompt_from_group_leader(monkeypatch):
+    """With lead/share_len, whole key chunks inside a row's shared prompt come from the leader's row: the
+    members' own copies of the prompt are never read (here they are NaN) and the result equals the
+    attention over clean copies.  One key split, so chunks start at multiples of 64."""
+    monkeypatch.setenv("VLMRL_DECODE_SPLITS", "1")
+    B, gs, Hq, Hkv, D, Tmax = 8, 4, 8, 2, 128, 320
+    g = torch.Generator(device=DEV).manual_seed(3)
+    kc = _r(B, Hkv, Tmax, D, seed=4)
+    vc = _r(B, Hkv, Tmax, D, seed=5)
+    plen = torch.tensor([200, 200, 200, 200, 137, 137, 137, 137], dtype=torch.int32, device=DEV)
+    for b in range(B):
+        lead = b // gs * gs
+        kc[b, :, :int(plen[b])] = kc[lead, :, :int(plen[b])]
+        vc[b, :, :int(plen[b])] = vc[lead, :, :int(plen[b])]
+    lens = plen + torch.randint(1, 100, (B,), generator=g, device=DEV, dtype=torch.int32)
+    q = _r(B, Hq, D, seed=6)
+    ref_o = ops.decode_attn(q, kc, vc, lens)
+    lead = (torch.arange(B, device=DEV, dtype=torch.int32) // gs) * gs
+    kp, vp = kc.clone(), vc.clone()
+    for b in range(B):
+        if b % gs:  # poison the members' whole-chunk prompt copies
+            n = int(plen[b]) // 64 * 64
+            kp[b, :, :n] = float("nan")
+            vp[b, :, :n] = float("nan")
+    out = ops.decode_attn(q, kp, vp, lens, lead=lead, share_len=plen)
+    assert torch.isfinite(out.float()).all()
+    _close(out, ref_o, rtol=1e-2, atol=1e-2, name="shared-prompt decode attention")
     _no_device_error()

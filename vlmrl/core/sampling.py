@@ -141,6 +141,9 @@ class Generator:
             lv = st.cache.lengths.view(G, gs)
             lv[:, 1:] = lv[:, :1]
             logits = logits.repeat_interleave(gs, dim=0)
+        # members' prompt KV rows are copies of their leader's: decode attention reads the leader's
+        st.cache.lead.copy_(torch.arange(B, device=m.device, dtype=torch.int32) // gs * gs)
+        st.cache.share_len.copy_(st.cache.lengths)
         nt, lp = ops.sample(logits, temperature=cfg.temperature, top_k=cfg.top_k or 0, top_p=cfg.top_p or 0.0,
                             seed=st.seed, step=st.step, row_offset=row_offset)
         self._record(st, nt, lp, cfg.eos_id)

@@ -97,6 +97,10 @@ class KVCache:
         self.keys = torch.zeros(shape, dtype=dtype, device=device)
         self.values = torch.zeros(shape, dtype=dtype, device=device)
         self.lengths = torch.zeros(batch, dtype=torch.int32, device=device)
+        # rows whose first share_len[b] entries equal row lead[b]'s (a group's shared prompt); decode
+        # attention reads those from the leader's row.  Identity / 0 = no sharing.
+        self.lead = torch.arange(batch, dtype=torch.int32, device=device)
+        self.share_len = torch.zeros(batch, dtype=torch.int32, device=device)
         self.max_len = max_len
 
     @classmethod
@@ -108,9 +112,10 @@ class KVCache:
 # on the 4B model at batch 64 it measured slower (4.70 vs 4.44 ms per step); the decode GEMMs are bound by
 # their fixed pipeline latency, and the prefetched lines compete with the KV-cache stream for L2.
 _DECODE_L2_PREFETCH = os.environ.get("VLMRL_DECODE_L2_PREFETCH", "0") == "1"
-# Decode GEMMs run their consumer (q/k/v, residual + norm, SwiGLU) in the same launch after a grid-wide
-# barrier; VLMRL_DECODE_FUSED=0 selects separate consumer kernels.
-_DECODE_FUSED_CONSUMERS = os.environ.get("VLMRL_DECODE_FUSED", "1") != "0"
+# VLMRL_DECODE_FUSED=1: decode GEMMs run their consumer (q/k/v, residual + norm, SwiGLU) in the same launch
+# after a grid-wide barrier.  Off by default: measured slower (5.04 vs 4.10 ms per 4B decode step at batch
+# 64) than the separate consumer kernels, which overlap the GEMM's tail through programmatic launch.
+_DECODE_FUSED_CONSUMERS = os.environ.get("VLMRL_DECODE_FUSED", "0") == "1"
 
 
 # --------------------------------------------------------------------------- parameter sources
@@ -413,7 +418,8 @@ class TextDecoder:
                 q = ops.dec_linear_qkv(xn, w["qkv_w"], w["qkv_b"], w.get("q_norm"), w.get("k_norm"), lens, delta,
                                        self.rope, cache.keys[i], cache.values[i], n_q=self.nq, n_kv=self.nkv,
                                        eps=self.eps)
-                o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale)
+                o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale,
+                                    lead=cache.lead, share_len=cache.share_len)
                 h1, hn = ops.dec_linear_residual_norm(o.reshape(B, self.nq * self.D), w["o_w"], x, w["post_norm"],
                                                       self.eps)
                 act = ops.dec_linear_swiglu(hn, w["gu_w"])
@@ -427,7 +433,7 @@ class TextDecoder:
                             cache.keys[i], cache.values[i], n_q=self.nq, n_kv=self.nkv, eps=self.eps,
                             prefetch=w["o_w"] if pf else None)
             o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale,
-                                prefetch=gu[:half] if pf else None)
+                                prefetch=gu[:half] if pf else None, lead=cache.lead, share_len=cache.share_len)
             ws, meta = ops.gemm_partials(o.reshape(B, self.nq * self.D), w["o_w"])
             h1, hn = ops.dec_residual_norm(ws, meta, x, w["post_norm"], self.eps, prefetch=gu[half:] if pf else None)
             ws, meta = ops.gemm_partials(hn, w["gu_w"])

@@ -410,13 +410,17 @@ def flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen: int, *, causal: 
     return dq, dk, dv
 
 
-def decode_attn(q, k_cache, v_cache, lengths, *, scale: Optional[float] = None, out=None, prefetch=None):
-    """``prefetch``: a weight the L2 should fetch while the kernel runs (the next GEMM's operand)."""
+def decode_attn(q, k_cache, v_cache, lengths, *, scale: Optional[float] = None, out=None, prefetch=None,
+                lead=None, share_len=None):
+    """``prefetch``: a weight the L2 should fetch while the kernel runs (the next GEMM's operand).
+    ``lead``/``share_len`` (int32 [B]): the first ``share_len[b]`` cache entries of row b equal those of row
+    ``lead[b]`` (members of a GRPO group share the prompt); the kernel then reads them from the leader's
+    row, so a group streams its prompt's KV once."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if not _cuda(q):
         return ref.decode_attn(q, k_cache, v_cache, lengths, scale=scale)
     o = out if out is not None else torch.empty_like(q)
-    ext().decode_attn(q, k_cache, v_cache, lengths, o, float(scale), prefetch)
+    ext().decode_attn(q, k_cache, v_cache, lengths, o, float(scale), prefetch, lead, share_len)
     return o
 
 

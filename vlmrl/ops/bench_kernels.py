@@ -207,6 +207,14 @@ def bench_decode_step(t: Timer, eager_steps: int = 0):
     with ops.static_weights():
         ms = t(step)
     emit("decode_step_4b_B64_T390", ms, bytes_=weights + 36 * 2 * B * 8 * 390 * 128 * 2)
+    # GRPO rollout layout: 8 groups of 8 members sharing a 262-token prompt; decode attention reads the
+    # prompt's keys from the group leader's cache row (KV bytes: 8 prompts + 64 x 128 generated entries)
+    cache.lead.copy_(torch.arange(B, device="cuda", dtype=torch.int32) // 8 * 8)
+    cache.share_len.fill_(262)
+    with ops.static_weights():
+        ms = t(step)
+    emit("decode_step_4b_B64_T390_grpo8x8_shared_prompt", ms,
+         bytes_=weights + 36 * 2 * 8 * (8 * 262 + B * 128) * 128 * 2)
 
 
 def bench_train_step(t: Timer = None, eager_steps: int = 0, iters: int = 5):
@@ -336,7 +344,10 @@ def _gather_case(M: int, W: int = 8):
     x = _r(M, K)
     y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
     full = torch.cat(shards)[:N * K].view(N, K)
-    return (lambda: ops.linear(x, sw, out=y)), (lambda: ops.linear(x, full, out=y))
+
+    def fused(keep=shards):  # the kernel reads the shards through raw pointers: keep them alive
+        return ops.linear(x, sw, out=y)
+    return fused, (lambda: ops.linear(x, full, out=y))
 
 
 def bench_gather(t: Timer):
@@ -346,6 +357,7 @@ def bench_gather(t: Timer):
     flops = 2.0 * M * N * K
     for name, fn in (("gemm_gather_8shards", fused), ("gemm_resident_weight", plain)):
         emit(f"{name}_{M}x{K}x{N}", t(fn), flops=flops)
+        ops.check_errors()
 
 
 def profile_small(case: str = "decode"):
