@@ -42,8 +42,9 @@ WORKLOADS = {
                  max_new=16, minibatches=1),
     "truefalse_4b": dict(preset="qwen3vl_4b", env="synthetic_truefalse", groups=32, group_size=8, image=384,
                          prompt_tokens=48, max_new=8, minibatches=2),
+    # 8B: FSDP over all ranks for the update, rollout tensor parallel over pairs of GPUs (TP-2 x DP-N/2)
     "grpo_8b": dict(preset="qwen3vl_8b", env="synthetic_geo", groups=16, group_size=8, image=672, prompt_tokens=128,
-                    max_new=512, minibatches=2),
+                    max_new=512, minibatches=2, rollout="tp", tp_size=2),
 }
 
 
@@ -67,12 +68,18 @@ def parse():
     ap.add_argument("--fsdp-params", choices=["gathered", "sharded"], default="gathered",
                     help="gathered: bf16 parameters stay all-gathered (pushed by the fused AdamW); sharded: "
                          "decoder-layer weights are all-gathered inside the GEMMs that consume them")
-    ap.add_argument("--rollout", choices=["tp", "dp"], default="dp",
-                    help="N>1: tensor-parallel decode of the whole batch (tp) or each rank decodes its own groups (dp)")
+    ap.add_argument("--rollout", choices=["tp", "dp"], default=None,
+                    help="N>1: tensor-parallel decode (tp) or each rank decodes its own groups (dp, the default)")
+    ap.add_argument("--tp-size", type=int, default=None,
+                    help="GPUs per tensor-parallel rollout group with --rollout tp (default: all)")
     args = ap.parse_args()
     for k, v in WORKLOADS[args.workload].items():
         if getattr(args, k, None) is None:
             setattr(args, k, v)
+    if args.rollout is None:
+        args.rollout = "dp"
+    if args.tp_size is None:
+        args.tp_size = 0
     return args
 
 
@@ -194,7 +201,8 @@ def main():
         train_state = None
     trainer = GRPOTrainer(model, tok, env, cfg, adamw, ref_model=ref_model, seed=0, rank=rank, world_size=world,
                           train_state=train_state,
-                          tp_rollout=(world > 1 and args.rollout == "tp"))
+                          tp_rollout=(world > 1 and args.rollout == "tp"),
+                          tp_size=min(args.tp_size, world) if args.tp_size else 0)
 
     def barrier():
         if world > 1:
@@ -278,7 +286,8 @@ def main():
                    "seq_len": f"{(2 if args.env == 'synthetic_truefalse' else 1) * (image_tokens + 2) + args.prompt_tokens}"
                               f" prompt + {args.max_new} new",
                    "workload": args.workload,
-                   "parallelism": (f"fsdp{world}+tp{world}-rollout" if trainer.tp is not None else f"fsdp{world}")
+                   "parallelism": ((f"fsdp{world}+tp{trainer.tp_size}x"
+                                    f"dp{world // trainer.tp_size}-rollout") if trainer.tp is not None else f"fsdp{world}")
                    + ("-sharded-params" if args.fsdp_params == "sharded" and world > 1 else "")
                    if world > 1 else "single-gpu",
                    "fsdp_comm": getattr(model.params, "comm", None) if world > 1 else None,

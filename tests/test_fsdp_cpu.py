@@ -104,3 +104,12 @@ def test_sharded_unit_small_leaf_ranges():
             assert set(range(lo, lo + prm.numel * 2, 2)) <= covered, prm.name
     # input_norm | qkv_b..k_norm | post_norm
     assert len(rng) == 3
+
+
+def test_tp_partition_blocks_of_consecutive_ranks():
+    from vlmrl.parallel.tp import tp_partition
+
+    assert tp_partition(8, 2) == [[0, 1], [2, 3], [4, 5], [6, 7]]
+    assert tp_partition(4, 4) == [[0, 1, 2, 3]]
+    with pytest.raises(ValueError):
+        tp_partition(6, 4)

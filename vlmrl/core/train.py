@@ -15,7 +15,9 @@ same names and defaults, plus the flags of this framework's extensions:
 * ``old_logprob_source`` — ``sampler`` (reference) or ``policy``;
 * ``preset`` — random-init architecture (``tiny``, ``qwen3vl_4b``, ...) when
   ``model_dir`` holds no weights;
-* ``fsdp`` — shard optimizer state and gradients over the process group.
+* ``fsdp`` — shard optimizer state and gradients over the process group;
+* ``fsdp_shard_params`` — also shard the decoder-layer bf16 weights (gathered inside the GEMMs);
+* ``tp_rollout`` / ``tp_size`` — tensor-parallel rollout over groups of ``tp_size`` GPUs (0 = all).
 
 Model loading accepts a converted checkpoint (``config.json`` + ``params.pkl``,
 reference ``create_model_from_ckpt``) or a HuggingFace snapshot (safetensors).
@@ -95,6 +97,9 @@ CONFIG: Dict[str, Any] = {
     "old_logprob_source": "sampler",
     "preset": "",
     "fsdp": 1,
+    "fsdp_shard_params": 0,
+    "tp_rollout": 0,
+    "tp_size": 0,
     "metrics_path": "",
     "env_kwargs": "",
 }
@@ -304,7 +309,8 @@ def build_trainer(args, device=None, rank: int = 0, world: int = 1):
         probe, units = load_policy(args.model_dir, args.preset, "cpu", torch.float32, seed=int(args.seed)) \
             if not args.preset else (None, None)
         spec = probe.spec if probe is not None else get_preset(args.preset)
-        model, ref_model, ts = build_fsdp_models(spec, opt_cfg, seed=int(args.seed), device=device, units=units)
+        model, ref_model, ts = build_fsdp_models(spec, opt_cfg, seed=int(args.seed), device=device, units=units,
+                                                 shard_params=bool(int(args.fsdp_shard_params)))
         master = None
     else:
         model, master = load_policy(args.model_dir, args.preset, device, dtype, seed=int(args.seed))
@@ -317,7 +323,8 @@ def build_trainer(args, device=None, rank: int = 0, world: int = 1):
     _, eos_id = resolve_pad_and_eos(tokenizer, model.spec)
     env = RollingEnv(build_env(args, tokenizer))
     trainer = GRPOTrainer(model, tokenizer, env, cfg, opt_cfg, ref_model=ref_model, seed=int(args.seed),
-                          master=master, eos_id=eos_id, rank=rank, world_size=world, train_state=ts)
+                          master=master, eos_id=eos_id, rank=rank, world_size=world, train_state=ts,
+                          tp_rollout=bool(int(args.tp_rollout)) and world > 1, tp_size=int(args.tp_size))
     if int(args.use_ema) and trainer.ts.params_ema is None:
         trainer.ts.enable_ema()
     return trainer

@@ -36,20 +36,29 @@ from vlmrl.utils.train_state import TrainState
 class GRPOTrainer:
     def __init__(self, model, tokenizer, env, cfg: TrainerConfig, adamw: AdamWConfig, *, ref_model=None,
                  seed: int = 0, master=None, eos_id: Optional[int] = None, rank: int = 0, world_size: int = 1,
-                 train_state=None, tp_rollout: bool = False):
+                 train_state=None, tp_rollout: bool = False, tp_size: int = 0):
         self.model = model
         self.tokenizer = tokenizer
         self.env = env
         self.cfg = cfg
         self.ts = train_state if train_state is not None else TrainState.create_with_params(model, adamw, master)
         self.ref_model = ref_model
-        # tp_rollout: every rank decodes the whole batch with 1/world of each layer's weights (tensor
-        # parallel over NVLink), then trains on its own share of the groups (FSDP data parallel)
+        # tp_rollout: the ranks form tensor-parallel groups of tp_size consecutive ranks (0 = all ranks).
+        # Each group decodes the union of its ranks' prompt groups with 1/tp_size of each layer's weights
+        # (tensor parallel over NVLink; groups are data parallel), then every rank trains on its own share
+        # of the groups (FSDP over all ranks).
         self.tp = None
+        self.tp_size = 1
         if tp_rollout and world_size > 1:
-            from vlmrl.parallel.tp import maybe_tp_decoder
+            from vlmrl.parallel.tp import maybe_tp_decoder, tp_subgroup
 
-            self.tp = maybe_tp_decoder(model, max_batch=int(cfg.groups_per_batch) * max(1, int(cfg.group_size)))
+            t = int(tp_size) or int(world_size)
+            group = tp_subgroup(t)
+            self.tp = maybe_tp_decoder(model, group=group,
+                                       max_batch=int(cfg.groups_per_batch) * max(1, int(cfg.group_size)) * t
+                                       // int(world_size))
+            if self.tp is not None:
+                self.tp_size = t
         self.generator = Generator(model, tp=self.tp)
         self.kl_ctrl = (AdaptiveKL(cfg.kl_target, cfg.kl_adapt_rate, cfg.kl_coef_min, cfg.kl_coef_max)
                         if cfg.adaptive_kl else None)
@@ -92,10 +101,12 @@ class GRPOTrainer:
 
     def _collect(self, seed: int, G: int):
         cfg = self.cfg
-        if self.tp is not None:   # every rank rolls out all groups, then keeps its share for training
-            return collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G * self.world, rng=seed,
-                           eos_id=self.eos_id, generator=self.generator, task_offset=self.cursor, row_offset=0,
-                           keep_groups=(self.rank * G, (self.rank + 1) * G))
+        if self.tp is not None:   # the TP group rolls out its ranks' groups, then each rank keeps its share
+            t = self.tp_size
+            d, lr = self.rank // t, self.rank % t
+            return collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G * t, rng=seed,
+                           eos_id=self.eos_id, generator=self.generator, task_offset=self.cursor + d * G * t,
+                           row_offset=d * G * t * cfg.group_size, keep_groups=(lr * G, (lr + 1) * G))
         return collect(self.env, self.tokenizer, self.model, self.ts, cfg, batch_size=G, rng=seed, eos_id=self.eos_id,
                        generator=self.generator, task_offset=self.cursor + self.rank * G,
                        row_offset=self.rank * G * cfg.group_size)

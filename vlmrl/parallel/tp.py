@@ -154,6 +154,27 @@ class TPDecoder:
             b.close()
 
 
+def tp_partition(world: int, tp_size: int):
+    """Rank lists of the tensor-parallel groups: consecutive blocks of ``tp_size`` ranks (NVLink peers on one
+    node), ``world // tp_size`` data-parallel replicas."""
+    if tp_size < 1 or world % tp_size:
+        raise ValueError(f"tp_size={tp_size} must divide the world size {world}")
+    return [list(range(i, i + tp_size)) for i in range(0, world, tp_size)]
+
+
+def tp_subgroup(tp_size: int):
+    """This rank's tensor-parallel process group (collective: every rank creates every group, in order)."""
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if tp_size == world:
+        return None  # the default group
+    mine = None
+    for ranks in tp_partition(world, tp_size):
+        g = dist.new_group(ranks)
+        if rank in ranks:
+            mine = g
+    return mine
+
+
 def maybe_tp_decoder(model, group=None, max_batch: int = 64) -> Optional[TPDecoder]:
     """A TPDecoder when the process group spans several GPUs with peer access, else None."""
     from vlmrl.parallel.symm import p2p_supported
