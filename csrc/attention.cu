@@ -1038,6 +1038,10 @@ static const int* seg_ptr(const c10::optional<at::Tensor>& t, const at::Tensor& 
   return t->data_ptr<int>();
 }
 
+// attention_tc.cu: the tcgen05 forward for head_dim 64 / 128 (false: not handled, use the kernels here)
+bool flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
+                       at::Tensor& o, at::Tensor& lse, int max_seqlen, bool causal, float scale, const int* pre);
+
 // pre[b] = (start, len): keys every query of segment b also attends to (a shared prefix).
 void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at::Tensor o, at::Tensor lse,
                     int64_t max_seqlen, bool causal, double scale, c10::optional<at::Tensor> pre) {
@@ -1050,6 +1054,7 @@ void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at:
   const int* pp = seg_ptr(pre, cu, "pre");
   const int ms = static_cast<int>(max_seqlen);
   const float sc = static_cast<float>(scale);
+  if (flash_attn_fwd_tc(q, k, v, cu, o, lse, ms, causal, sc, pp)) return;
   switch (D) {
     case 16: fwd_dispatch<16>(q, k, v, cu, o, lse, ms, causal, sc, pp); break;
     case 32: fwd_dispatch<32>(q, k, v, cu, o, lse, ms, causal, sc, pp); break;

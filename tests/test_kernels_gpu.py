@@ -164,7 +164,8 @@ def test_qk_rope_bwd_large_and_rotation_only(T, norm):
         torch.testing.assert_close(dkw, dkwr.float(), rtol=2e-3, atol=2e-1)
 
 
-@pytest.mark.parametrize("D,Hq,Hkv,causal", [(128, 8, 2, True), (64, 4, 4, False), (32, 4, 2, True), (16, 4, 4, False)])
+@pytest.mark.parametrize("D,Hq,Hkv,causal", [(128, 8, 2, True), (128, 8, 2, False), (64, 4, 4, False), (64, 8, 2, True),
+                                             (32, 4, 2, True), (16, 4, 4, False)])
 def test_flash_attn(D, Hq, Hkv, causal):
     lens = [1, 63, 64, 130, 388, 17]
     cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device=DEV)
