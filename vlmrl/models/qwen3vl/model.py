@@ -271,7 +271,7 @@ class TextDecoder:
                                      dkw_accum=None if g is None else g.get("k_norm"))
         if g is not None:
             ops.grad_weight(d_qkv, c.xn, accumulate=g["qkv_w"])
-            g["qkv_b"].add_(d_qkv.float().sum(0))
+            g["qkv_b"].add_(d_qkv.sum(0, dtype=torch.float32))  # fp32 accumulation, no fp32 copy of d_qkv
         d_xn = ops.grad_input(d_qkv, w["qkv_w"], out_dtype=dt)
         return ops.rms_norm_bwd(d_xn, c.x, w["input_norm"], c.r1, dw_accum=None if g is None else g["input_norm"],
                                 add=d_h1)
