@@ -104,5 +104,10 @@ def test_sharded_params_match_gathered(tmp_path):
     for u, w in a["master"].items():
         torch.testing.assert_close(b["master"][u], w, atol=1e-5, rtol=1e-4, msg=lambda s: f"master {u}: {s}")
     for u, w in a["full"].items():
-        torch.testing.assert_close(b["full"][u], w, atol=0, rtol=0, msg=lambda s: f"bf16 params {u}: {s}")
+        # each engine's gathered bf16 parameters are exactly its fp32 master rounded: the in-GEMM / unit
+        # gathers assembled every shard byte; across engines the two AdamW kernels may round one ulp apart
+        for e in (a, b):
+            torch.testing.assert_close(e["full"][u], e["master"][u].bfloat16().float(), atol=0, rtol=0,
+                                       msg=lambda s: f"bf16 params {u} vs master: {s}")
+        torch.testing.assert_close(b["full"][u], w, atol=1e-4, rtol=2 ** -7, msg=lambda s: f"bf16 params {u}: {s}")
     torch.testing.assert_close(b["prefill"], a["prefill"], atol=1e-3, rtol=1e-3)
