@@ -355,6 +355,9 @@ def test_adamw_and_sqnorm():
     torch.testing.assert_close(p.cpu(), p2, atol=1e-6, rtol=1e-5)
     s = ops.sq_norm(g)
     torch.testing.assert_close(s.cpu()[0], (g2 ** 2).sum(), rtol=1e-4, atol=1e-3)
+    for n in (10001, 5_000_016, 7):  # scalar tail path, vectorised grid-stride path, tiny
+        x = torch.randn(n, device=DEV)
+        torch.testing.assert_close(ops.sq_norm(x).cpu()[0], (x.double() ** 2).sum().float().cpu(), rtol=1e-4, atol=1e-3)
 
 
 def test_down_dgrad_with_fused_swiglu_backward():

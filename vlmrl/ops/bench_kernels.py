@@ -320,6 +320,10 @@ def _profile_inputs(case: str):
         ph = torch.empty(n, dtype=torch.bfloat16, device="cuda")
         return lambda: ops.adamw_(p, gg, m, v, lr=1e-6, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01,
                                   step=1, p_half=ph)
+    if case == "wgrad":         # weight gradient dW[6144, 2560] += dY[8192, 6144]^T . X[8192, 2560] (MN-major A and B)
+        dy, x = _r(8192, 6144), _r(8192, H)
+        acc = torch.zeros(6144, H, device="cuda")
+        return lambda: ops.grad_weight(dy, x, accumulate=acc)
     if case == "gather":        # gate/up GEMM 4096 x 2560 -> 19456 whose weight is assembled from 8 shards
         return _gather_case(4096)[0]
     if case == "decode_fused":  # decode GEMMs with their consumers fused behind a grid barrier (B=64)
@@ -384,7 +388,7 @@ def main():
     ap.add_argument("--eager-steps", type=int, default=0,
                     help="decode_step (default) or --only train_step: run N eager steps inside a profiler range "
                          "(for a launch list)")
-    ap.add_argument("--profile-small", default=None, choices=["decode", "gemm", "attn", "vocab", "adamw", "gather", "decode_fused"],
+    ap.add_argument("--profile-small", default=None, choices=["decode", "gemm", "attn", "vocab", "adamw", "gather", "decode_fused", "wgrad"],
                     help="one launch of the named case's kernels inside a profiler range")
     args = ap.parse_args()
     if args.profile_small:
