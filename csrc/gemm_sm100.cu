@@ -119,10 +119,11 @@ struct WorkIter {
   int kb_count, units_total;
   long long u, u_end, U;
   int t, grid;
-  VLM_DEV WorkIter(const GemmParams& p, int kbc) : kb_count(kbc) {
-    grid = gridDim.x;
+  // pair: CTAs 2c and 2c+1 (one cluster) walk the same tiles, c = 0 .. gridDim.x/2 - 1
+  VLM_DEV WorkIter(const GemmParams& p, int kbc, bool pair = false) : kb_count(kbc) {
+    grid = gridDim.x >> (pair ? 1 : 0);
     units_total = p.tiles_m * p.tiles_n * p.splits;
-    t = blockIdx.x;
+    t = blockIdx.x >> (pair ? 1 : 0);
     U = static_cast<long long>(p.tiles_m) * p.tiles_n * kbc;
     u = (static_cast<long long>(blockIdx.x) * U) / grid;
     u_end = (static_cast<long long>(blockIdx.x + 1) * U) / grid;
@@ -156,11 +157,13 @@ struct WorkIter {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 
-template <int BN>
+// PAIR: a 256 x BN tile on a CTA pair; each CTA stages 128 rows of A and BN/2 rows of B per k-block.
+template <int BN, bool PAIR = false>
 struct GemmCfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int BNC = PAIR ? BN / 2 : BN;  // B rows (N) staged by this CTA
+  static constexpr int STAGES = PAIR ? (BN == 256 ? 6 : 8) : (BN == 256 ? 4 : 6);
   static constexpr int A_BYTES = kBM * kBK * 2;
-  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int B_BYTES = BNC * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   // per epilogue warp: a 32 x 16 fp32 staging tile (rows padded to 20 words) for coalesced partial stores
@@ -401,10 +404,15 @@ VLM_DEV void gather_copy(const GemmParams& p, int lane) {
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, bool GATHER = false>
+// PAIR kernels run as clusters of 2 CTAs (cta_group::2): the leader (rank 0) issues the 128-row-per-CTA
+// MMAs of a 256-row tile; both CTAs load their rows of A and their half of B (TMA completion counted on the
+// leader's barrier), and both drain their own TMEM rows.
+template <int BN, bool A_MN, bool B_MN, bool GATHER = false, bool PAIR = false>
 __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
-  using C = GemmCfg<BN>;
+  using C = GemmCfg<BN, PAIR>;
+  static_assert(!(PAIR && GATHER), "pair tiles do not gather");
+  constexpr int TILE_M = PAIR ? 2 * kBM : kBM;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -422,6 +430,9 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kb_count = (p.K + kBK - 1) / kBK;
+  uint32_t rank = 0;
+  if constexpr (PAIR) rank = cluster_ctarank();
+  const bool leader = rank == 0;
   if (threadIdx.x == 0) trace_mark(p, 0);
 
   if (threadIdx.x == 0) {
@@ -431,7 +442,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], PAIR ? 8 : 4);  // the epilogue warps of both CTAs release an accumulator
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -446,7 +457,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
   // the first STAGES k-blocks is requested right after the barriers exist — before the TMEM allocation
   // and the CTA barrier, and before waiting for the previous kernel.  Thread 0 is the TMA producer.
   int prefetched = 0;
-  if (threadIdx.x == 0 && p.b_prefetch) {
+  if (!PAIR && threadIdx.x == 0 && p.b_prefetch) {
     WorkIter it0(p, kb_count);
     Work w0;
     if (it0.next(p, w0)) {
@@ -467,11 +478,17 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {  // the same warp of both CTAs allocates the pair's TMEM
+      tmem_alloc_pair(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the leader's barriers exist before the peer's copies signal them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if (threadIdx.x == 0) trace_mark(p, 1);
@@ -482,22 +499,29 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       bool ok = true;
       int stage = 0;
       uint32_t phase = 0;
+      // one 2-D load into this CTA's stage; PAIR: completion counted on the leader's full barrier
+      auto ld = [&](uint8_t* dst, const CUtensorMap* map, int x, int y) {
+        if constexpr (PAIR)
+          tma_load_2d_pair(dst, map, mapa_shared(smem_u32(&full[stage]), 0), x, y);
+        else
+          tma_load_2d(dst, map, &full[stage], x, y);
+      };
       auto load_b = [&](uint8_t* b, int k0, int n0) {
         if constexpr (!B_MN) {
-          tma_load_2d(b, &tmB, &full[stage], k0, n0);
+          ld(b, &tmB, k0, n0);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 8192, &tmB, &full[stage], n0 + 64 * j, k0);
+          for (int j = 0; j < C::BNC / 64; ++j) ld(b + j * 8192, &tmB, n0 + 64 * j, k0);
         }
       };
-      WorkIter it(p, kb_count);
+      WorkIter it(p, kb_count, PAIR);
       Work w;
       pdl_wait();
       trace_mark(p, 2);
       while (ok && it.next(p, w)) {
         int tm, tn;
         tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
-        const int m0 = tm * kBM, n0 = tn * BN;
+        const int m0 = tm * TILE_M + static_cast<int>(rank) * kBM, n0 = tn * BN + static_cast<int>(rank) * C::BNC;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           const bool pre = prefetched > 0;
           if (!pre && !mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.err, kErrTimeoutProducer)) {
@@ -515,13 +539,14 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           }
           uint8_t* a = sA + stage * C::A_BYTES;
           uint8_t* b = sB + stage * C::B_BYTES;
-          if (!pre) mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          // PAIR: the leader expects the bytes of both CTAs on its barrier (the peer's may land first)
+          if (!pre && leader) mbar_arrive_expect_tx(&full[stage], (PAIR ? 2 : 1) * C::STAGE_BYTES);
           const int k0 = kb * kBK;
           if constexpr (!A_MN) {
-            tma_load_2d(a, &tmA, &full[stage], k0, m0);
+            ld(a, &tmA, k0, m0);
           } else {
-            tma_load_2d(a, &tmA, &full[stage], m0, k0);
-            tma_load_2d(a + 8192, &tmA, &full[stage], m0 + 64, k0);
+            ld(a, &tmA, m0, k0);
+            ld(a + 8192, &tmA, m0 + 64, k0);
           }
           if (!pre) load_b(b, k0, n0);
           if (pre) --prefetched;
@@ -532,27 +557,34 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           }
         }
       }
-      if (!ok) {
+      if (!ok && !PAIR) {
         // drain this thread's in-flight copies (at most STAGES) before the CTA exits
         for (long long i = issued - 1; i >= 0 && i >= issued - C::STAGES; --i) {
           volatile int no_abort = 0;
           mbar_wait(&full[i % C::STAGES], static_cast<uint32_t>((i / C::STAGES) & 1), &no_abort, nullptr, 0);
         }
       }
+      if (!ok && PAIR) {
+        // a pair's copies complete on the leader's barrier, which the peer cannot wait on: give this CTA's
+        // own in-flight copies time to land before the teardown (error path only)
+        for (int i = 0; i < 2000; ++i) __nanosleep(1000);
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(kBM, BN, A_MN, B_MN);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_bf16_f32(TILE_M, BN, A_MN, B_MN);
       bool ok = true;
       int stage = 0;
       uint32_t phase = 0;
       int lt = 0;
-      WorkIter it(p, kb_count);
+      WorkIter it(p, kb_count, PAIR);
       Work w;
       for (; ok && it.next(p, w); ++lt) {
         const int acc = lt & 1;
         const uint32_t use = static_cast<uint32_t>(lt >> 1);
-        if (!mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abort_flag, p.err, kErrTimeoutMma)) {
+        const bool freed = PAIR ? mbar_wait_cluster(&tempty[acc], (use & 1u) ^ 1u, abort_flag, p.err, kErrTimeoutMma)
+                                : mbar_wait(&tempty[acc], (use & 1u) ^ 1u, abort_flag, p.err, kErrTimeoutMma);
+        if (!freed) {
           ok = false;
           break;
         }
@@ -572,20 +604,32 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t ad = A_MN ? sdesc_sw128(a_addr + k * 2048, 8192, 1024) : sdesc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(b_addr + k * 2048, 8192, 1024) : sdesc_sw128(b_addr + k * 32, 16, 1024);
-            umma_f16(d_tmem, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              umma_f16_pair(d_tmem, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            else
+              umma_f16(d_tmem, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
-          umma_commit(&empty[stage]);
+          if constexpr (PAIR)
+            umma_commit_pair(&empty[stage]);  // frees the stage in both CTAs
+          else
+            umma_commit(&empty[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        if constexpr (PAIR)
+          umma_commit_pair(&tfull[acc]);
+        else
+          umma_commit(&tfull[acc]);
         trace_mark(p, 4);
       }
       if (!ok) {
-        umma_commit(drain);
+        if constexpr (PAIR)
+          umma_commit_pair(drain);
+        else
+          umma_commit(drain);
         volatile int no_abort = 0;
         mbar_wait(drain, 0, &no_abort, nullptr, 0);
       }
@@ -599,7 +643,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     const int q = warp & 3;  // TMEM lanes [32q, 32q+32) are the ones this warp may read
     const int row_in_tile = q * 32 + lane;
     int lt = 0;
-    WorkIter it(p, kb_count);
+    WorkIter it(p, kb_count, PAIR);
     Work w;
     for (; it.next(p, w); ++lt) {
       const int acc = lt & 1;
@@ -609,17 +653,18 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       tc_fence_after();
       int tm, tn;
       tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
-      const int row = tm * kBM + row_in_tile;
+      const int m_base = tm * TILE_M + static_cast<int>(rank) * kBM;  // this CTA's 128 rows of the tile
+      const int row = m_base + row_in_tile;
       const int n0 = tn * BN;
       const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(q * 32) << 16);
-      if (tm * kBM + q * 32 >= p.M) {
+      if (m_base + q * 32 >= p.M) {
         // every row of this warp's TMEM lanes is past M (decode-shaped M): nothing to load or store
       } else if (p.streamk) {
         // Each lane holds one row's 16 columns after tcgen05.ld; storing that directly makes every warp
         // store touch 32 rows.  Stage the 32 x 16 block in shared memory and store it transposed: lane
         // (r4, c) writes 16 bytes of row 8*i + r4, so one store instruction covers 8 rows x 64 bytes.
         float* stg = epi_stage + (warp - 2) * C::EPI_STAGE_FLOATS;
-        const int row_base = tm * kBM + q * 32;
+        const int row_base = m_base + q * 32;
         const int sr = lane >> 2, sc = (lane & 3) * 4;
 #pragma unroll 1
         for (int c4 = 0; c4 < BN; c4 += 128) {
@@ -754,16 +799,26 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));  // the leader's MMA waits on both CTAs
+        else
+          mbar_arrive(&tempty[acc]);
+      }
       if (threadIdx.x == 128) trace_mark(p, 6);
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  // PAIR: neither CTA frees TMEM or leaves while the pair's MMAs, remote arrivals or copies may touch it
+  if constexpr (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
   if constexpr (GATHER) {
     // every role of this CTA is done with the gather state; the last CTA out zeroes it for the next launch
@@ -832,6 +887,71 @@ static thread_local bool g_static_weights = false;
 // Set only inside gemm_partials_traced: the next launch records per-CTA phase timestamps here.
 static thread_local unsigned long long* g_trace = nullptr;
 void set_static_weights(bool on) { g_static_weights = on; }
+
+// Cluster-of-2 launch of a PAIR kernel (grid = 2 x pairs) with programmatic serialization.
+template <int BN, bool A_MN, bool B_MN>
+static void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int pairs, cudaStream_t st) {
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, false, true>;
+  static bool configured = false;
+  if (!configured) {
+    VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN, true>::SMEM));
+    VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = GemmCfg<BN, true>::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  unsigned n = 1;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  VLM_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+  note_launch();
+}
+
+// How many 2-CTA clusters of the pair kernel can be resident at once (cached per tile width).
+template <int BN>
+static int max_pairs(int device) {
+  static int cached[64] = {0};
+  if (!cached[device]) {
+    auto kern = gemm_tcgen05_kernel<BN, false, false, false, true>;
+    VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN, true>::SMEM));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 148);
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = GemmCfg<BN, true>::SMEM;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    VLM_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    cached[device] = std::max(1, n);
+  }
+  return cached[device];
+}
+
+static bool pair_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("VLMRL_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 template <int BN, bool A_MN, bool B_MN, bool GATHER = false>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid, cudaStream_t st) {
@@ -953,6 +1073,48 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
                 "gemm: bad aux");
     p.aux = reinterpret_cast<__nv_bfloat16*>(aux.data_ptr());
     p.ld_aux = aux.stride(0);
+  }
+
+  // Training-sized GEMMs run on CTA pairs (256-row tiles, half of B per SM): fewer operand bytes per FLOP
+  // through L2 than single-CTA 128-row tiles.  Decode (stream-K), gather, vocab and fused-consumer GEMMs
+  // keep the single-CTA kernel.  VLMRL_GEMM_PAIR=0 turns pairs off.
+  const bool use_pair = pair_enabled() && !gather && !fuse && !want_partials && epi != EPI_VOCAB_STATS &&
+                        epi != EPI_VOCAB_GRAD && force_bn == 0 && (a_kmajor || !b_kmajor) && M >= 4 * kBM;
+  if (use_pair) {
+    const int dev = A.device().index();
+    const int64_t tm2 = (M + 2 * kBM - 1) / (2 * kBM);
+    const int s256 = max_pairs<256>(dev), s128 = max_pairs<128>(dev);
+    auto eff2 = [&](int bn, int slots) {
+      const double t = static_cast<double>(tm2 * ((N + bn - 1) / bn));
+      return t / (std::ceil(t / slots) * slots);
+    };
+    const int bn = eff2(128, s128) > eff2(256, s256) + 0.1 ? 128 : 256;
+    p.tiles_m = static_cast<int>(tm2);
+    p.tiles_n = static_cast<int>((N + bn - 1) / bn);
+    p.bn = bn;
+    p.splits = 1;
+    p.kb_per_split = static_cast<int>((K + kBK - 1) / kBK);
+    p.streamk = 0;
+    p.b_prefetch = 0;
+    const int64_t tiles2 = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+    const int pairs = static_cast<int>(std::min<int64_t>(tiles2, bn == 256 ? s256 : s128));
+    CUtensorMap ta, tb;
+    if (a_kmajor)
+      ta = make_tmap_2d_bf16(A.data_ptr(), K, M, A.stride(0), 64, 128);
+    else
+      ta = make_tmap_2d_bf16(A.data_ptr(), M, K, A.stride(0), 64, 64);
+    if (b_kmajor)
+      tb = make_tmap_2d_bf16(B.data_ptr(), K, N, B.stride(0), 64, bn / 2);
+    else
+      tb = make_tmap_2d_bf16(B.data_ptr(), N, K, B.stride(0), 64, 64);
+    cudaStream_t st = at::cuda::getCurrentCUDAStream();
+    if (a_kmajor && b_kmajor)
+      bn == 256 ? launch_pair<256, false, false>(ta, tb, p, pairs, st) : launch_pair<128, false, false>(ta, tb, p, pairs, st);
+    else if (a_kmajor)
+      bn == 256 ? launch_pair<256, false, true>(ta, tb, p, pairs, st) : launch_pair<128, false, true>(ta, tb, p, pairs, st);
+    else
+      bn == 256 ? launch_pair<256, true, true>(ta, tb, p, pairs, st) : launch_pair<128, true, true>(ta, tb, p, pairs, st);
+    return;
   }
 
   const int sms = num_sms(A.device().index());

@@ -550,3 +550,30 @@ def test_decode_attn_reads_shared_prompt_from_group_leader(monkeypatch):
     assert torch.isfinite(out.float()).all()
     _close(out, ref_o, rtol=1e-2, atol=1e-2, name="shared-prompt decode attention")
     _no_device_error()
+
+
+@pytest.mark.parametrize("M,N,K", [(520, 264, 200), (2304, 1536, 640), (4608, 2304, 256)])
+def test_gemm_cta_pair_tiles(M, N, K):
+    """GEMMs with M >= 512 run as CTA pairs (256-row tiles, tcgen05 cta_group::2, half of B per CTA). Ragged
+    M / N, both tile widths (the last shape picks 128-wide pair tiles for wave efficiency), every operand
+    layout and every epilogue against the fp32 oracle, twice in a row."""
+    a, w = _r(M, K, seed=70), _r(N, K, scale=0.1, seed=71)
+    bias, res = _r(N, seed=72), _r(M, N, seed=73)
+    for rep in range(2):
+        _close(ops.gemm(a, w, bias=bias, residual=res), ref.gemm(a, w, bias=bias, residual=res, out_dtype=torch.float32),
+               name=f"pair nt+epi rep {rep}")
+    _close(ops.gemm(a, w, out_dtype=torch.float32), ref.gemm(a, w, out_dtype=torch.float32), rtol=5e-3, atol=5e-3,
+           name="pair nt f32")
+    act, pre = ops.linear_swiglu(a, w)
+    pre_ref = ref.gemm(a, w, out_dtype=torch.float32)
+    _close(pre, pre_ref, name="pair swiglu pre")
+    _close(act, ref.swiglu_interleaved(pre_ref.to(torch.bfloat16)), name="pair swiglu")
+    out = ops.gemm(a, w, bias=bias, epilogue=ops.EPI_GELU_TANH)
+    _close(out, ref.gelu(ref.gemm(a, w, bias=bias, out_dtype=torch.float32), "tanh"), name="pair gelu")
+    dy = _r(M, N, seed=74)
+    _close(ops.grad_input(dy, w), dy.float() @ w.float(), name="pair dgrad")
+    x = _r(M, K, seed=75)
+    acc = torch.ones(N, K, device=DEV)
+    ops.grad_weight(dy, x, accumulate=acc)
+    _close(acc, dy.float().t() @ x.float() + 1.0, rtol=5e-3, atol=5e-3, name="pair wgrad acc")
+    _no_device_error()
