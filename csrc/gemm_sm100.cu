@@ -97,6 +97,7 @@ struct GemmParams {
   int consumer;
   unsigned* gbar;
   DecArgs dec;
+  int group_m;  // M-tiles per raster group (tile_coords); 16 unless a pair launch picks another
 };
 
 constexpr int kGatherPiece = 16384;   // bytes per claimed piece
@@ -171,8 +172,9 @@ struct GemmCfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + 4 * EPI_STAGE_FLOATS * 4 + kGatherMaxChunks / 8;
 };
 
-VLM_DEV void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
-  constexpr int G = 16;
+// Tile t -> (tm, tn): groups of G M-tiles, walked M-fastest inside a group, so the CTAs of a wave share
+// their B tiles (and G of A) in L2.  Stream-K consumers (streamk.cuh) assume G = 16.
+VLM_DEV void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn, int G = 16) {
   const int group = G * tiles_n;
   const int gid = t / group;
   const int first = gid * G;
@@ -462,7 +464,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
     Work w0;
     if (it0.next(p, w0)) {
       int tm0, tn0;
-      tile_coords(w0.tile, p.tiles_m, p.tiles_n, tm0, tn0);
+      tile_coords(w0.tile, p.tiles_m, p.tiles_n, tm0, tn0, p.group_m);
       prefetched = min(C::STAGES, w0.kb1 - w0.kb0);
       for (int i = 0; i < prefetched; ++i) {
         mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
@@ -520,7 +522,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       trace_mark(p, 2);
       while (ok && it.next(p, w)) {
         int tm, tn;
-        tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
+        tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn, p.group_m);
         const int m0 = tm * TILE_M + static_cast<int>(rank) * kBM, n0 = tn * BN + static_cast<int>(rank) * C::BNC;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           const bool pre = prefetched > 0;
@@ -652,7 +654,7 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
       if (threadIdx.x == 128 && lt == 0) trace_mark(p, 5);
       tc_fence_after();
       int tm, tn;
-      tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn);
+      tile_coords(w.tile, p.tiles_m, p.tiles_n, tm, tn, p.group_m);
       const int m_base = tm * TILE_M + static_cast<int>(rank) * kBM;  // this CTA's 128 rows of the tile
       const int row = m_base + row_in_tile;
       const int n0 = tn * BN;
@@ -945,6 +947,15 @@ static int max_pairs(int device) {
   return cached[device];
 }
 
+// M-tiles per raster group of pair launches (VLMRL_GEMM_GROUP overrides, for measurements).
+static int pair_group() {
+  static const int g = [] {
+    const char* e = std::getenv("VLMRL_GEMM_GROUP");
+    return e ? std::max(1, std::atoi(e)) : 16;
+  }();
+  return g;
+}
+
 static bool pair_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("VLMRL_GEMM_PAIR");
@@ -1007,6 +1018,7 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   }
 
   GemmParams p{};
+  p.group_m = 16;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
@@ -1096,6 +1108,7 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
     p.kb_per_split = static_cast<int>((K + kBK - 1) / kBK);
     p.streamk = 0;
     p.b_prefetch = 0;
+    p.group_m = pair_group();
     const int64_t tiles2 = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
     const int pairs = static_cast<int>(std::min<int64_t>(tiles2, bn == 256 ? s256 : s128));
     CUtensorMap ta, tb;
