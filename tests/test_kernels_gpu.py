@@ -554,9 +554,8 @@ def test_decode_attn_reads_shared_prompt_from_group_leader(monkeypatch):
 
 @pytest.mark.parametrize("M,N,K", [(520, 272, 200), (2304, 1536, 640), (4608, 2304, 256)])
 def test_gemm_cta_pair_tiles(M, N, K):
-    """GEMMs with M >= 512 run as CTA pairs (256-row tiles, tcgen05 cta_group::2, half of B per CTA). Ragged
-    M / N, both tile widths (the last shape picks 128-wide pair tiles for wave efficiency), every operand
-    layout and every epilogue against the fp32 oracle, twice in a row."""
+    """GEMMs with M >= 512 run as CTA pairs (256 x 256 tiles, tcgen05 cta_group::2, half of B per CTA). Ragged
+    M / N, every operand layout and every epilogue against the fp32 oracle, twice in a row."""
     a, w = _r(M, K, seed=70), _r(N, K, scale=0.1, seed=71)
     bias, res = _r(N, seed=72), _r(M, N, seed=73)
     for rep in range(2):
