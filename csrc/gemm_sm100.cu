@@ -1338,15 +1338,25 @@ at::Tensor dec_gemm_swiglu(at::Tensor x, at::Tensor w) {
 
 // Stream-K partials with per-CTA phase timestamps written to ``trace`` (int64 [>= grid * 8]): a measurement
 // aid for the decode GEMM's fixed latency.
+static std::tuple<at::Tensor, std::vector<int64_t>> tcgen05_partials(const at::Tensor& A, const at::Tensor& B);
+
 std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials_traced(at::Tensor A, at::Tensor B, at::Tensor trace) {
   TORCH_CHECK(trace.scalar_type() == at::kLong && trace.is_cuda() && trace.numel() >= 148 * 8, "trace: int64 [grid*8]");
   g_trace = reinterpret_cast<unsigned long long*>(trace.data_ptr());
-  auto out = gemm_partials(A, B);
+  auto out = tcgen05_partials(A, B);
   g_trace = nullptr;
   return out;
 }
 
+// Decode-shaped partial sums: the skinny mma.sync kernel (decode_gemm.cu) for M <= 64 when
+// VLMRL_SKINNY_GEMM=1, else the stream-K tcgen05 kernel; both write the same [slots, M, N] layout.
 std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials(at::Tensor A, at::Tensor B) {
+  if (skinny_enabled() && A.size(0) <= 64 && A.size(1) % 8 == 0 && B.size(0) % 8 == 0)
+    return skinny_partials(A, B, g_static_weights);
+  return tcgen05_partials(A, B);
+}
+
+static std::tuple<at::Tensor, std::vector<int64_t>> tcgen05_partials(const at::Tensor& A, const at::Tensor& B) {
   at::Tensor ws;
   SkMeta m{};
   gemm_ex(A, B, at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(), true, true, 1.0, EPI_STORE, false, nullptr, 0,

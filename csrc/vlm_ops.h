@@ -56,6 +56,11 @@ void unit_gather(std::vector<int64_t> srcs, int64_t dst_base, int64_t shard_byte
 // Stream-K partial sums of A.B^T without an epilogue: (ws [slots, M, N] fp32, meta) for the fused consumers.
 std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials(at::Tensor A, at::Tensor B);
 std::tuple<at::Tensor, std::vector<int64_t>> gemm_partials_traced(at::Tensor A, at::Tensor B, at::Tensor trace);
+// decode_gemm.cu: skinny (M <= 64) partial sums in the stream-K layout; static_weights lets the first weight
+// chunks go out before the wait on the previous kernel.
+bool skinny_enabled();
+std::tuple<at::Tensor, std::vector<int64_t>> skinny_partials(const at::Tensor& x, const at::Tensor& w,
+                                                             bool static_weights);
 // While on, GEMMs prefetch their K-major B operand before waiting on the previous kernel (PDL).
 void set_static_weights(bool on);
 

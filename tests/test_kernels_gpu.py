@@ -576,3 +576,20 @@ def test_gemm_cta_pair_tiles(M, N, K):
     ops.grad_weight(dy, x, accumulate=acc)
     _close(acc, dy.float().t() @ x.float() + 1.0, rtol=5e-3, atol=5e-3, name="pair wgrad acc")
     _no_device_error()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 2560, 4096), (8, 6144, 2560), (17, 1000, 2560), (64, 2560, 9728), (64, 6144, 2560)])
+def test_decode_partials(M, N, K):
+    """The decode-shaped partial-sum GEMM (stream-K layout; the skinny mma.sync kernel when it is selected)
+    summed by the residual + RMSNorm consumer equals x @ w.T; ragged M and N, inside and outside the
+    static-weights mode."""
+    x, w = _r(M, K, seed=80), _r(N, K, scale=0.02, seed=81)
+    zero = torch.zeros(M, N, dtype=torch.bfloat16, device=DEV)
+    ones = torch.ones(N, dtype=torch.bfloat16, device=DEV)
+    want = x.float() @ w.float().T
+    for static in (False, True):
+        with ops.static_weights() if static else torch.no_grad():
+            ws, meta = ops.gemm_partials(x, w)
+            h, _ = ops.dec_residual_norm(ws, meta, zero, ones, 1e-6)
+        _close(h, want, name=f"skinny partials static={static}")
+    _no_device_error()

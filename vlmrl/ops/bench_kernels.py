@@ -105,6 +105,18 @@ def bench_gemm(t: Timer):
         emit(f"gemm_swiglu_M{M}", ms, flops=2 * M * 2 * F * H)
 
 
+def bench_decode_gemms(t: Timer):
+    """Decode-step GEMM shapes (batch 64 and 8): the stream-K tcgen05 partial-sum GEMM the decode loop runs,
+    against cuBLAS through torch (a baseline only, never on the hot path)."""
+    H, F = 2560, 9728
+    for M in (64, 8):
+        for name, N, K in (("qkv", 6144, H), ("o_proj", H, 4096), ("gate_up", 2 * F, H), ("down", H, F)):
+            x, w = _r(M, K), _r(N, K, scale=0.02)
+            wb = N * K * 2
+            emit(f"decode_gemm_partials_{name}_M{M}", t(lambda: ops.gemm_partials(x, w)), bytes_=wb)
+            emit(f"cublas_linear_{name}_M{M}", t(lambda: torch.nn.functional.linear(x, w)), bytes_=wb)
+
+
 def bench_gemm_tiny(t: Timer):
     """Fixed per-launch cost of the GEMM: one k-block / one tile / many k-blocks / many tiles."""
     for M, N, K in ((64, 128, 64), (64, 128, 2560), (64, 6144, 64), (64, 6144, 2560), (256, 6144, 2560)):
@@ -377,7 +389,7 @@ def profile_small(case: str = "decode"):
 
 
 CASES = {"gemm": bench_gemm, "attn": bench_attn, "decode": bench_decode, "vocab": bench_vocab, "norm": bench_norm,
-         "decode_step": bench_decode_step, "gather": bench_gather,
+         "decode_step": bench_decode_step, "gather": bench_gather, "decode_gemms": bench_decode_gemms,
          "gemm_tiny": bench_gemm_tiny, "train_step": bench_train_step}
 
 
