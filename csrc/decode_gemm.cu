@@ -6,6 +6,11 @@
 // mma.sync m16n8k16 with fp32 accumulators in registers, and (while the weights are static, i.e. inside
 // the decode loop) the first weight chunks requested before waiting for the previous kernel.
 //
+// Opt-in (VLMRL_SKINNY_GEMM=1).  Measured against the stream-K tcgen05 GEMM on the 4B decode shapes:
+// faster alone for qkv / o_proj at batch 64 (20 vs 28 us, 15 vs 18 us, L2 evicted), slower for gate/up
+// (35 vs 30 us), and slower in the graph-captured decode step (5.00 vs 3.92 ms), where the tcgen05
+// kernel's early weight prefetch and programmatic launch overlap matter more.
+//
 // Work decomposition and output layout are exactly those of the stream-K tcgen05 GEMM (streamk.cuh): the
 // U = tiles_n * kb_count (tile, 64-wide k-block) units are split evenly over the G CTAs, and each CTA
 // writes one fp32 partial per tile segment to ws[slot][M][N].  So the decode consumers (dec_qkv,

@@ -643,16 +643,14 @@ __global__ void __launch_bounds__(256) adamw_vec8_kernel(float* __restrict__ p, 
     const float4* g4 = reinterpret_cast<const float4*>(g) + 2 * i;
     const float4* m4 = reinterpret_cast<const float4*>(m) + 2 * i;
     const float4* v4 = reinterpret_cast<const float4*>(v) + 2 * i;
-    // the fp32 state is touched once per step: streaming (evict-first) loads and stores keep it from
-    // displacing the bf16 weights the next forward reads
-    *reinterpret_cast<float4*>(pv) = __ldcs(p4);
-    *reinterpret_cast<float4*>(pv + 4) = __ldcs(p4 + 1);
-    *reinterpret_cast<float4*>(gv) = __ldcs(g4);
-    *reinterpret_cast<float4*>(gv + 4) = __ldcs(g4 + 1);
-    *reinterpret_cast<float4*>(mv) = __ldcs(m4);
-    *reinterpret_cast<float4*>(mv + 4) = __ldcs(m4 + 1);
-    *reinterpret_cast<float4*>(vv) = __ldcs(v4);
-    *reinterpret_cast<float4*>(vv + 4) = __ldcs(v4 + 1);
+    *reinterpret_cast<float4*>(pv) = p4[0];
+    *reinterpret_cast<float4*>(pv + 4) = p4[1];
+    *reinterpret_cast<float4*>(gv) = g4[0];
+    *reinterpret_cast<float4*>(gv + 4) = g4[1];
+    *reinterpret_cast<float4*>(mv) = m4[0];
+    *reinterpret_cast<float4*>(mv + 4) = m4[1];
+    *reinterpret_cast<float4*>(vv) = v4[0];
+    *reinterpret_cast<float4*>(vv + 4) = v4[1];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float gi = gv[j] * scale;
@@ -664,12 +662,12 @@ __global__ void __launch_bounds__(256) adamw_vec8_kernel(float* __restrict__ p, 
     float4* po = reinterpret_cast<float4*>(p) + 2 * i;
     float4* mo = reinterpret_cast<float4*>(m) + 2 * i;
     float4* vo = reinterpret_cast<float4*>(v) + 2 * i;
-    __stcs(po, *reinterpret_cast<float4*>(pv));
-    __stcs(po + 1, *reinterpret_cast<float4*>(pv + 4));
-    __stcs(mo, *reinterpret_cast<float4*>(mv));
-    __stcs(mo + 1, *reinterpret_cast<float4*>(mv + 4));
-    __stcs(vo, *reinterpret_cast<float4*>(vv));
-    __stcs(vo + 1, *reinterpret_cast<float4*>(vv + 4));
+    po[0] = *reinterpret_cast<float4*>(pv);
+    po[1] = *reinterpret_cast<float4*>(pv + 4);
+    mo[0] = *reinterpret_cast<float4*>(mv);
+    mo[1] = *reinterpret_cast<float4*>(mv + 4);
+    vo[0] = *reinterpret_cast<float4*>(vv);
+    vo[1] = *reinterpret_cast<float4*>(vv + 4);
     if (ph)
       reinterpret_cast<uint4*>(ph)[i] = make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]),
                                                    pack_bf16x2(pv[4], pv[5]), pack_bf16x2(pv[6], pv[7]));
