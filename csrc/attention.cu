@@ -1015,6 +1015,10 @@ static const int* seg_ptr(const c10::optional<at::Tensor>& t, const at::Tensor& 
 // attention_tc.cu: the tcgen05 forward for head_dim 64 / 128 (false: not handled, use the kernels here)
 bool flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
                        at::Tensor& o, at::Tensor& lse, int max_seqlen, bool causal, float scale, const int* pre);
+// attention_tc.cu: dK / dV on tcgen05 for head_dim 64 / 128 (false: not handled)
+bool flash_attn_bwd_dkdv_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
+                            const at::Tensor& lse, const at::Tensor& delta, const at::Tensor& cu, at::Tensor& dk,
+                            at::Tensor& dv, int max_seqlen, bool causal, float scale, const int* xq);
 
 // pre[b] = (start, len): keys every query of segment b also attends to (a shared prefix).
 void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu, at::Tensor o, at::Tensor lse,
@@ -1047,7 +1051,7 @@ static void bwd_dispatch(const at::Tensor& dout, const at::Tensor& q, const at::
   const int T = static_cast<int>(q.size(0));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const float sl2 = scale * kLog2e;
-  {
+  if (!flash_attn_bwd_dkdv_tc(q, k, v, dout, lse, delta, cu, dk, dv, max_seqlen, causal, scale, xq)) {
     const dim3 grid((max_seqlen + 63) / 64, Hkv, B);
     const int smem = (2 * 64 * D + 4 * 32 * D) * 2 + 4 * 32 * 4;
     auto kern = causal ? flash_bwd_dkdv_kernel<D, true> : flash_bwd_dkdv_kernel<D, false>;

@@ -338,6 +338,324 @@ void launch_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
              err_word(q.device().index()));
 }
 
+
+// ------------------------------------------------------------------ backward: dK, dV
+// One CTA = 128 keys of one KV head of one segment; 4 warps, thread r owns key row r (TMEM lane r).  For
+// each of the rep query heads sharing the KV head and each 64-query chunk that sees these keys (the
+// segment's own queries at or after the keys, causal; then xq = the member queries of segments that use
+// this one as a shared prefix, unmasked):
+//   thread 0   S^T = K . Q^T and dP^T = V . dO^T       tcgen05.mma 128 x 64 x D into TMEM
+//   all        P = exp2(S^T * scale_log2 - lse_log2), dS = P * (dP - delta), both bf16 into shared memory
+//   thread 0   dV += P^T . dO and dK += dS^T . Q        tcgen05.mma 128 x D x 64 (Q and dO chunks read as the
+//                                                      MN-major operand: the same tiles as above)
+// dK is scaled once at the end.  The Q / dO chunks are TMA-staged in two buffers; LSE and delta of the next
+// chunk are read while the current one's MMAs run.  Every wait is bounded (as in the forward).
+template <int D>
+struct TcBwdCfg {
+  static constexpr int K_BYTES = kBM * D * 2;    // D/64 sub-tiles [128 rows][128 B]
+  static constexpr int C_BYTES = 64 * D * 2;     // a 64-query chunk: D/64 sub-tiles [64 rows][128 B]
+  static constexpr int P_BYTES = kBM * 64 * 2;   // [128 rows][128 B]
+  static constexpr int K_OFF = 0, V_OFF = K_BYTES;
+  static constexpr int Q_OFF = 2 * K_BYTES;                 // [2] chunks
+  static constexpr int DO_OFF = Q_OFF + 2 * C_BYTES;        // [2] chunks
+  static constexpr int P_OFF = DO_OFF + 2 * C_BYTES;
+  static constexpr int DS_OFF = P_OFF + P_BYTES;
+  static constexpr int L_OFF = DS_OFF + P_BYTES;            // float [2][64] lse (log2 units), [2][64] delta
+  static constexpr int BAR_OFF = L_OFF + 4 * 64 * 4;
+  static constexpr int SMEM = 1024 + BAR_OFF + 128;
+  static constexpr uint32_t ST_COL = 0, DP_COL = 64, DV_COL = 128, DK_COL = D == 64 ? 192 : 256;
+  static constexpr uint32_t TMEM_COLS = D == 64 ? 256 : 512;
+};
+
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(128) flash_bwd_dkdv_tc_kernel(
+    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO, const float* __restrict__ LSE,
+    const float* __restrict__ DELTA, const int* __restrict__ cu, bf16* __restrict__ dK, bf16* __restrict__ dV, int Hq,
+    int Hkv, int T, float scale_log2, float scale, const int* __restrict__ xq, int* err) {
+  using C = TcBwdCfg<D>;
+  const int kblk = blockIdx.x, hk = blockIdx.y, b = blockIdx.z;
+  const int s0 = cu[b], L = cu[b + 1] - s0;
+  const int k0 = kblk * kBM;
+  if (k0 >= L) return;
+  const int xs = xq ? xq[2 * b] : 0, xlen = xq ? xq[2 * b + 1] - xq[2 * b] : 0;
+  const int rep = Hq / Hkv;
+  const int qc_start = CAUSAL ? k0 / 64 : 0;
+  const int n_own = (L + 63) / 64 - qc_start;
+  const int n_chunks = n_own + (xlen + 63) / 64;
+  const int total = rep * n_chunks;
+
+  extern __shared__ __align__(1024) uint8_t tcb_smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tcb_smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = sm + C::K_OFF;
+  uint8_t* sV = sm + C::V_OFF;
+  uint8_t* sQ = sm + C::Q_OFF;
+  uint8_t* sdO = sm + C::DO_OFF;
+  uint8_t* sP = sm + C::P_OFF;
+  uint8_t* sdS = sm + C::DS_OFF;
+  float* sL = reinterpret_cast<float*>(sm + C::L_OFF);  // [2][64]
+  float* sDl = sL + 2 * 64;                              // [2][64]
+  uint64_t* kvbar = reinterpret_cast<uint64_t*>(sm + C::BAR_OFF);
+  uint64_t* qfull = kvbar + 1;  // [2]
+  uint64_t* sbar = kvbar + 3;
+  uint64_t* gbar = kvbar + 4;
+  uint64_t* drain = kvbar + 5;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(kvbar + 6);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+
+  // chunk it -> (query head, first query row in the tensors, first query index inside its range, limit, own?)
+  struct Chunk {
+    int hh, row0, qs, qlim;
+    bool own;
+  };
+  auto chunk = [&](int it) {
+    Chunk ch;
+    ch.hh = hk * rep + it / n_chunks;
+    const int c = it % n_chunks;
+    ch.own = c < n_own;
+    ch.qs = ch.own ? (qc_start + c) * 64 : (c - n_own) * 64;
+    ch.qlim = ch.own ? L : xlen;
+    ch.row0 = (ch.own ? s0 : xs) + ch.qs;
+    return ch;
+  };
+  auto load_chunk = [&](int it) {
+    const Chunk ch = chunk(it);
+    uint64_t* bar = &qfull[it & 1];
+    mbar_arrive_expect_tx(bar, 2 * C::C_BYTES);
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c) {
+      tma_load_2d(sQ + (it & 1) * C::C_BYTES + c * (64 * 128), &tmQ, bar, ch.hh * D + 64 * c, ch.row0);
+      tma_load_2d(sdO + (it & 1) * C::C_BYTES + c * (64 * 128), &tmdO, bar, ch.hh * D + 64 * c, ch.row0);
+    }
+  };
+  auto load_stats = [&](int it) {  // LSE (log2 units) and delta of chunk it; +inf LSE masks a query
+    if (tid < 64) {
+      const Chunk ch = chunk(it);
+      const bool ok = ch.qs + tid < ch.qlim;
+      const int64_t idx = static_cast<int64_t>(ch.hh) * T + ch.row0 + tid;
+      sL[(it & 1) * 64 + tid] = ok ? LSE[idx] * kLog2eTc : INFINITY;
+      sDl[(it & 1) * 64 + tid] = ok ? DELTA[idx] : 0.f;
+    }
+  };
+
+  if (tid == 0) {
+    mbar_init(kvbar, 1);
+    mbar_init(&qfull[0], 1);
+    mbar_init(&qfull[1], 1);
+    mbar_init(sbar, 1);
+    mbar_init(gbar, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  pdl_wait();
+  if (tid == 0 && total > 0) {
+    mbar_arrive_expect_tx(kvbar, 2 * C::K_BYTES);
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c) {
+      tma_load_2d(sK + c * (kBM * 128), &tmK, kvbar, hk * D + 64 * c, s0 + k0);
+      tma_load_2d(sV + c * (kBM * 128), &tmV, kvbar, hk * D + 64 * c, s0 + k0);
+    }
+    load_chunk(0);
+    if (total > 1) load_chunk(1);
+  }
+  if (total > 0) load_stats(0);
+  if (warp == 0) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_trigger();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sQa = smem_u32(sQ), sdOa = smem_u32(sdO);
+  const uint32_t sPa = smem_u32(sP), sdSa = smem_u32(sdS);
+  constexpr uint32_t idesc_s = idesc_bf16_f32(kBM, 64, false, false);
+  constexpr uint32_t idesc_g = idesc_bf16_f32(kBM, D, false, true);
+  const int r = tid, key = k0 + r;  // key index inside the segment
+  bool ok = true;
+  int loads_issued = total > 1 ? 2 : total;
+
+  for (int it = 0; it < total && ok; ++it) {
+    const int st = it & 1;
+    const Chunk ch = chunk(it);
+    if (tid == 0) {
+      bool t_ok = it > 0 || mbar_wait(kvbar, 0, abort_flag, err, kErrTimeoutFlag);
+      t_ok = t_ok && mbar_wait(&qfull[st], static_cast<uint32_t>((it >> 1) & 1), abort_flag, err, kErrTimeoutFlag);
+      if (t_ok) {
+        tc_fence_after();
+        const uint32_t qa = sQa + st * C::C_BYTES, da = sdOa + st * C::C_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t ko = (kk >> 2) * (kBM * 128) + (kk & 3) * 32, co = (kk >> 2) * (64 * 128) + (kk & 3) * 32;
+          umma_f16(tmem + C::ST_COL, sdesc_sw128(sKa + ko, 16, 1024), sdesc_sw128(qa + co, 16, 1024), idesc_s,
+                   kk > 0 ? 1u : 0u);
+          umma_f16(tmem + C::DP_COL, sdesc_sw128(sVa + ko, 16, 1024), sdesc_sw128(da + co, 16, 1024), idesc_s,
+                   kk > 0 ? 1u : 0u);
+        }
+        umma_commit(sbar);
+      } else {
+        *abort_flag = 1;
+      }
+    }
+    ok = mbar_wait(sbar, static_cast<uint32_t>(it & 1), abort_flag, err, kErrTimeoutFlag);
+    if (__syncthreads_or(!ok)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    uint32_t sv[4][16], dp[4][16];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      tmem_ld16(tmem + lane_base + C::ST_COL + 16 * c, sv[c]);
+      tmem_ld16(tmem + lane_base + C::DP_COL + 16 * c, dp[c]);
+    }
+    tmem_ld_wait();
+    uint32_t pk[32], dk2[32];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+      for (int e = 0; e < 16; e += 2) {
+        float pr[2], ds[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int q = 16 * c + e + h;
+          const bool valid = key < L && (!CAUSAL || !ch.own || key <= ch.qs + q);
+          const float pv = valid ? exp2f(__uint_as_float(sv[c][e + h]) * scale_log2 - sL[st * 64 + q]) : 0.f;
+          pr[h] = pv;
+          ds[h] = pv * (__uint_as_float(dp[c][e + h]) - sDl[st * 64 + q]);
+        }
+        pk[(16 * c + e) / 2] = pack_bf16x2(pr[0], pr[1]);
+        dk2[(16 * c + e) / 2] = pack_bf16x2(ds[0], ds[1]);
+      }
+    }
+    // the previous chunk's dV / dK MMAs read sP / sdS: wait for them before overwriting
+    if (it > 0) {
+      ok = mbar_wait(gbar, static_cast<uint32_t>((it - 1) & 1), abort_flag, err, kErrTimeoutFlag);
+      if (__syncthreads_or(!ok)) {
+        ok = false;
+        break;
+      }
+    }
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {
+      const int off = r * 128 + ((cc ^ (r & 7)) << 4);
+      *reinterpret_cast<uint4*>(sP + off) = make_uint4(pk[4 * cc], pk[4 * cc + 1], pk[4 * cc + 2], pk[4 * cc + 3]);
+      *reinterpret_cast<uint4*>(sdS + off) =
+          make_uint4(dk2[4 * cc], dk2[4 * cc + 1], dk2[4 * cc + 2], dk2[4 * cc + 3]);
+    }
+    if (it + 1 < total) load_stats(it + 1);  // buffer (it+1)&1 was last read by chunk it-1's softmax
+    fence_proxy_async_cta();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t qa = sQa + st * C::C_BYTES, da = sdOa + st * C::C_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        umma_f16(tmem + C::DV_COL, sdesc_sw128(sPa + kk * 32, 16, 1024), sdesc_sw128(da + kk * 2048, 8192, 1024),
+                 idesc_g, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_f16(tmem + C::DK_COL, sdesc_sw128(sdSa + kk * 32, 16, 1024), sdesc_sw128(qa + kk * 2048, 8192, 1024),
+                 idesc_g, (it > 0 || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(gbar);
+      // chunk it+2 reuses this chunk's buffers once these MMAs are done
+      if (it + 2 < total) {
+        if (mbar_wait(gbar, static_cast<uint32_t>(it & 1), abort_flag, err, kErrTimeoutFlag)) {
+          load_chunk(it + 2);
+          ++loads_issued;
+        } else {
+          *abort_flag = 1;
+        }
+      }
+    }
+  }
+
+  if (ok && total > 0) {
+    ok = mbar_wait(gbar, static_cast<uint32_t>((total - 1) & 1), abort_flag, err, kErrTimeoutFlag);
+    ok = !__syncthreads_or(!ok);
+  }
+  if (ok && total > 0) {
+    tc_fence_after();
+    const bool row_ok = key < L;
+    const int64_t orow = (static_cast<int64_t>(s0 + key) * Hkv + hk) * D;
+#pragma unroll 1
+    for (int which = 0; which < 2; ++which) {
+      const uint32_t col = which == 0 ? C::DV_COL : C::DK_COL;
+      const float mul = which == 0 ? 1.f : scale;
+      bf16* out = (which == 0 ? dV : dK) + orow;
+#pragma unroll 1
+      for (int c0 = 0; c0 < D; c0 += 64) {
+        uint32_t o[4][16];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld16(tmem + lane_base + col + c0 + 16 * c, o[c]);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t w[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              w[e] = pack_bf16x2(__uint_as_float(o[c][2 * e]) * mul, __uint_as_float(o[c][2 * e + 1]) * mul);
+            uint4* dst = reinterpret_cast<uint4*>(out + c0 + 16 * c);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          }
+        }
+      }
+    }
+  } else if (total == 0 && key < L) {
+    // keys no query attends to (cannot happen for a non-empty segment; kept for completeness)
+    const int64_t orow = (static_cast<int64_t>(s0 + key) * Hkv + hk) * D;
+    for (int c = 0; c < D; ++c) dK[orow + c] = dV[orow + c] = f2bf(0.f);
+  }
+  if (!ok && tid == 0) {
+    volatile int no_abort = 0;
+    umma_commit(drain);
+    mbar_wait(drain, 0, &no_abort, nullptr, 0);
+    mbar_wait(kvbar, 0, &no_abort, nullptr, 0);
+    for (int i = max(0, loads_issued - 2); i < loads_issued; ++i)
+      mbar_wait(&qfull[i & 1], static_cast<uint32_t>((i >> 1) & 1), &no_abort, nullptr, 0);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D, bool CAUSAL>
+void launch_bwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
+                   const at::Tensor& lse, const at::Tensor& delta, const at::Tensor& cu, at::Tensor& dk, at::Tensor& dv,
+                   int max_seqlen, float scale, const int* xq) {
+  using C = TcBwdCfg<D>;
+  const int B = static_cast<int>(cu.numel() - 1), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(k.size(1));
+  const int T = static_cast<int>(q.size(0));
+  const CUtensorMap tq = make_tmap_2d_bf16(q.data_ptr(), static_cast<int64_t>(Hq) * D, T, static_cast<int64_t>(Hq) * D,
+                                           64, 64);
+  const CUtensorMap tdo = make_tmap_2d_bf16(dout.data_ptr(), static_cast<int64_t>(Hq) * D, T,
+                                            static_cast<int64_t>(Hq) * D, 64, 64);
+  const CUtensorMap tk = make_tmap_2d_bf16(k.data_ptr(), static_cast<int64_t>(Hkv) * D, T,
+                                           static_cast<int64_t>(Hkv) * D, 64, kBM);
+  const CUtensorMap tv = make_tmap_2d_bf16(v.data_ptr(), static_cast<int64_t>(Hkv) * D, T,
+                                           static_cast<int64_t>(Hkv) * D, 64, kBM);
+  auto kern = flash_bwd_dkdv_tc_kernel<D, CAUSAL>;
+  static bool configured = false;
+  if (!configured) {
+    VLM_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured = true;
+  }
+  const dim3 grid((max_seqlen + kBM - 1) / kBM, Hkv, B);
+  launch_pdl(kern, grid, dim3(128), C::SMEM, at::cuda::getCurrentCUDAStream(), tq, tk, tv, tdo, lse.data_ptr<float>(),
+             delta.data_ptr<float>(), cu.data_ptr<int>(), reinterpret_cast<bf16*>(dk.data_ptr()),
+             reinterpret_cast<bf16*>(dv.data_ptr()), Hq, Hkv, T, scale * kLog2eTc, scale, xq,
+             err_word(q.device().index()));
+}
+
 }  // namespace
 
 bool flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& cu,
@@ -354,6 +672,28 @@ bool flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tenso
   else
     causal ? launch_tc<64, true>(q, k, v, cu, o, lse, max_seqlen, scale, pre)
            : launch_tc<64, false>(q, k, v, cu, o, lse, max_seqlen, scale, pre);
+  return true;
+}
+
+}  // namespace vlm
+
+namespace vlm {
+
+bool flash_attn_bwd_dkdv_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
+                            const at::Tensor& lse, const at::Tensor& delta, const at::Tensor& cu, at::Tensor& dk,
+                            at::Tensor& dv, int max_seqlen, bool causal, float scale, const int* xq) {
+  static const bool enabled = [] {
+    const char* e = std::getenv("VLMRL_ATTN_BWD_TC");
+    return e && e[0] == '1';
+  }();
+  const int D = static_cast<int>(q.size(2));
+  if (!enabled || (D != 64 && D != 128)) return false;
+  if (D == 128)
+    causal ? launch_bwd_tc<128, true>(q, k, v, dout, lse, delta, cu, dk, dv, max_seqlen, scale, xq)
+           : launch_bwd_tc<128, false>(q, k, v, dout, lse, delta, cu, dk, dv, max_seqlen, scale, xq);
+  else
+    causal ? launch_bwd_tc<64, true>(q, k, v, dout, lse, delta, cu, dk, dv, max_seqlen, scale, xq)
+           : launch_bwd_tc<64, false>(q, k, v, dout, lse, delta, cu, dk, dv, max_seqlen, scale, xq);
   return true;
 }
 
