@@ -539,6 +539,11 @@ __global__ void __launch_bounds__(128) flash_bwd_dkdv_tc_kernel(
         ok = false;
         break;
       }
+      // chunk it+1 goes into the buffers chunk it-1 used, now that its dV / dK MMAs are done
+      if (tid == 0 && it + 1 < total && it + 1 >= 2) {
+        load_chunk(it + 1);
+        ++loads_issued;
+      }
     }
 #pragma unroll
     for (int cc = 0; cc < 8; ++cc) {
@@ -562,15 +567,6 @@ __global__ void __launch_bounds__(128) flash_bwd_dkdv_tc_kernel(
                  idesc_g, (it > 0 || kk > 0) ? 1u : 0u);
       }
       umma_commit(gbar);
-      // chunk it+2 reuses this chunk's buffers once these MMAs are done
-      if (it + 2 < total) {
-        if (mbar_wait(gbar, static_cast<uint32_t>(it & 1), abort_flag, err, kErrTimeoutFlag)) {
-          load_chunk(it + 2);
-          ++loads_issued;
-        } else {
-          *abort_flag = 1;
-        }
-      }
     }
   }
 

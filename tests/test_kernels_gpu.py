@@ -593,3 +593,40 @@ def test_decode_partials(M, N, K):
             h, _ = ops.dec_residual_norm(ws, meta, zero, ones, 1e-6)
         _close(h, want, name=f"skinny partials static={static}")
     _no_device_error()
+
+
+def test_tcgen05_dkdv_backward_matches_oracle():
+    """The tcgen05 dK / dV backward (opt-in, VLMRL_ATTN_BWD_TC=1; the switch is read once per process, so
+    the comparison runs in a child process): causal GQA and shared-prefix segments against the fp32 oracle."""
+    import os
+    import subprocess
+    import sys
+
+    code = r"""
+import math, torch
+from vlmrl import ops
+from vlmrl.ops import reference as ref
+def r(*s, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return torch.randn(*s, generator=g, device="cuda").bfloat16()
+for D, Hq, Hkv in ((128, 8, 2), (64, 4, 4)):
+    lens = [1, 63, 130, 388, 17]
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32, device="cuda")
+    T = sum(lens)
+    q, k, v, do = r(T, Hq, D, seed=1), r(T, Hkv, D, seed=2), r(T, Hkv, D, seed=3), r(T, Hq, D, seed=4)
+    sc = 1 / math.sqrt(D)
+    o, lse = ops.flash_attn(q, k, v, cu, max(lens), causal=True, scale=sc)
+    dq, dk, dv = ops.flash_attn_bwd(do, q, k, v, o, lse, cu, max(lens), causal=True, scale=sc)
+    orf, lr = ref.flash_attn(q, k, v, cu, max(lens), causal=True, scale=sc)
+    _, dkr, dvr = ref.flash_attn_bwd(do, q, k, v, orf, lr, cu, max(lens), causal=True, scale=sc)
+    for a, b, n in ((dk, dkr, "dk"), (dv, dvr, "dv")):
+        err = (a.float() - b.float()).abs().max().item()
+        lim = 2e-2 + 2e-2 * b.float().abs().max().item()
+        assert err <= lim, (D, n, err, lim)
+from vlmrl.ops._ext import ext
+assert ext().read_and_clear_error(torch.cuda.current_device()) == 0
+print("ok")
+"""
+    env = dict(os.environ, VLMRL_ATTN_BWD_TC="1")
+    res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stdout[-2000:] + res.stderr[-2000:]
