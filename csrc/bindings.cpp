@@ -28,7 +28,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layer_norm_fwd", &vlm::layer_norm_fwd);
   m.def("qk_norm_rope_fwd", &vlm::qk_norm_rope_fwd);
   m.def("qk_norm_rope_bwd", &vlm::qk_norm_rope_bwd);
-  m.def("vision_rope", &vlm::vision_rope);
+  m.def("vision_rope", &vlm::vision_rope, py::arg("qkv"), py::arg("rc"), py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("n_heads"), py::arg("style") = 0);
   m.def("swiglu_bwd", &vlm::swiglu_bwd);
   m.def("embed", &vlm::embed);
   m.def("scatter_rows", &vlm::scatter_rows);

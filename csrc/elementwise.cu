@@ -449,9 +449,12 @@ void qk_norm_rope_bwd(at::Tensor dq, at::Tensor dk, at::Tensor dv, at::Tensor qk
 }
 
 // ------------------------------------------------------------------ ViT 2-D rotary
-// qkv [N, 3, H, D] -> q, k (rotated), v.  Pair j of (j, j+D/2): angle = (j < D/4 ? row : col) * 1e4^(-(j mod D/4)/(D/4)).
+// qkv [N, 3, H, D] -> q, k (rotated), v.  Rotation pairs are (j, j+D/2).
+//   style 0 (HF Qwen3-VL / Qwen2.5-VL): one angle per pair, (j < D/4 ? row : col) * 1e4^(-(j mod D/4)/(D/4)).
+//   style 1 (the reference's Qwen3-VL tower, models/qwen3vl/vision.py:21-30,69-77): D/2 frequencies
+//     1e4^(-j/(D/2)); element j uses row * f_j and element j+D/2 uses col * f_j (two angles per pair).
 __global__ void vision_rope_kernel(const bf16* __restrict__ qkv, const int* __restrict__ rc, bf16* __restrict__ q,
-                                   bf16* __restrict__ k, bf16* __restrict__ v, int N, int H, int D) {
+                                   bf16* __restrict__ k, bf16* __restrict__ v, int N, int H, int D, int style) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int half = D / 2, quarter = D / 4;
   const int64_t total = static_cast<int64_t>(N) * H * half;
@@ -461,33 +464,44 @@ __global__ void vision_rope_kernel(const bf16* __restrict__ qkv, const int* __re
   const int n = static_cast<int>(idx / (static_cast<int64_t>(half) * H));
   const int64_t base = static_cast<int64_t>(n) * 3 * H * D;
   const int64_t o = (static_cast<int64_t>(n) * H + h) * D;
-  const int coord = j < quarter ? rc[2 * n] : rc[2 * n + 1];
-  const float freq = exp2f(-static_cast<float>(j % quarter) / quarter * 13.287712379549449f);  // log2(1e4)
-  float s, c;
-  sincosf(static_cast<float>(coord) * freq, &s, &c);
+  constexpr float kLog2Theta = 13.287712379549449f;  // log2(1e4)
+  float s1, c1, s2, c2;
+  if (style == 0) {
+    const int coord = j < quarter ? rc[2 * n] : rc[2 * n + 1];
+    const float freq = exp2f(-static_cast<float>(j % quarter) / quarter * kLog2Theta);
+    sincosf(static_cast<float>(coord) * freq, &s1, &c1);
+    s2 = s1;
+    c2 = c1;
+  } else {
+    const float freq = exp2f(-static_cast<float>(j) / half * kLog2Theta);
+    sincosf(static_cast<float>(rc[2 * n]) * freq, &s1, &c1);
+    sincosf(static_cast<float>(rc[2 * n + 1]) * freq, &s2, &c2);
+  }
 #pragma unroll
   for (int which = 0; which < 2; ++which) {
     const bf16* src = qkv + base + static_cast<int64_t>(which) * H * D + static_cast<int64_t>(h) * D;
     bf16* dst = (which == 0 ? q : k) + o;
     const float x1 = bf2f(src[j]), x2 = bf2f(src[j + half]);
-    dst[j] = f2bf(x1 * c - x2 * s);
-    dst[j + half] = f2bf(x2 * c + x1 * s);
+    dst[j] = f2bf(x1 * c1 - x2 * s1);
+    dst[j + half] = f2bf(x2 * c2 + x1 * s2);
   }
   const bf16* sv = qkv + base + 2ll * H * D + static_cast<int64_t>(h) * D;
   v[o + j] = sv[j];
   v[o + j + half] = sv[j + half];
 }
 
-void vision_rope(at::Tensor qkv, at::Tensor rc, at::Tensor q, at::Tensor k, at::Tensor v, int64_t n_heads) {
+void vision_rope(at::Tensor qkv, at::Tensor rc, at::Tensor q, at::Tensor k, at::Tensor v, int64_t n_heads, int64_t style) {
   const int N = static_cast<int>(qkv.size(0));
   const int D = static_cast<int>(q.size(-1));
   if (N == 0) return;
   TORCH_CHECK(rc.scalar_type() == at::kInt && rc.is_contiguous(), "vision_rope: rc int32 [N,2]");
+  TORCH_CHECK(style == 0 || style == 1, "vision_rope: style 0 (HF) or 1 (reference tower)");
   const c10::cuda::CUDAGuard g(qkv.device());
   const int64_t total = static_cast<int64_t>(N) * n_heads * (D / 2);
   vision_rope_kernel<<<static_cast<int>((total + 255) / 256), 256, 0, cur_stream()>>>(
       reinterpret_cast<const bf16*>(qkv.data_ptr()), rc.data_ptr<int>(), reinterpret_cast<bf16*>(q.data_ptr()),
-      reinterpret_cast<bf16*>(k.data_ptr()), reinterpret_cast<bf16*>(v.data_ptr()), N, static_cast<int>(n_heads), D);
+      reinterpret_cast<bf16*>(k.data_ptr()), reinterpret_cast<bf16*>(v.data_ptr()), N, static_cast<int>(n_heads), D,
+      static_cast<int>(style));
   VLM_LAUNCHED();
 }
 

@@ -85,7 +85,8 @@ void qk_norm_rope_fwd(at::Tensor qkv, at::Tensor qw, at::Tensor kw, at::Tensor p
 void qk_norm_rope_bwd(at::Tensor dq, at::Tensor dk, at::Tensor dv, at::Tensor qkv, at::Tensor qw, at::Tensor kw,
                       at::Tensor pos, at::Tensor inv_freq, at::Tensor ax, at::Tensor rq, at::Tensor rk, at::Tensor dqkv,
                       at::Tensor dqw, at::Tensor dkw, int64_t nq, int64_t nkv, double eps);
-void vision_rope(at::Tensor qkv, at::Tensor rc, at::Tensor q, at::Tensor k, at::Tensor v, int64_t n_heads);
+void vision_rope(at::Tensor qkv, at::Tensor rc, at::Tensor q, at::Tensor k, at::Tensor v, int64_t n_heads,
+                 int64_t style);
 void swiglu_bwd(at::Tensor d_act, at::Tensor pre, at::Tensor out);
 void embed(at::Tensor tokens, at::Tensor table, at::Tensor out);
 void scatter_rows(at::Tensor h, at::Tensor rows, at::Tensor src, bool add);

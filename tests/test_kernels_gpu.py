@@ -295,8 +295,10 @@ def test_swiglu_bwd_and_vision_rope():
     N, H, D = 64, 16, 64
     qkv = _r(N, 3 * H * D, seed=36)
     rc = torch.randint(0, 40, (N, 2), device=DEV, dtype=torch.int32)
-    for a, b in zip(ops.vision_rope(qkv, rc, n_heads=H, head_dim=D), ref.vision_rope(qkv, rc, n_heads=H, head_dim=D)):
-        _close(a, b, name="vision rope")
+    for style in (0, 1):
+        for a, b in zip(ops.vision_rope(qkv, rc, n_heads=H, head_dim=D, style=style),
+                        ref.vision_rope(qkv, rc, n_heads=H, head_dim=D, style=style)):
+            _close(a, b, name=f"vision rope style {style}")
 
 
 def test_patchify():

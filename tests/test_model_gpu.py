@@ -143,3 +143,25 @@ def test_tiny_qwen25_gpu_vs_cpu():
     m_gpu.prefill(pb, cache, torch.arange(1, device="cuda"))
     step = m_gpu.decode_step(torch.tensor([ids[P]], device="cuda"), cache, torch.from_numpy(deltas).cuda())
     assert (step[0].float() - lg[P].float()).abs().max().item() < 0.05
+
+
+def test_reference_vision_tower_gpu_vs_cpu():
+    """The reference's Qwen3-VL tower variant (RMSNorm/SwiGLU, 4-token windows, its rotary) on the CUDA path."""
+    from dataclasses import replace
+
+    from vlmrl.models.qwen3vl.config import get_preset
+    from vlmrl.models.qwen3vl.params import init_params
+
+    spec = get_preset("tiny", vision_arch="reference")
+    spec = replace(spec, vision=replace(spec.vision, window_size=32, num_position_embeddings=None))
+    units = init_params(spec, seed=8)
+    units["visual"] += 0.05 * torch.randn(units["visual"].shape, generator=torch.Generator().manual_seed(2))
+    m_cpu = Qwen3VLModel(spec, units=units, dtype=torch.float32)
+    m_gpu = Qwen3VLModel(spec, units=units, dtype=torch.bfloat16, device="cuda")
+    grid = [(1, 8, 12)]
+    pix = torch.randn(96, spec.vision.patch_volume, generator=torch.Generator().manual_seed(4))
+    vc = m_cpu.encode_vision(pix, grid)
+    vg = m_gpu.encode_vision(pix.cuda().to(torch.bfloat16), grid)
+    assert _rel(vg.tokens.cpu(), vc.tokens) < 0.03
+    assert len(vg.deepstack) == len(vc.deepstack) == 1
+    assert _rel(vg.deepstack[0].cpu(), vc.deepstack[0]) < 0.03

@@ -89,7 +89,11 @@ class Qwen3VLSpec:
     vision_end_token_id: int = VISION_END_TOKEN_ID
     # "hf": LayerNorm + GELU MLP ViT with learned pos-embed and full attention (HF Qwen3-VL);
     # "qwen25": RMSNorm + SwiGLU ViT with window attention and full attention at fullatt_block_indexes
-    # (HF Qwen2.5-VL).
+    # (HF Qwen2.5-VL);
+    # "reference": the Qwen3-VL tower as the reference computes it (reference models/qwen3vl/vision.py:
+    # RMSNorm + biased SwiGLU blocks, no position table, windows of window_size px with full attention at
+    # fullatt_block_indexes, its own rotary frequencies, RMSNorm mergers with tanh-GELU, deepstack
+    # mergers), for numerical parity with parameter trees that the reference trained or converted.
     vision_arch: str = "hf"
 
     def to_dict(self) -> Dict[str, Any]:
@@ -159,7 +163,7 @@ def spec_from_config(cfg: Dict[str, Any]) -> Qwen3VLSpec:
         video_token_id=int(cfg.get("video_token_id", VIDEO_TOKEN_ID)),
         vision_start_token_id=int(cfg.get("vision_start_token_id", VISION_START_TOKEN_ID)),
         vision_end_token_id=int(cfg.get("vision_end_token_id", VISION_END_TOKEN_ID)),
-        vision_arch="qwen25" if qwen25 else "hf",
+        vision_arch="qwen25" if qwen25 else str(cfg.get("vision_arch", "hf")),
     )
 
 
@@ -202,6 +206,9 @@ def spec_to_config(spec: Qwen3VLSpec) -> Dict[str, Any]:
             cfg["vision_config"].pop("num_position_embeddings")
             cfg["vision_config"].pop("deepstack_visual_indexes")
             cfg["text_config"]["rope_scaling"] = {"type": "mrope", "mrope_section": list(t.rope_section)}
+        elif spec.vision_arch == "reference":
+            cfg["vision_arch"] = "reference"
+            cfg["vision_config"].update(window_size=v.window_size, fullatt_block_indexes=list(v.fullatt_block_indexes))
     return cfg
 
 

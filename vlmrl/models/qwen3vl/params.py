@@ -111,8 +111,9 @@ def vision_layout(spec: Qwen3VLSpec) -> Optional[UnitLayout]:
     if v is None:
         return None
     Hv, I, out, M = v.hidden_size, v.intermediate_size, v.out_hidden_size, v.merged_hidden_size
-    if spec.vision_arch == "qwen25":
-        # RMSNorm blocks with a biased SwiGLU MLP (gate/up rows interleaved), one RMSNorm merger
+    if spec.vision_arch in ("qwen25", "reference"):
+        # RMSNorm blocks with a biased SwiGLU MLP (gate/up rows interleaved), RMSNorm merger(s); the
+        # reference tower adds one post-shuffle merger (RMSNorm over 4*Hv) per deepstack index
         ps = [ParamSpec("patch_w", (Hv, v.patch_volume))]
         for j in range(v.depth):
             p = f"b{j}."
@@ -122,9 +123,13 @@ def vision_layout(spec: Qwen3VLSpec) -> Optional[UnitLayout]:
                    ParamSpec(p + "n2_w", (Hv,), "ones"),
                    ParamSpec(p + "gu_w", (2 * I, Hv)), ParamSpec(p + "gu_b", (2 * I,), "zeros"),
                    ParamSpec(p + "down_w", (Hv, I)), ParamSpec(p + "down_b", (Hv,), "zeros")]
-        ps += [ParamSpec("m.norm_w", (Hv,), "ones"),
-               ParamSpec("m.fc1_w", (M, M)), ParamSpec("m.fc1_b", (M,), "zeros"),
-               ParamSpec("m.fc2_w", (out, M)), ParamSpec("m.fc2_b", (out,), "zeros")]
+        mergers = [("m.", Hv)]
+        if spec.vision_arch == "reference":
+            mergers += [(f"d{k}.", M) for k in range(len(v.deepstack_visual_indexes))]
+        for prefix, norm_dim in mergers:
+            ps += [ParamSpec(prefix + "norm_w", (norm_dim,), "ones"),
+                   ParamSpec(prefix + "fc1_w", (M, M)), ParamSpec(prefix + "fc1_b", (M,), "zeros"),
+                   ParamSpec(prefix + "fc2_w", (out, M)), ParamSpec(prefix + "fc2_b", (out,), "zeros")]
         return UnitLayout("visual", ps, trainable=False)
     ps = [ParamSpec("patch_w", (Hv, v.patch_volume)), ParamSpec("patch_b", (Hv,), "zeros")]
     if v.num_position_embeddings:
@@ -266,7 +271,7 @@ def flax_leaves(spec: Qwen3VLSpec, views: Dict[str, Dict[str, torch.Tensor]]):
         return
     v = views["visual"]
     yield "visual/patch_embed/proj/kernel", v["patch_w"], True
-    if spec.vision_arch == "qwen25":
+    if spec.vision_arch in ("qwen25", "reference"):
         for j in range(spec.vision.depth):
             b, p = f"b{j}.", f"visual/blocks_{j}"
             yield f"{p}/norm1/weight", v[b + "n1_w"], False
@@ -280,10 +285,12 @@ def flax_leaves(spec: Qwen3VLSpec, views: Dict[str, Dict[str, torch.Tensor]]):
             yield f"{p}/mlp/up_proj/bias", v[b + "gu_b"][1::2], False
             yield f"{p}/mlp/down_proj/kernel", v[b + "down_w"], True
             yield f"{p}/mlp/down_proj/bias", v[b + "down_b"], False
-        yield "visual/merger/norm/weight", v["m.norm_w"], False
-        for src, dst in (("fc1", "linear1"), ("fc2", "linear2")):
-            yield f"visual/merger/{dst}/kernel", v["m." + src + "_w"], True
-            yield f"visual/merger/{dst}/bias", v["m." + src + "_b"], False
+        names = list(_merged_names(spec)) if spec.vision_arch == "reference" else [("m.", "visual/merger")]
+        for b, p in names:
+            yield f"{p}/norm/weight", v[b + "norm_w"], False
+            for src, dst in (("fc1", "linear1"), ("fc2", "linear2")):
+                yield f"{p}/{dst}/kernel", v[b + src + "_w"], True
+                yield f"{p}/{dst}/bias", v[b + src + "_b"], False
         return
     yield "visual/patch_embed/proj/bias", v["patch_b"], False
     if "pos_embed" in v:

@@ -2,7 +2,7 @@
 
 HF-faithful architecture (``transformers`` ``Qwen3VLVisionModel``), which the
 reference approximates (reference ``models/qwen3vl/vision.py:178-331``; its
-RMSNorm/SwiGLU/windowed deviations are not reproduced):
+RMSNorm/SwiGLU/windowed variant is ``vision_arch="reference"``, below):
 
 1. patch embedding: rows ``[N, C*Tp*P*P]`` -> ``[N, Hv]`` (Conv3d as one GEMM, with bias);
 2. + bilinearly interpolated learned position embedding (merge-window order);
@@ -23,6 +23,16 @@ together); blocks are RMSNorm -> qkv -> 2-D rotary -> attention within each
 window (whole frame at ``fullatt_block_indexes``) -> proj, then RMSNorm ->
 biased SwiGLU MLP; one merger (RMSNorm -> 2x2 concat -> fc1 -> GELU -> fc2);
 the merged tokens are put back in raster order.
+
+``vision_arch == "reference"`` (the Qwen3-VL tower as the reference computes it, reference
+``models/qwen3vl/vision.py:178-331``): the qwen25 block structure with the reference's own
+rotary pairing (``ops.vision_rope(style=1)``), windows of ``window_size`` pixels (one 2x2 merge unit
+for Qwen3-VL configs, which give no window size), full attention over each whole image at
+``fullatt_block_indexes`` (by default the deepstack indexes), a post-shuffle RMSNorm merger after
+each deepstack block, and tanh-GELU in every merger; merged tokens and deepstack features are put
+back in raster order.  The reference's full-attention ``cu_seqlens`` count ``4 * t*h*w`` tokens per
+image (``vision.py:286-290``), which equals whole-image attention for the one image per call it
+encodes; here each image is its own sequence for any batch of images.
 """
 
 from __future__ import annotations
@@ -89,8 +99,11 @@ def prepare_vision_inputs(spec: Qwen3VLSpec, grids: Sequence[Tuple[int, int, int
     for t, h, w in grids:
         seq += [int(h) * int(w)] * int(t)
     cu = torch.tensor(np.concatenate([[0], np.cumsum(seq)]).astype(np.int32), device=device)
+    if spec.vision_arch == "reference":  # full-attention blocks span all frames of an image
+        seq = [int(t) * int(h) * int(w) for t, h, w in grids]
+        cu = torch.tensor(np.concatenate([[0], np.cumsum(seq)]).astype(np.int32), device=device)
     vin = VisionInputs(rc=rc, pos_idx=pos_idx, pos_w=pos_w, cu_seqlens=cu, max_seqlen=max(seq) if seq else 0)
-    if spec.vision_arch == "qwen25":
+    if spec.vision_arch in ("qwen25", "reference"):
         unit = v.spatial_merge_size ** 2
         order, cuw = window_index(grids, v.spatial_merge_size, v.window_size, v.patch_size)
         perm = (order[:, None] * unit + np.arange(unit)[None]).reshape(-1)
@@ -124,7 +137,9 @@ class VisionTower:
     def forward(self, flat: torch.Tensor, pixel_rows: torch.Tensor, vin: VisionInputs):
         """pixel_rows [N, patch_volume] -> (merged [N/4, out], [deepstack_k [N/4, out]])."""
         if self.spec.vision_arch == "qwen25":
-            return self._forward_windowed(flat, pixel_rows, vin), []
+            return self._forward_windowed(flat, pixel_rows, vin)[0], []
+        if self.spec.vision_arch == "reference":
+            return self._forward_windowed(flat, pixel_rows, vin)
         v = self.v
         p = self.layout.views(flat)
         dt = flat.dtype
@@ -153,31 +168,41 @@ class VisionTower:
         merged = self._merge(x, p, "m.", post_norm=False)
         return merged, deep
 
-    def _forward_windowed(self, flat: torch.Tensor, pixel_rows: torch.Tensor, vin: VisionInputs) -> torch.Tensor:
+    def _forward_windowed(self, flat: torch.Tensor, pixel_rows: torch.Tensor, vin: VisionInputs):
+        """RMSNorm/SwiGLU towers over window-ordered patches -> (merged, deepstack features), raster order."""
         v = self.v
+        ref_tower = self.spec.vision_arch == "reference"
         p = self.layout.views(flat)
         dt = flat.dtype
         H, nh = v.hidden_size, v.num_heads
         hd = H // nh
+        M = v.merged_hidden_size
+        gelu = ops.EPI_GELU_TANH if ref_tower else ops.EPI_GELU_ERF
         x = ops.gemm(pixel_rows.to(dt), p["patch_w"], out_dtype=dt)
         x = x.index_select(0, vin.perm)
         full = set(int(i) for i in v.fullatt_block_indexes)
+        deep_idx = list(v.deepstack_visual_indexes) if ref_tower else []
+        deep: List[torch.Tensor] = []
         for j in range(v.depth):
             b = f"b{j}."
             cu, ms = (vin.cu_seqlens, vin.max_seqlen) if j in full else (vin.cu_window, vin.max_window)
             xn, _ = ops.rms_norm(x, p[b + "n1_w"], 1e-6)
             qkv = ops.gemm(xn, p[b + "qkv_w"], bias=p[b + "qkv_b"], out_dtype=dt)
-            q, k, vv = ops.vision_rope(qkv, vin.rc, n_heads=nh, head_dim=hd)
+            q, k, vv = ops.vision_rope(qkv, vin.rc, n_heads=nh, head_dim=hd, style=1 if ref_tower else 0)
             o, _ = ops.flash_attn(q, k, vv, cu, ms, causal=False)
             x = ops.gemm(o.reshape(-1, H), p[b + "proj_w"], bias=p[b + "proj_b"], residual=x, out_dtype=dt)
             xn, _ = ops.rms_norm(x, p[b + "n2_w"], 1e-6)
             a = ops.gemm(xn, p[b + "gu_w"], bias=p[b + "gu_b"], epilogue=ops.EPI_SWIGLU, out_dtype=dt)
             x = ops.gemm(a, p[b + "down_w"], bias=p[b + "down_b"], residual=x, out_dtype=dt)
-        M = v.merged_hidden_size
+            if j in deep_idx:  # post-shuffle merger: RMSNorm over the concatenated 2x2 unit
+                pre = f"d{deep_idx.index(j)}."
+                xn, _ = ops.rms_norm(x.reshape(-1, M), p[pre + "norm_w"], 1e-6)
+                h = ops.gemm(xn, p[pre + "fc1_w"], bias=p[pre + "fc1_b"], epilogue=gelu, out_dtype=dt)
+                deep.append(ops.gemm(h, p[pre + "fc2_w"], bias=p[pre + "fc2_b"], out_dtype=dt).index_select(0, vin.unperm))
         xn, _ = ops.rms_norm(x, p["m.norm_w"], 1e-6)
-        h = ops.gemm(xn.reshape(-1, M), p["m.fc1_w"], bias=p["m.fc1_b"], epilogue=ops.EPI_GELU_ERF, out_dtype=dt)
+        h = ops.gemm(xn.reshape(-1, M), p["m.fc1_w"], bias=p["m.fc1_b"], epilogue=gelu, out_dtype=dt)
         merged = ops.gemm(h, p["m.fc2_w"], bias=p["m.fc2_b"], out_dtype=dt)
-        return merged.index_select(0, vin.unperm)
+        return merged.index_select(0, vin.unperm), deep
 
 
 __all__ = ["VisionInputs", "prepare_vision_inputs", "VisionTower"]

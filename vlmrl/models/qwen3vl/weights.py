@@ -64,6 +64,15 @@ def _put_qwen25_vision(v: Dict[str, torch.Tensor], vk: str, val: torch.Tensor, p
         if name == "norm" and m.group(2) == "bias":
             return
         put(v[f"m.{name}_{'w' if m.group(2) == 'weight' else 'b'}"], val)
+        return
+    # reference tower: HF Qwen3-VL deepstack mergers (LayerNorm bias dropped, as the reference's converter
+    # does, reference models/qwen3vl/model.py:1076-1087)
+    m = re.match(r"deepstack_merger_list\.(\d+)\.(norm|linear_fc1|linear_fc2)\.(weight|bias)$", vk)
+    if m and f"d{int(m.group(1))}.norm_w" in v:
+        name = {"norm": "norm", "linear_fc1": "fc1", "linear_fc2": "fc2"}[m.group(2)]
+        if name == "norm" and m.group(3) == "bias":
+            return
+        put(v[f"d{int(m.group(1))}.{name}_{'w' if m.group(3) == 'weight' else 'b'}"], val)
 
 
 def hf_state_dict_to_units(spec: Qwen3VLSpec, sd: Dict[str, torch.Tensor], dtype=torch.float32,
@@ -88,11 +97,11 @@ def hf_state_dict_to_units(spec: Qwen3VLSpec, sd: Dict[str, torch.Tensor], dtype
             v = views["visual"]
             if vk == "patch_embed.proj.weight":
                 put(v["patch_w"], val.reshape(val.shape[0], -1))
-            elif vk == "patch_embed.proj.bias":
-                put(v["patch_b"], val)
-            elif vk == "pos_embed.weight":
-                put(v["pos_embed"], val)
-            elif spec.vision_arch == "qwen25":
+            elif vk in ("patch_embed.proj.bias", "pos_embed.weight"):
+                name = "patch_b" if vk == "patch_embed.proj.bias" else "pos_embed"
+                if name in v:  # the RMSNorm towers have neither
+                    put(v[name], val)
+            elif spec.vision_arch in ("qwen25", "reference"):
                 _put_qwen25_vision(v, vk, val, put)
             else:
                 m = re.match(r"blocks\.(\d+)\.(.+)\.(weight|bias)$", vk)
@@ -189,7 +198,7 @@ def units_to_hf_state_dict(spec: Qwen3VLSpec, units: Dict[str, torch.Tensor]) ->
         V = "model.visual."
         sd[V + "patch_embed.proj.weight"] = v["patch_w"].reshape(vs.hidden_size, vs.in_channels, vs.temporal_patch_size,
                                                                  vs.patch_size, vs.patch_size).clone()
-        if spec.vision_arch == "qwen25":
+        if spec.vision_arch in ("qwen25", "reference"):
             for j in range(vs.depth):
                 b, q = f"b{j}.", f"{V}blocks.{j}."
                 sd[q + "norm1.weight"] = v[b + "n1_w"].clone()
@@ -206,6 +215,13 @@ def units_to_hf_state_dict(spec: Qwen3VLSpec, units: Dict[str, torch.Tensor]) ->
             for src, dst in (("fc1", "mlp.0"), ("fc2", "mlp.2")):
                 sd[f"{V}merger.{dst}.weight"] = v[f"m.{src}_w"].clone()
                 sd[f"{V}merger.{dst}.bias"] = v[f"m.{src}_b"].clone()
+            if spec.vision_arch == "reference":
+                for k in range(len(vs.deepstack_visual_indexes)):
+                    q = f"{V}deepstack_merger_list.{k}."
+                    sd[q + "norm.weight"] = v[f"d{k}.norm_w"].clone()
+                    for src, dst in (("fc1", "linear_fc1"), ("fc2", "linear_fc2")):
+                        sd[q + f"{dst}.weight"] = v[f"d{k}.{src}_w"].clone()
+                        sd[q + f"{dst}.bias"] = v[f"d{k}.{src}_b"].clone()
             return sd
         sd[V + "patch_embed.proj.bias"] = v["patch_b"].clone()
         if "pos_embed" in v:

@@ -361,14 +361,15 @@ def qk_norm_rope_bwd(dq, dk, dv, qkv, q_w, k_w, pos, rq, rk, rope: RopeCfg, *, n
     return dqkv
 
 
-def vision_rope(qkv, rc, *, n_heads: int, head_dim: int):
+def vision_rope(qkv, rc, *, n_heads: int, head_dim: int, style: int = 0):
+    """ViT 2-D rotary; ``style`` 0 is HF's pairing, 1 the reference tower's (see ``reference.vision_rope``)."""
     if not _cuda(qkv):
-        return ref.vision_rope(qkv, rc, n_heads=n_heads, head_dim=head_dim)
+        return ref.vision_rope(qkv, rc, n_heads=n_heads, head_dim=head_dim, style=style)
     N = qkv.shape[0]
     q = torch.empty(N, n_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
     k = torch.empty_like(q)
     v = torch.empty_like(q)
-    ext().vision_rope(qkv, rc, q, k, v, n_heads)
+    ext().vision_rope(qkv, rc, q, k, v, n_heads, int(style))
     return q, k, v
 
 

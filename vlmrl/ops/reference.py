@@ -173,15 +173,34 @@ def qk_norm_rope_bwd(dq, dk, dv, qkv, q_w, k_w, pos, rq, rk, *, n_q, n_kv, head_
     return dqkv.to(qkv.dtype), dqw, dkw
 
 
-def vision_rope(qkv: torch.Tensor, rc: torch.Tensor, *, n_heads: int, head_dim: int, theta: float = 10000.0):
-    """ViT: qkv [N, 3*H*D] (q|k|v, head-major) -> q, k, v [N, H, D] with 2-D rotary on q, k."""
+def vision_rope(qkv: torch.Tensor, rc: torch.Tensor, *, n_heads: int, head_dim: int, theta: float = 10000.0,
+                style: int = 0):
+    """ViT: qkv [N, 3*H*D] (q|k|v, head-major) -> q, k, v [N, H, D] with 2-D rotary on q, k.
+
+    ``style`` 0: HF (D/4 frequencies per axis, one angle per rotation pair).  ``style`` 1: the reference's
+    Qwen3-VL tower (reference ``models/qwen3vl/vision.py:21-30,69-77,226-230,280-284``): D/2 frequencies
+    ``theta**(-j/(D/2))``; element j of the first half turns by ``row * f_j`` and element j of the second
+    half by ``col * f_j``, through ``x * cos + rotate_half(x) * sin``.
+    """
     N, D = qkv.shape[0], head_dim
     x = qkv.float().view(N, 3, n_heads, D)
     rdim = D // 2
+    dt = qkv.dtype
+    if style == 1:
+        freq = 1.0 / (theta ** (torch.arange(0, rdim, dtype=torch.float32, device=qkv.device) / rdim))
+        a = rc[:, 0:1].float() * freq[None]  # [N, D/2]
+        b = rc[:, 1:2].float() * freq[None]
+        cos = torch.cat([torch.cos(a), torch.cos(b)], dim=-1)[:, None, :]
+        sin = torch.cat([torch.sin(a), torch.sin(b)], dim=-1)[:, None, :]
+
+        def rot(t):
+            t1, t2 = t[..., :rdim], t[..., rdim:]
+            return t * cos + torch.cat([-t2, t1], dim=-1) * sin
+
+        return rot(x[:, 0]).to(dt), rot(x[:, 1]).to(dt), x[:, 2].to(dt).contiguous()
     freq = 1.0 / (theta ** (torch.arange(0, rdim, 2, dtype=torch.float32, device=qkv.device) / rdim))
     ang = torch.cat([rc[:, 0:1].float() * freq[None], rc[:, 1:2].float() * freq[None]], dim=-1)  # [N, D/2]
     cos, sin = torch.cos(ang), torch.sin(ang)
-    dt = qkv.dtype
     return (_rotate(x[:, 0], cos, sin).to(dt), _rotate(x[:, 1], cos, sin).to(dt), x[:, 2].to(dt).contiguous())
 
 
