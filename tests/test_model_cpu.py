@@ -193,3 +193,42 @@ def test_qwen25_hf_parity_tiny():
                  position_ids=torch.from_numpy(pos)[:, None, :])
     logits = m.forward_vlm(tok, vis, grid)
     torch.testing.assert_close(logits, out.logits, atol=2e-5, rtol=1e-4)
+
+
+def test_compat_refeed_last_token_matches_duplicated_prompt():
+    """``compat_refeed_last_token``: the first token comes from decoding the last prompt token again."""
+    from vlmrl.core.sampling import Generator
+    from vlmrl.core.types import SamplingConfig
+
+    spec, units, m = tiny_model(seed=4)
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(1, 900, 7), rng.integers(1, 900, 11)]
+    gen = Generator(m)
+    for refeed in (False, True):
+        cfg = SamplingConfig(temperature=1.0, top_k=1, max_new_tokens=3, compat_refeed_last_token=refeed)
+        res = gen.generate(prompts, [[], []], None, cfg, seed=3)
+        for i, p in enumerate(prompts):
+            seq = list(p) + ([int(p[-1])] if refeed else [])
+            for t in range(3):
+                logits = m.forward_text(torch.tensor([seq]))[0, -1]
+                want = int(logits.argmax())
+                assert int(res.tokens[i, t]) == want, (refeed, i, t)
+                seq.append(want)
+
+
+def test_decay_frozen_matches_reference_drift():
+    """``AdamWConfig.decay_frozen``: the frozen vision tower shrinks by (1 - lr*wd) per step, in fp32."""
+    from vlmrl.core.optim import AdamWConfig, LocalOptimizer
+
+    spec, units, m = tiny_model(seed=2)
+    assert "visual" in m.params.units and "visual" not in m.params.trainable
+    v0 = m.params.units["visual"].clone()
+    lr, wd = 1e-3, 0.5
+    for decay in (False, True):
+        m.params.units["visual"].copy_(v0)
+        opt = LocalOptimizer(m.params, AdamWConfig(lr=lr, weight_decay=wd, decay_frozen=decay))
+        for step in range(1, 4):
+            opt.step(step)
+        want = v0 * (1 - lr * wd) ** 3 if decay else v0
+        torch.testing.assert_close(m.params.units["visual"], want, rtol=1e-6, atol=1e-7)
+        torch.testing.assert_close(opt.all_param_units()["visual"], want, rtol=1e-6, atol=1e-7)

@@ -208,6 +208,8 @@ def parse_args(argv=None):
     ap.add_argument("--max_new_tokens", type=int, default=30)
     ap.add_argument("--temperature", type=float, default=0.1)
     ap.add_argument("--top_p", type=float, default=0.9)
+    ap.add_argument("--compat_refeed_last_token", action="store_true",
+                    help="start decoding like the reference sampler: drop the prefill logits, decode the last prompt token again")
     ap.add_argument("--top_k", type=int, default=None)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--pad_id", type=int, default=None)
@@ -236,7 +238,8 @@ def main(argv=None) -> Dict[str, Any]:
     if args.pad_id is not None:
         pad_id = int(args.pad_id)
     cfg = SamplingConfig(temperature=args.temperature, top_p=args.top_p if 0 < args.top_p < 1 else None,
-                         top_k=args.top_k, eos_id=eos_id, pad_id=pad_id, max_new_tokens=args.max_new_tokens)
+                         top_k=args.top_k, eos_id=eos_id, pad_id=pad_id, max_new_tokens=args.max_new_tokens,
+                         compat_refeed_last_token=bool(args.compat_refeed_last_token))
     inputs = build_inputs(model, tokenizer, args.prompt, args.image, max(1, args.batch), pad_id)
     res, summary, first = benchmark_native(model, inputs, cfg, args.seed, tokenizer, args.benchmark_runs)
     print(format_summary_table("vlmrl sampler", summary, first))

@@ -30,6 +30,40 @@ class AdamWConfig:
     eps: float = 1e-8
     weight_decay: float = 1e-2
     max_grad_norm: float = 1.0
+    # the reference's optax chain decays every leaf, the gradient-free vision tower included (reference
+    # core/train.py:225-228); on: frozen units drift by (1 - lr * weight_decay) per step as there
+    decay_frozen: bool = False
+
+
+class FrozenDecay:
+    """Decoupled weight decay of gradient-free units: ``p <- p * (1 - lr * wd)`` every optimizer step.
+
+    AdamW with a zero gradient leaves both moments at zero, so its step on such a leaf is the decay term
+    alone.  The product is kept in an fp32 copy (per-step factors such as 1 - 1e-8 are below bf16
+    resolution) and written back to the compute copy after each step.
+    """
+
+    def __init__(self, units: Dict[str, torch.Tensor]):
+        self.units = units
+        self.master = {u: t.detach().float().clone() for u, t in units.items()}
+
+    def step(self, lr: float, weight_decay: float) -> None:
+        f = 1.0 - float(lr) * float(weight_decay)
+        for u, m in self.master.items():
+            m.mul_(f)
+            self.units[u].copy_(m)
+
+    def reseed(self, names=None) -> None:
+        """Take the compute copies as the new starting point (after a checkpoint load)."""
+        for u in (self.master if names is None else [n for n in names if n in self.master]):
+            self.master[u].copy_(self.units[u])
+
+
+def frozen_decay(units: Dict[str, torch.Tensor], trainable, cfg) -> Optional[FrozenDecay]:
+    if not getattr(cfg, "decay_frozen", False) or not getattr(cfg, "weight_decay", 0.0):
+        return None
+    frozen = {u: t for u, t in units.items() if u not in set(trainable)}
+    return FrozenDecay(frozen) if frozen else None
 
 
 class LocalOptimizer:
@@ -50,6 +84,7 @@ class LocalOptimizer:
             self.v[u] = torch.zeros_like(self.master[u])
             params.grad(u)
         self.count = 0
+        self.frozen = frozen_decay(params.units, params.trainable, cfg)
 
     def grad_sq_sum(self) -> torch.Tensor:
         dev = self.master[self.units[0]].device
@@ -72,6 +107,8 @@ class LocalOptimizer:
                        beta2=c.beta2, eps=c.eps, weight_decay=c.weight_decay, step=step, grad_scale=scale,
                        p_half=self.params.units[u])
             self.params.grads[u].zero_()
+        if self.frozen is not None:
+            self.frozen.step(c.lr, c.weight_decay)
         self.count = step
         return {"grad_norm": norm[0], "grad_sq_sum": sq[0]}
 
@@ -80,8 +117,10 @@ class LocalOptimizer:
         return dict(self.master)
 
     def all_param_units(self) -> Dict[str, torch.Tensor]:
-        """Every unit (frozen ones from the compute copy, trainable ones from the fp32 master)."""
+        """Every unit (frozen ones from the compute copy or their decay copy, trainable ones from the fp32 master)."""
         out = dict(self.params.units)
+        if self.frozen is not None:
+            out.update(self.frozen.master)
         out.update(self.master)
         return out
 
@@ -92,6 +131,10 @@ class LocalOptimizer:
         for name, buf in self.params.units.items():
             if name in units:
                 buf.copy_(units[name].to(buf.device, buf.dtype))
+        if self.frozen is not None:
+            for name in units:
+                if name in self.frozen.master:
+                    self.frozen.master[name].copy_(units[name].to(self.frozen.master[name].device, torch.float32))
         for u in self.units:
             self.master[u].copy_(units[u].to(self.master[u].device, torch.float32))
             if mu is not None:

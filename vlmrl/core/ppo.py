@@ -56,6 +56,8 @@ class TrainerConfig:
     kl_ref_coef: float = 0.0
     adv_norm: str = "group"
     old_logprob_source: str = "policy"
+    # rollouts start like the reference's sampler (last prompt token decoded twice); for parity runs only
+    compat_refeed_last_token: bool = False
     share_prompt: bool = True
     vlm_min_pixels: int = -1
     vlm_max_pixels: int = -1
@@ -83,7 +85,8 @@ class CollectResult:
 
 def sampling_config(cfg: TrainerConfig, eos_id: Optional[int], pad_id: int = 0) -> SamplingConfig:
     return SamplingConfig(temperature=cfg.temperature, top_p=cfg.top_p, top_k=cfg.top_k, eos_id=eos_id,
-                          pad_id=pad_id, max_new_tokens=cfg.max_new_tokens)
+                          pad_id=pad_id, max_new_tokens=cfg.max_new_tokens,
+                          compat_refeed_last_token=bool(getattr(cfg, "compat_refeed_last_token", False)))
 
 
 def _minibatch_count(cfg: TrainerConfig, n: int) -> int:

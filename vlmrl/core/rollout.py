@@ -274,6 +274,8 @@ def main(argv=None) -> List[float]:
     ap.add_argument("--top_p", type=float, default=0.9)
     ap.add_argument("--top_k", type=int, default=None)
     ap.add_argument("--max_new_tokens", type=int, default=64)
+    ap.add_argument("--compat_refeed_last_token", action="store_true",
+                    help="start decoding like the reference sampler (last prompt token decoded twice)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--min_pixels", type=int, default=-1)
     ap.add_argument("--max_pixels", type=int, default=-1)
@@ -287,7 +289,8 @@ def main(argv=None) -> List[float]:
     cfg = SamplingConfig(temperature=float(args.temperature),
                          top_p=float(args.top_p) if 0.0 < float(args.top_p) < 1.0 else None,
                          top_k=int(args.top_k) if args.top_k is not None and int(args.top_k) > 0 else None,
-                         eos_id=eos_id, pad_id=pad_id, max_new_tokens=int(args.max_new_tokens))
+                         eos_id=eos_id, pad_id=pad_id, max_new_tokens=int(args.max_new_tokens),
+                         compat_refeed_last_token=bool(args.compat_refeed_last_token))
     rng = RngSeq(int(args.seed))
     gen = Generator(model)
     remaining, taken, cursor = max(0, int(args.episodes)), 0, 0

@@ -121,7 +121,8 @@ class Generator:
             empty = torch.zeros(B, 0, dtype=torch.int64)
             return SampleResult(tokens=empty, logprobs=empty.float(), lengths=torch.zeros(B, dtype=torch.int64))
         plen = max(len(p) for p in prompts)
-        max_len = int(-(-(plen + max_new) // 64) * 64)
+        refeed = bool(getattr(cfg, "compat_refeed_last_token", False))
+        max_len = int(-(-(plen + max_new + int(refeed)) // 64) * 64)
         st = self._state(B, max_len, max_new)
         batch, deltas = pack_prompts(m.spec, prompts, grids_per_seq, vision, device=m.device)
         st.cache.lengths.zero_()
@@ -144,12 +145,17 @@ class Generator:
         # members' prompt KV rows are copies of their leader's: decode attention reads the leader's
         st.cache.lead.copy_(torch.arange(B, device=m.device, dtype=torch.int32) // gs * gs)
         st.cache.share_len.copy_(st.cache.lengths)
+        if refeed:
+            # reference start: discard the prefill logits, decode the last prompt token once more
+            last = torch.tensor([int(p[-1]) for p in prompts], dtype=torch.int64).repeat_interleave(gs)
+            st.tok.copy_(last.to(st.tok.device))
+            logits = m.decode_step(st.tok, st.cache, st.deltas)
         nt, lp = ops.sample(logits, temperature=cfg.temperature, top_k=cfg.top_k or 0, top_p=cfg.top_p or 0.0,
                             seed=st.seed, step=st.step, row_offset=row_offset)
         self._record(st, nt, lp, cfg.eos_id)
         if self.tp is not None:
             self.tp.refresh(getattr(m.params, "version", None))
-            self.tp.load_cache(st.cache, st.tp_cache, plen)
+            self.tp.load_cache(st.cache, st.tp_cache, plen + int(refeed))
         steps = max_new - 1
         if steps > 0:
             if self.use_cuda_graph:

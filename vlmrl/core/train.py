@@ -13,6 +13,10 @@ same names and defaults, plus the flags of this framework's extensions:
 * ``adv_norm`` — ``auto`` (batch normalisation as in the reference when
   ``group_size == 1``, per-group otherwise), ``batch``, ``group`` or ``none``;
 * ``old_logprob_source`` — ``sampler`` (reference) or ``policy``;
+* ``compat_refeed_last_token`` — rollouts start as the reference's sampler does (the last prompt
+  token decoded a second time, prefill logits dropped); for parity runs;
+* ``compat_decay_frozen`` — AdamW weight decay also shrinks the frozen vision tower every step, as the
+  reference's optimizer does; for parity runs;
 * ``preset`` — random-init architecture (``tiny``, ``qwen3vl_4b``, ...) when
   ``model_dir`` holds no weights;
 * ``fsdp`` — shard optimizer state and gradients over the process group;
@@ -95,6 +99,8 @@ CONFIG: Dict[str, Any] = {
     "kl_ref_coef": 0.0,
     "adv_norm": "auto",
     "old_logprob_source": "sampler",
+    "compat_refeed_last_token": 0,
+    "compat_decay_frozen": 0,
     "preset": "",
     "fsdp": 1,
     "fsdp_shard_params": 0,
@@ -231,13 +237,14 @@ def make_configs(args):
         kl_coef_max=float(args.kl_coef_max), ppo_minibatch=int(args.ppo_minibatch), ppo_epochs=int(args.ppo_epochs),
         n_minibatches=int(args.n_minibatches), groups_per_batch=groups, group_size=gs,
         kl_ref_coef=float(args.kl_ref_coef), adv_norm=adv, old_logprob_source=str(args.old_logprob_source),
+        compat_refeed_last_token=bool(int(args.compat_refeed_last_token)),
         vlm_min_pixels=int(args.vlm_min_pixels), vlm_max_pixels=int(args.vlm_max_pixels))
     if str(args.optimizer).lower() == "adafactor":
         opt = AdafactorConfig(lr=float(args.learning_rate), weight_decay=float(args.weight_decay),
                               max_grad_norm=float(args.max_grad_norm))
     else:
         opt = AdamWConfig(lr=float(args.learning_rate), weight_decay=float(args.weight_decay),
-                          max_grad_norm=float(args.max_grad_norm))
+                          max_grad_norm=float(args.max_grad_norm), decay_frozen=bool(int(args.compat_decay_frozen)))
     return cfg, opt
 
 

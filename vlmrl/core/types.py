@@ -28,6 +28,9 @@ class SamplingConfig:
     eos_id: Optional[int] = None
     pad_id: int = 0
     max_new_tokens: int = 64
+    # the reference's decode start (reference core/sampling.py:248-288): the prefill logits are dropped and the
+    # first decode step re-feeds each prompt's last token at position len(prompt), so the cache holds it twice
+    compat_refeed_last_token: bool = False
 
 
 @dataclass

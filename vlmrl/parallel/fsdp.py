@@ -48,7 +48,7 @@ import torch.distributed as dist
 
 from vlmrl import ops
 from vlmrl.ops._ext import ext
-from vlmrl.core.optim import AdamWConfig, _unit_order
+from vlmrl.core.optim import AdamWConfig, _unit_order, frozen_decay
 from vlmrl.models.qwen3vl.params import UnitLayout
 from vlmrl.parallel.dist import all_gather_into, all_reduce_, reduce_scatter_into
 
@@ -385,9 +385,13 @@ class FSDPOptimizer:
         self.master = {u: params.shards[u].float().clone() for u in self.units}
         self.m = {u: torch.zeros_like(self.master[u]) for u in self.units}
         self.v = {u: torch.zeros_like(self.master[u]) for u in self.units}
+        # replicated frozen units decay identically on every rank (no communication)
+        self.frozen = frozen_decay(params.replicated, params.trainable, cfg)
 
     def step(self, step: int) -> Dict[str, torch.Tensor]:
         p, c = self.params, self.cfg
+        if self.frozen is not None:
+            self.frozen.step(c.lr, c.weight_decay)
         p.sync_grads()
         sq = torch.zeros(1, dtype=torch.float32, device=p.device)
         for u in self.units:
@@ -448,6 +452,8 @@ class FSDPOptimizer:
 
     def all_param_units(self) -> Dict[str, torch.Tensor]:
         out = dict(self.params.replicated)
+        if self.frozen is not None:
+            out.update(self.frozen.master)
         out.update(self.master_units())
         return out
 
@@ -459,6 +465,8 @@ class FSDPOptimizer:
         for name, buf in p.replicated.items():
             if name in units:
                 buf.copy_(units[name].to(buf.device, buf.dtype))
+                if self.frozen is not None and name in self.frozen.master:
+                    self.frozen.master[name].copy_(units[name].to(buf.device, torch.float32))
         for u in self.units:
             n = p.padded[u] // p.world
             sl = slice(p.rank * n, (p.rank + 1) * n)
