@@ -181,6 +181,13 @@ def bench_norm(t: Timer):
     x, w = _r(M, H), _r(H)
     ms = t(lambda: ops.rms_norm(x, w, 1e-6))
     emit("rms_norm_12448x2560", ms, bytes_=2 * 2 * M * H)
+    # backward of one decoder norm of a GRPO minibatch (5112 packed tokens): dx (+ residual gradient), dw
+    Mb = 5112
+    xb, dyb, addb, wb = _r(Mb, H), _r(Mb, H), _r(Mb, H), _r(H)
+    _, rstd = ops.rms_norm(xb, wb, 1e-6)
+    dw = torch.zeros(H, device="cuda")
+    ms = t(lambda: ops.rms_norm_bwd(dyb, xb, wb, rstd, dw_accum=dw, add=addb))
+    emit("rms_norm_bwd_5112x2560", ms, bytes_=2 * 4 * Mb * H)
     n = 100_000_000
     p, g, m, v = (torch.zeros(n, device="cuda") for _ in range(4))
     ph = torch.empty(n, device="cuda", dtype=torch.bfloat16)
