@@ -298,6 +298,113 @@ __global__ void qk_norm_rope_fwd_kernel(const bf16* __restrict__ qkv, const bf16
   }
 }
 
+// The same forward for D = 64 and 128.  A warp takes HPW = 4 consecutive heads of one token; each lane holds
+// PER = D/64 adjacent rotation pairs of every one of them.  All heads' elements are requested before any is
+// used (bf16x2 words when PER = 2), and the angles, which depend on the token and the pair only, are
+// computed once per warp for its four heads (the scalar kernel above reads 2-byte elements twice and
+// evaluates sincos per head).
+template <int D>
+__global__ void __launch_bounds__(256) qk_norm_rope_fwd_vec_kernel(
+    const bf16* __restrict__ qkv, const bf16* __restrict__ qw, const bf16* __restrict__ kw,
+    const int* __restrict__ pos, int64_t pos_stride, const float* __restrict__ inv_freq, const int* __restrict__ ax,
+    bf16* __restrict__ q, bf16* __restrict__ k, bf16* __restrict__ v, float* __restrict__ rq, float* __restrict__ rk,
+    int T, int nq, int nkv, float eps) {
+  constexpr int HALF = D / 2, PER = HALF / 32, HPW = 4;
+  static_assert(PER == 1 || PER == 2, "D = 64 or 128");
+  const int nh = nq + 2 * nkv;
+  const int groups = (nh + HPW - 1) / HPW;
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (gw >= static_cast<int64_t>(T) * groups) return;
+  const int t = static_cast<int>(gw / groups), h0 = static_cast<int>(gw % groups) * HPW;
+  const int j0 = lane * PER;
+  const bf16* row = qkv + static_cast<int64_t>(t) * nh * D;
+  float x1[HPW][PER], x2[HPW][PER];
+#pragma unroll
+  for (int e = 0; e < HPW; ++e) {
+    const int h = min(h0 + e, nh - 1);  // a ragged last group re-reads its last head and skips it below
+    const bf16* src = row + static_cast<int64_t>(h) * D;
+    if constexpr (PER == 2) {
+      const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(src + j0));
+      const float2 b = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(src + HALF + j0));
+      x1[e][0] = a.x;
+      x1[e][1] = a.y;
+      x2[e][0] = b.x;
+      x2[e][1] = b.y;
+    } else {
+      x1[e][0] = bf2f(src[j0]);
+      x2[e][0] = bf2f(src[HALF + j0]);
+    }
+  }
+  float sn[PER], cs[PER];
+  bool angles = false;
+  const bool norm = qw != nullptr;  // Qwen2.5-style attention has no q/k RMSNorm: rotate only
+#pragma unroll
+  for (int e = 0; e < HPW; ++e) {
+    const int h = h0 + e;
+    if (h >= nh) break;
+    if (h >= nq + nkv) {  // v: a plain copy
+      bf16* dst = v + (static_cast<int64_t>(t) * nkv + (h - nq - nkv)) * D;
+      if constexpr (PER == 2) {
+        *reinterpret_cast<uint32_t*>(dst + j0) = pack_bf16x2(x1[e][0], x1[e][1]);
+        *reinterpret_cast<uint32_t*>(dst + HALF + j0) = pack_bf16x2(x2[e][0], x2[e][1]);
+      } else {
+        dst[j0] = f2bf(x1[e][0]);
+        dst[HALF + j0] = f2bf(x2[e][0]);
+      }
+      continue;
+    }
+    if (!angles) {
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int j = j0 + i;
+        sincosf(static_cast<float>(pos[ax[j] * pos_stride + t]) * inv_freq[j], &sn[i], &cs[i]);
+      }
+      angles = true;
+    }
+    const bool is_q = h < nq;
+    float r = 1.f;
+    float a1[PER], a2[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      a1[i] = x1[e][i];
+      a2[i] = x2[e][i];
+    }
+    if (norm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) ss += a1[i] * a1[i] + a2[i] * a2[i];
+      r = rsqrtf(warp_sum(ss) / D + eps);
+      const bf16* wt = is_q ? qw : kw;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        a1[i] *= r * bf2f(wt[j0 + i]);
+        a2[i] *= r * bf2f(wt[HALF + j0 + i]);
+      }
+    }
+    bf16* dst = is_q ? q + (static_cast<int64_t>(t) * nq + h) * D : k + (static_cast<int64_t>(t) * nkv + (h - nq)) * D;
+    if (lane == 0) {
+      if (is_q)
+        rq[static_cast<int64_t>(t) * nq + h] = r;
+      else
+        rk[static_cast<int64_t>(t) * nkv + (h - nq)] = r;
+    }
+    float o1[PER], o2[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      o1[i] = a1[i] * cs[i] - a2[i] * sn[i];
+      o2[i] = a2[i] * cs[i] + a1[i] * sn[i];
+    }
+    if constexpr (PER == 2) {
+      *reinterpret_cast<uint32_t*>(dst + j0) = pack_bf16x2(o1[0], o1[1]);
+      *reinterpret_cast<uint32_t*>(dst + HALF + j0) = pack_bf16x2(o2[0], o2[1]);
+    } else {
+      dst[j0] = f2bf(o1[0]);
+      dst[HALF + j0] = f2bf(o2[0]);
+    }
+  }
+}
+
 // Backward: un-rotate the incoming gradient, then the per-head RMSNorm backward.
 // One warp per (token, head) item, grid-stride over items.  Lane l owns elements l + 32 i of a head, so
 // the norm-weight gradient (sum over tokens and heads of g * xhat) accumulates in registers across the
@@ -414,6 +521,21 @@ void qk_norm_rope_fwd(at::Tensor qkv, at::Tensor qw, at::Tensor kw, at::Tensor p
               "qk_norm_rope: layout");
   const c10::cuda::CUDAGuard g(qkv.device());
   const int64_t warps = static_cast<int64_t>(T) * (nq + 2 * nkv);
+  static const bool vec = [] {  // VLMRL_QK_ROPE_VEC=0 keeps the scalar kernel (for A/B timing)
+    const char* e = std::getenv("VLMRL_QK_ROPE_VEC");
+    return !(e && e[0] == '0');
+  }();
+  if (vec && (D == 64 || D == 128)) {
+    auto kern = D == 128 ? qk_norm_rope_fwd_vec_kernel<128> : qk_norm_rope_fwd_vec_kernel<64>;
+    const int64_t vwarps = static_cast<int64_t>(T) * ((nq + 2 * nkv + 3) / 4);
+    kern<<<static_cast<int>((vwarps * 32 + 255) / 256), 256, 0, cur_stream()>>>(
+        reinterpret_cast<const bf16*>(qkv.data_ptr()), opt_bf16(qw), opt_bf16(kw), pos.data_ptr<int>(), pos.stride(0),
+        inv_freq.data_ptr<float>(), ax.data_ptr<int>(), reinterpret_cast<bf16*>(q.data_ptr()),
+        reinterpret_cast<bf16*>(k.data_ptr()), reinterpret_cast<bf16*>(v.data_ptr()), rq.data_ptr<float>(),
+        rk.data_ptr<float>(), T, static_cast<int>(nq), static_cast<int>(nkv), static_cast<float>(eps));
+    VLM_LAUNCHED();
+    return;
+  }
   qk_norm_rope_fwd_kernel<<<static_cast<int>((warps * 32 + 255) / 256), 256, 0, cur_stream()>>>(
       reinterpret_cast<const bf16*>(qkv.data_ptr()), opt_bf16(qw), opt_bf16(kw), pos.data_ptr<int>(), pos.stride(0),
       inv_freq.data_ptr<float>(), ax.data_ptr<int>(), reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(k.data_ptr()),

@@ -114,13 +114,13 @@ def test_norms():
     _close(ops.layer_norm(x2, w2, b, 1e-6), ref.layer_norm(x2, w2, b, 1e-6), name="layernorm")
 
 
-@pytest.mark.parametrize("D,nq,nkv", [(128, 32, 8), (32, 4, 2)])
+@pytest.mark.parametrize("D,nq,nkv", [(128, 32, 8), (128, 5, 1), (64, 8, 4), (32, 4, 2)])
 def test_qk_norm_rope(D, nq, nkv):
     T = 97
     qkv = _r(T, (nq + 2 * nkv) * D, seed=18)
     qw, kw = (1 + 0.1 * _r(D, seed=19).float()).bfloat16(), (1 + 0.1 * _r(D, seed=20).float()).bfloat16()
     pos = torch.randint(0, 500, (3, T), device=DEV, dtype=torch.int32)
-    rope = ops.RopeCfg(D, 5e6, (24, 20, 20) if D == 128 else (6, 5, 5), True)
+    rope = ops.RopeCfg(D, 5e6, {128: (24, 20, 20), 64: (12, 10, 10)}.get(D, (6, 5, 5)), True)
     q, k, v, rq, rk = ops.qk_norm_rope(qkv, qw, kw, pos, rope, n_q=nq, n_kv=nkv, eps=1e-6)
     qr, kr, vr, rqr, rkr = ref.qk_norm_rope(qkv, qw, kw, pos, n_q=nq, n_kv=nkv, head_dim=D, theta=5e6,
                                             section=rope.section, interleaved=True, eps=1e-6)

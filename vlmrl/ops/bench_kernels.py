@@ -188,6 +188,13 @@ def bench_norm(t: Timer):
     dw = torch.zeros(H, device="cuda")
     ms = t(lambda: ops.rms_norm_bwd(dyb, xb, wb, rstd, dw_accum=dw, add=addb))
     emit("rms_norm_bwd_5112x2560", ms, bytes_=2 * 4 * Mb * H)
+    # q/k RMSNorm + MRoPE + v split of one layer of that minibatch (32 q / 8 kv heads of 128)
+    qkv = _r(Mb, 48 * 128)
+    qw, kw = _r(128), _r(128)
+    pos = torch.randint(0, 400, (3, Mb), device="cuda", dtype=torch.int32)
+    rope = ops.RopeCfg(128, 5e6, (24, 20, 20), True)
+    ms = t(lambda: ops.qk_norm_rope(qkv, qw, kw, pos, rope, n_q=32, n_kv=8, eps=1e-6))
+    emit("qk_norm_rope_5112x48x128", ms, bytes_=2 * 2 * Mb * 48 * 128)
     n = 100_000_000
     p, g, m, v = (torch.zeros(n, device="cuda") for _ in range(4))
     ph = torch.empty(n, device="cuda", dtype=torch.bfloat16)
