@@ -195,6 +195,13 @@ def bench_norm(t: Timer):
     rope = ops.RopeCfg(128, 5e6, (24, 20, 20), True)
     ms = t(lambda: ops.qk_norm_rope(qkv, qw, kw, pos, rope, n_q=32, n_kv=8, eps=1e-6))
     emit("qk_norm_rope_5112x48x128", ms, bytes_=2 * 2 * Mb * 48 * 128)
+    q, k, v, rq, rk = ops.qk_norm_rope(qkv, qw, kw, pos, rope, n_q=32, n_kv=8, eps=1e-6)
+    dq, dk, dv = torch.randn_like(q), torch.randn_like(k), torch.randn_like(v)
+    dqw, dkw = torch.zeros(128, device="cuda"), torch.zeros(128, device="cuda")
+    ms = t(lambda: ops.qk_norm_rope_bwd(dq, dk, dv, qkv, qw, kw, pos, rq, rk, rope, n_q=32, n_kv=8, eps=1e-6,
+                                        dqw_accum=dqw, dkw_accum=dkw))
+    # reads the gradients and the layer input, writes the input gradient
+    emit("qk_norm_rope_bwd_5112x48x128", ms, bytes_=2 * 3 * Mb * 48 * 128)
     n = 100_000_000
     p, g, m, v = (torch.zeros(n, device="cuda") for _ in range(4))
     ph = torch.empty(n, device="cuda", dtype=torch.bfloat16)
