@@ -16,6 +16,7 @@
 // tiles and both products run on mma.sync; other head sizes use 1-D bulk copies
 // and warp-shuffle dot products.  A combine kernel merges key splits.
 #include <ATen/cuda/CUDAContext.h>
+#include <atomic>
 #include <cstdlib>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -23,6 +24,7 @@
 #include "common.cuh"
 #include "host_utils.h"
 #include "mma_sync.cuh"
+#include "vlm_noalloc.h"
 
 namespace vlm {
 
@@ -1205,32 +1207,65 @@ void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at
 // fail under its memory cap), code running where allocation would be an unsynchronised driver call in
 // a latency-critical loop, or plugin code that may only touch buffers it was handed.  Such callers
 // pass inputs and outputs only; the key-split partial results, which the regular decode_attn path
-// keeps in a temporary buffer from the PyTorch allocator, live here in a fixed device array instead.
+// keeps in a temporary buffer from the PyTorch allocator, live here in a fixed device array instead,
+// and the kernels report a timed-out wait in a second fixed device word rather than in the lazily
+// allocated error word of the regular path.  The C declarations are in vlm_noalloc.h.
 //
 // Contract:
 //  * Scratch: the file-scope array below, kNoAllocScratchFloats floats (4 MiB) per GPU.  Every GPU
 //    that loads this library holds it until the process exits.  A problem needing more than
 //    B * Hq * splits * (D + 2) <= kNoAllocScratchFloats floats is rejected (return value -2).
-//  * Set-up: the first call on a device (with that device current) resolves the array's device
-//    address with cudaGetSymbolAddress; make that first call before any CUDA-graph capture.
+//  * Set-up: the first call on a device (with that device current) resolves the device addresses of
+//    the array and of the status word with cudaGetSymbolAddress; make that first call before any
+//    CUDA-graph capture.  Two host threads making their first call at once both resolve the same
+//    addresses, so the unsynchronised store of the cached pointer is harmless.
 //  * Sharing: all calls on a device share the one array and it keeps the last call's contents.
-//    Every partial slot a call reads is written earlier by the same call, so nothing needs clearing,
-//    but calls that overlap on the GPU (different streams, or graphs replayed concurrently) race
-//    on the array and must be serialised by the caller.
-//  * No cudaMalloc, cudaFree or allocating library routine is called.
+//    Every partial slot a call reads is written earlier by the same call, unless one of that call's
+//    bounded waits ran out, so nothing needs clearing; calls that overlap on the GPU (different
+//    streams, or graphs replayed concurrently) race on the array and must be serialised by the caller.
+//  * Timeouts: a wait that runs out stops its CTA early and records a non-zero code in the status
+//    word; that call's output is then undefined (the merge may read an earlier call's partials).
+//    vlmrl_decode_attention_noalloc_status reads and clears the word.
+//  * No cudaMalloc, cudaFree or allocating library routine is called, and no C++ exception leaves
+//    either function: every failure is a return code.
 //  * Return value: 0 ok, -1 unsupported shape, -2 problem exceeds the scratch array, -3 CUDA error.
 // =====================================================================================================
 namespace vlm {
 
 constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 20;  // 4 MiB of fp32 partials
 static __device__ __align__(256) float g_noalloc_decode_scratch[kNoAllocScratchFloats];
+static __device__ __align__(16) int g_noalloc_status[4];
 
 namespace {
-float* g_noalloc_ptr[64] = {nullptr};
+constexpr int kNoAllocMaxDevices = 64;
+struct NoAllocSlots {
+  float* scratch;
+  int* status;
+};
+std::atomic<float*> g_noalloc_scratch_ptr[kNoAllocMaxDevices];
+std::atomic<int*> g_noalloc_status_ptr[kNoAllocMaxDevices];
+
+// Device addresses of the scratch array and the status word for the current device, resolved once.
+int noalloc_slots(NoAllocSlots& s) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return -3;
+  s.scratch = g_noalloc_scratch_ptr[dev].load(std::memory_order_acquire);
+  s.status = g_noalloc_status_ptr[dev].load(std::memory_order_acquire);
+  if (s.scratch && s.status) return 0;
+  void* p = nullptr;
+  void* w = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_decode_scratch) != cudaSuccess || p == nullptr) return -3;
+  if (cudaGetSymbolAddress(&w, g_noalloc_status) != cudaSuccess || w == nullptr) return -3;
+  s.scratch = static_cast<float*>(p);
+  s.status = static_cast<int*>(w);
+  g_noalloc_status_ptr[dev].store(s.status, std::memory_order_release);
+  g_noalloc_scratch_ptr[dev].store(s.scratch, std::memory_order_release);
+  return 0;
+}
 
 template <int D, int REP>
 int noalloc_decode_launch(const bf16* q, const bf16* kc, const bf16* vc, const int* lens, bf16* o, int B, int Hq,
-                          int Hkv, int Tmax, float scale, float* scratch, int sms, cudaStream_t st) {
+                          int Hkv, int Tmax, float scale, const NoAllocSlots& s, int sms, cudaStream_t st) {
   constexpr int NW = 8, KC = 32, STAGES = 4;
   // at least two key splits, so the partial results always go through the scratch array
   const int splits =
@@ -1239,14 +1274,36 @@ int noalloc_decode_launch(const bf16* q, const bf16* kc, const bf16* vc, const i
   const int smem = 2 * STAGES * KC * D * 2 + STAGES * 8 + (2 * NW * REP + NW * REP * D) * 4;
   auto kern = decode_attn_kernel<D, REP, NW, KC, STAGES>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -3;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return -3;
-  kern<<<dim3(Hkv, B, splits), NW * 32, smem, st>>>(q, kc, vc, lens, o, scratch, Hq, Hkv, Tmax, scale * kLog2e,
-                                                     splits, err_word(dev));
+  kern<<<dim3(Hkv, B, splits), NW * 32, smem, st>>>(q, kc, vc, lens, o, s.scratch, Hq, Hkv, Tmax, scale * kLog2e,
+                                                     splits, s.status);
   if (cudaGetLastError() != cudaSuccess) return -3;
-  decode_combine_kernel<<<B * Hq, 128, 0, st>>>(scratch, o, B * Hq, splits, D);
+  decode_combine_kernel<<<B * Hq, 128, 0, st>>>(s.scratch, o, B * Hq, splits, D);
   if (cudaGetLastError() != cudaSuccess) return -3;
   return 0;
+}
+
+int noalloc_decode(const void* q, const void* k_cache, const void* v_cache, const int* lengths, void* out, int B,
+                   int Hq, int Hkv, int Tmax, int D, float scale, void* stream) {
+  if (B <= 0 || Hkv <= 0 || Hq <= 0 || Hq % Hkv != 0 || Tmax <= 0) return -1;
+  const int rep = Hq / Hkv;
+  const bool shape_ok = (D == 128 && (rep == 4 || rep == 2 || rep == 1)) || (D == 64 && rep == 4) ||
+                        (D == 32 && rep == 2);
+  if (!shape_ok) return -1;
+  NoAllocSlots s{};
+  if (const int rc = noalloc_slots(s)) return rc;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -3;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -3;
+  const auto* qq = static_cast<const bf16*>(q);
+  const auto* kk = static_cast<const bf16*>(k_cache);
+  const auto* vv = static_cast<const bf16*>(v_cache);
+  auto* oo = static_cast<bf16*>(out);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 128 && rep == 4) return noalloc_decode_launch<128, 4>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, s, sms, st);
+  if (D == 128 && rep == 2) return noalloc_decode_launch<128, 2>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, s, sms, st);
+  if (D == 128 && rep == 1) return noalloc_decode_launch<128, 1>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, s, sms, st);
+  if (D == 64 && rep == 4) return noalloc_decode_launch<64, 4>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, s, sms, st);
+  return noalloc_decode_launch<32, 2>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, s, sms, st);
 }
 }  // namespace
 
@@ -1259,28 +1316,28 @@ int noalloc_decode_launch(const bf16* q, const bf16* kc, const bf16* vc, const i
 extern "C" int vlmrl_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                               const int* lengths, void* out, int B, int Hq, int Hkv, int Tmax, int D,
                                               float scale, void* stream) {
-  using namespace vlm;
-  if (B <= 0 || Hkv <= 0 || Hq % Hkv != 0 || Tmax <= 0) return -1;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_decode_scratch) != cudaSuccess || p == nullptr) return -3;
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  try {
+    return vlm::noalloc_decode(q, k_cache, v_cache, lengths, out, B, Hq, Hkv, Tmax, D, scale, stream);
+  } catch (...) {
+    return -3;
   }
-  int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -3;
-  const auto* qq = static_cast<const bf16*>(q);
-  const auto* kk = static_cast<const bf16*>(k_cache);
-  const auto* vv = static_cast<const bf16*>(v_cache);
-  auto* oo = static_cast<bf16*>(out);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int rep = Hq / Hkv;
-  float* scratch = g_noalloc_ptr[dev];
-  if (D == 128 && rep == 4) return noalloc_decode_launch<128, 4>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, scratch, sms, st);
-  if (D == 128 && rep == 2) return noalloc_decode_launch<128, 2>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, scratch, sms, st);
-  if (D == 128 && rep == 1) return noalloc_decode_launch<128, 1>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, scratch, sms, st);
-  if (D == 64 && rep == 4) return noalloc_decode_launch<64, 4>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, scratch, sms, st);
-  if (D == 32 && rep == 2) return noalloc_decode_launch<32, 2>(qq, kk, vv, lengths, oo, B, Hq, Hkv, Tmax, scale, scratch, sms, st);
-  return -1;
+}
+
+// Waits for `stream`, then stores the status word of the current device in *status (0 = no wait ran
+// out since the last read; otherwise the first error code recorded) and clears it.  Returns 0, or -3
+// on a CUDA error.
+extern "C" int vlmrl_decode_attention_noalloc_status(void* stream, int* status) {
+  try {
+    vlm::NoAllocSlots s{};
+    if (const int rc = vlm::noalloc_slots(s)) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int h = 0;
+    if (cudaMemcpyAsync(&h, s.status, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return -3;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return -3;
+    if (h != 0 && cudaMemsetAsync(s.status, 0, sizeof(int), st) != cudaSuccess) return -3;
+    if (status) *status = h;
+    return 0;
+  } catch (...) {
+    return -3;
+  }
 }
