@@ -1,6 +1,7 @@
 // Python bindings of the vlmrl sm_100a kernels (module vlmrl._C).
 #include <torch/extension.h>
 
+#include "host_utils.h"
 #include "vlm_ops.h"
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -60,6 +61,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_wait", &vlm::peer_wait, py::arg("local_sig"), py::arg("slot"), py::arg("target"), py::arg("rank"),
         py::arg("world"), py::arg("device"), py::arg("budget_cycles") = 0);
   m.def("peer_barrier", &vlm::peer_barrier);
+  m.def("decode_step_maps", &vlm::decode_step_maps, "tensor maps (CPU bytes) of the persistent decode step");
+  m.def("decode_step_sync_words", &vlm::decode_step_sync_words);
+  m.def("decode_step_ws_floats", &vlm::decode_step_ws_floats);
+  m.def("decode_step", &vlm::decode_step, "all decoder layers of one decode step in one persistent launch",
+        py::arg("wmaps"), py::arg("amaps"), py::arg("layers"), py::arg("x"), py::arg("h1"), py::arg("xn"), py::arg("o"),
+        py::arg("hn"), py::arg("act"), py::arg("ws"), py::arg("ssq"), py::arg("sync"), py::arg("lens"), py::arg("delta"),
+        py::arg("inv_freq"), py::arg("lead") = py::none(), py::arg("share_len") = py::none(), py::arg("dims"),
+        py::arg("eps"), py::arg("scale"), py::arg("trace") = py::none());
   m.def("read_and_clear_error", &vlm::read_and_clear_error);
+  m.def("read_error_words", &vlm::read_error_words, "error code and detail words of a device, then cleared");
   m.def("launch_count", &vlm::launch_count, "kernel launches issued by this library so far");
 }

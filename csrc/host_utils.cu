@@ -70,6 +70,16 @@ int64_t read_and_clear_error(int64_t device) {
   return h;
 }
 
+std::vector<int64_t> read_error_words(int64_t device) {
+  int* w = err_word(static_cast<int>(device));
+  int h[4] = {0, 0, 0, 0};
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  VLM_CUDA_CHECK(cudaMemcpyAsync(h, w, sizeof(h), cudaMemcpyDeviceToHost, st));
+  VLM_CUDA_CHECK(cudaStreamSynchronize(st));
+  if (h[0] || h[1] || h[2] || h[3]) VLM_CUDA_CHECK(cudaMemsetAsync(w, 0, sizeof(h), st));
+  return {h[0], h[1], h[2], h[3]};
+}
+
 int num_sms(int device) {
   if (!g_sms[device]) {
     int v = 0;

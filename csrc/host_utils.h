@@ -1,6 +1,8 @@
 // Host-side helpers shared by the kernel launchers.
 #pragma once
 
+#include <vector>
+
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <torch/extension.h>
@@ -91,6 +93,9 @@ int* err_word(int device);
 unsigned* grid_barrier_words(int device);
 // Reads and clears the error word of ``device`` (synchronises the current stream).
 int64_t read_and_clear_error(int64_t device);
+// All four error words (code, then kernel-specific detail such as the CTA and the wait that gave up),
+// cleared afterwards (synchronises the current stream).
+std::vector<int64_t> read_error_words(int64_t device);
 int num_sms(int device);
 // Row-major 2-D bf16 tensor map with 128-byte swizzle. inner/outer in elements, ld in elements.
 CUtensorMap make_tmap_2d_bf16(const void* base, int64_t inner, int64_t outer, int64_t ld, int box_inner, int box_outer);

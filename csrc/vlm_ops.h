@@ -141,6 +141,17 @@ void peer_wait(int64_t local_sig, int64_t slot, int64_t target, int64_t rank, in
                int64_t budget_cycles);
 void peer_barrier(std::vector<int64_t> sigs, int64_t slot, int64_t epoch, int64_t rank, int64_t device);
 
+// decode_step.cu (persistent decode step)
+std::vector<at::Tensor> decode_step_maps(std::vector<at::Tensor> weights, std::vector<at::Tensor> caches,
+                                         std::vector<at::Tensor> acts, int64_t BP);
+int64_t decode_step_sync_words(int64_t L, int64_t F, int64_t B);
+int64_t decode_step_ws_floats(std::vector<int64_t> dims, int64_t grid);
+void decode_step(at::Tensor wmaps, at::Tensor amaps, at::Tensor layers, at::Tensor x, at::Tensor h1, at::Tensor xn,
+                 at::Tensor o, at::Tensor hn, at::Tensor act, at::Tensor ws, at::Tensor ssq, at::Tensor sync,
+                 at::Tensor lens, at::Tensor delta, at::Tensor inv_freq, c10::optional<at::Tensor> lead,
+                 c10::optional<at::Tensor> share_len, std::vector<int64_t> dims, double eps, double scale,
+                 c10::optional<at::Tensor> trace);
+
 // host_utils.cu
 int64_t read_and_clear_error(int64_t device);
 int64_t launch_count();

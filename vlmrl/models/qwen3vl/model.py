@@ -32,6 +32,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import torch
 
 from vlmrl import ops
+from vlmrl.ops import decode_step
 from vlmrl.models.qwen3vl.config import Qwen3VLSpec
 from vlmrl.models.qwen3vl.params import UnitLayout, all_layouts, text_layouts, vision_layout
 
@@ -372,9 +373,15 @@ class TextDecoder:
         already normalised by ``final_norm``; on the CPU ``h`` is the raw residual stream.
         """
         e = self._w(params, "embed")["embed"]
+        B = tokens.shape[0]
+        if tokens.is_cuda and self._persistent_ok(params, B):
+            plan = decode_step.plan_for(self, params, cache, B)
+            ops.embed(tokens, e, out=plan.x)
+            params.release("embed")
+            plan.xn.copy_(ops.rms_norm(plan.x, self._w(params, "layer0")["input_norm"], self.eps)[0])
+            return plan.run(cache.lengths, rope_delta.to(torch.int64), cache.lead, cache.share_len), True
         x = ops.embed(tokens, e)
         params.release("embed")
-        B = tokens.shape[0]
         if tokens.is_cuda:
             return self._decode_fused(params, x, cache, rope_delta), True
         p1 = (cache.lengths.to(torch.int64) + rope_delta.to(torch.int64)).to(torch.int32)
@@ -396,6 +403,16 @@ class TextDecoder:
             x = ops.linear(act, w["down_w"], residual=h1, out_dtype=x.dtype)
             params.release(f"layer{i}")
         return x, False
+
+    def _persistent_ok(self, params, B: int) -> bool:
+        """The persistent decode step applies: enabled, supported shape, resident bf16 weights, and none of
+        the per-kernel path's experiment switches set."""
+        if not decode_step.ENABLED or _DECODE_L2_PREFETCH or _DECODE_FUSED_CONSUMERS:
+            return False
+        if not decode_step.supported(self.spec.text, B):
+            return False
+        w = self._w(params, "layer0")["qkv_w"]
+        return torch.is_tensor(w) and w.dtype == torch.bfloat16
 
     def _decode_fused(self, params, x: torch.Tensor, cache: KVCache, rope_delta: torch.Tensor) -> torch.Tensor:
         B = x.shape[0]
