@@ -42,6 +42,10 @@ WORKLOADS = {
                  max_new=16, minibatches=1),
     "truefalse_4b": dict(preset="qwen3vl_4b", env="synthetic_truefalse", groups=32, group_size=8, image=384,
                          prompt_tokens=48, max_new=8, minibatches=2),
+    # rollout only (inference): batch 64, one 448x448 image + 64 prompt tokens, 128 new tokens; the value is
+    # generated tokens per second of the whole rollout (vision + prefill + decode), DP over ranks by default
+    "rollout_4b": dict(preset="qwen3vl_4b", env="synthetic_geo", groups=8, group_size=8, image=448, prompt_tokens=64,
+                       max_new=128, minibatches=1, mode="rollout"),
     # 8B: FSDP over all ranks for the update, rollout tensor parallel over pairs of GPUs (TP-2 x DP-N/2)
     "grpo_8b": dict(preset="qwen3vl_8b", env="synthetic_geo", groups=16, group_size=8, image=672, prompt_tokens=128,
                     max_new=512, minibatches=2, rollout="tp", tp_size=2),
@@ -73,6 +77,7 @@ def parse():
     ap.add_argument("--tp-size", type=int, default=None,
                     help="GPUs per tensor-parallel rollout group with --rollout tp (default: all)")
     args = ap.parse_args()
+    args.mode = WORKLOADS[args.workload].get("mode", "train")
     for k, v in WORKLOADS[args.workload].items():
         if getattr(args, k, None) is None:
             setattr(args, k, v)
@@ -215,8 +220,10 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    rollout_only = args.mode == "rollout"
+    run = trainer.rollout if rollout_only else trainer.step
     for _ in range(args.warmup):
-        trainer.step()
+        run()
     ops.check_errors()
 
     # ---- device-timed region
@@ -230,7 +237,7 @@ def main():
         start.record()
         metrics = []
         for _ in range(args.steps):
-            m = trainer.step()
+            m = run()
             metrics.append(m)
             decode_ms += gen.decode_time_ms()
             decode_tokens += gen.last_decode_tokens
@@ -251,7 +258,7 @@ def main():
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            trainer.step()
+            run()
         torch.cuda.synchronize()
         barrier()
         e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps)
@@ -261,18 +268,24 @@ def main():
         prompt_len = n_img * (image_tokens + 2) + args.prompt_tokens
         seqs = args.groups * args.group_size // world                                   # trained on this rank
         # images + prefill ids/positions + packed training ids/positions/indices (int64)
-        h2d = img_bytes + roll_groups * prompt_len * 8 * 5 + seqs * (prompt_len + args.max_new) * 8 * 5
+        h2d = img_bytes + roll_groups * prompt_len * 8 * 5
+        if not rollout_only:
+            h2d += seqs * (prompt_len + args.max_new) * 8 * 5
         d2h = seqs * args.max_new * 12 + 8 * 64                         # tokens, logprobs, lengths, metrics
-        e2e = {"value": 1.0 / e2e_s, "unit": "RL steps/s", "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3}
+        if rollout_only:
+            e2e = {"value": args.groups * args.group_size * args.max_new / e2e_s, "unit": "generated tokens/s",
+                   "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3}
+        else:
+            e2e = {"value": 1.0 / e2e_s, "unit": "RL steps/s", "h2d_bytes_per_step": int(h2d),
+                   "d2h_bytes_per_step": int(d2h), "ms_per_step": e2e_s * 1e3}
 
     total_seqs = args.groups * args.group_size
     decode_tok_s = (total_seqs * (args.max_new - 1)) / (decode_ms / 1e3) if decode_ms > 0 else None
     last = metrics[-1]
     out = {
         "metric": METRIC,
-        "value": 1000.0 / ms,
-        "unit": "RL steps/s",
+        "value": (total_seqs * args.max_new / (ms / 1e3)) if rollout_only else 1000.0 / ms,
+        "unit": "generated tokens/s (rollout)" if rollout_only else "RL steps/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
@@ -286,7 +299,9 @@ def main():
                    "seq_len": f"{(2 if args.env == 'synthetic_truefalse' else 1) * (image_tokens + 2) + args.prompt_tokens}"
                               f" prompt + {args.max_new} new",
                    "workload": args.workload,
-                   "parallelism": ((f"fsdp{world}+tp{trainer.tp_size}x"
+                   "parallelism": (((f"tp{trainer.tp_size}xdp{world // trainer.tp_size}") if trainer.tp is not None
+                                    else f"dp{world}") if rollout_only else
+                                   (f"fsdp{world}+tp{trainer.tp_size}x"
                                     f"dp{world // trainer.tp_size}-rollout") if trainer.tp is not None else f"fsdp{world}")
                    + ("-sharded-params" if args.fsdp_params == "sharded" and world > 1 else "")
                    if world > 1 else "single-gpu",

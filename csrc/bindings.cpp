@@ -48,6 +48,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("prefetch") = py::none(), py::arg("lead") = py::none(),
         py::arg("share_len") = py::none());
   m.def("sample", &vlm::sample);
+  m.def("lm_head_sample", &vlm::lm_head_sample, "lm_head GEMM with a top-k epilogue + merge / top-p / Philox draw");
   m.def("vocab_logprob_fwd", &vlm::vocab_logprob_fwd);
   m.def("vocab_logprob_bwd", &vlm::vocab_logprob_bwd);
   m.def("symm_alloc", &vlm::symm_alloc, "cudaMalloc an IPC-exportable buffer");

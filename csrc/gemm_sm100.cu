@@ -44,8 +44,11 @@ struct DecFuse {
 enum Epi : int {
   EPI_STORE = 0, EPI_SWIGLU = 1, EPI_GELU_TANH = 2, EPI_GELU_ERF = 3, EPI_VOCAB_STATS = 4, EPI_VOCAB_GRAD = 5,
   // D [M, 2N] = SwiGLU backward of the product (= dL/d act) with aux = the forward's interleaved (gate, up)
-  EPI_SWIGLU_BWD = 6
+  EPI_SWIGLU_BWD = 6,
+  // no D: per (row, N-tile) the topk largest products (value desc, index asc) -> part / cand_i [M][tiles_n][topk]
+  EPI_TOPK = 7
 };
+constexpr int kTopkMax = 16;  // top-k epilogue: at most this many candidates per (row, tile)
 
 struct GemmParams {
   int M, N, K;
@@ -68,7 +71,9 @@ struct GemmParams {
   const float* row_ent;
   const float* g_lp;
   const float* g_ent;
-  float* part;  // [M, tiles_n, 4] partial (max, sum exp, sum exp*z, target logit)
+  float* part;  // [M, tiles_n, 4] partial (max, sum exp, sum exp*z, target logit); EPI_TOPK: candidate values
+  int* cand_i;  // EPI_TOPK: candidate indices [M, tiles_n, topk]
+  int topk;
   // split-K: tile t -> (mn tile = t / splits, split = t % splits); each split stores raw fp32
   // partial sums to ws[split] ([M, N] row-major) and splitk_reduce applies the epilogue.
   int splits;
@@ -747,6 +752,47 @@ __global__ void __launch_bounds__(GATHER ? 256 : 192, 1)
         if (row < p.M) {
           reinterpret_cast<float4*>(p.part)[static_cast<int64_t>(row) * p.tiles_n + tn] = make_float4(mx, se, sz, zt);
         }
+      } else if (p.epi == EPI_TOPK) {
+        // this row's topk largest logits of the tile (value desc, index asc), found by topk selection passes
+        // over the accumulator (each pass re-reads TMEM and takes the best entry after the previous pick);
+        // scalar state only, no per-lane divergence, and the logits are never stored
+        const int kk = p.topk;
+        const int64_t base = (static_cast<int64_t>(row) * p.tiles_n + tn) * kk;
+        float pv = INFINITY;
+        int pi = -1;
+#pragma unroll 1
+        for (int r = 0; r < kk; ++r) {
+          float bv = -INFINITY;
+          int bi = 0x7fffffff;
+#pragma unroll 1
+          for (int c4 = 0; c4 < BN; c4 += 64) {
+            uint32_t rr[4][16];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tmem_ld16(tbase + c4 + 16 * j, rr[j]);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int col0 = n0 + c4 + 16 * j;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float z = __uint_as_float(rr[j][i]) * p.alpha;
+                const int zi = col0 + i;
+                const bool after = z < pv || (z == pv && zi > pi);  // not picked yet
+                const bool better = z > bv || (z == bv && zi < bi);
+                if (zi < p.N && after && better) {
+                  bv = z;
+                  bi = zi;
+                }
+              }
+            }
+          }
+          if (row < p.M) {
+            p.part[base + r] = bv;
+            p.cand_i[base + r] = bi;
+          }
+          pv = bv;
+          pi = bi;
+        }
       } else if (p.epi == EPI_VOCAB_GRAD) {
         // dlogits = g_lp * (onehot - p) - g_ent * p * (log p + H), p = exp(z - lse)
         float lse = 0.f, ent = 0.f, glp = 0.f, gent = 0.f;
@@ -1003,9 +1049,12 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   TORCH_CHECK(K > 0 && M > 0 && N > 0, "gemm: empty problem");
   TORCH_CHECK(N % 8 == 0, "gemm: N must be a multiple of 8");
   const bool want_partials = partials_out != nullptr;
-  const bool is_stats = epi == EPI_VOCAB_STATS || want_partials;
+  const bool is_stats = epi == EPI_VOCAB_STATS || epi == EPI_TOPK || want_partials;
   TORCH_CHECK(is_stats || (D.is_cuda() && D.dim() == 2 && D.stride(1) == 1), "gemm: bad output");
-  TORCH_CHECK((epi != EPI_VOCAB_STATS && epi != EPI_VOCAB_GRAD) || vocab != nullptr, "gemm: vocab epilogue needs row data");
+  TORCH_CHECK((epi != EPI_VOCAB_STATS && epi != EPI_VOCAB_GRAD && epi != EPI_TOPK) || vocab != nullptr,
+              "gemm: vocab epilogue needs row data");
+  TORCH_CHECK(epi != EPI_TOPK || (vocab->topk >= 1 && vocab->topk <= kTopkMax && vocab->cand_i && vocab->part),
+              "gemm: top-k epilogue needs 1..", kTopkMax, " candidates per tile and candidate buffers");
   const bool d_f32 = !is_stats && D.scalar_type() == at::kFloat;
   if (!is_stats) {
     TORCH_CHECK(d_f32 || D.scalar_type() == at::kBFloat16, "gemm: output must be bf16 or fp32");
@@ -1031,6 +1080,8 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
     p.g_lp = vocab->g_lp;
     p.g_ent = vocab->g_ent;
     p.part = vocab->part;
+    p.cand_i = vocab->cand_i;
+    p.topk = vocab->topk;
   }
   p.d_f32 = d_f32;
   p.alpha = static_cast<float>(alpha);
@@ -1090,7 +1141,7 @@ void gemm_ex(at::Tensor A, at::Tensor B, at::Tensor D, at::Tensor bias, at::Tens
   // Training-sized GEMMs run on CTA pairs (256-row tiles, half of B per SM): fewer operand bytes per FLOP
   // through L2 than single-CTA 128-row tiles.  Decode (stream-K), gather, vocab and fused-consumer GEMMs
   // keep the single-CTA kernel.  VLMRL_GEMM_PAIR=0 turns pairs off.
-  const bool use_pair = pair_enabled() && !gather && !fuse && !want_partials && epi != EPI_VOCAB_STATS &&
+  const bool use_pair = pair_enabled() && !gather && !fuse && !want_partials && epi != EPI_VOCAB_STATS && epi != EPI_TOPK &&
                         epi != EPI_VOCAB_GRAD && force_bn == 0 && (a_kmajor || !b_kmajor) && M >= 4 * kBM;
   if (use_pair) {
     // Always 256-wide: 128-wide pair tiles (64 B rows per CTA) measured at about 0.5 of the bf16 peak on

@@ -21,6 +21,7 @@
 namespace vlm {
 
 constexpr int kSampThreads = 1024;
+constexpr int kEpiTopk = 7;  // gemm_sm100.cu EPI_TOPK
 constexpr int kKMax = 1024;
 
 VLM_DEV uint32_t ordered_key(float f) {
@@ -180,6 +181,206 @@ void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, a
              logits.stride(0), static_cast<int>(logits.size(1)), tok.data_ptr<int64_t>(), lp.data_ptr<float>(),
              step.data_ptr<int64_t>(), static_cast<float>(1.0 / temperature), k, static_cast<float>(top_p),
              seed.data_ptr<int64_t>(), static_cast<long long>(row_offset));
+}
+
+// ------------------------------------------------------------------ lm_head fused with the sampler
+// The lm_head GEMM runs with the EPI_TOPK epilogue: per (row, 128-column tile) it keeps the k largest
+// logits (value desc, index asc), so the fp32 [B, V] logits are never written.  One CTA per row then merges
+// the tiles' candidates into the row's top k and finishes exactly as sample_kernel does for those k
+// survivors: tempered softmax, inclusive prefix sum (the same Hillis-Steele order), nucleus cut, Philox
+// draw, log-probability of the choice.  With the same GEMM tiling as the unfused lm_head the logits are
+// bitwise the same, so both paths sample the same tokens.  Reference: core/sampling.py:198-204 and
+// utils/vlm.py:227-258 (mask logits to top-k / top-p, then sample).
+constexpr int kFusedTopkMax = 16;
+constexpr int kMergeThreads = 256;
+
+VLM_DEV bool cand_before(float a, int ia, float b, int ib) { return a > b || (a == b && ia < ib); }
+
+__global__ void __launch_bounds__(kMergeThreads) topk_merge_sample_kernel(
+    const float* __restrict__ cand_v, const int* __restrict__ cand_i, int tiles, int k, int64_t* __restrict__ tok_out,
+    float* __restrict__ lp_out, const int64_t* __restrict__ step_ptr, float inv_temp, float top_p,
+    const int64_t* __restrict__ seed_ptr, long long row_offset) {
+  __shared__ float wv[kMergeThreads / 32];
+  __shared__ int wi[kMergeThreads / 32];
+  __shared__ int wt[kMergeThreads / 32];
+  __shared__ float cv[kFusedTopkMax];
+  __shared__ int ci[kFusedTopkMax];
+  __shared__ int s_win;
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = tiles * k;
+  const float* v = cand_v + static_cast<int64_t>(row) * n;
+  const int* ix = cand_i + static_cast<int64_t>(row) * n;
+  // 1. this thread's sorted top k of its strided share of the candidates
+  float tv[kFusedTopkMax];
+  int ti[kFusedTopkMax];
+#pragma unroll
+  for (int j = 0; j < kFusedTopkMax; ++j) {
+    tv[j] = -INFINITY;
+    ti[j] = 0x7fffffff;
+  }
+  float tvk = -INFINITY;  // tv[k - 1], ti[k - 1] in registers (every array index below is static)
+  int tik = 0x7fffffff;
+  for (int c = tid; c < n; c += kMergeThreads) {
+    const float z = v[c];
+    const int zi = ix[c];
+    if (!cand_before(z, zi, tvk, tik)) continue;
+    bool placed = false;
+#pragma unroll
+    for (int q = kFusedTopkMax - 1; q > 0; --q) {
+      if (q < k && !placed) {
+        if (cand_before(z, zi, tv[q - 1], ti[q - 1])) {
+          tv[q] = tv[q - 1];
+          ti[q] = ti[q - 1];
+        } else {
+          tv[q] = z;
+          ti[q] = zi;
+          placed = true;
+        }
+      }
+    }
+    if (!placed) {
+      tv[0] = z;
+      ti[0] = zi;
+    }
+#pragma unroll
+    for (int q = 0; q < kFusedTopkMax; ++q)
+      if (q == k - 1) {
+        tvk = tv[q];
+        tik = ti[q];
+      }
+  }
+  // 2. k rounds of a block-wide arg-max over the threads' heads; the winner pops its head
+  int head = 0;
+  for (int r = 0; r < k; ++r) {
+    float bv = head < k ? tv[0] : -INFINITY;
+    int bi = head < k ? ti[0] : 0x7fffffff;
+    int bt = tid;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      const int ot = __shfl_xor_sync(0xffffffffu, bt, off);
+      if (cand_before(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+        bt = ot;
+      }
+    }
+    if (lane == 0) {
+      wv[warp] = bv;
+      wi[warp] = bi;
+      wt[warp] = bt;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float xv = wv[0];
+      int xi = wi[0], xt = wt[0];
+      for (int w = 1; w < kMergeThreads / 32; ++w)
+        if (cand_before(wv[w], wi[w], xv, xi)) {
+          xv = wv[w];
+          xi = wi[w];
+          xt = wt[w];
+        }
+      cv[r] = xv;
+      ci[r] = xi;
+      s_win = xt;
+    }
+    __syncthreads();
+    if (tid == s_win) {  // pop the head (a shift of the sorted list)
+#pragma unroll
+      for (int j = 0; j < kFusedTopkMax - 1; ++j) {
+        tv[j] = tv[j + 1];
+        ti[j] = ti[j + 1];
+      }
+      tv[kFusedTopkMax - 1] = -INFINITY;
+      ti[kFusedTopkMax - 1] = 0x7fffffff;
+      ++head;
+    }
+    __syncthreads();
+  }
+  // 3. tempered softmax over the survivors, inclusive prefix sum in sample_kernel's order, nucleus, draw
+  if (tid == 0) {
+    const float vmax = cv[0];
+    float cum[kFusedTopkMax];
+#pragma unroll
+    for (int i = 0; i < kFusedTopkMax; ++i) cum[i] = i < k ? __expf((cv[i] - vmax) * inv_temp) : 0.f;
+#pragma unroll
+    for (int off = 1; off < kFusedTopkMax; off <<= 1) {
+      float nxt[kFusedTopkMax];
+#pragma unroll
+      for (int i = 0; i < kFusedTopkMax; ++i) nxt[i] = cum[i] + (i >= off ? cum[i - off] : 0.f);
+#pragma unroll
+      for (int i = 0; i < kFusedTopkMax; ++i) cum[i] = nxt[i];
+    }
+    float total = 0.f;
+#pragma unroll
+    for (int i = 0; i < kFusedTopkMax; ++i)
+      if (i == k - 1) total = cum[i];
+    int keep = k;
+    if (top_p > 0.f && top_p < 1.f) {
+      keep = 1;
+#pragma unroll
+      for (int i = 0; i < kFusedTopkMax; ++i)
+        if (i < k && cum[i] / total <= top_p) keep = max(keep, i + 1);
+    }
+    float kept_total = 0.f;
+#pragma unroll
+    for (int i = 0; i < kFusedTopkMax; ++i)
+      if (i == keep - 1) kept_total = cum[i];
+    const unsigned int step = static_cast<unsigned int>(*step_ptr);
+    const unsigned long long seed = static_cast<unsigned long long>(*seed_ptr);
+    const float u = philox_uniform(seed, static_cast<unsigned long long>(row + row_offset), step) * kept_total;
+    int choice = keep - 1;
+    float prev_c = 0.f, cur_c = 0.f;
+#pragma unroll
+    for (int i = kFusedTopkMax - 1; i >= 0; --i) {
+      if (i < keep) {
+        const float prev = i == 0 ? 0.f : cum[i - 1];
+        if (cum[i] >= u && prev < u) choice = i;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kFusedTopkMax; ++i)
+      if (i == choice) {
+        cur_c = cum[i];
+        prev_c = i == 0 ? 0.f : cum[i - 1];
+      }
+    int tok = 0;
+#pragma unroll
+    for (int i = 0; i < kFusedTopkMax; ++i)
+      if (i == choice) tok = ci[i];
+    tok_out[row] = tok;
+    lp_out[row] = logf(fmaxf((cur_c - prev_c) / kept_total, 1e-30f));
+  }
+}
+
+void lm_head_sample(at::Tensor h, at::Tensor w, at::Tensor tok, at::Tensor lp, at::Tensor step, at::Tensor seed,
+                    double temperature, int64_t top_k, double top_p, int64_t row_offset) {
+  TORCH_CHECK(step.scalar_type() == at::kLong && step.is_cuda(), "lm_head_sample: step must be an int64 CUDA tensor");
+  TORCH_CHECK(seed.scalar_type() == at::kLong && seed.is_cuda(), "lm_head_sample: seed must be an int64 CUDA tensor");
+  TORCH_CHECK(temperature > 0, "lm_head_sample: temperature must be positive");
+  TORCH_CHECK(top_k >= 1 && top_k <= kFusedTopkMax, "lm_head_sample: 1 <= top_k <= ", kFusedTopkMax);
+  const int64_t B = h.size(0), V = w.size(0);
+  if (B == 0) return;
+  TORCH_CHECK(top_k <= V, "lm_head_sample: top_k larger than the vocabulary");
+  const c10::cuda::CUDAGuard g(h.device());
+  constexpr int kTile = 128;  // the unfused lm_head's tile width for decode-sized M: bitwise the same logits
+  const int tiles = static_cast<int>((V + kTile - 1) / kTile);
+  const int k = static_cast<int>(top_k);
+  at::Tensor cv = at::empty({B, tiles, k}, h.options().dtype(at::kFloat));
+  at::Tensor ci = at::empty({B, tiles, k}, h.options().dtype(at::kInt));
+  VocabArgs va{nullptr, nullptr, nullptr, nullptr, nullptr, cv.data_ptr<float>()};
+  va.cand_i = ci.data_ptr<int>();
+  va.topk = k;
+  gemm_ex(h, w, at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(), true, true, 1.0, kEpiTopk, false, &va, kTile,
+          nullptr, nullptr);
+  launch_pdl(topk_merge_sample_kernel, dim3(static_cast<unsigned>(B)), dim3(kMergeThreads), 0,
+             at::cuda::getCurrentCUDAStream(), cv.data_ptr<float>(), ci.data_ptr<int>(), tiles, k,
+             tok.data_ptr<int64_t>(), lp.data_ptr<float>(), step.data_ptr<int64_t>(),
+             static_cast<float>(1.0 / temperature), static_cast<float>(top_p), seed.data_ptr<int64_t>(),
+             static_cast<long long>(row_offset));
 }
 
 }  // namespace vlm

@@ -18,6 +18,8 @@ struct VocabArgs {
   const float* g_lp;
   const float* g_ent;
   float* part;
+  int* cand_i = nullptr;  // EPI_TOPK: per (row, tile) top-k indices (values go to part)
+  int topk = 0;
 };
 
 // Fused all-gather of a GEMM's weight operand: B is a view into the local copy of a flat parameter unit
@@ -140,6 +142,10 @@ int64_t adamw_push(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, std::
 void peer_wait(int64_t local_sig, int64_t slot, int64_t target, int64_t rank, int64_t world, int64_t device,
                int64_t budget_cycles);
 void peer_barrier(std::vector<int64_t> sigs, int64_t slot, int64_t epoch, int64_t rank, int64_t device);
+
+// sampler.cu: lm_head fused with the top-k / top-p sampler (logits never materialised)
+void lm_head_sample(at::Tensor h, at::Tensor w, at::Tensor tok, at::Tensor lp, at::Tensor step, at::Tensor seed,
+                    double temperature, int64_t top_k, double top_p, int64_t row_offset);
 
 // decode_step.cu (persistent decode step)
 std::vector<at::Tensor> decode_step_maps(std::vector<at::Tensor> weights, std::vector<at::Tensor> caches,

@@ -342,6 +342,30 @@ def test_sampler_matches_oracle(k, p, temp):
     torch.testing.assert_close(lp.cpu()[same], lr[same], atol=1e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize("V,k,p,temp", [(151936, 5, 0.9, 0.7), (151936, 16, 1.0, 1.3), (1000, 1, 0.5, 0.7),
+                                        (1000, 7, 0.95, 2.0)])
+def test_lm_head_sample_matches_unfused(V, k, p, temp):
+    """The lm_head fused with the sampler draws the same tokens with the same log-probs as lm_logits + sample:
+    the GEMM tiling is the unfused one, so the logits are bitwise equal, and the merge follows the sampler's
+    arithmetic; no [B, V] logits buffer is written (V = 1000 has a partial last tile)."""
+    B, H = 64, 2560
+    h = _r(B, H, seed=3)
+    w = _r(V, H, scale=0.05, seed=4)
+    seed = torch.tensor([987654321], dtype=torch.int64, device=DEV)
+    for step in (3, 4):
+        st = torch.tensor([step], dtype=torch.int64, device=DEV)
+        logits = ops.lm_logits(h, w)
+        tu, lu = ops.sample(logits, temperature=temp, top_k=k, top_p=p, seed=seed, step=st, row_offset=17)
+        tf, lf = ops.lm_head_sample(h, w, temperature=temp, top_k=k, top_p=p, seed=seed, step=st, row_offset=17)
+        torch.cuda.synchronize()
+        assert torch.equal(tf, tu), (tf != tu).nonzero()
+        # V = 151936 uses the same GEMM tiling in both paths (bitwise equal logits); the small vocabulary's
+        # unfused lm_head runs stream-K, whose partial-sum order differs in the last bits
+        tol = 1e-6 if V == 151936 else 1e-4
+        torch.testing.assert_close(lf, lu, atol=tol, rtol=tol)
+    _no_device_error()
+
+
 def test_adamw_and_sqnorm():
     n = 10000
     p = torch.randn(n, device=DEV)

@@ -90,3 +90,15 @@ def test_train_state_roundtrip(tmp_path):
     for name, buf in trainer.ts.optimizer.master.items():
         torch.testing.assert_close(t2.ts.optimizer.master[name], buf)
     assert t2.ts.step == trainer.ts.step
+
+
+def test_rollout_only_tiny_cpu():
+    """GRPOTrainer.rollout: the inference workload — rollout and rewards, no optimizer step."""
+    trainer, units = _tiny_trainer()
+    m = trainer.rollout()
+    assert trainer.ts.step == 1  # no update ran
+    assert m["sequences"] == 16 and 0 < m["tokens/generated"] <= 16 * 16
+    assert np.isfinite(m["reward/mean"]) and "time/rollout_ms" in m
+    assert all(torch.equal(trainer.model.params.units[l.name], units[l.name]) for l in text_layouts(trainer.model.spec))
+    # the dataset cursor advances as for a training step
+    assert trainer.cursor == 4

@@ -73,6 +73,13 @@ class Generator:
         st.step += 1
 
     def _decode_step(self, st: _DecodeState, cfg: SamplingConfig, row_offset: int):
+        if self.tp is None and hasattr(self.model, "decode_step_sample"):
+            # lm_head + sampler fused where supported: the [B, V] logits are never written
+            nt, lp = self.model.decode_step_sample(st.tok, st.cache, st.deltas, temperature=cfg.temperature,
+                                                   top_k=cfg.top_k or 0, top_p=cfg.top_p or 0.0, seed=st.seed,
+                                                   step=st.step, row_offset=row_offset)
+            self._record(st, nt, lp, cfg.eos_id)
+            return
         if self.tp is not None:
             logits = self.tp.decode_step(st.tok, st.tp_cache, st.deltas)
         else:

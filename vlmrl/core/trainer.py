@@ -111,6 +111,42 @@ class GRPOTrainer:
                        generator=self.generator, task_offset=self.cursor + self.rank * G,
                        row_offset=self.rank * G * cfg.group_size)
 
+    def rollout(self) -> Dict[str, Any]:
+        """One rollout without the update: vision encode, prefill, KV-cache decode and rewards for this rank's
+        groups (the inference workload; reference ``core/rollout.py`` collect + ``core/eval.py`` sampler
+        benchmark).  Returns the phase times and the token counts summed over ranks."""
+        if self.watchdog is not None:
+            self.watchdog.check()
+        timer = PhaseTimer(self.model.device)
+        timer.mark("start")
+        seed = self.rng.next()
+        G = self.groups_per_rank
+        infer = getattr(getattr(self.model, "params", None), "inference_weights", None)
+        with phase("rollout"), (infer() if infer is not None else contextlib.nullcontext()):
+            cr = self._collect(seed, G)
+        timer.mark("rollout")
+        self.cursor += G * self.world
+        num_tasks = getattr(self.env, "num_tasks", -1)
+        if num_tasks and num_tasks > 0:
+            self.cursor %= num_tasks
+        self.last_collect = cr
+        eps = cr.episodes.episodes
+        m: Dict[str, Any] = dict(timer.spans())
+        stats = torch.tensor([float(sum(e.action_length for e in eps)), float(len(eps)),
+                              float(cr.rewards.double().sum())], dtype=torch.float64, device=self.model.device)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(stats)
+        m["tokens/generated"] = float(stats[0])
+        m["sequences"] = float(stats[1])
+        m["reward/mean"] = float(stats[2] / max(1.0, float(stats[1])))
+        if self.model.device.type == "cuda":
+            dec_ms = self.generator.decode_time_ms()
+            if dec_ms > 0:
+                m["perf/decode_tok_s"] = self.generator.last_decode_tokens / (dec_ms / 1e3)
+        return m
+
     def step(self) -> Dict[str, Any]:
         cfg = self.cfg
         if self.watchdog is not None:

@@ -9,6 +9,8 @@ attention mask; internally everything is packed (see ``vlmrl.core.batching``).
 
 from __future__ import annotations
 
+import os
+
 from typing import Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
@@ -20,6 +22,10 @@ from vlmrl.models.qwen3vl.model import KVCache, LocalParams, PackedBatch, TextDe
 from vlmrl.models.qwen3vl.params import all_layouts, init_params, text_layouts
 from vlmrl.models.qwen3vl.vision import VisionTower, prepare_vision_inputs
 from vlmrl.utils.vlm import CLIP_MEAN, CLIP_STD
+
+
+# VLMRL_FUSED_SAMPLER=0: decode steps write the fp32 logits and sample them with the separate kernel.
+_FUSED_SAMPLER = os.environ.get("VLMRL_FUSED_SAMPLER", "1") != "0"
 
 
 class Qwen3VLModel:
@@ -116,6 +122,24 @@ class Qwen3VLModel:
         h, normed = self.decoder.decode_hidden(self.params, token, cache, rope_deltas.reshape(-1))
         cache.lengths += 1
         return self.decoder.final_logits(self.params, h, normed=normed)
+
+    def decode_step_sample(self, token: torch.Tensor, cache: KVCache, rope_deltas: torch.Tensor, *,
+                           temperature: float, top_k: int, top_p: float, seed, step, row_offset: int = 0):
+        """One decode step that returns the sampled (tokens, log-probs) directly; on a GPU with
+        1 <= top_k <= 16 the lm_head and the top-k / top-p sampler are fused and no logits are written.
+        Appends this token's k/v and advances ``cache.lengths``."""
+        h, normed = self.decoder.decode_hidden(self.params, token, cache, rope_deltas.reshape(-1))
+        cache.lengths += 1
+        if h.is_cuda and _FUSED_SAMPLER and 1 <= int(top_k or 0) <= ops.FUSED_SAMPLER_MAX_TOPK:
+            head = self.decoder._w(self.params, "head")
+            hn = h if normed else ops.rms_norm(h, head["final_norm"], self.decoder.eps)[0]
+            out = ops.lm_head_sample(hn, head["lm_head"], temperature=temperature, top_k=int(top_k), top_p=top_p,
+                                     seed=seed, step=step, row_offset=row_offset)
+            self.params.release("head")
+            return out
+        logits = self.decoder.final_logits(self.params, h, normed=normed)
+        return ops.sample(logits, temperature=temperature, top_k=top_k or 0, top_p=top_p or 0.0, seed=seed, step=step,
+                          row_offset=row_offset)
 
     def parameter_count(self, trainable_only: bool = False) -> int:
         return sum(l.numel for l in all_layouts(self.spec) if (l.trainable or not trainable_only))

@@ -515,6 +515,25 @@ def sample(logits, *, temperature: float, top_k: int, top_p: float, seed, step, 
     return tok, lp
 
 
+FUSED_SAMPLER_MAX_TOPK = 16
+
+
+def lm_head_sample(h, w, *, temperature: float, top_k: int, top_p: float, seed, step, row_offset: int = 0,
+                   out_tokens=None, out_logprobs=None):
+    """``sample(h @ w.T, ...)`` without materialising the logits (CUDA, 1 <= top_k <= 16): the lm_head GEMM keeps
+    each row's top-k per 128-column tile, a per-row kernel merges them and draws exactly as ``sample`` does."""
+    B = h.shape[0]
+    tok = out_tokens if out_tokens is not None else torch.empty(B, dtype=torch.int64, device=h.device)
+    lp = out_logprobs if out_logprobs is not None else torch.empty(B, dtype=torch.float32, device=h.device)
+    if not torch.is_tensor(step):
+        step = torch.tensor([int(step)], dtype=torch.int64, device=h.device)
+    if not torch.is_tensor(seed):
+        seed = torch.tensor([int(seed) & ((1 << 63) - 1)], dtype=torch.int64, device=h.device)
+    ext().lm_head_sample(h, w, tok, lp, step, seed, float(temperature), int(top_k), float(top_p or 0.0),
+                         int(row_offset))
+    return tok, lp
+
+
 # ------------------------------------------------------------------ optimizer
 def adamw_(p, g, m, v, *, lr, beta1, beta2, eps, weight_decay, step, grad_scale=1.0, p_half=None):
     if not _cuda(p):

@@ -250,6 +250,27 @@ def bench_decode_step(t: Timer, eager_steps: int = 0):
          bytes_=weights + 36 * 2 * 8 * (8 * 262 + B * 128) * 128 * 2)
 
 
+def bench_sampler(t: Timer):
+    """Decode-step lm_head + top-k/top-p sampling, Qwen3-VL-4B vocabulary, batch 64: the fused path (no logits
+    written) against lm_logits (fp32 [64, 151936]) followed by the sampler kernel."""
+    B, H, V = 64, 2560, 151936
+    h = _r(B, H)
+    w = _r(V, H, scale=0.05)
+    seed = torch.tensor([1], dtype=torch.int64, device="cuda")
+    step = torch.tensor([1], dtype=torch.int64, device="cuda")
+    with ops.static_weights():
+        ms = t(lambda: ops.lm_head_sample(h, w, temperature=0.7, top_k=5, top_p=0.9, seed=seed, step=step))
+    emit("lm_head_sample_fused_64x151936x2560", ms, bytes_=V * H * 2)
+
+    def unfused():
+        logits = ops.lm_logits(h, w)
+        return ops.sample(logits, temperature=0.7, top_k=5, top_p=0.9, seed=seed, step=step)
+
+    with ops.static_weights():
+        ms = t(unfused)
+    emit("lm_logits_then_sample_64x151936x2560", ms, bytes_=V * H * 2)
+
+
 def bench_train_step(t: Timer = None, eager_steps: int = 0, iters: int = 5):
     """One GRPO minibatch update of Qwen3-VL-4B: 4 groups x 8 members (262-token prompt shared per group,
     128 response tokens), forward with activations saved, backward, AdamW over all text units."""
@@ -410,7 +431,7 @@ def profile_small(case: str = "decode"):
 
 
 CASES = {"gemm": bench_gemm, "attn": bench_attn, "decode": bench_decode, "vocab": bench_vocab, "norm": bench_norm,
-         "decode_step": bench_decode_step, "gather": bench_gather, "decode_gemms": bench_decode_gemms,
+         "decode_step": bench_decode_step, "sampler": bench_sampler, "gather": bench_gather, "decode_gemms": bench_decode_gemms,
          "gemm_tiny": bench_gemm_tiny, "train_step": bench_train_step}
 
 
