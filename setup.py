@@ -20,6 +20,7 @@ setup(
     name="vlmrl",
     version="0.1.0",
     packages=find_packages(include=["vlmrl", "vlmrl.*"]),
+    package_data={"vlmrl.assets": ["imgs/*.png"]},
     ext_modules=[
         CUDAExtension(
             name="vlmrl._C",

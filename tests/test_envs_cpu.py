@@ -169,6 +169,28 @@ def test_vision_caption_keyword_fraction():
     assert env.step(st, CharTokenizer().encode("zzzz"))[2] == 0.0
 
 
+def test_vision_caption_ships_its_demo_images():
+    """Every caption task's image exists in the package (no random placeholder) and preprocesses."""
+    from vlmrl.models.qwen3vl.config import get_preset
+    from vlmrl.utils.vlm import preprocess_image
+
+    env = VisionCaptionEnv(CharTokenizer())
+    spec = get_preset("tiny")
+    seen = set()
+    for i in range(env.num_tasks):
+        st, prompt = env.reset(i)
+        assert prompt.image is None, st.sample.image_path   # the file is there
+        if st.sample.image_path in seen:
+            continue
+        seen.add(st.sample.image_path)
+        v = spec.vision
+        rows, grid = preprocess_image(st.sample.image_path, patch_size=v.patch_size,
+                                      spatial_merge_size=v.spatial_merge_size,
+                                      temporal_patch_size=v.temporal_patch_size, max_pixels=64 * 64 * 4)
+        assert rows.shape[0] == int(grid.prod()) and torch.isfinite(rows).all()
+    assert len(seen) == 7
+
+
 def test_synthetic_envs_rewards():
     tok = CharTokenizer()
     par = SyntheticParityEnv(tok, num_tasks=4)

@@ -1,9 +1,10 @@
 """Keyword-coverage captioning demo env (reference ``envs/vision_caption.py:24-121``).
 
 Fifteen fixed (question, image, keywords) prompts over a folder of demo images;
-reward = fraction of keywords present (case-insensitive) in the response.  When
-an image file is missing the env substitutes a deterministic random image so
-that the env still runs offline.
+reward = fraction of keywords present (case-insensitive) in the response.  The
+package ships drawn versions of the seven scenes (``vlmrl/assets/imgs``, made by
+``vlmrl.assets.make_demo_images``); with another ``asset_root`` whose files are
+missing, the env substitutes a deterministic random image so that it still runs.
 """
 
 from __future__ import annotations
