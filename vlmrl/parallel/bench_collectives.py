@@ -15,9 +15,9 @@ CUDA events on the launching stream and the max over ranks:
                      (MN-major weight operand).
 
 Roofline: bytes that must cross NVLink per rank / 770 GB/s (the measured peer-copy bandwidth per
-direction), or for the GEMM cases the slower of that and FLOPs / 1651 TFLOP/s (the measured cuBLAS bf16
-burst peak); the achieved fraction is that time divided by the measured time.  Prints one JSON line
-per case on rank 0.
+direction), or for the GEMM cases the slower of that and FLOPs at the measured bf16 burst peak (HBM-side
+terms at the measured copy bandwidth; both from MEASURED_PEAKS.json, else the fallback figures); the
+achieved fraction is that time divided by the measured time.  Prints one JSON line per case on rank 0.
 """
 
 from __future__ import annotations
@@ -30,7 +30,15 @@ import torch
 import torch.distributed as dist
 
 LINK_GBS = 770.0
-GEMM_TFLOPS = 1651.0
+
+
+def _peaks():
+    from vlmrl.ops.bench_kernels import peaks
+
+    return peaks()
+
+
+GEMM_TFLOPS, HBM_GBS, PEAK_SOURCE = _peaks()
 
 
 def _timed(fn, iters: int = 20, warmup: int = 3) -> float:
@@ -106,7 +114,7 @@ def main() -> None:
     ops.check_errors(local)
     link_bytes = (W - 1) * n * 2             # this rank's bf16 shard stored into every peer
     local_bytes = n * (4 * 4 + 3 * 4 + 2)    # AdamW reads p, g, m, v and writes p, m, v, own bf16
-    ideal = max(link_bytes / (LINK_GBS * 1e9), local_bytes / 6.541e12) * 1e3
+    ideal = max(link_bytes / (LINK_GBS * 1e9), local_bytes / (HBM_GBS * 1e9)) * 1e3
     out.append({"case": f"adamw_push_{n_full}", "world": W, "ms": round(ms, 4), "roofline_ms": round(ideal, 4),
                 "frac_of_roofline": round(ideal / ms, 3)})
     gathered = torch.empty(n_full, dtype=torch.bfloat16, device=dev)
