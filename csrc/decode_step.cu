@@ -85,7 +85,7 @@ struct Layer {  // 8 pointers (64 bytes), filled by the host from the layer's pa
 struct Params {
   int L, B, BP, H, nq, nkv, F, Tmax, G;
   int NA;  // independent MMA accumulation chains per tile: k-step i of a k-block accumulates into chain i % NA
-  int w_stages, a_stages;
+  int w_stages, slot_bytes;  // ring slots: a 16 KB weight tile / KV chunk, then the k-block's activation tile
   float eps, scale_log2;
   const CUtensorMap* wmaps;  // [L][4] weights (qkv, o, gate/up, down; [N, K] row-major), then [L][2] K / V caches
   const CUtensorMap* amaps;  // [4]: xn, o, hn, act activations ([B, K] row-major)
@@ -321,19 +321,17 @@ VLM_DEV void frag_kn(uint32_t (&b)[4], const bf16* s, int k0, int n0, int lane) 
 }
 
 struct Smem {
-  uint8_t* wbuf;     // the ring: w_stages slots of kSlot bytes
-  uint8_t* abuf;
+  uint8_t* wbuf;     // the ring: w_stages slots of slot_bytes (weight tile or KV chunk, then activation tile)
   float* merge;      // [8 warps][REP][D + 2]
   bf16* qs;          // [kMaxItems][REP][D] the items' rotated q heads
   bf16* kvn;         // [kMaxItems][2][D] the items' k and v of this step
   float* red;        // [16]
-  uint64_t* wfull;
+  uint64_t* wfull;   // two arrivals: the ring producer's and the activation producer's
   uint64_t* wempty;
-  uint64_t* afull;
-  uint64_t* aempty;
   uint64_t* tfull;   // [2]
   uint64_t* tempty;  // [2]
   uint64_t* drain;
+  uint64_t* kvdone;  // one arrival per layer: the attention warps are done with the layer's KV slots
   uint32_t* tmem_holder;
   int* flags;        // [0] compute-group wait result, [1] last-arriver flag
 };
@@ -527,12 +525,16 @@ VLM_DEV void attention_phase(const Params& p, const Smem& s, int layer, int rp) 
     }
   }
   bar_named(kBarCompute, kCompute);  // q, k and v of every item in shared memory
+  int cbase = 0;  // KV chunks of this layer's earlier items
   for (int ii = 0; ii < n_items; ++ii) {
     const Item it = item_of(p, blockIdx.x + ii * p.G);
     const int b = it.b, hk = it.hk;
     const bf16* qs = s.qs + ii * REP * kD;
     const bf16* kvn = s.kvn + ii * 2 * kD;
-    // ---- 2) the cached prefix: group grp takes chunks grp, grp + 2, ... (K in slot 2j, V in slot 2j+1)
+    // ---- 2) the cached prefix: group grp takes the chunks whose index among the layer's chunks has parity
+    // grp (K in ring position rp + 2j, V in rp + 2j + 1).  A parity wait on a slot is only exact when the
+    // slot's previous phase is already complete; the ring depth is a multiple of 4, so that previous phase
+    // (S positions back = S / 2 chunks back, an even count) is a chunk this group has waited on itself.
     uint32_t qa[kD / 16][4];
 #pragma unroll
     for (int kk = 0; kk < kD / 16; ++kk) {
@@ -549,14 +551,14 @@ VLM_DEV void attention_phase(const Params& p, const Smem& s, int layer, int rp) 
 #pragma unroll
     for (int i = 0; i < kD / 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
     float mrun = -INFINITY, lrun = 0.f;  // running stats of row g (rows g < REP are the heads)
-    for (int j = grp; j < it.n_chunks; j += 2) {
+    for (int j = grp ^ (cbase & 1); j < it.n_chunks; j += 2) {
       int k0, cnt, row;
       chunk_of(it, j, k0, cnt, row);
       const int pk = rp + 2 * j, pv = pk + 1;
       const bool okk = DS_TIMED(p, kStAttKv, mwait_warp(&s.wfull[pk % S], static_cast<uint32_t>((pk / S) & 1), p, kErrTimeoutFlag));
       const bool okv = mwait_warp(&s.wfull[pv % S], static_cast<uint32_t>((pv / S) & 1), p, kErrTimeoutFlag);
-      const bf16* kt = reinterpret_cast<const bf16*>(s.wbuf + (pk % S) * kSlot);
-      bf16* vt = reinterpret_cast<bf16*>(s.wbuf + (pv % S) * kSlot);
+      const bf16* kt = reinterpret_cast<const bf16*>(s.wbuf + (pk % S) * p.slot_bytes);
+      bf16* vt = reinterpret_cast<bf16*>(s.wbuf + (pv % S) * p.slot_bytes);
       if (okk && okv) {
         if (cnt < kKC) {
           // keys past the chunk's range: their V rows hold another sequence's or unwritten cache rows, and
@@ -627,6 +629,7 @@ VLM_DEV void attention_phase(const Params& p, const Smem& s, int layer, int rp) 
       }
     }
     rp += 2 * it.n_chunks;
+    cbase += it.n_chunks;
     // ---- 3) merge the eight warps' states and this step's own key
     lrun += __shfl_xor_sync(0xffffffffu, lrun, 1);
     lrun += __shfl_xor_sync(0xffffffffu, lrun, 2);
@@ -740,39 +743,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
   extern __shared__ __align__(1024) uint8_t ds_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ds_raw) + 1023) & ~uintptr_t(1023));
   const int abytes = a_stage_bytes(p.BP);
+  const int SB = p.slot_bytes;
   Smem s;
   s.wbuf = base;
-  s.abuf = s.wbuf + p.w_stages * kSlot;
-  s.merge = reinterpret_cast<float*>(s.abuf + p.a_stages * abytes);
+  s.merge = reinterpret_cast<float*>(s.wbuf + p.w_stages * SB);
   s.qs = reinterpret_cast<bf16*>(s.merge + merge_floats(REP));
   s.kvn = s.qs + kMaxItems * REP * kD;
   s.red = reinterpret_cast<float*>(s.kvn + kMaxItems * 2 * kD);
   s.wfull = reinterpret_cast<uint64_t*>(s.red + 16);
   s.wempty = s.wfull + p.w_stages;
-  s.afull = s.wempty + p.w_stages;
-  s.aempty = s.afull + p.a_stages;
-  s.tfull = s.aempty + p.a_stages;
+  s.tfull = s.wempty + p.w_stages;
   s.tempty = s.tfull + 2;
   s.drain = s.tempty + 2;
-  s.tmem_holder = reinterpret_cast<uint32_t*>(s.drain + 1);
+  s.kvdone = s.drain + 1;
+  s.tmem_holder = reinterpret_cast<uint32_t*>(s.kvdone + 1);
   s.flags = reinterpret_cast<int*>(s.tmem_holder + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x < 16) ds_stats[threadIdx.x] = 0ull;
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.w_stages; ++i) {
-      mbar_init(&s.wfull[i], 1);
+      mbar_init(&s.wfull[i], 2);
       mbar_init(&s.wempty[i], 1);
-    }
-    for (int i = 0; i < p.a_stages; ++i) {
-      mbar_init(&s.afull[i], 1);
-      mbar_init(&s.aempty[i], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&s.tfull[a], 1);
       mbar_init(&s.tempty[a], 4);
     }
     mbar_init(s.drain, 1);
+    mbar_init(s.kvdone, 1);
     s.flags[0] = s.flags[1] = 0;
     fence_mbar_init();
   }
@@ -817,7 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
           if (lane == 0) {
             evlog(p, layer, 3, wlog++);
             mbar_arrive_expect_tx(&s.wfull[st], kSlot);
-            tma_load_2d(s.wbuf + st * kSlot, map, &s.wfull[st], kb * kBK, tile * kTileN);
+            tma_load_2d(s.wbuf + st * SB, map, &s.wfull[st], kb * kBK, tile * kTileN);
           }
           __syncwarp();
           advance();
@@ -843,7 +842,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
               }
               if (lane == 0) {
                 mbar_arrive_expect_tx(&s.wfull[st], kSlot);
-                uint8_t* dst = s.wbuf + st * kSlot;
+                uint8_t* dst = s.wbuf + st * SB;
                 tma_load_2d(dst, kmap + kv, &s.wfull[st], 0, y);
                 tma_load_2d(dst + kSlot / 2, kmap + kv, &s.wfull[st], 64, y);
               }
@@ -858,64 +857,83 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     for (long long i = issued - 1; i >= 0 && i >= issued - p.w_stages; --i)
       mwait_drain(&s.wfull[i % p.w_stages], static_cast<uint32_t>((i / p.w_stages) & 1));
   } else if (warp == 2) {
-    // ---- activation producer: waits for each GEMM's input, then streams its k-blocks (whole warp, lane 0 issues)
+    // ---- activation producer: walks the same ring positions as the ring producer.  For a GEMM unit it waits
+    // for the GEMM's input (once per GEMM), then adds the unit's activation tile to the slot (the slot's
+    // second arrival); for a KV slot it only arrives.  Whole warp, lane 0 issues.
     int st = 0;
     uint32_t ph = 0;
     long long issued = 0;
     bool ok = true;
+    const int kvs = kv_slots(p, c);
+    auto advance = [&]() {
+      ++issued;
+      if (++st == p.w_stages) {
+        st = 0;
+        ph ^= 1u;
+      }
+    };
     for (int layer = 0; ok && layer < p.L; ++layer) {
       const long long layer_first = issued;
       for (int g = 0; ok && g < 4; ++g) {
         const Gemm m = gemm_of(p, g);
         const int u0 = unit_begin(m, c), u1 = unit_begin(m, c + 1);
-        if (u0 == u1) continue;
-        const unsigned* wc = nullptr;
-        unsigned target = static_cast<unsigned>(p.G);
-        if (g == 0 && layer > 0) wc = ctr(p, layer - 1, kNorm2);
-        if (g == 1) wc = ctr(p, layer, kAtt);
-        if (g == 2) wc = ctr(p, layer, kNorm1);
-        if (g == 3) {
-          wc = ctr(p, layer, kGuf);
-          target = static_cast<unsigned>(gemm_of(p, 2).T);
-        }
-        bool ready = true;
-        if (wc && lane == 0) ready = DS_TIMED(p, kStActCtr, cwait(p, wc, target, kErrTimeoutFlag));
-        if (!__shfl_sync(0xffffffffu, ready ? 1 : 0, 0)) {
-          ok = false;
-          break;
-        }
-        fence_proxy_async_global();
-        const CUtensorMap* map = p.amaps + g;
-        int kb = u0 % m.KB;
-        for (int u = u0; u < u1; ++u, kb = (kb + 1 == m.KB) ? 0 : kb + 1) {
-          if (!DS_TIMED(p, kStActEmpty, mwait_warp(&s.aempty[st], ph ^ 1u, p, kErrTimeoutProducer))) {
+        if (u0 < u1) {
+          const unsigned* wc = nullptr;
+          unsigned target = static_cast<unsigned>(p.G);
+          if (g == 0 && layer > 0) wc = ctr(p, layer - 1, kNorm2);
+          if (g == 1) wc = ctr(p, layer, kAtt);
+          if (g == 2) wc = ctr(p, layer, kNorm1);
+          if (g == 3) {
+            wc = ctr(p, layer, kGuf);
+            target = static_cast<unsigned>(gemm_of(p, 2).T);
+          }
+          bool ready = true;
+          if (wc && lane == 0) ready = DS_TIMED(p, kStActCtr, cwait(p, wc, target, kErrTimeoutFlag));
+          if (!__shfl_sync(0xffffffffu, ready ? 1 : 0, 0)) {
             ok = false;
             break;
           }
-          if (lane == 0) {
-            evlog(p, layer, 0, static_cast<int>(issued - layer_first));
-            mbar_arrive_expect_tx(&s.afull[st], abytes);
-            tma_load_2d(s.abuf + st * abytes, map, &s.afull[st], kb * kBK, 0);
+          fence_proxy_async_global();
+          const CUtensorMap* map = p.amaps + g;
+          int kb = u0 % m.KB;
+          for (int u = u0; u < u1; ++u, kb = (kb + 1 == m.KB) ? 0 : kb + 1) {
+            if (!DS_TIMED(p, kStActEmpty, mwait_warp(&s.wempty[st], ph ^ 1u, p, kErrTimeoutProducer))) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) {
+              evlog(p, layer, 0, static_cast<int>(issued - layer_first));
+              mbar_arrive_expect_tx(&s.wfull[st], abytes);
+              tma_load_2d(s.wbuf + st * SB + kSlot, map, &s.wfull[st], kb * kBK, 0);
+            }
+            __syncwarp();
+            advance();
           }
-          __syncwarp();
-          ++issued;
-          if (++st == p.a_stages) {
-            st = 0;
-            ph ^= 1u;
+        }
+        if (g == 0) {
+          for (int i = 0; ok && i < kvs; ++i) {  // KV slots carry no activation: plain second arrival
+            if (!mwait_warp(&s.wempty[st], ph ^ 1u, p, kErrTimeoutProducer)) {
+              ok = false;
+              break;
+            }
+            if (lane == 0) mbar_arrive(&s.wfull[st]);
+            __syncwarp();
+            advance();
           }
         }
       }
     }
-    for (long long i = issued - 1; i >= 0 && i >= issued - p.a_stages; --i)
-      mwait_drain(&s.afull[i % p.a_stages], static_cast<uint32_t>((i / p.a_stages) & 1));
+    // this warp's activation copies have landed before the CTA can exit
+    for (long long i = issued - 1; i >= 0 && i >= issued - p.w_stages; --i)
+      mwait_drain(&s.wfull[i % p.w_stages], static_cast<uint32_t>((i / p.w_stages) & 1));
   } else if (warp == 1) {
     // ---- MMA issuer (steps over the ring slots of the KV chunks, which the attention warps consume); the
     // whole warp walks the loop, lane 0 issues
     const uint32_t idesc = idesc_bf16_f32(128, p.BP, false, false);
-    const uint32_t wb = smem_u32(s.wbuf), ab = smem_u32(s.abuf);
+    const uint32_t wb = smem_u32(s.wbuf);
     const int kvs = kv_slots(p, c);
-    int wst = 0, ast = 0;
-    uint32_t wph = 0, aph = 0;
+    int wst = 0;
+    uint32_t wph = 0;
     int lt = 0;
     bool ok = true;
     for (int layer = 0; ok && layer < p.L; ++layer) {
@@ -944,32 +962,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
               ok = false;
               break;
             }
-            if (lane == 0) evlog(p, layer, 2, kcount);
-            if (!DS_TIMED(p, kStMmaA, mwait_warp(&s.afull[ast], aph, p, kErrTimeoutMma))) {
-              ok = false;
-              break;
-            }
             if (lane == 0) {
-              evlog(p, layer, 1, kcount);
+              evlog(p, layer, 2, kcount);
               if (first_seg && kb == kb0) trace(p, layer, kTrMmaQkv + g);
               tc_fence_after();
 #pragma unroll
               for (int k = 0; k < kBK / 16; ++k) {
                 // chain k % NA: consecutive MMAs target different accumulators, so they pipeline
-                const uint64_t ad = sdesc_sw128(wb + wst * kSlot + k * 32, 16, 1024);
-                const uint64_t bd = sdesc_sw128(ab + ast * abytes + k * 32, 16, 1024);
+                const uint64_t ad = sdesc_sw128(wb + wst * SB + k * 32, 16, 1024);
+                const uint64_t bd = sdesc_sw128(wb + wst * SB + kSlot + k * 32, 16, 1024);
                 const int q = k % p.NA;
                 umma_f16(d + static_cast<uint32_t>(q * p.BP), ad, bd, idesc, (kb != kb0 || k >= p.NA) ? 1u : 0u);
               }
-              umma_commit(&s.wempty[wst]);
-              umma_commit(&s.aempty[ast]);
+              umma_commit(&s.wempty[wst]);  // frees the weight tile and the activation tile together
             }
             __syncwarp();
             ++kcount;
-            if (++ast == p.a_stages) {
-              ast = 0;
-              aph ^= 1u;
-            }
             if (++wst == p.w_stages) {
               wst = 0;
               wph ^= 1u;
@@ -986,6 +994,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
             wst -= p.w_stages;
             wph ^= 1u;
           }
+          // A parity wait cannot tell a phase from the one two uses later, so before waiting on the o tiles'
+          // slots, whose previous phase may be a KV chunk the attention warps have not seen yet, wait until
+          // the attention warps are done with every KV slot of the layer.
+          if (!DS_TIMED(p, kStMmaA, mwait_warp(s.kvdone, static_cast<uint32_t>(layer & 1), p, kErrTimeoutMma))) ok = false;
         }
       }
     }
@@ -1015,6 +1027,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         attention_phase<REP>(p, s, layer, layer * per_layer + nq_units);
         if (tr) stat_add(p, kStAttention, clock64() - t0);
       }
+      if (threadIdx.x == 128) mbar_arrive(s.kvdone);  // after the item loop's last compute barrier
       group_arrive(p, ctr(p, layer, kAtt));
       if (tr) trace(p, layer, kTrAtt);
       if (epi) epilogue_phase(p, s, tmem_base, layer, 1, lt);
@@ -1060,21 +1073,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
 namespace {
 
 struct DsGeom {
-  int w_stages, a_stages, smem;
+  int w_stages, slot_bytes, smem;
 };
 
 DsGeom ds_geom(int BP, int rep) {
   constexpr int kBudget = 227 * 1024;
-  const int abytes = ds::a_stage_bytes(BP);
-  const int a_stages = BP <= 64 ? 8 : 5;
+  const int slot = ds::kSlot + ds::a_stage_bytes(BP);  // multiple of 2 KB: every slot stays 1 KB aligned
   const int fixed = 1024 /* alignment */ + ds::merge_floats(rep) * 4 + ds::kMaxItems * (rep + 2) * ds::kD * 2 +
                     16 * 4 + 640 /* barriers, TMEM holder, flags */;
-  int w_stages = (kBudget - fixed - a_stages * abytes) / ds::kSlot;
-  w_stages = std::min(w_stages, 12);
+  // a multiple of 4: each attention group's parity waits then find the slot's previous phase among the
+  // group's own earlier chunks (decode_step_kernel's attention phase)
+  int w_stages = std::min((kBudget - fixed) / slot, 12) & ~3;
   DsGeom g;
   g.w_stages = w_stages;
-  g.a_stages = a_stages;
-  g.smem = fixed + a_stages * abytes + w_stages * ds::kSlot;
+  g.slot_bytes = slot;
+  g.smem = fixed + w_stages * slot;
   return g;
 }
 
@@ -1155,7 +1168,7 @@ void decode_step(at::Tensor wmaps, at::Tensor amaps, at::Tensor layers, at::Tens
   p.G = num_sms(dev);
   const DsGeom geo = ds_geom(p.BP, rep);
   p.w_stages = geo.w_stages;
-  p.a_stages = geo.a_stages;
+  p.slot_bytes = geo.slot_bytes;
   TORCH_CHECK(p.w_stages >= 4, "decode_step: shared memory too small");
   p.eps = static_cast<float>(eps);
   p.scale_log2 = static_cast<float>(scale) * 1.4426950408889634f;

@@ -22,7 +22,7 @@ from vlmrl.ops._ext import ext
 
 # VLMRL_DECODE_PERSISTENT=1 selects the persistent step.  Off by default: it is correct (bitwise
 # reproducible, tested against the per-kernel path) but measured slower on the 4B model at batch 64
-# (6.6 vs 4.2 ms per step): its GEMM phases advance about one k-block per microsecond per SM.
+# (6.8 vs 4.1 ms per step): its GEMM phases run at about a quarter of the HBM rate.
 ENABLED = os.environ.get("VLMRL_DECODE_PERSISTENT", "0") == "1"
 
 _MAX_BATCH = 128
