@@ -52,6 +52,16 @@ WORKLOADS = {
 }
 
 
+
+def _data_desc(args) -> str:
+    """What the synthetic inputs of the workload are (the JSON line's ``data`` field)."""
+    n_img = 2 if args.env == "synthetic_truefalse" else 1
+    targets = {"synthetic_geo": "uniform-on-sphere lat/lon targets",
+               "synthetic_truefalse": "Bernoulli(0.5) True/False labels",
+               "synthetic_parity": "parity-of-first-token reward"}.get(args.env, args.env)
+    return (f"synthetic ({n_img} uniform-random {args.image}x{args.image} RGB image{'s' if n_img > 1 else ''} and "
+            f"{args.prompt_tokens} uniform-random prompt ids per prompt, {targets}), random-init weights")
+
 def parse():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -294,7 +304,7 @@ def main():
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (uniform-random 448x448 RGB images and prompt ids, uniform-on-sphere targets), random-init weights",
+        "data": _data_desc(args),
         "config": {"model": f"{args.preset} architecture (random init)", "global_batch": total_seqs,
                    "seq_len": f"{(2 if args.env == 'synthetic_truefalse' else 1) * (image_tokens + 2) + args.prompt_tokens}"
                               f" prompt + {args.max_new} new",
