@@ -102,3 +102,64 @@ def test_rollout_only_tiny_cpu():
     assert all(torch.equal(trainer.model.params.units[l.name], units[l.name]) for l in text_layouts(trainer.model.spec))
     # the dataset cursor advances as for a training step
     assert trainer.cursor == 4
+
+
+def test_grpo_update_with_nonzero_geodesic_rewards():
+    """reward -> advantage -> loss -> gradient with the geodesic reward actually varying.
+
+    Random-init weights never emit parseable coordinates, so a plain rollout scores 0 everywhere.  Here the
+    sampled responses are replaced by byte-encoded answers at known distances from each group's target (exact,
+    ~150 km, ~2000 km, unparseable), and the whole trainer step runs on them: rewards must fall with
+    distance, advantages must be non-zero and centred per group, and the update must move the weights."""
+    from vlmrl.core.sampling import Generator
+
+    spec = get_preset("tiny")
+    units = init_params(spec, seed=0)
+    model = Qwen3VLModel(spec, units=units, dtype=torch.float32)
+    ref = Qwen3VLModel(spec, units={k: v for k, v in units.items() if k != "visual"}, dtype=torch.float32)
+    tok = ByteTokenizer(spec.text.vocab_size)
+    env = create_env("synthetic_geo", tok, image_size=64, prompt_tokens=16, num_tasks=64, seed=0, vocab_high=900)
+    G, gs, max_new = 2, 4, 48
+    cfg = TrainerConfig(temperature=0.7, top_p=0.9, top_k=5, max_new_tokens=max_new, groups_per_batch=G,
+                        group_size=gs, kl_ref_coef=0.01, n_minibatches=1, clip_epsilon=0.2)
+    trainer = GRPOTrainer(model, tok, env, cfg, AdamWConfig(lr=1e-4), ref_model=ref, seed=0)
+    targets = [env.reset(trainer.cursor + g)[0].target for g in range(G)]
+    offsets = [(0.0, 0.0), (1.0, 1.0), (15.0, 12.0), None]   # degrees; None: prose without coordinates
+
+    real = Generator.generate
+
+    def crafted(self, *a, **kw):
+        res = real(self, *a, **kw)
+        toks = torch.full_like(res.tokens, tok.pad_token_id)
+        lens = torch.zeros_like(res.lengths)
+        for g in range(G):
+            c = targets[g]
+            for j, off in enumerate(offsets):
+                text = ("I cannot tell." if off is None else
+                        f"Latitude: {max(-90.0, min(90.0, c.lat + off[0])):.4f}\nLongitude: {c.lon + off[1]:.4f}")
+                ids = tok.encode(text)[:max_new]
+                b = g * gs + j
+                toks[b, :len(ids)] = torch.tensor(ids, dtype=toks.dtype)
+                lens[b] = len(ids)
+        res.tokens, res.lengths = toks, lens
+        return res
+
+    Generator.generate = crafted
+    try:
+        m = trainer.step()
+    finally:
+        Generator.generate = real
+    cr = trainer.last_collect
+    r = cr.rewards.view(G, gs)
+    assert torch.all(r[:, 0] > r[:, 1]) and torch.all(r[:, 1] > r[:, 2]) and torch.all(r[:, 3] == 0), r
+    assert torch.allclose(r[:, 0], torch.ones(G), atol=1e-3)   # 4-decimal coordinates: metres off
+    adv = cr.advantages.view(G, gs).cpu()
+    assert torch.allclose(adv.mean(1), torch.zeros(G), atol=1e-5)
+    assert torch.all(adv[:, 0] > 0) and torch.all(adv[:, 3] < 0)
+    assert m["reward/mean"] > 0.2
+    for k in ("loss", "loss_pg", "grad_norm"):
+        assert np.isfinite(m[k]), k
+    assert m["grad_norm"] > 0 and abs(m["loss_pg"]) > 0
+    moved = any(not torch.equal(trainer.model.params.units[l.name], units[l.name])
+                for l in text_layouts(trainer.model.spec))
+    assert moved
