@@ -23,7 +23,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dec_swiglu", &vlm::dec_swiglu, py::arg("ws"), py::arg("meta"), py::arg("prefetch") = py::none());
   m.def("tp_step_begin", &vlm::tp_step_begin, "advance the tensor-parallel decode epoch (device counter)");
   m.def("dec_residual_norm_tp", &vlm::dec_residual_norm_tp,
-        "residual + RMSNorm consumer that all-reduces row-parallel partials over NVLink");
+        "residual + RMSNorm consumer that all-reduces row-parallel partials over NVLink (tagged 8-byte words "
+        "stored into every rank's slot, no fence or flag)");
   m.def("rms_norm_fwd", &vlm::rms_norm_fwd);
   m.def("rms_norm_bwd", &vlm::rms_norm_bwd);
   m.def("layer_norm_fwd", &vlm::layer_norm_fwd);

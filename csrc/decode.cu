@@ -209,62 +209,99 @@ at::Tensor dec_swiglu(at::Tensor ws, std::vector<int64_t> meta, c10::optional<at
 
 // ------------------------------------------------------------------ tensor-parallel decode consumers
 // Row-parallel GEMMs (o_proj, down_proj) leave each rank with a partial sum of the full [B, H] output.
-// dec_resnorm_tp_kernel all-reduces it over NVLink inside the consumer: CTA `row` (1) sums this rank's
-// stream-K slots of its row into the rank's IPC-shared row buffer, (2) publishes flag[point][row][rank]
-// = epoch on every peer, (3) waits (bounded) for every peer's flag of the same row, (4) sums all ranks'
-// row buffers in rank order (identical on every rank), adds the residual and applies the RMSNorm.
-// Per-row flags make the exchange fine grained: no grid-wide barrier.  A rank's row buffer for a point
-// is rewritten one decode step later, after the rank has seen every peer's flag of the next point,
-// i.e. after every peer finished reading it.
+// dec_resnorm_tp_kernel all-reduces it over NVLink inside the consumer, with no fence and no separate
+// flag on the critical path.  Every value travels with the step's tag in one 8-byte word: fp32 bits in
+// the low half, the low 32 bits of the device-side step epoch in the high half.  CTA `row` (1) sums this
+// rank's stream-K slots of its row and stores the tagged words straight into slot `rank` of every
+// rank's buffer ([W][max_batch][H] words per point), (2) polls its own buffer until every rank's word of
+// its columns carries the tag (bounded), (3) adds the ranks' values in rank order (identical on every
+// rank), then the residual, and applies the RMSNorm.  An aligned 8-byte store is single-copy atomic, so
+// a reader sees a word whole: old tag (keep polling) or new tag with its value.  Critical path: one
+// one-way NVLink store instead of a fence, a flag and a remote read.  A rank overwrites a peer's slot of
+// a point one decode step later, after it has seen that peer's words of a later point, which the peer
+// stores only after its kernel for this point (and its reads) completed.
 __global__ void tp_step_begin_kernel(unsigned long long* epoch) {
   pdl_wait();
   pdl_trigger();
   if (threadIdx.x == 0) epoch[0] += 1ull;
 }
 
+VLM_DEV unsigned long long tag_word(float v, unsigned tag) {
+  return (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+}
+VLM_DEV void st_tagged2(unsigned long long* a, unsigned long long w0, unsigned long long w1) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(a), "l"(w0), "l"(w1) : "memory");
+}
+VLM_DEV void ld_tagged2(const unsigned long long* a, unsigned long long& w0, unsigned long long& w1) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(a) : "memory");
+}
+
 __global__ void dec_resnorm_tp_kernel(const float* __restrict__ ws, SkMeta m, const bf16* __restrict__ res,
                                       const bf16* __restrict__ w, bf16* __restrict__ h_out, bf16* __restrict__ hn_out,
-                                      int H, float eps, PeerTable rows, PeerTable sigs, int64_t flag_base,
+                                      int H, float eps, PeerTable slots, int max_batch,
                                       const unsigned long long* __restrict__ epoch_ptr, int rank, int W, int* err) {
   __shared__ float red[32];
   __shared__ int ok;
   pdl_wait();
   pdl_trigger();
   const int row = blockIdx.x, col = threadIdx.x * 8;
-  const unsigned long long epoch = *epoch_ptr;
+  const unsigned tag = static_cast<unsigned>(*epoch_ptr);
+  if (threadIdx.x == 0) ok = 1;
   float x[8];
-  const int64_t off = static_cast<int64_t>(row) * H + col;
   if (col < H) {
     sk_sum8(ws, m, row, col, x);
-    float* mine = reinterpret_cast<float*>(rows.p[rank]) + off;
-    reinterpret_cast<float4*>(mine)[0] = make_float4(x[0], x[1], x[2], x[3]);
-    reinterpret_cast<float4*>(mine)[1] = make_float4(x[4], x[5], x[6], x[7]);
+    const int64_t off = (static_cast<int64_t>(rank) * max_batch + row) * H + col;
+    for (int p = 0; p < W; ++p) {
+      unsigned long long* dst = reinterpret_cast<unsigned long long*>(slots.p[p]) + off;
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) st_tagged2(dst + i, tag_word(x[i], tag), tag_word(x[i + 1], tag));
+    }
   }
-  __threadfence_system();
-  __syncthreads();
-  const int64_t fb = flag_base + static_cast<int64_t>(row) * W;
-  if (threadIdx.x < W && static_cast<int>(threadIdx.x) != rank)
-    store_release_sys(reinterpret_cast<unsigned long long*>(sigs.p[threadIdx.x]) + fb + rank, epoch);
-  if (threadIdx.x == 0) ok = wait_peers_at(reinterpret_cast<const unsigned long long*>(sigs.p[rank]), fb, W, rank, epoch, err);
+  __syncthreads();  // ok = 1 is seen before any thread can clear it
+  float sum[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) sum[i] = 0.f;
+  if (col < H) {
+    const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(slots.p[rank]);
+    const long long t0 = clock64();
+    bool good = true;
+    for (int p = 0; p < W && good; ++p) {
+      if (p == rank) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum[i] += x[i];
+        continue;
+      }
+      const unsigned long long* src = mine + (static_cast<int64_t>(p) * max_batch + row) * H + col;
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        unsigned long long w0, w1;
+        ld_tagged2(src + i, w0, w1);
+        while (static_cast<unsigned>(w0 >> 32) != tag || static_cast<unsigned>(w1 >> 32) != tag) {
+          if (clock64() - t0 > kPeerWait) {
+            atomicCAS(err, 0, kErrTimeoutPeer);
+            good = false;
+            break;
+          }
+          ld_tagged2(src + i, w0, w1);
+        }
+        sum[i] += __uint_as_float(static_cast<unsigned>(w0));
+        sum[i + 1] += __uint_as_float(static_cast<unsigned>(w1));
+      }
+    }
+    if (!good) ok = 0;
+  }
   __syncthreads();
   if (!ok) return;
   float ss = 0.f;
+  const int64_t off = static_cast<int64_t>(row) * H + col;
   if (col < H) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) x[i] = 0.f;
-    for (int p = 0; p < W; ++p) {
-      const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(rows.p[p]) + off);
-      const float4 a = src[0], b = src[1];
-      x[0] += a.x; x[1] += a.y; x[2] += a.z; x[3] += a.w;
-      x[4] += b.x; x[5] += b.y; x[6] += b.z; x[7] += b.w;
-    }
     const uint4 rv = *reinterpret_cast<const uint4*>(res + off);
     const uint32_t u[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 f = unpack_bf16x2(u[j]);
-      x[2 * j] = bf2f(f2bf(x[2 * j] + f.x));
-      x[2 * j + 1] = bf2f(f2bf(x[2 * j + 1] + f.y));
+      x[2 * j] = bf2f(f2bf(sum[2 * j] + f.x));
+      x[2 * j + 1] = bf2f(f2bf(sum[2 * j + 1] + f.y));
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
@@ -294,18 +331,18 @@ void tp_step_begin(int64_t epoch_ptr, int64_t device) {
              reinterpret_cast<unsigned long long*>(epoch_ptr));
 }
 
-// h = residual + all-reduce over ranks of this rank's partials; hn = rms_norm(h) * w.  `rows` / `sigs` are
-// the per-rank addresses of the IPC-shared row buffer of this point ([B, H] fp32) and of the flag pad.
+// h = residual + all-reduce over ranks of this rank's partials; hn = rms_norm(h) * w.  `slots` are the
+// per-rank addresses of the IPC-shared word buffer of this point ([W][max_batch][H] tagged 8-byte words).
 std::tuple<at::Tensor, at::Tensor> dec_residual_norm_tp(at::Tensor ws, std::vector<int64_t> meta, at::Tensor res,
-                                                        at::Tensor w, double eps, std::vector<int64_t> rows,
-                                                        int64_t rows_off_bytes, std::vector<int64_t> sigs,
-                                                        int64_t flag_base, int64_t epoch_ptr, int64_t rank) {
+                                                        at::Tensor w, double eps, std::vector<int64_t> slots,
+                                                        int64_t slot_off_bytes, int64_t max_batch, int64_t epoch_ptr,
+                                                        int64_t rank) {
   const SkMeta m = meta_of(meta);
   const int H = m.N;
-  const int W = static_cast<int>(rows.size());
+  const int W = static_cast<int>(slots.size());
   TORCH_CHECK(H % 8 == 0 && H / 8 <= 1024, "dec_residual_norm_tp: H must be a multiple of 8 and <= 8192");
-  TORCH_CHECK(static_cast<int>(sigs.size()) == W && rank >= 0 && rank < W, "dec_residual_norm_tp: tables");
-  TORCH_CHECK(rows_off_bytes % 16 == 0, "dec_residual_norm_tp: row buffer alignment");
+  TORCH_CHECK(rank >= 0 && rank < W && m.M <= max_batch, "dec_residual_norm_tp: rank / batch");
+  TORCH_CHECK(slot_off_bytes % 16 == 0, "dec_residual_norm_tp: slot buffer alignment");
   const c10::cuda::CUDAGuard g(ws.device());
   at::Tensor h = at::empty({m.M, H}, res.options());
   at::Tensor hn = at::empty({m.M, H}, res.options());
@@ -313,8 +350,8 @@ std::tuple<at::Tensor, at::Tensor> dec_residual_norm_tp(at::Tensor ws, std::vect
   launch_pdl(dec_resnorm_tp_kernel, dim3(m.M), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
              ws.data_ptr<float>(), m, reinterpret_cast<const bf16*>(res.data_ptr()),
              reinterpret_cast<const bf16*>(w.data_ptr()), reinterpret_cast<bf16*>(h.data_ptr()),
-             reinterpret_cast<bf16*>(hn.data_ptr()), H, static_cast<float>(eps), make_peer_table(rows, rows_off_bytes),
-             make_peer_table(sigs), flag_base, reinterpret_cast<const unsigned long long*>(epoch_ptr),
+             reinterpret_cast<bf16*>(hn.data_ptr()), H, static_cast<float>(eps), make_peer_table(slots, slot_off_bytes),
+             static_cast<int>(max_batch), reinterpret_cast<const unsigned long long*>(epoch_ptr),
              static_cast<int>(rank), W, err_word(ws.device().index()));
   return {h, hn};
 }

@@ -122,9 +122,9 @@ void vocab_logprob_bwd(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tenso
 // decode.cu (tensor-parallel decode)
 void tp_step_begin(int64_t epoch_ptr, int64_t device);
 std::tuple<at::Tensor, at::Tensor> dec_residual_norm_tp(at::Tensor ws, std::vector<int64_t> meta, at::Tensor res,
-                                                        at::Tensor w, double eps, std::vector<int64_t> rows,
-                                                        int64_t rows_off_bytes, std::vector<int64_t> sigs,
-                                                        int64_t flag_base, int64_t epoch_ptr, int64_t rank);
+                                                        at::Tensor w, double eps, std::vector<int64_t> slots,
+                                                        int64_t slot_off_bytes, int64_t max_batch, int64_t epoch_ptr,
+                                                        int64_t rank);
 
 // symm.cu (peer-memory collectives)
 int64_t symm_alloc(int64_t bytes, int64_t device);

@@ -131,8 +131,9 @@ def main() -> None:
 
     # ---- tensor-parallel decode consumer: 64 x 2560 partial rows all-reduced inside the kernel
     B, H = 64, 2560
-    rows = SymmetricBuffer(2 * B * H * 4, None, dev)     # two points, used alternately: a row buffer is
-    flags_tp = SymmetricBuffer(2 * B * W * 8, None, dev)    # rewritten only after every peer passed the other
+    # two points, used alternately: a rank's slot of a point is rewritten only after every peer passed the other
+    point_bytes = W * B * H * 8
+    slots = SymmetricBuffer(2 * point_bytes, None, dev)
     it = [0]
     ep = torch.zeros(1, dtype=torch.int64, device=dev)
     x = torch.randn(B, 2048 // W, device=dev).to(torch.bfloat16)
@@ -145,16 +146,15 @@ def main() -> None:
         pt = it[0] % 2
         it[0] += 1
         ext().tp_step_begin(ep.data_ptr(), local)
-        ext().dec_residual_norm_tp(ws, list(meta), res, nw, 1e-6, rows.ptrs, pt * B * H * 4, flags_tp.ptrs, pt * B * W,
-                                   ep.data_ptr(), r)
+        ext().dec_residual_norm_tp(ws, list(meta), res, nw, 1e-6, slots.ptrs, pt * point_bytes, B, ep.data_ptr(), r)
 
     ms = _timed(tp_consumer, iters=50)
     ops.check_errors(local)
-    link_bytes = (W - 1) * B * H * 4
+    link_bytes = (W - 1) * B * H * 4   # the fp32 payload (the tags are protocol overhead)
     ideal = link_bytes / (LINK_GBS * 1e9) * 1e3
     out.append({"case": f"dec_residual_norm_tp_{B}x{H}", "world": W, "ms": round(ms, 4),
                 "roofline_ms": round(ideal, 4), "frac_of_roofline": round(ideal / ms, 3),
-                "note": "latency-bound: one flag round trip per row"})
+                "note": "latency-bound: one one-way NVLink store per row, then the slowest rank"})
     red = torch.randn(B, H, device=dev)
     ms_nccl = _timed(lambda: dist.all_reduce(red), iters=50)
     out.append({"case": f"nccl_all_reduce_fp32_{B}x{H}", "world": W, "ms": round(ms_nccl, 4)})
@@ -207,7 +207,7 @@ def main() -> None:
             print(json.dumps(row), flush=True)
     torch.cuda.synchronize()
     dist.barrier()
-    for b in (grads, sig, params, rows, flags_tp, wsh):
+    for b in (grads, sig, params, slots, wsh):
         b.close()
     dist.destroy_process_group()
 

@@ -8,9 +8,11 @@ weights (Megatron-style split, rebuilt for the decode step):
   cache holds only the local kv heads, so attention needs no communication;
 * o_proj and down_proj: row-parallel; their stream-K partial sums are
   all-reduced INSIDE the residual + RMSNorm consumer kernel
-  (``dec_residual_norm_tp``): each CTA publishes its row of partials in an
-  IPC-shared buffer, flags every peer, waits for theirs and sums all ranks in
-  rank order — so every rank ends with bitwise-identical activations;
+  (``dec_residual_norm_tp``): each CTA stores its row of partials, every
+  value tagged with the step epoch in one 8-byte word, into this rank's slot
+  of every rank's IPC-shared buffer, polls its own buffer until all ranks'
+  words carry the tag, and sums all ranks in rank order — so every rank ends
+  with bitwise-identical activations, after one one-way NVLink store;
 * gate/up: column-parallel (interleaved gate/up row pairs stay together);
 * embedding, final norm, lm_head and the sampler are replicated: every rank
   computes the same logits and, with the same Philox seed, samples the same
@@ -21,7 +23,7 @@ rollout); the local kv heads are then copied into the tensor-parallel cache.
 Shards are re-sliced from the model's (gathered) parameters whenever they
 changed (``refresh``), into buffers at fixed addresses so a captured decode
 graph stays valid.  Synchronisation uses a device-side step counter (epoch)
-advanced by the first kernel of every step; flags are monotonic, so nothing is
+advanced by the first kernel of every step; tags only grow, so nothing is
 ever reset, and every wait is bounded (error code instead of a hang).
 
 No reference counterpart: the reference decodes on one device
@@ -68,8 +70,9 @@ class TPDecoder:
         self.gu_w = torch.empty(L, 2 * self.F_l, H, dtype=dt, device=dev)
         self.down_w = torch.empty(L, H, self.F_l, dtype=dt, device=dev)
         self.points = 2 * L
-        self.rows = SymmetricBuffer(self.points * self.max_batch * H * 4, group, dev)
-        self.sigs = SymmetricBuffer(self.points * self.max_batch * W * 8, group, dev)
+        # per reduction point: [W source ranks][max_batch][H] tagged 8-byte words (zeroed: tags start at 1)
+        self.point_bytes = W * self.max_batch * H * 8
+        self.slots = SymmetricBuffer(self.points * self.point_bytes, group, dev)
         self.epoch = torch.zeros(1, dtype=torch.int64, device=dev)
         self.version = None
         self.eps = t.rms_norm_eps
@@ -113,10 +116,8 @@ class TPDecoder:
 
     # ---------------------------------------------------------------- decode
     def _reduce_norm(self, ws, meta, res, w, point: int):
-        H, B = self.H, self.max_batch
-        return ext().dec_residual_norm_tp(ws, list(meta), res, w, float(self.eps), self.rows.ptrs,
-                                          point * B * H * 4, self.sigs.ptrs, point * B * self.world,
-                                          self.epoch.data_ptr(), self.rank)
+        return ext().dec_residual_norm_tp(ws, list(meta), res, w, float(self.eps), self.slots.ptrs,
+                                          point * self.point_bytes, self.max_batch, self.epoch.data_ptr(), self.rank)
 
     @torch.no_grad()
     def decode_step(self, tokens: torch.Tensor, cache: KVCache, rope_delta: torch.Tensor) -> torch.Tensor:
@@ -150,8 +151,7 @@ class TPDecoder:
         return dec.final_logits(params, xn, normed=True)
 
     def close(self) -> None:
-        for b in (self.rows, self.sigs):
-            b.close()
+        self.slots.close()
 
 
 def tp_partition(world: int, tp_size: int):
