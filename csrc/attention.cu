@@ -22,6 +22,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "kv_layout.cuh"
 #include "host_utils.h"
 #include "mma_sync.cuh"
 #include "vlm_noalloc.h"
@@ -576,8 +577,9 @@ template <int D, int REP, int NW = 8, int KC = 32, int STAGES = 4>
 __global__ void __launch_bounds__(NW * 32) decode_attn_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
                                                               const bf16* __restrict__ vc, const int* __restrict__ lens,
                                                               bf16* __restrict__ o, float* __restrict__ part, int Hq,
-                                                              int Hkv, int Tmax, float scale_log2, int splits,
+                                                              KvLayout lay, float scale_log2, int splits,
                                                               int* err) {
+  static_assert(kKvBlock % KC == 0, "a key chunk must not straddle a cache block");
   constexpr int ND = D / 32;
   constexpr int KPW = KC / NW;  // keys per warp per stage
   constexpr int CHUNK = KC * D * 2;
@@ -593,14 +595,13 @@ __global__ void __launch_bounds__(NW * 32) decode_attn_kernel(const bf16* __rest
   pdl_wait();
   pdl_trigger();
   const int hk = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
-  const int L = min(lens[b], Tmax);
-  const int per = (L + splits - 1) / splits;
+  const int L = min(lens[b], lay.cap);
+  int per = (L + splits - 1) / splits;
+  if (lay.table) per = (per + kKvBlock - 1) / kKvBlock * kKvBlock;  // splits start on block boundaries
   const int k0 = sp * per, k1 = min(L, k0 + per);
   const int nk = max(0, k1 - k0);
   const int nchunks = (nk + KC - 1) / KC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bf16* kbase = kc + ((static_cast<int64_t>(b) * Hkv + hk) * Tmax + k0) * D;
-  const bf16* vbase = vc + ((static_cast<int64_t>(b) * Hkv + hk) * Tmax + k0) * D;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -612,9 +613,11 @@ __global__ void __launch_bounds__(NW * 32) decode_attn_kernel(const bf16* __rest
     const int st = c % STAGES;
     const int keys = min(KC, nk - c * KC);
     const uint32_t bytes = static_cast<uint32_t>(keys) * D * 2;
+    // the chunk's keys are consecutive rows of one (sequence or block, head) run
+    const int64_t row = kv_row(lay, b, hk, k0 + c * KC);
     mbar_arrive_expect_tx(&full[st], 2 * bytes);
-    bulk_load(sK + st * KC * D, kbase + static_cast<int64_t>(c) * KC * D, bytes, &full[st]);
-    bulk_load(sV + st * KC * D, vbase + static_cast<int64_t>(c) * KC * D, bytes, &full[st]);
+    bulk_load(sK + st * KC * D, kc + row * D, bytes, &full[st]);
+    bulk_load(sV + st * KC * D, vc + row * D, bytes, &full[st]);
   };
   if (threadIdx.x == 0)
     for (int c = 0; c < STAGES && c < nchunks; ++c) issue(c);
@@ -766,10 +769,11 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_consta
                                                              const __grid_constant__ CUtensorMap tmV,
                                                              const bf16* __restrict__ q, const int* __restrict__ lens,
                                                              bf16* __restrict__ o, float* __restrict__ part, int Hq,
-                                                             int Hkv, int Tmax, float scale_log2, int splits, int* err,
+                                                             KvLayout lay, float scale_log2, int splits, int* err,
                                                              L2Prefetch pf, const int* __restrict__ lead,
                                                              const int* __restrict__ share_len) {
   constexpr int D = 128, KC = 64;
+  static_assert(KC == kKvBlock, "one TMA box of keys per cache block");
   constexpr int HALF = KC * 64;  // elements of one 64x64 box
   extern __shared__ __align__(1024) uint8_t tc_raw[];
   bf16* sm = reinterpret_cast<bf16*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
@@ -782,8 +786,9 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_consta
   pdl_wait();
   pdl_trigger();
   const int hk = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
-  const int L = min(lens[b], Tmax);
-  const int per = (L + splits - 1) / splits;
+  const int L = min(lens[b], lay.cap);
+  int per = (L + splits - 1) / splits;
+  if (lay.table) per = (per + kKvBlock - 1) / kKvBlock * kKvBlock;  // splits start on block boundaries
   const int k0 = sp * per, k1 = min(L, k0 + per);
   const int nk = max(0, k1 - k0);
   const int nchunks = (nk + KC - 1) / KC;
@@ -804,7 +809,7 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_consta
     const int st = c % STAGES;
     mbar_arrive_expect_tx(&full[st], 4 * HALF * 2);
     const int t0 = k0 + c * KC;
-    const int y = ((t0 + KC <= src_share ? src_lead : b) * Hkv + hk) * Tmax + t0;
+    const int y = static_cast<int>(kv_row(lay, t0 + KC <= src_share ? src_lead : b, hk, t0));
     tma_load_2d(sK + (st * 2 + 0) * HALF, &tmK, &full[st], 0, y);
     tma_load_2d(sK + (st * 2 + 1) * HALF, &tmK, &full[st], 64, y);
     tma_load_2d(sV + (st * 2 + 0) * HALF, &tmV, &full[st], 0, y);
@@ -1109,10 +1114,10 @@ void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, a
 
 template <int D, int REP>
 static void decode_dispatch(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& lens,
-                            at::Tensor& o, float scale) {
+                            at::Tensor& o, float scale, const KvLayout& lay) {
   constexpr int NW = 8, KC = 32, STAGES = 4;
-  const int B = static_cast<int>(q.size(0)), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(kc.size(1));
-  const int Tmax = static_cast<int>(kc.size(2));
+  const int B = static_cast<int>(q.size(0)), Hq = static_cast<int>(q.size(1)), Hkv = lay.Hkv;
+  const int Tmax = lay.cap;
   const int sms = num_sms(q.device().index());
   // ~3 CTAs per SM; each split keeps >= 2 chunks of keys
   const int splits = std::max(1, std::min((3 * sms + B * Hkv - 1) / (B * Hkv), Tmax / (2 * KC)));
@@ -1129,7 +1134,7 @@ static void decode_dispatch(const at::Tensor& q, const at::Tensor& kc, const at:
   launch_pdl(kern, dim3(Hkv, B, splits), dim3(NW * 32), smem, st, reinterpret_cast<const bf16*>(q.data_ptr()),
              reinterpret_cast<const bf16*>(kc.data_ptr()), reinterpret_cast<const bf16*>(vc.data_ptr()),
              lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()), splits > 1 ? part.data_ptr<float>() : nullptr,
-             Hq, Hkv, Tmax, scale * kLog2e, splits, err_word(q.device().index()));
+             Hq, lay, scale * kLog2e, splits, err_word(q.device().index()));
   if (splits > 1) {
     launch_pdl(decode_combine_kernel, dim3(B * Hq), dim3(128), 0, st, part.data_ptr<float>(),
                reinterpret_cast<bf16*>(o.data_ptr()), B * Hq, splits, D);
@@ -1138,10 +1143,11 @@ static void decode_dispatch(const at::Tensor& q, const at::Tensor& kc, const at:
 
 template <int REP>
 static void decode_tc_dispatch(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& lens,
-                               at::Tensor& o, float scale, L2Prefetch pf, const int* lead, const int* share_len) {
+                               at::Tensor& o, float scale, L2Prefetch pf, const int* lead, const int* share_len,
+                               const KvLayout& lay) {
   constexpr int STAGES = 3, D = 128;
-  const int B = static_cast<int>(q.size(0)), Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(kc.size(1));
-  const int Tmax = static_cast<int>(kc.size(2));
+  const int B = static_cast<int>(q.size(0)), Hq = static_cast<int>(q.size(1)), Hkv = lay.Hkv;
+  const int Tmax = lay.cap;
   const int sms = num_sms(q.device().index());
   // Key splits: enough CTAs for two per SM.  (Forcing two splits whenever one split leaves a partial last
   // wave measured slower: 4.70 vs 4.36 ms per 4B decode step at batch 64, cache length 390.)
@@ -1149,7 +1155,8 @@ static void decode_tc_dispatch(const at::Tensor& q, const at::Tensor& kc, const 
   int splits = std::max(1, std::min((2 * sms + B * Hkv - 1) / (B * Hkv), Tmax / 128));
   if (const char* e = std::getenv("VLMRL_DECODE_SPLITS")) splits = std::max(1, std::atoi(e));
   const int smem = 1024 + STAGES * 4 * 64 * 64 * 2 + STAGES * 8 + 4 * REP * (D + 2) * 4;
-  const int64_t rows = static_cast<int64_t>(B) * Hkv * Tmax;
+  const int64_t rows = kc.size(0) * kc.size(1) * kc.size(2);  // every row of the layer (or of the block pool)
+  TORCH_CHECK(rows < (int64_t(1) << 31), "decode_attn: cache layer too large for 32-bit TMA rows");
   const CUtensorMap tk = make_tmap_2d_bf16(kc.data_ptr(), D, rows, D, 64, 64);
   const CUtensorMap tv = make_tmap_2d_bf16(vc.data_ptr(), D, rows, D, 64, 64);
   auto kern = decode_attn_tc_kernel<REP, STAGES>;
@@ -1159,7 +1166,7 @@ static void decode_tc_dispatch(const at::Tensor& q, const at::Tensor& kc, const 
   if (splits > 1) part = at::empty({B, Hq, splits, D + 2}, q.options().dtype(at::kFloat));
   launch_pdl(kern, dim3(Hkv, B, splits), dim3(128), smem, st, tk, tv, reinterpret_cast<const bf16*>(q.data_ptr()),
              lens.data_ptr<int>(), reinterpret_cast<bf16*>(o.data_ptr()), splits > 1 ? part.data_ptr<float>() : nullptr,
-             Hq, Hkv, Tmax, scale * kLog2e, splits, err_word(q.device().index()), pf, lead, share_len);
+             Hq, lay, scale * kLog2e, splits, err_word(q.device().index()), pf, lead, share_len);
   if (splits > 1) {
     launch_pdl(decode_combine_kernel, dim3(B * Hq), dim3(128), 0, st, part.data_ptr<float>(),
                reinterpret_cast<bf16*>(o.data_ptr()), B * Hq, splits, D);
@@ -1168,10 +1175,14 @@ static void decode_tc_dispatch(const at::Tensor& q, const at::Tensor& kc, const 
 
 void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale,
                  c10::optional<at::Tensor> prefetch, c10::optional<at::Tensor> lead,
-                 c10::optional<at::Tensor> share_len) {
+                 c10::optional<at::Tensor> share_len, c10::optional<at::Tensor> block_table) {
   TORCH_CHECK(q.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(), "decode_attn: contiguous");
   TORCH_CHECK(lens.scalar_type() == at::kInt, "decode_attn: int32 lengths");
   if (q.size(0) == 0) return;
+  const KvLayout lay = kv_layout_of(kc, block_table);
+  TORCH_CHECK(vc.sizes() == kc.sizes() && (lay.table == nullptr ? kc.size(0) == q.size(0)
+                                                                 : block_table->size(0) == q.size(0)),
+              "decode_attn: cache / block table rows must match the batch");
   const c10::cuda::CUDAGuard g(q.device());
   const int D = static_cast<int>(q.size(2));
   const int rep = static_cast<int>(q.size(1) / kc.size(1));
@@ -1185,11 +1196,11 @@ void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at
   }
   const int* ld = share ? lead->data_ptr<int>() : nullptr;
   const int* sl = share ? share_len->data_ptr<int>() : nullptr;
-  if (D == 128 && rep == 4) return decode_tc_dispatch<4>(q, kc, vc, lens, o, sc, pf, ld, sl);
-  if (D == 128 && rep == 2) return decode_tc_dispatch<2>(q, kc, vc, lens, o, sc, pf, ld, sl);
-  if (D == 128 && rep == 8) return decode_tc_dispatch<8>(q, kc, vc, lens, o, sc, pf, ld, sl);
+  if (D == 128 && rep == 4) return decode_tc_dispatch<4>(q, kc, vc, lens, o, sc, pf, ld, sl, lay);
+  if (D == 128 && rep == 2) return decode_tc_dispatch<2>(q, kc, vc, lens, o, sc, pf, ld, sl, lay);
+  if (D == 128 && rep == 8) return decode_tc_dispatch<8>(q, kc, vc, lens, o, sc, pf, ld, sl, lay);
 #define VLM_DEC(DD, RR) \
-  if (D == DD && rep == RR) return decode_dispatch<DD, RR>(q, kc, vc, lens, o, sc);
+  if (D == DD && rep == RR) return decode_dispatch<DD, RR>(q, kc, vc, lens, o, sc, lay);
   VLM_DEC(128, 4) VLM_DEC(128, 2) VLM_DEC(128, 1) VLM_DEC(128, 8) VLM_DEC(64, 4) VLM_DEC(64, 2) VLM_DEC(64, 1)
   VLM_DEC(32, 2) VLM_DEC(32, 4) VLM_DEC(32, 1)
 #undef VLM_DEC
@@ -1274,8 +1285,9 @@ int noalloc_decode_launch(const bf16* q, const bf16* kc, const bf16* vc, const i
   const int smem = 2 * STAGES * KC * D * 2 + STAGES * 8 + (2 * NW * REP + NW * REP * D) * 4;
   auto kern = decode_attn_kernel<D, REP, NW, KC, STAGES>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -3;
-  kern<<<dim3(Hkv, B, splits), NW * 32, smem, st>>>(q, kc, vc, lens, o, s.scratch, Hq, Hkv, Tmax, scale * kLog2e,
-                                                     splits, s.status);
+  const KvLayout lay{nullptr, 0, Tmax, Hkv, Tmax};  // contiguous [B, Hkv, Tmax, D]
+  kern<<<dim3(Hkv, B, splits), NW * 32, smem, st>>>(q, kc, vc, lens, o, s.scratch, Hq, lay, scale * kLog2e, splits,
+                                                     s.status);
   if (cudaGetLastError() != cudaSuccess) return -3;
   decode_combine_kernel<<<B * Hq, 128, 0, st>>>(s.scratch, o, B * Hq, splits, D);
   if (cudaGetLastError() != cudaSuccess) return -3;

@@ -17,7 +17,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_static_weights", &vlm::set_static_weights);
   m.def("dec_qkv", &vlm::dec_qkv, py::arg("ws"), py::arg("meta"), py::arg("bias"), py::arg("qw"), py::arg("kw"),
         py::arg("lengths"), py::arg("delta"), py::arg("inv_freq"), py::arg("kc"), py::arg("vc"), py::arg("nq"),
-        py::arg("nkv"), py::arg("eps"), py::arg("prefetch") = py::none());
+        py::arg("nkv"), py::arg("eps"), py::arg("prefetch") = py::none(), py::arg("block_table") = py::none());
   m.def("dec_residual_norm", &vlm::dec_residual_norm, py::arg("ws"), py::arg("meta"), py::arg("residual"), py::arg("w"),
         py::arg("eps"), py::arg("prefetch") = py::none());
   m.def("dec_swiglu", &vlm::dec_swiglu, py::arg("ws"), py::arg("meta"), py::arg("prefetch") = py::none());
@@ -36,7 +36,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed", &vlm::embed);
   m.def("scatter_rows", &vlm::scatter_rows);
   m.def("embed_bwd", &vlm::embed_bwd);
-  m.def("kv_write", &vlm::kv_write);
+  m.def("kv_write", &vlm::kv_write, py::arg("k"), py::arg("v"), py::arg("kc"), py::arg("vc"), py::arg("seq"),
+        py::arg("pos"), py::arg("block_table") = py::none());
   m.def("adamw", &vlm::adamw);
   m.def("sq_norm_acc", &vlm::sq_norm_acc);
   m.def("patchify", &vlm::patchify);
@@ -47,7 +48,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("causal"), py::arg("scale"), py::arg("pre") = py::none(), py::arg("xq") = py::none());
   m.def("decode_attn", &vlm::decode_attn, py::arg("q"), py::arg("kc"), py::arg("vc"), py::arg("lens"), py::arg("o"),
         py::arg("scale"), py::arg("prefetch") = py::none(), py::arg("lead") = py::none(),
-        py::arg("share_len") = py::none());
+        py::arg("share_len") = py::none(), py::arg("block_table") = py::none());
   m.def("sample", &vlm::sample);
   m.def("lm_head_sample", &vlm::lm_head_sample, "lm_head GEMM with a top-k epilogue + merge / top-p / Philox draw");
   m.def("vocab_logprob_fwd", &vlm::vocab_logprob_fwd);

@@ -9,6 +9,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "kv_layout.cuh"
 #include "host_utils.h"
 #include "peer.cuh"
 #include "streamk.cuh"
@@ -35,7 +36,7 @@ __global__ void dec_qkv_kernel(const float* __restrict__ ws, SkMeta m, const bf1
                                const bf16* __restrict__ qw, const bf16* __restrict__ kw, const int* __restrict__ lengths,
                                const int64_t* __restrict__ delta, const float* __restrict__ inv_freq,
                                bf16* __restrict__ q, bf16* __restrict__ kc, bf16* __restrict__ vc, int nq, int nkv,
-                               int Tmax, float eps, L2Prefetch pf) {
+                               KvLayout lay, float eps, L2Prefetch pf) {
   constexpr int TPH = D / 8;
   l2_prefetch_share(pf);
   pdl_wait();
@@ -64,7 +65,7 @@ __global__ void dec_qkv_kernel(const float* __restrict__ ws, SkMeta m, const bf1
 #pragma unroll
   for (int i = 0; i < 8; ++i) y[i] = __shfl_xor_sync(0xffffffffu, xn[i], TPH / 2);
   if (is_v) {
-    store8(vc + ((static_cast<int64_t>(row) * nkv + (head - nq - nkv)) * Tmax + len) * D + t * 8, x);
+    if (len < lay.cap) store8(vc + kv_row(lay, row, head - nq - nkv, len) * D + t * 8, x);
     return;
   }
   const float pos = static_cast<float>(static_cast<int64_t>(len) + delta[row]);
@@ -78,8 +79,8 @@ __global__ void dec_qkv_kernel(const float* __restrict__ ws, SkMeta m, const bf1
   }
   if (is_q)
     store8(q + (static_cast<int64_t>(row) * nq + head) * D + t * 8, out);
-  else
-    store8(kc + ((static_cast<int64_t>(row) * nkv + (head - nq)) * Tmax + len) * D + t * 8, out);
+  else if (len < lay.cap)
+    store8(kc + kv_row(lay, row, head - nq, len) * D + t * 8, out);
 }
 
 // One CTA per row; thread i owns columns [8i, 8i+8).
@@ -146,11 +147,13 @@ __global__ void dec_swiglu_kernel(const float* __restrict__ ws, SkMeta m, bf16* 
 
 at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at::Tensor qw, at::Tensor kw,
                    at::Tensor lengths, at::Tensor delta, at::Tensor inv_freq, at::Tensor kc, at::Tensor vc, int64_t nq,
-                   int64_t nkv, double eps, c10::optional<at::Tensor> prefetch) {
+                   int64_t nkv, double eps, c10::optional<at::Tensor> prefetch,
+                   c10::optional<at::Tensor> block_table) {
   const SkMeta m = meta_of(meta);
   const L2Prefetch pf = l2_prefetch_of<L2Prefetch>(prefetch);
   const int D = static_cast<int>(kc.size(-1));
-  const int Tmax = static_cast<int>(kc.size(-2));
+  const KvLayout lay = kv_layout_of(kc, block_table);
+  TORCH_CHECK(lay.Hkv == nkv && vc.sizes() == kc.sizes(), "dec_qkv: cache heads / shapes");
   TORCH_CHECK(m.N == (nq + 2 * nkv) * D, "dec_qkv: width mismatch");
   TORCH_CHECK(lengths.scalar_type() == at::kInt && delta.scalar_type() == at::kLong, "dec_qkv: int32 lengths, int64 deltas");
   TORCH_CHECK(kc.is_contiguous() && vc.is_contiguous(), "dec_qkv: contiguous cache layer");
@@ -166,7 +169,7 @@ at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at
                kw.defined() && kw.numel() ? reinterpret_cast<const bf16*>(kw.data_ptr()) : nullptr,
                lengths.data_ptr<int>(), delta.data_ptr<int64_t>(), inv_freq.data_ptr<float>(),
                reinterpret_cast<bf16*>(q.data_ptr()), reinterpret_cast<bf16*>(kc.data_ptr()),
-               reinterpret_cast<bf16*>(vc.data_ptr()), static_cast<int>(nq), static_cast<int>(nkv), Tmax,
+               reinterpret_cast<bf16*>(vc.data_ptr()), static_cast<int>(nq), static_cast<int>(nkv), lay,
                static_cast<float>(eps), pf);
   };
   if (D == 128)

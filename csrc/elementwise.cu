@@ -10,6 +10,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "kv_layout.cuh"
 #include "host_utils.h"
 
 namespace vlm {
@@ -720,33 +721,37 @@ void embed_bwd(at::Tensor tokens, at::Tensor dh, at::Tensor dtable) {
 }
 
 // ------------------------------------------------------------------ KV-cache write
-// k, v [T, Hkv, D] -> cache [B, Hkv, Tmax, D] at (seq[t], pos[t])
+// k, v [T, Hkv, D] -> the cache layer (contiguous or paged, KvLayout) at (seq[t], pos[t])
 __global__ void kv_write_kernel(const bf16* __restrict__ k, const bf16* __restrict__ v, bf16* __restrict__ kc,
                                 bf16* __restrict__ vc, const int64_t* __restrict__ seq, const int64_t* __restrict__ pos,
-                                int T, int Hkv, int Tmax, int D) {
+                                int T, KvLayout lay, int D) {
   const int t = blockIdx.x;
   if (t >= T) return;
   const int64_t s = seq[t], p = pos[t];
-  if (p < 0 || p >= Tmax) return;
+  if (p < 0 || p >= lay.cap) return;
+  const int Hkv = lay.Hkv;
   for (int i = threadIdx.x; i < Hkv * D / 8; i += blockDim.x) {
     const int h = (i * 8) / D, d = (i * 8) % D;
     const int64_t src = (static_cast<int64_t>(t) * Hkv + h) * D + d;
-    const int64_t dst = ((s * Hkv + h) * Tmax + p) * D + d;
+    const int64_t dst = kv_row(lay, static_cast<int>(s), h, static_cast<int>(p)) * D + d;
     *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(k + src);
     *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(v + src);
   }
 }
 
-void kv_write(at::Tensor k, at::Tensor v, at::Tensor kc, at::Tensor vc, at::Tensor seq, at::Tensor pos) {
+void kv_write(at::Tensor k, at::Tensor v, at::Tensor kc, at::Tensor vc, at::Tensor seq, at::Tensor pos,
+              c10::optional<at::Tensor> block_table) {
   const int T = static_cast<int>(k.size(0));
   if (T == 0) return;
   TORCH_CHECK(k.is_contiguous() && v.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(), "kv_write: layout");
   TORCH_CHECK(seq.scalar_type() == at::kLong && pos.scalar_type() == at::kLong, "kv_write: int64 indices");
+  const KvLayout lay = kv_layout_of(kc, block_table);
+  TORCH_CHECK(k.size(1) == lay.Hkv && vc.sizes() == kc.sizes(), "kv_write: head count / cache shapes");
   const c10::cuda::CUDAGuard g(k.device());
   kv_write_kernel<<<T, 128, 0, cur_stream()>>>(
       reinterpret_cast<const bf16*>(k.data_ptr()), reinterpret_cast<const bf16*>(v.data_ptr()),
       reinterpret_cast<bf16*>(kc.data_ptr()), reinterpret_cast<bf16*>(vc.data_ptr()), seq.data_ptr<int64_t>(),
-      pos.data_ptr<int64_t>(), T, static_cast<int>(k.size(1)), static_cast<int>(kc.size(2)), static_cast<int>(k.size(2)));
+      pos.data_ptr<int64_t>(), T, lay, static_cast<int>(k.size(2)));
   VLM_LAUNCHED();
 }
 

@@ -70,7 +70,8 @@ void set_static_weights(bool on);
 at::Tensor dec_qkv(at::Tensor ws, std::vector<int64_t> meta, at::Tensor bias, at::Tensor qw, at::Tensor kw,
                    at::Tensor lengths, at::Tensor delta, at::Tensor inv_freq, at::Tensor kc, at::Tensor vc, int64_t nq,
                    int64_t nkv, double eps,
-                   c10::optional<at::Tensor> prefetch = c10::nullopt);
+                   c10::optional<at::Tensor> prefetch = c10::nullopt,
+                   c10::optional<at::Tensor> block_table = c10::nullopt);
 std::tuple<at::Tensor, at::Tensor> dec_residual_norm(at::Tensor ws, std::vector<int64_t> meta, at::Tensor residual,
                                                      at::Tensor w, double eps,
                                                      c10::optional<at::Tensor> prefetch = c10::nullopt);
@@ -93,7 +94,8 @@ void swiglu_bwd(at::Tensor d_act, at::Tensor pre, at::Tensor out);
 void embed(at::Tensor tokens, at::Tensor table, at::Tensor out);
 void scatter_rows(at::Tensor h, at::Tensor rows, at::Tensor src, bool add);
 void embed_bwd(at::Tensor tokens, at::Tensor dh, at::Tensor dtable);
-void kv_write(at::Tensor k, at::Tensor v, at::Tensor kc, at::Tensor vc, at::Tensor seq, at::Tensor pos);
+void kv_write(at::Tensor k, at::Tensor v, at::Tensor kc, at::Tensor vc, at::Tensor seq, at::Tensor pos,
+              c10::optional<at::Tensor> block_table);
 void adamw(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, at::Tensor ph, at::Tensor scale, double lr, double b1,
            double b2, double eps, double wd, int64_t step);
 void sq_norm_acc(at::Tensor x, at::Tensor out);
@@ -106,9 +108,11 @@ void flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, a
                     at::Tensor cu, at::Tensor dq, at::Tensor dk, at::Tensor dv, int64_t max_seqlen, bool causal,
                     double scale, c10::optional<at::Tensor> pre, c10::optional<at::Tensor> xq);
 // lead / share_len (int32 [B], optional): keys [0, share_len[b]) of row b may be read from row lead[b].
+// block_table (int32 [B, blocks], optional): kc / vc are block pools [NB, Hkv, 64, D] (kv_layout.cuh).
 void decode_attn(at::Tensor q, at::Tensor kc, at::Tensor vc, at::Tensor lens, at::Tensor o, double scale,
                  c10::optional<at::Tensor> prefetch = c10::nullopt, c10::optional<at::Tensor> lead = c10::nullopt,
-                 c10::optional<at::Tensor> share_len = c10::nullopt);
+                 c10::optional<at::Tensor> share_len = c10::nullopt,
+                 c10::optional<at::Tensor> block_table = c10::nullopt);
 
 // sampler.cu
 void sample(at::Tensor logits, at::Tensor tok, at::Tensor lp, at::Tensor step, at::Tensor seed, double temperature,

@@ -16,6 +16,7 @@ reference's EOS latch); ``lengths`` counts tokens up to and including the first 
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence, Tuple, Union
 
@@ -25,17 +26,20 @@ import torch
 from vlmrl import ops
 from vlmrl.core.batching import pack_prompts
 from vlmrl.core.types import SampleResult, SamplingConfig, VLMInputs
-from vlmrl.models.qwen3vl.model import KVCache, VisionEmbeddings
+from vlmrl.models.qwen3vl.model import KVCache, PagedKVCache, VisionEmbeddings
 from vlmrl.utils.profiling import phase
+
+
+_PAGED_KV = os.environ.get("VLMRL_PAGED_KV", "1") != "0"
 
 
 class _DecodeState:
     """Static buffers (and the captured graph) of one (batch, cache length) shape."""
 
-    def __init__(self, model, B: int, max_len: int, max_new: int):
+    def __init__(self, model, B: int, max_len: int, max_new: int, num_blocks: Optional[int] = None):
         dev = model.device
         self.B, self.max_len, self.max_new = B, max_len, max_new
-        self.cache: KVCache = model.new_cache(B, max_len)
+        self.cache = model.new_cache(B, max_len, num_blocks) if num_blocks is not None else model.new_cache(B, max_len)
         self.tok = torch.zeros(B, dtype=torch.int64, device=dev)
         self.deltas = torch.zeros(B, dtype=torch.int64, device=dev)
         self.step = torch.zeros(1, dtype=torch.int64, device=dev)
@@ -52,9 +56,12 @@ class Generator:
     """``tp``: a ``vlmrl.parallel.tp.TPDecoder`` — decode steps then run tensor-parallel over its ranks (every
     rank must call ``generate`` with the same prompts and seed); the prefill stays replicated."""
 
-    def __init__(self, model, *, use_cuda_graph: bool = True, tp=None):
+    def __init__(self, model, *, use_cuda_graph: bool = True, tp=None, paged_kv: Optional[bool] = None):
         self.model = model
         self.tp = tp
+        # rollouts keep their KV in 64-token blocks (a group shares its prompt's blocks) unless
+        # VLMRL_PAGED_KV=0 or paged_kv=False asks for one contiguous row per sequence
+        self.paged_kv = _PAGED_KV if paged_kv is None else bool(paged_kv)
         self.use_cuda_graph = bool(use_cuda_graph) and model.device.type == "cuda"
         self._states: Dict[Tuple[int, int, int], _DecodeState] = {}
         self.graph_kernel_launches = 0   # kernels executed by graph replays (not seen by the launch counter)
@@ -97,13 +104,13 @@ class Generator:
             self._pending_decode = None
         return self.last_decode_ms
 
-    def _state(self, B: int, max_len: int, max_new: int) -> _DecodeState:
-        key = (B, max_len, max_new)
+    def _state(self, B: int, max_len: int, max_new: int, num_blocks: Optional[int] = None) -> _DecodeState:
+        key = (B, max_len, max_new, num_blocks)
         st = self._states.get(key)
         if st is None:
             if len(self._states) >= 4:          # bound resident caches
                 self._states.clear()
-            st = _DecodeState(self.model, B, max_len, max_new)
+            st = _DecodeState(self.model, B, max_len, max_new, num_blocks)
             st.tp_cache = self.tp.new_cache(B, max_len) if self.tp is not None else None
             self._states[key] = st
         return st
@@ -130,7 +137,15 @@ class Generator:
         plen = max(len(p) for p in prompts)
         refeed = bool(getattr(cfg, "compat_refeed_last_token", False))
         max_len = int(-(-(plen + max_new + int(refeed)) // 64) * 64)
-        st = self._state(B, max_len, max_new)
+        paged = self.paged_kv
+        nb = None
+        if paged:
+            # pool sized for this call's prompts, rounded up so that similar batches reuse the state
+            nb = PagedKVCache.blocks_needed([len(p) for p in prompts], gs, max_len)
+            nb = -(-nb // 64) * 64
+        st = self._state(B, max_len, max_new, nb)
+        if paged:
+            st.cache.assign([len(p) for p in prompts], gs)
         batch, deltas = pack_prompts(m.spec, prompts, grids_per_seq, vision, device=m.device)
         st.cache.lengths.zero_()
         st.done.zero_()
@@ -142,16 +157,21 @@ class Generator:
         with phase("prefill"):
             logits = m.prefill(batch, st.cache, torch.arange(G, device=m.device) * gs)
         if gs > 1:
-            L = st.cache.keys.shape[0]
-            for buf in (st.cache.keys, st.cache.values):
-                v = buf.view(L, G, gs, *buf.shape[2:])
-                v[:, :, 1:, :, :plen] = v[:, :, :1, :, :plen]
+            if paged:
+                # members already point at the leader's full prompt blocks; copy the partial last one
+                st.cache.copy_prompt_tails()
+            else:
+                L = st.cache.keys.shape[0]
+                for buf in (st.cache.keys, st.cache.values):
+                    v = buf.view(L, G, gs, *buf.shape[2:])
+                    v[:, :, 1:, :, :plen] = v[:, :, :1, :, :plen]
             lv = st.cache.lengths.view(G, gs)
             lv[:, 1:] = lv[:, :1]
             logits = logits.repeat_interleave(gs, dim=0)
-        # members' prompt KV rows are copies of their leader's: decode attention reads the leader's
-        st.cache.lead.copy_(torch.arange(B, device=m.device, dtype=torch.int32) // gs * gs)
-        st.cache.share_len.copy_(st.cache.lengths)
+        if not paged:
+            # members' prompt KV rows are copies of their leader's: decode attention reads the leader's
+            st.cache.lead.copy_(torch.arange(B, device=m.device, dtype=torch.int32) // gs * gs)
+            st.cache.share_len.copy_(st.cache.lengths)
         if refeed:
             # reference start: discard the prefill logits, decode the last prompt token once more
             last = torch.tensor([int(p[-1]) for p in prompts], dtype=torch.int64).repeat_interleave(gs)

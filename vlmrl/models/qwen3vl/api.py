@@ -18,7 +18,7 @@ import torch
 
 from vlmrl import ops
 from vlmrl.models.qwen3vl.config import Qwen3VLSpec
-from vlmrl.models.qwen3vl.model import KVCache, LocalParams, PackedBatch, TextDecoder, VisionEmbeddings
+from vlmrl.models.qwen3vl.model import KVCache, LocalParams, PackedBatch, PagedKVCache, TextDecoder, VisionEmbeddings
 from vlmrl.models.qwen3vl.params import all_layouts, init_params, text_layouts
 from vlmrl.models.qwen3vl.vision import VisionTower, prepare_vision_inputs
 from vlmrl.utils.vlm import CLIP_MEAN, CLIP_STD
@@ -108,8 +108,13 @@ class Qwen3VLModel:
         self.decoder.backward(self.params, ctx, g_logp, g_ent)
 
     # ---------------------------------------------------------------- decoding
-    def new_cache(self, batch: int, max_len: int) -> KVCache:
+    def new_cache(self, batch: int, max_len: int, num_blocks: Optional[int] = None):
+        """A contiguous ``KVCache``, or with ``num_blocks`` a ``PagedKVCache`` whose pool holds that many
+        64-token blocks (lay it out with ``assign``)."""
         t = self.spec.text
+        if num_blocks is not None:
+            return PagedKVCache(t.num_hidden_layers, batch, t.num_key_value_heads, max_len, t.head_dim,
+                                int(num_blocks), self.dtype, self.device)
         return KVCache(t.num_hidden_layers, batch, t.num_key_value_heads, max_len, t.head_dim, self.dtype, self.device)
 
     @torch.no_grad()

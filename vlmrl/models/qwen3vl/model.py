@@ -29,6 +29,7 @@ import os
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional, Sequence, Tuple
 
+import numpy as np
 import torch
 
 from vlmrl import ops
@@ -103,10 +104,109 @@ class KVCache:
         self.lead = torch.arange(batch, dtype=torch.int32, device=device)
         self.share_len = torch.zeros(batch, dtype=torch.int32, device=device)
         self.max_len = max_len
+        self.block_table = None   # contiguous rows (see PagedKVCache)
 
     @classmethod
     def init(cls, batch, num_layers, num_heads, head_dim, max_len, dtype=torch.bfloat16, device="cpu"):
         return cls(num_layers, batch, num_heads, max_len, head_dim, dtype, device)
+
+    def rows(self, layer: int):
+        """(keys, values) of one layer as contiguous [B, Hkv, Tmax, D]."""
+        return self.keys[layer], self.values[layer]
+
+
+class PagedKVCache:
+    """KV cache in 64-token blocks: pools ``keys`` / ``values`` [L, NB, Hkv, 64, D] and a block table
+    ``block_table`` int32 [B, max_len / 64] naming, per sequence, the pool block of each 64-token span.
+
+    ``assign(prompt_lens, group_size)`` lays a GRPO batch out: the members of a group point at their
+    leader's full prompt blocks, so a prompt's keys and values are stored (and streamed by decode
+    attention) once per group; every row owns the blocks from its prompt's last, partial block on.
+    After the prefill has written the leaders' rows, ``copy_prompt_tails`` gives each member its own copy
+    of that partial block.  The decode kernels (``dec_qkv`` append, ``decode_attn``) and the prefill's
+    ``kv_write`` address through the table; the block pool and the table keep their addresses, so a
+    captured decode graph replays against whatever layout ``assign`` wrote last.
+
+    No reference counterpart: the reference keeps one contiguous row per sequence
+    (``models/qwen3vl/model.py:633-687``)."""
+
+    block_size = 64
+
+    def __init__(self, num_layers: int, batch: int, num_kv_heads: int, max_len: int, head_dim: int,
+                 num_blocks: int, dtype=torch.bfloat16, device="cpu"):
+        bs = self.block_size
+        if max_len % bs:
+            raise ValueError(f"paged KV cache: max_len {max_len} must be a multiple of {bs}")
+        self.blocks_per_row = max_len // bs
+        self.num_blocks = int(num_blocks)
+        shape = (num_layers, self.num_blocks, num_kv_heads, bs, head_dim)
+        self.keys = torch.zeros(shape, dtype=dtype, device=device)
+        self.values = torch.zeros(shape, dtype=dtype, device=device)
+        self.block_table = torch.zeros(batch, self.blocks_per_row, dtype=torch.int32, device=device)
+        self.lengths = torch.zeros(batch, dtype=torch.int32, device=device)
+        # sharing is expressed by the block table; the row-sharing fields stay identity / 0
+        self.lead = torch.arange(batch, dtype=torch.int32, device=device)
+        self.share_len = torch.zeros(batch, dtype=torch.int32, device=device)
+        self.max_len = max_len
+        self._tails = None
+
+    @staticmethod
+    def blocks_needed(prompt_lens, group_size: int, max_len: int) -> int:
+        """Pool blocks ``assign`` uses for these prompts (one per group member per block from the prompt's
+        partial block on, plus the leader's full prompt blocks)."""
+        mb = max_len // PagedKVCache.block_size
+        gs = max(1, int(group_size))
+        n = 0
+        for p in prompt_lens:
+            full = min(int(p) // PagedKVCache.block_size, mb)
+            n += full + gs * (mb - full)
+        return n
+
+    def assign(self, prompt_lens, group_size: int = 1) -> int:
+        """Write the block table for prompts ``prompt_lens`` (rows ordered (prompt, member)); returns the
+        number of pool blocks used."""
+        bs, mb = self.block_size, self.blocks_per_row
+        gs = max(1, int(group_size))
+        B = self.block_table.shape[0]
+        if len(prompt_lens) * gs != B:
+            raise ValueError(f"{len(prompt_lens)} prompts x group {gs} != {B} cache rows")
+        need = self.blocks_needed(prompt_lens, gs, self.max_len)
+        if need > self.num_blocks:
+            raise ValueError(f"paged KV cache: {need} blocks needed, pool has {self.num_blocks}")
+        table = np.zeros((B, mb), dtype=np.int32)
+        nxt = 0
+        src, dst = [], []
+        for g, p in enumerate(prompt_lens):
+            full = min(int(p) // bs, mb)
+            shared = np.arange(nxt, nxt + full, dtype=np.int32)
+            nxt += full
+            for j in range(gs):
+                b = g * gs + j
+                table[b, :full] = shared
+                table[b, full:] = np.arange(nxt, nxt + mb - full, dtype=np.int32)
+                nxt += mb - full
+            if gs > 1 and full < mb and int(p) % bs:
+                lead_tail = table[g * gs, full]
+                for j in range(1, gs):
+                    src.append(lead_tail)
+                    dst.append(table[g * gs + j, full])
+        self.block_table.copy_(torch.from_numpy(table))
+        dev = self.keys.device
+        self._tails = ((torch.tensor(src, dtype=torch.int64, device=dev), torch.tensor(dst, dtype=torch.int64, device=dev))
+                       if src else None)
+        return nxt
+
+    def copy_prompt_tails(self) -> None:
+        """Members get their own copy of the leader's partial prompt block (written by the prefill)."""
+        if self._tails is None:
+            return
+        src, dst = self._tails
+        for pool in (self.keys, self.values):
+            pool.index_copy_(1, dst, pool.index_select(1, src))
+
+    def rows(self, layer: int):
+        """(keys, values) of one layer as contiguous [B, Hkv, max_len, D] (a gathered copy)."""
+        return ops.paged_rows(self.keys[layer], self.block_table), ops.paged_rows(self.values[layer], self.block_table)
 
 
 # VLMRL_DECODE_L2_PREFETCH=1: decode kernels ask the L2 to fetch the next GEMM's weights.  Off by default:
@@ -358,7 +458,7 @@ class TextDecoder:
         slot_of_tok = slots.to(torch.int64)[seq_of_tok]
 
         def writer(i, k, v):
-            ops.kv_write(k, v, cache.keys[i], cache.values[i], slot_of_tok, pos_in_seq)
+            ops.kv_write(k, v, cache.keys[i], cache.values[i], slot_of_tok, pos_in_seq, cache.block_table)
 
         h = self.hidden_states(params, batch, save=False, kv_writer=writer)
         last = (cu[1:].to(torch.int64) - 1)
@@ -374,7 +474,7 @@ class TextDecoder:
         """
         e = self._w(params, "embed")["embed"]
         B = tokens.shape[0]
-        if tokens.is_cuda and self._persistent_ok(params, B):
+        if tokens.is_cuda and cache.block_table is None and self._persistent_ok(params, B):
             plan = decode_step.plan_for(self, params, cache, B)
             ops.embed(tokens, e, out=plan.x)
             params.release("embed")
@@ -395,8 +495,9 @@ class TextDecoder:
             qkv = ops.linear(xn, w["qkv_w"], bias=w["qkv_b"], out_dtype=x.dtype)
             q, k, v, _, _ = ops.qk_norm_rope(qkv, w.get("q_norm"), w.get("k_norm"), pos, self.rope,
                                              n_q=self.nq, n_kv=self.nkv, eps=self.eps)
-            ops.kv_write(k, v, cache.keys[i], cache.values[i], rows, cur)
-            o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale)
+            ops.kv_write(k, v, cache.keys[i], cache.values[i], rows, cur, cache.block_table)
+            o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale,
+                                block_table=cache.block_table)
             h1 = ops.linear(o.reshape(B, self.nq * self.D), w["o_w"], residual=x, out_dtype=x.dtype)
             hn, _ = ops.rms_norm(h1, w["post_norm"], self.eps)
             act, _ = ops.linear_swiglu(hn, w["gu_w"], save_pre=False)
@@ -425,7 +526,8 @@ class TextDecoder:
         # half of gate/up during attention and the rest during the o_proj consumer, down during SwiGLU, the
         # next layer's qkv during the closing residual + norm.
         pf = _DECODE_L2_PREFETCH
-        fused = _DECODE_FUSED_CONSUMERS and not pf
+        bt = cache.block_table
+        fused = _DECODE_FUSED_CONSUMERS and not pf and bt is None   # the in-GEMM consumers address rows only
         for i in range(self.n_layers):
             w = self._w(params, f"layer{i}")
             nxt_w = self._w(params, f"layer{i + 1}") if i + 1 < self.n_layers else None
@@ -448,9 +550,10 @@ class TextDecoder:
             ws, meta = ops.gemm_partials(xn, w["qkv_w"])
             q = ops.dec_qkv(ws, meta, w["qkv_b"], w.get("q_norm"), w.get("k_norm"), lens, delta, self.rope,
                             cache.keys[i], cache.values[i], n_q=self.nq, n_kv=self.nkv, eps=self.eps,
-                            prefetch=w["o_w"] if pf else None)
+                            prefetch=w["o_w"] if pf else None, block_table=bt)
             o = ops.decode_attn(q, cache.keys[i], cache.values[i], lens_after, scale=self.scale,
-                                prefetch=gu[:half] if pf else None, lead=cache.lead, share_len=cache.share_len)
+                                prefetch=gu[:half] if pf else None, lead=cache.lead, share_len=cache.share_len,
+                                block_table=bt)
             ws, meta = ops.gemm_partials(o.reshape(B, self.nq * self.D), w["o_w"])
             h1, hn = ops.dec_residual_norm(ws, meta, x, w["post_norm"], self.eps, prefetch=gu[half:] if pf else None)
             ws, meta = ops.gemm_partials(hn, w["gu_w"])
@@ -462,4 +565,4 @@ class TextDecoder:
         return xn
 
 
-__all__ = ["VisionEmbeddings", "PackedBatch", "KVCache", "LocalParams", "TextDecoder", "TrainCtx"]
+__all__ = ["VisionEmbeddings", "PackedBatch", "KVCache", "PagedKVCache", "LocalParams", "TextDecoder", "TrainCtx"]

@@ -198,15 +198,16 @@ def gemm_partials(a: torch.Tensor, b: torch.Tensor):
 
 
 def dec_qkv(ws, meta, bias, q_w, k_w, lengths, delta, rope: "RopeCfg", k_cache, v_cache, *, n_q: int, n_kv: int,
-            eps: float, prefetch=None):
+            eps: float, prefetch=None, block_table=None):
     """Sum QKV partials (+bias), RMSNorm q/k heads (skipped when ``q_w`` is None), MRoPE at position
     ``lengths + delta``, write k/v into the cache at ``lengths``; returns q [B, n_q, D].
 
     ``prefetch`` (here and in the other decode consumers): a weight tensor whose bytes every CTA asks the
-    L2 to fetch while the kernel runs, so the next GEMM streams it from L2."""
+    L2 to fetch while the kernel runs, so the next GEMM streams it from L2.  ``block_table``: the cache
+    layer is a block pool (``paged_rows``)."""
     f, _ = rope.device_tables(ws.device)
     return ext().dec_qkv(ws, list(meta), _opt(bias), _opt(q_w), _opt(k_w), lengths, delta, f, k_cache, v_cache, n_q, n_kv,
-                         float(eps), prefetch)
+                         float(eps), prefetch, block_table)
 
 
 def dec_linear_qkv(x, w, bias, q_w, k_w, lengths, delta, rope: "RopeCfg", k_cache, v_cache, *, n_q: int, n_kv: int,
@@ -412,27 +413,46 @@ def flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, max_seqlen: int, *, causal: 
 
 
 def decode_attn(q, k_cache, v_cache, lengths, *, scale: Optional[float] = None, out=None, prefetch=None,
-                lead=None, share_len=None):
+                lead=None, share_len=None, block_table=None):
     """``prefetch``: a weight the L2 should fetch while the kernel runs (the next GEMM's operand).
     ``lead``/``share_len`` (int32 [B]): the first ``share_len[b]`` cache entries of row b equal those of row
     ``lead[b]`` (members of a GRPO group share the prompt); the kernel then reads them from the leader's
-    row, so a group streams its prompt's KV once."""
+    row, so a group streams its prompt's KV once.  ``block_table`` (int32 [B, blocks]): the caches are
+    block pools [NB, Hkv, 64, D] and row b's token t lives in block ``block_table[b, t // 64]``."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if not _cuda(q):
+        if block_table is not None:
+            k_cache, v_cache = paged_rows(k_cache, block_table), paged_rows(v_cache, block_table)
         return ref.decode_attn(q, k_cache, v_cache, lengths, scale=scale)
     o = out if out is not None else torch.empty_like(q)
-    ext().decode_attn(q, k_cache, v_cache, lengths, o, float(scale), prefetch, lead, share_len)
+    ext().decode_attn(q, k_cache, v_cache, lengths, o, float(scale), prefetch, lead, share_len, block_table)
     return o
 
 
-def kv_write(k, v, k_cache, v_cache, seq_idx, pos_idx):
-    """Scatter packed k, v [T,Hkv,D] into caches [B,Hkv,Tmax,D] at (seq_idx[t], pos_idx[t])."""
+KV_BLOCK = 64   # tokens per block of a paged KV cache (kv_layout.cuh)
+
+
+def paged_rows(pool, block_table):
+    """The contiguous view [B, Hkv, blocks * 64, D] of a block pool [NB, Hkv, 64, D] under ``block_table``
+    (a gathered copy; for host-side consumers and the CPU executor)."""
+    B, nb = block_table.shape
+    g = pool[block_table.long().reshape(-1)]                       # [B * nb, Hkv, 64, D]
+    return g.view(B, nb, pool.shape[1], KV_BLOCK, pool.shape[3]).permute(0, 2, 1, 3, 4).reshape(
+        B, pool.shape[1], nb * KV_BLOCK, pool.shape[3])
+
+
+def kv_write(k, v, k_cache, v_cache, seq_idx, pos_idx, block_table=None):
+    """Scatter packed k, v [T,Hkv,D] into caches [B,Hkv,Tmax,D] at (seq_idx[t], pos_idx[t]); with
+    ``block_table`` the caches are block pools [NB, Hkv, 64, D]."""
     if not _cuda(k):
         si, pi = seq_idx.long(), pos_idx.long()
+        if block_table is not None:
+            si = block_table.long()[si, pi // KV_BLOCK]
+            pi = pi % KV_BLOCK
         k_cache[si, :, pi] = k.to(k_cache.dtype)
         v_cache[si, :, pi] = v.to(v_cache.dtype)
         return
-    ext().kv_write(k, v, k_cache, v_cache, seq_idx, pos_idx)
+    ext().kv_write(k, v, k_cache, v_cache, seq_idx, pos_idx, block_table)
 
 
 # ------------------------------------------------------------------ embedding

@@ -110,8 +110,14 @@ class TPDecoder:
     def load_cache(self, full: KVCache, local: KVCache, prefix_len: int) -> None:
         """Copy this rank's kv heads (first ``prefix_len`` positions) of a full cache into the local one."""
         h0, h1 = self.rank * self.nkv_l, (self.rank + 1) * self.nkv_l
-        local.keys[:, :, :, :prefix_len].copy_(full.keys[:, :, h0:h1, :prefix_len])
-        local.values[:, :, :, :prefix_len].copy_(full.values[:, :, h0:h1, :prefix_len])
+        if full.block_table is None:
+            local.keys[:, :, :, :prefix_len].copy_(full.keys[:, :, h0:h1, :prefix_len])
+            local.values[:, :, :, :prefix_len].copy_(full.values[:, :, h0:h1, :prefix_len])
+        else:   # a paged full cache: gather its rows layer by layer
+            for i in range(self.L):
+                k, v = full.rows(i)
+                local.keys[i, :, :, :prefix_len].copy_(k[:, h0:h1, :prefix_len])
+                local.values[i, :, :, :prefix_len].copy_(v[:, h0:h1, :prefix_len])
         local.lengths.copy_(full.lengths)
 
     # ---------------------------------------------------------------- decode
