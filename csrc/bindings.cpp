@@ -51,6 +51,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("share_len") = py::none(), py::arg("block_table") = py::none());
   m.def("sample", &vlm::sample);
   m.def("lm_head_sample", &vlm::lm_head_sample, "lm_head GEMM with a top-k epilogue + merge / top-p / Philox draw");
+  m.def("lm_head_sample_tp", &vlm::lm_head_sample_tp,
+        "vocab-parallel lm_head_sample: shard top-k survivors exchanged over NVLink as tagged words");
   m.def("vocab_logprob_fwd", &vlm::vocab_logprob_fwd);
   m.def("vocab_logprob_bwd", &vlm::vocab_logprob_bwd);
   m.def("symm_alloc", &vlm::symm_alloc, "cudaMalloc an IPC-exportable buffer");

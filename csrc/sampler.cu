@@ -16,6 +16,7 @@
 
 #include "common.cuh"
 #include "host_utils.h"
+#include "peer.cuh"
 #include "vlm_ops.h"
 
 namespace vlm {
@@ -196,10 +197,25 @@ constexpr int kMergeThreads = 256;
 
 VLM_DEV bool cand_before(float a, int ia, float b, int ib) { return a > b || (a == b && ia < ib); }
 
+// Vocab-parallel variant (tensor-parallel decode): each rank's lm_head GEMM covered its vocabulary shard,
+// so its merge finds the shard's top k.  Every value travels with the decode step's tag in an 8-byte word
+// (fp32 bits or the global token id in the low half, the tag in the high half); the rank stores its k
+// survivors into its slot of every rank's buffer ([W][B][kFusedTopkMax] word pairs), polls its own buffer
+// until all ranks' survivors carry the tag, and picks the row's global top k from the W x k of them.  The
+// global top k of a row is the top k of the shards' top k, so every rank draws the token a single GPU
+// would draw from the whole vocabulary.
+struct TopkExchange {
+  PeerTable slots;                       // per rank: this step's [W][B][kFusedTopkMax][2] u64 words
+  const unsigned long long* epoch;       // device step counter (its low 32 bits are the tag)
+  int voff, rank, world;
+  int* err;
+};
+
+template <bool TP>
 __global__ void __launch_bounds__(kMergeThreads) topk_merge_sample_kernel(
     const float* __restrict__ cand_v, const int* __restrict__ cand_i, int tiles, int k, int64_t* __restrict__ tok_out,
     float* __restrict__ lp_out, const int64_t* __restrict__ step_ptr, float inv_temp, float top_p,
-    const int64_t* __restrict__ seed_ptr, long long row_offset) {
+    const int64_t* __restrict__ seed_ptr, long long row_offset, TopkExchange ex) {
   __shared__ float wv[kMergeThreads / 32];
   __shared__ int wi[kMergeThreads / 32];
   __shared__ int wt[kMergeThreads / 32];
@@ -300,6 +316,72 @@ __global__ void __launch_bounds__(kMergeThreads) topk_merge_sample_kernel(
     }
     __syncthreads();
   }
+  if constexpr (TP) {
+    // 2b. publish this shard's survivors (global token ids) to every rank; gather every rank's
+    __shared__ float gv[kMaxRanks * kFusedTopkMax];
+    __shared__ int gi[kMaxRanks * kFusedTopkMax];
+    __shared__ int s_ok;
+    const unsigned long long tag = static_cast<unsigned long long>(static_cast<unsigned>(*ex.epoch)) << 32;
+    const int B = static_cast<int>(gridDim.x);
+    if (tid == 0) s_ok = 1;
+    if (tid < k) {
+      const unsigned long long w0 = tag | __float_as_uint(cv[tid]);
+      const unsigned long long w1 = tag | static_cast<unsigned>(ci[tid] + ex.voff);
+      const int64_t off = ((static_cast<int64_t>(ex.rank) * B + row) * kFusedTopkMax + tid) * 2;
+      for (int p = 0; p < ex.world; ++p) {
+        unsigned long long* dst = reinterpret_cast<unsigned long long*>(ex.slots.p[p]) + off;
+        asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(w0), "l"(w1) : "memory");
+      }
+    }
+    __syncthreads();
+    if (tid < ex.world * k) {
+      const int p = tid / k, j = tid - p * k;
+      const unsigned long long* src = reinterpret_cast<const unsigned long long*>(ex.slots.p[ex.rank]) +
+                                      ((static_cast<int64_t>(p) * B + row) * kFusedTopkMax + j) * 2;
+      unsigned long long w0, w1;
+      const long long t0 = clock64();
+      bool good = true;
+      while (true) {
+        asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(src) : "memory");
+        if ((w0 >> 32) == (tag >> 32) && (w1 >> 32) == (tag >> 32)) break;
+        if (clock64() - t0 > kPeerWait) {
+          atomicCAS(ex.err, 0, kErrTimeoutPeer);
+          good = false;
+          break;
+        }
+      }
+      gv[tid] = __uint_as_float(static_cast<unsigned>(w0));
+      gi[tid] = static_cast<int>(static_cast<unsigned>(w1));
+      if (!good) s_ok = 0;
+    }
+    __syncthreads();
+    if (!s_ok) {
+      if (tid == 0) {
+        tok_out[row] = 0;
+        lp_out[row] = 0.f;
+      }
+      return;
+    }
+    // 2c. the row's global top k: k selection passes over the W x k survivors (ids are unique)
+    if (tid == 0) {
+      float pv = INFINITY;
+      int pi = -1;
+      for (int r = 0; r < k; ++r) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int c = 0; c < ex.world * k; ++c)
+          if (cand_before(pv, pi, gv[c], gi[c]) && cand_before(gv[c], gi[c], bv, bi)) {
+            bv = gv[c];
+            bi = gi[c];
+          }
+        cv[r] = bv;
+        ci[r] = bi;
+        pv = bv;
+        pi = bi;
+      }
+    }
+    __syncthreads();
+  }
   // 3. tempered softmax over the survivors, inclusive prefix sum in sample_kernel's order, nucleus, draw
   if (tid == 0) {
     const float vmax = cv[0];
@@ -376,11 +458,44 @@ void lm_head_sample(at::Tensor h, at::Tensor w, at::Tensor tok, at::Tensor lp, a
   va.topk = k;
   gemm_ex(h, w, at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(), true, true, 1.0, kEpiTopk, false, &va, kTile,
           nullptr, nullptr);
-  launch_pdl(topk_merge_sample_kernel, dim3(static_cast<unsigned>(B)), dim3(kMergeThreads), 0,
+  launch_pdl(topk_merge_sample_kernel<false>, dim3(static_cast<unsigned>(B)), dim3(kMergeThreads), 0,
              at::cuda::getCurrentCUDAStream(), cv.data_ptr<float>(), ci.data_ptr<int>(), tiles, k,
              tok.data_ptr<int64_t>(), lp.data_ptr<float>(), step.data_ptr<int64_t>(),
              static_cast<float>(1.0 / temperature), static_cast<float>(top_p), seed.data_ptr<int64_t>(),
-             static_cast<long long>(row_offset));
+             static_cast<long long>(row_offset), TopkExchange{});
+}
+
+void lm_head_sample_tp(at::Tensor h, at::Tensor w, int64_t vocab_offset, at::Tensor tok, at::Tensor lp,
+                       at::Tensor step, at::Tensor seed, double temperature, int64_t top_k, double top_p,
+                       int64_t row_offset, std::vector<int64_t> slots, int64_t slot_off_bytes, int64_t epoch_ptr,
+                       int64_t rank) {
+  TORCH_CHECK(step.scalar_type() == at::kLong && step.is_cuda(), "lm_head_sample_tp: step must be an int64 CUDA tensor");
+  TORCH_CHECK(seed.scalar_type() == at::kLong && seed.is_cuda(), "lm_head_sample_tp: seed must be an int64 CUDA tensor");
+  TORCH_CHECK(temperature > 0, "lm_head_sample_tp: temperature must be positive");
+  TORCH_CHECK(top_k >= 1 && top_k <= kFusedTopkMax, "lm_head_sample_tp: 1 <= top_k <= ", kFusedTopkMax);
+  const int64_t B = h.size(0), V = w.size(0);
+  const int W = static_cast<int>(slots.size());
+  if (B == 0) return;
+  TORCH_CHECK(top_k <= V, "lm_head_sample_tp: top_k larger than the vocabulary shard");
+  TORCH_CHECK(rank >= 0 && rank < W && slot_off_bytes % 16 == 0, "lm_head_sample_tp: rank / slot alignment");
+  const c10::cuda::CUDAGuard g(h.device());
+  constexpr int kTile = 128;
+  const int tiles = static_cast<int>((V + kTile - 1) / kTile);
+  const int k = static_cast<int>(top_k);
+  at::Tensor cv = at::empty({B, tiles, k}, h.options().dtype(at::kFloat));
+  at::Tensor ci = at::empty({B, tiles, k}, h.options().dtype(at::kInt));
+  VocabArgs va{nullptr, nullptr, nullptr, nullptr, nullptr, cv.data_ptr<float>()};
+  va.cand_i = ci.data_ptr<int>();
+  va.topk = k;
+  gemm_ex(h, w, at::Tensor(), at::Tensor(), at::Tensor(), at::Tensor(), true, true, 1.0, kEpiTopk, false, &va, kTile,
+          nullptr, nullptr);
+  TopkExchange ex{make_peer_table(slots, slot_off_bytes), reinterpret_cast<const unsigned long long*>(epoch_ptr),
+                  static_cast<int>(vocab_offset), static_cast<int>(rank), W, err_word(h.device().index())};
+  launch_pdl(topk_merge_sample_kernel<true>, dim3(static_cast<unsigned>(B)), dim3(kMergeThreads), 0,
+             at::cuda::getCurrentCUDAStream(), cv.data_ptr<float>(), ci.data_ptr<int>(), tiles, k,
+             tok.data_ptr<int64_t>(), lp.data_ptr<float>(), step.data_ptr<int64_t>(),
+             static_cast<float>(1.0 / temperature), static_cast<float>(top_p), seed.data_ptr<int64_t>(),
+             static_cast<long long>(row_offset), ex);
 }
 
 }  // namespace vlm

@@ -150,6 +150,13 @@ void peer_barrier(std::vector<int64_t> sigs, int64_t slot, int64_t epoch, int64_
 // sampler.cu: lm_head fused with the top-k / top-p sampler (logits never materialised)
 void lm_head_sample(at::Tensor h, at::Tensor w, at::Tensor tok, at::Tensor lp, at::Tensor step, at::Tensor seed,
                     double temperature, int64_t top_k, double top_p, int64_t row_offset);
+// Vocab-parallel lm_head + sampler for tensor-parallel decode: w is this rank's [V_shard, H] rows starting at
+// vocab_offset; the shards' top-k survivors are exchanged through the IPC-shared `slots` buffers (tagged by
+// the decode step counter at epoch_ptr) and every rank draws the same token.
+void lm_head_sample_tp(at::Tensor h, at::Tensor w, int64_t vocab_offset, at::Tensor tok, at::Tensor lp,
+                       at::Tensor step, at::Tensor seed, double temperature, int64_t top_k, double top_p,
+                       int64_t row_offset, std::vector<int64_t> slots, int64_t slot_off_bytes, int64_t epoch_ptr,
+                       int64_t rank);
 
 // decode_step.cu (persistent decode step)
 std::vector<at::Tensor> decode_step_maps(std::vector<at::Tensor> weights, std::vector<at::Tensor> caches,

@@ -1,5 +1,6 @@
 """Tensor-parallel decode on 2 GPUs: the NVLink all-reduce inside the consumer kernels reproduces the
-single-GPU decode logits, and both ranks sample identical tokens."""
+single-GPU decode logits, both ranks sample identical tokens, and the vocab-parallel lm_head + sampler
+draws on every rank the token and log-probability the single-GPU fused sampler draws."""
 
 import os
 import socket
@@ -68,8 +69,29 @@ def _worker(rank, world, port, out_path, preset):
     toks = res.tokens.cpu()
     gathered = [torch.zeros_like(toks) for _ in range(world)]
     dist.all_gather_object(gathered, toks)
+    # vocab-parallel lm_head + sampler on the same rows: every rank draws what the single-GPU fused sampler
+    # draws from the whole vocabulary (the shard GEMMs give the same logits per column)
+    from vlmrl.ops._ext import ext
+
+    g = torch.Generator(device=dev).manual_seed(4)
+    hn = torch.randn(8, spec.text.hidden_size, generator=g, device=dev).to(torch.bfloat16)
+    lm = m.decoder._w(m.params, "head")["lm_head"]
+    seed_t = torch.tensor([123], dtype=torch.int64, device=dev)
+    fused = []
+    for step in range(3):
+        step_t = torch.tensor([step], dtype=torch.int64, device=dev)
+        ref_tok, ref_lp = ops.lm_head_sample(hn, lm, temperature=0.8, top_k=5, top_p=0.9, seed=seed_t, step=step_t)
+        ext().tp_step_begin(tp.epoch.data_ptr(), rank)   # a new exchange tag, as every decode step does
+        tp_tok = torch.empty(8, dtype=torch.int64, device=dev)
+        tp_lp = torch.empty(8, dtype=torch.float32, device=dev)
+        ext().lm_head_sample_tp(hn, tp.lm_w, tp.v0, tp_tok, tp_lp, step_t, seed_t, 0.8, 5, 0.9, 0,
+                                tp.samp_slots.ptrs, 0, tp.epoch.data_ptr(), rank)
+        fused.append((ref_tok.cpu(), ref_lp.cpu(), tp_tok.cpu(), tp_lp.cpu()))
+    ops.check_errors(rank)
+    fused_all = [None] * world
+    dist.all_gather_object(fused_all, fused)
     if rank == 0:
-        torch.save({"ref": ref_logits, "tp": tp_logits, "tokens": gathered}, out_path)
+        torch.save({"ref": ref_logits, "tp": tp_logits, "tokens": gathered, "fused": fused_all}, out_path)
     dist.barrier()
     tp.close()
     dist.destroy_process_group()
@@ -84,3 +106,7 @@ def test_tp_decode_matches_single_gpu(tmp_path, preset):
     for a, b in zip(res["tp"], res["ref"]):
         assert (a - b).abs().max().item() < 0.05 * max(1.0, b.abs().max().item())
     assert torch.equal(res["tokens"][0], res["tokens"][1])
+    for per_rank in res["fused"]:
+        for ref_tok, ref_lp, tp_tok, tp_lp in per_rank:
+            assert torch.equal(ref_tok, tp_tok)
+            torch.testing.assert_close(ref_lp, tp_lp, atol=1e-5, rtol=1e-5)

@@ -88,7 +88,12 @@ class Generator:
             self._record(st, nt, lp, cfg.eos_id)
             return
         if self.tp is not None:
-            logits = self.tp.decode_step(st.tok, st.tp_cache, st.deltas)
+            # every rank draws the same token (vocab-parallel lm_head + sampler, or replicated logits)
+            nt, lp = self.tp.decode_step_sample(st.tok, st.tp_cache, st.deltas, temperature=cfg.temperature,
+                                                top_k=cfg.top_k or 0, top_p=cfg.top_p or 0.0, seed=st.seed,
+                                                step=st.step, row_offset=row_offset)
+            self._record(st, nt, lp, cfg.eos_id)
+            return
         else:
             logits = self.model.decode_step(st.tok, st.cache, st.deltas)
         nt, lp = ops.sample(logits, temperature=cfg.temperature, top_k=cfg.top_k or 0, top_p=cfg.top_p or 0.0,

@@ -14,9 +14,13 @@ weights (Megatron-style split, rebuilt for the decode step):
   words carry the tag, and sums all ranks in rank order — so every rank ends
   with bitwise-identical activations, after one one-way NVLink store;
 * gate/up: column-parallel (interleaved gate/up row pairs stay together);
-* embedding, final norm, lm_head and the sampler are replicated: every rank
-  computes the same logits and, with the same Philox seed, samples the same
-  tokens, so no collective is needed to agree on the next token.
+* lm_head and sampler: vocab-parallel.  Rank r owns a contiguous shard of the
+  vocabulary rows; its lm_head GEMM keeps each row's top-k per tile, its merge
+  kernel finds the shard's top k, stores them (tagged with the step epoch) into
+  every rank's slot and picks the global top k from all shards' survivors, so
+  every rank draws the same token with the same Philox draw (``decode_step_sample``;
+  ``decode_step`` still returns full logits from the replicated lm_head).
+  Embedding and final norm are replicated.
 
 The prefill runs replicated with the full weights (it is a small part of a
 rollout); the local kv heads are then copied into the tensor-parallel cache.
@@ -32,6 +36,7 @@ No reference counterpart: the reference decodes on one device
 
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -40,6 +45,9 @@ import torch.distributed as dist
 from vlmrl import ops
 from vlmrl.models.qwen3vl.model import KVCache
 from vlmrl.ops._ext import ext
+
+# VLMRL_FUSED_SAMPLER=0: sample from full logits (replicated lm_head) instead of the vocab-parallel path
+_FUSED_SAMPLER = os.environ.get("VLMRL_FUSED_SAMPLER", "1") != "0"
 
 
 class TPDecoder:
@@ -69,6 +77,13 @@ class TPDecoder:
         self.o_w = torch.empty(L, H, self.nq_l * D, dtype=dt, device=dev)
         self.gu_w = torch.empty(L, 2 * self.F_l, H, dtype=dt, device=dev)
         self.down_w = torch.empty(L, H, self.F_l, dtype=dt, device=dev)
+        # vocab-parallel lm_head: shards of whole 128-column tiles, the last one shorter
+        V = t.vocab_size
+        vs = -(-V // (W * 128)) * 128
+        self.v0, self.v1 = min(V, self.rank * vs), min(V, (self.rank + 1) * vs)
+        self.lm_w = torch.empty(self.v1 - self.v0, H, dtype=dt, device=dev)
+        # per rank: [W][max_batch][16 survivors][2] tagged words of the sampler exchange
+        self.samp_slots = SymmetricBuffer(W * self.max_batch * ops.FUSED_SAMPLER_MAX_TOPK * 16, group, dev)
         self.points = 2 * L
         # per reduction point: [W source ranks][max_batch][H] tagged 8-byte words (zeroed: tags start at 1)
         self.point_bytes = W * self.max_batch * H * 8
@@ -97,6 +112,8 @@ class TPDecoder:
             self.gu_w[i].copy_(w["gu_w"][2 * r * F_l:2 * (r + 1) * F_l])
             self.down_w[i].copy_(w["down_w"][:, r * F_l:(r + 1) * F_l])
             params.release(f"layer{i}")
+        self.lm_w.copy_(dec._w(params, "head")["lm_head"][self.v0:self.v1])
+        params.release("head")
         self.version = version
 
     # ---------------------------------------------------------------- cache
@@ -128,6 +145,30 @@ class TPDecoder:
     @torch.no_grad()
     def decode_step(self, tokens: torch.Tensor, cache: KVCache, rope_delta: torch.Tensor) -> torch.Tensor:
         """Logits [B, V] (identical on every rank); appends this token's local k/v and advances the cache."""
+        xn = self._hidden(tokens, cache, rope_delta)
+        return self.model.decoder.final_logits(self.model.params, xn, normed=True)
+
+    @torch.no_grad()
+    def decode_step_sample(self, tokens: torch.Tensor, cache: KVCache, rope_delta: torch.Tensor, *,
+                           temperature: float, top_k: int, top_p: float, seed, step, row_offset: int = 0):
+        """One decode step that returns the sampled (tokens, log-probs), the same on every rank.  With
+        1 <= top_k <= 16 the lm_head and the sampler are vocab-parallel (no rank writes [B, V] logits);
+        otherwise the replicated lm_head feeds ``ops.sample``."""
+        xn = self._hidden(tokens, cache, rope_delta)
+        if _FUSED_SAMPLER and 1 <= int(top_k or 0) <= ops.FUSED_SAMPLER_MAX_TOPK:
+            B = xn.shape[0]
+            tok = torch.empty(B, dtype=torch.int64, device=xn.device)
+            lp = torch.empty(B, dtype=torch.float32, device=xn.device)
+            ext().lm_head_sample_tp(xn, self.lm_w, self.v0, tok, lp, step, seed, float(temperature), int(top_k),
+                                    float(top_p or 0.0), int(row_offset), self.samp_slots.ptrs, 0,
+                                    self.epoch.data_ptr(), self.rank)
+            return tok, lp
+        logits = self.model.decoder.final_logits(self.model.params, xn, normed=True)
+        return ops.sample(logits, temperature=temperature, top_k=top_k or 0, top_p=top_p or 0.0, seed=seed,
+                          step=step, row_offset=row_offset)
+
+    def _hidden(self, tokens: torch.Tensor, cache: KVCache, rope_delta: torch.Tensor) -> torch.Tensor:
+        """Every decoder layer of one step; returns the final-normed hidden rows (advances the cache)."""
         m = self.model
         dec, params = m.decoder, m.params
         ext().tp_step_begin(self.epoch.data_ptr(), m.device.index if m.device.index is not None else 0)
@@ -154,10 +195,11 @@ class TPDecoder:
             x, xn = self._reduce_norm(ws, meta, h1, nxt, 2 * i + 1)
             params.release(f"layer{i}")
         cache.lengths += 1
-        return dec.final_logits(params, xn, normed=True)
+        return xn
 
     def close(self) -> None:
         self.slots.close()
+        self.samp_slots.close()
 
 
 def tp_partition(world: int, tp_size: int):
