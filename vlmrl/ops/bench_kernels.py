@@ -156,6 +156,9 @@ def bench_decode(t: Timer):
     lens = torch.full((B,), T, dtype=torch.int32, device="cuda")
     ms = t(lambda: ops.decode_attn(q, kc, vc, lens))
     emit("decode_attn_64x390", ms, bytes_=2 * B * Hkv * T * D * 2)
+    pk, pv, table = _paged_case(B, Hkv, D)
+    ms = t(lambda: ops.decode_attn(q, pk, pv, lens, block_table=table))
+    emit("decode_attn_paged_64x390", ms, bytes_=2 * B * Hkv * T * D * 2)
     logits = torch.randn(B, 151936, device="cuda")
     seed = torch.ones(1, dtype=torch.int64, device="cuda")
     step = torch.zeros(1, dtype=torch.int64, device="cuda")
@@ -333,6 +336,15 @@ def bench_train_step(t: Timer = None, eager_steps: int = 0, iters: int = 5):
     emit("train_minibatch_4b_4x8_shared", ms, flops=flops, tokens=tokens, loss_rows=M)
 
 
+def _paged_case(B: int, Hkv: int, D: int, T: int = 448):
+    """A paged KV layer for B rows of T tokens: a block pool with the rows' 64-token blocks in shuffled order."""
+    mb = T // 64
+    pool_k, pool_v = _r(B * mb, Hkv, 64, D), _r(B * mb, Hkv, 64, D)
+    g = torch.Generator().manual_seed(0)
+    table = torch.randperm(B * mb, generator=g).view(B, mb).to(torch.int32).cuda()
+    return pool_k, pool_v, table
+
+
 def _profile_inputs(case: str):
     """-> a zero-argument callable running one launch of the kernel(s) of ``case`` on a small input."""
     H, D = 2560, 128
@@ -342,6 +354,11 @@ def _profile_inputs(case: str):
         q = _r(64, 32, D)
         lens = torch.full((64,), 390, dtype=torch.int32, device="cuda")
         return lambda: (ops.gemm(x, w), ops.decode_attn(q, kc, vc, lens))
+    if case == "decode_paged":  # decode attention over a paged cache (shuffled 64-token blocks), B=64, cache 390
+        pk, pv, table = _paged_case(64, 8, D)
+        q = _r(64, 32, D)
+        lens = torch.full((64,), 390, dtype=torch.int32, device="cuda")
+        return lambda: ops.decode_attn(q, pk, pv, lens, block_table=table)
     if case == "gemm":          # training-shaped GEMM, 8192 x 6144 x 2560 (173 MB of operands > L2)
         a, b = _r(8192, H), _r(6144, H, scale=0.02)
         return lambda: ops.gemm(a, b)
@@ -442,7 +459,7 @@ def main():
     ap.add_argument("--eager-steps", type=int, default=0,
                     help="decode_step (default) or --only train_step: run N eager steps inside a profiler range "
                          "(for a launch list)")
-    ap.add_argument("--profile-small", default=None, choices=["decode", "gemm", "attn", "vocab", "adamw", "gather", "decode_fused", "wgrad"],
+    ap.add_argument("--profile-small", default=None, choices=["decode", "decode_paged", "gemm", "attn", "vocab", "adamw", "gather", "decode_fused", "wgrad"],
                     help="one launch of the named case's kernels inside a profiler range")
     args = ap.parse_args()
     if args.profile_small:
