@@ -783,8 +783,8 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_consta
   float* red = reinterpret_cast<float*>(full + STAGES);  // merge area [4][REP][D + 2]
   __shared__ int abort_flag;
   l2_prefetch_share(pf);
-  pdl_wait();
-  pdl_trigger();
+  // Read before the grid dependency resolves: the lengths, the block table and the row-sharing fields are
+  // written before the previous kernel starts (a decode step writes them before its first layer).
   const int hk = blockIdx.x, b = blockIdx.y, sp = blockIdx.z;
   const int L = min(lens[b], lay.cap);
   int per = (L + splits - 1) / splits;
@@ -815,8 +815,17 @@ __global__ void __launch_bounds__(128) decode_attn_tc_kernel(const __grid_consta
     tma_load_2d(sV + (st * 2 + 0) * HALF, &tmV, &full[st], 0, y);
     tma_load_2d(sV + (st * 2 + 1) * HALF, &tmV, &full[st], 64, y);
   };
+  // Chunks wholly below the newest key (index L - 1) are issued before the grid dependency resolves: the
+  // kernel before this one (dec_qkv in a decode step) appends only that key, so the cached prefix can
+  // stream while it runs.  A predecessor that writes other keys must not trigger its dependents early.
+  int early = 0;
+  while (early < STAGES && early < nchunks && k0 + (early + 1) * KC <= L - 1) ++early;
   if (tid == 0)
-    for (int c = 0; c < STAGES && c < nchunks; ++c) issue(c);
+    for (int c = 0; c < early; ++c) issue(c);
+  pdl_wait();
+  pdl_trigger();
+  if (tid == 0)
+    for (int c = early; c < STAGES && c < nchunks; ++c) issue(c);
   // Q fragments: rows g < REP are the group's heads, the rest zero
   uint32_t qa[D / 16][4];
 #pragma unroll
