@@ -39,16 +39,22 @@ __global__ void dec_qkv_kernel(const float* __restrict__ ws, SkMeta m, const bf1
                                KvLayout lay, float eps, L2Prefetch pf) {
   constexpr int TPH = D / 8;
   l2_prefetch_share(pf);
-  pdl_wait();
-  pdl_trigger();
   const int row = blockIdx.x, tid = threadIdx.x;
   const int head = tid / TPH, t = tid % TPH;
   const int col = tid * 8;
+  // The cache lengths, rotary offsets and bias were written before the previous kernel (the GEMM whose
+  // partials this kernel sums) started, so they are read before the dependency wait.
+  const int len = lengths[row];
+  const int64_t dl = delta[row];
+  float bv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) bv[i] = bias ? bf2f(bias[col + i]) : 0.f;
+  pdl_wait();
+  pdl_trigger();
   float x[8];
   sk_sum8(ws, m, row, col, x);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = bf2f(f2bf(x[i] + (bias ? bf2f(bias[col + i]) : 0.f)));
-  const int len = lengths[row];
+  for (int i = 0; i < 8; ++i) x[i] = bf2f(f2bf(x[i] + bv[i]));
   const bool is_v = head >= nq + nkv;
   const bool is_q = head < nq;
   float ss = 0.f;
@@ -68,7 +74,7 @@ __global__ void dec_qkv_kernel(const float* __restrict__ ws, SkMeta m, const bf1
     if (len < lay.cap) store8(vc + kv_row(lay, row, head - nq - nkv, len) * D + t * 8, x);
     return;
   }
-  const float pos = static_cast<float>(static_cast<int64_t>(len) + delta[row]);
+  const float pos = static_cast<float>(static_cast<int64_t>(len) + dl);
   const bool first_half = t < TPH / 2;
   float out[8];
 #pragma unroll
@@ -89,14 +95,20 @@ __global__ void dec_resnorm_kernel(const float* __restrict__ ws, SkMeta m, const
                                    int H, float eps, L2Prefetch pf) {
   __shared__ float red[32];
   l2_prefetch_share(pf);
+  const int row = blockIdx.x, col = threadIdx.x * 8;
+  // The residual row and the norm weight were written before the previous kernel (the GEMM whose partials
+  // this kernel sums) started, so they are read before the dependency wait.
+  uint4 rv = make_uint4(0, 0, 0, 0), wv = make_uint4(0, 0, 0, 0);
+  if (col < H) {
+    rv = *reinterpret_cast<const uint4*>(res + static_cast<int64_t>(row) * H + col);
+    wv = *reinterpret_cast<const uint4*>(w + col);
+  }
   pdl_wait();
   pdl_trigger();
-  const int row = blockIdx.x, col = threadIdx.x * 8;
   float x[8];
   float ss = 0.f;
   if (col < H) {
     sk_sum8(ws, m, row, col, x);
-    const uint4 rv = *reinterpret_cast<const uint4*>(res + static_cast<int64_t>(row) * H + col);
     const uint32_t u[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -119,9 +131,14 @@ __global__ void dec_resnorm_kernel(const float* __restrict__ ws, SkMeta m, const
   __syncthreads();
   if (col < H) {
     const float r = rsqrtf(red[0] / H + eps);
+    const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
     float o[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = bf2f(f2bf(x[i] * r)) * bf2f(w[col + i]);
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = unpack_bf16x2(wu[j]);
+      o[2 * j] = bf2f(f2bf(x[2 * j] * r)) * f.x;
+      o[2 * j + 1] = bf2f(f2bf(x[2 * j + 1] * r)) * f.y;
+    }
     store8(hn_out + static_cast<int64_t>(row) * H + col, o);
   }
 }
