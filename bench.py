@@ -318,6 +318,8 @@ def main():
                    "fsdp_comm": getattr(model.params, "comm", None) if world > 1 else None,
                    "groups_per_batch": args.groups, "group_size": args.group_size, "minibatches": args.minibatches,
                    "kl_ref_coef": 0.01, "top_k": args.top_k, "top_p": 0.9, "temperature": 0.7,
+                   "kv_cache": ("paged, 64-token blocks, prompt blocks shared per group"
+                                if trainer.generator.paged_kv else "contiguous rows"),
                    "l2": "no flush: per-step working set (8.8 GB weights) >> 126 MB L2"},
         "decode_tok_s": decode_tok_s,
         "decode_ms_per_step": decode_ms,
