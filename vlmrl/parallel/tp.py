@@ -77,10 +77,7 @@ class TPDecoder:
         self.o_w = torch.empty(L, H, self.nq_l * D, dtype=dt, device=dev)
         self.gu_w = torch.empty(L, 2 * self.F_l, H, dtype=dt, device=dev)
         self.down_w = torch.empty(L, H, self.F_l, dtype=dt, device=dev)
-        # vocab-parallel lm_head: shards of whole 128-column tiles, the last one shorter
-        V = t.vocab_size
-        vs = -(-V // (W * 128)) * 128
-        self.v0, self.v1 = min(V, self.rank * vs), min(V, (self.rank + 1) * vs)
+        self.v0, self.v1 = vocab_shard(t.vocab_size, W, self.rank)
         self.lm_w = torch.empty(self.v1 - self.v0, H, dtype=dt, device=dev)
         # per rank: [W][max_batch][16 survivors][2] tagged words of the sampler exchange
         self.samp_slots = SymmetricBuffer(W * self.max_batch * ops.FUSED_SAMPLER_MAX_TOPK * 16, group, dev)
@@ -202,6 +199,14 @@ class TPDecoder:
         self.samp_slots.close()
 
 
+def vocab_shard(vocab: int, world: int, rank: int, tile: int = 128):
+    """Rows [v0, v1) of the lm_head that rank ``rank`` owns in the vocab-parallel sampler: contiguous shards
+    of whole ``tile``-row GEMM tiles (the last one shorter), so every shard's top-k epilogue sees the same
+    tiles, and column ids, as the unsharded lm_head."""
+    vs = -(-vocab // (world * tile)) * tile
+    return min(vocab, rank * vs), min(vocab, (rank + 1) * vs)
+
+
 def tp_partition(world: int, tp_size: int):
     """Rank lists of the tensor-parallel groups: consecutive blocks of ``tp_size`` ranks (NVLink peers on one
     node), ``world // tp_size`` data-parallel replicas."""
@@ -234,4 +239,4 @@ def maybe_tp_decoder(model, group=None, max_batch: int = 64) -> Optional[TPDecod
     return TPDecoder(model, group, max_batch)
 
 
-__all__ = ["TPDecoder", "maybe_tp_decoder"]
+__all__ = ["TPDecoder", "maybe_tp_decoder", "vocab_shard", "tp_partition"]
