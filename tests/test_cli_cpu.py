@@ -194,3 +194,39 @@ def test_rollout_cli(capsys):
     assert len(rewards) == 5
     out = capsys.readouterr().out
     assert "[episode 4]" in out and "Collected 5 episodes" in out
+
+
+def _eval_rank(rank, world, port, out_dir):
+    import os
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch.distributed as dist
+
+    from vlmrl.core import eval as eval_cli
+
+    rep = eval_cli.main(["--preset=tiny", "--prompt=hello there", "--max_new_tokens=6", "--benchmark_runs=1",
+                         "--batch=4", "--temperature=0.9"])
+    torch.save({"tokens": rep["native"]["tokens"], "summary": rep["native"]["summary"]}, f"{out_dir}/r{rank}.pt")
+    dist.destroy_process_group()
+
+
+def test_eval_cli_data_parallel_matches_one_process(tmp_path):
+    """Two gloo ranks split --batch 4: each samples its rows with their global row ids, so together they draw
+    the single-process tokens; throughput counts every rank's tokens."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    from vlmrl.core import eval as eval_cli
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.start_processes(_eval_rank, args=(2, port, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
+    single = eval_cli.main(["--preset=tiny", "--prompt=hello there", "--max_new_tokens=6", "--benchmark_runs=1",
+                            "--batch=4", "--temperature=0.9"])
+    parts = [torch.load(tmp_path / f"r{r}.pt") for r in range(2)]
+    assert torch.equal(torch.cat([p["tokens"] for p in parts]), single["native"]["tokens"])
+    assert parts[0]["summary"]["tokens_total"] == single["native"]["summary"]["tokens_total"]

@@ -9,7 +9,10 @@ and the first-token latency of a ``max_new_tokens=1`` run, as the reference's
 around the public ``sample`` call (which includes the prompt H2D copy and the
 token read-back); the device time of the same calls, taken with CUDA events,
 is reported next to it.  ``--batch`` replicates the prompt to measure batched
-decode throughput.
+decode throughput.  Launched with ``torchrun --nproc-per-node N`` the batch is split over N processes (one
+per GPU, data parallel, NCCL; gloo on CPU): each rank samples its rows with their global row ids, so the
+tokens equal a single-process run of the whole batch, and a run's duration is the slowest rank's while its
+tokens are summed over ranks.
 
 ``--compare_hf`` also times HuggingFace ``generate`` on a local snapshot
 (``--hf_model_name`` must be a directory: there is no network), text-only via
@@ -79,9 +82,27 @@ def _generated_tokens(res: SampleResult) -> int:
     return int(res.tokens.numel())
 
 
-def benchmark_native(model, inputs, cfg: SamplingConfig, seed: int, tokenizer, runs: int
+def _dist():
+    import torch.distributed as dist
+
+    return dist if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1 else None
+
+
+def _across_ranks(values: Sequence[float], op: str) -> List[float]:
+    """Element-wise max or sum of per-rank values (identity in a single process)."""
+    d = _dist()
+    if d is None:
+        return [float(v) for v in values]
+    dev = torch.device("cuda", torch.cuda.current_device()) if d.get_backend() == "nccl" else torch.device("cpu")
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=dev)
+    d.all_reduce(t, op=d.ReduceOp.MAX if op == "max" else d.ReduceOp.SUM)
+    return [float(x) for x in t.cpu()]
+
+
+def benchmark_native(model, inputs, cfg: SamplingConfig, seed: int, tokenizer, runs: int, row_offset: int = 0
                      ) -> Tuple[SampleResult, Dict[str, float], Optional[float]]:
-    """Warm-up + ``runs`` timed calls of the public ``sample``, then a timed 1-token run."""
+    """Warm-up + ``runs`` timed calls of the public ``sample``, then a timed 1-token run.  Under data
+    parallelism every duration is the slowest rank's and every token count the sum over ranks."""
     from vlmrl.core.sampling import sample
     from vlmrl.utils.rng import RngSeq
 
@@ -95,26 +116,29 @@ def benchmark_native(model, inputs, cfg: SamplingConfig, seed: int, tokenizer, r
             torch.cuda.synchronize()
             ev[0].record()
         t0 = time.perf_counter()
-        res = sample(model, None, inputs, cfg, rng.next(), tokenizer=tokenizer)
+        res = sample(model, None, inputs, cfg, rng.next(), tokenizer=tokenizer, row_offset=row_offset)
         if cuda:
             ev[1].record()
             torch.cuda.synchronize()
         dt = time.perf_counter() - t0
         last = res
         if i >= 1:
-            metrics.append({"duration": dt, "tokens": float(_generated_tokens(res)),
-                            "device_ms": ev[0].elapsed_time(ev[1]) if cuda else None})
+            dev_ms = ev[0].elapsed_time(ev[1]) if cuda else 0.0
+            dt, dev_ms = _across_ranks([dt, dev_ms], "max")
+            (tokens,) = _across_ranks([_generated_tokens(res)], "sum")
+            metrics.append({"duration": dt, "tokens": tokens, "device_ms": dev_ms if cuda else None})
     first = None
     one = replace(cfg, max_new_tokens=1)
-    sample(model, None, inputs, one, rng.next(), tokenizer=tokenizer)
+    sample(model, None, inputs, one, rng.next(), tokenizer=tokenizer, row_offset=row_offset)
     if cuda:
         torch.cuda.synchronize()
     t0 = time.perf_counter()
-    r1 = sample(model, None, inputs, one, rng.next(), tokenizer=tokenizer)
+    r1 = sample(model, None, inputs, one, rng.next(), tokenizer=tokenizer, row_offset=row_offset)
     if cuda:
         torch.cuda.synchronize()
-    if r1.tokens.shape[-1] > 0:
-        first = time.perf_counter() - t0
+    (first,) = _across_ranks([time.perf_counter() - t0], "max")
+    if r1.tokens.shape[-1] == 0:
+        first = None
     return last, summaries_from_metrics(metrics), first
 
 
@@ -230,6 +254,20 @@ def main(argv=None) -> Dict[str, Any]:
     args = parse_args(argv)
     if not args.prompt:
         raise SystemExit("--prompt is required")
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        if torch.cuda.is_available():
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        if not dist.is_initialized():
+            dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo",
+                                    timeout=datetime.timedelta(seconds=300))
+        if max(1, args.batch) % world:
+            raise SystemExit(f"--batch {args.batch} must be divisible by the {world} processes")
+    share = max(1, args.batch) // max(1, world)
     dev = torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
     dtype = torch.bfloat16 if dev.type == "cuda" else torch.float32
     model, _ = load_policy(args.ckpt_dir, args.preset, dev, dtype, seed=args.seed)
@@ -240,13 +278,16 @@ def main(argv=None) -> Dict[str, Any]:
     cfg = SamplingConfig(temperature=args.temperature, top_p=args.top_p if 0 < args.top_p < 1 else None,
                          top_k=args.top_k, eos_id=eos_id, pad_id=pad_id, max_new_tokens=args.max_new_tokens,
                          compat_refeed_last_token=bool(args.compat_refeed_last_token))
-    inputs = build_inputs(model, tokenizer, args.prompt, args.image, max(1, args.batch), pad_id)
-    res, summary, first = benchmark_native(model, inputs, cfg, args.seed, tokenizer, args.benchmark_runs)
-    print(format_summary_table("vlmrl sampler", summary, first))
+    inputs = build_inputs(model, tokenizer, args.prompt, args.image, share, pad_id)
+    res, summary, first = benchmark_native(model, inputs, cfg, args.seed, tokenizer, args.benchmark_runs,
+                                           row_offset=rank * share)
+    if rank != 0:
+        return {"native": {"summary": summary, "first_token_s": first, "tokens": res.tokens.cpu()}}
+    print(format_summary_table("vlmrl sampler" + (f" ({world} processes)" if world > 1 else ""), summary, first))
     if res.texts:
         print("sample:", res.texts[0][:500])
     report: Dict[str, Any] = {"native": {"summary": summary, "first_token_s": first,
-                                         "text": res.texts[0] if res.texts else ""}}
+                                         "text": res.texts[0] if res.texts else "", "tokens": res.tokens.cpu()}}
     if args.compare_hf:
         try:
             hf = benchmark_hf(args.hf_model_name, args.prompt, args.image, args.max_new_tokens, args.temperature,
@@ -264,7 +305,8 @@ def main(argv=None) -> Dict[str, Any]:
     if args.dump_metrics:
         os.makedirs(os.path.dirname(args.dump_metrics) or ".", exist_ok=True)
         with open(args.dump_metrics, "w", encoding="utf-8") as fh:
-            json.dump(report, fh, indent=2, default=str)
+            json.dump({k: ({kk: vv for kk, vv in v.items() if kk != "tokens"} if isinstance(v, dict) else v)
+                       for k, v in report.items()}, fh, indent=2, default=str)
     return report
 
 

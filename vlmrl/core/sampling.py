@@ -250,10 +250,12 @@ def _generator(model) -> Generator:
 
 
 def sample(model, params, inputs: Union[VLMInputs, torch.Tensor, np.ndarray], cfg: SamplingConfig, rng: int, *,
-           tokenizer=None, return_logprobs: bool = False) -> SampleResult:
+           tokenizer=None, return_logprobs: bool = False, row_offset: int = 0) -> SampleResult:
     """Reference-compatible entry point: ``rng`` is an integer seed (see ``vlmrl.utils.rng.RngSeq``).
 
-    ``params`` is accepted for API compatibility; the model's own parameters are used.
+    ``params`` is accepted for API compatibility; the model's own parameters are used.  ``row_offset``: the
+    global index of the first row, so a batch split over data-parallel ranks draws what one process
+    drawing the whole batch would (the sampler's random stream is keyed by (seed, row, step)).
     """
     if isinstance(inputs, VLMInputs):
         prompts = inputs.prompt_tokens
@@ -266,7 +268,7 @@ def sample(model, params, inputs: Union[VLMInputs, torch.Tensor, np.ndarray], cf
         prompts = [row[row != cfg.pad_id] for row in np.atleast_2d(arr)]
         grids = [[] for _ in prompts]
         vision = None
-    res = _generator(model).generate(prompts, grids, vision, cfg, seed=int(rng))
+    res = _generator(model).generate(prompts, grids, vision, cfg, seed=int(rng), row_offset=int(row_offset))
     if tokenizer is not None:
         lens = res.lengths.tolist()
         res.texts = [tokenizer.decode(row[:n].tolist(), skip_special_tokens=True) for row, n in zip(res.tokens.cpu(), lens)]
